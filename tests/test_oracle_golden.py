@@ -1,0 +1,99 @@
+"""The CPU oracle against golden vectors captured from the reference's own fp32 code paths
+(``tests/golden/make_golden.py`` drives ``tools/reference.py``'s ``DiT.forward`` and
+``gemma_encode``).  These pin the restatement before any CUDA result is compared with it."""
+
+import numpy as np
+import pytest
+
+from oracle import attention_oracle as O
+
+TOL = dict(rtol=2e-5, atol=2e-5)
+
+
+def test_rope_tables(golden):
+    t = golden("tables")
+    c, s = O.rope_2d(int(t["rope2d_h"]), int(t["rope2d_w"]))
+    np.testing.assert_allclose(c, t["rope2d_cos"], **TOL)
+    np.testing.assert_allclose(s, t["rope2d_sin"], **TOL)
+    L = int(t["rope1d_L"])
+    for name, theta in (("local", 1e4), ("global", 1e6)):
+        c, s = O.rope_1d(L, theta)
+        np.testing.assert_allclose(c, t[f"rope1d_{name}_cos"], rtol=1e-5, atol=5e-5)
+        np.testing.assert_allclose(s, t[f"rope1d_{name}_sin"], rtol=1e-5, atol=5e-5)
+
+
+def test_rms_norm_and_rope(golden):
+    t = golden("tables")
+    rn = O.rms_norm(t["rms_x"], t["rms_w"])
+    np.testing.assert_allclose(rn, t["rms_out"], **TOL)
+    rs = O.rope_split_half(rn.transpose(1, 0, 2), t["rope_cos"], t["rope_sin"]).transpose(1, 0, 2)
+    np.testing.assert_allclose(rs, t["rope_out"], **TOL)
+
+
+def test_gemma_theta_schedule():
+    assert [O.gemma_rope_theta(i) for i in range(12)] == [1e4] * 5 + [1e6] + [1e4] * 5 + [1e6]
+
+
+def test_dit_joint_block(golden):
+    g = golden("dit_joint_block")
+    L = g["q_raw"].shape[0]
+    # prologue: q/k norm + 2D rope on image rows, k norm only on text rows
+    qp = O.head_norm(g["q_raw"], g["q_w"], 16, 96, g["cos"], g["sin"])
+    kp = np.concatenate([O.head_norm(g["k_raw"], g["k_w"], 16, 96, g["cos"], g["sin"]),
+                         O.head_norm(g["ky_raw"], g["k_w"], 16, 96)])
+    np.testing.assert_allclose(qp, g["q_post"], **TOL)
+    np.testing.assert_allclose(kp, g["k_post"], **TOL)
+    # key bias derived from the prompt weights by the reference's forward pass
+    tb = O.text_key_bias(g["txt_weights"])
+    np.testing.assert_array_equal(np.isneginf(tb), np.isneginf(g["txt_bias"]))
+    np.testing.assert_allclose(tb, g["txt_bias"], rtol=1e-6, atol=0)   # numpy vs torch logf: 1 ulp
+    out = O.dit_joint_attention(g["q_raw"], g["k_raw"], g["v"], g["q_w"], g["k_w"], g["cos"], g["sin"],
+                                g["ky_raw"], g["vy"], g["txt_bias"])
+    np.testing.assert_allclose(out, g["out"], rtol=1e-4, atol=1e-5)
+    assert out.shape == (L, 1536)
+
+
+def test_dit_image_block(golden):
+    g = golden("dit_image_block")
+    out = O.dit_joint_attention(g["q_raw"], g["k_raw"], g["v"], g["q_w"], g["k_w"], g["cos"], g["sin"])
+    np.testing.assert_allclose(out, g["out"], rtol=1e-4, atol=1e-5)
+
+
+def test_dit_text_refine(golden):
+    g = golden("dit_text_refine")
+    np.testing.assert_array_equal(O.refine_keep_bias(g["txt_weights"]), g["keep_bias"])
+    out = O.text_refine_attention(g["q_raw"], g["k_raw"], g["v"], g["q_w"], g["k_w"], g["keep_bias"])
+    np.testing.assert_allclose(out, g["out"], rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("layer", [0, 5])
+def test_gemma_layer(golden, layer):
+    g = golden(f"gemma_layer{layer}")
+    assert float(g["theta"]) == O.gemma_rope_theta(layer)
+    L = g["q_raw"].shape[0]
+    cos, sin = O.rope_1d(L, float(g["theta"]))
+    np.testing.assert_allclose(O.head_norm(g["q_raw"], g["q_w"], 4, 256, cos, sin), g["q_post"], rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(O.head_norm(g["k_raw"], g["k_w"], 1, 256, cos, sin), g["k_post"], rtol=1e-4, atol=1e-4)
+    # the reference's mask is the causal triangle
+    m = g["mask"]
+    assert np.all(np.isneginf(m[np.triu_indices(L, 1)])) and np.all(m[np.tril_indices(L)] == 0)
+    out = O.gemma_attention(g["q_raw"], g["k_raw"], g["v"], g["q_w"], g["k_w"], float(g["theta"]))
+    np.testing.assert_allclose(out, g["out"], rtol=1e-4, atol=2e-5)
+
+
+def test_batched_joint_matches_unbatched(golden):
+    g = golden("dit_joint_block")
+    L, Lt = g["q_raw"].shape[0], g["ky_raw"].shape[0]
+    C = 1536
+    qkv = np.zeros((1, L + Lt, 3 * C), np.float32)
+    qkv[0, :L, :C], qkv[0, :L, C:2 * C], qkv[0, :L, 2 * C:] = g["q_raw"], g["k_raw"], g["v"]
+    qkv[0, L:, C:2 * C], qkv[0, L:, 2 * C:] = g["ky_raw"], g["vy"]
+    out = O.joint_attention_batched(qkv, L, Lt, [L + Lt], g["q_w"], g["k_w"], g["cos"], g["sin"],
+                                    bias=g["txt_bias"][None])
+    np.testing.assert_allclose(out[0], g["out"], rtol=1e-4, atol=1e-5)
+    # dropping the masked (w <= 0) text rows through kv_len gives the same result
+    valid = int(np.sum(g["txt_weights"] > 0))
+    assert np.all(g["txt_weights"][valid:] <= 0)
+    out2 = O.joint_attention_batched(qkv, L, Lt, [L + valid], g["q_w"], g["k_w"], g["cos"], g["sin"],
+                                     bias=g["txt_bias"][None])
+    np.testing.assert_allclose(out2[0], g["out"], rtol=1e-4, atol=1e-5)
