@@ -1,0 +1,407 @@
+"""Benchmark of the Nanosaur2 attention hot path on B200 (BASELINE config 2 by default).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one fused DiT joint-attention call (q/k RMSNorm + 2D RoPE prologue, log-weight key bias,
+text padding mask, 16 heads x 96) over one batch of synthetic inputs with config 2's shapes:
+52x76 = 3952 image tokens + 256 text slots (valid length ~ U[32, 256] per element), batch 2 (the CFG
+pair), q/k/v ~ N(0, 1) in bf16.  Under torchrun each rank runs its own batch of 2 on its own GPU
+(weak scaling, no data-path collective); the timing is the max over ranks.
+
+Prints one JSON line (rank 0).  ``value`` is the whole-job algorithmic TFLOP/s with inputs resident
+in HBM (4 * B * H * valid pairs * D, app/gpu/ops.js:207); ``e2e`` is the same metric through the
+public call with pinned host buffers copied in and the output copied back every step; ``roofline``
+relates the attention kernel's own event-timed throughput to the measured dense bf16 peak;
+``cpu_baseline`` times the CPU restatement of the reference (oracle/) on a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "attention TFLOP/s & ms/call at 3952+256 tokens, 1/2/4/8 B200 vs CPU ref"
+H, D, C = 16, 96, 1536
+IMG_H, IMG_W, LT = 76, 52, 256      # 832x1216 image -> 52 x 76 latent tokens (w x h)
+B_PER_GPU = 2
+FALLBACK_PEAK_TFLOPS = 1590.0
+
+
+def joint_flops(B, L, lvs):
+    """Algorithmic FLOPs of one joint call: 4 * H * D * sum_b L * (L + Lv_b) (app/gpu/ops.js:207)."""
+    return float(sum(4.0 * H * L * (L + int(lv)) * D for lv in lvs[:B]))
+
+
+def gemma_pairs(L, window):
+    """Unmasked (query, key) pairs of a causal layer of length L with an optional sliding window."""
+    if window <= 0:
+        return L * (L + 1) // 2
+    return sum(min(i + 1, window) for i in range(L))
+
+
+def make_inputs(seed, B, bf16=True):
+    from tests._helpers import joint_inputs
+    return joint_inputs(seed, B, IMG_H, IMG_W, LT, (32, 256), C=C, bf16=bf16)
+
+
+# ----------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling in the background (read-only queries)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:9]))
+                except ValueError:
+                    continue
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        loaded = [r for r in rows if r[2] > 300.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in loaded for n, v in zip(names, r[3][1:]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in loaded),
+                "reasons": reasons, "samples": len(loaded), "power_w_max": max(r[2] for r in loaded)}
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+
+class CpuSample:
+    """The CPU restatement of the reference (oracle/attention_oracle.py, fp32 numpy) on config 2's
+    inputs (batch element 0), timed on bounded samples: some heads x the first ``rows`` query rows
+    against all keys, prologue (q/k RMSNorm + 2D RoPE) included."""
+
+    def __init__(self):
+        from oracle import attention_oracle as O
+        self.O = O
+        qkv, self.q_w, self.k_w, lv, bias = make_inputs(1234, 1)
+        self.x = qkv[0]
+        self.L = IMG_H * IMG_W
+        self.n = self.L + int(lv[0])
+        self.bias = np.concatenate([np.zeros(self.L, np.float32), bias[0][: self.n - self.L]])
+        self.cos, self.sin = O.rope_2d(IMG_H, IMG_W)
+
+    def run(self, heads, rows=None):
+        """One pass over the sample; returns (flops, seconds)."""
+        O, x, L, n = self.O, self.x, self.L, self.n
+        nrows = L if rows is None else rows
+        t0 = time.perf_counter()
+        for h in heads:
+            q = O.head_norm(x[:nrows, h * D:(h + 1) * D], self.q_w, 1, D, self.cos[:nrows], self.sin[:nrows])
+            k = np.concatenate([O.head_norm(x[:L, C + h * D:C + (h + 1) * D], self.k_w, 1, D, self.cos, self.sin),
+                                O.head_norm(x[L:n, C + h * D:C + (h + 1) * D], self.k_w, 1, D)])
+            v = x[:n, 2 * C + h * D:2 * C + (h + 1) * D]
+            O.attention(q, k, v, 1, D, bias=self.bias)
+        return 4.0 * len(heads) * nrows * n * D, time.perf_counter() - t0
+
+    def describe(self, heads, rows=None):
+        nrows = self.L if rows is None else rows
+        return (f"batch element 0 of config 2, {len(heads)} of 16 heads, {nrows} of {self.L} query rows x {self.n} "
+                f"keys, fp32 numpy (prologue + attention)")
+
+
+def cpu_baseline(min_seconds=10.0):
+    """TFLOP/s of the CPU restatement on all 16 heads of one config-2 batch element, repeated until
+    ``min_seconds`` of CPU work; returns (TFLOP/s, seconds, description)."""
+    s = CpuSample()
+    heads = tuple(range(H))
+    flops, el, reps = 0.0, 0.0, 0
+    while reps == 0 or el < min_seconds:
+        f, t = s.run(heads)
+        flops, el, reps = flops + f, el + t, reps + 1
+    return flops / el / 1e12, el, s.describe(heads) + f", {reps} repetition(s) in {el:.1f} s"
+
+
+def cpu_threads():
+    try:
+        import threadpoolctl
+        info = threadpoolctl.threadpool_info()
+        n = [i.get("num_threads") for i in info if i.get("user_api") == "blas"]
+        if n:
+            return int(n[0])
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+# ----------------------------------------------------------------------------- reference arm
+
+def run_reference(args, rank):
+    """The reference arm: the CPU restatement of the reference's attention (fp32, all host BLAS
+    threads) on config 2; each step is one head x 512 query rows against all keys of batch element 0."""
+    if rank != 0:
+        return
+    s = CpuSample()
+    flops = secs = 0.0
+    for i in range(args.warmup + args.steps):
+        f, t = s.run((i % H,), rows=512)
+        if i >= args.warmup:
+            flops, secs = flops + f, secs + t
+    value = flops / secs / 1e12
+    cores = cpu_threads()
+    sample = "per step: " + s.describe((0,), rows=512)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * secs / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args.gpus),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(n):
+    return {"workload": "config 2: DiT joint attention, 52x76=3952 image + 256 text slots (valid ~U[32,256]), "
+                        "16 heads x 96, fused q/k RMSNorm + 2D RoPE prologue, log-weight key bias, padding mask",
+            "global_batch": B_PER_GPU * n, "batch_per_gpu": B_PER_GPU, "seq_len": IMG_H * IMG_W + LT,
+            "parallelism": f"batch-sharded x{n} (no data-path collective)",
+            "l2": "inputs rotate over 3 buffers (233 MB > 126 MB L2)"}
+
+
+# ----------------------------------------------------------------------------- our arm
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        try:
+            return float(json.load(open(p))["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+        except Exception:
+            pass
+    return FALLBACK_PEAK_TFLOPS, "fallback (1.59 PFLOP/s burst, earlier measurement on this pool)"
+
+
+def ncu_traffic_per_launch():
+    """Per-launch DRAM traffic of the attention kernel on this workload from the committed ncu summary
+    (profiles/attention_cfg2.md, line 'dram_bytes_per_launch = N'), or None."""
+    p = os.path.join(ROOT, "profiles", "attention_cfg2.md")
+    if os.path.exists(p):
+        m = re.search(r"dram_bytes_per_launch\s*=\s*([0-9.eE+]+)", open(p).read())
+        if m:
+            return float(m.group(1))
+    return None
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from nanosaur2_web_b200 import _lib
+    from nanosaur2_web_b200.blocks import dit_block_attention, fused_workspace_bytes
+    from nanosaur2_web_b200.ops import check_device, rope2dTable
+    from nanosaur2_web_b200.sharding import max_over_ranks
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    _lib.lib()
+    L = IMG_H * IMG_W
+    NBUF = 3
+    host = [make_inputs(1000 + 17 * rank + i, B_PER_GPU) for i in range(NBUF)]
+    q_w, k_w = host[0][1], host[0][2]
+    lvs = [h[3] for h in host]
+    qkv_dev = [torch.from_numpy(h[0]).to(dev, torch.bfloat16) for h in host]
+    kv_len_dev = [torch.from_numpy((L + h[3]).astype(np.int32)).to(dev) for h in host]
+    bias_dev = [torch.from_numpy(h[4]).to(dev) for h in host]
+    qn, kn = torch.from_numpy(q_w).to(dev), torch.from_numpy(k_w).to(dev)
+    cs = rope2dTable(IMG_H, IMG_W, D, dev)
+    outs = [torch.empty((B_PER_GPU, L, C), dtype=torch.bfloat16, device=dev) for _ in range(NBUF)]
+    ws = torch.empty(fused_workspace_bytes(B=B_PER_GPU, Lq=L, Lk=L + LT, Hq=H, Hkv=H, D=D), dtype=torch.uint8,
+                     device=dev)
+    flops = [joint_flops(B_PER_GPU, L, lv) for lv in lvs]
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        j = i % NBUF
+        dit_block_attention(qkv_dev[j], L=L, text_rows=LT, q_norm=qn, k_norm=kn, cs=cs, kv_len=kv_len_dev[j],
+                            bias=bias_dev[j], out=outs[j], workspace=ws)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    with ClockSampler(local_rank) as clocks:
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        check_device(dev)
+        # ---- device-resident timing
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms = e0.elapsed_time(e1)
+        check_device(dev)
+    clock = clocks.summary()
+    ms_max = max_over_ranks(ms)
+    total_flops = sum(flops[i % NBUF] for i in range(args.steps))
+    total_flops_all = max_over_ranks(total_flops) * world   # every rank runs the same-size batch
+    value = total_flops_all / (ms_max * 1e-3) / 1e12
+
+    # ---- per-kernel roofline pass: library profiler events around each launch, same stream
+    L_ = _lib.lib()
+    L_.nsa_profiler_reset()
+    L_.nsa_profiler_enable(1)
+    for i in range(args.steps):
+        step(i)
+    torch.cuda.synchronize()
+    L_.nsa_profiler_enable(0)
+    stats = (_lib.KernelStat * 8)()
+    n = L_.nsa_profiler_read(stats, 8)
+    kstats = {stats[i].name.decode(): stats[i] for i in range(n)}
+    L_.nsa_profiler_reset()
+    att = kstats.get("attention")
+    pro = kstats.get("prologue")
+    att_ms = att.total_ms / max(att.launches, 1)
+    att_tflops = (total_flops / args.steps) / (att_ms * 1e-3) / 1e12
+    peak, peak_src = measured_peak()
+    traffic = ncu_traffic_per_launch()
+
+    # ---- end to end through the public call with pinned host buffers
+    hq = [torch.from_numpy(h[0]).to(torch.bfloat16).pin_memory() for h in host]
+    hk = [torch.from_numpy((L + h[3]).astype(np.int32)).pin_memory() for h in host]
+    hb = [torch.from_numpy(h[4]).pin_memory() for h in host]
+    hout = torch.empty((B_PER_GPU, L, C), dtype=torch.bfloat16).pin_memory()
+    e2e_steps = max(3, min(args.steps, 50))
+    dq = torch.empty_like(qkv_dev[0])
+    dk = torch.empty_like(kv_len_dev[0])
+    db = torch.empty_like(bias_dev[0])
+    dout = torch.empty_like(outs[0])
+
+    def e2e_step(i):
+        j = i % NBUF
+        dq.copy_(hq[j], non_blocking=True)
+        dk.copy_(hk[j], non_blocking=True)
+        db.copy_(hb[j], non_blocking=True)
+        dit_block_attention(dq, L=L, text_rows=LT, q_norm=qn, k_norm=kn, cs=cs, kv_len=dk, bias=db, out=dout,
+                            workspace=ws)
+        hout.copy_(dout, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier()
+    e0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    check_device(dev)
+    e2e_flops = max_over_ranks(sum(flops[i % NBUF] for i in range(e2e_steps))) * world
+    e2e_value = e2e_flops / (e2e_ms * 1e-3) / 1e12
+    h2d = hq[0].numel() * 2 + hk[0].numel() * 4 + hb[0].numel() * 4
+    d2h = hout.numel() * 2
+
+    if rank != 0:
+        return
+    base = None
+    if world == 1 and not args.no_cpu_baseline:
+        tf, el, desc = cpu_baseline(min_seconds=args.cpu_seconds)
+        base = {"value": tf, "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port", "sample": desc}
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config_dict(world),
+        "roofline": {"bound": "tensor", "achieved": att_tflops, "peak": peak, "unit": "TFLOP/s",
+                     "frac": att_tflops / peak, "traffic": traffic, "peak_source": peak_src,
+                     "kernel": "attn_fwd_kernel<96>", "kernel_ms": att_ms,
+                     "prologue_ms": (pro.total_ms / max(pro.launches, 1)) if pro else None,
+                     "prologue_gbs": (pro.bytes / max(pro.launches, 1)) / (pro.total_ms / max(pro.launches, 1) * 1e-3) / 1e9
+                     if pro else None},
+        "cpu_baseline": base,
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms / e2e_steps},
+        "clocks": clock,
+        "gpu_launches": 2 * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    sys.path.insert(0, ROOT)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    import datetime
+
+    import torch.distributed as dist
+    if world > 1:
+        import torch
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,175 @@
+/*
+ * nsattn.h - C ABI of the B200 (sm_100a) Nanosaur2 attention library (libnsattn.so).
+ *
+ * Drop-in for the attention hot path of the Nanosaur2 web app: the operator surface the models call
+ * (`ops.attention`, `ops.headNorm` in app/gpu/ops.js) plus the fused call sequence of one DiT block
+ * / one Gemma3 layer, over caller-owned device buffers and a caller stream.
+ *
+ * Conventions
+ *  - All pointers are device pointers except descriptors (host structs, read during the call).
+ *  - Work is stream-ordered on `stream` (a cudaStream_t; NULL = legacy default stream).  Calls only
+ *    enqueue kernels; like the reference's command recording (app/gpu/device.js:170-216) nothing
+ *    blocks unless stated.
+ *  - Every entry point returns an nsa_status and never aborts the process; no C++ exception crosses
+ *    the ABI.  nsa_last_error() gives the message of the last failing call on the calling thread.
+ *  - Buffers and workspaces are owned by the caller; the library allocates no device memory.
+ *  - Strides and offsets are in elements.  Matrices are row-major packed rows as in the reference:
+ *    element (b, row, col) of a view is at ptr[b*bstride + row*ld + off + col].
+ */
+#ifndef NSATTN_H
+#define NSATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NSA_ABI_VERSION 1
+
+typedef enum nsa_status {
+  NSA_OK = 0,
+  NSA_ERR_INVALID_ARGUMENT = 1, /* bad pointer / shape / stride: the reference throws (ops.js:210,216) */
+  NSA_ERR_UNSUPPORTED = 2,      /* a shape no kernel covers, e.g. head dim (kernels.js:133) */
+  NSA_ERR_WORKSPACE = 3,        /* workspace missing or smaller than *_workspace_size() */
+  NSA_ERR_CUDA = 4,             /* CUDA runtime / driver error while enqueueing */
+  NSA_ERR_DEVICE = 5            /* a kernel reported a device-side error (a bounded wait expired);
+                                   surfaces at nsa_check_device, like device.js:224-231 */
+} nsa_status;
+
+typedef enum nsa_dtype { NSA_F32 = 0, NSA_BF16 = 1 } nsa_dtype;
+
+/* Library version string, e.g. "nsattn 0.1.0 sm_100a". */
+const char* nsa_version(void);
+/* Message of the last failing call on the calling thread ("" if none). */
+const char* nsa_last_error(void);
+const char* nsa_status_string(nsa_status status);
+
+/* ------------------------------------------------------------------------------------------------
+ * ops.attention (app/gpu/ops.js:194-242): multi-head attention over packed rows.
+ *   q: [Lq, ldq] with head h at column qOff + h*D; k, v: [Lk, ldk] / [Lk, ldv] with kv head
+ *   h/group at kOff / vOff + (h/group)*D; output [Lq, ldo] with head h at oOff + h*D.
+ *   bias: optional additive score bias per key, bias[key - biasStart] for keys biasStart ..
+ *   biasStart+biasLen-1 (kernels.js:199-207); -inf drops a key.  causal keeps keys j <= i
+ *   (kernels.js:44).  Extensions over the reference: a batch dimension with per-batch valid key
+ *   counts (`kv_len`, keys >= kv_len[b] are masked like kernels.js:269-271), a sliding window, and a
+ *   batch x head shard (b_begin/b_count, h_begin/h_count; 0 counts mean "all").
+ * q/k/v may be fp32 (the reference's dtype) or bf16; the tensor cores compute in bf16 with fp32
+ * accumulation.  The output is fp32 or bf16.
+ * ------------------------------------------------------------------------------------------------ */
+typedef struct nsa_attention_desc {
+  int32_t Lq, Lk, H, D;
+  int64_t ldq, ldk, ldv;
+  int64_t qOff, kOff, vOff;
+  int32_t group;      /* query heads per kv head (ops.js `group`, 1 for the DiT, 4 for Gemma) */
+  int32_t causal;     /* ops.js `causal` */
+  int32_t window;     /* 0 = none; else key j is visible to query i iff i - window < j */
+  int32_t biasStart;  /* ops.js `biasStart` */
+  int32_t biasLen;    /* number of bias entries per batch element (0 = no bias) */
+  int32_t B;          /* batch elements (>= 1) */
+  int64_t q_bstride, k_bstride, v_bstride, bias_bstride, o_bstride;
+  int64_t ldo, oOff;  /* reference: ldo = H*D, oOff = 0 */
+  int32_t in_dtype;   /* nsa_dtype of q, k, v */
+  int32_t out_dtype;  /* nsa_dtype of out */
+  float scale;        /* 0 = 1/sqrt(D) (ops.js:206,214) */
+  int32_t b_begin, b_count, h_begin, h_count;
+} nsa_attention_desc;
+
+size_t nsa_attention_workspace_size(const nsa_attention_desc* desc);
+/* Replaces ops.attention (app/gpu/ops.js:199). */
+nsa_status nsa_attention(const nsa_attention_desc* desc, const void* q, const void* k, const void* v,
+                         const float* bias, const int32_t* kv_len, void* out, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * ops.headNorm (app/gpu/ops.js:131-138, kernels.js:311-342): in place, per-head RMSNorm
+ * y = x * rsqrt(mean(x^2) + eps) * weight over L rows x H heads of D values at
+ * X[(rowOff + l)*ld + colOff + h*D], then, when cs is given, split-half RoPE of pair (i, i + D/2)
+ * with cos cs[l*D/2 + i] and sin cs[sinOff + l*D/2 + i].  X is fp32 or bf16.
+ * ------------------------------------------------------------------------------------------------ */
+nsa_status nsa_head_norm(void* X, int32_t dtype, const float* weight, int32_t L, int32_t H, int32_t D,
+                         int64_t ld, int64_t colOff, int64_t rowOff, const float* cs, int64_t sinOff,
+                         float eps, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Fused attention step of one DiT block / one Gemma3 layer over the packed qkv buffer, replacing
+ * the call sequence headNorm(q, cs) + headNorm(k, cs) [+ headNorm(text k)] + attention(bias,
+ * biasStart) of app/models/nanosaur2.js:196-208 and app/models/gemma3.js:63-70
+ * (tools/reference.py:272-286 and :186-194).
+ *   qkv: [B][Lk rows][ld]; rows [0, Lq) hold q|k|v (queries; their q and k get the q/k norm and,
+ *   when cs is given, RoPE with table row = row index); rows [Lq, Lk) hold extra keys (the DiT's
+ *   text k|v rows: k norm only, no RoPE; q columns unused).  kv_len[b] (optional) = valid keys of
+ *   element b; rows beyond it are ignored (text padding).  bias (optional): [B][biasLen] natural-log
+ *   key bias for keys biasStart.. (the DiT passes biasStart = Lq and log prompt weights,
+ *   app/models/nanosaur2.js:113,207).  q_norm_w / k_norm_w: [D] fp32 (Gemma's stored w - 1 already
+ *   lifted by +1, gemma3.js:22).  Output: out[b*o_bstride + row*ldo + oOff + h*D + d], rows < Lq.
+ * ------------------------------------------------------------------------------------------------ */
+typedef struct nsa_fused_desc {
+  int32_t B;
+  int32_t Lq;         /* query rows = RoPE rows */
+  int32_t Lk;         /* key rows (>= Lq) */
+  int32_t Hq, Hkv, D; /* DiT 16/16/96, Gemma 4/1/256 */
+  int64_t ld, bstride;
+  int64_t qOff, kOff, vOff;
+  int32_t in_dtype, out_dtype;
+  float eps;          /* 1e-6 in both models */
+  int64_t sinOff;     /* offset of the sin block in cs (tables from nsa_rope*_table: Lq*D/2) */
+  int32_t causal, window;
+  int32_t biasStart, biasLen;
+  int64_t bias_bstride;
+  int64_t ldo, o_bstride, oOff;
+  float scale;        /* 0 = 1/sqrt(D) */
+  int32_t b_begin, b_count, h_begin, h_count;
+} nsa_fused_desc;
+
+size_t nsa_fused_attention_workspace_size(const nsa_fused_desc* desc);
+nsa_status nsa_fused_attention(const nsa_fused_desc* desc, const void* qkv, const float* q_norm_w,
+                               const float* k_norm_w, const float* cs, const int32_t* kv_len,
+                               const float* bias, void* out, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * RoPE tables in the reference layout: cos block [L][D/2] then sin block [L][D/2] (sinOff = L*D/2).
+ *   nsa_rope2d_table: app/models/common.js:28-43 (tools/reference.py:220-227): L = h*w tokens,
+ *     the first D/4 pairs rotate by the centred column, the next D/4 by the centred row, theta 1e4.
+ *   nsa_rope1d_table: app/models/common.js:18-24 (tools/reference.py:169-172).
+ * out: device fp32 buffer of L*D floats.
+ * ------------------------------------------------------------------------------------------------ */
+nsa_status nsa_rope2d_table(int32_t h, int32_t w, int32_t D, float* out, void* stream);
+nsa_status nsa_rope1d_table(int32_t L, int32_t D, float theta, float* out, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Device-side failure surfacing (app/gpu/device.js:224-231 turns async validation errors into a
+ * throw at the next read/sync).  Synchronises `stream`, reads and clears the device error word of
+ * the current device: NSA_ERR_DEVICE if any kernel gave up a bounded wait since the last check.
+ * ------------------------------------------------------------------------------------------------ */
+nsa_status nsa_check_device(void* stream);
+
+/* Self-test of the failure path: launches one CTA that waits on a barrier nothing arrives on, with
+ * a limit of `timeout_us`; the wait expires, the kernel records the error and returns.  A following
+ * nsa_check_device reports NSA_ERR_DEVICE and the context stays usable. */
+nsa_status nsa_selftest_wait_timeout(int32_t timeout_us, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Profiler (app/gpu/device.js:61-80,185-196,235-288: per-dispatch timestamps aggregated per kernel
+ * name with a flop count).  When enabled, each library launch is bracketed by CUDA events on its
+ * stream.  nsa_profiler_read synchronises the recorded events and returns one entry per kernel name.
+ * ------------------------------------------------------------------------------------------------ */
+typedef struct nsa_kernel_stat {
+  char name[32];
+  int64_t launches;
+  double total_ms;
+  double flops;   /* algorithmic flops (4*B*H*valid pairs*D for attention, ops.js:207) */
+  double bytes;   /* algorithmic HBM bytes (prologue: bytes read + written) */
+} nsa_kernel_stat;
+
+void nsa_profiler_enable(int32_t on);
+void nsa_profiler_reset(void);
+int32_t nsa_profiler_read(nsa_kernel_stat* out, int32_t max_entries);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NSATTN_H */

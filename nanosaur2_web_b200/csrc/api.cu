@@ -1,0 +1,494 @@
+// C ABI of libnsattn.so (declared in include/nsattn.h): argument validation, workspace planning,
+// TMA descriptor encoding, the per-kernel profiler and the device error word.
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "nsa_internal.h"
+#include "nsattn.h"
+#include "ptx.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+nsa_status fail(nsa_status s, const std::string& msg) {
+  g_last_error = msg;
+  return s;
+}
+
+nsa_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(NSA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// The library's device error word.  Kernels record the first device-side error here; the host
+// reads and clears it in nsa_check_device.  Every device that loads the library has its own copy.
+__device__ int g_device_error_word;
+
+constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;   // 2 s per bounded wait
+
+unsigned long long wait_timeout_ns() {
+  static unsigned long long v = [] {
+    const char* s = std::getenv("NSA_WAIT_TIMEOUT_MS");
+    if (s && *s) {
+      const double ms = std::atof(s);
+      if (ms > 0) return (unsigned long long)(ms * 1e6);
+    }
+    return kDefaultTimeoutNs;
+  }();
+  return v;
+}
+
+// ------------------------------------------------------------------------------------ profiler
+
+struct ProfRecord {
+  std::string name;
+  double flops, bytes;
+  cudaEvent_t start, stop;
+};
+
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+std::vector<ProfRecord> g_prof_records;
+std::vector<cudaEvent_t> g_event_pool;
+
+cudaEvent_t take_event() {
+  if (!g_event_pool.empty()) {
+    cudaEvent_t e = g_event_pool.back();
+    g_event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+template <class Launch>
+cudaError_t profiled(const char* name, double flops, double bytes, cudaStream_t stream, Launch&& launch) {
+  bool on;
+  {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    on = g_prof_on;
+  }
+  if (!on) return launch();
+  cudaEvent_t a, b;
+  {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    a = take_event();
+    b = take_event();
+  }
+  cudaEventRecord(a, stream);
+  const cudaError_t e = launch();
+  cudaEventRecord(b, stream);
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  g_prof_records.push_back({name, flops, bytes, a, b});
+  return e;
+}
+
+// ------------------------------------------------------------------------------------ TMA maps
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Map over a head-major bf16 tile buffer [rows][D]; boxes of [128 rows][blk elements].
+bool encode_tiles(CUtensorMap* map, void* base, int D, int64_t rows, int blk) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)blk, (cuuint32_t)nsa::kTileM};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = blk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// ------------------------------------------------------------------------------------ planning
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+struct Plan {
+  int B, Lq, Lk, Hq, group, D;       // full problem
+  int b0, Bs, hq0, Hqs, hkv0, Hkvs;  // shard
+  int NQ, blk, Lq_pad, Lk_pad;
+  size_t q_bytes, k_bytes, v_bytes, total;
+};
+
+struct CommonArgs {
+  int B, Lq, Lk, H, group, D, causal, window, in_dtype, out_dtype;
+  int b_begin, b_count, h_begin, h_count;
+};
+
+nsa_status make_plan(const CommonArgs& a, Plan* pl) {
+  if (a.B < 1 || a.Lq < 1 || a.Lk < 1 || a.H < 1 || a.D < 1)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "B, Lq, Lk, H and D must be >= 1");
+  if (a.group < 1 || a.H % a.group != 0)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "group must divide the number of query heads");
+  const int NQ = nsa::attention_q_tiles_per_block(a.D);
+  if (NQ == 0)
+    return fail(NSA_ERR_UNSUPPORTED, "attention: unsupported head dim " + std::to_string(a.D) + " (64, 96, 128, 256)");
+  if (a.in_dtype != NSA_F32 && a.in_dtype != NSA_BF16) return fail(NSA_ERR_INVALID_ARGUMENT, "bad input dtype");
+  if (a.out_dtype != NSA_F32 && a.out_dtype != NSA_BF16) return fail(NSA_ERR_INVALID_ARGUMENT, "bad output dtype");
+  if (a.window < 0) return fail(NSA_ERR_INVALID_ARGUMENT, "window must be >= 0");
+  if (a.causal && a.Lq > a.Lk) return fail(NSA_ERR_INVALID_ARGUMENT, "causal attention needs Lq <= Lk");
+  if (a.b_begin < 0 || a.b_begin >= a.B || a.b_count < 0 || a.b_begin + a.b_count > a.B)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "batch shard out of range");
+  if (a.h_begin < 0 || a.h_begin >= a.H || a.h_count < 0 || a.h_begin + a.h_count > a.H)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "head shard out of range");
+  Plan p{};
+  p.B = a.B; p.Lq = a.Lq; p.Lk = a.Lk; p.Hq = a.H; p.group = a.group; p.D = a.D;
+  p.b0 = a.b_begin; p.Bs = a.b_count ? a.b_count : a.B - a.b_begin;
+  p.hq0 = a.h_begin; p.Hqs = a.h_count ? a.h_count : a.H - a.h_begin;
+  p.hkv0 = p.hq0 / a.group;
+  p.Hkvs = (p.hq0 + p.Hqs - 1) / a.group - p.hkv0 + 1;
+  p.NQ = NQ;
+  p.blk = nsa::attention_block_elems(a.D);
+  p.Lq_pad = (int)round_up(a.Lq, (int64_t)NQ * nsa::kTileM);
+  p.Lk_pad = (int)round_up(a.Lk, nsa::kTileN);
+  const int64_t q_rows = (int64_t)p.Bs * p.Hqs * p.Lq_pad;
+  const int64_t kv_rows = (int64_t)p.Bs * p.Hkvs * p.Lk_pad;
+  if (q_rows >= (int64_t)1 << 31 || kv_rows >= (int64_t)1 << 31 || (int64_t)p.Bs * p.Hqs * (p.Lq_pad / (NQ * 128)) >= (int64_t)1 << 31)
+    return fail(NSA_ERR_UNSUPPORTED, "problem too large for one launch");
+  p.q_bytes = align_up((size_t)q_rows * a.D * 2, 1024);
+  p.k_bytes = align_up((size_t)kv_rows * a.D * 2, 1024);
+  p.v_bytes = p.k_bytes;
+  p.total = p.q_bytes + p.k_bytes + p.v_bytes + 1024;
+  *pl = p;
+  return NSA_OK;
+}
+
+nsa_status check_out(const void* out, int out_dtype, int64_t ldo, int64_t oOff, int64_t o_bstride) {
+  if (!out) return fail(NSA_ERR_INVALID_ARGUMENT, "out is NULL");
+  const int64_t v = out_dtype == NSA_F32 ? 4 : 8;   // 16-byte vector stores of each row segment
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || ldo % v || oOff % v || o_bstride % v)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "out, ldo, oOff and o_bstride must keep rows 16-byte aligned");
+  return NSA_OK;
+}
+
+// Prologue + attention launches shared by nsa_attention and nsa_fused_attention.
+nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, const float* bias, int bias_start,
+               int bias_len, int64_t bias_bstride, const int32_t* kv_len, float scale, void* out, int64_t ldo,
+               int64_t o_bstride, int64_t oOff, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  if (!ws || ws_bytes < pl.total)
+    return fail(NSA_ERR_WORKSPACE, "workspace of " + std::to_string(pl.total) + " bytes required, got " +
+                                       std::to_string(ws_bytes));
+  uint8_t* base = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(ws), 1024));
+  auto* Qs = reinterpret_cast<__nv_bfloat16*>(base);
+  auto* Ks = reinterpret_cast<__nv_bfloat16*>(base + pl.q_bytes);
+  auto* Vs = reinterpret_cast<__nv_bfloat16*>(base + pl.q_bytes + pl.k_bytes);
+
+  int* err = nsa::device_error_word();
+  if (!err) return fail(NSA_ERR_CUDA, "cannot resolve the device error word on this device");
+
+  pp.src_f32 = a.in_dtype == NSA_F32;
+  pp.B = pl.Bs;
+  pp.b_begin = pl.b0;
+  pp.Lq = pl.Lq;
+  pp.Lk = pl.Lk;
+  pp.Hq = pl.Hqs;
+  pp.Hkv = pl.Hkvs;
+  pp.D = pl.D;
+  pp.hq_begin = pl.hq0;
+  pp.hkv_begin = pl.hkv0;
+  pp.kv_len = kv_len;
+  pp.Qs = Qs;
+  pp.Ks = Ks;
+  pp.Vs = Vs;
+  pp.Lq_pad = pl.Lq_pad;
+  pp.Lk_pad = pl.Lk_pad;
+  const double in_elem = a.in_dtype == NSA_F32 ? 4.0 : 2.0;
+  const double pro_bytes = (double)pl.Bs * ((double)pl.Lq * pl.Hqs + 2.0 * pl.Lk * pl.Hkvs) * pl.D * (in_elem + 2.0);
+  cudaError_t e = profiled("prologue", 0.0, pro_bytes, stream, [&] { return nsa::launch_prologue(pp, stream); });
+  if (e != cudaSuccess) return cuda_fail(e, "prologue launch");
+
+  CUtensorMap tq, tk, tv;
+  if (!encode_tiles(&tq, Qs, pl.D, (int64_t)pl.Bs * pl.Hqs * pl.Lq_pad, pl.blk) ||
+      !encode_tiles(&tk, Ks, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk) ||
+      !encode_tiles(&tv, Vs, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk))
+    return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed (driver entry point unavailable?)");
+
+  nsa::AttnParams ap{};
+  ap.B = pl.Bs;
+  ap.Hq = pl.Hqs;
+  ap.Hkv = pl.Hkvs;
+  ap.group = pl.group;
+  ap.b_begin = pl.b0;
+  ap.hq_begin = pl.hq0;
+  ap.hkv_begin = pl.hkv0;
+  ap.Lq = pl.Lq;
+  ap.Lq_pad = pl.Lq_pad;
+  ap.Lk = pl.Lk;
+  ap.Lk_pad = pl.Lk_pad;
+  ap.kv_len = kv_len;
+  ap.bias = bias_len > 0 ? bias : nullptr;
+  ap.bias_start = bias_start;
+  ap.bias_len = bias_len;
+  ap.bias_bstride = bias_bstride;
+  const float s = scale > 0.f ? scale : 1.0f / std::sqrt((float)pl.D);
+  ap.scale_log2 = s * 1.4426950408889634f;
+  ap.causal = a.causal;
+  ap.window = a.window;
+  ap.out = out;
+  ap.out_f32 = a.out_dtype == NSA_F32;
+  ap.out_ld = ldo;
+  ap.out_bstride = o_bstride;
+  ap.out_off = oOff;
+  ap.q_blocks = pl.Lq_pad / (pl.NQ * nsa::kTileM);
+  ap.err = err;
+  ap.timeout_ns = wait_timeout_ns();
+  double pairs = (double)pl.Lq * pl.Lk;
+  if (a.causal) pairs = (double)pl.Lq * (pl.Lq + 1) / 2.0;
+  const double flops = 4.0 * pl.Bs * pl.Hqs * pairs * pl.D;
+  e = profiled("attention", flops, 0.0, stream, [&] { return nsa::launch_attention(ap, pl.D, tq, tk, tv, stream); });
+  if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+  return NSA_OK;
+}
+
+__global__ void selftest_wait_kernel(int* err, unsigned long long timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    nsa::mbar_init(&bar, 1);
+    abort_flag = 0;
+    nsa::fence_mbar_init();
+  }
+  __syncthreads();
+  // nothing ever arrives on `bar`: the bounded wait must expire and record the error
+  if (threadIdx.x == 0) nsa::wait_bounded(&bar, 0, &abort_flag, err, 0x1E5, timeout_ns);
+  __syncthreads();
+}
+
+CommonArgs common_from(const nsa_attention_desc* d) {
+  return CommonArgs{d->B, d->Lq, d->Lk, d->H, d->group, d->D, d->causal, d->window, d->in_dtype, d->out_dtype,
+                    d->b_begin, d->b_count, d->h_begin, d->h_count};
+}
+
+CommonArgs common_from(const nsa_fused_desc* d) {
+  const int group = d->Hkv > 0 ? d->Hq / d->Hkv : 0;
+  return CommonArgs{d->B, d->Lq, d->Lk, d->Hq, group, d->D, d->causal, d->window, d->in_dtype, d->out_dtype,
+                    d->b_begin, d->b_count, d->h_begin, d->h_count};
+}
+
+}  // namespace
+
+namespace nsa {
+
+int* device_error_word() {
+  static std::mutex mu;
+  static int* cache[128] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!cache[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error_word) != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<int*>(p);
+  }
+  return cache[dev];
+}
+
+}  // namespace nsa
+
+extern "C" {
+
+const char* nsa_version(void) { return "nsattn 0.1.0 sm_100a"; }
+
+const char* nsa_last_error(void) { return g_last_error.c_str(); }
+
+const char* nsa_status_string(nsa_status s) {
+  switch (s) {
+    case NSA_OK: return "ok";
+    case NSA_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case NSA_ERR_UNSUPPORTED: return "unsupported";
+    case NSA_ERR_WORKSPACE: return "workspace too small";
+    case NSA_ERR_CUDA: return "cuda error";
+    case NSA_ERR_DEVICE: return "device-side error";
+  }
+  return "unknown status";
+}
+
+size_t nsa_attention_workspace_size(const nsa_attention_desc* desc) {
+  if (!desc) return 0;
+  Plan pl;
+  if (make_plan(common_from(desc), &pl) != NSA_OK) return 0;
+  return pl.total;
+}
+
+nsa_status nsa_attention(const nsa_attention_desc* d, const void* q, const void* k, const void* v, const float* bias,
+                         const int32_t* kv_len, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!d) return fail(NSA_ERR_INVALID_ARGUMENT, "desc is NULL");
+  if (!q || !k || !v) return fail(NSA_ERR_INVALID_ARGUMENT, "q, k and v must be device pointers");
+  const CommonArgs a = common_from(d);
+  Plan pl;
+  nsa_status st = make_plan(a, &pl);
+  if (st != NSA_OK) return st;
+  if ((st = check_out(out, d->out_dtype, d->ldo, d->oOff, d->o_bstride)) != NSA_OK) return st;
+  if (d->biasLen < 0) return fail(NSA_ERR_INVALID_ARGUMENT, "biasLen must be >= 0");
+  if (d->biasLen > 0 && !bias) return fail(NSA_ERR_INVALID_ARGUMENT, "biasLen > 0 needs a bias pointer");
+  nsa::PrologueParams pp{};
+  pp.q = {q, d->ldq, d->q_bstride, d->qOff};
+  pp.k = {k, d->ldk, d->k_bstride, d->kOff};
+  pp.v = {v, d->ldv, d->v_bstride, d->vOff};
+  pp.q_w = nullptr;
+  pp.k_w = nullptr;
+  pp.cs = nullptr;
+  pp.rope_rows = 0;
+  pp.eps = 0.f;
+  return run(pl, pp, a, bias, d->biasStart, bias ? d->biasLen : 0, d->bias_bstride, kv_len, d->scale, out, d->ldo,
+             d->o_bstride, d->oOff, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+size_t nsa_fused_attention_workspace_size(const nsa_fused_desc* desc) {
+  if (!desc) return 0;
+  Plan pl;
+  if (make_plan(common_from(desc), &pl) != NSA_OK) return 0;
+  return pl.total;
+}
+
+nsa_status nsa_fused_attention(const nsa_fused_desc* d, const void* qkv, const float* q_norm_w, const float* k_norm_w,
+                               const float* cs, const int32_t* kv_len, const float* bias, void* out, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (!d) return fail(NSA_ERR_INVALID_ARGUMENT, "desc is NULL");
+  if (!qkv) return fail(NSA_ERR_INVALID_ARGUMENT, "qkv is NULL");
+  if (!q_norm_w || !k_norm_w) return fail(NSA_ERR_INVALID_ARGUMENT, "q/k norm weights are required");
+  if (d->Hkv < 1 || d->Hq % d->Hkv) return fail(NSA_ERR_INVALID_ARGUMENT, "Hkv must divide Hq");
+  if (d->Lk < d->Lq) return fail(NSA_ERR_INVALID_ARGUMENT, "Lk must be >= Lq (query rows are also key rows)");
+  const CommonArgs a = common_from(d);
+  Plan pl;
+  nsa_status st = make_plan(a, &pl);
+  if (st != NSA_OK) return st;
+  if ((st = check_out(out, d->out_dtype, d->ldo, d->oOff, d->o_bstride)) != NSA_OK) return st;
+  if (d->biasLen < 0) return fail(NSA_ERR_INVALID_ARGUMENT, "biasLen must be >= 0");
+  if (d->biasLen > 0 && !bias) return fail(NSA_ERR_INVALID_ARGUMENT, "biasLen > 0 needs a bias pointer");
+  if (cs && d->D % 2) return fail(NSA_ERR_INVALID_ARGUMENT, "RoPE needs an even head dim");
+  nsa::PrologueParams pp{};
+  pp.q = {qkv, d->ld, d->bstride, d->qOff};
+  pp.k = {qkv, d->ld, d->bstride, d->kOff};
+  pp.v = {qkv, d->ld, d->bstride, d->vOff};
+  pp.q_w = q_norm_w;
+  pp.k_w = k_norm_w;
+  pp.cs = cs;
+  pp.sin_off = d->sinOff;
+  pp.rope_rows = cs ? d->Lq : 0;
+  pp.eps = d->eps;
+  return run(pl, pp, a, bias, d->biasStart, bias ? d->biasLen : 0, d->bias_bstride, kv_len, d->scale, out, d->ldo,
+             d->o_bstride, d->oOff, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+nsa_status nsa_head_norm(void* X, int32_t dtype, const float* weight, int32_t L, int32_t H, int32_t D, int64_t ld,
+                         int64_t colOff, int64_t rowOff, const float* cs, int64_t sinOff, float eps, void* stream) {
+  if (!X || !weight) return fail(NSA_ERR_INVALID_ARGUMENT, "X and weight must be device pointers");
+  if (dtype != NSA_F32 && dtype != NSA_BF16) return fail(NSA_ERR_INVALID_ARGUMENT, "bad dtype");
+  if (L < 0 || H < 1 || D < 2 || D % 2) return fail(NSA_ERR_INVALID_ARGUMENT, "need L >= 0, H >= 1, even D");
+  const double bytes = 2.0 * L * H * D * (dtype == NSA_F32 ? 4.0 : 2.0);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = profiled(cs ? "head_norm_rope" : "head_norm", 0.0, bytes, s, [&] {
+    return nsa::launch_head_norm(X, dtype == NSA_F32, weight, L, H, D, ld, colOff, rowOff, cs, sinOff, eps, s);
+  });
+  if (e != cudaSuccess) return cuda_fail(e, "head_norm launch");
+  return NSA_OK;
+}
+
+nsa_status nsa_rope2d_table(int32_t h, int32_t w, int32_t D, float* out, void* stream) {
+  if (!out) return fail(NSA_ERR_INVALID_ARGUMENT, "out is NULL");
+  if (h < 1 || w < 1 || D < 4 || D % 4) return fail(NSA_ERR_INVALID_ARGUMENT, "need h, w >= 1 and D % 4 == 0");
+  cudaError_t e = nsa::launch_rope2d_table(h, w, D, out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope2d table launch");
+  return NSA_OK;
+}
+
+nsa_status nsa_rope1d_table(int32_t L, int32_t D, float theta, float* out, void* stream) {
+  if (!out) return fail(NSA_ERR_INVALID_ARGUMENT, "out is NULL");
+  if (L < 1 || D < 2 || D % 2 || !(theta > 0.f)) return fail(NSA_ERR_INVALID_ARGUMENT, "need L >= 1, even D, theta > 0");
+  cudaError_t e = nsa::launch_rope1d_table(L, D, theta, out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope1d table launch");
+  return NSA_OK;
+}
+
+nsa_status nsa_check_device(void* stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* w = nsa::device_error_word();
+  if (!w) return fail(NSA_ERR_CUDA, "cannot resolve the device error word on this device");
+  int host = 0;
+  cudaError_t e = cudaMemcpyAsync(&host, w, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(w, 0, sizeof(int), s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "device check");
+  if (host != 0) {
+    char buf[96];
+    std::snprintf(buf, sizeof buf, "device-side error 0x%x (a bounded wait expired)", host);
+    return fail(NSA_ERR_DEVICE, buf);
+  }
+  return NSA_OK;
+}
+
+nsa_status nsa_selftest_wait_timeout(int32_t timeout_us, void* stream) {
+  if (timeout_us < 1 || timeout_us > 10000000) return fail(NSA_ERR_INVALID_ARGUMENT, "timeout_us in [1, 1e7]");
+  int* w = nsa::device_error_word();
+  if (!w) return fail(NSA_ERR_CUDA, "cannot resolve the device error word on this device");
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(w, (unsigned long long)timeout_us * 1000ull);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "self-test launch");
+  return NSA_OK;
+}
+
+void nsa_profiler_enable(int32_t on) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  g_prof_on = on != 0;
+}
+
+void nsa_profiler_reset(void) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  for (auto& r : g_prof_records) {
+    cudaEventSynchronize(r.stop);
+    g_event_pool.push_back(r.start);
+    g_event_pool.push_back(r.stop);
+  }
+  g_prof_records.clear();
+}
+
+int32_t nsa_profiler_read(nsa_kernel_stat* out, int32_t max_entries) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  std::vector<nsa_kernel_stat> stats;
+  for (auto& r : g_prof_records) {
+    cudaEventSynchronize(r.stop);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, r.start, r.stop);
+    nsa_kernel_stat* st = nullptr;
+    for (auto& s : stats)
+      if (r.name == s.name) st = &s;
+    if (!st) {
+      stats.push_back(nsa_kernel_stat{});
+      st = &stats.back();
+      std::snprintf(st->name, sizeof st->name, "%s", r.name.c_str());
+    }
+    st->launches += 1;
+    st->total_ms += ms;
+    st->flops += r.flops;
+    st->bytes += r.bytes;
+  }
+  const int32_t n = (int32_t)stats.size();
+  for (int32_t i = 0; out && i < n && i < max_entries; ++i) out[i] = stats[i];
+  return n;
+}
+
+}  // extern "C"

@@ -1,0 +1,503 @@
+// Fused multi-head attention forward for sm_100a (B200): TMA-staged Q/K/V tiles, tcgen05 MMAs
+// accumulating in tensor memory for S = Q K^T and O = P V, online softmax on the CUDA cores with
+// the key bias / padding mask / causal and window masks folded into the score tile.
+//
+// It replaces the reference's fused WGSL flash kernel (app/gpu/kernels.js:132-305: O = softmax(
+// s*QK^T + key bias + key mask) V, keys streamed in blocks with an online max/sum) and its unfused
+// GEMM + causal softmax + GEMM fallback for Gemma (app/gpu/ops.js:211-241).
+//
+// Layout of one CTA (one "block" of NQ query tiles of 128 rows for one (batch, query head)):
+//   warp 0        TMA producer: Q tiles once, then K/V tiles through NS-deep rings
+//   warp 1        TMEM allocator + MMA issuer (a single thread issues every tcgen05.mma)
+//   warps 2-3     idle (they complete the first warpgroup)
+//   warps 4..     one softmax warpgroup per query tile.  A warp may only touch the TMEM lane
+//                 quarter (warp id % 4), so lane l of warp w owns query row 32*(w%4) + l of its
+//                 tile: it reads its score row with tcgen05.ld, writes bf16 probabilities back
+//                 into the same TMEM columns, and finally normalises its output row.
+// Tensor memory (512 columns):
+//   NQ = 2 (head dim <= 128): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [384,384+D)
+//   NQ = 1 (head dim 256):    S double-buffered [0,128) [128,256), O [256,512)
+// P (bf16, two per 32-bit column) overwrites the first 64 columns of the S buffer it came from.
+// The MMA for the next S into a buffer is issued after the P*V MMA that reads it; tcgen05.mma
+// operations issued by one thread execute in order.
+#include "nsa_internal.h"
+#include "ptx.cuh"
+
+namespace nsa {
+
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;   // log2 units: P may reach 2^8 before O is rescaled
+
+template <int D>
+struct Cfg {
+  static constexpr int NQ = (D <= 128) ? 2 : 1;
+  static constexpr int NS = (D <= 128) ? 2 : 1;
+  static constexpr int BLK = (D % 64 == 0) ? 64 : 32;     // elements per swizzle row
+  static constexpr int NB = D / BLK;
+  static constexpr int ROWB = BLK * 2;                    // bytes per row of one block
+  static constexpr uint32_t SWZ = (BLK == 64) ? 2u : 4u;  // 128-byte / 64-byte swizzle
+  static constexpr int BLK_BYTES = kTileM * ROWB;         // one [128 rows][BLK] block
+  static constexpr int TILE_BYTES = kTileM * D * 2;
+  static constexpr int KSTEPS_QK = D / 16;
+  static constexpr int KSTEPS_PV = kTileN / 16;
+  static constexpr int THREADS = 128 + NQ * 128;
+  static constexpr int SMEM_TILES = (NQ + 2 * NS) * TILE_BYTES;
+  // at least 117 KB so that two CTAs never share an SM (each allocates all 512 TMEM columns)
+  static constexpr int SMEM_BYTES = (SMEM_TILES + 1024 + 256) > 117 * 1024 ? (SMEM_TILES + 1024 + 256) : 117 * 1024;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, kTileN, 0, 0);
+  static constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, D, 0, 1);
+  static_assert(kTileM == kTileN, "Q and K/V tiles share the block geometry");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static __device__ __forceinline__ uint32_t s_col(int buf) { return (uint32_t)buf * 128u; }
+  static __device__ __forceinline__ uint32_t o_col(int tile) { return NQ == 2 ? 256u + (uint32_t)tile * 128u : 256u; }
+  // byte offset of MMA k-step kk (16 elements) inside a K-major [128][D] tile
+  static __device__ __forceinline__ uint32_t kmajor_off(int kk) {
+    constexpr int per_blk = BLK / 16;
+    return (uint32_t)((kk / per_blk) * BLK_BYTES + (kk % per_blk) * 32);
+  }
+};
+
+template <int D>
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t sq, uint32_t sk) {
+  using C = Cfg<D>;
+#pragma unroll
+  for (int kk = 0; kk < C::KSTEPS_QK; ++kk) {
+    const uint64_t a = smem_desc(sq + C::kmajor_off(kk), 16, 8 * C::ROWB, C::SWZ);
+    const uint64_t b = smem_desc(sk + C::kmajor_off(kk), 16, 8 * C::ROWB, C::SWZ);
+    mma_ss(d_tmem, a, b, C::IDESC_QK, kk > 0 ? 1u : 0u);
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t sv, bool accumulate) {
+  using C = Cfg<D>;
+#pragma unroll
+  for (int kk = 0; kk < C::KSTEPS_PV; ++kk) {
+    // V is MN-major: 16 keys per k-step, head-dim blocks of BLK elements BLK_BYTES apart
+    const uint64_t b = smem_desc(sv + (uint32_t)(kk * 16 * C::ROWB), C::BLK_BYTES, 8 * C::ROWB, C::SWZ);
+    mma_ts(d_tmem, p_tmem + (uint32_t)(kk * 8), b, C::IDESC_PV, (accumulate || kk > 0) ? 1u : 0u);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  using C = Cfg<D>;
+  constexpr int NQ = C::NQ, NS = C::NS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + NQ * C::TILE_BYTES;
+  uint8_t* sV = sK + NS * C::TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + NS * C::TILE_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + NS;
+  uint64_t* v_full = k_empty + NS;
+  uint64_t* v_empty = v_full + NS;
+  uint64_t* s_full = v_empty + NS;   // [2]
+  uint64_t* p_full = s_full + 2;     // [2]
+  uint64_t* o_full = p_full + 2;     // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  // ---- work unit: (batch, query head, query block)
+  const int qb_raw = blockIdx.x % p.q_blocks;
+  const int rest = blockIdx.x / p.q_blocks;
+  const int qb = p.causal ? (p.q_blocks - 1 - qb_raw) : qb_raw;   // long causal blocks first
+  const int hl = rest % p.Hq;
+  const int bl = rest / p.Hq;
+  const int b = p.b_begin + bl;
+  const int hkvl = (p.hq_begin + hl) / p.group - p.hkv_begin;
+  const int kv_valid = p.kv_len ? min(p.kv_len[b], p.Lk) : p.Lk;
+  const int q_row0 = qb * NQ * kTileM;
+  const int q_row_end = min(q_row0 + NQ * kTileM, p.Lq);
+  int kv_end = kv_valid;
+  if (p.causal) kv_end = min(kv_end, q_row_end);
+  const int kv_begin = p.window > 0 ? max(0, q_row0 - p.window + 1) : 0;
+  const int j0 = kv_begin / kTileN;
+  const int n = kv_end > kv_begin ? ((kv_end - 1) / kTileN - j0 + 1) : 0;
+  const int q_tma_row = (bl * p.Hq + hl) * p.Lq_pad + q_row0;
+  const int kv_tma_row = (bl * p.Hkv + hkvl) * p.Lk_pad;
+  const uint64_t to = p.timeout_ns;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0 && n > 0) {
+      bool ok = true;
+      mbar_arrive_expect_tx(q_full, NQ * C::TILE_BYTES);
+      for (int i = 0; i < NQ; ++i)
+        for (int c = 0; c < C::NB; ++c)
+          tma_load_2d(sQ + i * C::TILE_BYTES + c * C::BLK_BYTES, &tmQ, q_full, c * C::BLK, q_tma_row + i * kTileM);
+      auto load_k = [&](int j) -> bool {
+        const int s = j % NS;
+        if (j >= NS && !wait_bounded(&k_empty[s], ((j / NS) - 1) & 1, abort_flag, p.err, kErrTimeoutLoad, to))
+          return false;
+        mbar_arrive_expect_tx(&k_full[s], C::TILE_BYTES);
+        for (int c = 0; c < C::NB; ++c)
+          tma_load_2d(sK + s * C::TILE_BYTES + c * C::BLK_BYTES, &tmK, &k_full[s], c * C::BLK,
+                      kv_tma_row + (j0 + j) * kTileN);
+        return true;
+      };
+      auto load_v = [&](int j) -> bool {
+        const int s = j % NS;
+        if (j >= NS && !wait_bounded(&v_empty[s], ((j / NS) - 1) & 1, abort_flag, p.err, kErrTimeoutLoad, to))
+          return false;
+        mbar_arrive_expect_tx(&v_full[s], C::TILE_BYTES);
+        for (int c = 0; c < C::NB; ++c)
+          tma_load_2d(sV + s * C::TILE_BYTES + c * C::BLK_BYTES, &tmV, &v_full[s], c * C::BLK,
+                      kv_tma_row + (j0 + j) * kTileN);
+        return true;
+      };
+      int k_issued = 0, v_issued = 0;
+      ok = load_k(0);
+      if (ok) k_issued = 1;
+      for (int j = 0; ok && j < n; ++j) {
+        if (j + 1 < n) {
+          ok = load_k(j + 1);
+          if (ok) k_issued = j + 2;
+        }
+        if (ok) ok = load_v(j);
+        if (ok) v_issued = j + 1;
+      }
+      // On an abort, wait (bounded) for the copies already issued so none lands after exit:
+      // the latest issue into each stage completes after the earlier ones.
+      if (!ok) {
+        wait_drain(q_full, 0, 20000000ull);
+        for (int j = k_issued - 1; j >= 0 && j >= k_issued - NS; --j) wait_drain(&k_full[j % NS], (j / NS) & 1, 20000000ull);
+        for (int j = v_issued - 1; j >= 0 && j >= v_issued - NS; --j) wait_drain(&v_full[j % NS], (j / NS) & 1, 20000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n > 0) {
+      const uint32_t sq = smem_u32(sQ), sk = smem_u32(sK), sv = smem_u32(sV);
+      bool ok = wait_bounded(q_full, 0, abort_flag, p.err, kErrTimeoutMma, to);
+      tc_fence_after();
+      if constexpr (NQ == 2) {
+        if (ok) ok = wait_bounded(&k_full[0], 0, abort_flag, p.err, kErrTimeoutMma, to);
+        if (ok) {
+          tc_fence_after();
+          issue_qk<D>(tmem + C::s_col(0), sq, sk);
+          tc_commit(&s_full[0]);
+          issue_qk<D>(tmem + C::s_col(1), sq + C::TILE_BYTES, sk);
+          tc_commit(&s_full[1]);
+          tc_commit(&k_empty[0]);
+        }
+        for (int j = 1; ok && j < n; ++j) {
+          const int svs = (j - 1) % NS, sks = j % NS;
+          ok = wait_bounded(&v_full[svs], ((j - 1) / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to) &&
+               wait_bounded(&p_full[0], (j - 1) & 1, abort_flag, p.err, kErrTimeoutMma, to);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv<D>(tmem + C::o_col(0), tmem + C::s_col(0), sv + svs * C::TILE_BYTES, j - 1 > 0);
+          ok = wait_bounded(&k_full[sks], (j / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to);
+          if (!ok) break;
+          tc_fence_after();
+          issue_qk<D>(tmem + C::s_col(0), sq, sk + sks * C::TILE_BYTES);
+          tc_commit(&s_full[0]);
+          ok = wait_bounded(&p_full[1], (j - 1) & 1, abort_flag, p.err, kErrTimeoutMma, to);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv<D>(tmem + C::o_col(1), tmem + C::s_col(1), sv + svs * C::TILE_BYTES, j - 1 > 0);
+          tc_commit(&v_empty[svs]);
+          issue_qk<D>(tmem + C::s_col(1), sq + C::TILE_BYTES, sk + sks * C::TILE_BYTES);
+          tc_commit(&s_full[1]);
+          tc_commit(&k_empty[sks]);
+        }
+        if (ok) {
+          const int svs = (n - 1) % NS;
+          ok = wait_bounded(&v_full[svs], ((n - 1) / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to);
+          for (int i = 0; ok && i < 2; ++i) {
+            ok = wait_bounded(&p_full[i], (n - 1) & 1, abort_flag, p.err, kErrTimeoutMma, to);
+            if (!ok) break;
+            tc_fence_after();
+            issue_pv<D>(tmem + C::o_col(i), tmem + C::s_col(i), sv + svs * C::TILE_BYTES, n - 1 > 0);
+            tc_commit(&o_full[i]);
+          }
+          if (ok) tc_commit(&v_empty[svs]);
+        }
+      } else {
+        // one query tile, S double-buffered: S(0), S(1), then PV(j) followed by S(j+2)
+        for (int j = 0; ok && j < 2 && j < n; ++j) {
+          ok = wait_bounded(&k_full[j % NS], (j / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to);
+          if (!ok) break;
+          tc_fence_after();
+          issue_qk<D>(tmem + C::s_col(j & 1), sq, sk + (j % NS) * C::TILE_BYTES);
+          tc_commit(&s_full[j & 1]);
+          tc_commit(&k_empty[j % NS]);
+        }
+        for (int j = 0; ok && j < n; ++j) {
+          const int svs = j % NS;
+          ok = wait_bounded(&v_full[svs], (j / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to) &&
+               wait_bounded(&p_full[0], j & 1, abort_flag, p.err, kErrTimeoutMma, to);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv<D>(tmem + C::o_col(0), tmem + C::s_col(j & 1), sv + svs * C::TILE_BYTES, j > 0);
+          tc_commit(&o_full[0]);
+          tc_commit(&v_empty[svs]);
+          if (j + 2 < n) {
+            const int sks = (j + 2) % NS;
+            ok = wait_bounded(&k_full[sks], ((j + 2) / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to);
+            if (!ok) break;
+            tc_fence_after();
+            issue_qk<D>(tmem + C::s_col(j & 1), sq, sk + sks * C::TILE_BYTES);
+            tc_commit(&s_full[j & 1]);
+            tc_commit(&k_empty[sks]);
+          }
+        }
+      }
+      if (!ok) {
+        // let every MMA already issued finish before the CTA tears down its tensor memory
+        // (o_full[1] is the last barrier the normal path arrives on, so it is still in phase 0)
+        tc_commit(&o_full[1]);
+        wait_drain(&o_full[1], 0, 20000000ull);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int tile = (warp - 4) / 4;
+    const int quarter = warp % 4;
+    const int row = q_row0 + tile * kTileM + quarter * 32 + lane;
+    const int tile_row0 = q_row0 + tile * kTileM;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+    const float sl2 = p.scale_log2;
+    const float* bias_b = p.bias ? p.bias + (int64_t)b * p.bias_bstride : nullptr;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      const int sbuf = NQ == 2 ? tile : (j & 1);
+      const uint32_t sparity = NQ == 2 ? (uint32_t)(j & 1) : (uint32_t)((j >> 1) & 1);
+      ok = __all_sync(0xffffffffu, wait_bounded(&s_full[sbuf], sparity, abort_flag, p.err, kErrTimeoutSoftmax, to));
+      if (!ok) break;
+      tc_fence_after();
+      float x[128];
+      {
+        uint32_t r[64];
+        tmem_ld64(lane_base + C::s_col(sbuf), r);
+#pragma unroll
+        for (int c = 0; c < 64; ++c) x[c] = __uint_as_float(r[c]);
+        tmem_ld64(lane_base + C::s_col(sbuf) + 64u, r);
+#pragma unroll
+        for (int c = 0; c < 64; ++c) x[64 + c] = __uint_as_float(r[c]);
+      }
+      const int key0 = (j0 + j) * kTileN;
+      const bool t_invalid = key0 + kTileN > kv_valid;
+      const bool t_causal = p.causal && key0 + kTileN - 1 > tile_row0;
+      const bool t_window = p.window > 0 && key0 <= tile_row0 + kTileM - 1 - p.window;
+      const bool t_bias = bias_b != nullptr && key0 + kTileN > p.bias_start && key0 < p.bias_start + p.bias_len;
+      float tmax = -INFINITY;
+      if (!(t_invalid || t_causal || t_window || t_bias)) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          x[c] *= sl2;
+          tmax = fmaxf(tmax, x[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          const int key = key0 + c;
+          float v = x[c] * sl2;
+          if (t_bias && key >= p.bias_start && key < p.bias_start + p.bias_len)
+            v += __ldg(bias_b + (key - p.bias_start)) * kLog2e;
+          const bool keep = key < kv_valid && (!p.causal || key <= row) && (p.window <= 0 || key > row - p.window);
+          v = keep ? v : -INFINITY;
+          x[c] = v;
+          tmax = fmaxf(tmax, v);
+        }
+      }
+      const float m_new = fmaxf(m_run, tmax);
+      if (j == 0) {
+        m_run = m_new;
+      } else {
+        const bool need = m_new > m_run + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          const float alpha = need ? ex2(m_run - m_new) : 1.f;
+          if (need) {
+            l_run *= alpha;
+            m_run = m_new;
+          }
+          if constexpr (NQ == 1) {
+            // O must hold every P*V up to tile j-1 before it is rescaled
+            ok = __all_sync(0xffffffffu,
+                            wait_bounded(&o_full[0], (uint32_t)((j - 1) & 1), abort_flag, p.err, kErrTimeoutSoftmax, to));
+            if (!ok) break;
+            tc_fence_after();
+          }
+#pragma unroll 1
+          for (int cc = 0; cc < D / 32; ++cc) {
+            uint32_t r[32];
+            const uint32_t oaddr = lane_base + C::o_col(tile) + (uint32_t)(cc * 32);
+            tmem_ld32(oaddr, r);
+#pragma unroll
+            for (int c = 0; c < 32; ++c) r[c] = __float_as_uint(__uint_as_float(r[c]) * alpha);
+            tmem_st32(oaddr, r);
+          }
+        }
+      }
+      const float m_use = m_run == -INFINITY ? 0.f : m_run;
+      float rs = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float a0 = ex2(x[2 * c] - m_use);
+        const float a1 = ex2(x[2 * c + 1] - m_use);
+        rs += a0 + a1;
+        pk[c] = pack_bf16x2(a0, a1);
+      }
+      l_run += rs;
+      tmem_st64(lane_base + C::s_col(sbuf), pk);
+      tc_fence_before();
+      mbar_arrive(&p_full[NQ == 2 ? tile : 0]);
+    }
+    if (ok && n > 0) {
+      if constexpr (NQ == 2) {
+        ok = wait_bounded(&o_full[tile], 0, abort_flag, p.err, kErrTimeoutSoftmax, to);
+      } else {
+        // O's barrier completes once per P*V; step through the last two completions so the
+        // parity test never skips a phase
+        if (n >= 2) ok = wait_bounded(&o_full[0], (uint32_t)((n - 2) & 1), abort_flag, p.err, kErrTimeoutSoftmax, to);
+        if (ok) ok = wait_bounded(&o_full[0], (uint32_t)((n - 1) & 1), abort_flag, p.err, kErrTimeoutSoftmax, to);
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) tc_fence_after();
+    }
+    if (ok) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const bool store = row < p.Lq;
+      const int64_t obase = (int64_t)b * p.out_bstride + (int64_t)row * p.out_ld + p.out_off +
+                            (int64_t)(p.hq_begin + hl) * D;
+#pragma unroll 1
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t r[32];
+        if (n > 0) {
+          tmem_ld32(lane_base + C::o_col(tile) + (uint32_t)(cc * 32), r);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) r[c] = 0u;
+        }
+        if (store) {
+          if (p.out_f32) {
+            float* o = reinterpret_cast<float*>(p.out) + obase + cc * 32;
+#pragma unroll
+            for (int c = 0; c < 32; c += 4) {
+              float4 v = make_float4(__uint_as_float(r[c]) * inv, __uint_as_float(r[c + 1]) * inv,
+                                     __uint_as_float(r[c + 2]) * inv, __uint_as_float(r[c + 3]) * inv);
+              *reinterpret_cast<float4*>(o + c) = v;
+            }
+          } else {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + obase + cc * 32;
+#pragma unroll
+            for (int c = 0; c < 32; c += 8) {
+              uint4 v;
+              v.x = pack_bf16x2(__uint_as_float(r[c]) * inv, __uint_as_float(r[c + 1]) * inv);
+              v.y = pack_bf16x2(__uint_as_float(r[c + 2]) * inv, __uint_as_float(r[c + 3]) * inv);
+              v.z = pack_bf16x2(__uint_as_float(r[c + 4]) * inv, __uint_as_float(r[c + 5]) * inv);
+              v.w = pack_bf16x2(__uint_as_float(r[c + 6]) * inv, __uint_as_float(r[c + 7]) * inv);
+              *reinterpret_cast<uint4*>(o + c) = v;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int D>
+cudaError_t launch_d(const AttnParams& p, const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                     cudaStream_t stream) {
+  using C = Cfg<D>;
+  static bool configured[128] = {};   // the attribute is set once per device
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 128 || !configured[dev]) {
+    e = cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 128) configured[dev] = true;
+  }
+  const long long blocks = (long long)p.B * p.Hq * p.q_blocks;
+  if (blocks <= 0) return cudaSuccess;
+  if (blocks > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
+  attn_fwd_kernel<D><<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, stream>>>(tmQ, tmK, tmV, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int attention_q_tiles_per_block(int D) {
+  switch (D) {
+    case 64: return Cfg<64>::NQ;
+    case 96: return Cfg<96>::NQ;
+    case 128: return Cfg<128>::NQ;
+    case 256: return Cfg<256>::NQ;
+    default: return 0;
+  }
+}
+
+int attention_block_elems(int D) {
+  switch (D) {
+    case 64: return Cfg<64>::BLK;
+    case 96: return Cfg<96>::BLK;
+    case 128: return Cfg<128>::BLK;
+    case 256: return Cfg<256>::BLK;
+    default: return 0;
+  }
+}
+
+cudaError_t launch_attention(const AttnParams& p, int D, const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                             const CUtensorMap& tmV, cudaStream_t stream) {
+  switch (D) {
+    case 64: return launch_d<64>(p, tmQ, tmK, tmV, stream);
+    case 96: return launch_d<96>(p, tmQ, tmK, tmV, stream);
+    case 128: return launch_d<128>(p, tmQ, tmK, tmV, stream);
+    case 256: return launch_d<256>(p, tmQ, tmK, tmV, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace nsa

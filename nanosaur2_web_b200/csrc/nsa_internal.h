@@ -1,0 +1,79 @@
+// Private interface between the C ABI (api.cu) and the kernels (prologue.cu, attention.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace nsa {
+
+constexpr int kTileM = 128;  // query rows per tensor-core tile (one TMEM lane per row)
+constexpr int kTileN = 128;  // keys per K/V tile
+
+// One strided input matrix: element (b, row, col) lives at ptr[b*bstride + row*ld + off + col].
+struct RowView {
+  const void* ptr;
+  int64_t ld;
+  int64_t bstride;
+  int64_t off;
+};
+
+// Prologue: raw rows -> head-major bf16 tiles [b][head][row][D] (rows padded with zeros), with the
+// optional per-head RMSNorm and split-half RoPE of the query/key rows.
+struct PrologueParams {
+  RowView q, k, v;
+  int src_f32;          // 1: fp32 input, 0: bf16 input
+  int B;                // batch elements handled (shard)
+  int b_begin;          // first batch element of the shard
+  int Lq, Lk;           // query rows, key rows per batch element
+  int Hq, Hkv, D;       // heads in the shard
+  int hq_begin, hkv_begin;
+  const float* q_w;     // [D] or null (no norm)
+  const float* k_w;     // [D] or null
+  const float* cs;      // RoPE table: cos [rope_rows][D/2] then sin at sin_off; null = no RoPE
+  int64_t sin_off;
+  int rope_rows;        // rows [0, rope_rows) of q and k get RoPE
+  float eps;
+  const int* kv_len;    // [B_total] valid keys per batch element (null: Lk)
+  __nv_bfloat16* Qs;
+  __nv_bfloat16* Ks;
+  __nv_bfloat16* Vs;
+  int Lq_pad, Lk_pad;
+};
+
+struct AttnParams {
+  int B, Hq, Hkv, group;   // shard sizes (B, Hq, Hkv) and query heads per kv head
+  int b_begin, hq_begin;   // shard origin (output and per-batch inputs are indexed globally)
+  int hkv_begin;           // first kv head held in the K/V tiles
+  int Lq, Lq_pad, Lk, Lk_pad;
+  const int* kv_len;       // [B_total] or null
+  const float* bias;       // natural-log additive key bias for keys >= bias_start, or null
+  int bias_start, bias_len;
+  int64_t bias_bstride;
+  float scale_log2;        // softmax scale * log2(e)
+  int causal, window;
+  void* out;
+  int out_f32;
+  int64_t out_ld, out_bstride, out_off;
+  int q_blocks;            // query blocks (NQ tiles each) per (b, head)
+  int* err;
+  unsigned long long timeout_ns;
+};
+
+cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream);
+
+// Returns cudaErrorInvalidValue for unsupported head dims.
+cudaError_t launch_attention(const AttnParams& p, int D, const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                             const CUtensorMap& tmV, cudaStream_t stream);
+int attention_q_tiles_per_block(int D);   // NQ: query tiles per CTA for head dim D (0: unsupported)
+int attention_block_elems(int D);         // swizzle block width (elements) of the TMA boxes
+
+cudaError_t launch_head_norm(void* X, int f32, const float* w, int L, int H, int D, int64_t ld, int64_t col_off,
+                             int64_t row_off, const float* cs, int64_t sin_off, float eps, cudaStream_t stream);
+cudaError_t launch_rope2d_table(int h, int w, int D, float* out, cudaStream_t stream);
+cudaError_t launch_rope1d_table(int L, int D, float theta, float* out, cudaStream_t stream);
+
+int* device_error_word();   // address of the library's device error word on the current device
+
+}  // namespace nsa

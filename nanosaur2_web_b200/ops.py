@@ -1,0 +1,158 @@
+"""Host-side mirror of the reference's attention operator surface (app/gpu/ops.js), over torch CUDA
+tensors, calling the sm_100a kernels of libnsattn.so through the C ABI.
+
+Names, argument meanings and error behaviour follow the JS operators:
+
+* ``attention(q=, k=, v=, Lq=, Lk=, H=, D=, ldq=, ldk=, ldv=, qOff=, kOff=, vOff=, group=, causal=,
+  bias=, biasStart=, out=)`` (app/gpu/ops.js:194-242) returns the output tensor ``[Lq, H*D]``;
+* ``headNorm(X, weight, L=, H=, D=, ld=, colOff=, rowOff=, cs=, eps=)`` (app/gpu/ops.js:131-138)
+  works in place;
+* ``rope2dTable(h, w, D)`` / ``ropeTable(L, D, theta)`` (app/models/common.js:18-43) return a table
+  object with ``buf`` (cos block then sin block) and ``sinOff``, like the JS tables.
+
+Unsupported shapes raise ``NsaError`` synchronously, as the JS operators throw.  Extensions: a batch
+dimension (3-D tensors), per-batch valid key counts ``kv_len``, a sliding ``window`` and a
+``shard=(b_begin, b_count, h_begin, h_count)`` for batch x head partitioning across GPUs.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import NSA_BF16, NSA_F32, AttentionDesc, NsaError, check, lib
+
+__all__ = ["attention", "headNorm", "rope2dTable", "ropeTable", "RopeTable", "NsaError", "dtype_code",
+           "stream_handle", "check_device"]
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return NSA_F32
+    if t.dtype == torch.bfloat16:
+        return NSA_BF16
+    raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, f"unsupported dtype {t.dtype} (float32 or bfloat16)")
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "tensors must live on a CUDA device")
+
+
+def check_device(device: Optional[torch.device] = None) -> None:
+    """Synchronise the current stream and raise NsaError if any kernel reported a device-side error
+    (the async-error surfacing of app/gpu/device.js:224-231)."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    with torch.cuda.device(dev):
+        check(lib().nsa_check_device(stream_handle(dev)))
+
+
+@dataclass
+class RopeTable:
+    """cos block [L][D/2] followed by the sin block; ``sinOff`` = L*D/2 (app/models/common.js:4-13)."""
+    buf: torch.Tensor
+    sinOff: int
+    L: int
+    D: int
+
+
+def rope2dTable(h: int, w: int, D: int, device=None) -> RopeTable:
+    """2D centred-coordinate RoPE table (app/models/common.js:28-43)."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    L = h * w
+    buf = torch.empty(L * D, dtype=torch.float32, device=device)
+    with torch.cuda.device(buf.device):
+        check(lib().nsa_rope2d_table(h, w, D, buf.data_ptr(), stream_handle(buf.device)))
+    return RopeTable(buf, L * (D // 2), L, D)
+
+
+def ropeTable(L: int, D: int, theta: float, device=None) -> RopeTable:
+    """1D RoPE table, angle(l, i) = l / theta^(2i/D) (app/models/common.js:18-24)."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    buf = torch.empty(L * D, dtype=torch.float32, device=device)
+    with torch.cuda.device(buf.device):
+        check(lib().nsa_rope1d_table(L, D, float(theta), buf.data_ptr(), stream_handle(buf.device)))
+    return RopeTable(buf, L * (D // 2), L, D)
+
+
+def headNorm(X: torch.Tensor, weight: torch.Tensor, *, L: int, H: int, D: int, ld: int, colOff: int = 0,
+             rowOff: int = 0, cs: Optional[RopeTable] = None, eps: float = 1e-6) -> None:
+    """In-place per-head RMSNorm (+ split-half RoPE with ``cs``) on L rows x H heads of D values at
+    X[(rowOff + l) * ld + colOff + h * D] (app/gpu/ops.js:131-138)."""
+    _require_cuda(X, weight)
+    if weight.dtype != torch.float32:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "norm weight must be float32")
+    with torch.cuda.device(X.device):
+        check(lib().nsa_head_norm(X.data_ptr(), dtype_code(X), weight.data_ptr(), L, H, D, ld, colOff, rowOff,
+                                  _ptr(cs.buf) if cs is not None else None, cs.sinOff if cs is not None else 0,
+                                  float(eps), stream_handle(X.device)))
+
+
+def _bstride(t: torch.Tensor, rows_ld: int) -> int:
+    return t.stride(0) if t.dim() == 3 else 0
+
+
+def attention(*, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, Lq: int, Lk: int, H: int, D: int,
+              ldq: int, ldk: int, ldv: int, qOff: int = 0, kOff: int = 0, vOff: int = 0, group: int = 1,
+              causal: bool = False, bias: Optional[torch.Tensor] = None, biasStart: int = 0,
+              out: Optional[torch.Tensor] = None, window: int = 0, kv_len: Optional[torch.Tensor] = None,
+              out_dtype: Optional[torch.dtype] = None, scale: float = 0.0, shard=None) -> torch.Tensor:
+    """Multi-head attention (app/gpu/ops.js:194-242).
+
+    q: [Lq, ldq] (or [B, Lq, ldq]) with head h at column qOff + h*D; k, v: [Lk, ldk] / [Lk, ldv] with kv
+    head h // group at kOff / vOff + (h // group) * D; bias: [biasLen] (or [B, biasLen]) additive
+    score bias for keys biasStart..; out: [Lq, H*D] (or [B, Lq, H*D]), allocated when not given.
+    """
+    _require_cuda(q, k, v, bias, out, kv_len)
+    B = q.shape[0] if q.dim() == 3 else 1
+    if out is None:
+        odt = out_dtype or (torch.float32 if q.dtype == torch.float32 else torch.bfloat16)
+        shape = (B, Lq, H * D) if q.dim() == 3 else (Lq, H * D)
+        out = torch.empty(shape, dtype=odt, device=q.device)
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "q, k and v must share a dtype")
+    if kv_len is not None and kv_len.dtype != torch.int32:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "kv_len must be int32")
+    if bias is not None and bias.dtype != torch.float32:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "bias must be float32")
+    d = AttentionDesc()
+    d.Lq, d.Lk, d.H, d.D = Lq, Lk, H, D
+    d.ldq, d.ldk, d.ldv = ldq, ldk, ldv
+    d.qOff, d.kOff, d.vOff = qOff, kOff, vOff
+    d.group, d.causal, d.window = group, int(bool(causal)), window
+    d.biasStart = biasStart
+    d.biasLen = 0 if bias is None else bias.shape[-1]
+    d.B = B
+    d.q_bstride, d.k_bstride, d.v_bstride = _bstride(q, ldq), _bstride(k, ldk), _bstride(v, ldv)
+    d.bias_bstride = bias.stride(0) if (bias is not None and bias.dim() == 2) else 0
+    d.o_bstride = out.stride(0) if out.dim() == 3 else 0
+    d.ldo = out.stride(-2)
+    d.oOff = 0
+    d.in_dtype, d.out_dtype = dtype_code(q), dtype_code(out)
+    d.scale = scale
+    if shard is not None:
+        d.b_begin, d.b_count, d.h_begin, d.h_count = shard
+    L = lib()
+    ws_bytes = L.nsa_attention_workspace_size(ctypes.byref(d))
+    if ws_bytes == 0:
+        # re-run through the entry point to surface the validation message
+        check(L.nsa_attention(ctypes.byref(d), q.data_ptr(), k.data_ptr(), v.data_ptr(), None, None,
+                              out.data_ptr(), None, 0, None))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    with torch.cuda.device(q.device):
+        check(L.nsa_attention(ctypes.byref(d), q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(bias), _ptr(kv_len),
+                              out.data_ptr(), ws.data_ptr(), ws_bytes, stream_handle(q.device)))
+    return out

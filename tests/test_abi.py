@@ -1,0 +1,100 @@
+"""The C ABI library loads without a GPU, exports every entry point include/nsattn.h declares, its
+ctypes mirror matches the C struct layouts, and argument validation fails with the documented
+status codes before any CUDA call."""
+
+import ctypes
+import os
+import re
+import shutil
+import subprocess
+
+import pytest
+
+from nanosaur2_web_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "nsattn.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(nsa_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_and_binding_agree():
+    assert declared_functions() == sorted(_lib.SIGNATURES)
+
+
+def test_library_exports_every_symbol():
+    L = _lib.lib()
+    for name in declared_functions():
+        assert hasattr(L, name), name
+    assert _lib.version().startswith("nsattn")
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True).stdout
+    exported = set(re.findall(r" T (nsa_\w+)", out))
+    assert set(declared_functions()) <= exported
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs gcc")
+def test_struct_layouts_match_c(tmp_path):
+    src = tmp_path / "sizes.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "nsattn.h"\n'
+                   'int main(){printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(nsa_attention_desc),'
+                   'offsetof(nsa_attention_desc, b_begin), sizeof(nsa_fused_desc), offsetof(nsa_fused_desc, b_begin),'
+                   'sizeof(nsa_kernel_stat), offsetof(nsa_kernel_stat, bytes));return 0;}\n')
+    exe = tmp_path / "sizes"
+    subprocess.run(["gcc", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
+    want = [ctypes.sizeof(_lib.AttentionDesc), _lib.AttentionDesc.b_begin.offset, ctypes.sizeof(_lib.FusedDesc),
+            _lib.FusedDesc.b_begin.offset, ctypes.sizeof(_lib.KernelStat), _lib.KernelStat.bytes.offset]
+    assert got == want
+
+
+def _desc(**kw):
+    d = _lib.AttentionDesc()
+    base = dict(Lq=64, Lk=64, H=2, D=96, ldq=192, ldk=192, ldv=192, group=1, B=1, ldo=192,
+                in_dtype=_lib.NSA_BF16, out_dtype=_lib.NSA_F32)
+    base.update(kw)
+    for k, v in base.items():
+        setattr(d, k, v)
+    return d
+
+
+def test_validation_without_gpu():
+    L = _lib.lib()
+    assert L.nsa_attention(None, None, None, None, None, None, None, None, 0, None) == _lib.NSA_ERR_INVALID_ARGUMENT
+    assert b"desc" in L.nsa_last_error()
+    fake = 0x10000   # never dereferenced: validation fails first
+    cases = [
+        (_desc(D=80), _lib.NSA_ERR_UNSUPPORTED),
+        (_desc(H=3, group=2), _lib.NSA_ERR_INVALID_ARGUMENT),
+        (_desc(in_dtype=7), _lib.NSA_ERR_INVALID_ARGUMENT),
+        (_desc(causal=1, Lq=65, Lk=64), _lib.NSA_ERR_INVALID_ARGUMENT),
+        (_desc(h_begin=2), _lib.NSA_ERR_INVALID_ARGUMENT),
+        (_desc(ldo=190), _lib.NSA_ERR_INVALID_ARGUMENT),
+    ]
+    for d, want in cases:
+        st = L.nsa_attention(ctypes.byref(d), fake, fake, fake, None, None, fake, None, 0, None)
+        assert st == want, (st, want, L.nsa_last_error())
+    assert L.nsa_head_norm(None, 0, None, 1, 1, 96, 96, 0, 0, None, 0, 1e-6, None) == _lib.NSA_ERR_INVALID_ARGUMENT
+    assert L.nsa_rope2d_table(4, 4, 94, fake, None) == _lib.NSA_ERR_INVALID_ARGUMENT
+    assert L.nsa_selftest_wait_timeout(0, None) == _lib.NSA_ERR_INVALID_ARGUMENT
+    assert L.nsa_status_string(_lib.NSA_ERR_DEVICE) == b"device-side error"
+
+
+def test_workspace_sizes():
+    L = _lib.lib()
+    d = _desc(Lq=3952, Lk=4208, H=16, D=96, B=2)
+    ws = L.nsa_attention_workspace_size(ctypes.byref(d))
+    lq_pad, lk_pad = 4096, 4224   # query blocks of 2x128 rows, key tiles of 128
+    want = 2 * 16 * lq_pad * 96 * 2 + 2 * (2 * 16 * lk_pad * 96 * 2) + 1024
+    assert ws == want
+    d.h_begin, d.h_count = 4, 4
+    assert L.nsa_attention_workspace_size(ctypes.byref(d)) == (want - 1024) // 4 + 1024
+    f = _lib.FusedDesc()
+    f.B, f.Lq, f.Lk, f.Hq, f.Hkv, f.D, f.causal = 16, 1024, 1024, 4, 1, 256, 1
+    wsf = L.nsa_fused_attention_workspace_size(ctypes.byref(f))
+    assert wsf == 16 * 4 * 1024 * 256 * 2 + 2 * 16 * 1 * 1024 * 256 * 2 + 1024
+    f.D = 100
+    assert L.nsa_fused_attention_workspace_size(ctypes.byref(f)) == 0

@@ -1,0 +1,321 @@
+"""Parity of the sm_100a CUDA path (through the C ABI) with the reference's fp32 attention.
+
+Golden fixtures (tests/golden/*.npz, captured from the reference's own DiT and Gemma code) are run
+through the fused entry points and compared with the reference output; larger seeded cases with
+the benchmark configs' shapes are compared with the CPU oracle (oracle/attention_oracle.py, itself
+pinned by tests/test_oracle_golden.py).  Tolerance of the bf16 path: max-abs <= 2e-2 and per-head
+cosine >= 0.9999.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention_oracle as O
+from tests._helpers import assert_close_bf16, bf16_round, gemma_inputs, joint_inputs
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib_loaded():
+    torch.cuda.set_device(DEV)
+    from nanosaur2_web_b200 import _lib
+    _lib.lib()
+    yield
+    torch.cuda.synchronize()
+
+
+def t(x, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(device=DEV, dtype=dtype)
+
+
+def table_from(cos, sin):
+    from nanosaur2_web_b200.ops import RopeTable
+    L, half = cos.shape
+    return RopeTable(t(np.concatenate([cos.reshape(-1), sin.reshape(-1)])), L * half, L, 2 * half)
+
+
+def check_device():
+    from nanosaur2_web_b200.ops import check_device as cd
+    cd(DEV)
+
+
+# ----------------------------------------------------------------------------- tables and prologue
+
+def test_rope2d_table_matches_oracle():
+    from nanosaur2_web_b200.ops import rope2dTable
+    for (h, w) in ((76, 52), (48, 48), (7, 5)):
+        tab = rope2dTable(h, w, 96, DEV)
+        cos, sin = O.rope_2d(h, w)
+        buf = tab.buf.cpu().numpy()
+        np.testing.assert_allclose(buf[: tab.sinOff].reshape(cos.shape), cos, atol=2e-6, rtol=0)
+        np.testing.assert_allclose(buf[tab.sinOff:].reshape(sin.shape), sin, atol=2e-6, rtol=0)
+
+
+def test_rope1d_table_matches_oracle(golden):
+    from nanosaur2_web_b200.ops import ropeTable
+    g = golden("tables")
+    for theta, name in ((1e4, "local"), (1e6, "global")):
+        tab = ropeTable(40, 256, theta, DEV)
+        buf = tab.buf.cpu().numpy()
+        np.testing.assert_allclose(buf[: tab.sinOff].reshape(40, 128), g[f"rope1d_{name}_cos"], atol=2e-6, rtol=0)
+        np.testing.assert_allclose(buf[tab.sinOff:].reshape(40, 128), g[f"rope1d_{name}_sin"], atol=2e-6, rtol=0)
+        tab = ropeTable(1024, 256, theta, DEV)
+        cos, sin = O.rope_1d(1024, theta)
+        buf = tab.buf.cpu().numpy()
+        np.testing.assert_allclose(buf[: tab.sinOff].reshape(cos.shape), cos, atol=2e-6, rtol=0)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_head_norm_in_place(dtype):
+    """ops.headNorm on the DiT's packed layout: image q with RoPE, then text k rows without."""
+    from nanosaur2_web_b200.ops import headNorm, rope2dTable
+    rng = np.random.default_rng(5)
+    h, w, Lt = 6, 7, 9
+    L = h * w
+    x = bf16_round(rng.standard_normal((L + Lt, 4608), dtype=np.float32) * 2)
+    wq = (1 + 0.3 * rng.standard_normal(96)).astype(np.float32)
+    X = t(x, dtype)
+    cs = rope2dTable(h, w, 96, DEV)
+    headNorm(X, t(wq), L=L, H=16, D=96, ld=4608, colOff=0, cs=cs)
+    headNorm(X, t(wq), L=Lt, H=16, D=96, ld=4608, colOff=1536, rowOff=L)
+    got = X.float().cpu().numpy()
+    cos, sin = O.rope_2d(h, w)
+    want = x.copy()
+    want[:L, :1536] = O.head_norm(x[:L, :1536], wq, 16, 96, cos, sin)
+    want[L:, 1536:3072] = O.head_norm(x[L:, 1536:3072], wq, 16, 96)
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    np.testing.assert_allclose(got, want, atol=tol, rtol=tol)
+
+
+# ----------------------------------------------------------------------------- failure surfacing
+
+def test_selftest_wait_timeout_reports_device_error():
+    from nanosaur2_web_b200 import _lib
+    from nanosaur2_web_b200.ops import stream_handle
+    L = _lib.lib()
+    check_device()   # clean slate
+    _lib.check(L.nsa_selftest_wait_timeout(2000, stream_handle(DEV)))
+    with pytest.raises(_lib.NsaError) as ei:
+        check_device()
+    assert ei.value.status == _lib.NSA_ERR_DEVICE
+    check_device()   # the word was cleared and the context is still usable
+    x = torch.ones(4, device=DEV) * 2
+    assert float(x.sum()) == 8.0
+
+
+def test_invalid_arguments_raise():
+    from nanosaur2_web_b200 import _lib
+    from nanosaur2_web_b200.ops import attention
+    q = torch.zeros(8, 80, device=DEV)
+    with pytest.raises(_lib.NsaError) as ei:
+        attention(q=q, k=q, v=q, Lq=8, Lk=8, H=1, D=80, ldq=80, ldk=80, ldv=80)
+    assert ei.value.status == _lib.NSA_ERR_UNSUPPORTED
+    q = torch.zeros(8, 96, device=DEV)
+    with pytest.raises(_lib.NsaError) as ei:
+        attention(q=q, k=q, v=q, Lq=8, Lk=8, H=3, D=96, ldq=96, ldk=96, ldv=96, group=2)
+    assert ei.value.status == _lib.NSA_ERR_INVALID_ARGUMENT
+
+
+# ----------------------------------------------------------------------------- golden fixtures
+
+def _joint_from_fixture(g, with_text=True):
+    L = g["q_raw"].shape[0]
+    Lt = g["ky_raw"].shape[0] if with_text else 0
+    qkv = np.zeros((1, L + Lt, 4608), np.float32)
+    qkv[0, :L, :1536], qkv[0, :L, 1536:3072], qkv[0, :L, 3072:] = g["q_raw"], g["k_raw"], g["v"]
+    if with_text:
+        qkv[0, L:, 1536:3072], qkv[0, L:, 3072:] = g["ky_raw"], g["vy"]
+    return qkv, L, Lt
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_golden_dit_joint_block(golden, out_dtype):
+    from nanosaur2_web_b200.blocks import dit_block_attention
+    from nanosaur2_web_b200.ops import rope2dTable
+    g = golden("dit_joint_block")
+    qkv, L, Lt = _joint_from_fixture(g)
+    assert np.array_equal(bf16_round(qkv), qkv)   # the fixture's projections are bf16-exact
+    cs = rope2dTable(int(g["h"]), int(g["w"]), 96, DEV)
+    out = dit_block_attention(t(qkv, torch.bfloat16), L=L, text_rows=Lt, q_norm=t(g["q_w"]), k_norm=t(g["k_w"]),
+                              cs=cs, kv_len=t(np.array([L + Lt], np.int32), torch.int32),
+                              bias=t(g["txt_bias"][None]), out_dtype=out_dtype)
+    check_device()
+    assert_close_bf16(out[0].float().cpu().numpy(), g["out"], 96, what="joint block")
+    # same call with the w <= 0 text rows dropped through kv_len instead of a -inf bias
+    valid = int(np.sum(g["txt_weights"] > 0))
+    out2 = dit_block_attention(t(qkv, torch.bfloat16), L=L, text_rows=Lt, q_norm=t(g["q_w"]), k_norm=t(g["k_w"]),
+                               cs=cs, kv_len=t(np.array([L + valid], np.int32), torch.int32),
+                               bias=t(g["txt_bias"][None]), out_dtype=out_dtype)
+    check_device()
+    assert_close_bf16(out2[0].float().cpu().numpy(), g["out"], 96, what="joint block, kv_len")
+
+
+def test_golden_dit_image_block(golden):
+    from nanosaur2_web_b200.blocks import dit_block_attention
+    from nanosaur2_web_b200.ops import rope2dTable
+    g = golden("dit_image_block")
+    qkv, L, _ = _joint_from_fixture(g, with_text=False)
+    cs = rope2dTable(int(g["h"]), int(g["w"]), 96, DEV)
+    out = dit_block_attention(t(qkv, torch.bfloat16), L=L, q_norm=t(g["q_w"]), k_norm=t(g["k_w"]), cs=cs,
+                              out_dtype=torch.float32)
+    check_device()
+    assert_close_bf16(out[0].cpu().numpy(), g["out"], 96, what="image block")
+
+
+def test_golden_text_refine(golden):
+    from nanosaur2_web_b200.blocks import dit_block_attention
+    g = golden("dit_text_refine")
+    Lt = g["q_raw"].shape[0]
+    qkv = np.concatenate([g["q_raw"], g["k_raw"], g["v"]], axis=1)[None]
+    out = dit_block_attention(t(qkv, torch.bfloat16), L=Lt, q_norm=t(g["q_w"]), k_norm=t(g["k_w"]), cs=None,
+                              bias=t(g["keep_bias"][None]), out_dtype=torch.float32)
+    check_device()
+    assert_close_bf16(out[0].cpu().numpy(), g["out"], 96, what="text refine")
+
+
+@pytest.mark.parametrize("layer", [0, 5])
+def test_golden_gemma_layer(golden, layer):
+    from nanosaur2_web_b200.blocks import gemma_layer_attention
+    from nanosaur2_web_b200.ops import ropeTable
+    g = golden(f"gemma_layer{layer}")
+    L = g["q_raw"].shape[0]
+    qkv = np.concatenate([g["q_raw"], g["k_raw"], g["v"]], axis=1)[None].astype(np.float32)
+    cs = ropeTable(L, 256, float(g["theta"]), DEV)
+    for dtype in (torch.float32, torch.bfloat16):
+        out = gemma_layer_attention(t(qkv, dtype), q_norm=t(g["q_w"] + 1.0), k_norm=t(g["k_w"] + 1.0), cs=cs,
+                                    out_dtype=torch.float32)
+        check_device()
+        assert_close_bf16(out[0].cpu().numpy(), g["out"], 256, what=f"gemma layer {layer} {dtype}")
+
+
+# ----------------------------------------------------------------------------- seeded, config-sized
+
+def _run_joint(qkv, L, Lt, q_w, k_w, lv, bias, h, w, in_dtype=torch.bfloat16, out_dtype=torch.float32, shard=None,
+               out=None):
+    from nanosaur2_web_b200.blocks import dit_block_attention
+    from nanosaur2_web_b200.ops import rope2dTable
+    cs = rope2dTable(h, w, 96, DEV)
+    kv_len = t((L + lv).astype(np.int32), torch.int32)
+    return dit_block_attention(t(qkv, in_dtype), L=L, text_rows=Lt, q_norm=t(q_w), k_norm=t(k_w), cs=cs,
+                               kv_len=kv_len, bias=t(bias) if bias is not None else None, out_dtype=out_dtype,
+                               shard=shard, out=out)
+
+
+def _oracle_joint(qkv, L, Lt, q_w, k_w, lv, bias, h, w, heads):
+    cos, sin = O.rope_2d(h, w)
+    return O.joint_attention_batched(qkv, L, Lt, L + lv, q_w, k_w, cos, sin, bias=bias, acc=np.float64, heads=heads)
+
+
+def _cmp_heads(got, want, heads, D=96, what=""):
+    cols = np.concatenate([np.arange(hh * D, (hh + 1) * D) for hh in heads])
+    assert_close_bf16(got[..., cols], want[..., cols], D, what=what)
+
+
+def test_config1_shape_fp32_inputs():
+    """48x48 image tokens + 128 text slots (valid length in [20, 128]), fp32 inputs."""
+    h = w = 48
+    qkv, q_w, k_w, lv, bias = joint_inputs(11, 1, h, w, 128, (20, 128), bf16=False)
+    L = h * w
+    out = _run_joint(qkv, L, 128, q_w, k_w, lv, bias, h, w, in_dtype=torch.float32)
+    check_device()
+    heads = [0, 7, 15]
+    want = _oracle_joint(qkv, L, 128, q_w, k_w, lv, bias, h, w, heads)
+    _cmp_heads(out.cpu().numpy(), want, heads, what="config 1")
+
+
+def test_config2_shape_bf16():
+    """52x76 (w x h) image tokens + 256 text slots, batch 2, bf16."""
+    h, w = 76, 52
+    qkv, q_w, k_w, lv, bias = joint_inputs(22, 2, h, w, 256, (32, 256))
+    L = h * w
+    out = _run_joint(qkv, L, 256, q_w, k_w, lv, bias, h, w, out_dtype=torch.bfloat16)
+    check_device()
+    heads = [3, 12]
+    want = _oracle_joint(qkv, L, 256, q_w, k_w, lv, bias, h, w, heads)
+    _cmp_heads(out.float().cpu().numpy(), want, heads, what="config 2")
+
+
+@pytest.mark.parametrize("hw,Lt,lv", [((1, 5), 8, (1, 1)), ((10, 13), 40, (0, 0)), ((16, 16), 64, (64, 64)),
+                                      ((3, 43), 300, (1, 300))])
+def test_joint_edge_shapes(hw, Lt, lv):
+    """Ragged tiles: Lq below / not a multiple of 128, one valid text token, no valid text, all text
+    valid, more text than one key tile."""
+    h, w = hw
+    L = h * w
+    qkv, q_w, k_w, lvs, bias = joint_inputs(33 + L, 2, h, w, Lt, lv)
+    out = _run_joint(qkv, L, Lt, q_w, k_w, lvs, bias, h, w)
+    check_device()
+    heads = list(range(16))
+    want = _oracle_joint(qkv, L, Lt, q_w, k_w, lvs, bias, h, w, heads)
+    _cmp_heads(out.cpu().numpy(), want, heads, what=f"edge {hw} {Lt} {lv}")
+
+
+def test_shards_reproduce_full_run():
+    """Batch x head shards write exactly their slice of the output, identical to the full run."""
+    h, w = 12, 20
+    L = h * w
+    qkv, q_w, k_w, lv, bias = joint_inputs(44, 2, h, w, 64, (10, 64))
+    full = _run_joint(qkv, L, 64, q_w, k_w, lv, bias, h, w).cpu().numpy()
+    from nanosaur2_web_b200.sharding import shard_batch_heads
+    for world in (2, 3, 8):
+        out = torch.full((2, L, 1536), float("nan"), device=DEV)
+        for rank in range(world):
+            for shard in shard_batch_heads(2, 16, world, rank):
+                _run_joint(qkv, L, 64, q_w, k_w, lv, bias, h, w, shard=shard, out=out)
+        check_device()
+        np.testing.assert_array_equal(out.cpu().numpy(), full)
+
+
+@pytest.mark.parametrize("theta,window", [(1e6, 0), (1e4, 512), (1e4, 100)])
+def test_gemma_config4_shape(theta, window):
+    """BASELINE config 4 shape (L=1024, GQA 4/1, D=256), global and local (window) layers."""
+    from nanosaur2_web_b200.blocks import gemma_layer_attention
+    from nanosaur2_web_b200.ops import ropeTable
+    B, L = 2, 1024
+    qkv, q_w, k_w = gemma_inputs(55, B, L)
+    cs = ropeTable(L, 256, theta, DEV)
+    out = gemma_layer_attention(t(qkv, torch.bfloat16), q_norm=t(q_w), k_norm=t(k_w), cs=cs, window=window,
+                                out_dtype=torch.float32).cpu().numpy()
+    check_device()
+    for b in range(B):
+        want = O.gemma_attention(qkv[b, :, :1024], qkv[b, :, 1024:1280], qkv[b, :, 1280:], q_w, k_w, theta,
+                                 window=window, acc=np.float64)
+        assert_close_bf16(out[b], want, 256, what=f"gemma theta={theta} window={window} b={b}")
+
+
+@pytest.mark.parametrize("D,H,group,causal,Lq,Lk", [(64, 4, 1, False, 300, 257), (128, 4, 2, False, 200, 333),
+                                                     (96, 2, 1, True, 260, 260), (256, 2, 2, True, 129, 129)])
+def test_generic_attention_op(D, H, group, causal, Lq, Lk):
+    """ops.attention mirror (app/gpu/ops.js:199) with pre-normalised fp32 q/k/v, GQA and causal."""
+    from nanosaur2_web_b200.ops import attention
+    rng = np.random.default_rng(D + Lq)
+    Hk = H // group
+    q = rng.standard_normal((Lq, H * D), dtype=np.float32)
+    kv = rng.standard_normal((Lk, 2 * Hk * D), dtype=np.float32)
+    out = attention(q=t(q), k=t(kv), v=t(kv), Lq=Lq, Lk=Lk, H=H, D=D, ldq=H * D, ldk=2 * Hk * D, ldv=2 * Hk * D,
+                    kOff=0, vOff=Hk * D, group=group, causal=causal)
+    check_device()
+    assert out.dtype == torch.float32 and out.shape == (Lq, H * D)
+    want = O.attention(q, kv[:, : Hk * D], kv[:, Hk * D:], H, D, group=group, causal=causal, acc=np.float64)
+    assert_close_bf16(out.cpu().numpy(), want, D, what=f"generic D={D}")
+
+
+def test_reference_call_shape_fp32():
+    """The exact call of app/models/nanosaur2.js:205-208 on an fp32 qkv buffer: q = k = v = qkv,
+    ld 4608, offsets 0/1536/3072, bias on the text keys from biasStart = L."""
+    from nanosaur2_web_b200.ops import attention
+    rng = np.random.default_rng(7)
+    L, Lt = 300, 17
+    qkv = rng.standard_normal((L + Lt, 4608), dtype=np.float32)
+    bias = np.log(rng.choice(np.array([0.7, 1.3], np.float32), size=Lt)).astype(np.float32)
+    Q = t(qkv)
+    out = attention(q=Q, k=Q, v=Q, Lq=L, Lk=L + Lt, H=16, D=96, ldq=4608, ldk=4608, ldv=4608, qOff=0, kOff=1536,
+                    vOff=3072, bias=t(bias), biasStart=L)
+    check_device()
+    want = O.attention(qkv[:L, :1536], qkv[:, 1536:3072], qkv[:, 3072:], 16, 96,
+                       bias=np.concatenate([np.zeros(L, np.float32), bias]), acc=np.float64)
+    assert_close_bf16(out.cpu().numpy(), want, 96, what="reference call shape")

@@ -1,0 +1,51 @@
+"""Host-side logic that needs no GPU: work partitioning, the text-bias preparation, the Gemma layer
+schedule and the bench's algorithmic FLOP count."""
+
+import math
+
+import numpy as np
+import pytest
+
+from nanosaur2_web_b200 import blocks, sharding
+from oracle import attention_oracle as O
+
+
+@pytest.mark.parametrize("B,H", [(2, 16), (8, 16), (16, 4), (1, 16), (4, 16)])
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_shards_cover_units_once(B, H, world):
+    seen = []
+    for rank in range(world):
+        for b0, bc, h0, hc in sharding.shard_batch_heads(B, H, world, rank):
+            assert bc >= 1 and hc >= 1 and h0 + hc <= H and b0 + bc <= B
+            assert bc == 1 or (h0 == 0 and hc == H)
+            seen += [(b, h) for b in range(b0, b0 + bc) for h in range(h0, h0 + hc)]
+    assert sorted(seen) == [(b, h) for b in range(B) for h in range(H)]
+
+
+def test_split_range_balanced():
+    sizes = [sharding.split_range(10, 4, r) for r in range(4)]
+    assert sizes == [(0, 3), (3, 6), (6, 8), (8, 10)]
+    with pytest.raises(ValueError):
+        sharding.split_range(10, 0, 0)
+
+
+def test_prepare_text_bias_matches_reference_bias():
+    w = [1.0, 1.3, 0.0, 0.7, -1.0, 1.0]
+    keep, bias = blocks.prepare_text_bias(w)
+    assert keep == [0, 1, 3, 5]
+    ref = O.text_key_bias(w)
+    np.testing.assert_allclose(bias, ref[keep], rtol=1e-6)
+    assert blocks.prepare_text_bias([1.0, 1.0, 0.0]) == ([0, 1], None)
+
+
+def test_gemma_schedule():
+    assert [blocks.gemma_rope_theta(i) for i in range(18)] == [O.gemma_rope_theta(i) for i in range(18)]
+    assert sum(blocks.gemma_rope_theta(i) == 1e6 for i in range(18)) == 3
+
+
+def test_bench_flop_counts():
+    import bench
+    assert math.isclose(bench.joint_flops(2, 3952, [256, 256]), 204.35e9, rel_tol=1e-3)
+    assert math.isclose(bench.joint_flops(1, 2304, [128]), 34.43e9, rel_tol=1e-3)
+    g, l = bench.gemma_pairs(1024, 0), bench.gemma_pairs(1024, 512)
+    assert g == 524800 and l == 393472
