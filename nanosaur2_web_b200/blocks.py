@@ -5,8 +5,9 @@
 * ``dit_block_attention(...)``: one DiT block's attention step over the packed qkv buffer,
   headNorm(q, 2D rope) + headNorm(k, 2D rope) + headNorm(text k) + attention(bias, biasStart = L)
   (app/models/nanosaur2.js:196-208; tools/reference.py:272-286).  Also covers the odd, image-only
-  blocks (no text rows) and the text-refine blocks (no RoPE, all rows are queries,
-  app/models/nanosaur2.js:128-132).
+  blocks (no text rows).
+* ``text_refine_attention(...)``: the text-refine blocks' attention (no RoPE, every text row is a
+  query, app/models/nanosaur2.js:128-132; tools/reference.py:258-259).
 * ``gemma_layer_attention(...)``: one Gemma3 layer's attention, headNorm(q), headNorm(k) with the
   local/global RoPE table + causal GQA 4/1 attention (app/models/gemma3.js:63-70;
   tools/reference.py:186-194), with an optional sliding window.
@@ -116,12 +117,28 @@ def dit_block_attention(qkv: torch.Tensor, *, L: int, q_norm: torch.Tensor, k_no
                         workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """qkv: [B, L + text_rows, 3*1536] with rows [0, L) image q|k|v and rows [L, L+text_rows) text k|v
     (app/models/nanosaur2.js:194-202).  kv_len[b] = L + valid text rows; bias: [B, text_rows] log prompt
-    weights of the text keys (biasStart = L).  With cs = None and text_rows = 0 this is the text-refine
-    attention (app/models/nanosaur2.js:130-132).  Returns [B, L, 1536]."""
+    weights of the text keys (biasStart = L).  With text_rows = 0 this is an odd, image-only block.
+    Returns [B, L, 1536]."""
     C = DIT_HEADS * DIT_HEAD_DIM
     return _fused(qkv, Lq=L, Lk=L + text_rows, Hq=DIT_HEADS, Hkv=DIT_HEADS, D=DIT_HEAD_DIM, qOff=0, kOff=C,
                   vOff=2 * C, q_norm=q_norm, k_norm=k_norm, cs=cs, kv_len=kv_len, bias=bias, biasStart=L,
                   causal=False, window=0, eps=eps, out=out, out_dtype=out_dtype, shard=shard, workspace=workspace)
+
+
+def text_refine_attention(qkv: torch.Tensor, *, q_norm: torch.Tensor, k_norm: torch.Tensor,
+                          keep_bias: Optional[torch.Tensor] = None, kv_len: Optional[torch.Tensor] = None,
+                          eps: float = 1e-6, out: Optional[torch.Tensor] = None,
+                          out_dtype: Optional[torch.dtype] = None, shard=None,
+                          workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Attention of a text-refine block (app/models/nanosaur2.js:128-132; tools/reference.py:258-259):
+    qkv [B, Lt, 3*1536], q/k RMSNorm without RoPE, every text row is a query and a key.  Dropped
+    tokens are masked either by ``keep_bias`` [B, Lt] (0 / -inf on every key, the reference's
+    keep_bias) or by ``kv_len`` (the JS path compacts the kept tokens to the front)."""
+    C = DIT_HEADS * DIT_HEAD_DIM
+    Lt = qkv.shape[1]
+    return _fused(qkv, Lq=Lt, Lk=Lt, Hq=DIT_HEADS, Hkv=DIT_HEADS, D=DIT_HEAD_DIM, qOff=0, kOff=C, vOff=2 * C,
+                  q_norm=q_norm, k_norm=k_norm, cs=None, kv_len=kv_len, bias=keep_bias, biasStart=0, causal=False,
+                  window=0, eps=eps, out=out, out_dtype=out_dtype, shard=shard, workspace=workspace)
 
 
 def gemma_layer_attention(qkv: torch.Tensor, *, q_norm: torch.Tensor, k_norm: torch.Tensor, cs: RopeTable,

@@ -50,9 +50,12 @@ def rope_split_half(x, cos, sin, acc=np.float32):
 
 
 def inv_freq(D, theta):
-    """1 / theta^(2i/D) for i < D/2, in fp32 (app/models/common.js:15; tools/reference.py:170,222)."""
-    e = (np.arange(0, D, 2, dtype=np.float32) / np.float32(D)).astype(np.float32)
-    return (np.float32(1.0) / np.power(np.float32(theta), e, dtype=np.float32)).astype(np.float32)
+    """1 / theta^(2i/D) for i < D/2, rounded to fp32 the way app/models/common.js:15 does it: the
+    exponent 2i/D is rounded to fp32, the power and reciprocal are taken in double precision and the
+    result is rounded to fp32.  (tools/reference.py:170,222 takes the power in fp32; the two differ
+    by at most one fp32 ulp.)"""
+    e = (np.arange(0, D, 2, dtype=np.float64) / D).astype(np.float32).astype(np.float64)
+    return (1.0 / np.power(np.float64(theta), e)).astype(np.float32)
 
 
 def rope_2d(h, w, head_dim=DIT_HEAD_DIM):

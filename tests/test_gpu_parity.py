@@ -167,14 +167,22 @@ def test_golden_dit_image_block(golden):
 
 
 def test_golden_text_refine(golden):
-    from nanosaur2_web_b200.blocks import dit_block_attention
+    from nanosaur2_web_b200.blocks import text_refine_attention
     g = golden("dit_text_refine")
     Lt = g["q_raw"].shape[0]
     qkv = np.concatenate([g["q_raw"], g["k_raw"], g["v"]], axis=1)[None]
-    out = dit_block_attention(t(qkv, torch.bfloat16), L=Lt, q_norm=t(g["q_w"]), k_norm=t(g["k_w"]), cs=None,
-                              bias=t(g["keep_bias"][None]), out_dtype=torch.float32)
+    out = text_refine_attention(t(qkv, torch.bfloat16), q_norm=t(g["q_w"]), k_norm=t(g["k_w"]),
+                                keep_bias=t(g["keep_bias"][None]), out_dtype=torch.float32)
     check_device()
     assert_close_bf16(out[0].cpu().numpy(), g["out"], 96, what="text refine")
+    # the JS path instead compacts the kept tokens to the front and attends over them only
+    keep = np.isfinite(g["keep_bias"])
+    n = int(keep.sum())
+    assert np.all(keep[:n])
+    out2 = text_refine_attention(t(qkv, torch.bfloat16), q_norm=t(g["q_w"]), k_norm=t(g["k_w"]),
+                                 kv_len=t(np.array([n], np.int32), torch.int32), out_dtype=torch.float32)
+    check_device()
+    assert_close_bf16(out2[0].cpu().numpy(), g["out"], 96, what="text refine, kv_len")
 
 
 @pytest.mark.parametrize("layer", [0, 5])
@@ -186,7 +194,9 @@ def test_golden_gemma_layer(golden, layer):
     qkv = np.concatenate([g["q_raw"], g["k_raw"], g["v"]], axis=1)[None].astype(np.float32)
     cs = ropeTable(L, 256, float(g["theta"]), DEV)
     for dtype in (torch.float32, torch.bfloat16):
-        out = gemma_layer_attention(t(qkv, dtype), q_norm=t(g["q_w"] + 1.0), k_norm=t(g["k_w"] + 1.0), cs=cs,
+        # the fixture records the norm weights as the reference hands them to rms_norm, already
+        # lifted by +1 (tools/reference.py:185)
+        out = gemma_layer_attention(t(qkv, dtype), q_norm=t(g["q_w"]), k_norm=t(g["k_w"]), cs=cs,
                                     out_dtype=torch.float32)
         check_device()
         assert_close_bf16(out[0].cpu().numpy(), g["out"], 256, what=f"gemma layer {layer} {dtype}")
