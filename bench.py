@@ -370,6 +370,33 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_profile(args, local_rank):
+    """Small driver for ncu captures: the same fused call as the benchmark on ``--batch`` elements of
+    config 2, ``--warmup`` + ``--steps`` launches of each kernel, nothing else on the GPU."""
+    import torch
+
+    from nanosaur2_web_b200.blocks import dit_block_attention
+    from nanosaur2_web_b200.ops import check_device, rope2dTable
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L = IMG_H * IMG_W
+    qkv, q_w, k_w, lv, bias = make_inputs(99, args.batch)
+    x = torch.from_numpy(qkv).to(dev, torch.bfloat16)
+    kv_len = torch.from_numpy((L + lv).astype(np.int32)).to(dev)
+    b = torch.from_numpy(bias).to(dev)
+    qn, kn = torch.from_numpy(q_w).to(dev), torch.from_numpy(k_w).to(dev)
+    cs = rope2dTable(IMG_H, IMG_W, D, dev)
+    out = torch.empty((args.batch, L, C), dtype=torch.bfloat16, device=dev)
+    for _ in range(args.warmup + args.steps):
+        dit_block_attention(x, L=L, text_rows=LT, q_norm=qn, k_norm=kn, cs=cs, kv_len=kv_len, bias=b, out=out)
+    torch.cuda.synchronize()
+    check_device(dev)
+    flops = joint_flops(args.batch, L, lv)
+    print(json.dumps({"profile_run": "ok", "batch": args.batch, "flops_per_call": flops,
+                      "launches_per_kernel": args.warmup + args.steps}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -378,6 +405,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiling driver: warm-up + timed device-resident steps only (no e2e, CPU or clocks)")
+    ap.add_argument("--batch", type=int, default=B_PER_GPU, help="batch per GPU (profiling runs only)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -387,6 +417,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.profile:
+        run_profile(args, local_rank)
         return
     import datetime
 
