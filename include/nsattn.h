@@ -12,7 +12,8 @@
  *    blocks unless stated.
  *  - Every entry point returns an nsa_status and never aborts the process; no C++ exception crosses
  *    the ABI.  nsa_last_error() gives the message of the last failing call on the calling thread.
- *  - Buffers and workspaces are owned by the caller; the library allocates no device memory.
+ *  - Buffers and workspaces are owned by the caller; the library never calls a device allocator
+ *    (nsa_fused_attention_noalloc uses a fixed scratch array compiled into the library instead).
  *  - Strides and offsets are in elements.  Matrices are row-major packed rows as in the reference:
  *    element (b, row, col) of a view is at ptr[b*bstride + row*ld + off + col].
  */
@@ -128,6 +129,27 @@ nsa_status nsa_fused_attention(const nsa_fused_desc* desc, const void* qkv, cons
                                const float* k_norm_w, const float* cs, const int32_t* kv_len,
                                const float* bias, void* out, void* workspace, size_t workspace_bytes,
                                void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * nsa_fused_attention_noalloc: no counterpart in the reference (its WebGPU path always allocates
+ * through its buffer pool).  The same fused step as nsa_fused_attention for callers that cannot
+ * allocate device memory (a host runtime whose allocator is closed to plugins, or a process that
+ * must not call cudaMalloc while it shares the GPU): instead of a caller workspace it uses a scratch
+ * array of NSA_NOALLOC_SCRATCH_BYTES built into the library, which every GPU that loads it holds
+ * until exit.  The caller passes only inputs and outputs; nothing on this path allocates.
+ *  - Shapes whose nsa_fused_attention_workspace_size() exceeds NSA_NOALLOC_SCRATCH_BYTES are
+ *    rejected with NSA_ERR_WORKSPACE and a message (e.g. one config-2 DiT batch element or a
+ *    16 x 1024-token Gemma layer fit; the batch-2 DiT call does not).
+ *  - The first call on each device looks up the scratch address on that device
+ *    (cudaGetSymbolAddress); make that first call before any stream capture.
+ *  - All calls share the scratch and it keeps the previous call's contents (nothing in it has to
+ *    start at zero).  Calls that overlap on the GPU (other streams or threads on the same device)
+ *    race on it: order them, e.g. on one stream.
+ * ------------------------------------------------------------------------------------------------ */
+#define NSA_NOALLOC_SCRATCH_BYTES (64u << 20)
+nsa_status nsa_fused_attention_noalloc(const nsa_fused_desc* desc, const void* qkv, const float* q_norm_w,
+                                       const float* k_norm_w, const float* cs, const int32_t* kv_len,
+                                       const float* bias, void* out, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * RoPE tables in the reference layout: cos block [L][D/2] then sin block [L][D/2] (sinOff = L*D/2).

@@ -63,6 +63,7 @@ SIGNATURES = {
     "nsa_head_norm": (_i32, [_vp, _i32, _vp, _i32, _i32, _i32, _i64, _i64, _i64, _vp, _i64, _f32, _vp]),
     "nsa_fused_attention_workspace_size": (_sz, [ctypes.POINTER(FusedDesc)]),
     "nsa_fused_attention": (_i32, [ctypes.POINTER(FusedDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "nsa_fused_attention_noalloc": (_i32, [ctypes.POINTER(FusedDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "nsa_rope2d_table": (_i32, [_i32, _i32, _i32, _vp, _vp]),
     "nsa_rope1d_table": (_i32, [_i32, _i32, _f32, _vp, _vp]),
     "nsa_check_device": (_i32, [_vp]),

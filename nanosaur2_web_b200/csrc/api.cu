@@ -292,6 +292,8 @@ CommonArgs common_from(const nsa_fused_desc* d) {
 
 namespace nsa {
 
+void record_error(const std::string& msg) { g_last_error = msg; }
+
 int* device_error_word() {
   static std::mutex mu;
   static int* cache[128] = {};

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace nsa {
 
 constexpr int kTileM = 128;  // query rows per tensor-core tile (one TMEM lane per row)
@@ -75,5 +77,6 @@ cudaError_t launch_rope2d_table(int h, int w, int D, float* out, cudaStream_t st
 cudaError_t launch_rope1d_table(int L, int D, float theta, float* out, cudaStream_t stream);
 
 int* device_error_word();   // address of the library's device error word on the current device
+void record_error(const std::string& msg);   // sets the calling thread's nsa_last_error() message
 
 }  // namespace nsa
