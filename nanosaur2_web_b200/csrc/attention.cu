@@ -33,7 +33,7 @@ constexpr float kRescaleThreshold = 8.0f;   // log2 units: P may reach 2^8 befor
 template <int D>
 struct Cfg {
   static constexpr int NQ = (D <= 128) ? 2 : 1;
-  static constexpr int NS = (D <= 128) ? 2 : 1;
+  static constexpr int NS = (D <= 96) ? 3 : ((D <= 128) ? 2 : 1);   // K and V ring depth
   static constexpr int BLK = (D % 64 == 0) ? 64 : 32;     // elements per swizzle row
   static constexpr int NB = D / BLK;
   static constexpr int ROWB = BLK * 2;                    // bytes per row of one block
@@ -71,11 +71,15 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t sq, uint32_t 
   }
 }
 
+// O (+)= P V over keys [64*half, 64*half + 64) of the tile: the softmax hands P over in two halves
+// so the tensor core starts on the first while the second is still being exponentiated.
 template <int D>
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t sv, bool accumulate) {
+__device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint32_t sv, bool accumulate,
+                                              int half) {
   using C = Cfg<D>;
 #pragma unroll
-  for (int kk = 0; kk < C::KSTEPS_PV; ++kk) {
+  for (int k = 0; k < C::KSTEPS_PV / 2; ++k) {
+    const int kk = half * (C::KSTEPS_PV / 2) + k;
     // V is MN-major: 16 keys per k-step, head-dim blocks of BLK elements BLK_BYTES apart
     const uint64_t b = smem_desc(sv + (uint32_t)(kk * 16 * C::ROWB), C::BLK_BYTES, 8 * C::ROWB, C::SWZ);
     mma_ts(d_tmem, p_tmem + (uint32_t)(kk * 8), b, C::IDESC_PV, (accumulate || kk > 0) ? 1u : 0u);
@@ -99,9 +103,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   uint64_t* k_empty = k_full + NS;
   uint64_t* v_full = k_empty + NS;
   uint64_t* v_empty = v_full + NS;
-  uint64_t* s_full = v_empty + NS;   // [2]
-  uint64_t* p_full = s_full + 2;     // [2]
-  uint64_t* o_full = p_full + 2;     // [2]
+  uint64_t* s_full = v_empty + NS;   // [2]   S buffer ready
+  uint64_t* p_full = s_full + 2;     // [4]   P half ready: [tile * 2 + half]
+  uint64_t* o_full = p_full + 4;     // [2]   O complete (NQ = 1: once per P*V)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -137,9 +141,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
       mbar_init(&o_full[i], 1);
     }
+    for (int i = 0; i < 4; ++i) mbar_init(&p_full[i], 128);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -220,22 +224,26 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
           tc_commit(&s_full[1]);
           tc_commit(&k_empty[0]);
         }
+        // P*V of tile i for key tile jj, half by half as the softmax hands P over
+        auto pv = [&](int i, int jj, int svs) -> bool {
+          for (int h = 0; h < 2; ++h) {
+            if (!wait_bounded(&p_full[i * 2 + h], jj & 1, abort_flag, p.err, kErrTimeoutMma, to)) return false;
+            tc_fence_after();
+            issue_pv_half<D>(tmem + C::o_col(i), tmem + C::s_col(i), sv + svs * C::TILE_BYTES, jj > 0, h);
+          }
+          return true;
+        };
         for (int j = 1; ok && j < n; ++j) {
           const int svs = (j - 1) % NS, sks = j % NS;
-          ok = wait_bounded(&v_full[svs], ((j - 1) / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to) &&
-               wait_bounded(&p_full[0], (j - 1) & 1, abort_flag, p.err, kErrTimeoutMma, to);
+          ok = wait_bounded(&v_full[svs], ((j - 1) / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to) && pv(0, j - 1, svs);
           if (!ok) break;
-          tc_fence_after();
-          issue_pv<D>(tmem + C::o_col(0), tmem + C::s_col(0), sv + svs * C::TILE_BYTES, j - 1 > 0);
           ok = wait_bounded(&k_full[sks], (j / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to);
           if (!ok) break;
           tc_fence_after();
           issue_qk<D>(tmem + C::s_col(0), sq, sk + sks * C::TILE_BYTES);
           tc_commit(&s_full[0]);
-          ok = wait_bounded(&p_full[1], (j - 1) & 1, abort_flag, p.err, kErrTimeoutMma, to);
+          ok = pv(1, j - 1, svs);
           if (!ok) break;
-          tc_fence_after();
-          issue_pv<D>(tmem + C::o_col(1), tmem + C::s_col(1), sv + svs * C::TILE_BYTES, j - 1 > 0);
           tc_commit(&v_empty[svs]);
           issue_qk<D>(tmem + C::s_col(1), sq + C::TILE_BYTES, sk + sks * C::TILE_BYTES);
           tc_commit(&s_full[1]);
@@ -245,11 +253,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
           const int svs = (n - 1) % NS;
           ok = wait_bounded(&v_full[svs], ((n - 1) / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to);
           for (int i = 0; ok && i < 2; ++i) {
-            ok = wait_bounded(&p_full[i], (n - 1) & 1, abort_flag, p.err, kErrTimeoutMma, to);
-            if (!ok) break;
-            tc_fence_after();
-            issue_pv<D>(tmem + C::o_col(i), tmem + C::s_col(i), sv + svs * C::TILE_BYTES, n - 1 > 0);
-            tc_commit(&o_full[i]);
+            ok = pv(i, n - 1, svs);
+            if (ok) tc_commit(&o_full[i]);
           }
           if (ok) tc_commit(&v_empty[svs]);
         }
@@ -265,11 +270,14 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         }
         for (int j = 0; ok && j < n; ++j) {
           const int svs = j % NS;
-          ok = wait_bounded(&v_full[svs], (j / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to) &&
-               wait_bounded(&p_full[0], j & 1, abort_flag, p.err, kErrTimeoutMma, to);
+          ok = wait_bounded(&v_full[svs], (j / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to);
+          for (int h = 0; ok && h < 2; ++h) {
+            ok = wait_bounded(&p_full[h], j & 1, abort_flag, p.err, kErrTimeoutMma, to);
+            if (!ok) break;
+            tc_fence_after();
+            issue_pv_half<D>(tmem + C::o_col(0), tmem + C::s_col(j & 1), sv + svs * C::TILE_BYTES, j > 0, h);
+          }
           if (!ok) break;
-          tc_fence_after();
-          issue_pv<D>(tmem + C::o_col(0), tmem + C::s_col(j & 1), sv + svs * C::TILE_BYTES, j > 0);
           tc_commit(&o_full[0]);
           tc_commit(&v_empty[svs]);
           if (j + 2 < n) {
@@ -308,41 +316,51 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
       ok = __all_sync(0xffffffffu, wait_bounded(&s_full[sbuf], sparity, abort_flag, p.err, kErrTimeoutSoftmax, to));
       if (!ok) break;
       tc_fence_after();
-      float x[128];
-      {
-        uint32_t r[64];
-        tmem_ld64(lane_base + C::s_col(sbuf), r);
-#pragma unroll
-        for (int c = 0; c < 64; ++c) x[c] = __uint_as_float(r[c]);
-        tmem_ld64(lane_base + C::s_col(sbuf) + 64u, r);
-#pragma unroll
-        for (int c = 0; c < 64; ++c) x[64 + c] = __uint_as_float(r[c]);
-      }
       const int key0 = (j0 + j) * kTileN;
       const bool t_invalid = key0 + kTileN > kv_valid;
       const bool t_causal = p.causal && key0 + kTileN - 1 > tile_row0;
       const bool t_window = p.window > 0 && key0 <= tile_row0 + kTileM - 1 - p.window;
       const bool t_bias = bias_b != nullptr && key0 + kTileN > p.bias_start && key0 < p.bias_start + p.bias_len;
-      float tmax = -INFINITY;
-      if (!(t_invalid || t_causal || t_window || t_bias)) {
+      const uint32_t s_addr = lane_base + C::s_col(sbuf);
+      // Unmasked tiles keep the raw scores and fold the scale into the exponent (one FFMA per
+      // element).  Masked tiles (text bias, padding, causal or window edges; a few per row) are
+      // first rewritten in TMEM, 32 columns at a time, into scaled, biased, masked logits, and then
+      // take the same path with a unit scale.
+      float sc = sl2;
+      if (t_invalid || t_causal || t_window || t_bias) {
+        sc = 1.f;
+        const int lo = p.window > 0 ? row - p.window + 1 : 0;            // first visible key
+        const int hi = p.causal ? min(kv_valid, row + 1) : kv_valid;     // one past the last
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(s_addr + (uint32_t)(cc * 32), r);
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          x[c] *= sl2;
-          tmax = fmaxf(tmax, x[c]);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          const int key = key0 + c;
-          float v = x[c] * sl2;
-          if (t_bias && key >= p.bias_start && key < p.bias_start + p.bias_len)
-            v += __ldg(bias_b + (key - p.bias_start)) * kLog2e;
-          const bool keep = key < kv_valid && (!p.causal || key <= row) && (p.window <= 0 || key > row - p.window);
-          v = keep ? v : -INFINITY;
-          x[c] = v;
-          tmax = fmaxf(tmax, v);
+          for (int c = 0; c < 32; ++c) {
+            const int key = key0 + cc * 32 + c;
+            float v = __uint_as_float(r[c]) * sl2;
+            if (t_bias && key >= p.bias_start && key < p.bias_start + p.bias_len)
+              v += __ldg(bias_b + (key - p.bias_start)) * kLog2e;
+            r[c] = __float_as_uint(key >= lo && key < hi ? v : -INFINITY);
+          }
+          tmem_st32(s_addr + (uint32_t)(cc * 32), r);
         }
       }
+      float x[128];
+      {
+        uint32_t r[128];
+        tmem_ld128(s_addr, r);
+#pragma unroll
+        for (int c = 0; c < 128; ++c) x[c] = __uint_as_float(r[c]);
+      }
+      float mx[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) mx[c & 7] = fmaxf(mx[c & 7], x[c]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx[k] *= sc;
+      const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       const float m_new = fmaxf(m_run, tmax);
       if (j == 0) {
         m_run = m_new;
@@ -372,20 +390,25 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
           }
         }
       }
-      const float m_use = m_run == -INFINITY ? 0.f : m_run;
-      float rs = 0.f;
-      uint32_t pk[64];
+      const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
+      float ls[8];
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float a0 = ex2(x[2 * c] - m_use);
-        const float a1 = ex2(x[2 * c + 1] - m_use);
-        rs += a0 + a1;
-        pk[c] = pack_bf16x2(a0, a1);
+      for (int k = 0; k < 8; ++k) ls[k] = 0.f;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float a0 = ex2(fmaf(x[64 * h + 2 * c], sc, neg_m));
+          const float a1 = ex2(fmaf(x[64 * h + 2 * c + 1], sc, neg_m));
+          ls[c & 7] += a0 + a1;
+          pk[c] = pack_bf16x2(a0, a1);
+        }
+        tmem_st32(s_addr + (uint32_t)(32 * h), pk);
+        tc_fence_before();
+        mbar_arrive(&p_full[(NQ == 2 ? tile : 0) * 2 + h]);
       }
-      l_run += rs;
-      tmem_st64(lane_base + C::s_col(sbuf), pk);
-      tc_fence_before();
-      mbar_arrive(&p_full[NQ == 2 ? tile : 0]);
+      l_run += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
     }
     if (ok && n > 0) {
       if constexpr (NQ == 2) {

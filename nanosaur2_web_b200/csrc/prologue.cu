@@ -108,6 +108,127 @@ __global__ void __launch_bounds__(kPrologueThreads) prologue_kernel(const Prolog
   }
 }
 
+// Vectorised prologue for aligned layouts.  Each head of a row is handled by P consecutive threads;
+// thread `sub` owns elements [sub*S, sub*S + S) of both halves of the head (S = D / (2P)), so the
+// RoPE pair (i, i + D/2) stays in one thread, every load and store is a 16-byte vector, and the
+// RMSNorm sum is a P-lane shuffle reduction.  grid.y = part * B + batch element.
+template <int D, int P, typename T>
+__global__ void __launch_bounds__(256) prologue_vec_kernel(const PrologueParams p) {
+  constexpr int S = D / (2 * P);
+  constexpr int HALF = D / 2;
+  constexpr int EPV = 16 / sizeof(T);   // input elements per 16-byte vector
+  static_assert(S % 8 == 0 && S % EPV == 0, "vector width");
+  const int part = blockIdx.y / p.B;
+  const int bl = blockIdx.y % p.B;
+  const int b = p.b_begin + bl;
+  const int H = part == 0 ? p.Hq : p.Hkv;
+  const int pad = part == 0 ? p.Lq_pad : p.Lk_pad;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int sub = (int)(idx % P);
+  const long long rest = idx / P;
+  const int hh = (int)(rest % H);
+  const long long row_ll = rest / H;
+  // Threads past the last row stay until after the shuffle below (all lanes of a warp take part).
+  const bool in_range = row_ll < pad;
+  const int row = in_range ? (int)row_ll : 0;
+  const RowView& view = part == 0 ? p.q : (part == 1 ? p.k : p.v);
+  const int h_begin = part == 0 ? p.hq_begin : p.hkv_begin;
+  const float* w = part == 0 ? p.q_w : (part == 1 ? p.k_w : nullptr);
+  const int valid_rows = part == 0 ? p.Lq : (p.kv_len ? min(p.kv_len[b], p.Lk) : p.Lk);
+  const bool valid = in_range && row < valid_rows;
+  const bool rope = part < 2 && p.cs != nullptr && row < p.rope_rows;
+
+  float x1[S], x2[S];
+#pragma unroll
+  for (int i = 0; i < S; ++i) x1[i] = x2[i] = 0.f;
+  if (valid) {
+    const T* src = reinterpret_cast<const T*>(view.ptr) + (int64_t)b * view.bstride + (int64_t)row * view.ld + view.off +
+                   (int64_t)(h_begin + hh) * D + sub * S;
+#pragma unroll
+    for (int v = 0; v < S / EPV; ++v) {
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(src) + v);
+      const uint4 c = __ldg(reinterpret_cast<const uint4*>(src + HALF) + v);
+      if constexpr (sizeof(T) == 2) {
+        const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a);
+        const __nv_bfloat162* pc = reinterpret_cast<const __nv_bfloat162*>(&c);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 fa = __bfloat1622float2(pa[e]);
+          const float2 fc = __bfloat1622float2(pc[e]);
+          x1[v * 8 + 2 * e] = fa.x;
+          x1[v * 8 + 2 * e + 1] = fa.y;
+          x2[v * 8 + 2 * e] = fc.x;
+          x2[v * 8 + 2 * e + 1] = fc.y;
+        }
+      } else {
+        const float* fa = reinterpret_cast<const float*>(&a);
+        const float* fc = reinterpret_cast<const float*>(&c);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          x1[v * 4 + e] = fa[e];
+          x2[v * 4 + e] = fc[e];
+        }
+      }
+    }
+  }
+  // w is uniform over the block (one part per blockIdx.y), so every lane reaches the shuffle.
+  float r = 1.f;
+  if (w) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < S; ++i) ss += x1[i] * x1[i] + x2[i] * x2[i];
+#pragma unroll
+    for (int o = 1; o < P; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    r = rsqrtf(ss / (float)D + p.eps);
+  }
+  if (!in_range) return;
+  if (valid) {
+    if (w) {
+      const float4* w1 = reinterpret_cast<const float4*>(w + sub * S);
+      const float4* w2 = reinterpret_cast<const float4*>(w + HALF + sub * S);
+#pragma unroll
+      for (int v = 0; v < S / 4; ++v) {
+        const float4 a = __ldg(w1 + v), c = __ldg(w2 + v);
+        x1[4 * v] *= r * a.x; x1[4 * v + 1] *= r * a.y; x1[4 * v + 2] *= r * a.z; x1[4 * v + 3] *= r * a.w;
+        x2[4 * v] *= r * c.x; x2[4 * v + 1] *= r * c.y; x2[4 * v + 2] *= r * c.z; x2[4 * v + 3] *= r * c.w;
+      }
+    }
+    if (rope) {
+      const float4* cp = reinterpret_cast<const float4*>(p.cs + (int64_t)row * HALF + sub * S);
+      const float4* sp = reinterpret_cast<const float4*>(p.cs + p.sin_off + (int64_t)row * HALF + sub * S);
+#pragma unroll
+      for (int v = 0; v < S / 4; ++v) {
+        const float4 c4 = __ldg(cp + v), s4 = __ldg(sp + v);
+        const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float a = x1[4 * v + e], c = x2[4 * v + e];
+          x1[4 * v + e] = a * cc[e] - c * sn[e];
+          x2[4 * v + e] = c * cc[e] + a * sn[e];
+        }
+      }
+    }
+  }
+  // From here each thread writes its own chunk.
+  __nv_bfloat16* dst = (part == 0 ? p.Qs : (part == 1 ? p.Ks : p.Vs)) +
+                       (((int64_t)bl * H + hh) * pad + row) * D + sub * S;
+#pragma unroll
+  for (int v = 0; v < S / 8; ++v) {
+    uint4 o1, o2;
+    uint32_t* u1 = reinterpret_cast<uint32_t*>(&o1);
+    uint32_t* u2 = reinterpret_cast<uint32_t*>(&o2);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      __nv_bfloat162 t1 = __floats2bfloat162_rn(x1[v * 8 + 2 * e], x1[v * 8 + 2 * e + 1]);
+      __nv_bfloat162 t2 = __floats2bfloat162_rn(x2[v * 8 + 2 * e], x2[v * 8 + 2 * e + 1]);
+      u1[e] = *reinterpret_cast<uint32_t*>(&t1);
+      u2[e] = *reinterpret_cast<uint32_t*>(&t2);
+    }
+    reinterpret_cast<uint4*>(dst)[v] = o1;
+    reinterpret_cast<uint4*>(dst + HALF)[v] = o2;
+  }
+}
+
 // ops.headNorm: in place on X[(row_off + l) * ld + col_off + h * D + i]; one warp per (row, head).
 template <typename T>
 __global__ void head_norm_kernel(T* X, const float* w, int L, int H, int D, int64_t ld, int64_t col_off,
@@ -175,9 +296,53 @@ __global__ void rope1d_table_kernel(int L, int D, float theta, float* out) {
 
 }  // namespace
 
+namespace {
+
+bool aligned16(const void* ptr, int64_t elem_offset_multiple_bytes) {
+  return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && (elem_offset_multiple_bytes & 15) == 0;
+}
+
+// Every vector access of the fast path is 16-byte aligned iff the bases, strides, offsets and the
+// per-thread chunk are (the chunk and head sizes are multiples of 16 bytes by construction).
+bool vec_ok(const PrologueParams& p, int elem) {
+  const RowView* vs[3] = {&p.q, &p.k, &p.v};
+  for (const RowView* v : vs)
+    if (!aligned16(v->ptr, v->ld * elem) || ((v->bstride * elem) & 15) || ((v->off * elem) & 15)) return false;
+  if (p.cs && (!aligned16(p.cs, p.sin_off * 4))) return false;
+  if ((p.q_w && !aligned16(p.q_w, 0)) || (p.k_w && !aligned16(p.k_w, 0))) return false;
+  return true;
+}
+
+template <int D, int P, typename T>
+cudaError_t launch_vec(const PrologueParams& p, cudaStream_t stream) {
+  const int rows = p.Lq_pad > p.Lk_pad ? p.Lq_pad : p.Lk_pad;
+  const int H = p.Hq > p.Hkv ? p.Hq : p.Hkv;
+  const long long threads = (long long)rows * H * P;
+  const long long blocks = (threads + 255) / 256;
+  if (blocks > 0x7FFFFFFFLL || 3LL * p.B > 65535) return cudaErrorInvalidValue;
+  prologue_vec_kernel<D, P, T><<<dim3((unsigned)blocks, 3 * p.B), 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_vec_t(const PrologueParams& p, cudaStream_t stream) {
+  switch (p.D) {
+    case 64: return launch_vec<64, 2, T>(p, stream);
+    case 96: return launch_vec<96, 2, T>(p, stream);
+    case 128: return launch_vec<128, 2, T>(p, stream);
+    case 256: return launch_vec<256, 4, T>(p, stream);
+    default: return cudaErrorNotSupported;
+  }
+}
+
+}  // namespace
+
 cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream) {
   const int rows = p.Lq_pad > p.Lk_pad ? p.Lq_pad : p.Lk_pad;
   if (rows <= 0 || p.B <= 0) return cudaSuccess;
+  const int elem = p.src_f32 ? 4 : 2;
+  if ((p.D == 64 || p.D == 96 || p.D == 128 || p.D == 256) && vec_ok(p, elem))
+    return p.src_f32 ? launch_vec_t<float>(p, stream) : launch_vec_t<__nv_bfloat16>(p, stream);
   dim3 grid(rows, p.B, 3);
   prologue_kernel<<<grid, kPrologueThreads, 0, stream>>>(p);
   return cudaGetLastError();
