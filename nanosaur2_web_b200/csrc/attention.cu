@@ -29,6 +29,16 @@ namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units: P may reach 2^8 before O is rescaled
+constexpr int kKeyBiasMax = 1024;           // keys covered by the shared-memory key bias/mask table
+// Pairs c of the 32 per P half with (c % NSA_POLY_EVERY == NSA_POLY_EVERY - 1) take the FMA-pipe
+// exp2 in unmasked tiles (0 = none); the rest use ex2.approx on the special-function unit.
+#ifndef NSA_POLY_EVERY
+#define NSA_POLY_EVERY 0
+#endif
+#ifndef NSA_MAX3
+#define NSA_MAX3 1
+#endif
+constexpr int kPolyEvery = NSA_POLY_EVERY;
 
 template <int D>
 struct Cfg {
@@ -43,9 +53,17 @@ struct Cfg {
   static constexpr int KSTEPS_QK = D / 16;
   static constexpr int KSTEPS_PV = kTileN / 16;
   static constexpr int THREADS = 128 + NQ * 128;
+  // Register split (NQ = 2): the block launches at REG_LAUNCH per thread; the first warpgroup
+  // (producer, MMA issuer, two idle warps) drops to REG_CTRL and the two softmax warpgroups rise
+  // to REG_SOFTMAX.  128*REG_CTRL + 256*REG_SOFTMAX equals the launch total 384*REG_LAUNCH, so
+  // setmaxnreg.inc never waits; the launcher checks the compiled count before every first launch.
+  static constexpr int REG_LAUNCH = 168, REG_CTRL = 104, REG_SOFTMAX = 200;
+  static_assert(NQ != 2 || 128 * REG_CTRL + 256 * REG_SOFTMAX == THREADS * REG_LAUNCH, "register split");
   static constexpr int SMEM_TILES = (NQ + 2 * NS) * TILE_BYTES;
+  static constexpr int SMEM_KB = kKeyBiasMax * 4;   // key bias/mask table (log2 units)
   // at least 117 KB so that two CTAs never share an SM (each allocates all 512 TMEM columns)
-  static constexpr int SMEM_BYTES = (SMEM_TILES + 1024 + 256) > 117 * 1024 ? (SMEM_TILES + 1024 + 256) : 117 * 1024;
+  static constexpr int SMEM_NEED = SMEM_TILES + SMEM_KB + 1024 + 256;
+  static constexpr int SMEM_BYTES = SMEM_NEED > 117 * 1024 ? SMEM_NEED : 117 * 1024;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, kTileN, 0, 0);
   static constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, D, 0, 1);
@@ -97,7 +115,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + NQ * C::TILE_BYTES;
   uint8_t* sV = sK + NS * C::TILE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + NS * C::TILE_BYTES);
+  float* kb = reinterpret_cast<float*>(sV + NS * C::TILE_BYTES);   // [kKeyBiasMax]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(kb + kKeyBiasMax);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = k_full + NS;
@@ -161,6 +180,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  if constexpr (NQ == 2) {
+    if (warp < 4) reg_dealloc<C::REG_CTRL>();
+  }
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0 && n > 0) {
@@ -301,6 +323,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ softmax + epilogue
+    if constexpr (NQ == 2) reg_alloc<C::REG_SOFTMAX>();
     const int tile = (warp - 4) / 4;
     const int quarter = warp % 4;
     const int row = q_row0 + tile * kTileM + quarter * 32 + lane;
@@ -308,6 +331,22 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     const float sl2 = p.scale_log2;
     const float* bias_b = p.bias ? p.bias + (int64_t)b * p.bias_bstride : nullptr;
+    // Key bias + padding mask of the tiles that need one, in log2 units, for keys [kb0, kb0 +
+    // kKeyBiasMax): 0 for plain keys, log(w)*log2(e) for biased text keys, -inf past kv_valid.
+    // Built once per CTA by the softmax threads (named barrier 1 over them).
+    int kb0 = min(kv_valid, bias_b ? p.bias_start : kv_valid);
+    kb0 = max(kb0 - kb0 % kTileN, j0 * kTileN);
+    const int kb_end = (j0 + n) * kTileN;
+    const bool kb_ok = kb_end - kb0 <= kKeyBiasMax;
+    if (kb_ok) {
+      for (int i = threadIdx.x - 128; i < kb_end - kb0; i += NQ * 128) {
+        const int key = kb0 + i;
+        float v = 0.f;
+        if (bias_b && key >= p.bias_start && key < p.bias_start + p.bias_len) v = bias_b[key - p.bias_start] * kLog2e;
+        kb[i] = key < kv_valid ? v : -INFINITY;
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(NQ * 128) : "memory");
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
@@ -327,7 +366,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
       // first rewritten in TMEM, 32 columns at a time, into scaled, biased, masked logits, and then
       // take the same path with a unit scale.
       float sc = sl2;
-      if (t_invalid || t_causal || t_window || t_bias) {
+      const bool t_table = kb_ok && !t_causal && !t_window && (t_invalid || t_bias);
+      if (!t_table && (t_invalid || t_causal || t_window || t_bias)) {
         sc = 1.f;
         const int lo = p.window > 0 ? row - p.window + 1 : 0;            // first visible key
         const int hi = p.causal ? min(kv_valid, row + 1) : kv_valid;     // one past the last
@@ -353,14 +393,36 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
 #pragma unroll
         for (int c = 0; c < 128; ++c) x[c] = __uint_as_float(r[c]);
       }
+      if (t_table) {
+        // scaled logits + key bias / -inf from the shared table (broadcast reads)
+        sc = 1.f;
+        const float4* kt = reinterpret_cast<const float4*>(kb + (key0 - kb0));
+        const uint64_t sl2x2 = f2_pack(sl2, sl2);
+#pragma unroll
+        for (int c = 0; c < 128; c += 4) {
+          const float4 kv4 = kt[c / 4];
+          f2_unpack(f2_fma(f2_pack(x[c], x[c + 1]), sl2x2, f2_pack(kv4.x, kv4.y)), x[c], x[c + 1]);
+          f2_unpack(f2_fma(f2_pack(x[c + 2], x[c + 3]), sl2x2, f2_pack(kv4.z, kv4.w)), x[c + 2], x[c + 3]);
+        }
+      }
+#if NSA_MAX3
+      float mx[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) mx[k] = fmaxf(x[2 * k], x[2 * k + 1]);
+#pragma unroll
+      for (int c = 8; c < 128; c += 8) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) mx[k] = fmax3(mx[k], x[c + 2 * k], x[c + 2 * k + 1]);
+      }
+      const float tmax = fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3])) * sc;
+#else
       float mx[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
+      for (int k = 0; k < 8; ++k) mx[k] = x[k];
 #pragma unroll
-      for (int c = 0; c < 128; ++c) mx[c & 7] = fmaxf(mx[c & 7], x[c]);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mx[k] *= sc;
-      const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      for (int c = 8; c < 128; ++c) mx[c & 7] = fmaxf(mx[c & 7], x[c]);
+      const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sc;
+#endif
       const float m_new = fmaxf(m_run, tmax);
       if (j == 0) {
         m_run = m_new;
@@ -391,24 +453,40 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         }
       }
       const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
-      float ls[8];
+      const uint64_t sc2 = f2_pack(sc, sc), nm2 = f2_pack(neg_m, neg_m);
+      const bool poly_ok = kPolyEvery > 0 && sc == sl2;   // unmasked tile: every logit is finite
+      uint64_t ls[4];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) ls[k] = 0.f;
+      for (int k = 0; k < 4; ++k) ls[k] = 0ull;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t pk[32];
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          const float a0 = ex2(fmaf(x[64 * h + 2 * c], sc, neg_m));
-          const float a1 = ex2(fmaf(x[64 * h + 2 * c + 1], sc, neg_m));
-          ls[c & 7] += a0 + a1;
+          const uint64_t y = f2_fma(f2_pack(x[64 * h + 2 * c], x[64 * h + 2 * c + 1]), sc2, nm2);
+          float a0, a1;
+          if (kPolyEvery > 0 && c % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1 && poly_ok) {
+            ex2_poly2(y, a0, a1);
+          } else {
+            float y0, y1;
+            f2_unpack(y, y0, y1);
+            a0 = ex2(y0);
+            a1 = ex2(y1);
+          }
+          ls[c & 3] = f2_add(ls[c & 3], f2_pack(a0, a1));
           pk[c] = pack_bf16x2(a0, a1);
         }
         tmem_st32(s_addr + (uint32_t)(32 * h), pk);
         tc_fence_before();
         mbar_arrive(&p_full[(NQ == 2 ? tile : 0) * 2 + h]);
       }
-      l_run += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+      {
+        float s0, s1, s2, s3;
+        f2_unpack(f2_add(f2_add(ls[0], ls[1]), f2_add(ls[2], ls[3])), s0, s1);
+        (void)s2;
+        (void)s3;
+        l_run += s0 + s1;
+      }
     }
     if (ok && n > 0) {
       if constexpr (NQ == 2) {
@@ -481,6 +559,14 @@ cudaError_t launch_d(const AttnParams& p, const CUtensorMap& tmQ, const CUtensor
   if (dev < 0 || dev >= 128 || !configured[dev]) {
     e = cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
+    if constexpr (C::NQ == 2) {
+      // The setmaxnreg split is only safe if the kernel really launches with REG_LAUNCH registers
+      // per thread; anything else could make setmaxnreg.inc wait forever, so refuse to launch.
+      cudaFuncAttributes attr;
+      e = cudaFuncGetAttributes(&attr, attn_fwd_kernel<D>);
+      if (e != cudaSuccess) return e;
+      if (attr.numRegs != C::REG_LAUNCH) return cudaErrorInvalidConfiguration;
+    }
     if (dev >= 0 && dev < 128) configured[dev] = true;
   }
   const long long blocks = (long long)p.B * p.Hq * p.q_blocks;
