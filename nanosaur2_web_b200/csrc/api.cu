@@ -108,13 +108,28 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Map over a head-major bf16 tile buffer [rows][D]; boxes of [128 rows][blk elements].
-bool encode_tiles(CUtensorMap* map, void* base, int D, int64_t rows, int blk) {
+// Map over a bf16 matrix [rows][width] with a row pitch of `ld` elements; boxes of
+// [box_rows rows][blk elements] with the swizzle the tcgen05 descriptors expect.
+bool encode_rows(CUtensorMap* map, const void* base, int64_t width, int64_t ld, int64_t rows, int blk, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)blk, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = blk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Map over a head-major bf16 tile buffer [rows][D]; boxes of [box_rows rows][blk elements].
+bool encode_tiles(CUtensorMap* map, void* base, int D, int64_t rows, int blk, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)blk, (cuuint32_t)nsa::kTileM};
+  const cuuint32_t box[2] = {(cuuint32_t)blk, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUtensorMapSwizzle sw = blk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
@@ -129,7 +144,8 @@ int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 struct Plan {
   int B, Lq, Lk, Hq, group, D;       // full problem
   int b0, Bs, hq0, Hqs, hkv0, Hkvs;  // shard
-  int NQ, blk, Lq_pad, Lk_pad;
+  int NQ, BN, blk, Lq_pad, Lk_pad;
+  bool qtmem;
   size_t q_bytes, k_bytes, v_bytes, total;
 };
 
@@ -143,7 +159,8 @@ nsa_status make_plan(const CommonArgs& a, Plan* pl) {
     return fail(NSA_ERR_INVALID_ARGUMENT, "B, Lq, Lk, H and D must be >= 1");
   if (a.group < 1 || a.H % a.group != 0)
     return fail(NSA_ERR_INVALID_ARGUMENT, "group must divide the number of query heads");
-  const int NQ = nsa::attention_q_tiles_per_block(a.D);
+  const nsa::AttnGeometry geo = nsa::attention_geometry(a.D);
+  const int NQ = geo.NQ;
   if (NQ == 0)
     return fail(NSA_ERR_UNSUPPORTED, "attention: unsupported head dim " + std::to_string(a.D) + " (64, 96, 128, 256)");
   if (a.in_dtype != NSA_F32 && a.in_dtype != NSA_BF16) return fail(NSA_ERR_INVALID_ARGUMENT, "bad input dtype");
@@ -161,9 +178,11 @@ nsa_status make_plan(const CommonArgs& a, Plan* pl) {
   p.hkv0 = p.hq0 / a.group;
   p.Hkvs = (p.hq0 + p.Hqs - 1) / a.group - p.hkv0 + 1;
   p.NQ = NQ;
-  p.blk = nsa::attention_block_elems(a.D);
+  p.BN = geo.BN;
+  p.blk = geo.blk;
+  p.qtmem = geo.qtmem;
   p.Lq_pad = (int)round_up(a.Lq, (int64_t)NQ * nsa::kTileM);
-  p.Lk_pad = (int)round_up(a.Lk, nsa::kTileN);
+  p.Lk_pad = (int)round_up(a.Lk, geo.BN);
   const int64_t q_rows = (int64_t)p.Bs * p.Hqs * p.Lq_pad;
   const int64_t kv_rows = (int64_t)p.Bs * p.Hkvs * p.Lk_pad;
   if (q_rows >= (int64_t)1 << 31 || kv_rows >= (int64_t)1 << 31 || (int64_t)p.Bs * p.Hqs * (p.Lq_pad / (NQ * 128)) >= (int64_t)1 << 31)
@@ -215,15 +234,39 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
   pp.Vs = Vs;
   pp.Lq_pad = pl.Lq_pad;
   pp.Lk_pad = pl.Lk_pad;
+  // Kernels that keep Q in tensor memory TMA-load the raw bf16 query rows straight from the input
+  // when the layout allows a tiled map over it (16-byte aligned rows and head offsets, whole rows
+  // per batch element); they then apply the q norm and RoPE themselves.  Otherwise (fp32 input, odd
+  // layouts) the prologue writes normalised Q tiles and the kernel loads those.
+  // Off by default: when every CTA starts at once, pulling the raw rows and their fp32 RoPE table
+  // rows from HBM costs more than having the prologue write normalised Q tiles that stay in L2.
+#ifndef NSA_Q_FROM_INPUT
+#define NSA_Q_FROM_INPUT 0
+#endif
+  auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  const bool q_direct = NSA_Q_FROM_INPUT && pl.qtmem && a.in_dtype == NSA_BF16 && al16(pp.q.ptr) && pp.q.ld % 8 == 0 &&
+                        pp.q.off % 8 == 0 && (pl.B == 1 || (pp.q.bstride > 0 && pp.q.bstride % pp.q.ld == 0)) &&
+                        pp.q.off + (int64_t)pl.Hq * pl.D <= pp.q.ld && (!pp.q_w || al16(pp.q_w)) &&
+                        (!pp.cs || (al16(pp.cs) && (pp.sin_off * 4) % 16 == 0));
+  pp.skip_q = q_direct ? 1 : 0;
   const double in_elem = a.in_dtype == NSA_F32 ? 4.0 : 2.0;
-  const double pro_bytes = (double)pl.Bs * ((double)pl.Lq * pl.Hqs + 2.0 * pl.Lk * pl.Hkvs) * pl.D * (in_elem + 2.0);
+  const double pro_bytes = (double)pl.Bs * ((q_direct ? 0.0 : (double)pl.Lq * pl.Hqs) + 2.0 * pl.Lk * pl.Hkvs) *
+                           pl.D * (in_elem + 2.0);
   cudaError_t e = profiled("prologue", 0.0, pro_bytes, stream, [&] { return nsa::launch_prologue(pp, stream); });
   if (e != cudaSuccess) return cuda_fail(e, "prologue launch");
 
   CUtensorMap tq, tk, tv;
-  if (!encode_tiles(&tq, Qs, pl.D, (int64_t)pl.Bs * pl.Hqs * pl.Lq_pad, pl.blk) ||
-      !encode_tiles(&tk, Ks, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk) ||
-      !encode_tiles(&tv, Vs, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk))
+  bool maps_ok;
+  if (q_direct) {
+    // raw rows: [B * rows per element][ld]; rows past an element's Lq are ignored by the kernel
+    // the last batch element may end right after its own rows
+    const int64_t total_rows = pl.B == 1 ? pp.q.rows : (int64_t)(pl.B - 1) * (pp.q.bstride / pp.q.ld) + pp.q.rows;
+    maps_ok = encode_rows(&tq, pp.q.ptr, pp.q.ld, pp.q.ld, total_rows, pl.blk, nsa::kTileM);
+  } else {
+    maps_ok = encode_tiles(&tq, Qs, pl.D, (int64_t)pl.Bs * pl.Hqs * pl.Lq_pad, pl.blk, nsa::kTileM);
+  }
+  if (!maps_ok || !encode_tiles(&tk, Ks, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk, pl.BN) ||
+      !encode_tiles(&tv, Vs, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk, pl.BN))
     return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed (driver entry point unavailable?)");
 
   nsa::AttnParams ap{};
@@ -255,6 +298,32 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
   ap.q_blocks = pl.Lq_pad / (pl.NQ * nsa::kTileM);
   ap.err = err;
   ap.timeout_ns = wait_timeout_ns();
+  if (q_direct) {
+    ap.q_x0 = (int)pp.q.off;
+    ap.q_xh = pl.D;
+    ap.q_yb = pl.B == 1 ? 0 : (int)(pp.q.bstride / pp.q.ld);
+    ap.q_yh = 0;
+    ap.q_b0 = 0;
+    ap.q_h0 = 0;
+    ap.q_w = pp.q_w;
+    ap.q_eps = pp.eps;
+    ap.q_cs = pp.cs;
+    ap.q_sin_off = pp.sin_off;
+    ap.q_rope_rows = pp.rope_rows;
+  } else {
+    // the prologue's head-major Q tiles, already normalised and rotated
+    ap.q_x0 = 0;
+    ap.q_xh = 0;
+    ap.q_yb = pl.Hqs * pl.Lq_pad;
+    ap.q_yh = pl.Lq_pad;
+    ap.q_b0 = pl.b0;
+    ap.q_h0 = pl.hq0;
+    ap.q_w = nullptr;
+    ap.q_eps = 0.f;
+    ap.q_cs = nullptr;
+    ap.q_sin_off = 0;
+    ap.q_rope_rows = 0;
+  }
   double pairs = (double)pl.Lq * pl.Lk;
   if (a.causal) pairs = (double)pl.Lq * (pl.Lq + 1) / 2.0;
   const double flops = 4.0 * pl.Bs * pl.Hqs * pairs * pl.D;
@@ -347,9 +416,9 @@ nsa_status nsa_attention(const nsa_attention_desc* d, const void* q, const void*
   if (d->biasLen < 0) return fail(NSA_ERR_INVALID_ARGUMENT, "biasLen must be >= 0");
   if (d->biasLen > 0 && !bias) return fail(NSA_ERR_INVALID_ARGUMENT, "biasLen > 0 needs a bias pointer");
   nsa::PrologueParams pp{};
-  pp.q = {q, d->ldq, d->q_bstride, d->qOff};
-  pp.k = {k, d->ldk, d->k_bstride, d->kOff};
-  pp.v = {v, d->ldv, d->v_bstride, d->vOff};
+  pp.q = {q, d->ldq, d->q_bstride, d->qOff, d->Lq};
+  pp.k = {k, d->ldk, d->k_bstride, d->kOff, d->Lk};
+  pp.v = {v, d->ldv, d->v_bstride, d->vOff, d->Lk};
   pp.q_w = nullptr;
   pp.k_w = nullptr;
   pp.cs = nullptr;
@@ -383,9 +452,9 @@ nsa_status nsa_fused_attention(const nsa_fused_desc* d, const void* qkv, const f
   if (d->biasLen > 0 && !bias) return fail(NSA_ERR_INVALID_ARGUMENT, "biasLen > 0 needs a bias pointer");
   if (cs && d->D % 2) return fail(NSA_ERR_INVALID_ARGUMENT, "RoPE needs an even head dim");
   nsa::PrologueParams pp{};
-  pp.q = {qkv, d->ld, d->bstride, d->qOff};
-  pp.k = {qkv, d->ld, d->bstride, d->kOff};
-  pp.v = {qkv, d->ld, d->bstride, d->vOff};
+  pp.q = {qkv, d->ld, d->bstride, d->qOff, d->Lk};
+  pp.k = {qkv, d->ld, d->bstride, d->kOff, d->Lk};
+  pp.v = {qkv, d->ld, d->bstride, d->vOff, d->Lk};
   pp.q_w = q_norm_w;
   pp.k_w = k_norm_w;
   pp.cs = cs;

@@ -1,23 +1,27 @@
-// Fused multi-head attention forward for sm_100a (B200): TMA-staged Q/K/V tiles, tcgen05 MMAs
-// accumulating in tensor memory for S = Q K^T and O = P V, online softmax on the CUDA cores with
-// the key bias / padding mask / causal and window masks folded into the score tile.
+// Fused multi-head attention forward for sm_100a (B200): tcgen05 MMAs accumulating in tensor memory
+// for S = Q K^T and O = P V, K/V tiles staged by TMA, online softmax on the CUDA cores with the key
+// bias / padding mask / causal and window masks folded into the score tile.
 //
 // It replaces the reference's fused WGSL flash kernel (app/gpu/kernels.js:132-305: O = softmax(
 // s*QK^T + key bias + key mask) V, keys streamed in blocks with an online max/sum) and its unfused
 // GEMM + causal softmax + GEMM fallback for Gemma (app/gpu/ops.js:211-241).
 //
-// Layout of one CTA (one "block" of NQ query tiles of 128 rows for one (batch, query head)):
-//   warp 0        TMA producer: Q tiles once, then K/V tiles through NS-deep rings
+// One CTA handles one "block" of NQ query tiles of 128 rows for one (batch, query head):
+//   warp 0        TMA producer: K/V tiles through NS-deep rings (and Q tiles when Q lives in
+//                 shared memory)
 //   warp 1        TMEM allocator + MMA issuer (a single thread issues every tcgen05.mma)
 //   warps 2-3     idle (they complete the first warpgroup)
 //   warps 4..     one softmax warpgroup per query tile.  A warp may only touch the TMEM lane
 //                 quarter (warp id % 4), so lane l of warp w owns query row 32*(w%4) + l of its
 //                 tile: it reads its score row with tcgen05.ld, writes bf16 probabilities back
 //                 into the same TMEM columns, and finally normalises its output row.
-// Tensor memory (512 columns):
-//   NQ = 2 (head dim <= 128): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [384,384+D)
-//   NQ = 1 (head dim 256):    S double-buffered [0,128) [128,256), O [256,512)
-// P (bf16, two per 32-bit column) overwrites the first 64 columns of the S buffer it came from.
+// Head dims 64 and 96 (QTMEM): the softmax threads also load their own raw query row, apply the
+// q RMSNorm + RoPE prologue, and store the bf16 row into tensor memory, so S = Q K^T reads only K
+// from shared memory.  Tensor memory (512 columns) for D = 96, BN = 112 keys per tile:
+//   S0 [0,112) S1 [112,224) O0 [224,320) O1 [320,416) Q0 [416,464) Q1 [464,512)
+// D = 64: S 2 x 128, O 2 x 64, Q 2 x 32.  D = 128: Q in shared memory, S 2 x 128, O 2 x 128.
+// D = 256 (NQ = 1): Q in shared memory, S double-buffered [0,128) [128,256), O [256,512).
+// P (bf16, two per 32-bit column) overwrites the first BN/2 columns of the S buffer it came from.
 // The MMA for the next S into a buffer is issued after the P*V MMA that reads it; tcgen05.mma
 // operations issued by one thread execute in order.
 #include "nsa_internal.h"
@@ -30,28 +34,28 @@ namespace {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units: P may reach 2^8 before O is rescaled
 constexpr int kKeyBiasMax = 1024;           // keys covered by the shared-memory key bias/mask table
-// Pairs c of the 32 per P half with (c % NSA_POLY_EVERY == NSA_POLY_EVERY - 1) take the FMA-pipe
-// exp2 in unmasked tiles (0 = none); the rest use ex2.approx on the special-function unit.
-#ifndef NSA_POLY_EVERY
-#define NSA_POLY_EVERY 0
-#endif
 #ifndef NSA_MAX3
 #define NSA_MAX3 1
 #endif
-constexpr int kPolyEvery = NSA_POLY_EVERY;
 
 template <int D>
 struct Cfg {
+  static constexpr bool QTMEM = D <= 96;
   static constexpr int NQ = (D <= 128) ? 2 : 1;
-  static constexpr int NS = (D <= 96) ? 3 : ((D <= 128) ? 2 : 1);   // K and V ring depth
-  static constexpr int BLK = (D % 64 == 0) ? 64 : 32;     // elements per swizzle row
+  static constexpr int BN = (D == 96) ? 112 : 128;                   // keys per K/V tile
+  static constexpr int NS = (D <= 96) ? 3 : ((D <= 128) ? 2 : 1);    // K and V ring depth
+  static constexpr int BLK = (D % 64 == 0) ? 64 : 32;                // elements per swizzle row
   static constexpr int NB = D / BLK;
-  static constexpr int ROWB = BLK * 2;                    // bytes per row of one block
-  static constexpr uint32_t SWZ = (BLK == 64) ? 2u : 4u;  // 128-byte / 64-byte swizzle
-  static constexpr int BLK_BYTES = kTileM * ROWB;         // one [128 rows][BLK] block
-  static constexpr int TILE_BYTES = kTileM * D * 2;
+  static constexpr int ROWB = BLK * 2;                               // bytes per row of one block
+  static constexpr uint32_t SWZ = (BLK == 64) ? 2u : 4u;             // 128-byte / 64-byte swizzle
+  static constexpr int QBLK_BYTES = kTileM * ROWB;                   // [128 rows][BLK]
+  static constexpr int KBLK_BYTES = BN * ROWB;                       // [BN rows][BLK]
+  static constexpr int Q_TILE_BYTES = kTileM * D * 2;   // Q tile staged in shared memory
+  static constexpr int KV_TILE_BYTES = BN * D * 2;
   static constexpr int KSTEPS_QK = D / 16;
-  static constexpr int KSTEPS_PV = kTileN / 16;
+  static constexpr int KSTEPS_PV = BN / 16;
+  static constexpr int PV_HALF0 = 4;                                 // k-steps of keys 0..63
+  static constexpr int P1_COLS = BN / 2 - 32;                        // P columns of keys 64..BN-1
   static constexpr int THREADS = 128 + NQ * 128;
   // Register split (NQ = 2): the block launches at REG_LAUNCH per thread; the first warpgroup
   // (producer, MMA issuer, two idle warps) drops to REG_CTRL and the two softmax warpgroups rise
@@ -59,49 +63,147 @@ struct Cfg {
   // setmaxnreg.inc never waits; the launcher checks the compiled count before every first launch.
   static constexpr int REG_LAUNCH = 168, REG_CTRL = 104, REG_SOFTMAX = 200;
   static_assert(NQ != 2 || 128 * REG_CTRL + 256 * REG_SOFTMAX == THREADS * REG_LAUNCH, "register split");
-  static constexpr int SMEM_TILES = (NQ + 2 * NS) * TILE_BYTES;
-  static constexpr int SMEM_KB = kKeyBiasMax * 4;   // key bias/mask table (log2 units)
+  static constexpr int SMEM_TILES = NQ * Q_TILE_BYTES + 2 * NS * KV_TILE_BYTES;
+  static constexpr int SMEM_KB = kKeyBiasMax * 4 + D * 4;   // key bias/mask table, q norm weights
   // at least 117 KB so that two CTAs never share an SM (each allocates all 512 TMEM columns)
   static constexpr int SMEM_NEED = SMEM_TILES + SMEM_KB + 1024 + 256;
   static constexpr int SMEM_BYTES = SMEM_NEED > 117 * 1024 ? SMEM_NEED : 117 * 1024;
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, kTileN, 0, 0);
+  static constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, BN, 0, 0);
   static constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, D, 0, 1);
-  static_assert(kTileM == kTileN, "Q and K/V tiles share the block geometry");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-  static __device__ __forceinline__ uint32_t s_col(int buf) { return (uint32_t)buf * 128u; }
-  static __device__ __forceinline__ uint32_t o_col(int tile) { return NQ == 2 ? 256u + (uint32_t)tile * 128u : 256u; }
-  // byte offset of MMA k-step kk (16 elements) inside a K-major [128][D] tile
-  static __device__ __forceinline__ uint32_t kmajor_off(int kk) {
+  static_assert(BN % 16 == 0 && BN >= 64 && BN <= 128 && KV_TILE_BYTES % 1024 == 0, "key tile");
+  static __device__ __forceinline__ uint32_t s_col(int buf) { return (uint32_t)(buf * BN); }
+  static __device__ __forceinline__ uint32_t o_col(int tile) {
+    return NQ == 2 ? (uint32_t)(2 * BN + tile * (QTMEM ? D : 128)) : 256u;
+  }
+  static __device__ __forceinline__ uint32_t q_col(int tile) { return (uint32_t)(2 * BN + 2 * D + tile * (D / 2)); }
+  // byte offset of MMA k-step kk (16 elements) inside a K-major [rows][D] tile of row blocks
+  static __device__ __forceinline__ uint32_t kmajor_off(int kk, int blk_bytes) {
     constexpr int per_blk = BLK / 16;
-    return (uint32_t)((kk / per_blk) * BLK_BYTES + (kk % per_blk) * 32);
+    return (uint32_t)((kk / per_blk) * blk_bytes + (kk % per_blk) * 32);
   }
 };
+static_assert(Cfg<96>::QTMEM && 2 * Cfg<96>::BN + 2 * 96 + 96 == 512, "TMEM map, D = 96");
+static_assert(2 * Cfg<64>::BN + 2 * 64 + 64 <= 512, "TMEM map, D = 64");
 
+// S = Q K^T for one tile; Q from shared memory (SS) or tensor memory (TS).
 template <int D>
-__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t sq, uint32_t sk) {
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_src, uint32_t sk) {
   using C = Cfg<D>;
 #pragma unroll
   for (int kk = 0; kk < C::KSTEPS_QK; ++kk) {
-    const uint64_t a = smem_desc(sq + C::kmajor_off(kk), 16, 8 * C::ROWB, C::SWZ);
-    const uint64_t b = smem_desc(sk + C::kmajor_off(kk), 16, 8 * C::ROWB, C::SWZ);
-    mma_ss(d_tmem, a, b, C::IDESC_QK, kk > 0 ? 1u : 0u);
+    const uint64_t b = smem_desc(sk + C::kmajor_off(kk, C::KBLK_BYTES), 16, 8 * C::ROWB, C::SWZ);
+    if constexpr (C::QTMEM) {
+      mma_ts(d_tmem, q_src + (uint32_t)(kk * 8), b, C::IDESC_QK, kk > 0 ? 1u : 0u);
+    } else {
+      const uint64_t a = smem_desc(q_src + C::kmajor_off(kk, C::QBLK_BYTES), 16, 8 * C::ROWB, C::SWZ);
+      mma_ss(d_tmem, a, b, C::IDESC_QK, kk > 0 ? 1u : 0u);
+    }
   }
 }
 
-// O (+)= P V over keys [64*half, 64*half + 64) of the tile: the softmax hands P over in two halves
-// so the tensor core starts on the first while the second is still being exponentiated.
+// O (+)= P V over the keys of one P half (keys 0..63, then 64..BN-1): the softmax hands P over in
+// two halves so the tensor core starts on the first while the second is still being exponentiated.
 template <int D>
 __device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint32_t sv, bool accumulate,
                                               int half) {
   using C = Cfg<D>;
+  const int k_begin = half == 0 ? 0 : C::PV_HALF0;
+  const int k_end = half == 0 ? C::PV_HALF0 : C::KSTEPS_PV;
 #pragma unroll
-  for (int k = 0; k < C::KSTEPS_PV / 2; ++k) {
-    const int kk = half * (C::KSTEPS_PV / 2) + k;
-    // V is MN-major: 16 keys per k-step, head-dim blocks of BLK elements BLK_BYTES apart
-    const uint64_t b = smem_desc(sv + (uint32_t)(kk * 16 * C::ROWB), C::BLK_BYTES, 8 * C::ROWB, C::SWZ);
+  for (int kk = k_begin; kk < k_end; ++kk) {
+    // V is MN-major: 16 keys per k-step, head-dim blocks of BLK elements KBLK_BYTES apart
+    const uint64_t b = smem_desc(sv + (uint32_t)(kk * 16 * C::ROWB), C::KBLK_BYTES, 8 * C::ROWB, C::SWZ);
     mma_ts(d_tmem, p_tmem + (uint32_t)(kk * 8), b, C::IDESC_PV, (accumulate || kk > 0) ? 1u : 0u);
   }
+}
+
+// The RoPE table row of a query row (cos then sin, D/2 each), loaded early so its latency overlaps
+// the TMA load of the query tile.
+template <int D>
+struct RopeRow {
+  float4 c[D / 8], s[D / 8];
+};
+
+template <int D>
+__device__ __forceinline__ void load_rope_row(const AttnParams& p, int row, bool rope, RopeRow<D>& rr) {
+  constexpr int HALF = D / 2;
+  if (rope) {
+    const float4* c4 = reinterpret_cast<const float4*>(p.q_cs + (int64_t)row * HALF);
+    const float4* s4 = reinterpret_cast<const float4*>(p.q_cs + p.q_sin_off + (int64_t)row * HALF);
+#pragma unroll
+    for (int v = 0; v < HALF / 4; ++v) {
+      rr.c[v] = __ldg(c4 + v);
+      rr.s[v] = __ldg(s4 + v);
+    }
+  }
+}
+
+// The prologue of one query row, done by the thread that owns it (row r of the staged tile):
+// read D bf16 values from the swizzled shared-memory tile, RMSNorm with the staged weights w_s
+// (or none), split-half RoPE with the table row, pack to bf16 pairs.  Rows past Lq become zeros.
+template <int D>
+__device__ __forceinline__ void q_row_from_smem(const uint8_t* tile, int r, bool valid, const float* w_s, float eps,
+                                                bool rope, const RopeRow<D>& rr, uint32_t (&qp)[D / 2]) {
+  using C = Cfg<D>;
+  constexpr int HALF = D / 2;
+  constexpr int CHUNKS = C::ROWB / 16;   // 16-byte chunks per row of a swizzle block
+  float x[D];
+#pragma unroll
+  for (int blk = 0; blk < C::NB; ++blk) {
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+      // the TMA swizzle XORs the 16-byte chunk index with the row bits above the chunk span
+      const int phys = c ^ ((r / (128 / C::ROWB)) % CHUNKS);
+      const uint4 a = *reinterpret_cast<const uint4*>(tile + blk * C::QBLK_BYTES + r * C::ROWB + phys * 16);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h2[e]);
+        x[blk * C::BLK + c * 8 + 2 * e] = valid ? f.x : 0.f;
+        x[blk * C::BLK + c * 8 + 2 * e + 1] = valid ? f.y : 0.f;
+      }
+    }
+  }
+  if (w_s) {
+    float ss[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < D; ++i) ss[i & 3] = fmaf(x[i], x[i], ss[i & 3]);
+    const float rn = rsqrtf(((ss[0] + ss[1]) + (ss[2] + ss[3])) / (float)D + eps);
+#pragma unroll
+    for (int i = 0; i < D; ++i) x[i] *= rn * w_s[i];
+  }
+  if (rope) {
+#pragma unroll
+    for (int v = 0; v < HALF / 4; ++v) {
+      const float cc[4] = {rr.c[v].x, rr.c[v].y, rr.c[v].z, rr.c[v].w};
+      const float sn[4] = {rr.s[v].x, rr.s[v].y, rr.s[v].z, rr.s[v].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float a = x[4 * v + e], bb = x[HALF + 4 * v + e];
+        x[4 * v + e] = a * cc[e] - bb * sn[e];
+        x[HALF + 4 * v + e] = bb * cc[e] + a * sn[e];
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < HALF; ++i) qp[i] = pack_bf16x2(x[2 * i], x[2 * i + 1]);
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_n(uint32_t taddr, uint32_t (&r)[N]) {
+  if constexpr (N == 112) tmem_ld112(taddr, r);
+  else if constexpr (N == 128) tmem_ld128(taddr, r);
+  else static_assert(N == 112 || N == 128, "score row width");
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_st_n(uint32_t taddr, const uint32_t (&r)[N]) {
+  if constexpr (N == 24) tmem_st24(taddr, r);
+  else if constexpr (N == 32) tmem_st32(taddr, r);
+  else if constexpr (N == 48) tmem_st48(taddr, r);
+  else static_assert(N == 24 || N == 32 || N == 48, "column count");
 }
 
 template <int D>
@@ -109,16 +211,18 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   using C = Cfg<D>;
-  constexpr int NQ = C::NQ, NS = C::NS;
+  constexpr int NQ = C::NQ, NS = C::NS, BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sK = sQ + NQ * C::TILE_BYTES;
-  uint8_t* sV = sK + NS * C::TILE_BYTES;
-  float* kb = reinterpret_cast<float*>(sV + NS * C::TILE_BYTES);   // [kKeyBiasMax]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(kb + kKeyBiasMax);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
+  uint8_t* sK = sQ + NQ * C::Q_TILE_BYTES;
+  uint8_t* sV = sK + NS * C::KV_TILE_BYTES;
+  float* kb = reinterpret_cast<float*>(sV + NS * C::KV_TILE_BYTES);   // [kKeyBiasMax]
+  float* qw_s = kb + kKeyBiasMax;                                      // [D] q norm weights
+  uint64_t* bars = reinterpret_cast<uint64_t*>(qw_s + D);
+  uint64_t* q_full = bars;           // [2]   Q ready for the MMA (QTMEM: rows stored in TMEM)
+  uint64_t* q_smem = bars + 2;       //       Q tile(s) landed in shared memory (QTMEM)
+  uint64_t* k_full = bars + 3;
   uint64_t* k_empty = k_full + NS;
   uint64_t* v_full = k_empty + NS;
   uint64_t* v_empty = v_full + NS;
@@ -144,14 +248,16 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   int kv_end = kv_valid;
   if (p.causal) kv_end = min(kv_end, q_row_end);
   const int kv_begin = p.window > 0 ? max(0, q_row0 - p.window + 1) : 0;
-  const int j0 = kv_begin / kTileN;
-  const int n = kv_end > kv_begin ? ((kv_end - 1) / kTileN - j0 + 1) : 0;
+  const int j0 = kv_begin / BN;
+  const int n = kv_end > kv_begin ? ((kv_end - 1) / BN - j0 + 1) : 0;
   const int q_tma_row = (bl * p.Hq + hl) * p.Lq_pad + q_row0;
   const int kv_tma_row = (bl * p.Hkv + hkvl) * p.Lk_pad;
   const uint64_t to = p.timeout_ns;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    mbar_init(&q_full[0], C::QTMEM ? 128 : 1);
+    mbar_init(&q_full[1], C::QTMEM ? 128 : 1);
+    mbar_init(q_smem, 1);
     for (int s = 0; s < NS; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -187,28 +293,40 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0 && n > 0) {
       bool ok = true;
-      mbar_arrive_expect_tx(q_full, NQ * C::TILE_BYTES);
-      for (int i = 0; i < NQ; ++i)
-        for (int c = 0; c < C::NB; ++c)
-          tma_load_2d(sQ + i * C::TILE_BYTES + c * C::BLK_BYTES, &tmQ, q_full, c * C::BLK, q_tma_row + i * kTileM);
+      if constexpr (!C::QTMEM) {
+        mbar_arrive_expect_tx(&q_full[0], NQ * C::Q_TILE_BYTES);
+        for (int i = 0; i < NQ; ++i)
+          for (int c = 0; c < C::NB; ++c)
+            tma_load_2d(sQ + i * C::Q_TILE_BYTES + c * C::QBLK_BYTES, &tmQ, &q_full[0], c * C::BLK,
+                        q_tma_row + i * kTileM);
+      } else {
+        // raw (or prologue-prepared) query rows of this block; the softmax threads take it from here
+        const int hq = p.hq_begin + hl;
+        const int qx = p.q_x0 + (hq - p.q_h0) * p.q_xh;
+        const int qy = (b - p.q_b0) * p.q_yb + (hq - p.q_h0) * p.q_yh + q_row0;
+        mbar_arrive_expect_tx(q_smem, NQ * C::Q_TILE_BYTES);
+        for (int i = 0; i < NQ; ++i)
+          for (int c = 0; c < C::NB; ++c)
+            tma_load_2d(sQ + i * C::Q_TILE_BYTES + c * C::QBLK_BYTES, &tmQ, q_smem, qx + c * C::BLK, qy + i * kTileM);
+      }
       auto load_k = [&](int j) -> bool {
         const int s = j % NS;
         if (j >= NS && !wait_bounded(&k_empty[s], ((j / NS) - 1) & 1, abort_flag, p.err, kErrTimeoutLoad, to))
           return false;
-        mbar_arrive_expect_tx(&k_full[s], C::TILE_BYTES);
+        mbar_arrive_expect_tx(&k_full[s], C::KV_TILE_BYTES);
         for (int c = 0; c < C::NB; ++c)
-          tma_load_2d(sK + s * C::TILE_BYTES + c * C::BLK_BYTES, &tmK, &k_full[s], c * C::BLK,
-                      kv_tma_row + (j0 + j) * kTileN);
+          tma_load_2d(sK + s * C::KV_TILE_BYTES + c * C::KBLK_BYTES, &tmK, &k_full[s], c * C::BLK,
+                      kv_tma_row + (j0 + j) * BN);
         return true;
       };
       auto load_v = [&](int j) -> bool {
         const int s = j % NS;
         if (j >= NS && !wait_bounded(&v_empty[s], ((j / NS) - 1) & 1, abort_flag, p.err, kErrTimeoutLoad, to))
           return false;
-        mbar_arrive_expect_tx(&v_full[s], C::TILE_BYTES);
+        mbar_arrive_expect_tx(&v_full[s], C::KV_TILE_BYTES);
         for (int c = 0; c < C::NB; ++c)
-          tma_load_2d(sV + s * C::TILE_BYTES + c * C::BLK_BYTES, &tmV, &v_full[s], c * C::BLK,
-                      kv_tma_row + (j0 + j) * kTileN);
+          tma_load_2d(sV + s * C::KV_TILE_BYTES + c * C::KBLK_BYTES, &tmV, &v_full[s], c * C::BLK,
+                      kv_tma_row + (j0 + j) * BN);
         return true;
       };
       int k_issued = 0, v_issued = 0;
@@ -225,7 +343,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
       // On an abort, wait (bounded) for the copies already issued so none lands after exit:
       // the latest issue into each stage completes after the earlier ones.
       if (!ok) {
-        wait_drain(q_full, 0, 20000000ull);
+        wait_drain(C::QTMEM ? q_smem : &q_full[0], 0, 20000000ull);
         for (int j = k_issued - 1; j >= 0 && j >= k_issued - NS; --j) wait_drain(&k_full[j % NS], (j / NS) & 1, 20000000ull);
         for (int j = v_issued - 1; j >= 0 && j >= v_issued - NS; --j) wait_drain(&v_full[j % NS], (j / NS) & 1, 20000000ull);
       }
@@ -233,16 +351,26 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0 && n > 0) {
-      const uint32_t sq = smem_u32(sQ), sk = smem_u32(sK), sv = smem_u32(sV);
-      bool ok = wait_bounded(q_full, 0, abort_flag, p.err, kErrTimeoutMma, to);
+      const uint32_t sk = smem_u32(sK), sv = smem_u32(sV);
+      // Q source of tile i: TMEM columns (QTMEM) or the shared-memory tile
+      auto q_src = [&](int i) -> uint32_t {
+        return C::QTMEM ? tmem + C::q_col(i) : smem_u32(sQ) + (uint32_t)(i * C::Q_TILE_BYTES);
+      };
+      bool ok = true;
+      if constexpr (C::QTMEM) {
+        ok = wait_bounded(&q_full[0], 0, abort_flag, p.err, kErrTimeoutMma, to) &&
+             (NQ == 1 || wait_bounded(&q_full[1], 0, abort_flag, p.err, kErrTimeoutMma, to));
+      } else {
+        ok = wait_bounded(&q_full[0], 0, abort_flag, p.err, kErrTimeoutMma, to);
+      }
       tc_fence_after();
       if constexpr (NQ == 2) {
         if (ok) ok = wait_bounded(&k_full[0], 0, abort_flag, p.err, kErrTimeoutMma, to);
         if (ok) {
           tc_fence_after();
-          issue_qk<D>(tmem + C::s_col(0), sq, sk);
+          issue_qk<D>(tmem + C::s_col(0), q_src(0), sk);
           tc_commit(&s_full[0]);
-          issue_qk<D>(tmem + C::s_col(1), sq + C::TILE_BYTES, sk);
+          issue_qk<D>(tmem + C::s_col(1), q_src(1), sk);
           tc_commit(&s_full[1]);
           tc_commit(&k_empty[0]);
         }
@@ -251,7 +379,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
           for (int h = 0; h < 2; ++h) {
             if (!wait_bounded(&p_full[i * 2 + h], jj & 1, abort_flag, p.err, kErrTimeoutMma, to)) return false;
             tc_fence_after();
-            issue_pv_half<D>(tmem + C::o_col(i), tmem + C::s_col(i), sv + svs * C::TILE_BYTES, jj > 0, h);
+            issue_pv_half<D>(tmem + C::o_col(i), tmem + C::s_col(i), sv + svs * C::KV_TILE_BYTES, jj > 0, h);
           }
           return true;
         };
@@ -262,12 +390,12 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
           ok = wait_bounded(&k_full[sks], (j / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to);
           if (!ok) break;
           tc_fence_after();
-          issue_qk<D>(tmem + C::s_col(0), sq, sk + sks * C::TILE_BYTES);
+          issue_qk<D>(tmem + C::s_col(0), q_src(0), sk + sks * C::KV_TILE_BYTES);
           tc_commit(&s_full[0]);
           ok = pv(1, j - 1, svs);
           if (!ok) break;
           tc_commit(&v_empty[svs]);
-          issue_qk<D>(tmem + C::s_col(1), sq + C::TILE_BYTES, sk + sks * C::TILE_BYTES);
+          issue_qk<D>(tmem + C::s_col(1), q_src(1), sk + sks * C::KV_TILE_BYTES);
           tc_commit(&s_full[1]);
           tc_commit(&k_empty[sks]);
         }
@@ -286,7 +414,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
           ok = wait_bounded(&k_full[j % NS], (j / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to);
           if (!ok) break;
           tc_fence_after();
-          issue_qk<D>(tmem + C::s_col(j & 1), sq, sk + (j % NS) * C::TILE_BYTES);
+          issue_qk<D>(tmem + C::s_col(j & 1), q_src(0), sk + (j % NS) * C::KV_TILE_BYTES);
           tc_commit(&s_full[j & 1]);
           tc_commit(&k_empty[j % NS]);
         }
@@ -297,7 +425,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             ok = wait_bounded(&p_full[h], j & 1, abort_flag, p.err, kErrTimeoutMma, to);
             if (!ok) break;
             tc_fence_after();
-            issue_pv_half<D>(tmem + C::o_col(0), tmem + C::s_col(j & 1), sv + svs * C::TILE_BYTES, j > 0, h);
+            issue_pv_half<D>(tmem + C::o_col(0), tmem + C::s_col(j & 1), sv + svs * C::KV_TILE_BYTES, j > 0, h);
           }
           if (!ok) break;
           tc_commit(&o_full[0]);
@@ -307,7 +435,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             ok = wait_bounded(&k_full[sks], ((j + 2) / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to);
             if (!ok) break;
             tc_fence_after();
-            issue_qk<D>(tmem + C::s_col(j & 1), sq, sk + sks * C::TILE_BYTES);
+            issue_qk<D>(tmem + C::s_col(j & 1), q_src(0), sk + sks * C::KV_TILE_BYTES);
             tc_commit(&s_full[j & 1]);
             tc_commit(&k_empty[sks]);
           }
@@ -331,12 +459,15 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     const float sl2 = p.scale_log2;
     const float* bias_b = p.bias ? p.bias + (int64_t)b * p.bias_bstride : nullptr;
+    RopeRow<D> rr;
+    const bool q_rope = C::QTMEM && p.q_cs != nullptr && row < p.Lq && row < p.q_rope_rows;
+    if constexpr (C::QTMEM) load_rope_row<D>(p, row, q_rope, rr);
     // Key bias + padding mask of the tiles that need one, in log2 units, for keys [kb0, kb0 +
     // kKeyBiasMax): 0 for plain keys, log(w)*log2(e) for biased text keys, -inf past kv_valid.
     // Built once per CTA by the softmax threads (named barrier 1 over them).
     int kb0 = min(kv_valid, bias_b ? p.bias_start : kv_valid);
-    kb0 = max(kb0 - kb0 % kTileN, j0 * kTileN);
-    const int kb_end = (j0 + n) * kTileN;
+    kb0 = max(kb0 - kb0 % BN, j0 * BN);
+    const int kb_end = (j0 + n) * BN;
     const bool kb_ok = kb_end - kb0 <= kKeyBiasMax;
     if (kb_ok) {
       for (int i = threadIdx.x - 128; i < kb_end - kb0; i += NQ * 128) {
@@ -346,25 +477,42 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         kb[i] = key < kv_valid ? v : -INFINITY;
       }
     }
+    if (C::QTMEM && p.q_w) {
+      for (int i = threadIdx.x - 128; i < D; i += NQ * 128) qw_s[i] = p.q_w[i];
+    }
     asm volatile("bar.sync 1, %0;" ::"n"(NQ * 128) : "memory");
-    float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
+    if constexpr (C::QTMEM) {
+      // this thread's query row, normalised and rotated, into the Q columns of its TMEM lane
+      if (n > 0) {
+        ok = __all_sync(0xffffffffu, wait_bounded(q_smem, 0, abort_flag, p.err, kErrTimeoutSoftmax, to));
+        if (ok) {
+          uint32_t qp[D / 2];
+          q_row_from_smem<D>(sQ + tile * C::Q_TILE_BYTES, quarter * 32 + lane, row < p.Lq, p.q_w ? qw_s : nullptr,
+                             p.q_eps, q_rope, rr, qp);
+          tmem_st_n<D / 2>(lane_base + C::q_col(tile), qp);
+          tc_fence_before();
+          mbar_arrive(&q_full[tile]);
+        }
+      }
+    }
+    float m_run = -INFINITY, l_run = 0.f;
+    for (int j = 0; ok && j < n; ++j) {
       const int sbuf = NQ == 2 ? tile : (j & 1);
       const uint32_t sparity = NQ == 2 ? (uint32_t)(j & 1) : (uint32_t)((j >> 1) & 1);
       ok = __all_sync(0xffffffffu, wait_bounded(&s_full[sbuf], sparity, abort_flag, p.err, kErrTimeoutSoftmax, to));
       if (!ok) break;
       tc_fence_after();
-      const int key0 = (j0 + j) * kTileN;
-      const bool t_invalid = key0 + kTileN > kv_valid;
-      const bool t_causal = p.causal && key0 + kTileN - 1 > tile_row0;
+      const int key0 = (j0 + j) * BN;
+      const bool t_invalid = key0 + BN > kv_valid;
+      const bool t_causal = p.causal && key0 + BN - 1 > tile_row0;
       const bool t_window = p.window > 0 && key0 <= tile_row0 + kTileM - 1 - p.window;
-      const bool t_bias = bias_b != nullptr && key0 + kTileN > p.bias_start && key0 < p.bias_start + p.bias_len;
+      const bool t_bias = bias_b != nullptr && key0 + BN > p.bias_start && key0 < p.bias_start + p.bias_len;
       const uint32_t s_addr = lane_base + C::s_col(sbuf);
-      // Unmasked tiles keep the raw scores and fold the scale into the exponent (one FFMA per
-      // element).  Masked tiles (text bias, padding, causal or window edges; a few per row) are
-      // first rewritten in TMEM, 32 columns at a time, into scaled, biased, masked logits, and then
-      // take the same path with a unit scale.
+      // Unmasked tiles keep the raw scores and fold the scale into the exponent.  Tiles with a text
+      // bias or padding take the bias / -inf from the shared table; tiles on a causal or window
+      // edge (or beyond the table) are first rewritten in TMEM, 16 columns at a time, into scaled,
+      // biased, masked logits.  Both then use a unit scale.
       float sc = sl2;
       const bool t_table = kb_ok && !t_causal && !t_window && (t_invalid || t_bias);
       if (!t_table && (t_invalid || t_causal || t_window || t_bias)) {
@@ -372,26 +520,26 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         const int lo = p.window > 0 ? row - p.window + 1 : 0;            // first visible key
         const int hi = p.causal ? min(kv_valid, row + 1) : kv_valid;     // one past the last
 #pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t r[32];
-          tmem_ld32(s_addr + (uint32_t)(cc * 32), r);
+        for (int cc = 0; cc < BN / 16; ++cc) {
+          uint32_t r[16];
+          tmem_ld16(s_addr + (uint32_t)(cc * 16), r);
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int key = key0 + cc * 32 + c;
+          for (int c = 0; c < 16; ++c) {
+            const int key = key0 + cc * 16 + c;
             float v = __uint_as_float(r[c]) * sl2;
             if (t_bias && key >= p.bias_start && key < p.bias_start + p.bias_len)
               v += __ldg(bias_b + (key - p.bias_start)) * kLog2e;
             r[c] = __float_as_uint(key >= lo && key < hi ? v : -INFINITY);
           }
-          tmem_st32(s_addr + (uint32_t)(cc * 32), r);
+          tmem_st16(s_addr + (uint32_t)(cc * 16), r);
         }
       }
-      float x[128];
+      float x[BN];
       {
-        uint32_t r[128];
-        tmem_ld128(s_addr, r);
+        uint32_t r[BN];
+        tmem_ld_n<BN>(s_addr, r);
 #pragma unroll
-        for (int c = 0; c < 128; ++c) x[c] = __uint_as_float(r[c]);
+        for (int c = 0; c < BN; ++c) x[c] = __uint_as_float(r[c]);
       }
       if (t_table) {
         // scaled logits + key bias / -inf from the shared table (broadcast reads)
@@ -399,7 +547,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         const float4* kt = reinterpret_cast<const float4*>(kb + (key0 - kb0));
         const uint64_t sl2x2 = f2_pack(sl2, sl2);
 #pragma unroll
-        for (int c = 0; c < 128; c += 4) {
+        for (int c = 0; c < BN; c += 4) {
           const float4 kv4 = kt[c / 4];
           f2_unpack(f2_fma(f2_pack(x[c], x[c + 1]), sl2x2, f2_pack(kv4.x, kv4.y)), x[c], x[c + 1]);
           f2_unpack(f2_fma(f2_pack(x[c + 2], x[c + 3]), sl2x2, f2_pack(kv4.z, kv4.w)), x[c + 2], x[c + 3]);
@@ -410,7 +558,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
 #pragma unroll
       for (int k = 0; k < 4; ++k) mx[k] = fmaxf(x[2 * k], x[2 * k + 1]);
 #pragma unroll
-      for (int c = 8; c < 128; c += 8) {
+      for (int c = 8; c < BN; c += 8) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) mx[k] = fmax3(mx[k], x[c + 2 * k], x[c + 2 * k + 1]);
       }
@@ -420,7 +568,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
 #pragma unroll
       for (int k = 0; k < 8; ++k) mx[k] = x[k];
 #pragma unroll
-      for (int c = 8; c < 128; ++c) mx[c & 7] = fmaxf(mx[c & 7], x[c]);
+      for (int c = 8; c < BN; ++c) mx[c & 7] = fmaxf(mx[c & 7], x[c]);
       const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sc;
 #endif
       const float m_new = fmaxf(m_run, tmax);
@@ -441,50 +589,59 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             if (!ok) break;
             tc_fence_after();
           }
+          const uint64_t a2 = f2_pack(alpha, alpha);
 #pragma unroll 1
           for (int cc = 0; cc < D / 32; ++cc) {
             uint32_t r[32];
             const uint32_t oaddr = lane_base + C::o_col(tile) + (uint32_t)(cc * 32);
             tmem_ld32(oaddr, r);
 #pragma unroll
-            for (int c = 0; c < 32; ++c) r[c] = __float_as_uint(__uint_as_float(r[c]) * alpha);
+            for (int c = 0; c < 32; c += 2) {
+              float lo, hi;
+              f2_unpack(f2_mul(f2_pack(__uint_as_float(r[c]), __uint_as_float(r[c + 1])), a2), lo, hi);
+              r[c] = __float_as_uint(lo);
+              r[c + 1] = __float_as_uint(hi);
+            }
             tmem_st32(oaddr, r);
           }
         }
       }
       const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
       const uint64_t sc2 = f2_pack(sc, sc), nm2 = f2_pack(neg_m, neg_m);
-      const bool poly_ok = kPolyEvery > 0 && sc == sl2;   // unmasked tile: every logit is finite
-      uint64_t ls[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) ls[k] = 0ull;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      uint64_t ls[4] = {0ull, 0ull, 0ull, 0ull};
+      {
+        // keys 0..63 -> P columns 0..31
         uint32_t pk[32];
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          const uint64_t y = f2_fma(f2_pack(x[64 * h + 2 * c], x[64 * h + 2 * c + 1]), sc2, nm2);
-          float a0, a1;
-          if (kPolyEvery > 0 && c % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1 && poly_ok) {
-            ex2_poly2(y, a0, a1);
-          } else {
-            float y0, y1;
-            f2_unpack(y, y0, y1);
-            a0 = ex2(y0);
-            a1 = ex2(y1);
-          }
+          float y0, y1;
+          f2_unpack(f2_fma(f2_pack(x[2 * c], x[2 * c + 1]), sc2, nm2), y0, y1);
+          const float a0 = ex2(y0), a1 = ex2(y1);
           ls[c & 3] = f2_add(ls[c & 3], f2_pack(a0, a1));
           pk[c] = pack_bf16x2(a0, a1);
         }
-        tmem_st32(s_addr + (uint32_t)(32 * h), pk);
+        tmem_st32(s_addr, pk);
         tc_fence_before();
-        mbar_arrive(&p_full[(NQ == 2 ? tile : 0) * 2 + h]);
+        mbar_arrive(&p_full[(NQ == 2 ? tile : 0) * 2]);
       }
       {
-        float s0, s1, s2, s3;
+        // keys 64..BN-1 -> P columns 32..BN/2-1
+        uint32_t pk[C::P1_COLS];
+#pragma unroll
+        for (int c = 0; c < C::P1_COLS; ++c) {
+          float y0, y1;
+          f2_unpack(f2_fma(f2_pack(x[64 + 2 * c], x[64 + 2 * c + 1]), sc2, nm2), y0, y1);
+          const float a0 = ex2(y0), a1 = ex2(y1);
+          ls[c & 3] = f2_add(ls[c & 3], f2_pack(a0, a1));
+          pk[c] = pack_bf16x2(a0, a1);
+        }
+        tmem_st_n<C::P1_COLS>(s_addr + 32u, pk);
+        tc_fence_before();
+        mbar_arrive(&p_full[(NQ == 2 ? tile : 0) * 2 + 1]);
+      }
+      {
+        float s0, s1;
         f2_unpack(f2_add(f2_add(ls[0], ls[1]), f2_add(ls[2], ls[3])), s0, s1);
-        (void)s2;
-        (void)s3;
         l_run += s0 + s1;
       }
     }
@@ -578,23 +735,13 @@ cudaError_t launch_d(const AttnParams& p, const CUtensorMap& tmQ, const CUtensor
 
 }  // namespace
 
-int attention_q_tiles_per_block(int D) {
+AttnGeometry attention_geometry(int D) {
   switch (D) {
-    case 64: return Cfg<64>::NQ;
-    case 96: return Cfg<96>::NQ;
-    case 128: return Cfg<128>::NQ;
-    case 256: return Cfg<256>::NQ;
-    default: return 0;
-  }
-}
-
-int attention_block_elems(int D) {
-  switch (D) {
-    case 64: return Cfg<64>::BLK;
-    case 96: return Cfg<96>::BLK;
-    case 128: return Cfg<128>::BLK;
-    case 256: return Cfg<256>::BLK;
-    default: return 0;
+    case 64: return {Cfg<64>::NQ, Cfg<64>::BN, Cfg<64>::BLK, Cfg<64>::QTMEM};
+    case 96: return {Cfg<96>::NQ, Cfg<96>::BN, Cfg<96>::BLK, Cfg<96>::QTMEM};
+    case 128: return {Cfg<128>::NQ, Cfg<128>::BN, Cfg<128>::BLK, Cfg<128>::QTMEM};
+    case 256: return {Cfg<256>::NQ, Cfg<256>::BN, Cfg<256>::BLK, Cfg<256>::QTMEM};
+    default: return {0, 0, 0, false};
   }
 }
 

@@ -13,12 +13,14 @@ namespace nsa {
 constexpr int kTileM = 128;  // query rows per tensor-core tile (one TMEM lane per row)
 constexpr int kTileN = 128;  // keys per K/V tile
 
-// One strided input matrix: element (b, row, col) lives at ptr[b*bstride + row*ld + off + col].
+// One strided input matrix: element (b, row, col) lives at ptr[b*bstride + row*ld + off + col];
+// each batch element holds `rows` rows.
 struct RowView {
   const void* ptr;
   int64_t ld;
   int64_t bstride;
   int64_t off;
+  int64_t rows;
 };
 
 // Prologue: raw rows -> head-major bf16 tiles [b][head][row][D] (rows padded with zeros), with the
@@ -42,6 +44,7 @@ struct PrologueParams {
   __nv_bfloat16* Ks;
   __nv_bfloat16* Vs;
   int Lq_pad, Lk_pad;
+  int skip_q;           // 1: the attention kernel reads and prepares Q itself (no Q tiles written)
 };
 
 struct AttnParams {
@@ -61,15 +64,33 @@ struct AttnParams {
   int q_blocks;            // query blocks (NQ tiles each) per (b, head)
   int* err;
   unsigned long long timeout_ns;
+  // Kernels that keep Q in tensor memory TMA-load the query tile from tmQ into shared memory:
+  // box (x, y) with x = q_x0 + (head - q_h0)*q_xh + c*blk and
+  // y = (b - q_b0)*q_yb + (head - q_h0)*q_yh + row; the softmax threads then apply RMSNorm with q_w
+  // (if set) and RoPE with q_cs for rows < q_rope_rows (if set) and store the row into TMEM.
+  int q_x0, q_xh, q_yb, q_yh;
+  int q_b0, q_h0;
+  const float* q_w;
+  float q_eps;
+  const float* q_cs;
+  int64_t q_sin_off;
+  int q_rope_rows;
 };
+
+// Tile geometry of the attention kernel for a head dim.
+struct AttnGeometry {
+  int NQ;       // query tiles of 128 rows per CTA
+  int BN;       // keys per K/V tile (TMA box rows)
+  int blk;      // swizzle block width in elements (TMA box columns)
+  bool qtmem;   // Q prepared by the kernel itself into tensor memory
+};
+AttnGeometry attention_geometry(int D);   // NQ = 0: unsupported head dim
 
 cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream);
 
 // Returns cudaErrorInvalidValue for unsupported head dims.
 cudaError_t launch_attention(const AttnParams& p, int D, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                              const CUtensorMap& tmV, cudaStream_t stream);
-int attention_q_tiles_per_block(int D);   // NQ: query tiles per CTA for head dim D (0: unsupported)
-int attention_block_elems(int D);         // swizzle block width (elements) of the TMA boxes
 
 cudaError_t launch_head_norm(void* X, int f32, const float* w, int L, int H, int D, int64_t ld, int64_t col_off,
                              int64_t row_off, const float* cs, int64_t sin_off, float eps, cudaStream_t stream);

@@ -32,7 +32,7 @@ __global__ void __launch_bounds__(kPrologueThreads) prologue_kernel(const Prolog
   const int row = blockIdx.x;
   const int bl = blockIdx.y;          // batch index within the shard
   const int b = p.b_begin + bl;       // global batch index
-  const int part = blockIdx.z;
+  const int part = blockIdx.z + (p.skip_q ? 1 : 0);
   const int pad = part == 0 ? p.Lq_pad : p.Lk_pad;
   if (row >= pad) return;
 
@@ -113,12 +113,15 @@ __global__ void __launch_bounds__(kPrologueThreads) prologue_kernel(const Prolog
 // RoPE pair (i, i + D/2) stays in one thread, every load and store is a 16-byte vector, and the
 // RMSNorm sum is a P-lane shuffle reduction.  grid.y = part * B + batch element.
 template <int D, int P, typename T>
-__global__ void __launch_bounds__(256) prologue_vec_kernel(const PrologueParams p) {
+#ifndef NSA_PROLOGUE_MIN_BLOCKS
+#define NSA_PROLOGUE_MIN_BLOCKS 3
+#endif
+__global__ void __launch_bounds__(256, NSA_PROLOGUE_MIN_BLOCKS) prologue_vec_kernel(const PrologueParams p) {
   constexpr int S = D / (2 * P);
   constexpr int HALF = D / 2;
   constexpr int EPV = 16 / sizeof(T);   // input elements per 16-byte vector
   static_assert(S % 8 == 0 && S % EPV == 0, "vector width");
-  const int part = blockIdx.y / p.B;
+  const int part = blockIdx.y / p.B + (p.skip_q ? 1 : 0);
   const int bl = blockIdx.y % p.B;
   const int b = p.b_begin + bl;
   const int H = part == 0 ? p.Hq : p.Hkv;
@@ -315,12 +318,12 @@ bool vec_ok(const PrologueParams& p, int elem) {
 
 template <int D, int P, typename T>
 cudaError_t launch_vec(const PrologueParams& p, cudaStream_t stream) {
-  const int rows = p.Lq_pad > p.Lk_pad ? p.Lq_pad : p.Lk_pad;
-  const int H = p.Hq > p.Hkv ? p.Hq : p.Hkv;
+  const int rows = (!p.skip_q && p.Lq_pad > p.Lk_pad) ? p.Lq_pad : p.Lk_pad;
+  const int H = (!p.skip_q && p.Hq > p.Hkv) ? p.Hq : p.Hkv;
   const long long threads = (long long)rows * H * P;
   const long long blocks = (threads + 255) / 256;
   if (blocks > 0x7FFFFFFFLL || 3LL * p.B > 65535) return cudaErrorInvalidValue;
-  prologue_vec_kernel<D, P, T><<<dim3((unsigned)blocks, 3 * p.B), 256, 0, stream>>>(p);
+  prologue_vec_kernel<D, P, T><<<dim3((unsigned)blocks, (p.skip_q ? 2 : 3) * p.B), 256, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
@@ -338,12 +341,12 @@ cudaError_t launch_vec_t(const PrologueParams& p, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream) {
-  const int rows = p.Lq_pad > p.Lk_pad ? p.Lq_pad : p.Lk_pad;
+  const int rows = (!p.skip_q && p.Lq_pad > p.Lk_pad) ? p.Lq_pad : p.Lk_pad;
   if (rows <= 0 || p.B <= 0) return cudaSuccess;
   const int elem = p.src_f32 ? 4 : 2;
   if ((p.D == 64 || p.D == 96 || p.D == 128 || p.D == 256) && vec_ok(p, elem))
     return p.src_f32 ? launch_vec_t<float>(p, stream) : launch_vec_t<__nv_bfloat16>(p, stream);
-  dim3 grid(rows, p.B, 3);
+  dim3 grid(rows, p.B, p.skip_q ? 2 : 3);
   prologue_kernel<<<grid, kPrologueThreads, 0, stream>>>(p);
   return cudaGetLastError();
 }

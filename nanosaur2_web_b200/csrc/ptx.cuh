@@ -176,87 +176,6 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn, in
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
-// TMEM loads/stores: 32 lanes x 32-bit, N consecutive columns per thread.  The load and its
-// wait::ld sit in one asm statement so the compiler cannot use the registers early.
-#define NSA_R8(i) "=r"(r[i + 0]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), \
-                  "=r"(r[i + 6]), "=r"(r[i + 7])
-#define NSA_W8(i) "r"(r[i + 0]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), "r"(r[i + 5]), \
-                  "r"(r[i + 6]), "r"(r[i + 7])
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : NSA_R8(0), NSA_R8(8), NSA_R8(16), NSA_R8(24)
-      : "r"(taddr)
-      : "memory");
-}
-
-// 64 columns as two x32 loads followed by a single wait.
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
-      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : NSA_R8(0), NSA_R8(8), NSA_R8(16), NSA_R8(24), NSA_R8(32), NSA_R8(40), NSA_R8(48), NSA_R8(56)
-      : "r"(taddr), "r"(taddr + 32u)
-      : "memory");
-}
-
-// 128 columns as four x32 loads followed by a single wait.
-__device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&r)[128]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%128];\n\t"
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
-      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%129];\n\t"
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,"
-      "%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95}, [%130];\n\t"
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,"
-      "%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%131];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : NSA_R8(0), NSA_R8(8), NSA_R8(16), NSA_R8(24), NSA_R8(32), NSA_R8(40), NSA_R8(48), NSA_R8(56),
-        NSA_R8(64), NSA_R8(72), NSA_R8(80), NSA_R8(88), NSA_R8(96), NSA_R8(104), NSA_R8(112), NSA_R8(120)
-      : "r"(taddr), "r"(taddr + 32u), "r"(taddr + 64u), "r"(taddr + 96u)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n\t"
-      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
-      NSA_W8(0), NSA_W8(8), NSA_W8(16), NSA_W8(24)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t (&r)[64]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
-      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33};\n\t"
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%1], "
-      "{%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,"
-      "%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65};\n\t"
-      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
-      "r"(taddr + 32u), NSA_W8(0), NSA_W8(8), NSA_W8(16), NSA_W8(24), NSA_W8(32), NSA_W8(40), NSA_W8(48),
-      NSA_W8(56)
-      : "memory");
-}
-
-#undef NSA_R8
-#undef NSA_W8
 
 // Per-warpgroup register reallocation; every warp of the warpgroup executes it.
 template <int N>
@@ -351,3 +270,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 }  // namespace nsa
+
+// tcgen05.ld / tcgen05.st of N columns with the wait in the same asm statement (generated).
+#include "tmem_ops.cuh"
