@@ -236,7 +236,7 @@ def run_ours(args, rank, world, local_rank):
     from nanosaur2_web_b200 import _lib
     from nanosaur2_web_b200.blocks import dit_block_attention, fused_workspace_bytes
     from nanosaur2_web_b200.ops import check_device, rope2dTable
-    from nanosaur2_web_b200.sharding import max_over_ranks
+    from nanosaur2_web_b200.sharding import max_over_ranks, sum_over_ranks
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -286,7 +286,7 @@ def run_ours(args, rank, world, local_rank):
     clock = clocks.summary()
     ms_max = max_over_ranks(ms)
     total_flops = sum(flops[i % NBUF] for i in range(args.steps))
-    total_flops_all = max_over_ranks(total_flops) * world   # every rank runs the same-size batch
+    total_flops_all = sum_over_ranks(total_flops)
     value = total_flops_all / (ms_max * 1e-3) / 1e12
 
     # ---- per-kernel roofline pass: library profiler events around each launch, same stream
@@ -340,7 +340,7 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     check_device(dev)
-    e2e_flops = max_over_ranks(sum(flops[i % NBUF] for i in range(e2e_steps))) * world
+    e2e_flops = sum_over_ranks(sum(flops[i % NBUF] for i in range(e2e_steps)))
     e2e_value = e2e_flops / (e2e_ms * 1e-3) / 1e12
     h2d = hq[0].numel() * 2 + hk[0].numel() * 4 + hb[0].numel() * 4
     d2h = hout.numel() * 2

@@ -43,8 +43,7 @@ def shard_batch_heads(B: int, H: int, world: int, rank: int) -> List[Tuple[int, 
     return merged
 
 
-def max_over_ranks(value: float, group=None) -> float:
-    """Max of a per-rank float over the process group (identity without torch.distributed)."""
+def _reduce(value: float, op_name: str, group=None) -> float:
     import torch
     import torch.distributed as dist
 
@@ -53,5 +52,15 @@ def max_over_ranks(value: float, group=None) -> float:
     backend = dist.get_backend(group)
     dev = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else torch.device("cpu")
     t = torch.tensor([value], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    dist.all_reduce(t, op=getattr(dist.ReduceOp, op_name), group=group)
     return float(t.item())
+
+
+def max_over_ranks(value: float, group=None) -> float:
+    """Max of a per-rank float over the process group (identity without torch.distributed)."""
+    return _reduce(value, "MAX", group)
+
+
+def sum_over_ranks(value: float, group=None) -> float:
+    """Sum of a per-rank float over the process group (identity without torch.distributed)."""
+    return _reduce(value, "SUM", group)

@@ -30,7 +30,8 @@ def _worker(rank, world, port, q):
         gathered = [None] * world
         dist.all_gather_object(gathered, units)
         t = sharding.max_over_ranks(float(rank + 1) * 1.5)
-        q.put((rank, gathered, t))
+        tot = sharding.sum_over_ranks(float(rank + 1))
+        q.put((rank, gathered, t, tot))
     finally:
         dist.destroy_process_group()
 
@@ -47,8 +48,9 @@ def test_two_rank_sharding_and_timing_reduction():
     for p in procs:
         p.join(timeout=30)
         assert p.exitcode == 0
-    for rank, gathered, t in results:
+    for rank, gathered, t, tot in results:
         allu = sorted(u for part in gathered for u in part)
         assert allu == [(b, h) for b in range(2) for h in range(16)]
         assert set(gathered[0]).isdisjoint(gathered[1])
         assert t == 3.0
+        assert tot == 3.0
