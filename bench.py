@@ -370,6 +370,243 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- configs 3, 4 and 5
+
+def _timed(step, steps, warmup, world, stream):
+    """Warm-up, then ``steps`` steps between CUDA events on ``stream`` with a barrier and a device
+    synchronise on both sides; returns the max over ranks of the elapsed ms."""
+    import torch
+    import torch.distributed as dist
+
+    from nanosaur2_web_b200.ops import check_device
+    from nanosaur2_web_b200.sharding import max_over_ranks
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    check_device()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    check_device()
+    return max_over_ranks(e0.elapsed_time(e1))
+
+
+def _kernel_stats(step, steps):
+    """Per-kernel totals of the library profiler (CUDA events around each launch) over ``steps`` steps."""
+    import torch
+
+    from nanosaur2_web_b200 import _lib
+    L_ = _lib.lib()
+    L_.nsa_profiler_reset()
+    L_.nsa_profiler_enable(1)
+    for i in range(steps):
+        step(i)
+    torch.cuda.synchronize()
+    L_.nsa_profiler_enable(0)
+    stats = (_lib.KernelStat * 8)()
+    n = L_.nsa_profiler_read(stats, 8)
+    out = {stats[i].name.decode(): (stats[i].launches, stats[i].total_ms, stats[i].flops, stats[i].bytes)
+           for i in range(n)}
+    L_.nsa_profiler_reset()
+    return out
+
+
+def _roofline(kstats, kernel):
+    launches, ms, flops, _ = kstats["attention"]
+    peak, src = measured_peak()
+    achieved = flops / (ms * 1e-3) / 1e12
+    pro = kstats.get("prologue")
+    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "traffic": None, "peak_source": src, "kernel": kernel, "kernel_ms": ms / max(launches, 1),
+            "prologue_gbs": (pro[3] / (pro[1] * 1e-3) / 1e9) if pro and pro[1] > 0 else None}
+
+
+def _line(args, world, value, ms, config, roofline, clocks, launches, scaling, **extra):
+    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": scaling,
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config, "roofline": roofline,
+            "clocks": clocks, "gpu_launches": launches}
+    line.update(extra)
+    return line
+
+
+def run_config3(args, rank, world, local_rank):
+    """Config 3: one 18-block DiT pass over batch 8 (eight seeds), joint attention with 256 text slots
+    on even blocks and image-only attention on odd blocks; (batch x head) units split over the ranks
+    (strong scaling, no data-path collective).  A step is the whole 18-block pass."""
+    import torch
+
+    from nanosaur2_web_b200.blocks import dit_block_attention, fused_workspace_bytes
+    from nanosaur2_web_b200.ops import rope2dTable
+    from nanosaur2_web_b200.sharding import shard_batch_heads, sum_over_ranks
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, L, BLOCKS = 8, IMG_H * IMG_W, 18
+    shards = shard_batch_heads(B, H, world, rank)
+    bufs = []
+    for i in range(2):   # two 310 MB input sets (> L2) alternate between blocks
+        qkv, q_w, k_w, lv, bias = make_inputs(3000 + i, B)
+        bufs.append((torch.from_numpy(qkv).to(dev, torch.bfloat16), torch.from_numpy((L + lv).astype(np.int32)).to(dev),
+                     torch.from_numpy(bias).to(dev), lv))
+    qn, kn = torch.from_numpy(q_w).to(dev), torch.from_numpy(k_w).to(dev)
+    cs = rope2dTable(IMG_H, IMG_W, D, dev)
+    out = torch.empty((B, L, C), dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(max(fused_workspace_bytes(B=B, Lq=L, Lk=L + LT, Hq=H, Hkv=H, D=D, shard=s) for s in shards),
+                     dtype=torch.uint8, device=dev)
+
+    def step(i):
+        for blk in range(BLOCKS):
+            x, kv_len, bias_t, _ = bufs[(i * BLOCKS + blk) % 2]
+            joint = blk % 2 == 0
+            for s in shards:
+                dit_block_attention(x, L=L, text_rows=LT if joint else 0, q_norm=qn, k_norm=kn, cs=cs,
+                                    kv_len=kv_len if joint else None, bias=bias_t if joint else None, out=out,
+                                    shard=s, workspace=ws)
+
+    def step_flops(i):
+        f = 0.0
+        for blk in range(BLOCKS):
+            lv = bufs[(i * BLOCKS + blk) % 2][3]
+            for b0, bc, h0, hc in shards:
+                for b in range(b0, b0 + bc):
+                    f += 4.0 * hc * L * (L + (int(lv[b]) if blk % 2 == 0 else 0)) * D
+        return f
+
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(local_rank) as clocks:
+        ms = _timed(step, args.steps, args.warmup, world, stream)
+    flops = sum_over_ranks(sum(step_flops(i) for i in range(args.steps)))
+    kst = _kernel_stats(step, min(args.steps, 3))
+    if rank != 0:
+        return
+    cfg = {"workload": "config 3: 18-block DiT pass, batch 8 (eight seeds), 52x76=3952 image tokens, 16 heads x 96, "
+                       "joint (+256 text slots, valid ~U[32,256], log-weight bias) on even blocks, image-only on odd",
+           "global_batch": B, "seq_len": L, "blocks": BLOCKS, "parallelism": f"(batch x head)-sharded x{world}",
+           "l2": "two 310 MB input sets alternate between blocks (> 126 MB L2)"}
+    print(json.dumps(_line(args, world, flops / (ms * 1e-3) / 1e12, ms, cfg, _roofline(kst, "attn_fwd_kernel<96>"),
+                           clocks.summary(), 2 * BLOCKS * len(shards) * args.steps, "strong")), flush=True)
+
+
+def run_config4(args, rank, world, local_rank):
+    """Config 4: the Gemma3-270M text encoder's 18 attention layers (GQA 4/1, head dim 256, causal;
+    15 local layers with a 512-key window and RoPE theta 1e4, 3 global with theta 1e6) over batch 16
+    x 1024 tokens, batch-sharded over the ranks (strong scaling).  A step is one 18-layer pass."""
+    import torch
+
+    from nanosaur2_web_b200.blocks import (GEMMA_HEAD_DIM, GEMMA_HEADS, fused_workspace_bytes, gemma_layer_attention,
+                                           gemma_rope_theta)
+    from nanosaur2_web_b200.ops import ropeTable
+    from nanosaur2_web_b200.sharding import split_range, sum_over_ranks
+    from tests._helpers import gemma_inputs
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, L, LAYERS, WINDOW = 16, 1024, 18, 512
+    b0, b1 = split_range(B, world, rank)
+    bufs = []
+    for i in range(3):   # three 50 MB layer inputs rotate (150 MB > L2)
+        qkv, q_w, k_w = gemma_inputs(4000 + i, B, L)
+        bufs.append(torch.from_numpy(qkv).to(dev, torch.bfloat16))
+    qn, kn = torch.from_numpy(q_w).to(dev), torch.from_numpy(k_w).to(dev)
+    tables = {th: ropeTable(L, GEMMA_HEAD_DIM, th, dev) for th in (1e4, 1e6)}
+    out = torch.empty((B, L, GEMMA_HEADS * GEMMA_HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    shard = (b0, b1 - b0, 0, 0)
+    ws = torch.empty(fused_workspace_bytes(B=B, Lq=L, Lk=L, Hq=GEMMA_HEADS, Hkv=1, D=GEMMA_HEAD_DIM, causal=1,
+                                           shard=shard), dtype=torch.uint8, device=dev)
+
+    def step(i):
+        for layer in range(LAYERS):
+            th = gemma_rope_theta(layer)
+            gemma_layer_attention(bufs[(i * LAYERS + layer) % 3], q_norm=qn, k_norm=kn, cs=tables[th],
+                                  window=0 if th == 1e6 else WINDOW, out=out, shard=shard, workspace=ws)
+
+    per_elem = sum(4.0 * GEMMA_HEADS * gemma_pairs(L, 0 if gemma_rope_theta(i) == 1e6 else WINDOW) * GEMMA_HEAD_DIM
+                   for i in range(LAYERS))
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(local_rank) as clocks:
+        ms = _timed(step, args.steps, args.warmup, world, stream)
+    flops = sum_over_ranks(per_elem * (b1 - b0) * args.steps)
+    kst = _kernel_stats(step, min(args.steps, 3))
+    if rank != 0:
+        return
+    cfg = {"workload": "config 4: Gemma3-270M text encoder attention, 18 layers (15 local window 512 theta 1e4, "
+                       "3 global theta 1e6), GQA 4/1, head dim 256, causal, q/k RMSNorm + 1D RoPE",
+           "global_batch": B, "seq_len": L, "layers": LAYERS, "parallelism": f"batch-sharded x{world}",
+           "l2": "three 50 MB layer inputs rotate (150 MB > 126 MB L2)",
+           "flops_note": "valid (unmasked) pairs only: 4*Hq*pairs*256 per element-layer"}
+    print(json.dumps(_line(args, world, flops / (ms * 1e-3) / 1e12, ms, cfg, _roofline(kst, "attn_fwd_kernel<256>"),
+                           clocks.summary(), 2 * LAYERS * args.steps, "strong")), flush=True)
+
+
+def run_config5(args, rank, world, local_rank):
+    """Config 5: 2048x2048 -> 128x128 = 16384 image tokens + 256 text slots, batch 4, sequence-sharded
+    queries with one in-place NCCL all-gather of the k'|v' image rows per batch element, overlapped
+    with the previous element's attention (strong scaling).  A step is one call over the 4 elements;
+    the all-gather's exposed time is the step time minus the kernels' own event-timed time."""
+    import torch
+
+    from nanosaur2_web_b200.ops import rope2dTable
+    from nanosaur2_web_b200.seqshard import SeqShardedJointAttention
+    from nanosaur2_web_b200.sharding import max_over_ranks, sum_over_ranks
+    from tests._helpers import bf16_round
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, HW, LT5 = 4, 128, 256
+    L = HW * HW
+    m = SeqShardedJointAttention(B=B, L=L, text_rows=LT5, world=world, rank=rank, device=dev)
+    g = np.random.default_rng(5000)   # shared by every rank: weights, text lengths, prompt weights
+    q_w = (1.0 + 0.2 * g.standard_normal(D)).astype(np.float32)
+    k_w = (1.0 + 0.2 * g.standard_normal(D)).astype(np.float32)
+    lv = g.integers(32, LT5 + 1, size=B).astype(np.int32)
+    bias = np.log(g.choice(np.array([0.7, 1.0, 1.3], np.float32), size=(B, LT5))).astype(np.float32)
+    bufs = []
+    for i in range(2):   # this rank's rows (own image rows, then the text rows), two sets > L2
+        r = np.random.default_rng(5100 + 16 * i + rank)
+        x = r.standard_normal((B, m.q_count + LT5, 3 * C), dtype=np.float32)
+        x[:, m.q_count:, :C] = 0.0
+        bufs.append(torch.from_numpy(bf16_round(x)).to(dev, torch.bfloat16))
+    qn, kn = torch.from_numpy(q_w).to(dev), torch.from_numpy(k_w).to(dev)
+    kv_len = torch.from_numpy((L + lv).astype(np.int32)).to(dev)
+    bias_t = torch.from_numpy(bias).to(dev)
+    cs = rope2dTable(HW, HW, D, dev)
+    out = torch.empty((B, m.q_count, C), dtype=torch.bfloat16, device=dev)
+
+    def step(i):
+        m(bufs[i % 2], q_norm=qn, k_norm=kn, cs=cs, kv_len=kv_len, bias=bias_t, out=out)
+
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(local_rank) as clocks:
+        ms = _timed(step, args.steps, args.warmup, world, stream)
+    gather_ms = max_over_ranks(m.timing().gather_ms)
+    kst = _kernel_stats(step, min(args.steps, 3))
+    nprof = min(args.steps, 3)
+    kernel_ms = sum(v[1] for v in kst.values()) / nprof
+    exposed = max_over_ranks(ms / args.steps - kernel_ms)
+    flops = sum_over_ranks(sum(4.0 * H * m.q_count * (L + int(lv[b])) * D for b in range(B)) * args.steps)
+    recv = B * (L - m.q_count) * m.kv_ld * 2
+    if rank != 0:
+        return
+    cfg = {"workload": "config 5: DiT joint attention at 128x128=16384 image tokens + 256 text slots (valid "
+                       "~U[32,256], log-weight bias), 16 heads x 96, batch 4, fused q/k RMSNorm + 2D RoPE",
+           "global_batch": B, "seq_len": L + LT5, "parallelism": f"sequence-sharded x{world} "
+                                                                 f"({m.q_count} query rows per rank)",
+           "collective": "in-place NCCL all_gather_into_tensor of the k'|v' image rows per batch element "
+                         "(torch.distributed), overlapped with the previous element's attention",
+           "l2": "two input sets of this rank's rows alternate; kv_packed is rewritten every step"}
+    extra = {"allgather": {"bytes_received_per_rank_per_step": recv, "gather_ms_per_step": gather_ms,
+                           "kernel_ms_per_step": kernel_ms, "exposed_ms_per_step": exposed,
+                           "gather_gbs": recv / (gather_ms * 1e-3) / 1e9 if gather_ms > 0 else None}}
+    print(json.dumps(_line(args, world, flops / (ms * 1e-3) / 1e12, ms, cfg, _roofline(kst, "attn_fwd_kernel<96>"),
+                           clocks.summary(), 3 * B * args.steps, "strong", **extra)), flush=True)
+
+
 def run_profile(args, local_rank):
     """Small driver for ncu captures: the same fused call as the benchmark on ``--batch`` elements of
     config 2, ``--warmup`` + ``--steps`` launches of each kernel, nothing else on the GPU."""
@@ -408,6 +645,8 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="profiling driver: warm-up + timed device-resident steps only (no e2e, CPU or clocks)")
     ap.add_argument("--batch", type=int, default=B_PER_GPU, help="batch per GPU (profiling runs only)")
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2,
+                    help="BASELINE config to run (2 = the headline line; 3, 4, 5 print their own line)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -430,7 +669,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5}[args.config](args, rank, world, local_rank)
     finally:
         if world > 1:
             dist.destroy_process_group()

@@ -152,6 +152,46 @@ nsa_status nsa_fused_attention_noalloc(const nsa_fused_desc* desc, const void* q
                                        const float* bias, void* out, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * Sequence-sharded DiT joint attention (the 16384-token high-resolution case).  No counterpart in
+ * the reference, which runs on one device: this is the nsa_fused_attention call of the DiT block
+ * (app/models/nanosaur2.js:196-208) split by query rows over the GPUs of one box.  Rank r owns
+ * image rows [q_begin, q_begin + q_count); every rank holds all text rows.
+ *   1. nsa_seq_shard_prologue normalises and rotates the rank's query rows into q_prime, and
+ *      writes the k'|v' rows of its image rows and of all text rows into kv_packed, each at its
+ *      global key row.
+ *   2. The caller gathers rows [0, Lq) of kv_packed across ranks: per batch element they are one
+ *      contiguous block with q_count rows per rank (one in-place ncclAllGather per element).
+ *   3. nsa_seq_shard_attention runs the rank's queries over all keys of kv_packed.
+ * Layouts: kv_packed [b_count][kv_rows][2*Hkv*D] bf16, k' heads at columns [0, Hkv*D) and v' heads
+ * at [Hkv*D, 2*Hkv*D); q_prime [b_count][Hq][q_pad][D] bf16 (q_pad = q_count rounded up to the
+ * query tile).  Both hold the elements [b_begin, b_begin + b_count) of the descriptor, so a caller
+ * that overlaps the gather of element b with the attention of element b-1 calls each step with
+ * b_count = 1 and pointers advanced by one element.
+ * The descriptor is that of nsa_fused_attention (Lq = image rows, Lk = image + text rows,
+ * kv_len[b] = valid keys of element b), with whole heads (h_begin 0, h_count 0 or Hq) and no causal
+ * mask or window.  out receives the rank's rows: out[b*o_bstride + i*ldo + oOff + h*D + d] for
+ * local row i = global row q_begin + i.
+ * ------------------------------------------------------------------------------------------------ */
+typedef struct nsa_seq_shard {
+  int32_t q_begin;         /* first image row (query and key) this rank owns */
+  int32_t q_count;         /* number of image rows this rank owns */
+  int32_t qkv_image_row0;  /* row of qkv holding image row q_begin (q_begin for a full-length qkv,
+                              0 for a local [own image rows | text rows] buffer) */
+  int32_t qkv_text_row0;   /* row of qkv holding key row Lq, the first text row (Lq, or q_count) */
+} nsa_seq_shard;
+
+/* Byte sizes of q_prime and kv_packed for the descriptor's b_count elements, and the rows of one
+ * element of kv_packed (its stride is kv_rows * 2*Hkv*D elements). */
+nsa_status nsa_seq_shard_buffer_sizes(const nsa_fused_desc* desc, const nsa_seq_shard* shard,
+                                      size_t* q_prime_bytes, size_t* kv_packed_bytes, int32_t* kv_rows);
+nsa_status nsa_seq_shard_prologue(const nsa_fused_desc* desc, const nsa_seq_shard* shard, const void* qkv,
+                                  const float* q_norm_w, const float* k_norm_w, const float* cs,
+                                  const int32_t* kv_len, void* q_prime, void* kv_packed, void* stream);
+nsa_status nsa_seq_shard_attention(const nsa_fused_desc* desc, const nsa_seq_shard* shard,
+                                   const void* q_prime, const void* kv_packed, const int32_t* kv_len,
+                                   const float* bias, void* out, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
  * RoPE tables in the reference layout: cos block [L][D/2] then sin block [L][D/2] (sinOff = L*D/2).
  *   nsa_rope2d_table: app/models/common.js:28-43 (tools/reference.py:220-227): L = h*w tokens,
  *     the first D/4 pairs rotate by the centred column, the next D/4 by the centred row, theta 1e4.

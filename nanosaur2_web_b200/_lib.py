@@ -48,6 +48,11 @@ class FusedDesc(ctypes.Structure):
     ]
 
 
+class SeqShard(ctypes.Structure):
+    """nsa_seq_shard (include/nsattn.h)."""
+    _fields_ = [("q_begin", _i32), ("q_count", _i32), ("qkv_image_row0", _i32), ("qkv_text_row0", _i32)]
+
+
 class KernelStat(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 32), ("launches", _i64), ("total_ms", ctypes.c_double),
                 ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
@@ -64,6 +69,12 @@ SIGNATURES = {
     "nsa_fused_attention_workspace_size": (_sz, [ctypes.POINTER(FusedDesc)]),
     "nsa_fused_attention": (_i32, [ctypes.POINTER(FusedDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "nsa_fused_attention_noalloc": (_i32, [ctypes.POINTER(FusedDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "nsa_seq_shard_buffer_sizes": (_i32, [ctypes.POINTER(FusedDesc), ctypes.POINTER(SeqShard), ctypes.POINTER(_sz),
+                                          ctypes.POINTER(_sz), ctypes.POINTER(_i32)]),
+    "nsa_seq_shard_prologue": (_i32, [ctypes.POINTER(FusedDesc), ctypes.POINTER(SeqShard), _vp, _vp, _vp, _vp, _vp,
+                                      _vp, _vp, _vp]),
+    "nsa_seq_shard_attention": (_i32, [ctypes.POINTER(FusedDesc), ctypes.POINTER(SeqShard), _vp, _vp, _vp, _vp, _vp,
+                                       _vp]),
     "nsa_rope2d_table": (_i32, [_i32, _i32, _i32, _vp, _vp]),
     "nsa_rope1d_table": (_i32, [_i32, _i32, _f32, _vp, _vp]),
     "nsa_check_device": (_i32, [_vp]),

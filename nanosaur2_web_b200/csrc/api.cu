@@ -203,6 +203,49 @@ nsa_status check_out(const void* out, int out_dtype, int64_t ldo, int64_t oOff, 
   return NSA_OK;
 }
 
+// Attention parameters shared by every entry point; the caller sets the Q / K / V tile coordinates.
+nsa::AttnParams attn_params(const Plan& pl, const CommonArgs& a, const float* bias, int bias_start, int bias_len,
+                            int64_t bias_bstride, const int32_t* kv_len, float scale, void* out, int64_t ldo,
+                            int64_t o_bstride, int64_t oOff, int* err) {
+  nsa::AttnParams ap{};
+  ap.B = pl.Bs;
+  ap.Hq = pl.Hqs;
+  ap.Hkv = pl.Hkvs;
+  ap.group = pl.group;
+  ap.b_begin = pl.b0;
+  ap.hq_begin = pl.hq0;
+  ap.hkv_begin = pl.hkv0;
+  ap.Lq = pl.Lq;
+  ap.Lq_pad = pl.Lq_pad;
+  ap.Lk = pl.Lk;
+  ap.Lk_pad = pl.Lk_pad;
+  ap.kv_len = kv_len;
+  ap.bias = bias_len > 0 ? bias : nullptr;
+  ap.bias_start = bias_start;
+  ap.bias_len = bias_len;
+  ap.bias_bstride = bias_bstride;
+  const float s = scale > 0.f ? scale : 1.0f / std::sqrt((float)pl.D);
+  ap.scale_log2 = s * 1.4426950408889634f;
+  ap.causal = a.causal;
+  ap.window = a.window;
+  ap.out = out;
+  ap.out_f32 = a.out_dtype == NSA_F32;
+  ap.out_ld = ldo;
+  ap.out_bstride = o_bstride;
+  ap.out_off = oOff;
+  ap.q_blocks = pl.Lq_pad / (pl.NQ * nsa::kTileM);
+  ap.err = err;
+  ap.timeout_ns = wait_timeout_ns();
+  return ap;
+}
+
+// Algorithmic flops of one attention launch: 4 * B * H * valid pairs * D (app/gpu/ops.js:207).
+double attn_flops(const Plan& pl, const CommonArgs& a) {
+  double pairs = (double)pl.Lq * pl.Lk;
+  if (a.causal) pairs = (double)pl.Lq * (pl.Lq + 1) / 2.0;
+  return 4.0 * pl.Bs * pl.Hqs * pairs * pl.D;
+}
+
 // Prologue + attention launches shared by nsa_attention and nsa_fused_attention.
 nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, const float* bias, int bias_start,
                int bias_len, int64_t bias_bstride, const int32_t* kv_len, float scale, void* out, int64_t ldo,
@@ -229,11 +272,12 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
   pp.hq_begin = pl.hq0;
   pp.hkv_begin = pl.hkv0;
   pp.kv_len = kv_len;
-  pp.Qs = Qs;
-  pp.Ks = Ks;
-  pp.Vs = Vs;
-  pp.Lq_pad = pl.Lq_pad;
-  pp.Lk_pad = pl.Lk_pad;
+  pp.out[0] = {Qs, (int64_t)pl.Hqs * pl.Lq_pad * pl.D, (int64_t)pl.Lq_pad * pl.D, pl.D};
+  pp.out[1] = {Ks, (int64_t)pl.Hkvs * pl.Lk_pad * pl.D, (int64_t)pl.Lk_pad * pl.D, pl.D};
+  pp.out[2] = {Vs, (int64_t)pl.Hkvs * pl.Lk_pad * pl.D, (int64_t)pl.Lk_pad * pl.D, pl.D};
+  pp.rows[0] = pl.Lq_pad;
+  pp.rows[1] = pp.rows[2] = pl.Lk_pad;
+  for (int i = 0; i < 3; ++i) pp.row0[i] = pp.src_row0[i] = 0;
   // Kernels that keep Q in tensor memory TMA-load the raw bf16 query rows straight from the input
   // when the layout allows a tiled map over it (16-byte aligned rows and head offsets, whole rows
   // per batch element); they then apply the q norm and RoPE themselves.  Otherwise (fp32 input, odd
@@ -269,35 +313,11 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
       !encode_tiles(&tv, Vs, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk, pl.BN))
     return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed (driver entry point unavailable?)");
 
-  nsa::AttnParams ap{};
-  ap.B = pl.Bs;
-  ap.Hq = pl.Hqs;
-  ap.Hkv = pl.Hkvs;
-  ap.group = pl.group;
-  ap.b_begin = pl.b0;
-  ap.hq_begin = pl.hq0;
-  ap.hkv_begin = pl.hkv0;
-  ap.Lq = pl.Lq;
-  ap.Lq_pad = pl.Lq_pad;
-  ap.Lk = pl.Lk;
-  ap.Lk_pad = pl.Lk_pad;
-  ap.kv_len = kv_len;
-  ap.bias = bias_len > 0 ? bias : nullptr;
-  ap.bias_start = bias_start;
-  ap.bias_len = bias_len;
-  ap.bias_bstride = bias_bstride;
-  const float s = scale > 0.f ? scale : 1.0f / std::sqrt((float)pl.D);
-  ap.scale_log2 = s * 1.4426950408889634f;
-  ap.causal = a.causal;
-  ap.window = a.window;
-  ap.out = out;
-  ap.out_f32 = a.out_dtype == NSA_F32;
-  ap.out_ld = ldo;
-  ap.out_bstride = o_bstride;
-  ap.out_off = oOff;
-  ap.q_blocks = pl.Lq_pad / (pl.NQ * nsa::kTileM);
-  ap.err = err;
-  ap.timeout_ns = wait_timeout_ns();
+  nsa::AttnParams ap = attn_params(pl, a, bias, bias_start, bias_len, bias_bstride, kv_len, scale, out, ldo,
+                                   o_bstride, oOff, err);
+  ap.k_x0 = ap.v_x0 = ap.kv_xh = 0;
+  ap.kv_yb = pl.Hkvs * pl.Lk_pad;
+  ap.kv_yh = pl.Lk_pad;
   if (q_direct) {
     ap.q_x0 = (int)pp.q.off;
     ap.q_xh = pl.D;
@@ -324,9 +344,7 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
     ap.q_sin_off = 0;
     ap.q_rope_rows = 0;
   }
-  double pairs = (double)pl.Lq * pl.Lk;
-  if (a.causal) pairs = (double)pl.Lq * (pl.Lq + 1) / 2.0;
-  const double flops = 4.0 * pl.Bs * pl.Hqs * pairs * pl.D;
+  const double flops = attn_flops(pl, a);
   e = profiled("attention", flops, 0.0, stream, [&] { return nsa::launch_attention(ap, pl.D, tq, tk, tv, stream); });
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");
   return NSA_OK;
@@ -356,6 +374,52 @@ CommonArgs common_from(const nsa_fused_desc* d) {
   return CommonArgs{d->B, d->Lq, d->Lk, d->Hq, group, d->D, d->causal, d->window, d->in_dtype, d->out_dtype,
                     d->b_begin, d->b_count, d->h_begin, d->h_count};
 }
+
+// ------------------------------------------------------------------------------------ sequence shards
+
+// One rank's part of a sequence-sharded fused call: the plan of its q_count query rows over all Lk
+// keys, and the layout of its q_prime / kv_packed buffers.
+struct SeqPlan {
+  Plan pl;             // Lq = q_count, Lq_pad = q_pad; Lk / Lk_pad of the whole key sequence
+  CommonArgs a;        // the descriptor with Lq = q_count
+  int L;               // image rows (the descriptor's Lq)
+  int q_begin, q_count, img_row0, text_row0;
+  int64_t kv_ld;       // elements per kv_packed row: 2 * Hkv * D
+  size_t q_bytes, kv_bytes;
+};
+
+nsa_status make_seq_plan(const nsa_fused_desc* d, const nsa_seq_shard* s, SeqPlan* sp) {
+  if (!d || !s) return fail(NSA_ERR_INVALID_ARGUMENT, "desc and shard must not be NULL");
+  if (d->Hkv < 1 || d->Hq % d->Hkv) return fail(NSA_ERR_INVALID_ARGUMENT, "Hkv must divide Hq");
+  if (d->Lk < d->Lq) return fail(NSA_ERR_INVALID_ARGUMENT, "Lk must be >= Lq (query rows are also key rows)");
+  if (d->causal || d->window)
+    return fail(NSA_ERR_UNSUPPORTED, "sequence sharding supports neither a causal mask nor a window");
+  if (d->h_begin != 0 || (d->h_count != 0 && d->h_count != d->Hq))
+    return fail(NSA_ERR_UNSUPPORTED, "sequence sharding takes whole heads (h_begin 0, h_count 0 or Hq)");
+  if (s->q_begin < 0 || s->q_count < 1 || (int64_t)s->q_begin + s->q_count > d->Lq)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "shard rows [q_begin, q_begin + q_count) must lie in [0, Lq)");
+  if (s->qkv_image_row0 < 0 || s->qkv_text_row0 < 0)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "qkv_image_row0 and qkv_text_row0 must be >= 0");
+  SeqPlan p{};
+  p.a = common_from(d);
+  p.a.Lq = s->q_count;
+  nsa_status st = make_plan(p.a, &p.pl);
+  if (st != NSA_OK) return st;
+  p.L = d->Lq;
+  p.q_begin = s->q_begin;
+  p.q_count = s->q_count;
+  p.img_row0 = s->qkv_image_row0;
+  p.text_row0 = s->qkv_text_row0;
+  p.kv_ld = 2LL * d->Hkv * d->D;
+  if ((int64_t)p.pl.Bs * p.pl.Lk_pad >= (int64_t)1 << 31)
+    return fail(NSA_ERR_UNSUPPORTED, "problem too large for one launch");
+  p.q_bytes = (size_t)p.pl.Bs * p.pl.Hqs * p.pl.Lq_pad * p.pl.D * 2;
+  p.kv_bytes = (size_t)p.pl.Bs * p.pl.Lk_pad * p.kv_ld * 2;
+  *sp = p;
+  return NSA_OK;
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
 
 }  // namespace
 
@@ -560,6 +624,124 @@ int32_t nsa_profiler_read(nsa_kernel_stat* out, int32_t max_entries) {
   const int32_t n = (int32_t)stats.size();
   for (int32_t i = 0; out && i < n && i < max_entries; ++i) out[i] = stats[i];
   return n;
+}
+
+nsa_status nsa_seq_shard_buffer_sizes(const nsa_fused_desc* desc, const nsa_seq_shard* shard, size_t* q_prime_bytes,
+                                      size_t* kv_packed_bytes, int32_t* kv_rows) {
+  SeqPlan sp;
+  nsa_status st = make_seq_plan(desc, shard, &sp);
+  if (st != NSA_OK) return st;
+  if (q_prime_bytes) *q_prime_bytes = sp.q_bytes;
+  if (kv_packed_bytes) *kv_packed_bytes = sp.kv_bytes;
+  if (kv_rows) *kv_rows = sp.pl.Lk_pad;
+  return NSA_OK;
+}
+
+nsa_status nsa_seq_shard_prologue(const nsa_fused_desc* d, const nsa_seq_shard* s, const void* qkv,
+                                  const float* q_norm_w, const float* k_norm_w, const float* cs, const int32_t* kv_len,
+                                  void* q_prime, void* kv_packed, void* stream) {
+  SeqPlan sp;
+  nsa_status st = make_seq_plan(d, s, &sp);
+  if (st != NSA_OK) return st;
+  if (!qkv) return fail(NSA_ERR_INVALID_ARGUMENT, "qkv is NULL");
+  if (!q_norm_w || !k_norm_w) return fail(NSA_ERR_INVALID_ARGUMENT, "q/k norm weights are required");
+  if (!q_prime || !kv_packed || !aligned16(q_prime) || !aligned16(kv_packed))
+    return fail(NSA_ERR_INVALID_ARGUMENT, "q_prime and kv_packed must be 16-byte aligned device pointers");
+  if (cs && d->D % 2) return fail(NSA_ERR_INVALID_ARGUMENT, "RoPE needs an even head dim");
+  const Plan& pl = sp.pl;
+  nsa::PrologueParams pp{};
+  pp.q = {qkv, d->ld, d->bstride, d->qOff, d->Lk};
+  pp.k = {qkv, d->ld, d->bstride, d->kOff, d->Lk};
+  pp.v = {qkv, d->ld, d->bstride, d->vOff, d->Lk};
+  pp.q_w = q_norm_w;
+  pp.k_w = k_norm_w;
+  pp.cs = cs;
+  pp.sin_off = d->sinOff;
+  pp.rope_rows = cs ? sp.L : 0;
+  pp.eps = d->eps;
+  pp.src_f32 = d->in_dtype == NSA_F32;
+  pp.B = pl.Bs;
+  pp.b_begin = pl.b0;
+  pp.Lq = sp.q_begin + sp.q_count;   // query rows past the shard are zero padding
+  pp.Lk = pl.Lk;
+  pp.Hq = pl.Hqs;
+  pp.Hkv = pl.Hkvs;
+  pp.D = pl.D;
+  pp.hq_begin = 0;
+  pp.hkv_begin = 0;
+  pp.kv_len = kv_len;
+  auto* Q = static_cast<__nv_bfloat16*>(q_prime);
+  auto* KV = static_cast<__nv_bfloat16*>(kv_packed);
+  const int64_t kv_elem = (int64_t)pl.Lk_pad * sp.kv_ld;   // one batch element of kv_packed
+  const int64_t v_col = (int64_t)pl.Hkvs * pl.D;
+  // the shard's own image rows: q' tiles, and k'|v' at their global key rows
+  pp.out[0] = {Q, (int64_t)pl.Hqs * pl.Lq_pad * pl.D, (int64_t)pl.Lq_pad * pl.D, pl.D};
+  pp.out[1] = {KV + sp.q_begin * sp.kv_ld, kv_elem, pl.D, sp.kv_ld};
+  pp.out[2] = {KV + sp.q_begin * sp.kv_ld + v_col, kv_elem, pl.D, sp.kv_ld};
+  pp.rows[0] = pl.Lq_pad;
+  pp.rows[1] = pp.rows[2] = sp.q_count;
+  for (int i = 0; i < 3; ++i) {
+    pp.row0[i] = sp.q_begin;
+    pp.src_row0[i] = sp.img_row0;
+  }
+  pp.skip_q = 0;
+  const double in_elem = d->in_dtype == NSA_F32 ? 4.0 : 2.0;
+  const cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  double bytes = (double)pl.Bs * sp.q_count * (pl.Hqs + 2.0 * pl.Hkvs) * pl.D * (in_elem + 2.0);
+  cudaError_t e = profiled("prologue", 0.0, bytes, strm, [&] { return nsa::launch_prologue(pp, strm); });
+  if (e != cudaSuccess) return cuda_fail(e, "prologue launch");
+  // the text rows (and the zero padding up to kv_rows), which every rank computes for itself
+  if (pl.Lk_pad > sp.L) {
+    pp.skip_q = 1;
+    pp.out[1].ptr = KV + (int64_t)sp.L * sp.kv_ld;
+    pp.out[2].ptr = KV + (int64_t)sp.L * sp.kv_ld + v_col;
+    pp.rows[1] = pp.rows[2] = pl.Lk_pad - sp.L;
+    pp.row0[1] = pp.row0[2] = sp.L;
+    pp.src_row0[1] = pp.src_row0[2] = sp.text_row0;
+    bytes = (double)pl.Bs * (pl.Lk - sp.L) * 2.0 * pl.Hkvs * pl.D * (in_elem + 2.0);
+    e = profiled("prologue", 0.0, bytes, strm, [&] { return nsa::launch_prologue(pp, strm); });
+    if (e != cudaSuccess) return cuda_fail(e, "prologue launch");
+  }
+  return NSA_OK;
+}
+
+nsa_status nsa_seq_shard_attention(const nsa_fused_desc* d, const nsa_seq_shard* s, const void* q_prime,
+                                   const void* kv_packed, const int32_t* kv_len, const float* bias, void* out,
+                                   void* stream) {
+  SeqPlan sp;
+  nsa_status st = make_seq_plan(d, s, &sp);
+  if (st != NSA_OK) return st;
+  if (!q_prime || !kv_packed || !aligned16(q_prime) || !aligned16(kv_packed))
+    return fail(NSA_ERR_INVALID_ARGUMENT, "q_prime and kv_packed must be 16-byte aligned device pointers");
+  if ((st = check_out(out, d->out_dtype, d->ldo, d->oOff, d->o_bstride)) != NSA_OK) return st;
+  if (d->biasLen < 0) return fail(NSA_ERR_INVALID_ARGUMENT, "biasLen must be >= 0");
+  if (d->biasLen > 0 && !bias) return fail(NSA_ERR_INVALID_ARGUMENT, "biasLen > 0 needs a bias pointer");
+  int* err = nsa::device_error_word();
+  if (!err) return fail(NSA_ERR_CUDA, "cannot resolve the device error word on this device");
+  const Plan& pl = sp.pl;
+  CUtensorMap tq, tkv;
+  if (!encode_tiles(&tq, const_cast<void*>(q_prime), pl.D, (int64_t)pl.Bs * pl.Hqs * pl.Lq_pad, pl.blk, nsa::kTileM) ||
+      !encode_rows(&tkv, kv_packed, sp.kv_ld, sp.kv_ld, (int64_t)pl.Bs * pl.Lk_pad, pl.blk, pl.BN))
+    return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed (driver entry point unavailable?)");
+  nsa::AttnParams ap = attn_params(pl, sp.a, bias, d->biasStart, bias ? d->biasLen : 0, d->bias_bstride, kv_len,
+                                   d->scale, out, d->ldo, d->o_bstride, d->oOff, err);
+  // k' head h at columns [h*D, h*D + D) of the packed rows, v' head h at [(Hkv + h)*D, ...)
+  ap.k_x0 = 0;
+  ap.v_x0 = pl.Hkvs * pl.D;
+  ap.kv_xh = pl.D;
+  ap.kv_yb = pl.Lk_pad;
+  ap.kv_yh = 0;
+  ap.q_x0 = 0;
+  ap.q_xh = 0;
+  ap.q_yb = pl.Hqs * pl.Lq_pad;
+  ap.q_yh = pl.Lq_pad;
+  ap.q_b0 = pl.b0;
+  ap.q_h0 = 0;
+  const cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  cudaError_t e = profiled("attention", attn_flops(pl, sp.a), 0.0, strm,
+                           [&] { return nsa::launch_attention(ap, pl.D, tq, tkv, tkv, strm); });
+  if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+  return NSA_OK;
 }
 
 }  // extern "C"

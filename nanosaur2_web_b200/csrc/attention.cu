@@ -227,8 +227,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   uint64_t* v_full = k_empty + NS;
   uint64_t* v_empty = v_full + NS;
   uint64_t* s_full = v_empty + NS;   // [2]   S buffer ready
-  uint64_t* p_full = s_full + 2;     // [4]   P half ready: [tile * 2 + half]
-  uint64_t* o_full = p_full + 4;     // [2]   O complete (NQ = 1: once per P*V)
+  uint64_t* p_full = s_full + 2;     // [4]   P half ready: [buffer * 2 + half], buffer = tile (NQ = 2)
+                                     //       or S buffer j & 1 (NQ = 1)
+  uint64_t* o_full = p_full + 4;     // [2]   O complete (NQ = 1: [0] once per P*V, [1] after the last)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -251,7 +252,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   const int j0 = kv_begin / BN;
   const int n = kv_end > kv_begin ? ((kv_end - 1) / BN - j0 + 1) : 0;
   const int q_tma_row = (bl * p.Hq + hl) * p.Lq_pad + q_row0;
-  const int kv_tma_row = (bl * p.Hkv + hkvl) * p.Lk_pad;
+  const int kv_y0 = bl * p.kv_yb + hkvl * p.kv_yh;
+  const int k_x = p.k_x0 + hkvl * p.kv_xh, v_x = p.v_x0 + hkvl * p.kv_xh;
   const uint64_t to = p.timeout_ns;
 
   if (threadIdx.x == 0) {
@@ -315,8 +317,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
           return false;
         mbar_arrive_expect_tx(&k_full[s], C::KV_TILE_BYTES);
         for (int c = 0; c < C::NB; ++c)
-          tma_load_2d(sK + s * C::KV_TILE_BYTES + c * C::KBLK_BYTES, &tmK, &k_full[s], c * C::BLK,
-                      kv_tma_row + (j0 + j) * BN);
+          tma_load_2d(sK + s * C::KV_TILE_BYTES + c * C::KBLK_BYTES, &tmK, &k_full[s], k_x + c * C::BLK,
+                      kv_y0 + (j0 + j) * BN);
         return true;
       };
       auto load_v = [&](int j) -> bool {
@@ -325,8 +327,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
           return false;
         mbar_arrive_expect_tx(&v_full[s], C::KV_TILE_BYTES);
         for (int c = 0; c < C::NB; ++c)
-          tma_load_2d(sV + s * C::KV_TILE_BYTES + c * C::KBLK_BYTES, &tmV, &v_full[s], c * C::BLK,
-                      kv_tma_row + (j0 + j) * BN);
+          tma_load_2d(sV + s * C::KV_TILE_BYTES + c * C::KBLK_BYTES, &tmV, &v_full[s], v_x + c * C::BLK,
+                      kv_y0 + (j0 + j) * BN);
         return true;
       };
       int k_issued = 0, v_issued = 0;
@@ -422,7 +424,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
           const int svs = j % NS;
           ok = wait_bounded(&v_full[svs], (j / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to);
           for (int h = 0; ok && h < 2; ++h) {
-            ok = wait_bounded(&p_full[h], j & 1, abort_flag, p.err, kErrTimeoutMma, to);
+            // one barrier pair per S buffer: the softmax may hand over P(j + 1) before this wait
+            // for P(j) runs, but never P(j + 2), whose S is issued only after this P*V
+            ok = wait_bounded(&p_full[(j & 1) * 2 + h], (j >> 1) & 1, abort_flag, p.err, kErrTimeoutMma, to);
             if (!ok) break;
             tc_fence_after();
             issue_pv_half<D>(tmem + C::o_col(0), tmem + C::s_col(j & 1), sv + svs * C::KV_TILE_BYTES, j > 0, h);
@@ -440,6 +444,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             tc_commit(&k_empty[sks]);
           }
         }
+        if (ok) tc_commit(&o_full[1]);   // every P*V done: the epilogue's barrier
       }
       if (!ok) {
         // let every MMA already issued finish before the CTA tears down its tensor memory
@@ -622,7 +627,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         }
         tmem_st32(s_addr, pk);
         tc_fence_before();
-        mbar_arrive(&p_full[(NQ == 2 ? tile : 0) * 2]);
+        mbar_arrive(&p_full[sbuf * 2]);
       }
       {
         // keys 64..BN-1 -> P columns 32..BN/2-1
@@ -637,7 +642,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         }
         tmem_st_n<C::P1_COLS>(s_addr + 32u, pk);
         tc_fence_before();
-        mbar_arrive(&p_full[(NQ == 2 ? tile : 0) * 2 + 1]);
+        mbar_arrive(&p_full[sbuf * 2 + 1]);
       }
       {
         float s0, s1;
@@ -649,10 +654,10 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
       if constexpr (NQ == 2) {
         ok = wait_bounded(&o_full[tile], 0, abort_flag, p.err, kErrTimeoutSoftmax, to);
       } else {
-        // O's barrier completes once per P*V; step through the last two completions so the
-        // parity test never skips a phase
-        if (n >= 2) ok = wait_bounded(&o_full[0], (uint32_t)((n - 2) & 1), abort_flag, p.err, kErrTimeoutSoftmax, to);
-        if (ok) ok = wait_bounded(&o_full[0], (uint32_t)((n - 1) & 1), abort_flag, p.err, kErrTimeoutSoftmax, to);
+        // o_full[0] completes once per P*V and may be up to two phases ahead of this thread here,
+        // which a parity wait cannot tell apart; the issuer commits o_full[1] once, after the last
+        // P*V, for this wait.
+        ok = wait_bounded(&o_full[1], 0, abort_flag, p.err, kErrTimeoutSoftmax, to);
       }
       ok = __all_sync(0xffffffffu, ok);
       if (ok) tc_fence_after();

@@ -23,8 +23,17 @@ struct RowView {
   int64_t rows;
 };
 
-// Prologue: raw rows -> head-major bf16 tiles [b][head][row][D] (rows padded with zeros), with the
-// optional per-head RMSNorm and split-half RoPE of the query/key rows.
+// Destination of prepared bf16 rows: element (local batch bl, local head h, produced row r, d) at
+// ptr[bl*bs + h*hs + r*rs + d].  Head-major tiles: hs = pad*D, rs = D; packed K|V rows: hs = D.
+struct TileOut {
+  __nv_bfloat16* ptr;
+  int64_t bs, hs, rs;
+};
+
+// Prologue: raw rows -> bf16 tiles (rows padded with zeros), with the optional per-head RMSNorm and
+// split-half RoPE of the query/key rows.  Part 0 = q, 1 = k, 2 = v.  Produced row r of part i is
+// logical row row0[i] + r (its key / query index and RoPE table row), read from source row
+// src_row0[i] + r.
 struct PrologueParams {
   RowView q, k, v;
   int src_f32;          // 1: fp32 input, 0: bf16 input
@@ -40,11 +49,11 @@ struct PrologueParams {
   int rope_rows;        // rows [0, rope_rows) of q and k get RoPE
   float eps;
   const int* kv_len;    // [B_total] valid keys per batch element (null: Lk)
-  __nv_bfloat16* Qs;
-  __nv_bfloat16* Ks;
-  __nv_bfloat16* Vs;
-  int Lq_pad, Lk_pad;
-  int skip_q;           // 1: the attention kernel reads and prepares Q itself (no Q tiles written)
+  TileOut out[3];
+  int rows[3];          // rows produced per part (padded counts)
+  int row0[3];          // logical row (query / key index, RoPE row) of produced row 0, per part
+  int src_row0[3];      // row of the source buffer holding produced row 0, per part
+  int skip_q;           // 1: no Q tiles (the attention kernel prepares Q itself)
 };
 
 struct AttnParams {
@@ -52,6 +61,9 @@ struct AttnParams {
   int b_begin, hq_begin;   // shard origin (output and per-batch inputs are indexed globally)
   int hkv_begin;           // first kv head held in the K/V tiles
   int Lq, Lq_pad, Lk, Lk_pad;
+  // K / V tile (x, y) of local kv head h and key k: x = k_x0 (v_x0) + h*kv_xh + c*blk,
+  // y = bl*kv_yb + h*kv_yh + k  (head-major tiles: x0 = xh = 0, yb = Hkv*Lk_pad, yh = Lk_pad)
+  int k_x0, v_x0, kv_xh, kv_yb, kv_yh;
   const int* kv_len;       // [B_total] or null
   const float* bias;       // natural-log additive key bias for keys >= bias_start, or null
   int bias_start, bias_len;

@@ -29,12 +29,13 @@ __global__ void __launch_bounds__(kPrologueThreads) prologue_kernel(const Prolog
   __shared__ float buf[kRowBufFloats];
   __shared__ __align__(16) __nv_bfloat16 obuf[kRowBufFloats];
 
-  const int row = blockIdx.x;
+  const int r_out = blockIdx.x;       // produced row
   const int bl = blockIdx.y;          // batch index within the shard
   const int b = p.b_begin + bl;       // global batch index
   const int part = blockIdx.z + (p.skip_q ? 1 : 0);
-  const int pad = part == 0 ? p.Lq_pad : p.Lk_pad;
-  if (row >= pad) return;
+  const int pad = p.rows[part];
+  if (r_out >= pad) return;
+  const int row = p.row0[part] + r_out;   // source row, key / query index and RoPE row
 
   const RowView& view = part == 0 ? p.q : (part == 1 ? p.k : p.v);
   const int H = part == 0 ? p.Hq : p.Hkv;
@@ -49,7 +50,7 @@ __global__ void __launch_bounds__(kPrologueThreads) prologue_kernel(const Prolog
   }
   const bool valid = row < valid_rows;
   const bool rope = part < 2 && p.cs != nullptr && row < p.rope_rows;
-  __nv_bfloat16* dst = part == 0 ? p.Qs : (part == 1 ? p.Ks : p.Vs);
+  const TileOut& dst = p.out[part];
   const int half = D / 2;
   const int heads_per_pass = kRowBufFloats / D;
   const int nwarps = blockDim.x / 32;
@@ -59,7 +60,8 @@ __global__ void __launch_bounds__(kPrologueThreads) prologue_kernel(const Prolog
     const int hn = min(heads_per_pass, H - h0);
     const int W = hn * D;
     if (valid) {
-      const int64_t src0 = (int64_t)b * view.bstride + (int64_t)row * view.ld + view.off + (int64_t)(h_begin + h0) * D;
+      const int64_t src0 = (int64_t)b * view.bstride + (int64_t)(p.src_row0[part] + r_out) * view.ld + view.off +
+                           (int64_t)(h_begin + h0) * D;
       for (int e = threadIdx.x; e < W; e += blockDim.x) buf[e] = load_elem(view.ptr, src0 + e, p.src_f32);
     }
     __syncthreads();
@@ -96,12 +98,12 @@ __global__ void __launch_bounds__(kPrologueThreads) prologue_kernel(const Prolog
       }
     }
     __syncthreads();
-    // 16-byte stores: head hh occupies D contiguous bf16 of row `row` in its [pad][D] slab.
+    // 16-byte stores: head hh of the produced row occupies D contiguous bf16 at its destination.
     const int chunks_per_head = D / 8;
     for (int c = threadIdx.x; c < hn * chunks_per_head; c += blockDim.x) {
       const int hh = c / chunks_per_head, sub = c % chunks_per_head;
-      const int64_t slab = (int64_t)bl * H + h0 + hh;
-      uint4* out = reinterpret_cast<uint4*>(dst + (slab * pad + row) * D + sub * 8);
+      uint4* out = reinterpret_cast<uint4*>(dst.ptr + (int64_t)bl * dst.bs + (int64_t)(h0 + hh) * dst.hs +
+                                            (int64_t)r_out * dst.rs + sub * 8);
       *out = *reinterpret_cast<const uint4*>(obuf + hh * D + sub * 8);
     }
     __syncthreads();
@@ -125,7 +127,7 @@ __global__ void __launch_bounds__(256, NSA_PROLOGUE_MIN_BLOCKS) prologue_vec_ker
   const int bl = blockIdx.y % p.B;
   const int b = p.b_begin + bl;
   const int H = part == 0 ? p.Hq : p.Hkv;
-  const int pad = part == 0 ? p.Lq_pad : p.Lk_pad;
+  const int pad = p.rows[part];
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const int sub = (int)(idx % P);
   const long long rest = idx / P;
@@ -133,7 +135,8 @@ __global__ void __launch_bounds__(256, NSA_PROLOGUE_MIN_BLOCKS) prologue_vec_ker
   const long long row_ll = rest / H;
   // Threads past the last row stay until after the shuffle below (all lanes of a warp take part).
   const bool in_range = row_ll < pad;
-  const int row = in_range ? (int)row_ll : 0;
+  const int r_out = in_range ? (int)row_ll : 0;
+  const int row = p.row0[part] + r_out;   // source row, key / query index and RoPE row
   const RowView& view = part == 0 ? p.q : (part == 1 ? p.k : p.v);
   const int h_begin = part == 0 ? p.hq_begin : p.hkv_begin;
   const float* w = part == 0 ? p.q_w : (part == 1 ? p.k_w : nullptr);
@@ -145,8 +148,8 @@ __global__ void __launch_bounds__(256, NSA_PROLOGUE_MIN_BLOCKS) prologue_vec_ker
 #pragma unroll
   for (int i = 0; i < S; ++i) x1[i] = x2[i] = 0.f;
   if (valid) {
-    const T* src = reinterpret_cast<const T*>(view.ptr) + (int64_t)b * view.bstride + (int64_t)row * view.ld + view.off +
-                   (int64_t)(h_begin + hh) * D + sub * S;
+    const T* src = reinterpret_cast<const T*>(view.ptr) + (int64_t)b * view.bstride +
+                   (int64_t)(p.src_row0[part] + r_out) * view.ld + view.off + (int64_t)(h_begin + hh) * D + sub * S;
 #pragma unroll
     for (int v = 0; v < S / EPV; ++v) {
       const uint4 a = __ldg(reinterpret_cast<const uint4*>(src) + v);
@@ -213,8 +216,8 @@ __global__ void __launch_bounds__(256, NSA_PROLOGUE_MIN_BLOCKS) prologue_vec_ker
     }
   }
   // From here each thread writes its own chunk.
-  __nv_bfloat16* dst = (part == 0 ? p.Qs : (part == 1 ? p.Ks : p.Vs)) +
-                       (((int64_t)bl * H + hh) * pad + row) * D + sub * S;
+  const TileOut& to = p.out[part];
+  __nv_bfloat16* dst = to.ptr + (int64_t)bl * to.bs + (int64_t)hh * to.hs + (int64_t)r_out * to.rs + sub * S;
 #pragma unroll
   for (int v = 0; v < S / 8; ++v) {
     uint4 o1, o2;
@@ -312,13 +315,17 @@ bool vec_ok(const PrologueParams& p, int elem) {
   for (const RowView* v : vs)
     if (!aligned16(v->ptr, v->ld * elem) || ((v->bstride * elem) & 15) || ((v->off * elem) & 15)) return false;
   if (p.cs && (!aligned16(p.cs, p.sin_off * 4))) return false;
+  for (int i = p.skip_q ? 1 : 0; i < 3; ++i) {
+    const TileOut& o = p.out[i];
+    if (!aligned16(o.ptr, o.bs * 2) || ((o.hs * 2) & 15) || ((o.rs * 2) & 15)) return false;
+  }
   if ((p.q_w && !aligned16(p.q_w, 0)) || (p.k_w && !aligned16(p.k_w, 0))) return false;
   return true;
 }
 
 template <int D, int P, typename T>
 cudaError_t launch_vec(const PrologueParams& p, cudaStream_t stream) {
-  const int rows = (!p.skip_q && p.Lq_pad > p.Lk_pad) ? p.Lq_pad : p.Lk_pad;
+  const int rows = (!p.skip_q && p.rows[0] > p.rows[1]) ? p.rows[0] : (p.rows[1] > p.rows[2] ? p.rows[1] : p.rows[2]);
   const int H = (!p.skip_q && p.Hq > p.Hkv) ? p.Hq : p.Hkv;
   const long long threads = (long long)rows * H * P;
   const long long blocks = (threads + 255) / 256;
@@ -341,7 +348,7 @@ cudaError_t launch_vec_t(const PrologueParams& p, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream) {
-  const int rows = (!p.skip_q && p.Lq_pad > p.Lk_pad) ? p.Lq_pad : p.Lk_pad;
+  const int rows = (!p.skip_q && p.rows[0] > p.rows[1]) ? p.rows[0] : (p.rows[1] > p.rows[2] ? p.rows[1] : p.rows[2]);
   if (rows <= 0 || p.B <= 0) return cudaSuccess;
   const int elem = p.src_f32 ? 4 : 2;
   if ((p.D == 64 || p.D == 96 || p.D == 128 || p.D == 256) && vec_ok(p, elem))

@@ -1,0 +1,199 @@
+"""Sequence-sharded DiT joint attention over the GPUs of one box (the 16384-token, 2048x2048 case).
+
+The reference runs the DiT block's attention (app/models/nanosaur2.js:196-208) on one device.  Here
+rank r of n owns image rows [q_begin, q_begin + q_count) of every batch element: it normalises and
+rotates its own q/k rows, every rank computes the text k/v rows itself, and one in-place NCCL
+all-gather per batch element assembles the full image k'|v' rows in each GPU's HBM before the
+attention of the local queries runs.  The gather of element b overlaps the attention of element
+b - 1 (the gathers run on their own stream, each attention waits only for its own element).
+
+Per element and rank the C library is called twice (include/nsattn.h):
+``nsa_seq_shard_prologue`` -> all_gather_into_tensor(kv_packed[b, :L]) -> ``nsa_seq_shard_attention``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import List, Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import FusedDesc, NsaError, SeqShard, check, lib
+from .blocks import DIT_HEAD_DIM, DIT_HEADS
+from .ops import RopeTable, dtype_code
+
+
+def seq_shard_rows(L: int, world: int, rank: int) -> Tuple[int, int]:
+    """(q_begin, q_count) of ``rank``: equal contiguous slices of the L image rows.  The in-place
+    all-gather needs equal chunks, so L must be a multiple of ``world``."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("bad rank / world size")
+    if L % world:
+        raise ValueError(f"L={L} image rows do not split evenly over {world} ranks")
+    n = L // world
+    return rank * n, n
+
+
+def gather_views(kv_packed: torch.Tensor, b: int, L: int, q_begin: int, q_count: int):
+    """(output, input) of the in-place all-gather of element b: the image rows [0, L) of kv_packed
+    and this rank's own rows inside them (ncclAllGather's in-place form, sendbuff = recvbuff +
+    rank * count)."""
+    out = kv_packed[b, :L]
+    return out, kv_packed[b, q_begin:q_begin + q_count]
+
+
+@dataclass
+class GatherTiming:
+    """Device times of the last call, in ms: the whole call on the compute stream, and the
+    all-gathers on the communication stream (summed over batch elements)."""
+    call_ms: float
+    gather_ms: float
+
+
+class SeqShardedJointAttention:
+    """One rank's part of the sequence-sharded joint attention.
+
+    qkv (per call): [B, q_count + text_rows, 3*1536] holding this rank's image rows and then the text
+    rows (``local_qkv=True``), or [B, L + text_rows, 3*1536] with every image row present
+    (``local_qkv=False``; only the rank's own rows are read).  kv_len[b] = L + valid text rows,
+    bias [B, text_rows] = log prompt weights (biasStart = L).  Returns [B, q_count, 1536], the rank's
+    rows of the block output.
+    """
+
+    def __init__(self, *, B: int, L: int, text_rows: int, world: int, rank: int, device: torch.device,
+                 group=None, local_qkv: bool = True, eps: float = 1e-6, out_dtype: torch.dtype = torch.bfloat16,
+                 kv_packed: Optional[torch.Tensor] = None):
+        self.B, self.L, self.text_rows, self.world, self.rank = B, L, text_rows, world, rank
+        self.device = torch.device(device)
+        self.group = group
+        self.local_qkv = local_qkv
+        self.eps = eps
+        self.out_dtype = out_dtype
+        self.q_begin, self.q_count = seq_shard_rows(L, world, rank)
+        self.shard = SeqShard(self.q_begin, self.q_count, 0 if local_qkv else self.q_begin,
+                              self.q_count if local_qkv else L)
+        d = self._desc(b=0, count=1)
+        qb, kb, rows = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_int32()
+        check(lib().nsa_seq_shard_buffer_sizes(ctypes.byref(d), ctypes.byref(self.shard), ctypes.byref(qb),
+                                               ctypes.byref(kb), ctypes.byref(rows)))
+        self.q_elem_bytes = qb.value
+        self.kv_rows = rows.value
+        self.kv_ld = 2 * DIT_HEADS * DIT_HEAD_DIM
+        assert kb.value == self.kv_rows * self.kv_ld * 2
+        self.q_prime = torch.empty((B, self.q_elem_bytes), dtype=torch.uint8, device=self.device)
+        shape = (B, self.kv_rows, self.kv_ld)
+        if kv_packed is None:
+            kv_packed = torch.empty(shape, dtype=torch.bfloat16, device=self.device)
+        elif tuple(kv_packed.shape) != shape or kv_packed.dtype != torch.bfloat16 or not kv_packed.is_contiguous():
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, f"kv_packed must be a contiguous bf16 {shape} tensor")
+        self.kv_packed = kv_packed
+        self.comm_stream = torch.cuda.Stream(self.device)
+        self._prologue_done = [torch.cuda.Event() for _ in range(B)]
+        self._gathered = [torch.cuda.Event(enable_timing=True) for _ in range(B)]
+        self._gather_start = [torch.cuda.Event(enable_timing=True) for _ in range(B)]
+        self._call_start = torch.cuda.Event(enable_timing=True)
+        self._call_end = torch.cuda.Event(enable_timing=True)
+
+    def _desc(self, b: int, count: int, qkv: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+              cs: Optional[RopeTable] = None, bias: Optional[torch.Tensor] = None) -> FusedDesc:
+        C = DIT_HEADS * DIT_HEAD_DIM
+        d = FusedDesc()
+        d.B, d.Lq, d.Lk = self.B, self.L, self.L + self.text_rows
+        d.Hq, d.Hkv, d.D = DIT_HEADS, DIT_HEADS, DIT_HEAD_DIM
+        d.qOff, d.kOff, d.vOff = 0, C, 2 * C
+        d.in_dtype = _lib.NSA_BF16 if qkv is None else dtype_code(qkv)
+        d.out_dtype = _lib.NSA_BF16 if out is None else dtype_code(out)
+        if qkv is not None:
+            d.ld, d.bstride = qkv.stride(1), qkv.stride(0)
+        if out is not None:
+            d.ldo, d.o_bstride, d.oOff = out.stride(1), out.stride(0), 0
+        d.eps = self.eps
+        d.sinOff = cs.sinOff if cs is not None else 0
+        d.causal, d.window = 0, 0
+        d.biasStart = self.L
+        d.biasLen = 0 if bias is None else bias.shape[-1]
+        d.bias_bstride = bias.stride(0) if (bias is not None and bias.dim() == 2) else 0
+        d.scale = 0.0
+        d.b_begin, d.b_count, d.h_begin, d.h_count = b, count, 0, 0
+        return d
+
+    def _check(self, qkv, q_norm, k_norm, kv_len, bias, out):
+        rows = self.q_count + self.text_rows if self.local_qkv else self.L + self.text_rows
+        if qkv.dim() != 3 or qkv.shape[0] != self.B or qkv.shape[1] < rows or qkv.stride(-1) != 1:
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, f"qkv must be [{self.B}, >= {rows}, ld] with unit stride")
+        for t in (qkv, q_norm, k_norm, kv_len, bias, out):
+            if t is not None and t.device != self.device:
+                raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, f"tensors must live on {self.device}")
+        if kv_len.dtype != torch.int32 or q_norm.dtype != torch.float32 or k_norm.dtype != torch.float32:
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "kv_len int32, norm weights float32")
+        if bias is not None and bias.dtype != torch.float32:
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "bias must be float32")
+
+    def prologue(self, b: int, qkv: torch.Tensor, *, q_norm: torch.Tensor, k_norm: torch.Tensor,
+                 cs: Optional[RopeTable], kv_len: torch.Tensor) -> None:
+        """Step 1 for element b on the current stream: q' of the rank's rows, k'|v' of its image rows
+        and of all text rows into kv_packed[b]."""
+        d = self._desc(b, 1, qkv, None, cs, None)
+        check(lib().nsa_seq_shard_prologue(
+            ctypes.byref(d), ctypes.byref(self.shard), qkv.data_ptr(), q_norm.data_ptr(), k_norm.data_ptr(),
+            cs.buf.data_ptr() if cs is not None else None, kv_len.data_ptr(), self.q_prime[b].data_ptr(),
+            self.kv_packed[b].data_ptr(), torch.cuda.current_stream(self.device).cuda_stream))
+
+    def gather(self, b: int) -> None:
+        """Step 2 for element b on the current stream: the in-place all-gather of the image rows."""
+        import torch.distributed as dist
+
+        if self.world > 1:
+            o, i = gather_views(self.kv_packed, b, self.L, self.q_begin, self.q_count)
+            dist.all_gather_into_tensor(o, i, group=self.group)
+
+    def attention(self, b: int, *, kv_len: torch.Tensor, bias: Optional[torch.Tensor], out: torch.Tensor) -> None:
+        """Step 3 for element b on the current stream: the rank's queries over all keys."""
+        d = self._desc(b, 1, None, out, None, bias)
+        check(lib().nsa_seq_shard_attention(
+            ctypes.byref(d), ctypes.byref(self.shard), self.q_prime[b].data_ptr(), self.kv_packed[b].data_ptr(),
+            kv_len.data_ptr(), None if bias is None else bias.data_ptr(), out.data_ptr(),
+            torch.cuda.current_stream(self.device).cuda_stream))
+
+    def __call__(self, qkv: torch.Tensor, *, q_norm: torch.Tensor, k_norm: torch.Tensor, cs: Optional[RopeTable],
+                 kv_len: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """All three steps for every element; the gathers run on their own stream so that the gather
+        of element b overlaps the attention of element b - 1."""
+        self._check(qkv, q_norm, k_norm, kv_len, bias, out)
+        if out is None:
+            out = torch.empty((self.B, self.q_count, DIT_HEADS * DIT_HEAD_DIM), dtype=self.out_dtype,
+                              device=self.device)
+        compute = torch.cuda.current_stream(self.device)
+        self._call_start.record(compute)
+        for b in range(self.B):
+            self.prologue(b, qkv, q_norm=q_norm, k_norm=k_norm, cs=cs, kv_len=kv_len)
+            self._prologue_done[b].record(compute)
+        for b in range(self.B):
+            self.comm_stream.wait_event(self._prologue_done[b])
+            with torch.cuda.stream(self.comm_stream):
+                self._gather_start[b].record(self.comm_stream)
+                self.gather(b)
+                self._gathered[b].record(self.comm_stream)
+        for b in range(self.B):
+            compute.wait_event(self._gathered[b])
+            self.attention(b, kv_len=kv_len, bias=bias, out=out)
+        self._call_end.record(compute)
+        return out
+
+    def timing(self) -> GatherTiming:
+        """Device times of the last call (synchronises on it)."""
+        self._call_end.synchronize()
+        gather = sum(self._gather_start[b].elapsed_time(self._gathered[b]) for b in range(self.B))
+        return GatherTiming(call_ms=self._call_start.elapsed_time(self._call_end), gather_ms=gather)
+
+
+def local_rows(qkv_full: torch.Tensor, L: int, q_begin: int, q_count: int) -> torch.Tensor:
+    """The [B, q_count + text_rows, ld] buffer a rank holds in the local layout: its own image rows
+    followed by the text rows of a full-length qkv [B, L + text_rows, ld]."""
+    return torch.cat([qkv_full[:, q_begin:q_begin + q_count], qkv_full[:, L:]], dim=1).contiguous()
+
+
+__all__: List[str] = ["seq_shard_rows", "gather_views", "local_rows", "SeqShardedJointAttention", "GatherTiming"]

@@ -40,14 +40,16 @@ def test_library_exports_every_symbol():
 def test_struct_layouts_match_c(tmp_path):
     src = tmp_path / "sizes.c"
     src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "nsattn.h"\n'
-                   'int main(){printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(nsa_attention_desc),'
+                   'int main(){printf("%zu %zu %zu %zu %zu %zu %zu %zu\\n", sizeof(nsa_attention_desc),'
                    'offsetof(nsa_attention_desc, b_begin), sizeof(nsa_fused_desc), offsetof(nsa_fused_desc, b_begin),'
-                   'sizeof(nsa_kernel_stat), offsetof(nsa_kernel_stat, bytes));return 0;}\n')
+                   'sizeof(nsa_kernel_stat), offsetof(nsa_kernel_stat, bytes), sizeof(nsa_seq_shard),'
+                   'offsetof(nsa_seq_shard, qkv_text_row0));return 0;}\n')
     exe = tmp_path / "sizes"
     subprocess.run(["gcc", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)], check=True)
     got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
     want = [ctypes.sizeof(_lib.AttentionDesc), _lib.AttentionDesc.b_begin.offset, ctypes.sizeof(_lib.FusedDesc),
-            _lib.FusedDesc.b_begin.offset, ctypes.sizeof(_lib.KernelStat), _lib.KernelStat.bytes.offset]
+            _lib.FusedDesc.b_begin.offset, ctypes.sizeof(_lib.KernelStat), _lib.KernelStat.bytes.offset,
+            ctypes.sizeof(_lib.SeqShard), _lib.SeqShard.qkv_text_row0.offset]
     assert got == want
 
 
@@ -98,3 +100,34 @@ def test_workspace_sizes():
     assert wsf == 16 * 4 * 1024 * 256 * 2 + 2 * 16 * 1 * 1024 * 256 * 2 + 1024
     f.D = 100
     assert L.nsa_fused_attention_workspace_size(ctypes.byref(f)) == 0
+
+
+def test_seq_shard_sizes_and_validation():
+    L = _lib.lib()
+    d = _lib.FusedDesc()
+    d.B, d.Lq, d.Lk, d.Hq, d.Hkv, d.D = 4, 16384, 16640, 16, 16, 96
+    d.b_begin, d.b_count = 1, 1
+    s = _lib.SeqShard(2048, 2048, 0, 2048)
+    qb, kb, rows = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_int32()
+    st = L.nsa_seq_shard_buffer_sizes(ctypes.byref(d), ctypes.byref(s), ctypes.byref(qb), ctypes.byref(kb),
+                                      ctypes.byref(rows))
+    assert st == _lib.NSA_OK, L.nsa_last_error()
+    assert rows.value == 16688   # 16640 keys rounded up to 112-key tiles
+    assert qb.value == 16 * 2048 * 96 * 2
+    assert kb.value == rows.value * 2 * 16 * 96 * 2
+    fake = 0x10000   # never dereferenced: validation fails first
+    d.causal = 1
+    assert L.nsa_seq_shard_buffer_sizes(ctypes.byref(d), ctypes.byref(s), None, None, None) == _lib.NSA_ERR_UNSUPPORTED
+    assert L.nsa_seq_shard_prologue(ctypes.byref(d), ctypes.byref(s), fake, fake, fake, None, None, fake, fake,
+                                    None) == _lib.NSA_ERR_UNSUPPORTED
+    d.causal, d.h_begin, d.h_count = 0, 4, 4
+    assert L.nsa_seq_shard_attention(ctypes.byref(d), ctypes.byref(s), fake, fake, None, None, fake,
+                                     None) == _lib.NSA_ERR_UNSUPPORTED
+    d.h_begin, d.h_count = 0, 0
+    s.q_begin = 15000   # rows [15000, 17048) run past Lq
+    assert L.nsa_seq_shard_buffer_sizes(ctypes.byref(d), ctypes.byref(s), None, None, None) == \
+        _lib.NSA_ERR_INVALID_ARGUMENT
+    s.q_begin = 0
+    assert L.nsa_seq_shard_prologue(ctypes.byref(d), ctypes.byref(s), fake, fake, fake, None, None, fake + 8, fake,
+                                    None) == _lib.NSA_ERR_INVALID_ARGUMENT   # q_prime not 16-byte aligned
+    assert L.nsa_seq_shard_buffer_sizes(None, ctypes.byref(s), None, None, None) == _lib.NSA_ERR_INVALID_ARGUMENT

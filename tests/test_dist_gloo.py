@@ -54,3 +54,72 @@ def test_two_rank_sharding_and_timing_reduction():
         assert set(gathered[0]).isdisjoint(gathered[1])
         assert t == 3.0
         assert tot == 3.0
+
+
+def _packed_kv(qkv, L, kv_len, k_w, cos, sin, rows):
+    """k'|v' rows (head-normed k, 2D RoPE on image rows; raw v) of the given key rows, through the
+    oracle; rows at or past kv_len stay zero."""
+    import numpy as np
+
+    from oracle import attention_oracle as O
+    C = 16 * 96
+    out = np.zeros((len(rows), 2 * C), dtype=np.float32)
+    for i, r in enumerate(rows):
+        if r >= kv_len:
+            continue
+        k = qkv[r:r + 1, C:2 * C]
+        rope = (cos[r:r + 1], sin[r:r + 1]) if r < L else (None, None)
+        out[i, :C] = O.head_norm(k, k_w, 16, 96, *rope)
+        out[i, C:] = qkv[r, 2 * C:]
+    return out
+
+
+def _seq_worker(rank, world, port, q):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from nanosaur2_web_b200.seqshard import gather_views, seq_shard_rows
+    from oracle import attention_oracle as O
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        B, h, w, Lt, kv_rows = 2, 4, 8, 8, 48
+        L = h * w
+        g = np.random.default_rng(7)   # same inputs on every rank
+        qkv = g.standard_normal((B, L + Lt, 3 * 16 * 96)).astype(np.float32)
+        k_w = (1 + 0.1 * g.standard_normal(96)).astype(np.float32)
+        kv_len = [L + 5, L + Lt]
+        cos, sin = O.rope_2d(h, w)
+        q0, qn = seq_shard_rows(L, world, rank)
+        kv = torch.full((B, kv_rows, 2 * 16 * 96), float("nan"))
+        for b in range(B):
+            # what this rank's prologue writes: its own image rows, then every text / padding row
+            kv[b, q0:q0 + qn] = torch.from_numpy(_packed_kv(qkv[b], L, kv_len[b], k_w, cos, sin, range(q0, q0 + qn)))
+            kv[b, L:] = torch.from_numpy(_packed_kv(qkv[b], L, kv_len[b], k_w, cos, sin, range(L, kv_rows)))
+            out, inp = gather_views(kv, b, L, q0, qn)
+            dist.all_gather_into_tensor(out, inp.clone())
+        full = [_packed_kv(qkv[b], L, kv_len[b], k_w, cos, sin, range(kv_rows)) for b in range(B)]
+        err = max(float(np.abs(kv[b].numpy() - full[b]).max()) for b in range(B))
+        q.put((rank, err))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(120)
+def test_two_rank_sequence_shard_gather_assembles_all_keys():
+    """Each rank writes the k'|v' rows of its own image rows and of all text rows; the per-element
+    all-gather over the views the CUDA path uses yields every rank the full key set."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_seq_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=100) for _ in procs]
+    for p in procs:
+        p.join(timeout=30)
+        assert p.exitcode == 0
+    for rank, err in results:
+        assert err == 0.0, (rank, err)

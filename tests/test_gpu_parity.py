@@ -297,6 +297,29 @@ def test_gemma_config4_shape(theta, window):
         assert_close_bf16(out[b], want, 256, what=f"gemma theta={theta} window={window} b={b}")
 
 
+def test_gemma_full_pass_many_waves():
+    """Config 4's full pass: batch 16 (512 CTAs per layer, several waves per SM) through all 18
+    layers, twice.  Every CTA's barrier hand-offs must complete under load (a lost phase shows up
+    as an expired bounded wait in check_device); the last layer is checked against the oracle."""
+    from nanosaur2_web_b200.blocks import gemma_layer_attention, gemma_rope_theta
+    from nanosaur2_web_b200.ops import ropeTable
+    B, L = 16, 1024
+    qkv, q_w, k_w = gemma_inputs(56, B, L)
+    x, qn, kn = t(qkv, torch.bfloat16), t(q_w), t(k_w)
+    tables = {th: ropeTable(L, 256, th, DEV) for th in (1e4, 1e6)}
+    out = torch.empty((B, L, 1024), dtype=torch.float32, device=DEV)
+    for _ in range(2):
+        for layer in range(18):
+            th = gemma_rope_theta(layer)
+            gemma_layer_attention(x, q_norm=qn, k_norm=kn, cs=tables[th], window=0 if th == 1e6 else 512, out=out)
+    check_device()
+    got = out.cpu().numpy()
+    for b in (0, 15):   # layer 17 is global (theta 1e6, no window)
+        want = O.gemma_attention(qkv[b, :, :1024], qkv[b, :, 1024:1280], qkv[b, :, 1280:], q_w, k_w, 1e6,
+                                 acc=np.float64)
+        assert_close_bf16(got[b], want, 256, what=f"gemma pass b={b}")
+
+
 @pytest.mark.parametrize("D,H,group,causal,Lq,Lk", [(64, 4, 1, False, 300, 257), (128, 4, 2, False, 200, 333),
                                                      (96, 2, 1, True, 260, 260), (256, 2, 2, True, 129, 129)])
 def test_generic_attention_op(D, H, group, causal, Lq, Lk):

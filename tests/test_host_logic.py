@@ -49,3 +49,36 @@ def test_bench_flop_counts():
     assert math.isclose(bench.joint_flops(1, 2304, [128]), 34.43e9, rel_tol=1e-3)
     g, l = bench.gemma_pairs(1024, 0), bench.gemma_pairs(1024, 512)
     assert g == 524800 and l == 393472
+
+
+@pytest.mark.parametrize("L,world", [(16384, 2), (16384, 4), (16384, 8), (3952, 4), (512, 1)])
+def test_seq_shard_rows_tile_the_image_rows(L, world):
+    from nanosaur2_web_b200.seqshard import seq_shard_rows
+    rows = [seq_shard_rows(L, world, r) for r in range(world)]
+    assert rows[0][0] == 0 and all(c == L // world for _, c in rows)
+    assert all(rows[i][0] + rows[i][1] == rows[i + 1][0] for i in range(world - 1))
+    assert rows[-1][0] + rows[-1][1] == L
+
+
+def test_seq_shard_rows_rejects_uneven_split():
+    from nanosaur2_web_b200.seqshard import seq_shard_rows
+    with pytest.raises(ValueError):
+        seq_shard_rows(3952, 3, 0)
+    with pytest.raises(ValueError):
+        seq_shard_rows(64, 2, 2)
+
+
+def test_gather_views_are_in_place_chunks():
+    import torch
+
+    from nanosaur2_web_b200.seqshard import gather_views, seq_shard_rows
+    L, world, kv_rows, ld = 64, 4, 96, 12
+    kv = torch.zeros(2, kv_rows, ld)
+    for rank in range(world):
+        q0, qn = seq_shard_rows(L, world, rank)
+        out, inp = gather_views(kv, 1, L, q0, qn)
+        assert out.is_contiguous() and inp.is_contiguous()
+        assert out.numel() == world * inp.numel()
+        # ncclAllGather's in-place form: sendbuff = recvbuff + rank * sendcount
+        assert inp.data_ptr() == out.data_ptr() + rank * inp.numel() * inp.element_size()
+        assert out.data_ptr() == kv.data_ptr() + kv_rows * ld * kv.element_size()
