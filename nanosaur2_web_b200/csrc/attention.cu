@@ -37,6 +37,11 @@ constexpr int kKeyBiasMax = 1024;           // keys covered by the shared-memory
 #ifndef NSA_MAX3
 #define NSA_MAX3 1
 #endif
+// Bit i set: pairs c with c % 8 == i take 2^x from the FMA-pipe polynomial (ex2_poly2) instead of
+// the special-function unit, to balance the two pipes.
+#ifndef NSA_POLY_MASK
+#define NSA_POLY_MASK 0
+#endif
 
 template <int D>
 struct Cfg {
@@ -619,9 +624,16 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         uint32_t pk[32];
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          float y0, y1;
-          f2_unpack(f2_fma(f2_pack(x[2 * c], x[2 * c + 1]), sc2, nm2), y0, y1);
-          const float a0 = ex2(y0), a1 = ex2(y1);
+          float a0, a1;
+          const uint64_t y = f2_fma(f2_pack(x[2 * c], x[2 * c + 1]), sc2, nm2);
+          if ((NSA_POLY_MASK >> (c & 7)) & 1) {
+            ex2_poly2(y, a0, a1);
+          } else {
+            float y0, y1;
+            f2_unpack(y, y0, y1);
+            a0 = ex2(y0);
+            a1 = ex2(y1);
+          }
           ls[c & 3] = f2_add(ls[c & 3], f2_pack(a0, a1));
           pk[c] = pack_bf16x2(a0, a1);
         }
@@ -634,9 +646,16 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         uint32_t pk[C::P1_COLS];
 #pragma unroll
         for (int c = 0; c < C::P1_COLS; ++c) {
-          float y0, y1;
-          f2_unpack(f2_fma(f2_pack(x[64 + 2 * c], x[64 + 2 * c + 1]), sc2, nm2), y0, y1);
-          const float a0 = ex2(y0), a1 = ex2(y1);
+          float a0, a1;
+          const uint64_t y = f2_fma(f2_pack(x[64 + 2 * c], x[64 + 2 * c + 1]), sc2, nm2);
+          if ((NSA_POLY_MASK >> (c & 7)) & 1) {
+            ex2_poly2(y, a0, a1);
+          } else {
+            float y0, y1;
+            f2_unpack(y, y0, y1);
+            a0 = ex2(y0);
+            a1 = ex2(y1);
+          }
           ls[c & 3] = f2_add(ls[c & 3], f2_pack(a0, a1));
           pk[c] = pack_bf16x2(a0, a1);
         }

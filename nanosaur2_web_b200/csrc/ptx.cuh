@@ -196,20 +196,9 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, to take part of the exponentials off the special-function unit:
-// x = n + f with n = round(x), f in [-0.5, 0.5]; 2^f from a degree-3 polynomial (coefficients from
-// csrc/fit_exp2_poly.py, max relative error 8.4e-5), 2^n added to the exponent field.  Inputs below
-// -125 (masked keys are -inf) return exactly 0, like ex2.approx does for -inf.
-__device__ __forceinline__ float ex2_poly(float x_in) {
-  const float x = fmaxf(x_in, -125.f);
-  const float t = x + 12582912.f;   // 1.5 * 2^23: the low mantissa bits of t now hold round(x)
-  const float f = x - (t - 12582912.f);
-  float p = fmaf(0.0552130044f, f, 0.242713943f);
-  p = fmaf(p, f, 0.69326216f);
-  p = fmaf(p, f, 0.999919593f);
-  const float r = __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-  return x_in < -125.f ? 0.f : r;
-}
+// 2^x on the FMA pipe, to take part of the exponentials off the special-function unit (see
+// ex2_poly2 below): x = n + f with n = round(x), f in [-0.5, 0.5]; 2^f from a degree-3 polynomial
+// (coefficients from csrc/fit_exp2_poly.py, max relative error 8.4e-5) times 2^n.
 
 // Packed fp32x2 arithmetic (sm_100): two floats per 64-bit register, one instruction for both.
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
@@ -237,12 +226,13 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
 }
 
 // ex2_poly on a packed pair: the argument reduction and the polynomial run as f32x2 instructions.
-// Inputs are clamped to -125 (callers use it only where every logit is finite); 2^-125 is zero for
-// every use here.
+// Inputs are clamped to -127: n = round(x) >= -127 and 2^n is built as a float from its exponent
+// field, (n + 127) << 23, which is exactly +0 for n = -127.  So masked keys (-inf) give exactly 0,
+// like ex2.approx, and no input can carry into the sign bit.
 __device__ __forceinline__ void ex2_poly2(uint64_t y, float& r0, float& r1) {
   float y0, y1;
   f2_unpack(y, y0, y1);
-  const uint64_t x = f2_pack(fmaxf(y0, -125.f), fmaxf(y1, -125.f));
+  const uint64_t x = f2_pack(fmaxf(y0, -127.f), fmaxf(y1, -127.f));
   const uint64_t magic = f2_pack(12582912.f, 12582912.f);   // 1.5 * 2^23
   const uint64_t t = f2_add(x, magic);                       // low mantissa bits hold round(x)
   const uint64_t nf = f2_add(t, f2_pack(-12582912.f, -12582912.f));
@@ -250,11 +240,12 @@ __device__ __forceinline__ void ex2_poly2(uint64_t y, float& r0, float& r1) {
   uint64_t p = f2_fma(f2_pack(0.0552130044f, 0.0552130044f), f, f2_pack(0.242713943f, 0.242713943f));
   p = f2_fma(p, f, f2_pack(0.69326216f, 0.69326216f));
   p = f2_fma(p, f, f2_pack(0.999919593f, 0.999919593f));
-  float p0, p1, t0, t1;
-  f2_unpack(p, p0, p1);
+  float t0, t1;
   f2_unpack(t, t0, t1);
-  r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-  r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+  // the low bits of t hold n in two's complement: t << 23 is n << 23 modulo 2^32
+  const float s0 = __uint_as_float((__float_as_uint(t0) << 23) + (127u << 23));
+  const float s1 = __uint_as_float((__float_as_uint(t1) << 23) + (127u << 23));
+  f2_unpack(f2_mul(p, f2_pack(s0, s1)), r0, r1);
 }
 
 // max of three floats in one instruction (sm_100).
