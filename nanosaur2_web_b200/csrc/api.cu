@@ -1,5 +1,6 @@
 // C ABI of libnsattn.so (declared in include/nsattn.h): argument validation, workspace planning,
 // TMA descriptor encoding, the per-kernel profiler and the device error word.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -146,8 +147,51 @@ struct Plan {
   int b0, Bs, hq0, Hqs, hkv0, Hkvs;  // shard
   int NQ, BN, blk, Lq_pad, Lk_pad;
   bool qtmem;
-  size_t q_bytes, k_bytes, v_bytes, total;
+  int split_cap;   // work units whose key range may be split over two CTAs (0: never)
+  size_t q_bytes, k_bytes, v_bytes, split_bytes, total;
 };
+
+// Scratch of the tail split (nsa::AttnParams::part_o / part_ml / split_count) for `units` units.
+size_t split_scratch_bytes(int units, int NQ, int D) {
+  if (units <= 0) return 0;
+  const size_t rows = (size_t)units * 2 * NQ * nsa::kTileM;
+  return align_up(rows * D * 4, 256) + align_up(rows * 2 * 4, 256) + align_up((size_t)units * 4, 256);
+}
+
+struct SplitScratch {
+  float* part_o;
+  float* part_ml;
+  int* count;
+};
+
+SplitScratch split_scratch(uint8_t* base, int units, int NQ, int D) {
+  const size_t rows = (size_t)units * 2 * NQ * nsa::kTileM;
+  SplitScratch s;
+  s.part_o = reinterpret_cast<float*>(base);
+  s.part_ml = reinterpret_cast<float*>(base + align_up(rows * D * 4, 256));
+  s.count = reinterpret_cast<int*>(base + align_up(rows * D * 4, 256) + align_up(rows * 2 * 4, 256));
+  return s;
+}
+
+unsigned env_flag(const char* name, unsigned dflt) {
+  const char* v = std::getenv(name);
+  return (v && *v) ? (unsigned)std::atoi(v) : dflt;
+}
+
+// Units of the last, partial wave that run as two half-key-range CTAs each, or 0.  The split pays
+// when at most half the SMs would otherwise be busy in that wave: the wave then takes half as
+// long.  NSA_SPLIT_TAIL=0 turns it off.
+int split_units_for(const Plan& pl, int causal, int window) {
+  static const unsigned enabled = env_flag("NSA_SPLIT_TAIL", 1);
+  if (!enabled || pl.split_cap <= 0 || causal || window || pl.Lk < 2 * pl.BN) return 0;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      sms <= 0)
+    return 0;
+  const long long units = (long long)pl.Bs * pl.Hqs * (pl.Lq_pad / (pl.NQ * nsa::kTileM));
+  const int rem = (int)(units % sms);
+  return (rem > 0 && 2 * rem <= sms && rem <= pl.split_cap) ? rem : 0;
+}
 
 struct CommonArgs {
   int B, Lq, Lk, H, group, D, causal, window, in_dtype, out_dtype;
@@ -190,7 +234,10 @@ nsa_status make_plan(const CommonArgs& a, Plan* pl) {
   p.q_bytes = align_up((size_t)q_rows * a.D * 2, 1024);
   p.k_bytes = align_up((size_t)kv_rows * a.D * 2, 1024);
   p.v_bytes = p.k_bytes;
-  p.total = p.q_bytes + p.k_bytes + p.v_bytes + 1024;
+  const long long units = (long long)p.Bs * p.Hqs * (p.Lq_pad / (NQ * nsa::kTileM));
+  p.split_cap = (NQ == 2 && !a.causal && !a.window) ? (int)std::min<long long>(units, nsa::kSplitUnitsMax) : 0;
+  p.split_bytes = split_scratch_bytes(p.split_cap, NQ, a.D);
+  p.total = p.q_bytes + p.k_bytes + p.v_bytes + p.split_bytes + 1024;
   *pl = p;
   return NSA_OK;
 }
@@ -239,6 +286,16 @@ nsa::AttnParams attn_params(const Plan& pl, const CommonArgs& a, const float* bi
   return ap;
 }
 
+void set_split(nsa::AttnParams* ap, const Plan& pl, const CommonArgs& a, const SplitScratch& s) {
+  const int r = split_units_for(pl, a.causal, a.window);
+  if (r <= 0) return;
+  ap->split_units = r;
+  ap->split_first = pl.Bs * pl.Hqs * (pl.Lq_pad / (pl.NQ * nsa::kTileM)) - r;
+  ap->part_o = s.part_o;
+  ap->part_ml = s.part_ml;
+  ap->split_count = s.count;
+}
+
 // Algorithmic flops of one attention launch: 4 * B * H * valid pairs * D (app/gpu/ops.js:207).
 double attn_flops(const Plan& pl, const CommonArgs& a) {
   double pairs = (double)pl.Lq * pl.Lk;
@@ -278,6 +335,9 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
   pp.rows[0] = pl.Lq_pad;
   pp.rows[1] = pp.rows[2] = pl.Lk_pad;
   for (int i = 0; i < 3; ++i) pp.row0[i] = pp.src_row0[i] = 0;
+  const SplitScratch split = split_scratch(base + pl.q_bytes + pl.k_bytes + pl.v_bytes, pl.split_cap, pl.NQ, pl.D);
+  pp.zero_ptr = pl.split_cap > 0 ? split.count : nullptr;   // the attention's split counters start at zero
+  pp.zero_count = pl.split_cap;
   // Kernels that keep Q in tensor memory TMA-load the raw bf16 query rows straight from the input
   // when the layout allows a tiled map over it (16-byte aligned rows and head offsets, whole rows
   // per batch element); they then apply the q norm and RoPE themselves.  Otherwise (fp32 input, odd
@@ -318,6 +378,7 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
   ap.k_x0 = ap.v_x0 = ap.kv_xh = 0;
   ap.kv_yb = pl.Hkvs * pl.Lk_pad;
   ap.kv_yh = pl.Lk_pad;
+  set_split(&ap, pl, a, split);
   if (q_direct) {
     ap.q_x0 = (int)pp.q.off;
     ap.q_xh = pl.D;
@@ -385,6 +446,7 @@ struct SeqPlan {
   int L;               // image rows (the descriptor's Lq)
   int q_begin, q_count, img_row0, text_row0;
   int64_t kv_ld;       // elements per kv_packed row: 2 * Hkv * D
+  size_t q_tiles_bytes;  // the q' tiles at the start of q_prime; the tail-split scratch follows
   size_t q_bytes, kv_bytes;
 };
 
@@ -413,7 +475,8 @@ nsa_status make_seq_plan(const nsa_fused_desc* d, const nsa_seq_shard* s, SeqPla
   p.kv_ld = 2LL * d->Hkv * d->D;
   if ((int64_t)p.pl.Bs * p.pl.Lk_pad >= (int64_t)1 << 31)
     return fail(NSA_ERR_UNSUPPORTED, "problem too large for one launch");
-  p.q_bytes = (size_t)p.pl.Bs * p.pl.Hqs * p.pl.Lq_pad * p.pl.D * 2;
+  p.q_tiles_bytes = align_up((size_t)p.pl.Bs * p.pl.Hqs * p.pl.Lq_pad * p.pl.D * 2, 1024);
+  p.q_bytes = p.q_tiles_bytes + p.pl.split_bytes;
   p.kv_bytes = (size_t)p.pl.Bs * p.pl.Lk_pad * p.kv_ld * 2;
   *sp = p;
   return NSA_OK;
@@ -685,6 +748,10 @@ nsa_status nsa_seq_shard_prologue(const nsa_fused_desc* d, const nsa_seq_shard* 
     pp.src_row0[i] = sp.img_row0;
   }
   pp.skip_q = 0;
+  const SplitScratch split =
+      split_scratch(static_cast<uint8_t*>(q_prime) + sp.q_tiles_bytes, pl.split_cap, pl.NQ, pl.D);
+  pp.zero_ptr = pl.split_cap > 0 ? split.count : nullptr;   // the attention's split counters start at zero
+  pp.zero_count = pl.split_cap;
   const double in_elem = d->in_dtype == NSA_F32 ? 4.0 : 2.0;
   const cudaStream_t strm = static_cast<cudaStream_t>(stream);
   double bytes = (double)pl.Bs * sp.q_count * (pl.Hqs + 2.0 * pl.Hkvs) * pl.D * (in_elem + 2.0);
@@ -693,6 +760,8 @@ nsa_status nsa_seq_shard_prologue(const nsa_fused_desc* d, const nsa_seq_shard* 
   // the text rows (and the zero padding up to kv_rows), which every rank computes for itself
   if (pl.Lk_pad > sp.L) {
     pp.skip_q = 1;
+    pp.zero_ptr = nullptr;
+    pp.zero_count = 0;
     pp.out[1].ptr = KV + (int64_t)sp.L * sp.kv_ld;
     pp.out[2].ptr = KV + (int64_t)sp.L * sp.kv_ld + v_col;
     pp.rows[1] = pp.rows[2] = pl.Lk_pad - sp.L;
@@ -737,6 +806,9 @@ nsa_status nsa_seq_shard_attention(const nsa_fused_desc* d, const nsa_seq_shard*
   ap.q_yh = pl.Lq_pad;
   ap.q_b0 = pl.b0;
   ap.q_h0 = 0;
+  set_split(&ap, pl, sp.a,
+            split_scratch(static_cast<uint8_t*>(const_cast<void*>(q_prime)) + sp.q_tiles_bytes, pl.split_cap, pl.NQ,
+                          pl.D));
   const cudaStream_t strm = static_cast<cudaStream_t>(stream);
   cudaError_t e = profiled("attention", attn_flops(pl, sp.a), 0.0, strm,
                            [&] { return nsa::launch_attention(ap, pl.D, tq, tkv, tkv, strm); });

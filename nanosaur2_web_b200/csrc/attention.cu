@@ -237,12 +237,20 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   uint64_t* o_full = p_full + 4;     // [2]   O complete (NQ = 1: [0] once per P*V, [1] after the last)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* split_arrival = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
-  // ---- work unit: (batch, query head, query block)
-  const int qb_raw = blockIdx.x % p.q_blocks;
-  const int rest = blockIdx.x / p.q_blocks;
+  // ---- work unit: (batch, query head, query block); units of the split tail run as two CTAs,
+  // one per half of the unit's key tiles (split_half 0 / 1)
+  int unit = (int)blockIdx.x, split_half = -1, split_idx = 0;
+  if (p.split_units > 0 && unit >= p.split_first) {
+    split_idx = (unit - p.split_first) >> 1;
+    split_half = (unit - p.split_first) & 1;
+    unit = p.split_first + split_idx;
+  }
+  const int qb_raw = unit % p.q_blocks;
+  const int rest = unit / p.q_blocks;
   const int qb = p.causal ? (p.q_blocks - 1 - qb_raw) : qb_raw;   // long causal blocks first
   const int hl = rest % p.Hq;
   const int bl = rest / p.Hq;
@@ -254,8 +262,17 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   int kv_end = kv_valid;
   if (p.causal) kv_end = min(kv_end, q_row_end);
   const int kv_begin = p.window > 0 ? max(0, q_row0 - p.window + 1) : 0;
-  const int j0 = kv_begin / BN;
-  const int n = kv_end > kv_begin ? ((kv_end - 1) / BN - j0 + 1) : 0;
+  int j0 = kv_begin / BN;
+  int n = kv_end > kv_begin ? ((kv_end - 1) / BN - j0 + 1) : 0;
+  if (split_half >= 0) {
+    const int n_first = n / 2;
+    if (split_half == 0) {
+      n = n_first;
+    } else {
+      j0 += n_first;
+      n -= n_first;
+    }
+  }
   const int q_tma_row = (bl * p.Hq + hl) * p.Lq_pad + q_row0;
   const int kv_y0 = bl * p.kv_yb + hkvl * p.kv_yh;
   const int k_x = p.k_x0 + hkvl * p.kv_xh, v_x = p.v_x0 + hkvl * p.kv_xh;
@@ -681,7 +698,77 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (ok) tc_fence_after();
     }
-    if (ok) {
+    // Tail split: publish this half's unnormalised O and (m, l); the CTA that finishes second
+    // merges both halves (O = (O_a 2^(m_a - m) + O_b 2^(m_b - m)) / (l_a 2^(m_a - m) + l_b 2^(m_b - m))).
+    // The go / no-go is CTA-uniform over the softmax threads (bar.red), because the hand-off below
+    // uses named barriers that every one of them must reach.
+    const bool split_ok = split_half >= 0 && bar_and_pred<1, NQ * 128>(ok);
+    if (split_ok) {
+      const int urow = tile * kTileM + quarter * 32 + lane;   // row within the unit
+      const int64_t mine = ((int64_t)split_idx * 2 + split_half) * (NQ * kTileM) + urow;
+      const int64_t other = ((int64_t)split_idx * 2 + (split_half ^ 1)) * (NQ * kTileM) + urow;
+#pragma unroll 1
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t r[32];
+        if (n > 0) {
+          tmem_ld32(lane_base + C::o_col(tile) + (uint32_t)(cc * 32), r);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) r[c] = 0u;
+        }
+        float4* po = reinterpret_cast<float4*>(p.part_o + mine * D + cc * 32);
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          po[c] = make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]), __uint_as_float(r[4 * c + 2]),
+                              __uint_as_float(r[4 * c + 3]));
+      }
+      *reinterpret_cast<float2*>(p.part_ml + mine * 2) = make_float2(m_run, l_run);
+      __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"n"(NQ * 128) : "memory");
+      if (threadIdx.x == 128) *split_arrival = atomicAdd(&p.split_count[split_idx], 1);
+      asm volatile("bar.sync 1, %0;" ::"n"(NQ * 128) : "memory");
+      if (*split_arrival == 1) {
+        __threadfence();
+        const float2 mo = __ldcg(reinterpret_cast<const float2*>(p.part_ml + other * 2));
+        const float m = fmaxf(m_run, mo.x);
+        const float w_me = m_run == -INFINITY ? 0.f : ex2(m_run - m);
+        const float w_ot = mo.x == -INFINITY ? 0.f : ex2(mo.x - m);
+        const float l = l_run * w_me + mo.y * w_ot;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const float a_me = w_me * inv, a_ot = w_ot * inv;
+        const bool store = row < p.Lq;
+        const int64_t obase = (int64_t)b * p.out_bstride + (int64_t)row * p.out_ld + p.out_off +
+                              (int64_t)(p.hq_begin + hl) * D;
+#pragma unroll 1
+        for (int cc = 0; cc < D / 32; ++cc) {
+          float v[32];
+          const float4* pm = reinterpret_cast<const float4*>(p.part_o + mine * D + cc * 32);
+          const float4* pt = reinterpret_cast<const float4*>(p.part_o + other * D + cc * 32);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float4 x0 = pm[c], x1 = __ldcg(pt + c);
+            v[4 * c] = x0.x * a_me + x1.x * a_ot;
+            v[4 * c + 1] = x0.y * a_me + x1.y * a_ot;
+            v[4 * c + 2] = x0.z * a_me + x1.z * a_ot;
+            v[4 * c + 3] = x0.w * a_me + x1.w * a_ot;
+          }
+          if (store) {
+            if (p.out_f32) {
+              float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + obase + cc * 32);
+#pragma unroll
+              for (int c = 0; c < 8; ++c) o[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+            } else {
+              uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + obase + cc * 32);
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                o[c] = make_uint4(pack_bf16x2(v[8 * c], v[8 * c + 1]), pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
+                                  pack_bf16x2(v[8 * c + 4], v[8 * c + 5]), pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
+            }
+          }
+        }
+        if (threadIdx.x == 128) p.split_count[split_idx] = 0;   // ready for the next launch
+      }
+    } else if (ok && split_half < 0) {
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       const bool store = row < p.Lq;
       const int64_t obase = (int64_t)b * p.out_bstride + (int64_t)row * p.out_ld + p.out_off +
@@ -750,7 +837,12 @@ cudaError_t launch_d(const AttnParams& p, const CUtensorMap& tmQ, const CUtensor
     }
     if (dev >= 0 && dev < 128) configured[dev] = true;
   }
-  const long long blocks = (long long)p.B * p.Hq * p.q_blocks;
+  long long blocks = (long long)p.B * p.Hq * p.q_blocks;
+  if (p.split_units > 0) {
+    // the split tail: split_units units from split_first on, two CTAs each
+    if (C::NQ != 2 || p.causal || p.window || p.split_first + p.split_units != blocks) return cudaErrorInvalidValue;
+    blocks += p.split_units;
+  }
   if (blocks <= 0) return cudaSuccess;
   if (blocks > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   attn_fwd_kernel<D><<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, stream>>>(tmQ, tmK, tmV, p);

@@ -54,6 +54,8 @@ struct PrologueParams {
   int row0[3];          // logical row (query / key index, RoPE row) of produced row 0, per part
   int src_row0[3];      // row of the source buffer holding produced row 0, per part
   int skip_q;           // 1: no Q tiles (the attention kernel prepares Q itself)
+  int* zero_ptr;        // zero_count ints cleared by the first block (the attention's split counters)
+  int zero_count;
 };
 
 struct AttnParams {
@@ -87,7 +89,19 @@ struct AttnParams {
   const float* q_cs;
   int64_t q_sin_off;
   int q_rope_rows;
+  // Tail split (two query tiles per CTA, no causal mask or window): the work units from
+  // split_first on (the last, partial wave) run as two CTAs each, one per half of the key tiles.
+  // Each writes its unnormalised O and (m, l) per row to part_o / part_ml; whichever finishes
+  // second (split_count) merges the halves and writes the output.  split_units = 0: no split.
+  int split_first, split_units;
+  float* part_o;         // [split_units][2][2 * 128][D]
+  float* part_ml;        // [split_units][2][2 * 128][2]
+  int* split_count;      // [split_units], zero at launch (the prologue clears it)
 };
+
+// Work units at or above this count in the last wave are not split (bounds the partial-result
+// scratch: half the SMs of a B200).
+constexpr int kSplitUnitsMax = 74;
 
 // Tile geometry of the attention kernel for a head dim.
 struct AttnGeometry {

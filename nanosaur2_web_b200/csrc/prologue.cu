@@ -28,6 +28,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 __global__ void __launch_bounds__(kPrologueThreads) prologue_kernel(const PrologueParams p) {
   __shared__ float buf[kRowBufFloats];
   __shared__ __align__(16) __nv_bfloat16 obuf[kRowBufFloats];
+  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+    for (int i = threadIdx.x; i < p.zero_count; i += blockDim.x) p.zero_ptr[i] = 0;
 
   const int r_out = blockIdx.x;       // produced row
   const int bl = blockIdx.y;          // batch index within the shard
@@ -123,6 +125,8 @@ __global__ void __launch_bounds__(256, NSA_PROLOGUE_MIN_BLOCKS) prologue_vec_ker
   constexpr int HALF = D / 2;
   constexpr int EPV = 16 / sizeof(T);   // input elements per 16-byte vector
   static_assert(S % 8 == 0 && S % EPV == 0, "vector width");
+  if (blockIdx.x == 0 && blockIdx.y == 0)
+    for (int i = threadIdx.x; i < p.zero_count; i += blockDim.x) p.zero_ptr[i] = 0;
   const int part = blockIdx.y / p.B + (p.skip_q ? 1 : 0);
   const int bl = blockIdx.y % p.B;
   const int b = p.b_begin + bl;

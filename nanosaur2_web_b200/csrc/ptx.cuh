@@ -248,6 +248,21 @@ __device__ __forceinline__ void ex2_poly2(uint64_t y, float& r0, float& r1) {
   f2_unpack(f2_mul(p, f2_pack(s0, s1)), r0, r1);
 }
 
+// Named barrier `ID` over `N` threads that also ANDs a predicate across them (bar.red.and).
+template <int ID, int N>
+__device__ __forceinline__ bool bar_and_pred(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "n"(ID), "n"(N)
+      : "memory");
+  return r != 0;
+}
+
 // max of three floats in one instruction (sm_100).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;

@@ -2,8 +2,9 @@
 
 Every rank builds the same seeded joint-attention inputs, keeps its own image rows plus the text rows
 (the local layout), and runs SeqShardedJointAttention, which gathers the k'|v' rows over NCCL.  Rank 0
-stitches the ranks' output rows together and compares them with the single-GPU fused call (bit for
-bit) and with the CPU oracle on a few heads; it writes the verdict as JSON to argv[1].
+stitches the ranks' output rows together and compares them with the single-GPU fused call (to the
+size of P's bf16 rounding) and with the CPU oracle on a few heads; it writes the verdict as JSON to
+argv[1].
 """
 
 import datetime
@@ -59,7 +60,9 @@ def main():
                                              heads=heads)
             cols = np.concatenate([np.arange(hh * 96, (hh + 1) * 96) for hh in heads])
             got = full.float().cpu().numpy()[..., cols]
-            res = {"world": world, "equal_to_fused": bool(torch.equal(full, ref)),
+            # equal to the size of P's bf16 rounding: a split tail rounds each half against its own max
+            diff = float((full.float() - ref.float()).abs().max())
+            res = {"world": world, "equal_to_fused": diff <= 2e-3, "max_abs_vs_fused": diff,
                    "max_abs_vs_oracle": float(np.abs(got - want[..., cols]).max()),
                    "min_cos_vs_oracle": float(per_head_cosine(got, want[..., cols], 96).min()),
                    "call_ms": timing.call_ms, "gather_ms": timing.gather_ms}

@@ -85,15 +85,26 @@ def test_validation_without_gpu():
     assert L.nsa_status_string(_lib.NSA_ERR_DEVICE) == b"device-side error"
 
 
+def _split_scratch(units, D, nq=2):
+    """Scratch of the tail split: partial O and (m, l) of two half-key CTAs per unit, plus a counter;
+    reserved for at most 74 units (half a B200's SMs)."""
+    u = min(units, 74)
+    up = lambda x: (x + 255) // 256 * 256
+    rows = u * 2 * nq * 128
+    return up(rows * D * 4) + up(rows * 2 * 4) + up(u * 4)
+
+
 def test_workspace_sizes():
     L = _lib.lib()
     d = _desc(Lq=3952, Lk=4208, H=16, D=96, B=2)
     ws = L.nsa_attention_workspace_size(ctypes.byref(d))
     lq_pad, lk_pad = 4096, 4256   # query blocks of 2x128 rows; key tiles of 112 rows for head dim 96
-    want = 2 * 16 * lq_pad * 96 * 2 + 2 * (2 * 16 * lk_pad * 96 * 2) + 1024
-    assert ws == want
+    tiles = 2 * 16 * lq_pad * 96 * 2 + 2 * (2 * 16 * lk_pad * 96 * 2)
+    assert ws == tiles + _split_scratch(2 * 16 * 16, 96) + 1024
     d.h_begin, d.h_count = 4, 4
-    assert L.nsa_attention_workspace_size(ctypes.byref(d)) == (want - 1024) // 4 + 1024
+    assert L.nsa_attention_workspace_size(ctypes.byref(d)) == tiles // 4 + _split_scratch(2 * 4 * 16, 96) + 1024
+    d.h_begin, d.h_count, d.causal = 0, 0, 1   # causal: no tail split, no scratch
+    assert L.nsa_attention_workspace_size(ctypes.byref(d)) == tiles + 1024
     f = _lib.FusedDesc()
     f.B, f.Lq, f.Lk, f.Hq, f.Hkv, f.D, f.causal = 16, 1024, 1024, 4, 1, 256, 1
     wsf = L.nsa_fused_attention_workspace_size(ctypes.byref(f))
@@ -113,7 +124,7 @@ def test_seq_shard_sizes_and_validation():
                                       ctypes.byref(rows))
     assert st == _lib.NSA_OK, L.nsa_last_error()
     assert rows.value == 16688   # 16640 keys rounded up to 112-key tiles
-    assert qb.value == 16 * 2048 * 96 * 2
+    assert qb.value == 16 * 2048 * 96 * 2 + _split_scratch(16 * 8, 96)
     assert kb.value == rows.value * 2 * 16 * 96 * 2
     fake = 0x10000   # never dereferenced: validation fails first
     d.causal = 1
