@@ -34,14 +34,6 @@ namespace {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units: P may reach 2^8 before O is rescaled
 constexpr int kKeyBiasMax = 1024;           // keys covered by the shared-memory key bias/mask table
-#ifndef NSA_MAX3
-#define NSA_MAX3 1
-#endif
-// Bit i set: pairs c with c % 8 == i take 2^x from the FMA-pipe polynomial (ex2_poly2) instead of
-// the special-function unit, to balance the two pipes.
-#ifndef NSA_POLY_MASK
-#define NSA_POLY_MASK 0
-#endif
 
 template <int D>
 struct Cfg {
@@ -580,7 +572,6 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
           f2_unpack(f2_fma(f2_pack(x[c + 2], x[c + 3]), sl2x2, f2_pack(kv4.z, kv4.w)), x[c + 2], x[c + 3]);
         }
       }
-#if NSA_MAX3
       float mx[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) mx[k] = fmaxf(x[2 * k], x[2 * k + 1]);
@@ -590,14 +581,6 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         for (int k = 0; k < 4; ++k) mx[k] = fmax3(mx[k], x[c + 2 * k], x[c + 2 * k + 1]);
       }
       const float tmax = fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3])) * sc;
-#else
-      float mx[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mx[k] = x[k];
-#pragma unroll
-      for (int c = 8; c < BN; ++c) mx[c & 7] = fmaxf(mx[c & 7], x[c]);
-      const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sc;
-#endif
       const float m_new = fmaxf(m_run, tmax);
       if (j == 0) {
         m_run = m_new;
@@ -641,16 +624,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         uint32_t pk[32];
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          float a0, a1;
-          const uint64_t y = f2_fma(f2_pack(x[2 * c], x[2 * c + 1]), sc2, nm2);
-          if ((NSA_POLY_MASK >> (c & 7)) & 1) {
-            ex2_poly2(y, a0, a1);
-          } else {
-            float y0, y1;
-            f2_unpack(y, y0, y1);
-            a0 = ex2(y0);
-            a1 = ex2(y1);
-          }
+          float y0, y1;
+          f2_unpack(f2_fma(f2_pack(x[2 * c], x[2 * c + 1]), sc2, nm2), y0, y1);
+          const float a0 = ex2(y0), a1 = ex2(y1);
           ls[c & 3] = f2_add(ls[c & 3], f2_pack(a0, a1));
           pk[c] = pack_bf16x2(a0, a1);
         }
@@ -663,16 +639,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         uint32_t pk[C::P1_COLS];
 #pragma unroll
         for (int c = 0; c < C::P1_COLS; ++c) {
-          float a0, a1;
-          const uint64_t y = f2_fma(f2_pack(x[64 + 2 * c], x[64 + 2 * c + 1]), sc2, nm2);
-          if ((NSA_POLY_MASK >> (c & 7)) & 1) {
-            ex2_poly2(y, a0, a1);
-          } else {
-            float y0, y1;
-            f2_unpack(y, y0, y1);
-            a0 = ex2(y0);
-            a1 = ex2(y1);
-          }
+          float y0, y1;
+          f2_unpack(f2_fma(f2_pack(x[64 + 2 * c], x[64 + 2 * c + 1]), sc2, nm2), y0, y1);
+          const float a0 = ex2(y0), a1 = ex2(y1);
           ls[c & 3] = f2_add(ls[c & 3], f2_pack(a0, a1));
           pk[c] = pack_bf16x2(a0, a1);
         }

@@ -196,10 +196,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, to take part of the exponentials off the special-function unit (see
-// ex2_poly2 below): x = n + f with n = round(x), f in [-0.5, 0.5]; 2^f from a degree-3 polynomial
-// (coefficients from csrc/fit_exp2_poly.py, max relative error 8.4e-5) times 2^n.
-
 // Packed fp32x2 arithmetic (sm_100): two floats per 64-bit register, one instruction for both.
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   uint64_t r;
@@ -223,29 +219,6 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   uint64_t r;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
-}
-
-// ex2_poly on a packed pair: the argument reduction and the polynomial run as f32x2 instructions.
-// Inputs are clamped to -127: n = round(x) >= -127 and 2^n is built as a float from its exponent
-// field, (n + 127) << 23, which is exactly +0 for n = -127.  So masked keys (-inf) give exactly 0,
-// like ex2.approx, and no input can carry into the sign bit.
-__device__ __forceinline__ void ex2_poly2(uint64_t y, float& r0, float& r1) {
-  float y0, y1;
-  f2_unpack(y, y0, y1);
-  const uint64_t x = f2_pack(fmaxf(y0, -127.f), fmaxf(y1, -127.f));
-  const uint64_t magic = f2_pack(12582912.f, 12582912.f);   // 1.5 * 2^23
-  const uint64_t t = f2_add(x, magic);                       // low mantissa bits hold round(x)
-  const uint64_t nf = f2_add(t, f2_pack(-12582912.f, -12582912.f));
-  const uint64_t f = f2_fma(nf, f2_pack(-1.f, -1.f), x);     // x - round(x), in [-0.5, 0.5]
-  uint64_t p = f2_fma(f2_pack(0.0552130044f, 0.0552130044f), f, f2_pack(0.242713943f, 0.242713943f));
-  p = f2_fma(p, f, f2_pack(0.69326216f, 0.69326216f));
-  p = f2_fma(p, f, f2_pack(0.999919593f, 0.999919593f));
-  float t0, t1;
-  f2_unpack(t, t0, t1);
-  // the low bits of t hold n in two's complement: t << 23 is n << 23 modulo 2^32
-  const float s0 = __uint_as_float((__float_as_uint(t0) << 23) + (127u << 23));
-  const float s1 = __uint_as_float((__float_as_uint(t1) << 23) + (127u << 23));
-  f2_unpack(f2_mul(p, f2_pack(s0, s1)), r0, r1);
 }
 
 // Named barrier `ID` over `N` threads that also ANDs a predicate across them (bar.red.and).
