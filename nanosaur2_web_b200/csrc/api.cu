@@ -353,8 +353,19 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
                         pp.q.off + (int64_t)pl.Hq * pl.D <= pp.q.ld && (!pp.q_w || al16(pp.q_w)) &&
                         (!pp.cs || (al16(pp.cs) && (pp.sin_off * 4) % 16 == 0));
   pp.skip_q = q_direct ? 1 : 0;
+  // V needs no normalisation: for bf16 rows that a tiled map can cover (16-byte aligned rows and
+  // head offsets, whole rows per batch element) the attention kernel reads V tiles of valid keys
+  // straight from the input, and the prologue writes only the last partial tile and the padding.
+  static const unsigned v_direct_enabled = env_flag("NSA_V_DIRECT", 1);   // NSA_V_DIRECT=0 turns it off
+  const bool v_direct = v_direct_enabled && a.in_dtype == NSA_BF16 && al16(pp.v.ptr) &&
+                        pp.v.ld % 8 == 0 && pp.v.off % 8 == 0 &&
+                        (pl.B == 1 || (pp.v.bstride > 0 && pp.v.bstride % pp.v.ld == 0)) &&
+                        pp.v.off + (int64_t)(pl.hkv0 + pl.Hkvs) * pl.D <= pp.v.ld;
+  pp.v_tile = v_direct ? pl.BN : 0;
   const double in_elem = a.in_dtype == NSA_F32 ? 4.0 : 2.0;
-  const double pro_bytes = (double)pl.Bs * ((q_direct ? 0.0 : (double)pl.Lq * pl.Hqs) + 2.0 * pl.Lk * pl.Hkvs) *
+  // algorithmic bytes: q and k rows, and the v rows the prologue writes (all, or about one tile)
+  const double v_rows = v_direct ? (double)pl.BN : (double)pl.Lk;
+  const double pro_bytes = (double)pl.Bs * ((q_direct ? 0.0 : (double)pl.Lq * pl.Hqs) + (pl.Lk + v_rows) * pl.Hkvs) *
                            pl.D * (in_elem + 2.0);
   cudaError_t e = profiled("prologue", 0.0, pro_bytes, stream, [&] { return nsa::launch_prologue(pp, stream); });
   if (e != cudaSuccess) return cuda_fail(e, "prologue launch");
@@ -372,6 +383,13 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
   if (!maps_ok || !encode_tiles(&tk, Ks, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk, pl.BN) ||
       !encode_tiles(&tv, Vs, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk, pl.BN))
     return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed (driver entry point unavailable?)");
+  CUtensorMap tvd = tv;
+  if (v_direct) {
+    // the input rows of every batch element: [B * rows per element][ld]
+    const int64_t total_rows = pl.B == 1 ? pp.v.rows : (int64_t)(pl.B - 1) * (pp.v.bstride / pp.v.ld) + pp.v.rows;
+    if (!encode_rows(&tvd, pp.v.ptr, pp.v.ld, pp.v.ld, total_rows, pl.blk, pl.BN))
+      return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed (driver entry point unavailable?)");
+  }
 
   nsa::AttnParams ap = attn_params(pl, a, bias, bias_start, bias_len, bias_bstride, kv_len, scale, out, ldo,
                                    o_bstride, oOff, err);
@@ -379,6 +397,12 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
   ap.kv_yb = pl.Hkvs * pl.Lk_pad;
   ap.kv_yh = pl.Lk_pad;
   set_split(&ap, pl, a, split);
+  if (v_direct) {
+    ap.v_direct = 1;
+    ap.vd_x0 = (int)(pp.v.off + (int64_t)pl.hkv0 * pl.D);
+    ap.vd_xh = pl.D;
+    ap.vd_yb = pl.B == 1 ? 0 : (int)(pp.v.bstride / pp.v.ld);
+  }
   if (q_direct) {
     ap.q_x0 = (int)pp.q.off;
     ap.q_xh = pl.D;
@@ -406,7 +430,8 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
     ap.q_rope_rows = 0;
   }
   const double flops = attn_flops(pl, a);
-  e = profiled("attention", flops, 0.0, stream, [&] { return nsa::launch_attention(ap, pl.D, tq, tk, tv, stream); });
+  e = profiled("attention", flops, 0.0, stream,
+               [&] { return nsa::launch_attention(ap, pl.D, tq, tk, tv, tvd, stream); });
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");
   return NSA_OK;
 }
@@ -811,7 +836,7 @@ nsa_status nsa_seq_shard_attention(const nsa_fused_desc* d, const nsa_seq_shard*
                           pl.D));
   const cudaStream_t strm = static_cast<cudaStream_t>(stream);
   cudaError_t e = profiled("attention", attn_flops(pl, sp.a), 0.0, strm,
-                           [&] { return nsa::launch_attention(ap, pl.D, tq, tkv, tkv, strm); });
+                           [&] { return nsa::launch_attention(ap, pl.D, tq, tkv, tkv, tkv, strm); });
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");
   return NSA_OK;
 }

@@ -206,7 +206,8 @@ __device__ __forceinline__ void tmem_st_n(uint32_t taddr, const uint32_t (&r)[N]
 template <int D>
 __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmVd,
+                    const AttnParams p) {
   using C = Cfg<D>;
   constexpr int NQ = C::NQ, NS = C::NS, BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
@@ -268,6 +269,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   const int q_tma_row = (bl * p.Hq + hl) * p.Lq_pad + q_row0;
   const int kv_y0 = bl * p.kv_yb + hkvl * p.kv_yh;
   const int k_x = p.k_x0 + hkvl * p.kv_xh, v_x = p.v_x0 + hkvl * p.kv_xh;
+  const int vd_x = p.vd_x0 + hkvl * p.vd_xh, vd_y0 = b * p.vd_yb;
   const uint64_t to = p.timeout_ns;
 
   if (threadIdx.x == 0) {
@@ -292,6 +294,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
+    if (p.v_direct) tma_prefetch_desc(&tmVd);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -340,9 +343,16 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         if (j >= NS && !wait_bounded(&v_empty[s], ((j / NS) - 1) & 1, abort_flag, p.err, kErrTimeoutLoad, to))
           return false;
         mbar_arrive_expect_tx(&v_full[s], C::KV_TILE_BYTES);
-        for (int c = 0; c < C::NB; ++c)
-          tma_load_2d(sV + s * C::KV_TILE_BYTES + c * C::KBLK_BYTES, &tmV, &v_full[s], v_x + c * C::BLK,
-                      kv_y0 + (j0 + j) * BN);
+        if (p.v_direct && (j0 + j + 1) * BN <= kv_valid) {
+          // a tile of valid keys only: straight from the input rows
+          for (int c = 0; c < C::NB; ++c)
+            tma_load_2d(sV + s * C::KV_TILE_BYTES + c * C::KBLK_BYTES, &tmVd, &v_full[s], vd_x + c * C::BLK,
+                        vd_y0 + (j0 + j) * BN);
+        } else {
+          for (int c = 0; c < C::NB; ++c)
+            tma_load_2d(sV + s * C::KV_TILE_BYTES + c * C::KBLK_BYTES, &tmV, &v_full[s], v_x + c * C::BLK,
+                        kv_y0 + (j0 + j) * BN);
+        }
         return true;
       };
       int k_issued = 0, v_issued = 0;
@@ -787,7 +797,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
 
 template <int D>
 cudaError_t launch_d(const AttnParams& p, const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
-                     cudaStream_t stream) {
+                     const CUtensorMap& tmVd, cudaStream_t stream) {
   using C = Cfg<D>;
   static bool configured[128] = {};   // the attribute is set once per device
   int dev = 0;
@@ -814,7 +824,7 @@ cudaError_t launch_d(const AttnParams& p, const CUtensorMap& tmQ, const CUtensor
   }
   if (blocks <= 0) return cudaSuccess;
   if (blocks > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
-  attn_fwd_kernel<D><<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, stream>>>(tmQ, tmK, tmV, p);
+  attn_fwd_kernel<D><<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, stream>>>(tmQ, tmK, tmV, tmVd, p);
   return cudaGetLastError();
 }
 
@@ -831,12 +841,12 @@ AttnGeometry attention_geometry(int D) {
 }
 
 cudaError_t launch_attention(const AttnParams& p, int D, const CUtensorMap& tmQ, const CUtensorMap& tmK,
-                             const CUtensorMap& tmV, cudaStream_t stream) {
+                             const CUtensorMap& tmV, const CUtensorMap& tmVd, cudaStream_t stream) {
   switch (D) {
-    case 64: return launch_d<64>(p, tmQ, tmK, tmV, stream);
-    case 96: return launch_d<96>(p, tmQ, tmK, tmV, stream);
-    case 128: return launch_d<128>(p, tmQ, tmK, tmV, stream);
-    case 256: return launch_d<256>(p, tmQ, tmK, tmV, stream);
+    case 64: return launch_d<64>(p, tmQ, tmK, tmV, tmVd, stream);
+    case 96: return launch_d<96>(p, tmQ, tmK, tmV, tmVd, stream);
+    case 128: return launch_d<128>(p, tmQ, tmK, tmV, tmVd, stream);
+    case 256: return launch_d<256>(p, tmQ, tmK, tmV, tmVd, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -56,6 +56,10 @@ struct PrologueParams {
   int skip_q;           // 1: no Q tiles (the attention kernel prepares Q itself)
   int* zero_ptr;        // zero_count ints cleared by the first block (the attention's split counters)
   int zero_count;
+  // > 0: the attention kernel reads V straight from the input for key tiles of v_tile rows that
+  // hold only valid keys; the prologue then writes V rows only from the first tile that does not
+  // (the last partial tile and the padding, zero-filled).
+  int v_tile;
 };
 
 struct AttnParams {
@@ -97,6 +101,10 @@ struct AttnParams {
   float* part_o;         // [split_units][2][2 * 128][D]
   float* part_ml;        // [split_units][2][2 * 128][2]
   int* split_count;      // [split_units], zero at launch (the prologue clears it)
+  // V straight from the input (tmVd) for key tiles that hold only valid keys: box (x, y) with
+  // x = vd_x0 + h*vd_xh + c*blk (h = local kv head), y = b*vd_yb + key (b = global batch index);
+  // other tiles come from the prologue's V tiles (tmV).
+  int v_direct, vd_x0, vd_xh, vd_yb;
 };
 
 // Work units at or above this count in the last wave are not split (bounds the partial-result
@@ -116,7 +124,7 @@ cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream);
 
 // Returns cudaErrorInvalidValue for unsupported head dims.
 cudaError_t launch_attention(const AttnParams& p, int D, const CUtensorMap& tmQ, const CUtensorMap& tmK,
-                             const CUtensorMap& tmV, cudaStream_t stream);
+                             const CUtensorMap& tmV, const CUtensorMap& tmVd, cudaStream_t stream);
 
 cudaError_t launch_head_norm(void* X, int f32, const float* w, int L, int H, int D, int64_t ld, int64_t col_off,
                              int64_t row_off, const float* cs, int64_t sin_off, float eps, cudaStream_t stream);

@@ -53,6 +53,7 @@ __global__ void __launch_bounds__(kPrologueThreads) prologue_kernel(const Prolog
   const bool valid = row < valid_rows;
   const bool rope = part < 2 && p.cs != nullptr && row < p.rope_rows;
   const TileOut& dst = p.out[part];
+  if (part == 2 && p.v_tile > 0 && row < valid_rows / p.v_tile * p.v_tile) return;   // read from the input
   const int half = D / 2;
   const int heads_per_pass = kRowBufFloats / D;
   const int nwarps = blockDim.x / 32;
@@ -192,6 +193,7 @@ __global__ void __launch_bounds__(256, NSA_PROLOGUE_MIN_BLOCKS) prologue_vec_ker
     r = rsqrtf(ss / (float)D + p.eps);
   }
   if (!in_range) return;
+  if (part == 2 && p.v_tile > 0 && row < valid_rows / p.v_tile * p.v_tile) return;   // read from the input
   if (valid) {
     if (w) {
       const float4* w1 = reinterpret_cast<const float4*>(w + sub * S);
@@ -338,11 +340,16 @@ cudaError_t launch_vec(const PrologueParams& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// threads per head of a row at head dim 96
+#ifndef NSA_PROLOGUE_P96
+#define NSA_PROLOGUE_P96 2
+#endif
+
 template <typename T>
 cudaError_t launch_vec_t(const PrologueParams& p, cudaStream_t stream) {
   switch (p.D) {
     case 64: return launch_vec<64, 2, T>(p, stream);
-    case 96: return launch_vec<96, 2, T>(p, stream);
+    case 96: return launch_vec<96, NSA_PROLOGUE_P96, T>(p, stream);
     case 128: return launch_vec<128, 2, T>(p, stream);
     case 256: return launch_vec<256, 4, T>(p, stream);
     default: return cudaErrorNotSupported;
