@@ -586,7 +586,7 @@ def run_config5(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     B, HW, LT5 = 4, 128, 256
     L = HW * HW
-    m = SeqShardedJointAttention(B=B, L=L, text_rows=LT5, world=world, rank=rank, device=dev)
+    m = SeqShardedJointAttention(B=B, L=L, text_rows=LT5, world=world, rank=rank, device=dev, mode=args.seq_mode)
     g = np.random.default_rng(5000)   # shared by every rank: weights, text lengths, prompt weights
     q_w = (1.0 + 0.2 * g.standard_normal(D)).astype(np.float32)
     k_w = (1.0 + 0.2 * g.standard_normal(D)).astype(np.float32)
@@ -617,14 +617,22 @@ def run_config5(args, rank, world, local_rank):
     exposed = max_over_ranks(ms / args.steps - kernel_ms)
     flops = sum_over_ranks(sum(4.0 * H * m.q_count * (L + int(lv[b])) * D for b in range(B)) * args.steps)
     recv = B * (L - m.q_count) * m.kv_ld * 2
+    m.close()
     if rank != 0:
         return
     cfg = {"workload": "config 5: DiT joint attention at 128x128=16384 image tokens + 256 text slots (valid "
                        "~U[32,256], log-weight bias), 16 heads x 96, batch 4, fused q/k RMSNorm + 2D RoPE",
            "global_batch": B, "seq_len": L + LT5, "parallelism": f"sequence-sharded x{world} "
                                                                  f"({m.q_count} query rows per rank)",
-           "collective": "in-place NCCL all_gather_into_tensor of the k'|v' image rows per batch element "
-                         "(torch.distributed), overlapped with the previous element's attention",
+           "collective": ("in-place NCCL all_gather_into_tensor of the k'|v' image rows per batch element "
+                          "(torch.distributed), overlapped with the previous element's attention")
+                         if m.mode == "nccl" else
+                         ("the prologue stores each k'|v' image row into every peer's buffer over NVLink (CUDA "
+                          "IPC mappings), one-element NCCL all-reduce as the barrier per batch element, "
+                          "overlapped with the previous element's attention") if m.mode == "p2p" else
+                         ("local prologue, then one copy-engine cudaMemcpyAsync of the rank's k'|v' rows into "
+                          "each peer's buffer (CUDA IPC mappings), one-element NCCL all-reduce as the barrier "
+                          "per batch element, overlapped with the previous element's attention"),
            "l2": "two input sets of this rank's rows alternate; kv_packed is rewritten every step"}
     extra = {"allgather": {"bytes_received_per_rank_per_step": recv, "gather_ms_per_step": gather_ms,
                            "kernel_ms_per_step": kernel_ms, "exposed_ms_per_step": exposed,
@@ -671,6 +679,9 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="profiling driver: warm-up + timed device-resident steps only (no e2e, CPU or clocks)")
     ap.add_argument("--batch", type=int, default=B_PER_GPU, help="batch per GPU (profiling runs only)")
+    ap.add_argument("--seq-mode", choices=["nccl", "p2p", "ce"], default="ce",
+                    help="config 5: k'|v' exchange by NCCL all-gather, peer stores from the prologue, or "
+                         "copy-engine pushes")
     ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2,
                     help="BASELINE config to run (2 = the headline line; 3, 4, 5 print their own line)")
     args = ap.parse_args()

@@ -187,6 +187,29 @@ nsa_status nsa_seq_shard_buffer_sizes(const nsa_fused_desc* desc, const nsa_seq_
 nsa_status nsa_seq_shard_prologue(const nsa_fused_desc* desc, const nsa_seq_shard* shard, const void* qkv,
                                   const float* q_norm_w, const float* k_norm_w, const float* cs,
                                   const int32_t* kv_len, void* q_prime, void* kv_packed, void* stream);
+/* CUDA IPC for the peer buffers: nsa_ipc_export writes NSA_IPC_HANDLE_BYTES describing the
+ * device allocation holding device_ptr (a cudaIpcMemHandle_t and the offset into it); another
+ * process passes them to nsa_ipc_import, which maps the allocation on its current device (peer
+ * access enabled) and returns the same address in its space; nsa_ipc_close unmaps it. */
+#define NSA_IPC_HANDLE_BYTES 72
+nsa_status nsa_ipc_export(const void* device_ptr, void* handle_out);
+nsa_status nsa_ipc_import(const void* handle, void** device_ptr_out);
+nsa_status nsa_ipc_close(void* device_ptr);
+/* One stream-ordered copy (cudaMemcpyAsync, cudaMemcpyDefault): with a peer mapping from
+ * nsa_ipc_import as dst, the copy engines move the rank's k'|v' rows over NVLink without SMs. */
+nsa_status nsa_memcpy_async(void* dst, const void* src, size_t bytes, void* stream);
+
+/* Step 1 fused with step 2 over peer memory: also stores the image rows' k'|v' into each of
+ * kv_peers[0 .. n_peers) (n_peers <= 8): the other GPUs' kv_packed buffers for the same batch
+ * elements, mapped into this process (CUDA IPC), at the same offsets as in kv_packed.  The stores
+ * cross NVLink directly from the prologue's registers.  Before any GPU's attention reads
+ * kv_packed, every GPU's prologue must have completed (a barrier on the stream, e.g. a one-element
+ * all-reduce); before a prologue overwrites a peer's kv_packed, that peer's previous attention
+ * must have completed. */
+nsa_status nsa_seq_shard_prologue_peers(const nsa_fused_desc* desc, const nsa_seq_shard* shard, const void* qkv,
+                                        const float* q_norm_w, const float* k_norm_w, const float* cs,
+                                        const int32_t* kv_len, void* q_prime, void* kv_packed,
+                                        void* const* kv_peers, int32_t n_peers, void* stream);
 nsa_status nsa_seq_shard_attention(const nsa_fused_desc* desc, const nsa_seq_shard* shard,
                                    const void* q_prime, const void* kv_packed, const int32_t* kv_len,
                                    const float* bias, void* out, void* stream);

@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(HERE, "libnsattn.so")
 
 NSA_OK, NSA_ERR_INVALID_ARGUMENT, NSA_ERR_UNSUPPORTED, NSA_ERR_WORKSPACE, NSA_ERR_CUDA, NSA_ERR_DEVICE = range(6)
 NSA_F32, NSA_BF16 = 0, 1
+NSA_IPC_HANDLE_BYTES = 72
 
 _i32, _i64, _f32, _vp, _sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
 
@@ -73,6 +74,12 @@ SIGNATURES = {
                                           ctypes.POINTER(_sz), ctypes.POINTER(_i32)]),
     "nsa_seq_shard_prologue": (_i32, [ctypes.POINTER(FusedDesc), ctypes.POINTER(SeqShard), _vp, _vp, _vp, _vp, _vp,
                                       _vp, _vp, _vp]),
+    "nsa_ipc_export": (_i32, [_vp, _vp]),
+    "nsa_ipc_import": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "nsa_ipc_close": (_i32, [_vp]),
+    "nsa_memcpy_async": (_i32, [_vp, _vp, _sz, _vp]),
+    "nsa_seq_shard_prologue_peers": (_i32, [ctypes.POINTER(FusedDesc), ctypes.POINTER(SeqShard), _vp, _vp, _vp, _vp,
+                                            _vp, _vp, _vp, ctypes.POINTER(_vp), _i32, _vp]),
     "nsa_seq_shard_attention": (_i32, [ctypes.POINTER(FusedDesc), ctypes.POINTER(SeqShard), _vp, _vp, _vp, _vp, _vp,
                                        _vp]),
     "nsa_rope2d_table": (_i32, [_i32, _i32, _i32, _vp, _vp]),

@@ -509,6 +509,26 @@ nsa_status make_seq_plan(const nsa_fused_desc* d, const nsa_seq_shard* s, SeqPla
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
 
+// ------------------------------------------------------------------------------------ CUDA IPC
+
+using GetAddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+GetAddressRangeFn address_range_fn() {
+  static GetAddressRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<GetAddressRangeFn>(p);
+  });
+  return fn;
+}
+
+std::mutex g_ipc_mu;
+std::vector<std::pair<void*, void*>> g_ipc_open;   // (pointer handed out, mapping base)
+
 }  // namespace
 
 namespace nsa {
@@ -714,6 +734,65 @@ int32_t nsa_profiler_read(nsa_kernel_stat* out, int32_t max_entries) {
   return n;
 }
 
+nsa_status nsa_ipc_export(const void* device_ptr, void* handle_out) {
+  if (!device_ptr || !handle_out) return fail(NSA_ERR_INVALID_ARGUMENT, "device_ptr and handle_out are required");
+  GetAddressRangeFn range = address_range_fn();
+  if (!range) return fail(NSA_ERR_CUDA, "cuMemGetAddressRange unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(device_ptr)) != CUDA_SUCCESS)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "device_ptr is not in a device allocation");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  const uint64_t off = reinterpret_cast<uintptr_t>(device_ptr) - static_cast<uintptr_t>(base);
+  std::memcpy(handle_out, &h, sizeof h);
+  std::memcpy(static_cast<uint8_t*>(handle_out) + sizeof h, &off, sizeof off);
+  return NSA_OK;
+}
+
+nsa_status nsa_ipc_import(const void* handle, void** device_ptr_out) {
+  if (!handle || !device_ptr_out) return fail(NSA_ERR_INVALID_ARGUMENT, "handle and device_ptr_out are required");
+  cudaIpcMemHandle_t h;
+  uint64_t off = 0;
+  std::memcpy(&h, handle, sizeof h);
+  std::memcpy(&off, static_cast<const uint8_t*>(handle) + sizeof h, sizeof off);
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  void* ptr = static_cast<uint8_t*>(base) + off;
+  {
+    std::lock_guard<std::mutex> lk(g_ipc_mu);
+    g_ipc_open.emplace_back(ptr, base);
+  }
+  *device_ptr_out = ptr;
+  return NSA_OK;
+}
+
+nsa_status nsa_ipc_close(void* device_ptr) {
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_ipc_mu);
+    for (size_t i = 0; i < g_ipc_open.size(); ++i)
+      if (g_ipc_open[i].first == device_ptr) {
+        base = g_ipc_open[i].second;
+        g_ipc_open.erase(g_ipc_open.begin() + (long)i);
+        break;
+      }
+  }
+  if (!base) return fail(NSA_ERR_INVALID_ARGUMENT, "not a pointer returned by nsa_ipc_import");
+  cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return NSA_OK;
+}
+
+nsa_status nsa_memcpy_async(void* dst, const void* src, size_t bytes, void* stream) {
+  if (!dst || !src) return fail(NSA_ERR_INVALID_ARGUMENT, "dst and src are required");
+  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync");
+  return NSA_OK;
+}
+
 nsa_status nsa_seq_shard_buffer_sizes(const nsa_fused_desc* desc, const nsa_seq_shard* shard, size_t* q_prime_bytes,
                                       size_t* kv_packed_bytes, int32_t* kv_rows) {
   SeqPlan sp;
@@ -728,6 +807,19 @@ nsa_status nsa_seq_shard_buffer_sizes(const nsa_fused_desc* desc, const nsa_seq_
 nsa_status nsa_seq_shard_prologue(const nsa_fused_desc* d, const nsa_seq_shard* s, const void* qkv,
                                   const float* q_norm_w, const float* k_norm_w, const float* cs, const int32_t* kv_len,
                                   void* q_prime, void* kv_packed, void* stream) {
+  return nsa_seq_shard_prologue_peers(d, s, qkv, q_norm_w, k_norm_w, cs, kv_len, q_prime, kv_packed, nullptr, 0,
+                                      stream);
+}
+
+nsa_status nsa_seq_shard_prologue_peers(const nsa_fused_desc* d, const nsa_seq_shard* s, const void* qkv,
+                                        const float* q_norm_w, const float* k_norm_w, const float* cs,
+                                        const int32_t* kv_len, void* q_prime, void* kv_packed,
+                                        void* const* kv_peers, int32_t n_peers, void* stream) {
+  if (n_peers < 0 || n_peers > nsa::kMaxPeers || (n_peers > 0 && !kv_peers))
+    return fail(NSA_ERR_INVALID_ARGUMENT, "n_peers must be in [0, 8] with a kv_peers array");
+  for (int i = 0; i < n_peers; ++i)
+    if (!kv_peers[i] || (reinterpret_cast<uintptr_t>(kv_peers[i]) & 15))
+      return fail(NSA_ERR_INVALID_ARGUMENT, "kv_peers must be 16-byte aligned device pointers");
   SeqPlan sp;
   nsa_status st = make_seq_plan(d, s, &sp);
   if (st != NSA_OK) return st;
@@ -772,6 +864,10 @@ nsa_status nsa_seq_shard_prologue(const nsa_fused_desc* d, const nsa_seq_shard* 
     pp.row0[i] = sp.q_begin;
     pp.src_row0[i] = sp.img_row0;
   }
+  // the image rows' k'|v' also go to the other GPUs' kv_packed (same offsets, through their mappings)
+  pp.n_peers = n_peers;
+  for (int i = 0; i < n_peers; ++i)
+    pp.peer_off[i] = reinterpret_cast<const uint8_t*>(kv_peers[i]) - reinterpret_cast<const uint8_t*>(kv_packed);
   pp.skip_q = 0;
   const SplitScratch split =
       split_scratch(static_cast<uint8_t*>(q_prime) + sp.q_tiles_bytes, pl.split_cap, pl.NQ, pl.D);
@@ -785,6 +881,7 @@ nsa_status nsa_seq_shard_prologue(const nsa_fused_desc* d, const nsa_seq_shard* 
   // the text rows (and the zero padding up to kv_rows), which every rank computes for itself
   if (pl.Lk_pad > sp.L) {
     pp.skip_q = 1;
+    pp.n_peers = 0;   // every GPU computes the text rows itself
     pp.zero_ptr = nullptr;
     pp.zero_count = 0;
     pp.out[1].ptr = KV + (int64_t)sp.L * sp.kv_ld;

@@ -23,6 +23,8 @@ struct RowView {
   int64_t rows;
 };
 
+constexpr int kMaxPeers = 8;   // GPUs of one box a sequence-sharded prologue writes to
+
 // Destination of prepared bf16 rows: element (local batch bl, local head h, produced row r, d) at
 // ptr[bl*bs + h*hs + r*rs + d].  Head-major tiles: hs = pad*D, rs = D; packed K|V rows: hs = D.
 struct TileOut {
@@ -60,6 +62,10 @@ struct PrologueParams {
   // hold only valid keys; the prologue then writes V rows only from the first tile that does not
   // (the last partial tile and the padding, zero-filled).
   int v_tile;
+  // k and v rows also go to n_peers further copies of their buffer: the destination plus
+  // peer_off[i] bytes (another GPU's buffer mapped into this process; sequence shards).
+  int n_peers;
+  int64_t peer_off[kMaxPeers];
 };
 
 struct AttnParams {

@@ -107,10 +107,14 @@ __global__ void __launch_bounds__(kPrologueThreads) prologue_kernel(const Prolog
       const int hh = c / chunks_per_head, sub = c % chunks_per_head;
       uint4* out = reinterpret_cast<uint4*>(dst.ptr + (int64_t)bl * dst.bs + (int64_t)(h0 + hh) * dst.hs +
                                             (int64_t)r_out * dst.rs + sub * 8);
-      *out = *reinterpret_cast<const uint4*>(obuf + hh * D + sub * 8);
+      const uint4 val = *reinterpret_cast<const uint4*>(obuf + hh * D + sub * 8);
+      *out = val;
+      if (part > 0)
+        for (int i = 0; i < p.n_peers; ++i) *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out) + p.peer_off[i]) = val;
     }
     __syncthreads();
   }
+  if (part > 0 && p.n_peers > 0) __threadfence_system();   // peer stores visible before any later signal
 }
 
 // Vectorised prologue for aligned layouts.  Each head of a row is handled by P consecutive threads;
@@ -238,7 +242,16 @@ __global__ void __launch_bounds__(256, NSA_PROLOGUE_MIN_BLOCKS) prologue_vec_ker
     }
     reinterpret_cast<uint4*>(dst)[v] = o1;
     reinterpret_cast<uint4*>(dst + HALF)[v] = o2;
+    if (part > 0) {
+      // the same k / v rows into the other GPUs' buffers (NVLink stores through their mappings)
+      for (int i = 0; i < p.n_peers; ++i) {
+        uint8_t* pd = reinterpret_cast<uint8_t*>(dst) + p.peer_off[i];
+        reinterpret_cast<uint4*>(pd)[v] = o1;
+        reinterpret_cast<uint4*>(pd + HALF * 2)[v] = o2;
+      }
+    }
   }
+  if (part > 0 && p.n_peers > 0) __threadfence_system();   // peer stores visible before any later signal
 }
 
 // ops.headNorm: in place on X[(row_off + l) * ld + col_off + h * D + i]; one warp per (row, head).
@@ -340,9 +353,12 @@ cudaError_t launch_vec(const PrologueParams& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-// threads per head of a row at head dim 96
+// threads per head of a row at head dims 96 and 256
 #ifndef NSA_PROLOGUE_P96
 #define NSA_PROLOGUE_P96 2
+#endif
+#ifndef NSA_PROLOGUE_P256
+#define NSA_PROLOGUE_P256 4
 #endif
 
 template <typename T>
@@ -351,7 +367,7 @@ cudaError_t launch_vec_t(const PrologueParams& p, cudaStream_t stream) {
     case 64: return launch_vec<64, 2, T>(p, stream);
     case 96: return launch_vec<96, NSA_PROLOGUE_P96, T>(p, stream);
     case 128: return launch_vec<128, 2, T>(p, stream);
-    case 256: return launch_vec<256, 4, T>(p, stream);
+    case 256: return launch_vec<256, NSA_PROLOGUE_P256, T>(p, stream);
     default: return cudaErrorNotSupported;
   }
 }
@@ -362,7 +378,9 @@ cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream) {
   const int rows = (!p.skip_q && p.rows[0] > p.rows[1]) ? p.rows[0] : (p.rows[1] > p.rows[2] ? p.rows[1] : p.rows[2]);
   if (rows <= 0 || p.B <= 0) return cudaSuccess;
   const int elem = p.src_f32 ? 4 : 2;
-  if ((p.D == 64 || p.D == 96 || p.D == 128 || p.D == 256) && vec_ok(p, elem))
+  // Rows that also go to other GPUs take the row-per-block kernel: its consecutive threads write
+  // each row's head segments contiguously, which NVLink stores need to run at speed.
+  if (p.n_peers == 0 && (p.D == 64 || p.D == 96 || p.D == 128 || p.D == 256) && vec_ok(p, elem))
     return p.src_f32 ? launch_vec_t<float>(p, stream) : launch_vec_t<__nv_bfloat16>(p, stream);
   dim3 grid(rows, p.B, p.skip_q ? 2 : 3);
   prologue_kernel<<<grid, kPrologueThreads, 0, stream>>>(p);

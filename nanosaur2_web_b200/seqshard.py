@@ -2,13 +2,21 @@
 
 The reference runs the DiT block's attention (app/models/nanosaur2.js:196-208) on one device.  Here
 rank r of n owns image rows [q_begin, q_begin + q_count) of every batch element: it normalises and
-rotates its own q/k rows, every rank computes the text k/v rows itself, and one in-place NCCL
-all-gather per batch element assembles the full image k'|v' rows in each GPU's HBM before the
-attention of the local queries runs.  The gather of element b overlaps the attention of element
-b - 1 (the gathers run on their own stream, each attention waits only for its own element).
+rotates its own q/k rows, and every rank computes the text k/v rows itself.  The full image k'|v'
+rows are then assembled in each GPU's HBM before the attention of the local queries runs, in one
+of three ways (``mode``):
 
-Per element and rank the C library is called twice (include/nsattn.h):
-``nsa_seq_shard_prologue`` -> all_gather_into_tensor(kv_packed[b, :L]) -> ``nsa_seq_shard_attention``.
+* ``ce`` (default): the rank's rows of an element go to every peer's buffer with one copy-engine
+  ``cudaMemcpyAsync`` per peer through a CUDA IPC mapping.  No SM time is taken from the
+  attention kernel that runs at the same time.
+* ``nccl``: one in-place NCCL all-gather per element.
+* ``p2p``: the prologue itself stores the rows into the peers' buffers over NVLink.
+
+In every mode the exchange of element b overlaps the attention of element b - 1: it runs on its
+own stream, and each attention waits only for its own element.  ce and p2p end each element with
+a one-element all-reduce as the barrier.  Per element and rank the C library is called twice
+(include/nsattn.h): ``nsa_seq_shard_prologue[_peers]``, then the exchange, then
+``nsa_seq_shard_attention``.
 """
 
 from __future__ import annotations
@@ -47,7 +55,8 @@ def gather_views(kv_packed: torch.Tensor, b: int, L: int, q_begin: int, q_count:
 @dataclass
 class GatherTiming:
     """Device times of the last call, in ms: the whole call on the compute stream, and the
-    all-gathers on the communication stream (summed over batch elements)."""
+    exchange on the second stream summed over batch elements (nccl: the all-gathers; p2p: each
+    element's peer-storing prologue and its barrier)."""
     call_ms: float
     gather_ms: float
 
@@ -64,7 +73,7 @@ class SeqShardedJointAttention:
 
     def __init__(self, *, B: int, L: int, text_rows: int, world: int, rank: int, device: torch.device,
                  group=None, local_qkv: bool = True, eps: float = 1e-6, out_dtype: torch.dtype = torch.bfloat16,
-                 kv_packed: Optional[torch.Tensor] = None):
+                 kv_packed: Optional[torch.Tensor] = None, mode: str = "ce"):
         self.B, self.L, self.text_rows, self.world, self.rank = B, L, text_rows, world, rank
         self.device = torch.device(device)
         self.group = group
@@ -89,12 +98,47 @@ class SeqShardedJointAttention:
         elif tuple(kv_packed.shape) != shape or kv_packed.dtype != torch.bfloat16 or not kv_packed.is_contiguous():
             raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, f"kv_packed must be a contiguous bf16 {shape} tensor")
         self.kv_packed = kv_packed
+        if mode not in ("nccl", "p2p", "ce"):
+            raise ValueError("mode is 'nccl' (all-gather), 'p2p' (the prologue stores into the peers) or "
+                             "'ce' (copy-engine pushes into the peers)")
+        self.mode = mode if world > 1 else "nccl"
+        self._peers: List[int] = []   # other ranks' kv_packed, mapped into this process
+        if self.mode in ("p2p", "ce"):
+            self._map_peers()
         self.comm_stream = torch.cuda.Stream(self.device)
         self._prologue_done = [torch.cuda.Event() for _ in range(B)]
         self._gathered = [torch.cuda.Event(enable_timing=True) for _ in range(B)]
         self._gather_start = [torch.cuda.Event(enable_timing=True) for _ in range(B)]
+        self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)   # one-element barrier
         self._call_start = torch.cuda.Event(enable_timing=True)
         self._call_end = torch.cuda.Event(enable_timing=True)
+
+    def _map_peers(self) -> None:
+        """Exchange CUDA IPC handles of kv_packed over the process group and map the other ranks'
+        buffers into this process (their k'|v' rows are then written with NVLink stores)."""
+        import torch.distributed as dist
+
+        L_ = lib()
+        h = ctypes.create_string_buffer(_lib.NSA_IPC_HANDLE_BYTES)
+        with torch.cuda.device(self.device):
+            check(L_.nsa_ipc_export(self.kv_packed.data_ptr(), h))
+            handles: List[Optional[bytes]] = [None] * self.world
+            dist.all_gather_object(handles, h.raw, group=self.group)
+            for r, hb in enumerate(handles):
+                if r == self.rank:
+                    continue
+                ptr = ctypes.c_void_p()
+                check(L_.nsa_ipc_import(ctypes.create_string_buffer(hb, len(hb)), ctypes.byref(ptr)))
+                self._peers.append(ptr.value)
+
+    def close(self) -> None:
+        """Unmap the peer buffers (p2p mode); call before the process group is destroyed."""
+        L_ = lib()
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            for ptr in self._peers:
+                check(L_.nsa_ipc_close(ctypes.c_void_p(ptr)))
+        self._peers = []
 
     def _desc(self, b: int, count: int, qkv: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
               cs: Optional[RopeTable] = None, bias: Optional[torch.Tensor] = None) -> FusedDesc:
@@ -136,10 +180,13 @@ class SeqShardedJointAttention:
         """Step 1 for element b on the current stream: q' of the rank's rows, k'|v' of its image rows
         and of all text rows into kv_packed[b]."""
         d = self._desc(b, 1, qkv, None, cs, None)
-        check(lib().nsa_seq_shard_prologue(
+        elem = self.kv_rows * self.kv_ld * 2
+        mine = self._peers if self.mode == "p2p" else []
+        peers = (ctypes.c_void_p * max(1, len(mine)))(*[ptr + b * elem for ptr in mine])
+        check(lib().nsa_seq_shard_prologue_peers(
             ctypes.byref(d), ctypes.byref(self.shard), qkv.data_ptr(), q_norm.data_ptr(), k_norm.data_ptr(),
             cs.buf.data_ptr() if cs is not None else None, kv_len.data_ptr(), self.q_prime[b].data_ptr(),
-            self.kv_packed[b].data_ptr(), torch.cuda.current_stream(self.device).cuda_stream))
+            self.kv_packed[b].data_ptr(), peers, len(mine), torch.cuda.current_stream(self.device).cuda_stream))
 
     def gather(self, b: int) -> None:
         """Step 2 for element b on the current stream: the in-place all-gather of the image rows."""
@@ -168,20 +215,54 @@ class SeqShardedJointAttention:
                               device=self.device)
         compute = torch.cuda.current_stream(self.device)
         self._call_start.record(compute)
-        for b in range(self.B):
-            self.prologue(b, qkv, q_norm=q_norm, k_norm=k_norm, cs=cs, kv_len=kv_len)
-            self._prologue_done[b].record(compute)
-        for b in range(self.B):
-            self.comm_stream.wait_event(self._prologue_done[b])
-            with torch.cuda.stream(self.comm_stream):
-                self._gather_start[b].record(self.comm_stream)
-                self.gather(b)
-                self._gathered[b].record(self.comm_stream)
+        if self.mode in ("p2p", "ce"):
+            self._call_p2p(qkv, q_norm, k_norm, cs, kv_len, bias, out, compute)
+        else:
+            for b in range(self.B):
+                self.prologue(b, qkv, q_norm=q_norm, k_norm=k_norm, cs=cs, kv_len=kv_len)
+                self._prologue_done[b].record(compute)
+            for b in range(self.B):
+                self.comm_stream.wait_event(self._prologue_done[b])
+                with torch.cuda.stream(self.comm_stream):
+                    self._gather_start[b].record(self.comm_stream)
+                    self.gather(b)
+                    self._gathered[b].record(self.comm_stream)
+            for b in range(self.B):
+                compute.wait_event(self._gathered[b])
+                self.attention(b, kv_len=kv_len, bias=bias, out=out)
+        self._call_end.record(compute)
+        return out
+
+    def _call_p2p(self, qkv, q_norm, k_norm, cs, kv_len, bias, out, compute) -> None:
+        """p2p / ce modes: on the second stream, a barrier (every rank's previous attention is done,
+        so its kv_packed may be overwritten), then per element the prologue that also stores the
+        rank's k'|v' rows into every peer's kv_packed (p2p), or the local prologue followed by one
+        copy-engine push of those rows per peer (ce), and a barrier (every rank's rows are in);
+        each attention waits for its element's barrier, so element b's prologue overlaps element
+        b - 1's attention."""
+        import torch.distributed as dist
+
+        s2 = self.comm_stream
+        s2.wait_stream(compute)
+        with torch.cuda.stream(s2):
+            dist.all_reduce(self._flag, group=self.group)
+            elem = self.kv_rows * self.kv_ld * 2
+            row = self.kv_ld * 2
+            for b in range(self.B):
+                self._gather_start[b].record(s2)
+                self.prologue(b, qkv, q_norm=q_norm, k_norm=k_norm, cs=cs, kv_len=kv_len)
+                if self.mode == "ce":
+                    # the rank's rows of element b, one copy-engine push per peer
+                    off = b * elem + self.q_begin * row
+                    src = self.kv_packed.data_ptr() + off
+                    for ptr in self._peers:
+                        check(lib().nsa_memcpy_async(ctypes.c_void_p(ptr + off), ctypes.c_void_p(src),
+                                                     self.q_count * row, s2.cuda_stream))
+                dist.all_reduce(self._flag, group=self.group)
+                self._gathered[b].record(s2)
         for b in range(self.B):
             compute.wait_event(self._gathered[b])
             self.attention(b, kv_len=kv_len, bias=bias, out=out)
-        self._call_end.record(compute)
-        return out
 
     def timing(self) -> GatherTiming:
         """Device times of the last call (synchronises on it)."""

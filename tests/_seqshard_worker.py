@@ -22,6 +22,7 @@ import torch.distributed as dist  # noqa: E402
 
 def main():
     out_path = sys.argv[1]
+    mode = sys.argv[2] if len(sys.argv) > 2 else "nccl"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dev = torch.device("cuda", int(os.environ["LOCAL_RANK"]))
     torch.cuda.set_device(dev)
@@ -41,7 +42,7 @@ def main():
         kv_len = torch.from_numpy((L + lv).astype(np.int32)).to(dev)
         kb = torch.from_numpy(bias).to(dev)
         cs = rope2dTable(h, w, 96, dev)
-        m = SeqShardedJointAttention(B=B, L=L, text_rows=Lt, world=world, rank=rank, device=dev)
+        m = SeqShardedJointAttention(B=B, L=L, text_rows=Lt, world=world, rank=rank, device=dev, mode=mode)
         src = local_rows(x, L, m.q_begin, m.q_count)
         for _ in range(3):   # reuses the gather buffers across calls
             out = m(src, q_norm=qn, k_norm=kn, cs=cs, kv_len=kv_len, bias=kb)
@@ -62,13 +63,14 @@ def main():
             got = full.float().cpu().numpy()[..., cols]
             # equal to the size of P's bf16 rounding: a split tail rounds each half against its own max
             diff = float((full.float() - ref.float()).abs().max())
-            res = {"world": world, "equal_to_fused": diff <= 2e-3, "max_abs_vs_fused": diff,
+            res = {"world": world, "mode": m.mode, "equal_to_fused": diff <= 2e-3, "max_abs_vs_fused": diff,
                    "max_abs_vs_oracle": float(np.abs(got - want[..., cols]).max()),
                    "min_cos_vs_oracle": float(per_head_cosine(got, want[..., cols], 96).min()),
                    "call_ms": timing.call_ms, "gather_ms": timing.gather_ms}
             with open(out_path, "w") as f:
                 json.dump(res, f)
         dist.barrier()
+        m.close()
     finally:
         dist.destroy_process_group()
 
