@@ -51,8 +51,9 @@ def _seq_sharded(x, h, w, Lt, world, local_qkv, out_dtype=torch.float32):
     cs = rope2dTable(h, w, 96, DEV)
     ranks, shared = [], None
     for r in range(world):
+        # mode "nccl" maps no peer buffers: the emulated ranks share one kv_packed instead
         m = SeqShardedJointAttention(B=B, L=L, text_rows=Lt, world=world, rank=r, device=DEV, local_qkv=local_qkv,
-                                     kv_packed=shared, out_dtype=out_dtype)
+                                     kv_packed=shared, out_dtype=out_dtype, mode="nccl")
         shared = m.kv_packed
         ranks.append(m)
     shared.fill_(float("nan"))   # a key row no prologue writes would poison every query
