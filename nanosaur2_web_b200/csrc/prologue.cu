@@ -358,7 +358,7 @@ cudaError_t launch_vec(const PrologueParams& p, cudaStream_t stream) {
 #define NSA_PROLOGUE_P96 2
 #endif
 #ifndef NSA_PROLOGUE_P256
-#define NSA_PROLOGUE_P256 4
+#define NSA_PROLOGUE_P256 8
 #endif
 
 template <typename T>
