@@ -830,6 +830,12 @@ cudaError_t launch_d(const AttnParams& p, const CUtensorMap& tmQ, const CUtensor
 
 }  // namespace
 
+// Head dim 256 runs the persistent kernel of attention_persist.cu unless built with
+// NSA_PERSIST_256=0.
+#ifndef NSA_PERSIST_256
+#define NSA_PERSIST_256 1
+#endif
+
 AttnGeometry attention_geometry(int D) {
   switch (D) {
     case 64: return {Cfg<64>::NQ, Cfg<64>::BN, Cfg<64>::BLK, Cfg<64>::QTMEM};
@@ -846,7 +852,8 @@ cudaError_t launch_attention(const AttnParams& p, int D, const CUtensorMap& tmQ,
     case 64: return launch_d<64>(p, tmQ, tmK, tmV, tmVd, stream);
     case 96: return launch_d<96>(p, tmQ, tmK, tmV, tmVd, stream);
     case 128: return launch_d<128>(p, tmQ, tmK, tmV, tmVd, stream);
-    case 256: return launch_d<256>(p, tmQ, tmK, tmV, tmVd, stream);
+    case 256: return NSA_PERSIST_256 ? launch_attention_persist(p, tmQ, tmK, tmV, tmVd, stream)
+                                     : launch_d<256>(p, tmQ, tmK, tmV, tmVd, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -125,6 +125,9 @@ struct AttnGeometry {
   bool qtmem;   // Q prepared by the kernel itself into tensor memory
 };
 AttnGeometry attention_geometry(int D);   // NQ = 0: unsupported head dim
+// persistent head-dim-256 kernel (attention_persist.cu): one CTA per SM looping over work units
+cudaError_t launch_attention_persist(const AttnParams& p, const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                                     const CUtensorMap& tmV, const CUtensorMap& tmVd, cudaStream_t stream);
 
 cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream);
 

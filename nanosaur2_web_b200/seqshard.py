@@ -110,6 +110,9 @@ class SeqShardedJointAttention:
         self._gathered = [torch.cuda.Event(enable_timing=True) for _ in range(B)]
         self._gather_start = [torch.cuda.Event(enable_timing=True) for _ in range(B)]
         self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)   # one-element barrier
+        self._peer_streams = [torch.cuda.Stream(self.device) for _ in self._peers]
+        self._pro_done = torch.cuda.Event()
+        self._push_done = [torch.cuda.Event() for _ in self._peers]
         self._call_start = torch.cuda.Event(enable_timing=True)
         self._call_end = torch.cuda.Event(enable_timing=True)
 
@@ -252,12 +255,18 @@ class SeqShardedJointAttention:
                 self._gather_start[b].record(s2)
                 self.prologue(b, qkv, q_norm=q_norm, k_norm=k_norm, cs=cs, kv_len=kv_len)
                 if self.mode == "ce":
-                    # the rank's rows of element b, one copy-engine push per peer
+                    # the rank's rows of element b, one copy-engine push per peer, each on its own
+                    # stream so that several copy engines run at once
                     off = b * elem + self.q_begin * row
                     src = self.kv_packed.data_ptr() + off
-                    for ptr in self._peers:
+                    self._pro_done.record(s2)
+                    for i, ptr in enumerate(self._peers):
+                        ps = self._peer_streams[i]
+                        ps.wait_event(self._pro_done)
                         check(lib().nsa_memcpy_async(ctypes.c_void_p(ptr + off), ctypes.c_void_p(src),
-                                                     self.q_count * row, s2.cuda_stream))
+                                                     self.q_count * row, ps.cuda_stream))
+                        self._push_done[i].record(ps)
+                        s2.wait_event(self._push_done[i])
                 dist.all_reduce(self._flag, group=self.group)
                 self._gathered[b].record(s2)
         for b in range(self.B):
