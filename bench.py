@@ -679,7 +679,7 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="profiling driver: warm-up + timed device-resident steps only (no e2e, CPU or clocks)")
     ap.add_argument("--batch", type=int, default=B_PER_GPU, help="batch per GPU (profiling runs only)")
-    ap.add_argument("--seq-mode", choices=["nccl", "p2p", "ce"], default="ce",
+    ap.add_argument("--seq-mode", choices=["auto", "nccl", "p2p", "ce"], default="auto",
                     help="config 5: k'|v' exchange by NCCL all-gather, peer stores from the prologue, or "
                          "copy-engine pushes")
     ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2,

@@ -6,11 +6,12 @@ rotates its own q/k rows, and every rank computes the text k/v rows itself.  The
 rows are then assembled in each GPU's HBM before the attention of the local queries runs, in one
 of three ways (``mode``):
 
-* ``ce`` (default): the rank's rows of an element go to every peer's buffer with one copy-engine
+* ``ce``: the rank's rows of an element go to every peer's buffer with one copy-engine
   ``cudaMemcpyAsync`` per peer through a CUDA IPC mapping.  No SM time is taken from the
   attention kernel that runs at the same time.
 * ``nccl``: one in-place NCCL all-gather per element.
 * ``p2p``: the prologue itself stores the rows into the peers' buffers over NVLink.
+* ``auto`` (default): ``ce`` on 2 GPUs, ``nccl`` on more (the faster of the two as measured).
 
 In every mode the exchange of element b overlaps the attention of element b - 1: it runs on its
 own stream, and each attention waits only for its own element.  ce and p2p end each element with
@@ -73,7 +74,7 @@ class SeqShardedJointAttention:
 
     def __init__(self, *, B: int, L: int, text_rows: int, world: int, rank: int, device: torch.device,
                  group=None, local_qkv: bool = True, eps: float = 1e-6, out_dtype: torch.dtype = torch.bfloat16,
-                 kv_packed: Optional[torch.Tensor] = None, mode: str = "ce"):
+                 kv_packed: Optional[torch.Tensor] = None, mode: str = "auto"):
         self.B, self.L, self.text_rows, self.world, self.rank = B, L, text_rows, world, rank
         self.device = torch.device(device)
         self.group = group
@@ -98,9 +99,13 @@ class SeqShardedJointAttention:
         elif tuple(kv_packed.shape) != shape or kv_packed.dtype != torch.bfloat16 or not kv_packed.is_contiguous():
             raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, f"kv_packed must be a contiguous bf16 {shape} tensor")
         self.kv_packed = kv_packed
-        if mode not in ("nccl", "p2p", "ce"):
-            raise ValueError("mode is 'nccl' (all-gather), 'p2p' (the prologue stores into the peers) or "
+        if mode not in ("auto", "nccl", "p2p", "ce"):
+            raise ValueError("mode is 'auto', 'nccl' (all-gather), 'p2p' (the prologue stores into the peers) or "
                              "'ce' (copy-engine pushes into the peers)")
+        if mode == "auto":
+            # measured on B200s: the copy engines win at 2 GPUs (they leave every SM to the
+            # attention); from 4 GPUs the NCCL all-gather moves the rows faster
+            mode = "ce" if world == 2 else "nccl"
         self.mode = mode if world > 1 else "nccl"
         self._peers: List[int] = []   # other ranks' kv_packed, mapped into this process
         if self.mode in ("p2p", "ce"):
