@@ -338,21 +338,8 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
   const SplitScratch split = split_scratch(base + pl.q_bytes + pl.k_bytes + pl.v_bytes, pl.split_cap, pl.NQ, pl.D);
   pp.zero_ptr = pl.split_cap > 0 ? split.count : nullptr;   // the attention's split counters start at zero
   pp.zero_count = pl.split_cap;
-  // Kernels that keep Q in tensor memory TMA-load the raw bf16 query rows straight from the input
-  // when the layout allows a tiled map over it (16-byte aligned rows and head offsets, whole rows
-  // per batch element); they then apply the q norm and RoPE themselves.  Otherwise (fp32 input, odd
-  // layouts) the prologue writes normalised Q tiles and the kernel loads those.
-  // Off by default: when every CTA starts at once, pulling the raw rows and their fp32 RoPE table
-  // rows from HBM costs more than having the prologue write normalised Q tiles that stay in L2.
-#ifndef NSA_Q_FROM_INPUT
-#define NSA_Q_FROM_INPUT 0
-#endif
   auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
-  const bool q_direct = NSA_Q_FROM_INPUT && pl.qtmem && a.in_dtype == NSA_BF16 && al16(pp.q.ptr) && pp.q.ld % 8 == 0 &&
-                        pp.q.off % 8 == 0 && (pl.B == 1 || (pp.q.bstride > 0 && pp.q.bstride % pp.q.ld == 0)) &&
-                        pp.q.off + (int64_t)pl.Hq * pl.D <= pp.q.ld && (!pp.q_w || al16(pp.q_w)) &&
-                        (!pp.cs || (al16(pp.cs) && (pp.sin_off * 4) % 16 == 0));
-  pp.skip_q = q_direct ? 1 : 0;
+  pp.skip_q = 0;
   // V needs no normalisation: for bf16 rows that a tiled map can cover (16-byte aligned rows and
   // head offsets, whole rows per batch element) the attention kernel reads V tiles of valid keys
   // straight from the input, and the prologue writes only the last partial tile and the padding.
@@ -365,21 +352,13 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
   const double in_elem = a.in_dtype == NSA_F32 ? 4.0 : 2.0;
   // algorithmic bytes: q and k rows, and the v rows the prologue writes (all, or about one tile)
   const double v_rows = v_direct ? (double)pl.BN : (double)pl.Lk;
-  const double pro_bytes = (double)pl.Bs * ((q_direct ? 0.0 : (double)pl.Lq * pl.Hqs) + (pl.Lk + v_rows) * pl.Hkvs) *
-                           pl.D * (in_elem + 2.0);
+  const double pro_bytes = (double)pl.Bs * ((double)pl.Lq * pl.Hqs + (pl.Lk + v_rows) * pl.Hkvs) * pl.D *
+                           (in_elem + 2.0);
   cudaError_t e = profiled("prologue", 0.0, pro_bytes, stream, [&] { return nsa::launch_prologue(pp, stream); });
   if (e != cudaSuccess) return cuda_fail(e, "prologue launch");
 
   CUtensorMap tq, tk, tv;
-  bool maps_ok;
-  if (q_direct) {
-    // raw rows: [B * rows per element][ld]; rows past an element's Lq are ignored by the kernel
-    // the last batch element may end right after its own rows
-    const int64_t total_rows = pl.B == 1 ? pp.q.rows : (int64_t)(pl.B - 1) * (pp.q.bstride / pp.q.ld) + pp.q.rows;
-    maps_ok = encode_rows(&tq, pp.q.ptr, pp.q.ld, pp.q.ld, total_rows, pl.blk, nsa::kTileM);
-  } else {
-    maps_ok = encode_tiles(&tq, Qs, pl.D, (int64_t)pl.Bs * pl.Hqs * pl.Lq_pad, pl.blk, nsa::kTileM);
-  }
+  const bool maps_ok = encode_tiles(&tq, Qs, pl.D, (int64_t)pl.Bs * pl.Hqs * pl.Lq_pad, pl.blk, nsa::kTileM);
   if (!maps_ok || !encode_tiles(&tk, Ks, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk, pl.BN) ||
       !encode_tiles(&tv, Vs, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk, pl.BN))
     return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed (driver entry point unavailable?)");
@@ -403,32 +382,13 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
     ap.vd_xh = pl.D;
     ap.vd_yb = pl.B == 1 ? 0 : (int)(pp.v.bstride / pp.v.ld);
   }
-  if (q_direct) {
-    ap.q_x0 = (int)pp.q.off;
-    ap.q_xh = pl.D;
-    ap.q_yb = pl.B == 1 ? 0 : (int)(pp.q.bstride / pp.q.ld);
-    ap.q_yh = 0;
-    ap.q_b0 = 0;
-    ap.q_h0 = 0;
-    ap.q_w = pp.q_w;
-    ap.q_eps = pp.eps;
-    ap.q_cs = pp.cs;
-    ap.q_sin_off = pp.sin_off;
-    ap.q_rope_rows = pp.rope_rows;
-  } else {
-    // the prologue's head-major Q tiles, already normalised and rotated
-    ap.q_x0 = 0;
-    ap.q_xh = 0;
-    ap.q_yb = pl.Hqs * pl.Lq_pad;
-    ap.q_yh = pl.Lq_pad;
-    ap.q_b0 = pl.b0;
-    ap.q_h0 = pl.hq0;
-    ap.q_w = nullptr;
-    ap.q_eps = 0.f;
-    ap.q_cs = nullptr;
-    ap.q_sin_off = 0;
-    ap.q_rope_rows = 0;
-  }
+  // the prologue's head-major Q tiles, already normalised and rotated
+  ap.q_x0 = 0;
+  ap.q_xh = 0;
+  ap.q_yb = pl.Hqs * pl.Lq_pad;
+  ap.q_yh = pl.Lq_pad;
+  ap.q_b0 = pl.b0;
+  ap.q_h0 = pl.hq0;
   const double flops = attn_flops(pl, a);
   e = profiled("attention", flops, 0.0, stream,
                [&] { return nsa::launch_attention(ap, pl.D, tq, tk, tv, tvd, stream); });

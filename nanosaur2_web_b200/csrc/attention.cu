@@ -61,7 +61,7 @@ struct Cfg {
   static constexpr int REG_LAUNCH = 168, REG_CTRL = 104, REG_SOFTMAX = 200;
   static_assert(NQ != 2 || 128 * REG_CTRL + 256 * REG_SOFTMAX == THREADS * REG_LAUNCH, "register split");
   static constexpr int SMEM_TILES = NQ * Q_TILE_BYTES + 2 * NS * KV_TILE_BYTES;
-  static constexpr int SMEM_KB = kKeyBiasMax * 4 + D * 4;   // key bias/mask table, q norm weights
+  static constexpr int SMEM_KB = kKeyBiasMax * 4;   // key bias/mask table
   // at least 117 KB so that two CTAs never share an SM (each allocates all 512 TMEM columns)
   static constexpr int SMEM_NEED = SMEM_TILES + SMEM_KB + 1024 + 256;
   static constexpr int SMEM_BYTES = SMEM_NEED > 117 * 1024 ? SMEM_NEED : 117 * 1024;
@@ -116,37 +116,12 @@ __device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, 
   }
 }
 
-// The RoPE table row of a query row (cos then sin, D/2 each), loaded early so its latency overlaps
-// the TMA load of the query tile.
+// Row r of a staged Q tile (already normalised and rotated by the prologue) as D/2 bf16 pairs, in
+// column order, read from the swizzled shared-memory tile.
 template <int D>
-struct RopeRow {
-  float4 c[D / 8], s[D / 8];
-};
-
-template <int D>
-__device__ __forceinline__ void load_rope_row(const AttnParams& p, int row, bool rope, RopeRow<D>& rr) {
-  constexpr int HALF = D / 2;
-  if (rope) {
-    const float4* c4 = reinterpret_cast<const float4*>(p.q_cs + (int64_t)row * HALF);
-    const float4* s4 = reinterpret_cast<const float4*>(p.q_cs + p.q_sin_off + (int64_t)row * HALF);
-#pragma unroll
-    for (int v = 0; v < HALF / 4; ++v) {
-      rr.c[v] = __ldg(c4 + v);
-      rr.s[v] = __ldg(s4 + v);
-    }
-  }
-}
-
-// The prologue of one query row, done by the thread that owns it (row r of the staged tile):
-// read D bf16 values from the swizzled shared-memory tile, RMSNorm with the staged weights w_s
-// (or none), split-half RoPE with the table row, pack to bf16 pairs.  Rows past Lq become zeros.
-template <int D>
-__device__ __forceinline__ void q_row_from_smem(const uint8_t* tile, int r, bool valid, const float* w_s, float eps,
-                                                bool rope, const RopeRow<D>& rr, uint32_t (&qp)[D / 2]) {
+__device__ __forceinline__ void q_row_from_smem(const uint8_t* tile, int r, uint32_t (&qp)[D / 2]) {
   using C = Cfg<D>;
-  constexpr int HALF = D / 2;
   constexpr int CHUNKS = C::ROWB / 16;   // 16-byte chunks per row of a swizzle block
-  float x[D];
 #pragma unroll
   for (int blk = 0; blk < C::NB; ++blk) {
 #pragma unroll
@@ -154,38 +129,13 @@ __device__ __forceinline__ void q_row_from_smem(const uint8_t* tile, int r, bool
       // the TMA swizzle XORs the 16-byte chunk index with the row bits above the chunk span
       const int phys = c ^ ((r / (128 / C::ROWB)) % CHUNKS);
       const uint4 a = *reinterpret_cast<const uint4*>(tile + blk * C::QBLK_BYTES + r * C::ROWB + phys * 16);
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&a);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(h2[e]);
-        x[blk * C::BLK + c * 8 + 2 * e] = valid ? f.x : 0.f;
-        x[blk * C::BLK + c * 8 + 2 * e + 1] = valid ? f.y : 0.f;
-      }
+      const int w0 = (blk * C::BLK + c * 8) / 2;
+      qp[w0] = a.x;
+      qp[w0 + 1] = a.y;
+      qp[w0 + 2] = a.z;
+      qp[w0 + 3] = a.w;
     }
   }
-  if (w_s) {
-    float ss[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int i = 0; i < D; ++i) ss[i & 3] = fmaf(x[i], x[i], ss[i & 3]);
-    const float rn = rsqrtf(((ss[0] + ss[1]) + (ss[2] + ss[3])) / (float)D + eps);
-#pragma unroll
-    for (int i = 0; i < D; ++i) x[i] *= rn * w_s[i];
-  }
-  if (rope) {
-#pragma unroll
-    for (int v = 0; v < HALF / 4; ++v) {
-      const float cc[4] = {rr.c[v].x, rr.c[v].y, rr.c[v].z, rr.c[v].w};
-      const float sn[4] = {rr.s[v].x, rr.s[v].y, rr.s[v].z, rr.s[v].w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float a = x[4 * v + e], bb = x[HALF + 4 * v + e];
-        x[4 * v + e] = a * cc[e] - bb * sn[e];
-        x[HALF + 4 * v + e] = bb * cc[e] + a * sn[e];
-      }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < HALF; ++i) qp[i] = pack_bf16x2(x[2 * i], x[2 * i + 1]);
 }
 
 template <int N>
@@ -216,8 +166,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   uint8_t* sK = sQ + NQ * C::Q_TILE_BYTES;
   uint8_t* sV = sK + NS * C::KV_TILE_BYTES;
   float* kb = reinterpret_cast<float*>(sV + NS * C::KV_TILE_BYTES);   // [kKeyBiasMax]
-  float* qw_s = kb + kKeyBiasMax;                                      // [D] q norm weights
-  uint64_t* bars = reinterpret_cast<uint64_t*>(qw_s + D);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(kb + kKeyBiasMax);
   uint64_t* q_full = bars;           // [2]   Q ready for the MMA (QTMEM: rows stored in TMEM)
   uint64_t* q_smem = bars + 2;       //       Q tile(s) landed in shared memory (QTMEM)
   uint64_t* k_full = bars + 3;
@@ -488,9 +437,6 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     const float sl2 = p.scale_log2;
     const float* bias_b = p.bias ? p.bias + (int64_t)b * p.bias_bstride : nullptr;
-    RopeRow<D> rr;
-    const bool q_rope = C::QTMEM && p.q_cs != nullptr && row < p.Lq && row < p.q_rope_rows;
-    if constexpr (C::QTMEM) load_rope_row<D>(p, row, q_rope, rr);
     // Key bias + padding mask of the tiles that need one, in log2 units, for keys [kb0, kb0 +
     // kKeyBiasMax): 0 for plain keys, log(w)*log2(e) for biased text keys, -inf past kv_valid.
     // Built once per CTA by the softmax threads (named barrier 1 over them).
@@ -506,19 +452,15 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         kb[i] = key < kv_valid ? v : -INFINITY;
       }
     }
-    if (C::QTMEM && p.q_w) {
-      for (int i = threadIdx.x - 128; i < D; i += NQ * 128) qw_s[i] = p.q_w[i];
-    }
     asm volatile("bar.sync 1, %0;" ::"n"(NQ * 128) : "memory");
     bool ok = true;
     if constexpr (C::QTMEM) {
-      // this thread's query row, normalised and rotated, into the Q columns of its TMEM lane
+      // this thread's query row into the Q columns of its TMEM lane
       if (n > 0) {
         ok = __all_sync(0xffffffffu, wait_bounded(q_smem, 0, abort_flag, p.err, kErrTimeoutSoftmax, to));
         if (ok) {
           uint32_t qp[D / 2];
-          q_row_from_smem<D>(sQ + tile * C::Q_TILE_BYTES, quarter * 32 + lane, row < p.Lq, p.q_w ? qw_s : nullptr,
-                             p.q_eps, q_rope, rr, qp);
+          q_row_from_smem<D>(sQ + tile * C::Q_TILE_BYTES, quarter * 32 + lane, qp);
           tmem_st_n<D / 2>(lane_base + C::q_col(tile), qp);
           tc_fence_before();
           mbar_arrive(&q_full[tile]);

@@ -88,17 +88,10 @@ struct AttnParams {
   int q_blocks;            // query blocks (NQ tiles each) per (b, head)
   int* err;
   unsigned long long timeout_ns;
-  // Kernels that keep Q in tensor memory TMA-load the query tile from tmQ into shared memory:
-  // box (x, y) with x = q_x0 + (head - q_h0)*q_xh + c*blk and
-  // y = (b - q_b0)*q_yb + (head - q_h0)*q_yh + row; the softmax threads then apply RMSNorm with q_w
-  // (if set) and RoPE with q_cs for rows < q_rope_rows (if set) and store the row into TMEM.
+  // Query tile of the prologue's Q' tiles: box (x, y) with x = q_x0 + (head - q_h0)*q_xh + c*blk and
+  // y = (b - q_b0)*q_yb + (head - q_h0)*q_yh + row.
   int q_x0, q_xh, q_yb, q_yh;
   int q_b0, q_h0;
-  const float* q_w;
-  float q_eps;
-  const float* q_cs;
-  int64_t q_sin_off;
-  int q_rope_rows;
   // Tail split (two query tiles per CTA, no causal mask or window): the work units from
   // split_first on (the last, partial wave) run as two CTAs each, one per half of the key tiles.
   // Each writes its unnormalised O and (m, l) per row to part_o / part_ml; whichever finishes
@@ -122,7 +115,7 @@ struct AttnGeometry {
   int NQ;       // query tiles of 128 rows per CTA
   int BN;       // keys per K/V tile (TMA box rows)
   int blk;      // swizzle block width in elements (TMA box columns)
-  bool qtmem;   // Q prepared by the kernel itself into tensor memory
+  bool qtmem;   // Q copied into tensor memory by the softmax threads (S = Q K^T reads it from there)
 };
 AttnGeometry attention_geometry(int D);   // NQ = 0: unsupported head dim
 // persistent head-dim-256 kernel (attention_persist.cu): one CTA per SM looping over work units

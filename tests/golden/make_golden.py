@@ -197,9 +197,12 @@ def np32(t):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("NANOSAUR2_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("NANOSAUR2_REFERENCE"),
+                    help="checkout of the reference repository (or NANOSAUR2_REFERENCE)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("pass --reference <checkout of the reference> or set NANOSAUR2_REFERENCE")
     sys.path.insert(0, os.path.join(args.reference, "tools"))
     import reference as R  # noqa: E402  (the unmodified reference module)
     torch.set_num_threads(min(8, os.cpu_count() or 1))
