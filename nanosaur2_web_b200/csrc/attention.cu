@@ -15,9 +15,9 @@
 //                 quarter (warp id % 4), so lane l of warp w owns query row 32*(w%4) + l of its
 //                 tile: it reads its score row with tcgen05.ld, writes bf16 probabilities back
 //                 into the same TMEM columns, and finally normalises its output row.
-// Head dims 64 and 96 (QTMEM): the softmax threads also load their own raw query row, apply the
-// q RMSNorm + RoPE prologue, and store the bf16 row into tensor memory, so S = Q K^T reads only K
-// from shared memory.  Tensor memory (512 columns) for D = 96, BN = 112 keys per tile:
+// Head dims 64 and 96 (QTMEM): the producer loads the prologue's Q' tiles into shared memory once,
+// and each softmax thread copies its own bf16 query row into tensor memory, so S = Q K^T reads
+// only K from shared memory.  Tensor memory (512 columns) for D = 96, BN = 112 keys per tile:
 //   S0 [0,112) S1 [112,224) O0 [224,320) O1 [320,416) Q0 [416,464) Q1 [464,512)
 // D = 64: S 2 x 128, O 2 x 64, Q 2 x 32.  D = 128: Q in shared memory, S 2 x 128, O 2 x 128.
 // D = 256 (NQ = 1): Q in shared memory, S double-buffered [0,128) [128,256), O [256,512).
@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             tma_load_2d(sQ + i * C::Q_TILE_BYTES + c * C::QBLK_BYTES, &tmQ, &q_full[0], c * C::BLK,
                         q_tma_row + i * kTileM);
       } else {
-        // raw (or prologue-prepared) query rows of this block; the softmax threads take it from here
+        // the Q' rows of this block; the softmax threads copy them into tensor memory
         const int hq = p.hq_begin + hl;
         const int qx = p.q_x0 + (hq - p.q_h0) * p.q_xh;
         const int qy = (b - p.q_b0) * p.q_yb + (hq - p.q_h0) * p.q_yh + q_row0;

@@ -254,6 +254,151 @@ __global__ void __launch_bounds__(256, NSA_PROLOGUE_MIN_BLOCKS) prologue_vec_ker
   if (part > 0 && p.n_peers > 0) __threadfence_system();   // peer stores visible before any later signal
 }
 
+// Streaming form of the vector prologue (bf16 input, head dim 256): the thread mapping and the
+// arithmetic are the vector kernel's, but the blocks of one (part, batch element) stride over its
+// (row, head) items, NSA_PROLOGUE_ITEMS per thread, and each thread issues the loads of its next
+// item before it normalises, rotates and stores the current one, so its HBM reads stay in flight
+// while it computes.  V rows of key tiles the attention kernel reads straight from the input are
+// not visited.  At head dim 256 (P = 8, two items of 64 bytes in flight per thread at 127
+// registers, 16 warps per SM) it beats the one-item-per-thread kernel; at head dim 96 its 168
+// registers leave too few warps per SM and the vector kernel stays ahead.
+#ifndef NSA_PROLOGUE_ITEMS
+#define NSA_PROLOGUE_ITEMS 8   // (row, head) items per thread and part
+#endif
+constexpr int kStreamThreads = 128;   // 4 resident blocks per SM at <= 128 registers
+
+template <int D, int P>
+__global__ void __launch_bounds__(kStreamThreads, 4) prologue_stream_kernel(const PrologueParams p) {
+  using T = __nv_bfloat16;
+  constexpr int S = D / (2 * P);
+  constexpr int HALF = D / 2;
+  constexpr int NV = S / 8;   // 16-byte input vectors per half
+  static_assert(S % 8 == 0 && kStreamThreads % P == 0, "vector width");
+  if (blockIdx.x == 0 && blockIdx.y == 0)
+    for (int i = threadIdx.x; i < p.zero_count; i += blockDim.x) p.zero_ptr[i] = 0;
+  const int part = blockIdx.y / p.B + (p.skip_q ? 1 : 0);
+  const int bl = blockIdx.y % p.B;
+  const int b = p.b_begin + bl;
+  const int H = part == 0 ? p.Hq : p.Hkv;
+  const int pad = p.rows[part];
+  const RowView& view = part == 0 ? p.q : (part == 1 ? p.k : p.v);
+  const int h_begin = part == 0 ? p.hq_begin : p.hkv_begin;
+  const float* w = part == 0 ? p.q_w : (part == 1 ? p.k_w : nullptr);
+  const int valid_rows = part == 0 ? p.Lq : (p.kv_len ? min(p.kv_len[b], p.Lk) : p.Lk);
+  // first produced row: V rows of whole tiles of valid keys come from the input instead
+  const int r_begin = (part == 2 && p.v_tile > 0) ? max(0, valid_rows / p.v_tile * p.v_tile - p.row0[2]) : 0;
+  const long long count = (long long)max(pad - r_begin, 0) * H * P;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const int sub = (int)(threadIdx.x % P);   // blockIdx.x * blockDim.x and the stride are multiples of P
+  const T* src_b = reinterpret_cast<const T*>(view.ptr) + (int64_t)b * view.bstride + view.off + sub * S;
+  const TileOut& to = p.out[part];
+
+  // raw input of one item: NV vectors of each half (zeros past the last item or the valid rows)
+  auto load = [&](long long i, uint4 (&a)[NV], uint4 (&c)[NV]) {
+    const long long rest = i / P;
+    const int hh = (int)(rest % H);
+    const int r_out = r_begin + (int)(rest / H);
+    const bool valid = i < count && p.row0[part] + r_out < valid_rows;
+    const T* src = src_b + (int64_t)(p.src_row0[part] + r_out) * view.ld + (int64_t)(h_begin + hh) * D;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      a[v] = valid ? __ldg(reinterpret_cast<const uint4*>(src) + v) : make_uint4(0u, 0u, 0u, 0u);
+      c[v] = valid ? __ldg(reinterpret_cast<const uint4*>(src + HALF) + v) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+
+  long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long warp_first = idx - (threadIdx.x % 32);   // loop bound uniform over the warp (shuffles)
+  uint4 a[NV], c[NV];
+  load(idx, a, c);
+  for (long long wf = warp_first; wf < count; wf += stride, idx += stride) {
+    uint4 na[NV], nc[NV];
+    load(idx + stride, na, nc);
+    const bool in_range = idx < count;
+    const long long rest = idx / P;
+    const int hh = (int)(rest % H);
+    const int r_out = r_begin + (int)(rest / H);
+    const int row = p.row0[part] + r_out;   // key / query index and RoPE row
+    const bool valid = in_range && row < valid_rows;
+    const bool rope = part < 2 && p.cs != nullptr && row < p.rope_rows;
+    float x1[S], x2[S];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a[v]);
+      const __nv_bfloat162* pc = reinterpret_cast<const __nv_bfloat162*>(&c[v]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fa = __bfloat1622float2(pa[e]);
+        const float2 fc = __bfloat1622float2(pc[e]);
+        x1[v * 8 + 2 * e] = fa.x;
+        x1[v * 8 + 2 * e + 1] = fa.y;
+        x2[v * 8 + 2 * e] = fc.x;
+        x2[v * 8 + 2 * e + 1] = fc.y;
+      }
+    }
+    // w is uniform over the block (one part per blockIdx.y), so every lane reaches the shuffle.
+    float r = 1.f;
+    if (w) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < S; ++i) ss += x1[i] * x1[i] + x2[i] * x2[i];
+#pragma unroll
+      for (int o = 1; o < P; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      r = rsqrtf(ss / (float)D + p.eps);
+    }
+    if (in_range) {
+      if (valid) {
+        if (w) {
+          const float4* w1 = reinterpret_cast<const float4*>(w + sub * S);
+          const float4* w2 = reinterpret_cast<const float4*>(w + HALF + sub * S);
+#pragma unroll
+          for (int v = 0; v < S / 4; ++v) {
+            const float4 wa = __ldg(w1 + v), wc = __ldg(w2 + v);
+            x1[4 * v] *= r * wa.x; x1[4 * v + 1] *= r * wa.y; x1[4 * v + 2] *= r * wa.z; x1[4 * v + 3] *= r * wa.w;
+            x2[4 * v] *= r * wc.x; x2[4 * v + 1] *= r * wc.y; x2[4 * v + 2] *= r * wc.z; x2[4 * v + 3] *= r * wc.w;
+          }
+        }
+        if (rope) {
+          const float4* cp = reinterpret_cast<const float4*>(p.cs + (int64_t)row * HALF + sub * S);
+          const float4* sp = reinterpret_cast<const float4*>(p.cs + p.sin_off + (int64_t)row * HALF + sub * S);
+#pragma unroll
+          for (int v = 0; v < S / 4; ++v) {
+            const float4 c4 = __ldg(cp + v), s4 = __ldg(sp + v);
+            const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float xa = x1[4 * v + e], xc = x2[4 * v + e];
+              x1[4 * v + e] = xa * cc[e] - xc * sn[e];
+              x2[4 * v + e] = xc * cc[e] + xa * sn[e];
+            }
+          }
+        }
+      }
+      __nv_bfloat16* dst = to.ptr + (int64_t)bl * to.bs + (int64_t)hh * to.hs + (int64_t)r_out * to.rs + sub * S;
+#pragma unroll
+      for (int v = 0; v < S / 8; ++v) {
+        uint4 o1, o2;
+        uint32_t* u1 = reinterpret_cast<uint32_t*>(&o1);
+        uint32_t* u2 = reinterpret_cast<uint32_t*>(&o2);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          __nv_bfloat162 t1 = __floats2bfloat162_rn(x1[v * 8 + 2 * e], x1[v * 8 + 2 * e + 1]);
+          __nv_bfloat162 t2 = __floats2bfloat162_rn(x2[v * 8 + 2 * e], x2[v * 8 + 2 * e + 1]);
+          u1[e] = *reinterpret_cast<uint32_t*>(&t1);
+          u2[e] = *reinterpret_cast<uint32_t*>(&t2);
+        }
+        reinterpret_cast<uint4*>(dst)[v] = o1;
+        reinterpret_cast<uint4*>(dst + HALF)[v] = o2;
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      a[v] = na[v];
+      c[v] = nc[v];
+    }
+  }
+}
+
 // ops.headNorm: in place on X[(row_off + l) * ld + col_off + h * D + i]; one warp per (row, head).
 template <typename T>
 __global__ void head_norm_kernel(T* X, const float* w, int L, int H, int D, int64_t ld, int64_t col_off,
@@ -342,6 +487,17 @@ bool vec_ok(const PrologueParams& p, int elem) {
   return true;
 }
 
+template <int D, int P>
+cudaError_t launch_stream(const PrologueParams& p, cudaStream_t stream) {
+  const int rows = (!p.skip_q && p.rows[0] > p.rows[1]) ? p.rows[0] : (p.rows[1] > p.rows[2] ? p.rows[1] : p.rows[2]);
+  const int H = (!p.skip_q && p.Hq > p.Hkv) ? p.Hq : p.Hkv;
+  const long long threads = ((long long)rows * H * P + NSA_PROLOGUE_ITEMS - 1) / NSA_PROLOGUE_ITEMS;
+  const long long blocks = (threads + kStreamThreads - 1) / kStreamThreads;
+  if (blocks > 0x7FFFFFFFLL || 3LL * p.B > 65535) return cudaErrorInvalidValue;
+  prologue_stream_kernel<D, P><<<dim3((unsigned)blocks, (p.skip_q ? 2 : 3) * p.B), kStreamThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
 template <int D, int P, typename T>
 cudaError_t launch_vec(const PrologueParams& p, cudaStream_t stream) {
   const int rows = (!p.skip_q && p.rows[0] > p.rows[1]) ? p.rows[0] : (p.rows[1] > p.rows[2] ? p.rows[1] : p.rows[2]);
@@ -367,7 +523,9 @@ cudaError_t launch_vec_t(const PrologueParams& p, cudaStream_t stream) {
     case 64: return launch_vec<64, 2, T>(p, stream);
     case 96: return launch_vec<96, NSA_PROLOGUE_P96, T>(p, stream);
     case 128: return launch_vec<128, 2, T>(p, stream);
-    case 256: return launch_vec<256, NSA_PROLOGUE_P256, T>(p, stream);
+    case 256:
+      if constexpr (sizeof(T) == 2) return launch_stream<256, NSA_PROLOGUE_P256>(p, stream);
+      return launch_vec<256, NSA_PROLOGUE_P256, T>(p, stream);
     default: return cudaErrorNotSupported;
   }
 }
