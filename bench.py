@@ -641,6 +641,82 @@ def run_config5(args, rank, world, local_rank):
                            clocks.summary(), 3 * B * args.steps, "strong", **extra)), flush=True)
 
 
+def run_config6(args, rank, world, local_rank):
+    """Config 6 (the first "next" step of the path): one DiT block's attention step from the block input
+    with config 2's shapes: q|k|v = x W_qkv^T + b over the 3952 image rows and k|v = x_text W_kv^T + b
+    over the 256 text slots (K = 1536), q/k RMSNorm + 2D RoPE in the GEMM epilogue, then the joint
+    attention (blocks.dit_block_attention_projected).  Batch 2 per GPU (weak scaling, no collective).
+    The line also reports the same step unfused: cuBLAS bf16 linears (torch.matmul) writing qkv, then
+    the fused prologue + attention."""
+    import torch
+
+    from nanosaur2_web_b200.blocks import dit_block_attention, dit_block_attention_projected, projection_buffers
+    from nanosaur2_web_b200.ops import rope2dTable
+    from nanosaur2_web_b200.sharding import sum_over_ranks
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, L, K = B_PER_GPU, IMG_H * IMG_W, C
+    rng = np.random.default_rng(6000 + rank)
+    sets = []
+    for i in range(6):   # six 26 MB block inputs rotate (156 MB > 126 MB L2)
+        x = torch.from_numpy(rng.standard_normal((B, L, K), dtype=np.float32)).to(dev, torch.bfloat16)
+        xt = torch.from_numpy(rng.standard_normal((B, LT, K), dtype=np.float32)).to(dev, torch.bfloat16)
+        lv = rng.integers(32, LT + 1, size=B).astype(np.int32)
+        bias = torch.from_numpy(np.log(rng.choice(np.array([0.7, 1.0, 1.3], np.float32), size=(B, LT)))).to(dev)
+        sets.append((x, xt, torch.from_numpy(L + lv).to(dev), bias, lv))
+    w_qkv = (torch.randn((3 * C, K), device=dev) / math.sqrt(K)).to(torch.bfloat16)
+    b_qkv = 0.1 * torch.randn(3 * C, device=dev)
+    w_kv = (torch.randn((2 * C, K), device=dev) / math.sqrt(K)).to(torch.bfloat16)
+    b_kv = 0.1 * torch.randn(2 * C, device=dev)
+    qn = 1.0 + 0.2 * torch.randn(D, device=dev)
+    kn = 1.0 + 0.2 * torch.randn(D, device=dev)
+    cs = rope2dTable(IMG_H, IMG_W, D, dev)
+    bufs = projection_buffers(B, L, LT, dev)
+    out = torch.empty((B, L, C), dtype=torch.bfloat16, device=dev)
+    qkv = torch.zeros((B, L + LT, 3 * C), dtype=torch.bfloat16, device=dev)
+
+    def step(i):
+        x, xt, kv_len, bias, _ = sets[i % len(sets)]
+        dit_block_attention_projected(x, w_qkv=w_qkv, b_qkv=b_qkv, q_norm=qn, k_norm=kn, cs=cs, x_text=xt,
+                                      w_kv=w_kv, b_kv=b_kv, kv_len=kv_len, bias=bias, out=out, buffers=bufs)
+
+    b_qkv_h, b_kv_h = b_qkv.to(torch.bfloat16), b_kv.to(torch.bfloat16)
+
+    def step_unfused(i):
+        x, xt, kv_len, bias, _ = sets[i % len(sets)]
+        for b in range(B):
+            torch.addmm(b_qkv_h, x[b], w_qkv.T, out=qkv[b, :L])   # cuBLAS, bias in its epilogue
+            qkv[b, L:, C:] = torch.addmm(b_kv_h, xt[b], w_kv.T)
+        dit_block_attention(qkv, L=L, q_norm=qn, k_norm=kn, cs=cs, text_rows=LT, kv_len=kv_len, bias=bias, out=out)
+
+    def step_flops(i):
+        lv = sets[i % len(sets)][4]
+        return 2.0 * B * K * (L * 3 * C + LT * 2 * C) + joint_flops(B, L, lv)
+
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(local_rank) as clocks:
+        ms = _timed(step, args.steps, args.warmup, world, stream)
+    ms_unfused = _timed(step_unfused, args.steps, args.warmup, world, stream)
+    flops = sum_over_ranks(sum(step_flops(i) for i in range(args.steps)))
+    kst = _kernel_stats(step, min(args.steps, 3))
+    if rank != 0:
+        return
+    pl, pms, pfl, _ = kst["projection"]
+    peak, src = measured_peak()
+    proj_tf = pfl / (pms * 1e-3) / 1e12
+    roof = _roofline(kst, "attn_fwd_kernel<96>")
+    roof["projection"] = {"kernel": "proj_kernel<96>", "achieved": proj_tf, "peak": peak, "unit": "TFLOP/s",
+                          "frac": proj_tf / peak, "ms_per_step": pms / min(args.steps, 3)}
+    cfg = {"workload": "config 6: DiT block attention step from the block input, config 2 shapes (52x76=3952 image "
+                       "tokens + 256 text slots, batch 2, K=1536): qkv_x / kv_y linears with q/k RMSNorm + 2D RoPE "
+                       "in the GEMM epilogue, then joint attention",
+           "global_batch": B * world, "seq_len": L, "parallelism": f"dp{world}",
+           "l2": "six 26 MB block inputs rotate (156 MB > 126 MB L2)",
+           "flops_note": "2*B*K*(3952*4608 + 256*3072) linear + 4*B*H*valid pairs*D attention"}
+    print(json.dumps(_line(args, world, flops / (ms * 1e-3) / 1e12, ms, cfg, roof, clocks.summary(),
+                           4 * B * args.steps, "weak", unfused_ms_per_step=ms_unfused / args.steps)), flush=True)
+
+
 def run_profile(args, local_rank):
     """Small driver for ncu captures: the same fused call as the benchmark on ``--batch`` elements of
     config 2, ``--warmup`` + ``--steps`` launches of each kernel, nothing else on the GPU."""
@@ -682,8 +758,9 @@ def main():
     ap.add_argument("--seq-mode", choices=["auto", "nccl", "p2p", "ce"], default="auto",
                     help="config 5: k'|v' exchange by NCCL all-gather, peer stores from the prologue, or "
                          "copy-engine pushes")
-    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2,
-                    help="BASELINE config to run (2 = the headline line; 3, 4, 5 print their own line)")
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5, 6], default=2,
+                    help="BASELINE config to run (2 = the headline line; 3, 4, 5 print their own line; 6 = the "
+                         "config-2 block step from the block input, QKV projection fused with the prologue)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -706,7 +783,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5}[args.config](args, rank, world, local_rank)
+        {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5, 6: run_config6}[args.config](
+            args, rank, world, local_rank)
     finally:
         if world > 1:
             dist.destroy_process_group()

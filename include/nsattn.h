@@ -215,6 +215,39 @@ nsa_status nsa_seq_shard_attention(const nsa_fused_desc* desc, const nsa_seq_sha
                                    const float* bias, void* out, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * nsa_seq_shard_projection: step 1 computed from the block input instead of from qkv.  The
+ * reference builds qkv with ops.linear (app/gpu/ops.js:50; tools/reference.py:208-210, 272, 282):
+ * q|k|v = x @ W_qkv^T + b_qkv over the image rows (`dit.qkv`, app/models/nanosaur2.js:197) and
+ * k|v = x_text @ W_kv^T + b_kv over the text rows (`dit.kv_y`, nanosaur2.js:201), then runs
+ * ops.headNorm on q and k (nanosaur2.js:199-202).  Here one tcgen05 GEMM per row set computes the
+ * linear, and its epilogue adds the bias, applies the per-head RMSNorm and the RoPE, and writes
+ * q_prime and kv_packed exactly as nsa_seq_shard_prologue does (same layouts and zero padding; on
+ * one GPU use the full-sequence shard {0, Lq, 0, 0}).  The qkv matrix is never materialised.
+ * Inputs bf16 (desc->in_dtype NSA_BF16); weights bf16 in the PyTorch Linear layout [out][K] with
+ * rows q heads, then k heads, then v heads (w_kv: k heads, then v heads); biases fp32 or NULL.
+ * K a multiple of 8, all pointers and row pitches 16-byte aligned.  Head dims 64, 96, 128, 256 with
+ * Hq and Hkv multiples of the heads one output tile holds (2 at D = 96 and 128, 4 at 64, 1 at 256).
+ * ------------------------------------------------------------------------------------------------ */
+typedef struct nsa_proj_desc {
+  int32_t K;                  /* input features (model width) */
+  const void* x;              /* image rows: element (b, row, k) at x[b*x_bstride + row*ldx + k] */
+  int64_t ldx, x_bstride;
+  int32_t x_rows;             /* rows of one element of x; image row q_begin is row qkv_image_row0 */
+  const void* w_qkv;          /* [(Hq + 2*Hkv)*D][K] */
+  const float* b_qkv;         /* [(Hq + 2*Hkv)*D] or NULL */
+  const void* x_text;         /* text rows (keys Lq .. Lk-1) at x_text[b*text_bstride + t*ld_text + k],
+                                 text row 0 at row qkv_text_row0; NULL when Lk == Lq */
+  int64_t ld_text, text_bstride;
+  int32_t text_rows;          /* rows of one element of x_text */
+  const void* w_kv;           /* [2*Hkv*D][K] */
+  const float* b_kv;          /* [2*Hkv*D] or NULL */
+} nsa_proj_desc;
+nsa_status nsa_seq_shard_projection(const nsa_fused_desc* desc, const nsa_seq_shard* shard,
+                                    const nsa_proj_desc* proj, const float* q_norm_w, const float* k_norm_w,
+                                    const float* cs, const int32_t* kv_len, void* q_prime, void* kv_packed,
+                                    void* stream);
+
+/* ------------------------------------------------------------------------------------------------
  * RoPE tables in the reference layout: cos block [L][D/2] then sin block [L][D/2] (sinOff = L*D/2).
  *   nsa_rope2d_table: app/models/common.js:28-43 (tools/reference.py:220-227): L = h*w tokens,
  *     the first D/4 pairs rotate by the centred column, the next D/4 by the centred row, theta 1e4.

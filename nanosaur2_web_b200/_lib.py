@@ -54,6 +54,13 @@ class SeqShard(ctypes.Structure):
     _fields_ = [("q_begin", _i32), ("q_count", _i32), ("qkv_image_row0", _i32), ("qkv_text_row0", _i32)]
 
 
+class ProjDesc(ctypes.Structure):
+    """nsa_proj_desc (include/nsattn.h)."""
+    _fields_ = [("K", _i32), ("x", _vp), ("ldx", _i64), ("x_bstride", _i64), ("x_rows", _i32), ("w_qkv", _vp),
+                ("b_qkv", _vp), ("x_text", _vp), ("ld_text", _i64), ("text_bstride", _i64), ("text_rows", _i32),
+                ("w_kv", _vp), ("b_kv", _vp)]
+
+
 class KernelStat(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 32), ("launches", _i64), ("total_ms", ctypes.c_double),
                 ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
@@ -82,6 +89,8 @@ SIGNATURES = {
                                             _vp, _vp, _vp, ctypes.POINTER(_vp), _i32, _vp]),
     "nsa_seq_shard_attention": (_i32, [ctypes.POINTER(FusedDesc), ctypes.POINTER(SeqShard), _vp, _vp, _vp, _vp, _vp,
                                        _vp]),
+    "nsa_seq_shard_projection": (_i32, [ctypes.POINTER(FusedDesc), ctypes.POINTER(SeqShard), ctypes.POINTER(ProjDesc),
+                                        _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "nsa_rope2d_table": (_i32, [_i32, _i32, _i32, _vp, _vp]),
     "nsa_rope1d_table": (_i32, [_i32, _i32, _f32, _vp, _vp]),
     "nsa_check_device": (_i32, [_vp]),

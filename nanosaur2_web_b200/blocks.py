@@ -8,6 +8,11 @@
   blocks (no text rows).
 * ``text_refine_attention(...)``: the text-refine blocks' attention (no RoPE, every text row is a
   query, app/models/nanosaur2.js:128-132; tools/reference.py:258-259).
+* ``dit_block_attention_projected(...)``: the same DiT step from the block input instead of qkv:
+  ops.linear `dit.qkv` + `dit.kv_y` (app/models/nanosaur2.js:197-201; tools/reference.py:208-210,
+  272, 282) as one tcgen05 GEMM per row set whose epilogue applies the bias, the q/k RMSNorm and the
+  RoPE and writes the attention's inputs (nsa_seq_shard_projection), then the attention
+  (nsa_seq_shard_attention).
 * ``gemma_layer_attention(...)``: one Gemma3 layer's attention, headNorm(q), headNorm(k) with the
   local/global RoPE table + causal GQA 4/1 attention (app/models/gemma3.js:63-70;
   tools/reference.py:186-194), with an optional sliding window.
@@ -22,7 +27,7 @@ from typing import Optional, Sequence, Tuple
 import torch
 
 from . import _lib
-from ._lib import FusedDesc, NsaError, check, lib
+from ._lib import FusedDesc, NsaError, ProjDesc, SeqShard, check, lib
 from .ops import RopeTable, dtype_code, stream_handle
 
 DIT_HEADS, DIT_HEAD_DIM = 16, 96
@@ -123,6 +128,81 @@ def dit_block_attention(qkv: torch.Tensor, *, L: int, q_norm: torch.Tensor, k_no
     return _fused(qkv, Lq=L, Lk=L + text_rows, Hq=DIT_HEADS, Hkv=DIT_HEADS, D=DIT_HEAD_DIM, qOff=0, kOff=C,
                   vOff=2 * C, q_norm=q_norm, k_norm=k_norm, cs=cs, kv_len=kv_len, bias=bias, biasStart=L,
                   causal=False, window=0, eps=eps, out=out, out_dtype=out_dtype, shard=shard, workspace=workspace)
+
+
+def projection_buffers(B: int, L: int, text_rows: int, device) -> Tuple[torch.Tensor, torch.Tensor]:
+    """q_prime [B, bytes] (uint8) and kv_packed [B, kv_rows, 2*1536] (bf16) of a one-GPU DiT block."""
+    d = FusedDesc()
+    d.B, d.Lq, d.Lk, d.Hq, d.Hkv, d.D = B, L, L + text_rows, DIT_HEADS, DIT_HEADS, DIT_HEAD_DIM
+    d.in_dtype = d.out_dtype = _lib.NSA_BF16
+    d.b_begin, d.b_count = 0, 1
+    s = SeqShard(0, L, 0, 0)
+    qb, kb, rows = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_int32()
+    check(lib().nsa_seq_shard_buffer_sizes(ctypes.byref(d), ctypes.byref(s), ctypes.byref(qb), ctypes.byref(kb),
+                                           ctypes.byref(rows)))
+    q_prime = torch.empty((B, qb.value), dtype=torch.uint8, device=device)
+    kv_packed = torch.empty((B, rows.value, 2 * DIT_HEADS * DIT_HEAD_DIM), dtype=torch.bfloat16, device=device)
+    return q_prime, kv_packed
+
+
+def dit_block_attention_projected(x: torch.Tensor, *, w_qkv: torch.Tensor, b_qkv: Optional[torch.Tensor],
+                                  q_norm: torch.Tensor, k_norm: torch.Tensor, cs: Optional[RopeTable],
+                                  x_text: Optional[torch.Tensor] = None, w_kv: Optional[torch.Tensor] = None,
+                                  b_kv: Optional[torch.Tensor] = None, kv_len: Optional[torch.Tensor] = None,
+                                  bias: Optional[torch.Tensor] = None, eps: float = 1e-6,
+                                  out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                                  buffers: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
+    """One DiT block's attention step from its input rows (app/models/nanosaur2.js:196-208):
+    x [B, L, K] bf16 (the modulated block input), w_qkv [3*1536, K] bf16 and b_qkv [3*1536] fp32
+    (``attn.qkv_x``), x_text [B, text_rows, K] with w_kv [2*1536, K] / b_kv (``attn.kv_y``) for the
+    text keys.  kv_len[b] = L + valid text rows; bias [B, text_rows] log prompt weights.
+    ``buffers`` = projection_buffers(...) to reuse across calls.  Returns [B, L, 1536]."""
+    tensors = (x, w_qkv, b_qkv, q_norm, k_norm, x_text, w_kv, b_kv, kv_len, bias, out)
+    if any(t is not None and not t.is_cuda for t in tensors):
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "tensors must live on a CUDA device")
+    if x.dim() != 3 or x.stride(-1) != 1 or x.dtype != torch.bfloat16:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "x must be a bf16 [B, L, K] tensor with contiguous rows")
+    if not w_qkv.is_contiguous() or (w_kv is not None and not w_kv.is_contiguous()):
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "weights must be contiguous [out, K]")
+    if kv_len is not None and kv_len.dtype != torch.int32:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "kv_len must be int32")
+    B, L, K = x.shape
+    text_rows = 0 if x_text is None else x_text.shape[1]
+    C = DIT_HEADS * DIT_HEAD_DIM
+    if out is None:
+        out = torch.empty((B, L, C), dtype=out_dtype or torch.bfloat16, device=x.device)
+    q_prime, kv_packed = buffers if buffers is not None else projection_buffers(B, L, text_rows, x.device)
+    d = FusedDesc()
+    d.B, d.Lq, d.Lk, d.Hq, d.Hkv, d.D = B, L, L + text_rows, DIT_HEADS, DIT_HEADS, DIT_HEAD_DIM
+    d.qOff, d.kOff, d.vOff = 0, C, 2 * C
+    d.in_dtype, d.out_dtype = _lib.NSA_BF16, dtype_code(out)
+    d.ldo, d.o_bstride, d.oOff = out.stride(1), out.stride(0), 0
+    d.eps = eps
+    d.sinOff = cs.sinOff if cs is not None else 0
+    d.biasStart = L
+    d.biasLen = 0 if bias is None else bias.shape[-1]
+    d.bias_bstride = bias.stride(0) if (bias is not None and bias.dim() == 2) else 0
+    s = SeqShard(0, L, 0, 0)
+    p = ProjDesc()
+    p.K = K
+    p.x, p.ldx, p.x_bstride, p.x_rows = x.data_ptr(), x.stride(1), x.stride(0), L
+    p.w_qkv, p.b_qkv = w_qkv.data_ptr(), None if b_qkv is None else b_qkv.data_ptr()
+    if x_text is not None:
+        p.x_text, p.ld_text, p.text_bstride, p.text_rows = x_text.data_ptr(), x_text.stride(1), x_text.stride(0), text_rows
+        p.w_kv, p.b_kv = w_kv.data_ptr(), None if b_kv is None else b_kv.data_ptr()
+    L_ = lib()
+    with torch.cuda.device(x.device):
+        stream = stream_handle(x.device)
+        for b in range(B):
+            d.b_begin, d.b_count = b, 1
+            check(L_.nsa_seq_shard_projection(ctypes.byref(d), ctypes.byref(s), ctypes.byref(p), q_norm.data_ptr(),
+                                              k_norm.data_ptr(), cs.buf.data_ptr() if cs is not None else None,
+                                              None if kv_len is None else kv_len.data_ptr(), q_prime[b].data_ptr(),
+                                              kv_packed[b].data_ptr(), stream))
+            check(L_.nsa_seq_shard_attention(ctypes.byref(d), ctypes.byref(s), q_prime[b].data_ptr(),
+                                             kv_packed[b].data_ptr(), None if kv_len is None else kv_len.data_ptr(),
+                                             None if bias is None else bias.data_ptr(), out.data_ptr(), stream))
+    return out
 
 
 def text_refine_attention(qkv: torch.Tensor, *, q_norm: torch.Tensor, k_norm: torch.Tensor,

@@ -856,6 +856,152 @@ nsa_status nsa_seq_shard_prologue_peers(const nsa_fused_desc* d, const nsa_seq_s
   return NSA_OK;
 }
 
+namespace {
+
+// 128-byte-swizzled bf16 map over `rank` dims (dims[0] contiguous) for the projection's operands.
+bool encode_sw128(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                  const cuuint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// X map [elements][rows][K] (box [1][128][64]) and W map [N][K] (box [N tile][64]) of one GEMM.
+bool proj_maps(CUtensorMap* tx, CUtensorMap* tw, const void* x, int64_t ld, int64_t bstride, int rows, int b_count,
+               const void* w, int K, int N, int n_tile) {
+  const cuuint64_t xd[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)b_count};
+  const cuuint64_t xs[2] = {(cuuint64_t)ld * 2, (cuuint64_t)(bstride > 0 ? bstride : (int64_t)rows * ld) * 2};
+  const cuuint32_t xb[3] = {64, 128, 1};
+  const cuuint64_t wd[2] = {(cuuint64_t)K, (cuuint64_t)N};
+  const cuuint64_t ws[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t wb[2] = {64, (cuuint32_t)n_tile};
+  return encode_sw128(tx, x, 3, xd, xs, xb) && encode_sw128(tw, w, 2, wd, ws, wb);
+}
+
+}  // namespace
+
+nsa_status nsa_seq_shard_projection(const nsa_fused_desc* d, const nsa_seq_shard* s, const nsa_proj_desc* proj,
+                                    const float* q_norm_w, const float* k_norm_w, const float* cs,
+                                    const int32_t* kv_len, void* q_prime, void* kv_packed, void* stream) {
+  SeqPlan sp;
+  nsa_status st = make_seq_plan(d, s, &sp);
+  if (st != NSA_OK) return st;
+  if (!proj) return fail(NSA_ERR_INVALID_ARGUMENT, "proj is NULL");
+  if (d->in_dtype != NSA_BF16) return fail(NSA_ERR_UNSUPPORTED, "the projection takes bf16 inputs and weights");
+  if (!q_norm_w || !k_norm_w) return fail(NSA_ERR_INVALID_ARGUMENT, "q/k norm weights are required");
+  const int D = d->D;
+  const int hpt = nsa::projection_heads_per_tile(D);
+  if (!hpt) return fail(NSA_ERR_UNSUPPORTED, "the projection supports head dims 64, 96, 128 and 256");
+  if (d->Hq % hpt || d->Hkv % hpt)
+    return fail(NSA_ERR_UNSUPPORTED, "Hq and Hkv must be multiples of " + std::to_string(hpt) +
+                                         " (the heads of one projection tile)");
+  const Plan& pl = sp.pl;
+  const int K = proj->K;
+  auto a16 = [](const void* ptr) { return ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  if (K < 1 || K % 8) return fail(NSA_ERR_INVALID_ARGUMENT, "K must be a positive multiple of 8");
+  if (!proj->x || !proj->w_qkv || proj->x_rows < 1 || proj->ldx < K || proj->ldx % 8 || proj->x_bstride % 8 ||
+      proj->x_bstride < 0 || (pl.Bs > 1 && proj->x_bstride == 0))
+    return fail(NSA_ERR_INVALID_ARGUMENT, "x needs ldx >= K, ldx and x_bstride multiples of 8, and x_rows >= 1");
+  if ((int64_t)sp.img_row0 + sp.q_count > proj->x_rows)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "the shard's image rows exceed x_rows");
+  if (!a16(proj->x) || !a16(proj->w_qkv) || !a16(proj->b_qkv) || !a16(q_norm_w) || !a16(k_norm_w) || !a16(cs) ||
+      !a16(q_prime) || !a16(kv_packed) || !q_prime || !kv_packed)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "pointers must be 16-byte aligned (q_prime and kv_packed non-NULL)");
+  if (cs && d->sinOff % 4) return fail(NSA_ERR_INVALID_ARGUMENT, "sinOff must be a multiple of 4");
+  const bool text = pl.Lk > sp.L;
+  if (text && (!proj->x_text || !proj->w_kv || proj->text_rows < 1 || proj->ld_text < K || proj->ld_text % 8 ||
+               proj->text_bstride % 8 || proj->text_bstride < 0 || (pl.Bs > 1 && proj->text_bstride == 0) ||
+               !a16(proj->x_text) || !a16(proj->w_kv) || !a16(proj->b_kv)))
+    return fail(NSA_ERR_INVALID_ARGUMENT,
+                "text keys (Lk > Lq) need x_text and w_kv (16-byte aligned, ld_text >= K, multiples of 8)");
+  if (text && (int64_t)sp.text_row0 + (pl.Lk - sp.L) > proj->text_rows)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "the text rows exceed text_rows");
+  int* err = nsa::device_error_word();
+  if (!err) return fail(NSA_ERR_CUDA, "cannot resolve the device error word on this device");
+  const cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  auto* Q = static_cast<__nv_bfloat16*>(q_prime);
+  auto* KV = static_cast<__nv_bfloat16*>(kv_packed);
+  const SplitScratch split =
+      split_scratch(static_cast<uint8_t*>(q_prime) + sp.q_tiles_bytes, pl.split_cap, pl.NQ, pl.D);
+
+  nsa::ProjParams pp{};
+  pp.B = pl.Bs;
+  pp.b_begin = pl.b0;
+  pp.k_steps = (K + 63) / 64;
+  pp.Hq = d->Hq;
+  pp.Hkv = d->Hkv;
+  pp.Lk = pl.Lk;
+  pp.Lq_pad = pl.Lq_pad;
+  pp.Lk_pad = pl.Lk_pad;
+  pp.kv_ld = sp.kv_ld;
+  pp.q_w = q_norm_w;
+  pp.k_w = k_norm_w;
+  pp.eps = d->eps;
+  pp.kv_len = kv_len;
+  pp.q_prime = Q;
+  pp.kv_packed = KV;
+  pp.err = err;
+  pp.timeout_ns = wait_timeout_ns();
+
+  // image rows: q|k|v of the shard's own rows, q' rows past them zero
+  CUtensorMap tx, tw;
+  const auto* x0 = static_cast<const __nv_bfloat16*>(proj->x) + (int64_t)pl.b0 * proj->x_bstride;
+  if (!proj_maps(&tx, &tw, x0, proj->ldx, proj->x_bstride, proj->x_rows, pl.Bs, proj->w_qkv, K,
+                 (d->Hq + 2 * d->Hkv) * D, hpt * D))
+    return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the projection operands");
+  pp.image = 1;
+  pp.rows = pl.Lq_pad;
+  pp.m_tiles = pl.Lq_pad / 128;
+  pp.n_tiles = (d->Hq + 2 * d->Hkv) / hpt;
+  pp.valid_q = sp.q_count;
+  pp.key_row0 = sp.q_begin;
+  pp.x_row0 = sp.img_row0;
+  pp.rope_row0 = sp.q_begin;
+  pp.bias = proj->b_qkv;
+  pp.cs = cs;
+  pp.sin_off = d->sinOff;
+  pp.zero_ptr = pl.split_cap > 0 ? split.count : nullptr;   // the attention's split counters start at zero
+  pp.zero_count = pl.split_cap;
+  const double flops_img = 2.0 * pl.Bs * sp.q_count * (double)(d->Hq + 2 * d->Hkv) * D * K;
+  cudaError_t e = profiled("projection", flops_img, 0.0, strm, [&] { return nsa::launch_projection(pp, D, tx, tw, strm); });
+  if (e != cudaSuccess) return cuda_fail(e, "projection launch");
+
+  // text rows (every rank computes them), and the zero padding up to kv_rows
+  if (pl.Lk_pad > sp.L) {
+    if (text) {
+      const auto* t0 = static_cast<const __nv_bfloat16*>(proj->x_text) + (int64_t)pl.b0 * proj->text_bstride;
+      if (!proj_maps(&tx, &tw, t0, proj->ld_text, proj->text_bstride, proj->text_rows, pl.Bs, proj->w_kv, K,
+                     2 * d->Hkv * D, hpt * D))
+        return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the projection operands");
+      pp.image = 0;
+      pp.rows = pl.Lk_pad - sp.L;
+      pp.m_tiles = (pp.rows + 127) / 128;
+      pp.n_tiles = 2 * d->Hkv / hpt;
+      pp.valid_q = 0;
+      pp.key_row0 = sp.L;
+      pp.x_row0 = sp.text_row0;
+      pp.rope_row0 = 0;
+      pp.bias = proj->b_kv;
+      pp.cs = nullptr;
+      pp.zero_ptr = nullptr;
+      pp.zero_count = 0;
+      const double flops_txt = 2.0 * pl.Bs * (pl.Lk - sp.L) * (double)(2 * d->Hkv) * D * K;
+      e = profiled("projection", flops_txt, 0.0, strm, [&] { return nsa::launch_projection(pp, D, tx, tw, strm); });
+      if (e != cudaSuccess) return cuda_fail(e, "projection launch");
+    } else {
+      for (int bl = 0; bl < pl.Bs; ++bl) {
+        e = cudaMemsetAsync(KV + ((int64_t)bl * pl.Lk_pad + sp.L) * sp.kv_ld, 0,
+                            (size_t)(pl.Lk_pad - sp.L) * sp.kv_ld * 2, strm);
+        if (e != cudaSuccess) return cuda_fail(e, "kv padding");
+      }
+    }
+  }
+  return NSA_OK;
+}
+
 nsa_status nsa_seq_shard_attention(const nsa_fused_desc* d, const nsa_seq_shard* s, const void* q_prime,
                                    const void* kv_packed, const int32_t* kv_len, const float* bias, void* out,
                                    void* stream) {

@@ -124,6 +124,44 @@ cudaError_t launch_attention_persist(const AttnParams& p, const CUtensorMap& tmQ
 
 cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream);
 
+// QKV projection GEMM with the prologue in its epilogue (proj.cu): rows of X [.][K] times W^T
+// ([N][K], q heads then k then v, or k then v for the text rows), + bias, then per head the q/k
+// RMSNorm and split-half RoPE, written straight into the sequence-shard layouts: q' tiles
+// [B][Hq][Lq_pad][D] and packed k'|v' rows [B][Lk_pad][2 Hkv D].  GEMM row r of batch element bl
+// is input row x_row0 + r, query row r (image rows) and key row key_row0 + r.
+struct ProjParams {
+  int B, b_begin;          // batch elements of the call and the first one's global index
+  int m_tiles, n_tiles;    // 128-row tiles per batch element, head-group tiles over N
+  int k_steps;             // 64-element slices of K
+  int image;               // 1: q|k|v of the image rows; 0: k|v of the text rows
+  int Hq, Hkv;             // heads (whole model: sequence shards take whole heads)
+  int rows;                // GEMM rows per batch element (Lq_pad or Lk_pad - L)
+  int valid_q;             // image: query rows of the shard (rows past it are zeros in q')
+  int key_row0;            // key index of GEMM row 0 (image: q_begin, text: L)
+  int x_row0;              // input row of GEMM row 0
+  int Lk, Lq_pad, Lk_pad;  // keys; padded rows of q' and kv_packed
+  int64_t kv_ld;           // elements per kv_packed row
+  const float* bias;       // [N] or null
+  const float* q_w;        // [D] q RMSNorm weight
+  const float* k_w;        // [D] k RMSNorm weight
+  const float* cs;         // RoPE table (image rows): cos [rows][D/2], sin at sin_off; null = none
+  int64_t sin_off;
+  int rope_row0;           // RoPE table row of GEMM row 0 (image: q_begin)
+  float eps;
+  const int* kv_len;       // [B_total] valid keys, or null (Lk)
+  __nv_bfloat16* q_prime;
+  __nv_bfloat16* kv_packed;
+  int* zero_ptr;           // zero_count ints cleared by CTA 0 (the attention's split counters)
+  int zero_count;
+  int* err;
+  unsigned long long timeout_ns;
+};
+// D in {64, 96, 128, 256}; cudaErrorInvalidValue otherwise.  tmX: 3-D map [B][rows][K] over the
+// input, box [1][128][64], 128-byte swizzle; tmW: 2-D map [N][K], box [heads-per-tile * D][64].
+cudaError_t launch_projection(const ProjParams& p, int D, const CUtensorMap& tmX, const CUtensorMap& tmW,
+                              cudaStream_t stream);
+int projection_heads_per_tile(int D);   // 0: unsupported head dim
+
 // Returns cudaErrorInvalidValue for unsupported head dims.
 cudaError_t launch_attention(const AttnParams& p, int D, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                              const CUtensorMap& tmV, const CUtensorMap& tmVd, cudaStream_t stream);

@@ -57,6 +57,7 @@ enum : int {
   kErrTimeoutLoad = 0x101,     // producer waited too long for a free stage
   kErrTimeoutMma = 0x102,      // MMA issuer waited too long for data / probabilities
   kErrTimeoutSoftmax = 0x103,  // softmax warps waited too long for scores / output
+  kErrTimeoutProjection = 0x105,  // projection GEMM roles waited too long for a stage / accumulator
   kErrAborted = 0x1FF,         // another role of the CTA gave up first
 };
 
@@ -101,6 +102,14 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
           smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 

@@ -29,6 +29,15 @@ DIT_HEADS, DIT_HEAD_DIM = 16, 96          # tools/reference.py:205
 GEMMA_HEADS, GEMMA_KV_HEADS, GEMMA_HEAD_DIM = 4, 1, 256   # tools/reference.py:178
 
 
+# ----------------------------------------------------------------------------- projection
+
+def linear(x, w, b=None, acc=np.float32):
+    """The reference's lin / ops.linear (tools/reference.py:208-210; app/gpu/ops.js:50-66 with
+    app/gpu/gemm.js:141): y = x @ W^T (+ b), W in the Linear layout [out features][in features]."""
+    y = np.asarray(x, acc) @ np.asarray(w, acc).T
+    return y + np.asarray(b, acc) if b is not None else y
+
+
 # ----------------------------------------------------------------------------- prologue pieces
 
 def rms_norm(x, w, eps=1e-6, acc=np.float32):

@@ -15,6 +15,8 @@ drives its real code paths with small seeded stand-in weights (no model files ex
 * ``gemma_encode`` (``:175-200``): the raw q/k of each layer's q/k norm, the SDPA inputs/outputs and
   the causal mask.
 * ``rope_2d`` / ``gemma_rope`` tables and ``rms_norm`` / ``rope_split_half`` on seeded inputs.
+* ``lin`` (``:208-210``), the q|k|v projection's linear, on small seeded operands with and without a
+  bias (``--only linear`` writes just this fixture).
 
 The qkv projection outputs of the DiT are rounded to bf16 inside the reference run (a hook on its
 ``lin``), so the bf16 CUDA path sees exactly the inputs the fp32 reference saw.  The Gemma inputs
@@ -195,17 +197,44 @@ def np32(t):
     return t.detach().float().cpu().numpy().astype(np.float32)
 
 
+def write_linear(R, out):
+    """The reference's lin (y = x @ W^T + b) on a 7 x 64 input and a 96 x 64 weight."""
+
+    class Params:
+        def __init__(self, d):
+            self.d = d
+
+        def __call__(self, name):
+            return self.d[name]
+
+        def has(self, name):
+            return name in self.d
+
+    gen = torch.Generator().manual_seed(77)
+    x = torch.randn(7, 64, generator=gen)
+    w = torch.randn(96, 64, generator=gen) / 8
+    b = torch.randn(96, generator=gen)
+    y = R.lin(Params({"attn.qkv_x.weight": w, "attn.qkv_x.bias": b}), "attn.qkv_x", x)
+    y_nobias = R.lin(Params({"attn.kv_y.weight": w}), "attn.kv_y", x)
+    np.savez_compressed(os.path.join(out, "linear.npz"), x=np32(x), w=np32(w), b=np32(b), y=np32(y),
+                        y_nobias=np32(y_nobias))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("NANOSAUR2_REFERENCE"),
                     help="checkout of the reference repository (or NANOSAUR2_REFERENCE)")
     ap.add_argument("--out", default=HERE)
+    ap.add_argument("--only", choices=["linear"], help="write one fixture only")
     args = ap.parse_args()
     if not args.reference:
         ap.error("pass --reference <checkout of the reference> or set NANOSAUR2_REFERENCE")
     sys.path.insert(0, os.path.join(args.reference, "tools"))
     import reference as R  # noqa: E402  (the unmodified reference module)
     torch.set_num_threads(min(8, os.cpu_count() or 1))
+    write_linear(R, args.out)
+    if args.only == "linear":
+        return
 
     # ---- DiT: 4x5 latent (20 image tokens), 10 text slots with emphasis weights and dropped tokens
     h, w = 4, 5

@@ -1,0 +1,161 @@
+"""The QKV projection with the prologue in its GEMM epilogue (nsa_seq_shard_projection, through
+``blocks.dit_block_attention_projected``) against the CPU oracle: the reference's linear
+(tools/reference.py:208-210, pinned by tests/golden/linear.npz) followed by the DiT block's head
+norms, 2D RoPE and joint attention (:272-286).  Inputs are bf16; the oracle runs in float64 on the
+same bf16 values.  Tolerance of the bf16 path: max-abs <= 2e-2 and per-head cosine >= 0.9999."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention_oracle as O
+from tests._helpers import assert_close_bf16, bf16_round
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0)
+C, H, D = 1536, 16, 96
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib_loaded():
+    torch.cuda.set_device(DEV)
+    from nanosaur2_web_b200 import _lib
+    _lib.lib()
+    yield
+    torch.cuda.synchronize()
+
+
+def t(x, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(device=DEV, dtype=dtype)
+
+
+def proj_inputs(seed, B, L, Lt, K, lv_range):
+    """Block input rows, q|k|v and k|v weights (Linear layout, ~unit-variance outputs), biases,
+    norm weights, valid text lengths and log prompt-weight biases."""
+    rng = np.random.default_rng(seed)
+    x = bf16_round(rng.standard_normal((B, L, K), dtype=np.float32))
+    w = bf16_round(rng.standard_normal((3 * C, K), dtype=np.float32) / np.sqrt(K))
+    b = (0.1 * rng.standard_normal(3 * C)).astype(np.float32)
+    xt = bf16_round(rng.standard_normal((B, Lt, K), dtype=np.float32)) if Lt else None
+    wkv = bf16_round(rng.standard_normal((2 * C, K), dtype=np.float32) / np.sqrt(K)) if Lt else None
+    bkv = (0.1 * rng.standard_normal(2 * C)).astype(np.float32) if Lt else None
+    q_w = (1.0 + 0.2 * rng.standard_normal(D)).astype(np.float32)
+    k_w = (1.0 + 0.2 * rng.standard_normal(D)).astype(np.float32)
+    lv = rng.integers(lv_range[0], lv_range[1] + 1, size=B).astype(np.int32) if Lt else np.zeros(B, np.int32)
+    bias = np.log(rng.choice(np.array([0.7, 1.0, 1.3], np.float32), size=(B, Lt))).astype(np.float32) if Lt else None
+    return x, w, b, xt, wkv, bkv, q_w, k_w, lv, bias
+
+
+def oracle_qkv(x, w, b, xt, wkv, bkv):
+    """The packed qkv the reference builds: image rows q|k|v = lin(x), text rows k|v = lin(x_text)."""
+    B, L, _ = x.shape
+    Lt = 0 if xt is None else xt.shape[1]
+    qkv = np.zeros((B, L + Lt, 3 * C), np.float64)
+    for bb in range(B):
+        qkv[bb, :L] = O.linear(x[bb], w, b, acc=np.float64)
+        if Lt:
+            qkv[bb, L:, C:] = O.linear(xt[bb], wkv, bkv, acc=np.float64)
+    return qkv
+
+
+def run_projected(x, w, b, xt, wkv, bkv, q_w, k_w, lv, bias, h, wd, buffers=None, out_dtype=torch.float32):
+    from nanosaur2_web_b200.blocks import dit_block_attention_projected
+    from nanosaur2_web_b200.ops import rope2dTable
+    L = h * wd
+    Lt = 0 if xt is None else xt.shape[1]
+    return dit_block_attention_projected(
+        t(x, torch.bfloat16), w_qkv=t(w, torch.bfloat16), b_qkv=t(b), q_norm=t(q_w), k_norm=t(k_w),
+        cs=rope2dTable(h, wd, D, DEV), x_text=None if xt is None else t(xt, torch.bfloat16),
+        w_kv=None if wkv is None else t(wkv, torch.bfloat16), b_kv=None if bkv is None else t(bkv),
+        kv_len=t(L + lv, torch.int32) if Lt else None, bias=None if bias is None else t(bias),
+        buffers=buffers, out_dtype=out_dtype)
+
+
+def check_device():
+    from nanosaur2_web_b200.ops import check_device as chk
+    chk(DEV)
+
+
+@pytest.mark.parametrize("K", [1536, 200])
+def test_projected_block_matches_oracle(K):
+    """20 x 24 image tokens + 64 text slots (10-64 valid), batch 2; K = 200 leaves a partial last
+    K slice that the TMA fills with zeros on both operands."""
+    h, wd, Lt = 20, 24, 64
+    L = h * wd
+    x, w, b, xt, wkv, bkv, q_w, k_w, lv, bias = proj_inputs(5 + K, 2, L, Lt, K, (10, 64))
+    out = run_projected(x, w, b, xt, wkv, bkv, q_w, k_w, lv, bias, h, wd)
+    check_device()
+    cos, sin = O.rope_2d(h, wd)
+    want = O.joint_attention_batched(oracle_qkv(x, w, b, xt, wkv, bkv), L, Lt, L + lv, q_w, k_w, cos, sin, bias=bias,
+                                     acc=np.float64)
+    assert_close_bf16(out.cpu().numpy(), want, D, what=f"projected block K={K}")
+
+
+def test_projection_buffers_and_padding():
+    """q' tiles and packed k'|v' rows against the oracle's normalised, rotated q / k and v, and every
+    padding row zero: q' rows past L, k'|v' rows past kv_len up to kv_rows."""
+    from nanosaur2_web_b200.blocks import projection_buffers
+    h, wd, Lt = 9, 15, 40
+    L = h * wd
+    x, w, b, xt, wkv, bkv, q_w, k_w, lv, bias = proj_inputs(77, 1, L, Lt, 1536, (17, 17))
+    q_prime, kv_packed = projection_buffers(1, L, Lt, DEV)
+    q_prime.fill_(0xFF)                       # NaN patterns: every byte the attention reads is written
+    kv_packed.fill_(float("nan"))
+    run_projected(x, w, b, xt, wkv, bkv, q_w, k_w, lv, bias, h, wd, buffers=(q_prime, kv_packed))
+    check_device()
+    qkv = oracle_qkv(x, w, b, xt, wkv, bkv)[0]
+    cos, sin = O.rope_2d(h, wd)
+    n = L + int(lv[0])
+    qn = O.head_norm(qkv[:L, :C], q_w, H, D, cos, sin, acc=np.float64)
+    kn = np.concatenate([O.head_norm(qkv[:L, C:2 * C], k_w, H, D, cos, sin, acc=np.float64),
+                         O.head_norm(qkv[L:n, C:2 * C], k_w, H, D, acc=np.float64)])
+    v = qkv[:n, 2 * C:]
+    q_pad = (L + 255) // 256 * 256
+    tiles = q_prime[0, :H * q_pad * D * 2].view(torch.bfloat16).view(H, q_pad, D).float().cpu().numpy()
+    got_q = tiles[:, :L].transpose(1, 0, 2).reshape(L, C)
+    assert_close_bf16(got_q, qn, D, what="q' tiles")
+    assert not tiles[:, L:].any(), "q' padding rows must be zero"
+    kv = kv_packed[0].float().cpu().numpy()
+    assert_close_bf16(kv[:n, :C], kn, D, what="k' rows")
+    assert_close_bf16(kv[:n, C:], v, D, what="v rows")
+    assert not kv[n:].any(), "k'|v' rows past kv_len must be zero"
+
+
+def test_projected_image_only_block():
+    """An odd block (no text rows): Lk = L, the key padding up to kv_rows zero-filled."""
+    h, wd = 7, 19
+    L = h * wd
+    x, w, b, _, _, _, q_w, k_w, _, _ = proj_inputs(91, 1, L, 0, 1536, (0, 0))
+    out = run_projected(x, w, b, None, None, None, q_w, k_w, np.zeros(1, np.int32), None, h, wd)
+    check_device()
+    cos, sin = O.rope_2d(h, wd)
+    want = O.joint_attention_batched(oracle_qkv(x, w, b, None, None, None), L, 0, np.array([L]), q_w, k_w, cos, sin,
+                                     acc=np.float64)
+    assert_close_bf16(out.cpu().numpy(), want, D, what="image-only block")
+
+
+def test_projected_matches_fused_at_config2():
+    """BASELINE config 2 shapes (52 x 76 image tokens, 256 text slots, batch 2): the projected path
+    against the unfused one (qkv = x W^T + b by torch in fp32, rounded to bf16, then the fused
+    prologue + attention).  Both are bf16 paths; they must agree within the bf16 bound."""
+    from nanosaur2_web_b200.blocks import dit_block_attention
+    from nanosaur2_web_b200.ops import rope2dTable
+    h, wd, Lt = 76, 52, 256
+    L = h * wd
+    x, w, b, xt, wkv, bkv, q_w, k_w, lv, bias = proj_inputs(123, 2, L, Lt, 1536, (32, 256))
+    got = run_projected(x, w, b, xt, wkv, bkv, q_w, k_w, lv, bias, h, wd, out_dtype=torch.bfloat16)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        img = t(x) @ t(w).T + t(b)
+        txt = t(xt) @ t(wkv).T + t(bkv)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    qkv = torch.zeros((2, L + Lt, 3 * C), device=DEV)
+    qkv[:, :L] = img
+    qkv[:, L:, C:] = txt
+    ref = dit_block_attention(qkv.to(torch.bfloat16), L=L, q_norm=t(q_w), k_norm=t(k_w), cs=rope2dTable(h, wd, D, DEV),
+                              text_rows=Lt, kv_len=t(L + lv, torch.int32), bias=t(bias), out_dtype=torch.bfloat16)
+    check_device()
+    assert_close_bf16(got.float().cpu().numpy(), ref.float().cpu().numpy(), D, what="projected vs fused")

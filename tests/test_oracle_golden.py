@@ -30,6 +30,12 @@ def test_rms_norm_and_rope(golden):
     np.testing.assert_allclose(rs, t["rope_out"], **TOL)
 
 
+def test_linear(golden):
+    t = golden("linear")
+    np.testing.assert_allclose(O.linear(t["x"], t["w"], t["b"]), t["y"], **TOL)
+    np.testing.assert_allclose(O.linear(t["x"], t["w"]), t["y_nobias"], **TOL)
+
+
 def test_gemma_theta_schedule():
     assert [O.gemma_rope_theta(i) for i in range(12)] == [1e4] * 5 + [1e6] + [1e4] * 5 + [1e6]
 
