@@ -248,6 +248,29 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* desc, const nsa_seq_sh
                                     void* stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * nsa_linear: ops.linear(gpu, x, W, {bias, resid, gate, gOff, act, ldc, cOff}) (app/gpu/ops.js:50-66)
+ * with the epilogue of the reference's tiled GEMM (app/gpu/gemm.js:155-165):
+ *   r = alpha * sum_k A[m][k] W[n][k] (+ bias[n]) (silu when act = 1), then
+ *   C[m*ldc + cOff + n] = r, or with resid: C[...] += r, or with resid and a gate: C[...] += gate[gOff + n] * r.
+ * The DiT block's output projection is the gated form (app/models/nanosaur2.js:210). A is bf16
+ * [M][lda], W bf16 in the Linear layout [N][K], C fp32 (the reference's residual stream), bias and
+ * gate fp32.  K, lda multiples of 8; N, ldc, cOff and gOff multiples of 4; pointers 16-byte aligned.
+ * (The reference's int8 ConvRot weights and LoRA deltas are not part of this entry.)
+ * ------------------------------------------------------------------------------------------------ */
+typedef struct nsa_linear_desc {
+  int32_t M, N, K;
+  int64_t lda;      /* A row pitch in elements */
+  int64_t ldc;      /* C row pitch in elements (0: N) */
+  int64_t cOff;     /* first column of C written (opts.cOff) */
+  int64_t gOff;     /* offset into gate (opts.gOff) */
+  float alpha;      /* 0 means 1 */
+  int32_t resid;    /* 1: accumulate into C (opts.resid) */
+  int32_t act;      /* 0: none, 1: silu (opts.act) */
+} nsa_linear_desc;
+nsa_status nsa_linear(const nsa_linear_desc* desc, const void* A, const void* W, const float* bias,
+                      const float* gate, float* C, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
  * RoPE tables in the reference layout: cos block [L][D/2] then sin block [L][D/2] (sinOff = L*D/2).
  *   nsa_rope2d_table: app/models/common.js:28-43 (tools/reference.py:220-227): L = h*w tokens,
  *     the first D/4 pairs rotate by the centred column, the next D/4 by the centred row, theta 1e4.

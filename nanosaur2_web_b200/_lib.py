@@ -61,6 +61,12 @@ class ProjDesc(ctypes.Structure):
                 ("w_kv", _vp), ("b_kv", _vp)]
 
 
+class LinearDesc(ctypes.Structure):
+    """nsa_linear_desc (include/nsattn.h)."""
+    _fields_ = [("M", _i32), ("N", _i32), ("K", _i32), ("lda", _i64), ("ldc", _i64), ("cOff", _i64), ("gOff", _i64),
+                ("alpha", _f32), ("resid", _i32), ("act", _i32)]
+
+
 class KernelStat(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 32), ("launches", _i64), ("total_ms", ctypes.c_double),
                 ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
@@ -91,6 +97,7 @@ SIGNATURES = {
                                        _vp]),
     "nsa_seq_shard_projection": (_i32, [ctypes.POINTER(FusedDesc), ctypes.POINTER(SeqShard), ctypes.POINTER(ProjDesc),
                                         _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "nsa_linear": (_i32, [ctypes.POINTER(LinearDesc), _vp, _vp, _vp, _vp, _vp, _vp]),
     "nsa_rope2d_table": (_i32, [_i32, _i32, _i32, _vp, _vp]),
     "nsa_rope1d_table": (_i32, [_i32, _i32, _f32, _vp, _vp]),
     "nsa_check_device": (_i32, [_vp]),

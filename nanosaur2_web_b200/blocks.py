@@ -131,16 +131,17 @@ def dit_block_attention(qkv: torch.Tensor, *, L: int, q_norm: torch.Tensor, k_no
 
 
 def projection_buffers(B: int, L: int, text_rows: int, device) -> Tuple[torch.Tensor, torch.Tensor]:
-    """q_prime [B, bytes] (uint8) and kv_packed [B, kv_rows, 2*1536] (bf16) of a one-GPU DiT block."""
+    """q_prime (uint8, the q' tiles of all B elements then the split scratch) and kv_packed
+    [B, kv_rows, 2*1536] (bf16) of a one-GPU DiT block."""
     d = FusedDesc()
     d.B, d.Lq, d.Lk, d.Hq, d.Hkv, d.D = B, L, L + text_rows, DIT_HEADS, DIT_HEADS, DIT_HEAD_DIM
     d.in_dtype = d.out_dtype = _lib.NSA_BF16
-    d.b_begin, d.b_count = 0, 1
+    d.b_begin, d.b_count = 0, B
     s = SeqShard(0, L, 0, 0)
     qb, kb, rows = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_int32()
     check(lib().nsa_seq_shard_buffer_sizes(ctypes.byref(d), ctypes.byref(s), ctypes.byref(qb), ctypes.byref(kb),
                                            ctypes.byref(rows)))
-    q_prime = torch.empty((B, qb.value), dtype=torch.uint8, device=device)
+    q_prime = torch.empty(qb.value, dtype=torch.uint8, device=device)
     kv_packed = torch.empty((B, rows.value, 2 * DIT_HEADS * DIT_HEAD_DIM), dtype=torch.bfloat16, device=device)
     return q_prime, kv_packed
 
@@ -190,18 +191,17 @@ def dit_block_attention_projected(x: torch.Tensor, *, w_qkv: torch.Tensor, b_qkv
     if x_text is not None:
         p.x_text, p.ld_text, p.text_bstride, p.text_rows = x_text.data_ptr(), x_text.stride(1), x_text.stride(0), text_rows
         p.w_kv, p.b_kv = w_kv.data_ptr(), None if b_kv is None else b_kv.data_ptr()
+    d.b_begin, d.b_count = 0, B
     L_ = lib()
     with torch.cuda.device(x.device):
         stream = stream_handle(x.device)
-        for b in range(B):
-            d.b_begin, d.b_count = b, 1
-            check(L_.nsa_seq_shard_projection(ctypes.byref(d), ctypes.byref(s), ctypes.byref(p), q_norm.data_ptr(),
-                                              k_norm.data_ptr(), cs.buf.data_ptr() if cs is not None else None,
-                                              None if kv_len is None else kv_len.data_ptr(), q_prime[b].data_ptr(),
-                                              kv_packed[b].data_ptr(), stream))
-            check(L_.nsa_seq_shard_attention(ctypes.byref(d), ctypes.byref(s), q_prime[b].data_ptr(),
-                                             kv_packed[b].data_ptr(), None if kv_len is None else kv_len.data_ptr(),
-                                             None if bias is None else bias.data_ptr(), out.data_ptr(), stream))
+        check(L_.nsa_seq_shard_projection(ctypes.byref(d), ctypes.byref(s), ctypes.byref(p), q_norm.data_ptr(),
+                                          k_norm.data_ptr(), cs.buf.data_ptr() if cs is not None else None,
+                                          None if kv_len is None else kv_len.data_ptr(), q_prime.data_ptr(),
+                                          kv_packed.data_ptr(), stream))
+        check(L_.nsa_seq_shard_attention(ctypes.byref(d), ctypes.byref(s), q_prime.data_ptr(), kv_packed.data_ptr(),
+                                         None if kv_len is None else kv_len.data_ptr(),
+                                         None if bias is None else bias.data_ptr(), out.data_ptr(), stream))
     return out
 
 

@@ -939,66 +939,114 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* d, const nsa_seq_shard
   pp.kv_ld = sp.kv_ld;
   pp.q_w = q_norm_w;
   pp.k_w = k_norm_w;
+  pp.cs = cs;
+  pp.sin_off = d->sinOff;
   pp.eps = d->eps;
   pp.kv_len = kv_len;
   pp.q_prime = Q;
   pp.kv_packed = KV;
+  pp.zero_ptr = pl.split_cap > 0 ? split.count : nullptr;   // the attention's split counters start at zero
+  pp.zero_count = pl.split_cap;
   pp.err = err;
   pp.timeout_ns = wait_timeout_ns();
 
-  // image rows: q|k|v of the shard's own rows, q' rows past them zero
-  CUtensorMap tx, tw;
+  // set 0, the image rows: q|k|v of the shard's own rows, q' rows past them zero
+  CUtensorMap tx[2], tw[2];
   const auto* x0 = static_cast<const __nv_bfloat16*>(proj->x) + (int64_t)pl.b0 * proj->x_bstride;
-  if (!proj_maps(&tx, &tw, x0, proj->ldx, proj->x_bstride, proj->x_rows, pl.Bs, proj->w_qkv, K,
+  if (!proj_maps(&tx[0], &tw[0], x0, proj->ldx, proj->x_bstride, proj->x_rows, pl.Bs, proj->w_qkv, K,
                  (d->Hq + 2 * d->Hkv) * D, hpt * D))
     return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the projection operands");
-  pp.image = 1;
-  pp.rows = pl.Lq_pad;
-  pp.m_tiles = pl.Lq_pad / 128;
-  pp.n_tiles = (d->Hq + 2 * d->Hkv) / hpt;
-  pp.valid_q = sp.q_count;
-  pp.key_row0 = sp.q_begin;
-  pp.x_row0 = sp.img_row0;
-  pp.rope_row0 = sp.q_begin;
-  pp.bias = proj->b_qkv;
-  pp.cs = cs;
-  pp.sin_off = d->sinOff;
-  pp.zero_ptr = pl.split_cap > 0 ? split.count : nullptr;   // the attention's split counters start at zero
-  pp.zero_count = pl.split_cap;
-  const double flops_img = 2.0 * pl.Bs * sp.q_count * (double)(d->Hq + 2 * d->Hkv) * D * K;
-  cudaError_t e = profiled("projection", flops_img, 0.0, strm, [&] { return nsa::launch_projection(pp, D, tx, tw, strm); });
+  nsa::ProjSet& img = pp.set[0];
+  img.image = 1;
+  img.rows = pl.Lq_pad;
+  img.m_tiles = pl.Lq_pad / 128;
+  img.n_tiles = (d->Hq + 2 * d->Hkv) / hpt;
+  img.valid_q = sp.q_count;
+  img.key_row0 = sp.q_begin;
+  img.x_row0 = sp.img_row0;
+  img.rope_row0 = sp.q_begin;
+  img.bias = proj->b_qkv;
+  pp.n_sets = 1;
+  double flops = 2.0 * pl.Bs * sp.q_count * (double)(d->Hq + 2 * d->Hkv) * D * K;
+  // set 1, the text rows (every rank computes them) and the zero padding up to kv_rows
+  if (text) {
+    const auto* t0 = static_cast<const __nv_bfloat16*>(proj->x_text) + (int64_t)pl.b0 * proj->text_bstride;
+    if (!proj_maps(&tx[1], &tw[1], t0, proj->ld_text, proj->text_bstride, proj->text_rows, pl.Bs, proj->w_kv, K,
+                   2 * d->Hkv * D, hpt * D))
+      return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the projection operands");
+    nsa::ProjSet& txt = pp.set[1];
+    txt.image = 0;
+    txt.rows = pl.Lk_pad - sp.L;
+    txt.m_tiles = (txt.rows + 127) / 128;
+    txt.n_tiles = 2 * d->Hkv / hpt;
+    txt.valid_q = 0;
+    txt.key_row0 = sp.L;
+    txt.x_row0 = sp.text_row0;
+    txt.rope_row0 = 0;
+    txt.bias = proj->b_kv;
+    pp.n_sets = 2;
+    flops += 2.0 * pl.Bs * (pl.Lk - sp.L) * (double)(2 * d->Hkv) * D * K;
+  }
+  cudaError_t e = profiled("projection", flops, 0.0, strm, [&] { return nsa::launch_projection(pp, D, tx, tw, strm); });
+  if (e == cudaErrorNotSupported)
+    return fail(NSA_ERR_UNSUPPORTED, "the projection's bias vectors do not fit in shared memory");
   if (e != cudaSuccess) return cuda_fail(e, "projection launch");
-
-  // text rows (every rank computes them), and the zero padding up to kv_rows
-  if (pl.Lk_pad > sp.L) {
-    if (text) {
-      const auto* t0 = static_cast<const __nv_bfloat16*>(proj->x_text) + (int64_t)pl.b0 * proj->text_bstride;
-      if (!proj_maps(&tx, &tw, t0, proj->ld_text, proj->text_bstride, proj->text_rows, pl.Bs, proj->w_kv, K,
-                     2 * d->Hkv * D, hpt * D))
-        return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the projection operands");
-      pp.image = 0;
-      pp.rows = pl.Lk_pad - sp.L;
-      pp.m_tiles = (pp.rows + 127) / 128;
-      pp.n_tiles = 2 * d->Hkv / hpt;
-      pp.valid_q = 0;
-      pp.key_row0 = sp.L;
-      pp.x_row0 = sp.text_row0;
-      pp.rope_row0 = 0;
-      pp.bias = proj->b_kv;
-      pp.cs = nullptr;
-      pp.zero_ptr = nullptr;
-      pp.zero_count = 0;
-      const double flops_txt = 2.0 * pl.Bs * (pl.Lk - sp.L) * (double)(2 * d->Hkv) * D * K;
-      e = profiled("projection", flops_txt, 0.0, strm, [&] { return nsa::launch_projection(pp, D, tx, tw, strm); });
-      if (e != cudaSuccess) return cuda_fail(e, "projection launch");
-    } else {
-      for (int bl = 0; bl < pl.Bs; ++bl) {
-        e = cudaMemsetAsync(KV + ((int64_t)bl * pl.Lk_pad + sp.L) * sp.kv_ld, 0,
-                            (size_t)(pl.Lk_pad - sp.L) * sp.kv_ld * 2, strm);
-        if (e != cudaSuccess) return cuda_fail(e, "kv padding");
-      }
+  if (!text && pl.Lk_pad > sp.L) {
+    for (int bl = 0; bl < pl.Bs; ++bl) {
+      e = cudaMemsetAsync(KV + ((int64_t)bl * pl.Lk_pad + sp.L) * sp.kv_ld, 0, (size_t)(pl.Lk_pad - sp.L) * sp.kv_ld * 2,
+                          strm);
+      if (e != cudaSuccess) return cuda_fail(e, "kv padding");
     }
   }
+  return NSA_OK;
+}
+
+nsa_status nsa_linear(const nsa_linear_desc* d, const void* A, const void* W, const float* bias, const float* gate,
+                      float* C, void* stream) {
+  if (!d) return fail(NSA_ERR_INVALID_ARGUMENT, "desc is NULL");
+  if (!A || !W || !C) return fail(NSA_ERR_INVALID_ARGUMENT, "A, W and C must be device pointers");
+  if (d->M < 1 || d->N < 1 || d->K < 1) return fail(NSA_ERR_INVALID_ARGUMENT, "M, N and K must be >= 1");
+  const int64_t ldc = d->ldc ? d->ldc : d->N;
+  if (d->K % 8 || d->lda < d->K || d->lda % 8)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "K and lda must be multiples of 8 with lda >= K");
+  if (d->N % 4 || ldc % 4 || d->cOff % 4 || d->gOff % 4 || d->cOff < 0 || d->gOff < 0 || ldc < d->cOff + d->N)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "N, ldc, cOff and gOff must be multiples of 4, with ldc >= cOff + N");
+  auto a16 = [](const void* ptr) { return ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  if (!a16(A) || !a16(W) || !a16(C) || !a16(bias) || !a16(gate))
+    return fail(NSA_ERR_INVALID_ARGUMENT, "pointers must be 16-byte aligned");
+  if (gate && !d->resid) return fail(NSA_ERR_INVALID_ARGUMENT, "a gate needs resid (C += gate * r)");
+  if (d->act != 0 && d->act != 1) return fail(NSA_ERR_INVALID_ARGUMENT, "act is 0 (none) or 1 (silu)");
+  int* err = nsa::device_error_word();
+  if (!err) return fail(NSA_ERR_CUDA, "cannot resolve the device error word on this device");
+  CUtensorMap ta, tw;
+  const cuuint64_t ad[2] = {(cuuint64_t)d->K, (cuuint64_t)d->M};
+  const cuuint64_t as[1] = {(cuuint64_t)d->lda * 2};
+  const cuuint32_t ab[2] = {64, 128};
+  const cuuint64_t wd[2] = {(cuuint64_t)d->K, (cuuint64_t)d->N};
+  const cuuint64_t ws[1] = {(cuuint64_t)d->K * 2};
+  const cuuint32_t wb[2] = {64, 256};
+  if (!encode_sw128(&ta, A, 2, ad, as, ab) || !encode_sw128(&tw, W, 2, wd, ws, wb))
+    return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the linear operands");
+  nsa::LinearParams p{};
+  p.M = d->M;
+  p.N = d->N;
+  p.k_steps = (d->K + 63) / 64;
+  p.m_tiles = (d->M + 127) / 128;
+  p.n_tiles = (d->N + 255) / 256;
+  p.alpha = d->alpha != 0.f ? d->alpha : 1.f;
+  p.bias = bias;
+  p.gate = gate ? gate + d->gOff : nullptr;
+  p.resid = d->resid ? 1 : 0;
+  p.act = d->act;
+  p.C = C + d->cOff;
+  p.ldc = ldc;
+  p.err = err;
+  p.timeout_ns = wait_timeout_ns();
+  const cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  const double flops = 2.0 * d->M * (double)d->N * d->K;
+  cudaError_t e = profiled("linear", flops, 0.0, strm, [&] { return nsa::launch_linear(p, ta, tw, strm); });
+  if (e == cudaErrorNotSupported) return fail(NSA_ERR_UNSUPPORTED, "N too large for the staged bias / gate");
+  if (e != cudaSuccess) return cuda_fail(e, "linear launch");
   return NSA_OK;
 }
 

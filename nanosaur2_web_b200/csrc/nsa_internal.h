@@ -127,26 +127,32 @@ cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream);
 // QKV projection GEMM with the prologue in its epilogue (proj.cu): rows of X [.][K] times W^T
 // ([N][K], q heads then k then v, or k then v for the text rows), + bias, then per head the q/k
 // RMSNorm and split-half RoPE, written straight into the sequence-shard layouts: q' tiles
-// [B][Hq][Lq_pad][D] and packed k'|v' rows [B][Lk_pad][2 Hkv D].  GEMM row r of batch element bl
-// is input row x_row0 + r, query row r (image rows) and key row key_row0 + r.
-struct ProjParams {
-  int B, b_begin;          // batch elements of the call and the first one's global index
-  int m_tiles, n_tiles;    // 128-row tiles per batch element, head-group tiles over N
-  int k_steps;             // 64-element slices of K
+// [B][Hq][Lq_pad][D] and packed k'|v' rows [B][Lk_pad][2 Hkv D].  One launch covers up to two row
+// sets (the image rows, then the text rows).  GEMM row r of set s and batch element bl is input row
+// x_row0 + r of that set's X, query row r (image rows) and key row key_row0 + r.
+struct ProjSet {
   int image;               // 1: q|k|v of the image rows; 0: k|v of the text rows
-  int Hq, Hkv;             // heads (whole model: sequence shards take whole heads)
+  int m_tiles, n_tiles;    // 128-row tiles per batch element, head-group tiles over N
   int rows;                // GEMM rows per batch element (Lq_pad or Lk_pad - L)
   int valid_q;             // image: query rows of the shard (rows past it are zeros in q')
   int key_row0;            // key index of GEMM row 0 (image: q_begin, text: L)
   int x_row0;              // input row of GEMM row 0
+  int rope_row0;           // RoPE table row of GEMM row 0 (image: q_begin)
+  const float* bias;       // [n_tiles * heads-per-tile * D] or null
+};
+struct ProjParams {
+  int B, b_begin;          // batch elements of the call and the first one's global index
+  int k_steps;             // 64-element slices of K
+  int Hq, Hkv;             // heads (whole model: sequence shards take whole heads)
   int Lk, Lq_pad, Lk_pad;  // keys; padded rows of q' and kv_packed
   int64_t kv_ld;           // elements per kv_packed row
-  const float* bias;       // [N] or null
+  int n_sets;              // 1 or 2
+  ProjSet set[2];
+  int stages;              // depth of the shared-memory ring (chosen to fit beside the bias vectors)
   const float* q_w;        // [D] q RMSNorm weight
   const float* k_w;        // [D] k RMSNorm weight
   const float* cs;         // RoPE table (image rows): cos [rows][D/2], sin at sin_off; null = none
   int64_t sin_off;
-  int rope_row0;           // RoPE table row of GEMM row 0 (image: q_begin)
   float eps;
   const int* kv_len;       // [B_total] valid keys, or null (Lk)
   __nv_bfloat16* q_prime;
@@ -156,11 +162,30 @@ struct ProjParams {
   int* err;
   unsigned long long timeout_ns;
 };
-// D in {64, 96, 128, 256}; cudaErrorInvalidValue otherwise.  tmX: 3-D map [B][rows][K] over the
-// input, box [1][128][64], 128-byte swizzle; tmW: 2-D map [N][K], box [heads-per-tile * D][64].
-cudaError_t launch_projection(const ProjParams& p, int D, const CUtensorMap& tmX, const CUtensorMap& tmW,
+// D in {64, 96, 128, 256}; cudaErrorInvalidValue otherwise, cudaErrorNotSupported when the bias
+// vectors leave no room for a 2-stage ring.  tmX[s]: 3-D map [B][rows][K] over set s's input, box
+// [1][128][64], 128-byte swizzle; tmW[s]: 2-D map [N][K], box [heads-per-tile * D][64].
+cudaError_t launch_projection(ProjParams p, int D, const CUtensorMap* tmX, const CUtensorMap* tmW,
                               cudaStream_t stream);
 int projection_heads_per_tile(int D);   // 0: unsupported head dim
+
+// Linear layer with the reference's GEMM epilogue (linear.cu): C = epilogue(alpha * A W^T) over M x N
+// with A [M][K] bf16 (tmA: 2-D map, box [128][64]), W [N][K] bf16 (tmW: box [256][64]), 128-byte
+// swizzle; r = alpha*acc (+ bias[n]) (silu if act == 1), then C[m][n] = r or, with resid,
+// C[m][n] += gate[n] * r (gate null: 1).  C is fp32 with row pitch ldc (already offset by cOff).
+struct LinearParams {
+  int M, N, k_steps, m_tiles, n_tiles;
+  float alpha;
+  const float* bias;   // [N] or null (16-byte aligned, N a multiple of 4)
+  const float* gate;   // [N] (offset by gOff) or null
+  int resid;
+  int act;             // 0 none, 1 silu
+  float* C;
+  int64_t ldc;
+  int* err;
+  unsigned long long timeout_ns;
+};
+cudaError_t launch_linear(const LinearParams& p, const CUtensorMap& tmA, const CUtensorMap& tmW, cudaStream_t stream);
 
 // Returns cudaErrorInvalidValue for unsupported head dims.
 cudaError_t launch_attention(const AttnParams& p, int D, const CUtensorMap& tmQ, const CUtensorMap& tmK,

@@ -13,8 +13,12 @@
 //   warp 0      TMA producer: X [128 rows][64] and W [heads*D rows][64] slices through a ring
 //   warp 1      TMEM allocator + MMA issuer (one thread): 128 x N x 16 tcgen05.mma into one of two
 //               accumulators, so the epilogue of a tile overlaps the main loop of the next
-//   warps 2-5   epilogue: thread = one output row (its TMEM lane); per head two passes over the
-//               accumulator columns: sum of squares, then bias + norm weight + RoPE, bf16 stores
+//   warps 2-9   epilogue, two groups of four warps (each group covers the 128 TMEM lanes, a thread
+//               one output row): group g takes heads g, g+2, ... of the tile (or half of the RoPE
+//               pairs when a tile holds one head).  Per head: sum of squares over the accumulator
+//               columns, then bias + norm weight + RoPE, bf16 stores.  Bias and norm weights sit in
+//               shared memory; at head dim <= 96 a thread loads its RoPE row into registers before it
+//               waits for the accumulator.
 #include "nsa_internal.h"
 #include "ptx.cuh"
 
@@ -23,7 +27,7 @@ namespace nsa {
 namespace {
 
 constexpr int kProjBK = 64;         // K elements per stage: one 128-byte swizzle row
-constexpr int kProjThreads = 192;
+constexpr int kProjThreads = 320;
 
 template <int D>
 struct ProjCfg {
@@ -32,11 +36,9 @@ struct ProjCfg {
   static constexpr int A_BYTES = 128 * kProjBK * 2;
   static constexpr int B_BYTES = NT * kProjBK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE;  // 5 at N = 192, 4 at N = 256
-  static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
   static constexpr uint32_t ACC_COLS = 256;            // TMEM columns per accumulator
   static constexpr uint32_t IDESC = idesc_bf16_f32(128, NT, 0, 0);
-  static_assert(NT % 16 == 0 && NT <= 256 && STAGE % 1024 == 0 && SMEM <= 232448, "projection tile");
+  static_assert(NT % 16 == 0 && NT <= 256 && STAGE % 1024 == 0, "projection tile");
 };
 
 __device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, const float (&v)[16]) {
@@ -50,17 +52,24 @@ __device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, const float (&
 
 template <int D>
 __global__ void __launch_bounds__(kProjThreads, 1)
-    proj_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, const ProjParams p) {
+    proj_kernel(const __grid_constant__ CUtensorMap tmX0, const __grid_constant__ CUtensorMap tmW0,
+                const __grid_constant__ CUtensorMap tmX1, const __grid_constant__ CUtensorMap tmW1, const ProjParams p) {
   using C = ProjCfg<D>;
-  constexpr int S = C::STAGES;
+  const int S = p.stages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::STAGE);
+  const int nb0 = p.set[0].n_tiles * C::NT, nb1 = p.n_sets > 1 ? p.set[1].n_tiles * C::NT : 0;
+  float* sbias0 = reinterpret_cast<float*>(smem + S * C::STAGE);   // [nb0] (zeros without a bias)
+  float* sbias1 = sbias0 + nb0;                                    // [nb1]
+  float* sqw = sbias1 + nb1;                                       // [D] q norm weight
+  float* skw = sqw + D;                                            // [D] k norm weight
+  uint64_t* full = reinterpret_cast<uint64_t*>(skw + D);           // 16-byte aligned (all sizes x 16 B)
   uint64_t* empty = full + S;
-  uint64_t* acc_full = empty + S;    // [2] accumulator ready for the epilogue
-  uint64_t* acc_empty = acc_full + 2;   // [2] accumulator read out (128 arrivals)
+  uint64_t* acc_full = empty + S;       // [2] accumulator ready for the epilogue
+  uint64_t* acc_empty = acc_full + 2;   // [2] accumulator read out (256 epilogue arrivals)
   uint64_t* drain = acc_empty + 2;      // MMAs of an aborted CTA finished
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* pbar = drain + 1;           // bias vectors and norm weights landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint64_t to = p.timeout_ns;
@@ -72,15 +81,12 @@ __global__ void __launch_bounds__(kProjThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 128);
+      mbar_init(&acc_empty[i], 256);
     }
     mbar_init(drain, 1);
+    mbar_init(pbar, 1);
     *abort_flag = 0;
     fence_mbar_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmX);
-    tma_prefetch_desc(&tmW);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -88,22 +94,31 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   }
   if (blockIdx.x == 0)
     for (int i = threadIdx.x; i < p.zero_count; i += blockDim.x) p.zero_ptr[i] = 0;
+  // a missing bias reads as zeros
+  if (!p.set[0].bias)
+    for (int i = threadIdx.x; i < nb0; i += blockDim.x) sbias0[i] = 0.f;
+  if (nb1 && !p.set[1].bias)
+    for (int i = threadIdx.x; i < nb1; i += blockDim.x) sbias1[i] = 0.f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  const int tiles = p.B * p.m_tiles * p.n_tiles;
+  const int tiles0 = p.B * p.set[0].m_tiles * p.set[0].n_tiles;
+  const int tiles = tiles0 + (p.n_sets > 1 ? p.B * p.set[1].m_tiles * p.set[1].n_tiles : 0);
   const int G = gridDim.x;
-  const int nt_q = p.image ? p.Hq / C::HPT : 0;
-  const int nt_kv = p.Hkv / C::HPT;
-  // tile u -> (local batch element, first row, N tile, part 0/1/2 = q/k/v, first head); false for
-  // image k / v tiles wholly past the shard's query rows (those keys belong to other shards)
-  auto decode = [&](int u, int& bl, int& m0, int& nt, int& part, int& h0) -> bool {
-    nt = u % p.n_tiles;
-    const int rest = u / p.n_tiles;
-    m0 = (rest % p.m_tiles) * 128;
-    bl = rest / p.m_tiles;
+  // tile u -> (row set, local batch element, first row, N tile, part 0/1/2 = q/k/v, first head);
+  // false for image k / v tiles wholly past the shard's query rows (other shards' keys)
+  auto decode = [&](int u, int& si, int& bl, int& m0, int& nt, int& part, int& h0) -> bool {
+    si = u < tiles0 ? 0 : 1;
+    if (si) u -= tiles0;
+    const ProjSet& q = p.set[si];
+    nt = u % q.n_tiles;
+    const int rest = u / q.n_tiles;
+    m0 = (rest % q.m_tiles) * 128;
+    bl = rest / q.m_tiles;
+    const int nt_q = q.image ? p.Hq / C::HPT : 0;
+    const int nt_kv = p.Hkv / C::HPT;
     if (nt < nt_q) {
       part = 0;
       h0 = nt * C::HPT;
@@ -114,17 +129,30 @@ __global__ void __launch_bounds__(kProjThreads, 1)
       part = 2;
       h0 = (nt - nt_q - nt_kv) * C::HPT;
     }
-    return !(p.image && part > 0 && m0 >= p.valid_q);
+    return !(q.image && part > 0 && m0 >= q.valid_q);
   };
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
+      tma_prefetch_desc(&tmX0);
+      tma_prefetch_desc(&tmW0);
+      if (p.n_sets > 1) {
+        tma_prefetch_desc(&tmX1);
+        tma_prefetch_desc(&tmW1);
+      }
+      // bias vectors and norm weights: one bulk copy each
+      const uint32_t b0 = p.set[0].bias ? (uint32_t)nb0 * 4 : 0u, b1 = (nb1 && p.set[1].bias) ? (uint32_t)nb1 * 4 : 0u;
+      mbar_arrive_expect_tx(pbar, b0 + b1 + 2u * D * 4);
+      if (b0) bulk_load(sbias0, p.set[0].bias, b0, pbar);
+      if (b1) bulk_load(sbias1, p.set[1].bias, b1, pbar);
+      bulk_load(sqw, p.q_w, D * 4, pbar);
+      bulk_load(skw, p.k_w, D * 4, pbar);
       int step = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < tiles; u += G) {
-        int bl, m0, nt, part, h0;
-        if (!decode(u, bl, m0, nt, part, h0)) continue;
+        int si, bl, m0, nt, part, h0;
+        if (!decode(u, si, bl, m0, nt, part, h0)) continue;
         for (int ks = 0; ks < p.k_steps; ++ks, ++step) {
           const int s = step % S;
           if (step >= S &&
@@ -134,11 +162,12 @@ __global__ void __launch_bounds__(kProjThreads, 1)
           }
           uint8_t* st = smem + s * C::STAGE;
           mbar_arrive_expect_tx(&full[s], C::STAGE);
-          tma_load_3d(st, &tmX, &full[s], ks * kProjBK, p.x_row0 + m0, bl);
-          tma_load_2d(st + C::A_BYTES, &tmW, &full[s], ks * kProjBK, nt * C::NT);
+          tma_load_3d(st, si ? &tmX1 : &tmX0, &full[s], ks * kProjBK, p.set[si].x_row0 + m0, bl);
+          tma_load_2d(st + C::A_BYTES, si ? &tmW1 : &tmW0, &full[s], ks * kProjBK, nt * C::NT);
         }
       }
-      // loads still landing complete before the CTA may exit
+      // copies still landing complete before the CTA may exit
+      wait_drain(pbar, 0, to);
       for (int i = step > S ? step - S : 0; i < step; ++i) wait_drain(&full[i % S], (i / S) & 1, to);
     }
   } else if (warp == 1) {
@@ -147,8 +176,8 @@ __global__ void __launch_bounds__(kProjThreads, 1)
       int step = 0, t = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < tiles; u += G) {
-        int bl, m0, nt, part, h0;
-        if (!decode(u, bl, m0, nt, part, h0)) continue;
+        int si, bl, m0, nt, part, h0;
+        if (!decode(u, si, bl, m0, nt, part, h0)) continue;
         const int a = t & 1;
         if (t >= 2 && !wait_bounded(&acc_empty[a], ((t >> 1) - 1) & 1, abort_flag, p.err, kErrTimeoutProjection, to)) {
           ok = false;
@@ -181,46 +210,74 @@ __global__ void __launch_bounds__(kProjThreads, 1)
       }
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2-5)
+    // ---------------------------------------------------------------- epilogue (warps 2-9)
+    const int ew = warp - 2;
+    const int group = ew / 4;
     const int quarter = warp % 4;   // TMEM lane quarter this warp may access
     const int row_local = quarter * 32 + lane;
+    // heads of the tile this group handles, and its range of RoPE pairs within a head
+    constexpr int HSTEP = C::HPT >= 2 ? 2 : 1;
+    const int pair0 = C::HPT >= 2 ? 0 : group * (D / 4);
+    const int pair1 = C::HPT >= 2 ? D / 2 : pair0 + D / 4;
+    const int hh0 = C::HPT >= 2 ? group : 0;
+    constexpr bool CS_REGS = D <= 96;   // the whole RoPE row fits in registers
+    bool params_ready = false;
     int t = 0;
     for (int u = blockIdx.x; u < tiles; u += G) {
-      int bl, m0, nt, part, h0;
-      if (!decode(u, bl, m0, nt, part, h0)) continue;
+      int si, bl, m0, nt, part, h0;
+      if (!decode(u, si, bl, m0, nt, part, h0)) continue;
+      const ProjSet& q = p.set[si];
       const int a = t & 1;
-      if (!__all_sync(0xffffffffu, wait_bounded(&acc_full[a], (t >> 1) & 1, abort_flag, p.err, kErrTimeoutProjection,
-                                                to)))
-        break;
-      tc_fence_after();
-      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)a * C::ACC_COLS;
       const int r = m0 + row_local;   // GEMM row
       const int b = p.b_begin + bl;
-      const int key = p.key_row0 + r;
+      const int key = q.key_row0 + r;
       const int kv_valid = p.kv_len ? min(p.kv_len[b], p.Lk) : p.Lk;
       // which rows exist in the destination, and which hold data (the rest are zeros)
       bool write, valid;
       if (part == 0) {
         write = r < p.Lq_pad;
-        valid = r < p.valid_q;
-      } else if (p.image) {
-        write = r < p.valid_q;   // other keys are other shards' (or the text rows)
+        valid = r < q.valid_q;
+      } else if (q.image) {
+        write = r < q.valid_q;   // other keys are other shards' (or the text rows)
         valid = write && key < kv_valid;
       } else {
         write = key < p.Lk_pad;
         valid = key < kv_valid;
       }
-      const float* w = part == 0 ? p.q_w : (part == 1 ? p.k_w : nullptr);
-      const bool rope = p.image && part < 2 && p.cs != nullptr;
-      const int rrow = p.rope_row0 + r;
+      const float* wn = part == 0 ? sqw : (part == 1 ? skw : nullptr);
+      const bool rope = q.image && part < 2 && p.cs != nullptr && valid;
+      const int rrow = q.rope_row0 + r;
+      // the RoPE row, loaded while the accumulator is still being computed
+      float rc[CS_REGS ? D / 2 : 1], rs[CS_REGS ? D / 2 : 1];
+      if constexpr (CS_REGS) {
+        if (rope) {
+          const float4* cp = reinterpret_cast<const float4*>(p.cs + (int64_t)rrow * (D / 2));
+          const float4* sp = reinterpret_cast<const float4*>(p.cs + p.sin_off + (int64_t)rrow * (D / 2));
+#pragma unroll
+          for (int q4 = 0; q4 < D / 8; ++q4) {
+            const float4 c4 = __ldg(cp + q4), s4 = __ldg(sp + q4);
+            rc[4 * q4] = c4.x; rc[4 * q4 + 1] = c4.y; rc[4 * q4 + 2] = c4.z; rc[4 * q4 + 3] = c4.w;
+            rs[4 * q4] = s4.x; rs[4 * q4 + 1] = s4.y; rs[4 * q4 + 2] = s4.z; rs[4 * q4 + 3] = s4.w;
+          }
+        }
+      }
+      bool got = wait_bounded(&acc_full[a], (t >> 1) & 1, abort_flag, p.err, kErrTimeoutProjection, to);
+      if (got && !params_ready) {
+        got = wait_bounded(pbar, 0, abort_flag, p.err, kErrTimeoutProjection, to);
+        params_ready = true;
+      }
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)a * C::ACC_COLS;
+      const float* sbias = si ? sbias1 : sbias0;
 #pragma unroll 1
-      for (int hh = 0; hh < C::HPT; ++hh) {
+      for (int hh = hh0; hh < C::HPT; hh += HSTEP) {
         const int h = h0 + hh;
         const uint32_t col0 = (uint32_t)(hh * D);
-        const float* bias = p.bias ? p.bias + nt * C::NT + hh * D : nullptr;
+        const float* bias = sbias + nt * C::NT + hh * D;
         // pass 1: sum of squares of (acc + bias) over the head (tcgen05.ld is warp-wide: every lane)
         float rn = 1.f;
-        if (w) {
+        if (wn) {
           float ss = 0.f;
 #pragma unroll 1
           for (int c = 0; c < D; c += 16) {
@@ -228,7 +285,7 @@ __global__ void __launch_bounds__(kProjThreads, 1)
             tmem_ld16(tbase + col0 + (uint32_t)c, v);
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const float x = __uint_as_float(v[i]) + (bias ? __ldg(bias + c + i) : 0.f);
+              const float x = __uint_as_float(v[i]) + bias[c + i];
               ss = fmaf(x, x, ss);
             }
           }
@@ -240,38 +297,49 @@ __global__ void __launch_bounds__(kProjThreads, 1)
         else
           dst = p.kv_packed + ((int64_t)bl * p.Lk_pad + key) * p.kv_ld + (part == 2 ? (int64_t)p.Hkv * D : 0) +
                 (int64_t)h * D;
-        // pass 2: pairs (i, i + D/2): bias, norm weight, RoPE, bf16
-#pragma unroll 1
+        // pass 2: pairs (i, i + D/2) of this group: bias, norm weight, RoPE, bf16
+#pragma unroll
         for (int c = 0; c < D / 2; c += 16) {
+          if (c < pair0 || c >= pair1) continue;
           uint32_t v1[16], v2[16];
           tmem_ld16(tbase + col0 + (uint32_t)c, v1);
           tmem_ld16(tbase + col0 + (uint32_t)(c + D / 2), v2);
           float x1[16], x2[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            x1[i] = __uint_as_float(v1[i]) + (bias ? __ldg(bias + c + i) : 0.f);
-            x2[i] = __uint_as_float(v2[i]) + (bias ? __ldg(bias + D / 2 + c + i) : 0.f);
+            x1[i] = __uint_as_float(v1[i]) + bias[c + i];
+            x2[i] = __uint_as_float(v2[i]) + bias[D / 2 + c + i];
           }
-          if (w) {
+          if (wn) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              x1[i] *= rn * __ldg(w + c + i);
-              x2[i] *= rn * __ldg(w + D / 2 + c + i);
+              x1[i] *= rn * wn[c + i];
+              x2[i] *= rn * wn[D / 2 + c + i];
             }
           }
-          if (rope && valid) {
-            const float4* cp = reinterpret_cast<const float4*>(p.cs + (int64_t)rrow * (D / 2) + c);
-            const float4* sp = reinterpret_cast<const float4*>(p.cs + p.sin_off + (int64_t)rrow * (D / 2) + c);
+          if (rope) {
+            float cc[16], sn[16];
+            if constexpr (CS_REGS) {
 #pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-              const float4 c4 = __ldg(cp + q4), s4 = __ldg(sp + q4);
-              const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float xa = x1[4 * q4 + e], xc = x2[4 * q4 + e];
-                x1[4 * q4 + e] = xa * cc[e] - xc * sn[e];
-                x2[4 * q4 + e] = xc * cc[e] + xa * sn[e];
+              for (int i = 0; i < 16; ++i) {
+                cc[i] = rc[c + i];
+                sn[i] = rs[c + i];
               }
+            } else {
+              const float4* cp = reinterpret_cast<const float4*>(p.cs + (int64_t)rrow * (D / 2) + c);
+              const float4* sp = reinterpret_cast<const float4*>(p.cs + p.sin_off + (int64_t)rrow * (D / 2) + c);
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4) {
+                const float4 c4 = __ldg(cp + q4), s4 = __ldg(sp + q4);
+                cc[4 * q4] = c4.x; cc[4 * q4 + 1] = c4.y; cc[4 * q4 + 2] = c4.z; cc[4 * q4 + 3] = c4.w;
+                sn[4 * q4] = s4.x; sn[4 * q4 + 1] = s4.y; sn[4 * q4 + 2] = s4.z; sn[4 * q4 + 3] = s4.w;
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float xa = x1[i], xc = x2[i];
+              x1[i] = xa * cc[i] - xc * sn[i];
+              x2[i] = xc * cc[i] + xa * sn[i];
             }
           }
           if (!valid) {
@@ -299,7 +367,7 @@ __global__ void __launch_bounds__(kProjThreads, 1)
 }
 
 template <int D>
-cudaError_t launch_proj_d(const ProjParams& p, const CUtensorMap& tmX, const CUtensorMap& tmW, cudaStream_t stream) {
+cudaError_t launch_proj_d(ProjParams p, const CUtensorMap* tmX, const CUtensorMap* tmW, cudaStream_t stream) {
   using C = ProjCfg<D>;
   static int sms = 0;
   if (!sms) {
@@ -308,13 +376,28 @@ cudaError_t launch_proj_d(const ProjParams& p, const CUtensorMap& tmX, const CUt
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (sms <= 0) sms = 148;
   }
-  const long long tiles = (long long)p.B * p.m_tiles * p.n_tiles;
+  long long tiles = 0;
+  size_t bias_bytes = 0;
+  for (int s = 0; s < p.n_sets; ++s) {
+    tiles += (long long)p.B * p.set[s].m_tiles * p.set[s].n_tiles;
+    bias_bytes += (size_t)p.set[s].n_tiles * C::NT * 4;
+  }
   if (tiles <= 0) return cudaSuccess;
   if (tiles > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(proj_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  // ring depth: as many stages (up to 5) as fit beside the bias vectors, the norm weights, the
+  // barriers and the alignment slack
+  const size_t fixed = 1024 + bias_bytes + 2 * D * 4 + 256;
+  const long long room = 232448 - (long long)fixed;
+  int stages = room > 0 ? (int)(room / C::STAGE) : 0;
+  if (stages > 5) stages = 5;
+  if (stages < 2) return cudaErrorNotSupported;
+  p.stages = stages;
+  const size_t smem = fixed + (size_t)stages * C::STAGE;
+  cudaError_t e = cudaFuncSetAttribute(proj_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int grid = tiles < sms ? (int)tiles : sms;
-  proj_kernel<D><<<grid, kProjThreads, C::SMEM, stream>>>(tmX, tmW, p);
+  proj_kernel<D><<<grid, kProjThreads, smem, stream>>>(tmX[0], tmW[0], tmX[p.n_sets > 1 ? 1 : 0],
+                                                       tmW[p.n_sets > 1 ? 1 : 0], p);
   return cudaGetLastError();
 }
 
@@ -330,7 +413,7 @@ int projection_heads_per_tile(int D) {
   }
 }
 
-cudaError_t launch_projection(const ProjParams& p, int D, const CUtensorMap& tmX, const CUtensorMap& tmW,
+cudaError_t launch_projection(ProjParams p, int D, const CUtensorMap* tmX, const CUtensorMap* tmW,
                               cudaStream_t stream) {
   switch (D) {
     case 64: return launch_proj_d<64>(p, tmX, tmW, stream);

@@ -101,6 +101,36 @@ def headNorm(X: torch.Tensor, weight: torch.Tensor, *, L: int, H: int, D: int, l
                                   float(eps), stream_handle(X.device)))
 
 
+def linear(x: torch.Tensor, W: torch.Tensor, *, bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+           resid: bool = False, gate: Optional[torch.Tensor] = None, gOff: int = 0, act: Optional[str] = None,
+           cOff: int = 0, alpha: float = 1.0) -> torch.Tensor:
+    """y = x @ W^T (+ bias) (silu), then out = y, out += y (resid) or out += gate[gOff + n] * y (resid + gate)
+    (app/gpu/ops.js:50-66 with the epilogue of app/gpu/gemm.js:155-165).  x [M, K] bf16 (row pitch
+    x.stride(0)), W [N, K] bf16 contiguous, out [M, ldc] fp32 written at columns cOff..cOff+N-1,
+    allocated [M, N] when not given."""
+    _require_cuda(x, W, bias, out, gate)
+    if x.dim() != 2 or x.dtype != torch.bfloat16 or x.stride(1) != 1 or W.dtype != torch.bfloat16:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "x must be [M, K] and W [N, K], both bf16 with unit inner stride")
+    if not W.is_contiguous():
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "W must be contiguous [N, K]")
+    M, K = x.shape
+    N = W.shape[0]
+    if out is None:
+        if resid:
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "resid needs out")
+        out = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    if out.dtype != torch.float32 or out.dim() != 2 or out.stride(1) != 1:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "out must be a float32 [M, ldc] tensor with unit inner stride")
+    d = _lib.LinearDesc()
+    d.M, d.N, d.K = M, N, K
+    d.lda, d.ldc, d.cOff, d.gOff = x.stride(0), out.stride(0), cOff, gOff
+    d.alpha, d.resid, d.act = alpha, int(bool(resid)), {None: 0, "none": 0, "silu": 1}[act]
+    with torch.cuda.device(x.device):
+        check(lib().nsa_linear(ctypes.byref(d), x.data_ptr(), W.data_ptr(), _ptr(bias), _ptr(gate), out.data_ptr(),
+                               stream_handle(x.device)))
+    return out
+
+
 def _bstride(t: torch.Tensor, rows_ld: int) -> int:
     return t.stride(0) if t.dim() == 3 else 0
 

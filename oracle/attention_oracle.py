@@ -38,6 +38,19 @@ def linear(x, w, b=None, acc=np.float32):
     return y + np.asarray(b, acc) if b is not None else y
 
 
+def linear_epilogue(y, out=None, gate=None, resid=False, act=None, acc=np.float32):
+    """The epilogue of the reference's tiled GEMM (app/gpu/gemm.js:155-165) after ``linear``:
+    silu when act == "silu", then out = y, out += y (resid) or out += gate * y (resid with a gate, the
+    DiT block's gated residual x + m[2] * lin(...), tools/reference.py:285)."""
+    y = np.asarray(y, acc)
+    if act == "silu":
+        y = y / (1.0 + np.exp(-y))
+    if not resid:
+        return y
+    g = 1.0 if gate is None else np.asarray(gate, acc)
+    return np.asarray(out, acc) + g * y
+
+
 # ----------------------------------------------------------------------------- prologue pieces
 
 def rms_norm(x, w, eps=1e-6, acc=np.float32):

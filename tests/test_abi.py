@@ -45,14 +45,16 @@ def test_struct_layouts_match_c(tmp_path):
                    'sizeof(nsa_kernel_stat), offsetof(nsa_kernel_stat, bytes), sizeof(nsa_seq_shard),'
                    'offsetof(nsa_seq_shard, qkv_text_row0));printf("%zu %zu %zu %zu\\n", sizeof(nsa_proj_desc),'
                    'offsetof(nsa_proj_desc, x_rows), offsetof(nsa_proj_desc, text_rows), offsetof(nsa_proj_desc, b_kv));'
-                   'return 0;}\n')
+                   'printf("%zu %zu %zu\\n", sizeof(nsa_linear_desc), offsetof(nsa_linear_desc, lda), '
+                   'offsetof(nsa_linear_desc, act));return 0;}\n')
     exe = tmp_path / "sizes"
     subprocess.run(["gcc", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)], check=True)
     got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
     want = [ctypes.sizeof(_lib.AttentionDesc), _lib.AttentionDesc.b_begin.offset, ctypes.sizeof(_lib.FusedDesc),
             _lib.FusedDesc.b_begin.offset, ctypes.sizeof(_lib.KernelStat), _lib.KernelStat.bytes.offset,
             ctypes.sizeof(_lib.SeqShard), _lib.SeqShard.qkv_text_row0.offset, ctypes.sizeof(_lib.ProjDesc),
-            _lib.ProjDesc.x_rows.offset, _lib.ProjDesc.text_rows.offset, _lib.ProjDesc.b_kv.offset]
+            _lib.ProjDesc.x_rows.offset, _lib.ProjDesc.text_rows.offset, _lib.ProjDesc.b_kv.offset,
+            ctypes.sizeof(_lib.LinearDesc), _lib.LinearDesc.lda.offset, _lib.LinearDesc.act.offset]
     assert got == want
 
 

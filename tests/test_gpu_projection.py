@@ -112,7 +112,7 @@ def test_projection_buffers_and_padding():
                          O.head_norm(qkv[L:n, C:2 * C], k_w, H, D, acc=np.float64)])
     v = qkv[:n, 2 * C:]
     q_pad = (L + 255) // 256 * 256
-    tiles = q_prime[0, :H * q_pad * D * 2].view(torch.bfloat16).view(H, q_pad, D).float().cpu().numpy()
+    tiles = q_prime[:H * q_pad * D * 2].view(torch.bfloat16).view(H, q_pad, D).float().cpu().numpy()
     got_q = tiles[:, :L].transpose(1, 0, 2).reshape(L, C)
     assert_close_bf16(got_q, qn, D, what="q' tiles")
     assert not tiles[:, L:].any(), "q' padding rows must be zero"
