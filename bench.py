@@ -642,16 +642,18 @@ def run_config5(args, rank, world, local_rank):
 
 
 def run_config6(args, rank, world, local_rank):
-    """Config 6 (the first "next" step of the path): one DiT block's attention step from the block input
-    with config 2's shapes: q|k|v = x W_qkv^T + b over the 3952 image rows and k|v = x_text W_kv^T + b
-    over the 256 text slots (K = 1536), q/k RMSNorm + 2D RoPE in the GEMM epilogue, then the joint
-    attention (blocks.dit_block_attention_projected).  Batch 2 per GPU (weak scaling, no collective).
-    The line also reports the same step unfused: cuBLAS bf16 linears (torch.matmul) writing qkv, then
-    the fused prologue + attention."""
+    """Config 6 (the "next" steps either side of the path): one DiT block's attention sublayer with
+    config 2's shapes, batch 2 per GPU (weak scaling, no collective):
+      q|k|v = x W_qkv^T + b over the 3952 image rows and k|v = x_text W_kv^T + b over the 256 text
+      slots (K = 1536), q/k RMSNorm + 2D RoPE in the GEMM epilogue, the joint attention
+      (blocks.dit_block_attention_projected), then the output projection with its gated residual
+      into the fp32 residual stream, x += gate * (a W_proj^T + b) (ops.linear, nanosaur2.js:210).
+    The line also reports the same sublayer unfused: cuBLAS bf16 linears (torch.addmm) writing qkv,
+    the fused prologue + attention, cuBLAS for the output projection and a torch gated add."""
     import torch
 
     from nanosaur2_web_b200.blocks import dit_block_attention, dit_block_attention_projected, projection_buffers
-    from nanosaur2_web_b200.ops import rope2dTable
+    from nanosaur2_web_b200.ops import linear, rope2dTable
     from nanosaur2_web_b200.sharding import sum_over_ranks
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -674,13 +676,18 @@ def run_config6(args, rank, world, local_rank):
     bufs = projection_buffers(B, L, LT, dev)
     out = torch.empty((B, L, C), dtype=torch.bfloat16, device=dev)
     qkv = torch.zeros((B, L + LT, 3 * C), dtype=torch.bfloat16, device=dev)
+    w_o = (torch.randn((C, C), device=dev) / math.sqrt(C)).to(torch.bfloat16)
+    b_o = 0.1 * torch.randn(C, device=dev)
+    mod = torch.randn(6 * C, device=dev)
+    resid = torch.randn((B, L, C), device=dev)   # the fp32 residual stream the sublayer adds into
 
     def step(i):
         x, xt, kv_len, bias, _ = sets[i % len(sets)]
         dit_block_attention_projected(x, w_qkv=w_qkv, b_qkv=b_qkv, q_norm=qn, k_norm=kn, cs=cs, x_text=xt,
                                       w_kv=w_kv, b_kv=b_kv, kv_len=kv_len, bias=bias, out=out, buffers=bufs)
+        linear(out.view(-1, C), w_o, bias=b_o, out=resid.view(-1, C), resid=True, gate=mod, gOff=2 * C)
 
-    b_qkv_h, b_kv_h = b_qkv.to(torch.bfloat16), b_kv.to(torch.bfloat16)
+    b_qkv_h, b_kv_h, b_o_h = b_qkv.to(torch.bfloat16), b_kv.to(torch.bfloat16), b_o.to(torch.bfloat16)
 
     def step_unfused(i):
         x, xt, kv_len, bias, _ = sets[i % len(sets)]
@@ -688,10 +695,12 @@ def run_config6(args, rank, world, local_rank):
             torch.addmm(b_qkv_h, x[b], w_qkv.T, out=qkv[b, :L])   # cuBLAS, bias in its epilogue
             qkv[b, L:, C:] = torch.addmm(b_kv_h, xt[b], w_kv.T)
         dit_block_attention(qkv, L=L, q_norm=qn, k_norm=kn, cs=cs, text_rows=LT, kv_len=kv_len, bias=bias, out=out)
+        y = torch.addmm(b_o_h, out.view(-1, C), w_o.T)                  # cuBLAS
+        resid.view(-1, C).addcmul_(y.float(), mod[2 * C:3 * C])          # x += gate * y
 
     def step_flops(i):
         lv = sets[i % len(sets)][4]
-        return 2.0 * B * K * (L * 3 * C + LT * 2 * C) + joint_flops(B, L, lv)
+        return 2.0 * B * K * (L * 3 * C + LT * 2 * C) + joint_flops(B, L, lv) + 2.0 * B * L * C * C
 
     stream = torch.cuda.current_stream(dev)
     with ClockSampler(local_rank) as clocks:
@@ -707,14 +716,19 @@ def run_config6(args, rank, world, local_rank):
     roof = _roofline(kst, "attn_fwd_kernel<96>")
     roof["projection"] = {"kernel": "proj_kernel<96>", "achieved": proj_tf, "peak": peak, "unit": "TFLOP/s",
                           "frac": proj_tf / peak, "ms_per_step": pms / min(args.steps, 3)}
-    cfg = {"workload": "config 6: DiT block attention step from the block input, config 2 shapes (52x76=3952 image "
-                       "tokens + 256 text slots, batch 2, K=1536): qkv_x / kv_y linears with q/k RMSNorm + 2D RoPE "
-                       "in the GEMM epilogue, then joint attention",
+    ll, lms, lfl, _ = kst["linear"]
+    roof["output_projection"] = {"kernel": "linear_kernel", "achieved": lfl / (lms * 1e-3) / 1e12, "peak": peak,
+                                 "unit": "TFLOP/s", "frac": lfl / (lms * 1e-3) / 1e12 / peak,
+                                 "ms_per_step": lms / min(args.steps, 3)}
+    cfg = {"workload": "config 6: DiT block attention sublayer from the block input, config 2 shapes (52x76=3952 "
+                       "image tokens + 256 text slots, batch 2, K=1536): qkv_x / kv_y linears with q/k RMSNorm + 2D "
+                       "RoPE in the GEMM epilogue, joint attention, output projection with the gated residual",
            "global_batch": B * world, "seq_len": L, "parallelism": f"dp{world}",
            "l2": "six 26 MB block inputs rotate (156 MB > 126 MB L2)",
-           "flops_note": "2*B*K*(3952*4608 + 256*3072) linear + 4*B*H*valid pairs*D attention"}
+           "flops_note": "2*B*K*(3952*4608 + 256*3072) qkv linears + 4*B*H*valid pairs*D attention + "
+                         "2*B*3952*1536*1536 output projection"}
     print(json.dumps(_line(args, world, flops / (ms * 1e-3) / 1e12, ms, cfg, roof, clocks.summary(),
-                           4 * B * args.steps, "weak", unfused_ms_per_step=ms_unfused / args.steps)), flush=True)
+                           3 * args.steps, "weak", unfused_ms_per_step=ms_unfused / args.steps)), flush=True)
 
 
 def run_profile(args, local_rank):

@@ -147,3 +147,61 @@ def test_seq_shard_sizes_and_validation():
     assert L.nsa_seq_shard_prologue(ctypes.byref(d), ctypes.byref(s), fake, fake, fake, None, None, fake + 8, fake,
                                     None) == _lib.NSA_ERR_INVALID_ARGUMENT   # q_prime not 16-byte aligned
     assert L.nsa_seq_shard_buffer_sizes(None, ctypes.byref(s), None, None, None) == _lib.NSA_ERR_INVALID_ARGUMENT
+
+
+def test_projection_and_linear_validation():
+    """Argument checks of nsa_seq_shard_projection and nsa_linear (no device work: each case fails
+    before any CUDA call)."""
+    L = _lib.lib()
+    fake = 0x10000   # never dereferenced
+    d = _lib.FusedDesc()
+    d.B, d.Lq, d.Lk, d.Hq, d.Hkv, d.D = 2, 3952, 4208, 16, 16, 96
+    d.in_dtype = d.out_dtype = _lib.NSA_BF16
+    s = _lib.SeqShard(0, 3952, 0, 0)
+    p = _lib.ProjDesc()
+    p.K, p.x, p.ldx, p.x_bstride, p.x_rows, p.w_qkv = 1536, fake, 1536, 3952 * 1536, 3952, fake
+    p.x_text, p.ld_text, p.text_bstride, p.text_rows, p.w_kv = fake, 1536, 256 * 1536, 256, fake
+
+    def proj(q_prime=fake):
+        return L.nsa_seq_shard_projection(ctypes.byref(d), ctypes.byref(s), ctypes.byref(p), fake, fake, None, None,
+                                          q_prime, fake, None)
+    assert L.nsa_seq_shard_projection(ctypes.byref(d), ctypes.byref(s), None, fake, fake, None, None, fake, fake,
+                                      None) == _lib.NSA_ERR_INVALID_ARGUMENT            # no proj desc
+    assert proj(q_prime=fake + 8) == _lib.NSA_ERR_INVALID_ARGUMENT                         # unaligned output
+    p.K = 1540
+    assert proj() == _lib.NSA_ERR_INVALID_ARGUMENT                                          # K not a multiple of 8
+    p.K = 1536
+    p.x_text = None
+    assert proj() == _lib.NSA_ERR_INVALID_ARGUMENT                                          # text keys need x_text
+    p.x_text = fake
+    p.text_rows = 100
+    assert proj() == _lib.NSA_ERR_INVALID_ARGUMENT                                          # text rows past x_text
+    p.text_rows = 256
+    d.Hq = d.Hkv = 15
+    assert proj() == _lib.NSA_ERR_UNSUPPORTED                                               # heads not whole tiles
+    d.Hq = d.Hkv = 16
+    d.in_dtype = _lib.NSA_F32
+    assert proj() == _lib.NSA_ERR_UNSUPPORTED                                               # bf16 inputs only
+    d.in_dtype = _lib.NSA_BF16
+    d.causal = 1
+    assert proj() == _lib.NSA_ERR_UNSUPPORTED                                               # sequence layouts: no mask
+    d.causal = 0
+
+    ld = _lib.LinearDesc()
+    ld.M, ld.N, ld.K, ld.lda = 3952, 1536, 1536, 1536
+
+    def lin(bias=None, gate=None):
+        return L.nsa_linear(ctypes.byref(ld), fake, fake, bias, gate, fake, None)
+    assert L.nsa_linear(None, fake, fake, None, None, fake, None) == _lib.NSA_ERR_INVALID_ARGUMENT
+    ld.N = 1538
+    assert lin() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # N not a multiple of 4
+    ld.N, ld.lda = 1536, 1000
+    assert lin() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # lda < K
+    ld.lda = 1536
+    assert lin(gate=fake) == _lib.NSA_ERR_INVALID_ARGUMENT                                  # a gate needs resid
+    ld.resid, ld.gOff = 1, 2
+    assert lin(gate=fake) == _lib.NSA_ERR_INVALID_ARGUMENT                                  # gOff not a multiple of 4
+    ld.gOff, ld.act = 0, 3
+    assert lin() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # act 0 or 1
+    ld.act = 0
+    assert lin(bias=fake + 4) == _lib.NSA_ERR_INVALID_ARGUMENT                              # unaligned bias
