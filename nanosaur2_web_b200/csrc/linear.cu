@@ -9,8 +9,9 @@
 //   warp 0      TMA producer: A [128 rows][64] and W [256 rows][64] slices, 4-stage ring
 //   warp 1      TMEM allocator + MMA issuer: 128 x 256 x 16 tcgen05.mma into one of two accumulators
 //   warps 2-9   epilogue, two groups of four warps, each group half of the tile's columns; a thread
-//               owns one output row: alpha, bias, silu, then the store / residual / gated residual
-//               with 16-byte fp32 accesses of C.  Bias and gate are bulk-copied into shared memory.
+//               owns one output row: alpha, bias, silu, then the store (16-byte stores) or the
+//               residual / gated residual (16-byte fp32 vector reductions into C).  Bias and gate are
+//               bulk-copied into shared memory.
 #include "nsa_internal.h"
 #include "ptx.cuh"
 
@@ -176,23 +177,25 @@ __global__ void __launch_bounds__(kLinThreads, 1)
           if (p.act == 1) x = silu(x);
           y[i] = x;
         }
+        // The residual forms add into C with vector reductions (each element has one owner, so this is
+        // the in-place C += g * r of the reference without a load round trip per chunk).
         if (n + 16 <= p.N) {
           float4* dst = reinterpret_cast<float4*>(crow + n);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            float4 o = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
-            if (p.resid) {
-              const float4 old = dst[q];
-              o.x = old.x + sgate[n + 4 * q] * o.x;
-              o.y = old.y + sgate[n + 4 * q + 1] * o.y;
-              o.z = old.z + sgate[n + 4 * q + 2] * o.z;
-              o.w = old.w + sgate[n + 4 * q + 3] * o.w;
-            }
-            dst[q] = o;
+            if (p.resid)
+              atomicAdd(dst + q, make_float4(sgate[n + 4 * q] * y[4 * q], sgate[n + 4 * q + 1] * y[4 * q + 1],
+                                             sgate[n + 4 * q + 2] * y[4 * q + 2], sgate[n + 4 * q + 3] * y[4 * q + 3]));
+            else
+              dst[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
           }
         } else {
-          for (int i = 0; i < 16 && n + i < p.N; ++i)
-            crow[n + i] = p.resid ? crow[n + i] + sgate[n + i] * y[i] : y[i];
+          for (int i = 0; i < 16 && n + i < p.N; ++i) {
+            if (p.resid)
+              atomicAdd(crow + n + i, sgate[n + i] * y[i]);
+            else
+              crow[n + i] = y[i];
+          }
         }
       }
       tc_fence_before();
