@@ -29,7 +29,7 @@ from typing import List, Optional, Tuple
 import torch
 
 from . import _lib
-from ._lib import FusedDesc, NsaError, SeqShard, check, lib
+from ._lib import FusedDesc, NsaError, ProjDesc, SeqShard, check, lib
 from .blocks import DIT_HEAD_DIM, DIT_HEADS
 from .ops import RopeTable, dtype_code
 
@@ -195,6 +195,31 @@ class SeqShardedJointAttention:
             ctypes.byref(d), ctypes.byref(self.shard), qkv.data_ptr(), q_norm.data_ptr(), k_norm.data_ptr(),
             cs.buf.data_ptr() if cs is not None else None, kv_len.data_ptr(), self.q_prime[b].data_ptr(),
             self.kv_packed[b].data_ptr(), peers, len(mine), torch.cuda.current_stream(self.device).cuda_stream))
+
+    def projection(self, b: int, x: torch.Tensor, *, w_qkv: torch.Tensor, b_qkv: Optional[torch.Tensor],
+                   q_norm: torch.Tensor, k_norm: torch.Tensor, cs: Optional[RopeTable], kv_len: torch.Tensor,
+                   x_text: Optional[torch.Tensor] = None, w_kv: Optional[torch.Tensor] = None,
+                   b_kv: Optional[torch.Tensor] = None) -> None:
+        """Step 1 from the block input for element b (nsa_seq_shard_projection): q|k|v = x W_qkv^T + b
+        over the rank's image rows and k|v = x_text W_kv^T + b over the text rows, normalised and
+        rotated in the GEMM epilogue; writes the same q' and k'|v' rows as ``prologue``.  x [B, rows, K]
+        bf16 holds the rank's image rows (``local_qkv``) or all L of them; x_text [B, text_rows, K]."""
+        if x.dim() != 3 or x.dtype != torch.bfloat16 or x.stride(-1) != 1:
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "x must be a bf16 [B, rows, K] tensor with unit stride")
+        d = self._desc(b, 1, None, None, cs, None)
+        s = SeqShard(self.q_begin, self.q_count, 0 if self.local_qkv else self.q_begin, 0)
+        p = ProjDesc()
+        p.K = x.shape[2]
+        p.x, p.ldx, p.x_bstride, p.x_rows = x.data_ptr(), x.stride(1), x.stride(0), x.shape[1]
+        p.w_qkv, p.b_qkv = w_qkv.data_ptr(), None if b_qkv is None else b_qkv.data_ptr()
+        if x_text is not None:
+            p.x_text, p.ld_text, p.text_bstride = x_text.data_ptr(), x_text.stride(1), x_text.stride(0)
+            p.text_rows = x_text.shape[1]
+            p.w_kv, p.b_kv = w_kv.data_ptr(), None if b_kv is None else b_kv.data_ptr()
+        check(lib().nsa_seq_shard_projection(
+            ctypes.byref(d), ctypes.byref(s), ctypes.byref(p), q_norm.data_ptr(), k_norm.data_ptr(),
+            cs.buf.data_ptr() if cs is not None else None, kv_len.data_ptr(), self.q_prime[b].data_ptr(),
+            self.kv_packed[b].data_ptr(), torch.cuda.current_stream(self.device).cuda_stream))
 
     def gather(self, b: int) -> None:
         """Step 2 for element b on the current stream: the in-place all-gather of the image rows."""

@@ -159,3 +159,46 @@ def test_projected_matches_fused_at_config2():
                               text_rows=Lt, kv_len=t(L + lv, torch.int32), bias=t(bias), out_dtype=torch.bfloat16)
     check_device()
     assert_close_bf16(got.float().cpu().numpy(), ref.float().cpu().numpy(), D, what="projected vs fused")
+
+
+@pytest.mark.parametrize("world,local", [(2, True), (3, False)])
+def test_sequence_sharded_projection(world, local):
+    """Each emulated rank projects its own image rows (x holding only them, or all L rows) and every
+    text row into one shared kv_packed, then runs its queries: the stitched output matches the
+    one-GPU projected step to the bf16 rounding of P (a short last wave splits units differently)
+    and the oracle within the bf16 bound.  A key row no rank writes would poison every query."""
+    from nanosaur2_web_b200.ops import rope2dTable
+    from nanosaur2_web_b200.seqshard import SeqShardedJointAttention
+    h, wd, Lt = 12, 20, 64
+    L = h * wd
+    B = 2
+    x, w, b, xt, wkv, bkv, q_w, k_w, lv, bias = proj_inputs(321 + world, B, L, Lt, 1536, (10, 64))
+    full = run_projected(x, w, b, xt, wkv, bkv, q_w, k_w, lv, bias, h, wd).cpu().numpy()
+    cs = rope2dTable(h, wd, D, DEV)
+    xd, xtd = t(x, torch.bfloat16), t(xt, torch.bfloat16)
+    wqd, wkvd, bd, bkvd = t(w, torch.bfloat16), t(wkv, torch.bfloat16), t(b), t(bkv)
+    kv_len, bias_d = t(L + lv, torch.int32), t(bias)
+    ranks, shared = [], None
+    for r in range(world):
+        m = SeqShardedJointAttention(B=B, L=L, text_rows=Lt, world=world, rank=r, device=DEV, local_qkv=local,
+                                     kv_packed=shared, out_dtype=torch.float32, mode="nccl")
+        shared = m.kv_packed
+        ranks.append(m)
+    shared.fill_(float("nan"))
+    for m in ranks:
+        src = xd[:, m.q_begin:m.q_begin + m.q_count].contiguous() if local else xd
+        for bb in range(B):
+            m.projection(bb, src, w_qkv=wqd, b_qkv=bd, q_norm=t(q_w), k_norm=t(k_w), cs=cs, kv_len=kv_len,
+                         x_text=xtd, w_kv=wkvd, b_kv=bkvd)
+    out = torch.full((B, L, C), float("nan"), device=DEV)
+    for m in ranks:
+        view = out[:, m.q_begin:m.q_begin + m.q_count]
+        for bb in range(B):
+            m.attention(bb, kv_len=kv_len, bias=bias_d, out=view)
+    check_device()
+    got = out.cpu().numpy()
+    np.testing.assert_allclose(got, full, atol=2e-3, rtol=0)
+    cos, sin = O.rope_2d(h, wd)
+    want = O.joint_attention_batched(oracle_qkv(x, w, b, xt, wkv, bkv), L, Lt, L + lv, q_w, k_w, cos, sin, bias=bias,
+                                     acc=np.float64)
+    assert_close_bf16(got, want, D, what=f"sequence-sharded projection x{world}")
