@@ -731,6 +731,79 @@ def run_config6(args, rank, world, local_rank):
                            3 * args.steps, "weak", unfused_ms_per_step=ms_unfused / args.steps)), flush=True)
 
 
+def run_config7(args, rank, world, local_rank):
+    """Config 7 (Gemma's side of the "next" steps): the Gemma3-270M text encoder's 18 attention layers of
+    config 4 (batch 16 x 1024 tokens, GQA 4/1, head dim 256, causal; 15 local layers with a 512-key
+    window, 3 global) from each layer's normalised input rows: the te.qkv linear (K = 640, no bias)
+    with the q/k RMSNorm and 1D RoPE in the GEMM epilogue, then the attention over the prepared tiles
+    (blocks.gemma_layer_attention_projected).  Batch-sharded over the ranks (strong scaling).  The
+    line also reports the unfused form: cuBLAS writes qkv, then the fused prologue + attention."""
+    import torch
+
+    from nanosaur2_web_b200.blocks import (GEMMA_HEAD_DIM, GEMMA_HEADS, gemma_layer_attention,
+                                           gemma_layer_attention_projected, gemma_projection_buffers,
+                                           gemma_rope_theta)
+    from nanosaur2_web_b200.ops import ropeTable
+    from nanosaur2_web_b200.sharding import split_range, sum_over_ranks
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, L, LAYERS, WINDOW, K = 16, 1024, 18, 512, 640
+    b0, b1 = split_range(B, world, rank)
+    nb = b1 - b0
+    g = torch.Generator(device=dev).manual_seed(7000 + rank)
+    xs = [torch.randn((nb, L, K), device=dev, generator=g).to(torch.bfloat16) for _ in range(6)]   # 6 x 21 MB
+    ws = [(torch.randn((6 * GEMMA_HEAD_DIM, K), device=dev, generator=g) / math.sqrt(K)).to(torch.bfloat16)
+          for _ in range(3)]
+    qn = 1.0 + 0.2 * torch.randn(GEMMA_HEAD_DIM, device=dev, generator=g)
+    kn = 1.0 + 0.2 * torch.randn(GEMMA_HEAD_DIM, device=dev, generator=g)
+    tables = {th: ropeTable(L, GEMMA_HEAD_DIM, th, dev) for th in (1e4, 1e6)}
+    out = torch.empty((nb, L, GEMMA_HEADS * GEMMA_HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    qkv = torch.empty((nb, L, 6 * GEMMA_HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    bufs = gemma_projection_buffers(nb, L, dev)
+
+    def step(i):
+        for layer in range(LAYERS):
+            th = gemma_rope_theta(layer)
+            n = i * LAYERS + layer
+            gemma_layer_attention_projected(xs[n % 6], w_qkv=ws[n % 3], q_norm=qn, k_norm=kn, cs=tables[th],
+                                            window=0 if th == 1e6 else WINDOW, out=out, buffers=bufs)
+
+    def step_unfused(i):
+        for layer in range(LAYERS):
+            th = gemma_rope_theta(layer)
+            n = i * LAYERS + layer
+            torch.matmul(xs[n % 6], ws[n % 3].T, out=qkv)   # cuBLAS
+            gemma_layer_attention(qkv, q_norm=qn, k_norm=kn, cs=tables[th], window=0 if th == 1e6 else WINDOW,
+                                  out=out)
+
+    per_elem_attn = sum(4.0 * GEMMA_HEADS * gemma_pairs(L, 0 if gemma_rope_theta(i) == 1e6 else WINDOW) *
+                        GEMMA_HEAD_DIM for i in range(LAYERS))
+    per_elem_lin = LAYERS * 2.0 * L * K * 6 * GEMMA_HEAD_DIM
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(local_rank) as clocks:
+        ms = _timed(step, args.steps, args.warmup, world, stream)
+    ms_unfused = _timed(step_unfused, args.steps, args.warmup, world, stream)
+    flops = sum_over_ranks((per_elem_attn + per_elem_lin) * nb * args.steps)
+    kst = _kernel_stats(step, min(args.steps, 3))
+    if rank != 0:
+        return
+    roof = _roofline(kst, "attn_persist_kernel")
+    pl_, pms, pfl, _ = kst["projection"]
+    peak, _src = measured_peak()
+    roof["projection"] = {"kernel": "proj_kernel<256>", "achieved": pfl / (pms * 1e-3) / 1e12, "peak": peak,
+                          "unit": "TFLOP/s", "frac": pfl / (pms * 1e-3) / 1e12 / peak,
+                          "ms_per_step": pms / min(args.steps, 3)}
+    cfg = {"workload": "config 7: Gemma3-270M text encoder, 18 layers of config 4 (B=16 x 1024, GQA 4/1, head dim "
+                       "256, causal, 15 local window 512 + 3 global) from the normalised layer input: te.qkv linear "
+                       "(K=640) with q/k RMSNorm + 1D RoPE in the GEMM epilogue, then attention",
+           "global_batch": B, "seq_len": L, "layers": LAYERS, "parallelism": f"batch-sharded x{world}",
+           "l2": "six 21 MB layer inputs and three weights rotate",
+           "flops_note": "18 * (2*L*640*1536 linear + 4*Hq*valid pairs*256 attention) per element"}
+    print(json.dumps(_line(args, world, flops / (ms * 1e-3) / 1e12, ms, cfg, roof, clocks.summary(),
+                           2 * LAYERS * args.steps, "strong", unfused_ms_per_step=ms_unfused / args.steps)),
+          flush=True)
+
+
 def run_profile(args, local_rank):
     """Small driver for ncu captures: the same fused call as the benchmark on ``--batch`` elements of
     config 2, ``--warmup`` + ``--steps`` launches of each kernel, nothing else on the GPU."""
@@ -772,9 +845,10 @@ def main():
     ap.add_argument("--seq-mode", choices=["auto", "nccl", "p2p", "ce"], default="auto",
                     help="config 5: k'|v' exchange by NCCL all-gather, peer stores from the prologue, or "
                          "copy-engine pushes")
-    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5, 6], default=2,
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5, 6, 7], default=2,
                     help="BASELINE config to run (2 = the headline line; 3, 4, 5 print their own line; 6 = the "
-                         "config-2 block step from the block input, QKV projection fused with the prologue)")
+                         "config-2 block step from the block input, QKV projection fused with the prologue; 7 = "
+                         "config 4's Gemma layers from the layer input)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -797,7 +871,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5, 6: run_config6}[args.config](
+        {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5, 6: run_config6, 7: run_config7}[args.config](
             args, rank, world, local_rank)
     finally:
         if world > 1:

@@ -168,8 +168,9 @@ nsa_status nsa_fused_attention_noalloc(const nsa_fused_desc* desc, const void* q
  * that overlaps the gather of element b with the attention of element b-1 calls each step with
  * b_count = 1 and pointers advanced by one element.
  * The descriptor is that of nsa_fused_attention (Lq = image rows, Lk = image + text rows,
- * kv_len[b] = valid keys of element b), with whole heads (h_begin 0, h_count 0 or Hq) and no causal
- * mask or window.  out receives the rank's rows: out[b*o_bstride + i*ldo + oOff + h*D + d] for
+ * kv_len[b] = valid keys of element b), with whole heads (h_begin 0, h_count 0 or Hq); a causal
+ * mask or window only with the full-sequence shard {0, Lq, ., .} (one GPU, e.g. a Gemma layer
+ * through nsa_seq_shard_projection).  out receives the rank's rows: out[b*o_bstride + i*ldo + oOff + h*D + d] for
  * local row i = global row q_begin + i.
  * ------------------------------------------------------------------------------------------------ */
 typedef struct nsa_seq_shard {

@@ -13,6 +13,9 @@
   272, 282) as one tcgen05 GEMM per row set whose epilogue applies the bias, the q/k RMSNorm and the
   RoPE and writes the attention's inputs (nsa_seq_shard_projection), then the attention
   (nsa_seq_shard_attention).
+* ``gemma_layer_attention_projected(...)``: the Gemma layer's attention from its normalised input
+  rows: the ``te.qkv`` linear with the q/k norms and RoPE in the GEMM epilogue, then the causal
+  attention over the prepared tiles.
 * ``gemma_layer_attention(...)``: one Gemma3 layer's attention, headNorm(q), headNorm(k) with the
   local/global RoPE table + causal GQA 4/1 attention (app/models/gemma3.js:63-70;
   tools/reference.py:186-194), with an optional sliding window.
@@ -202,6 +205,66 @@ def dit_block_attention_projected(x: torch.Tensor, *, w_qkv: torch.Tensor, b_qkv
         check(L_.nsa_seq_shard_attention(ctypes.byref(d), ctypes.byref(s), q_prime.data_ptr(), kv_packed.data_ptr(),
                                          None if kv_len is None else kv_len.data_ptr(),
                                          None if bias is None else bias.data_ptr(), out.data_ptr(), stream))
+    return out
+
+
+def gemma_projection_buffers(B: int, L: int, device) -> Tuple[torch.Tensor, torch.Tensor]:
+    """q_prime (uint8) and kv_packed [B, kv_rows, 2*256] (bf16) of a Gemma layer from its input rows."""
+    d = FusedDesc()
+    d.B, d.Lq, d.Lk, d.Hq, d.Hkv, d.D = B, L, L, GEMMA_HEADS, GEMMA_KV_HEADS, GEMMA_HEAD_DIM
+    d.in_dtype = d.out_dtype = _lib.NSA_BF16
+    d.causal = 1
+    d.b_begin, d.b_count = 0, B
+    s = SeqShard(0, L, 0, 0)
+    qb, kb, rows = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_int32()
+    check(lib().nsa_seq_shard_buffer_sizes(ctypes.byref(d), ctypes.byref(s), ctypes.byref(qb), ctypes.byref(kb),
+                                           ctypes.byref(rows)))
+    return (torch.empty(qb.value, dtype=torch.uint8, device=device),
+            torch.empty((B, rows.value, 2 * GEMMA_KV_HEADS * GEMMA_HEAD_DIM), dtype=torch.bfloat16, device=device))
+
+
+def gemma_layer_attention_projected(x: torch.Tensor, *, w_qkv: torch.Tensor, q_norm: torch.Tensor,
+                                    k_norm: torch.Tensor, cs: RopeTable, window: int = 0, eps: float = 1e-6,
+                                    out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                                    buffers: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
+    """One Gemma3 layer's attention from the layer's normalised input rows (app/models/gemma3.js:62-70):
+    qkv = h W_qkv^T (``te.qkv``, no bias; W_qkv [(4 + 2) * 256, K] bf16, rows q heads then k then v)
+    as one tcgen05 GEMM whose epilogue applies the q/k RMSNorm and the layer's 1D RoPE
+    (nsa_seq_shard_projection), then causal GQA 4/1 attention with an optional sliding window over
+    the prepared tiles (nsa_seq_shard_attention with the full-sequence shard).  x [B, L, K] bf16.
+    ``buffers`` = gemma_projection_buffers(B, L, device), to reuse.  Returns [B, L, 1024]."""
+    tensors = (x, w_qkv, q_norm, k_norm, out)
+    if any(t is not None and not t.is_cuda for t in tensors):
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "tensors must live on a CUDA device")
+    if x.dim() != 3 or x.stride(-1) != 1 or x.dtype != torch.bfloat16 or not w_qkv.is_contiguous():
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "x must be bf16 [B, L, K] with contiguous rows, w_qkv contiguous")
+    B, L, K = x.shape
+    H, KH, D = GEMMA_HEADS, GEMMA_KV_HEADS, GEMMA_HEAD_DIM
+    if out is None:
+        out = torch.empty((B, L, H * D), dtype=out_dtype or torch.bfloat16, device=x.device)
+    d = FusedDesc()
+    d.B, d.Lq, d.Lk, d.Hq, d.Hkv, d.D = B, L, L, H, KH, D
+    d.qOff, d.kOff, d.vOff = 0, H * D, (H + KH) * D
+    d.in_dtype, d.out_dtype = _lib.NSA_BF16, dtype_code(out)
+    d.ldo, d.o_bstride, d.oOff = out.stride(1), out.stride(0), 0
+    d.eps = eps
+    d.sinOff = cs.sinOff
+    d.causal, d.window = 1, window
+    d.b_begin, d.b_count = 0, B
+    s = SeqShard(0, L, 0, 0)
+    L_ = lib()
+    q_prime, kv_packed = buffers if buffers is not None else gemma_projection_buffers(B, L, x.device)
+    p = ProjDesc()
+    p.K = K
+    p.x, p.ldx, p.x_bstride, p.x_rows = x.data_ptr(), x.stride(1), x.stride(0), L
+    p.w_qkv = w_qkv.data_ptr()
+    with torch.cuda.device(x.device):
+        stream = stream_handle(x.device)
+        check(L_.nsa_seq_shard_projection(ctypes.byref(d), ctypes.byref(s), ctypes.byref(p), q_norm.data_ptr(),
+                                          k_norm.data_ptr(), cs.buf.data_ptr(), None, q_prime.data_ptr(),
+                                          kv_packed.data_ptr(), stream))
+        check(L_.nsa_seq_shard_attention(ctypes.byref(d), ctypes.byref(s), q_prime.data_ptr(), kv_packed.data_ptr(),
+                                         None, None, out.data_ptr(), stream))
     return out
 
 

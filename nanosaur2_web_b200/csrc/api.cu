@@ -439,8 +439,10 @@ nsa_status make_seq_plan(const nsa_fused_desc* d, const nsa_seq_shard* s, SeqPla
   if (!d || !s) return fail(NSA_ERR_INVALID_ARGUMENT, "desc and shard must not be NULL");
   if (d->Hkv < 1 || d->Hq % d->Hkv) return fail(NSA_ERR_INVALID_ARGUMENT, "Hkv must divide Hq");
   if (d->Lk < d->Lq) return fail(NSA_ERR_INVALID_ARGUMENT, "Lk must be >= Lq (query rows are also key rows)");
-  if (d->causal || d->window)
-    return fail(NSA_ERR_UNSUPPORTED, "sequence sharding supports neither a causal mask nor a window");
+  // Causal masks and windows compare query and key indices; they are exact when the shard holds every
+  // query row (q_begin 0, q_count Lq: one GPU), where local and global query indices coincide.
+  if ((d->causal || d->window) && !(s->q_begin == 0 && s->q_count == d->Lq))
+    return fail(NSA_ERR_UNSUPPORTED, "a causal mask or a window needs a shard that holds every query row");
   if (d->h_begin != 0 || (d->h_count != 0 && d->h_count != d->Hq))
     return fail(NSA_ERR_UNSUPPORTED, "sequence sharding takes whole heads (h_begin 0, h_count 0 or Hq)");
   if (s->q_begin < 0 || s->q_count < 1 || (int64_t)s->q_begin + s->q_count > d->Lq)

@@ -165,36 +165,44 @@ __global__ void __launch_bounds__(kLinThreads, 1)
       const int r = m0 + row_local;
       float* crow = p.C + (int64_t)r * p.ldc;
 #pragma unroll 1
-      for (int c = group * 128; c < group * 128 + 128; c += 16) {
-        uint32_t v[16];
-        tmem_ld16(tbase + (uint32_t)c, v);   // warp-wide: every lane, whatever its row
-        const int n = nt * kLinNT + c;
-        if (r >= p.M || n >= p.N) continue;
-        float y[16];
+      for (int c64 = group * 128; c64 < group * 128 + 128; c64 += 64) {
+        // 64 columns under one wait (warp-wide: every lane, whatever its row)
+        uint32_t v64[64];
+        tmem_ld64(tbase + (uint32_t)c64, v64);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float x = p.alpha * __uint_as_float(v[i]) + sbias[n + i];
-          if (p.act == 1) x = silu(x);
-          y[i] = x;
-        }
-        // The residual forms add into C with vector reductions (each element has one owner, so this is
-        // the in-place C += g * r of the reference without a load round trip per chunk).
-        if (n + 16 <= p.N) {
-          float4* dst = reinterpret_cast<float4*>(crow + n);
+        for (int sub = 0; sub < 4; ++sub) {
+          const int c = c64 + sub * 16;
+          const int n = nt * kLinNT + c;
+          if (r >= p.M || n >= p.N) continue;
+          float y[16];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            if (p.resid)
-              atomicAdd(dst + q, make_float4(sgate[n + 4 * q] * y[4 * q], sgate[n + 4 * q + 1] * y[4 * q + 1],
-                                             sgate[n + 4 * q + 2] * y[4 * q + 2], sgate[n + 4 * q + 3] * y[4 * q + 3]));
-            else
-              dst[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+          for (int i = 0; i < 16; ++i) {
+            float x = p.alpha * __uint_as_float(v64[sub * 16 + i]) + sbias[n + i];
+            if (p.act == 1) x = silu(x);
+            y[i] = x;
           }
-        } else {
-          for (int i = 0; i < 16 && n + i < p.N; ++i) {
-            if (p.resid)
-              atomicAdd(crow + n + i, sgate[n + i] * y[i]);
-            else
-              crow[n + i] = y[i];
+          // The residual forms add into C with vector reductions (each element has one owner, so this
+          // is the in-place C += g * r of the reference without a load round trip per chunk).
+          if (n + 16 <= p.N) {
+            float4* dst = reinterpret_cast<float4*>(crow + n);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              if (p.resid)
+                atomicAdd(dst + q, make_float4(sgate[n + 4 * q] * y[4 * q], sgate[n + 4 * q + 1] * y[4 * q + 1],
+                                               sgate[n + 4 * q + 2] * y[4 * q + 2],
+                                               sgate[n + 4 * q + 3] * y[4 * q + 3]));
+              else
+                dst[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              if (n + i >= p.N) break;
+              if (p.resid)
+                atomicAdd(crow + n + i, sgate[n + i] * y[i]);
+              else
+                crow[n + i] = y[i];
+            }
           }
         }
       }

@@ -17,8 +17,9 @@
 //               one output row): group g takes heads g, g+2, ... of the tile (or half of the RoPE
 //               pairs when a tile holds one head).  Per head: sum of squares over the accumulator
 //               columns, then bias + norm weight + RoPE, bf16 stores.  Bias and norm weights sit in
-//               shared memory; at head dim <= 96 a thread loads its RoPE row into registers before it
-//               waits for the accumulator.
+//               shared memory.  Tensor-memory reads are few and wide (a wait costs about a thousand
+//               cycles while the next tile's MMAs run), and each chunk's cos / sin loads are issued
+//               before its tensor-memory wait.
 #include "nsa_internal.h"
 #include "ptx.cuh"
 
@@ -220,7 +221,6 @@ __global__ void __launch_bounds__(kProjThreads, 1)
     const int pair0 = C::HPT >= 2 ? 0 : group * (D / 4);
     const int pair1 = C::HPT >= 2 ? D / 2 : pair0 + D / 4;
     const int hh0 = C::HPT >= 2 ? group : 0;
-    constexpr bool CS_REGS = D <= 96;   // the whole RoPE row fits in registers
     bool params_ready = false;
     int t = 0;
     for (int u = blockIdx.x; u < tiles; u += G) {
@@ -247,20 +247,6 @@ __global__ void __launch_bounds__(kProjThreads, 1)
       const float* wn = part == 0 ? sqw : (part == 1 ? skw : nullptr);
       const bool rope = q.image && part < 2 && p.cs != nullptr && valid;
       const int rrow = q.rope_row0 + r;
-      // the RoPE row, loaded while the accumulator is still being computed
-      float rc[CS_REGS ? D / 2 : 1], rs[CS_REGS ? D / 2 : 1];
-      if constexpr (CS_REGS) {
-        if (rope) {
-          const float4* cp = reinterpret_cast<const float4*>(p.cs + (int64_t)rrow * (D / 2));
-          const float4* sp = reinterpret_cast<const float4*>(p.cs + p.sin_off + (int64_t)rrow * (D / 2));
-#pragma unroll
-          for (int q4 = 0; q4 < D / 8; ++q4) {
-            const float4 c4 = __ldg(cp + q4), s4 = __ldg(sp + q4);
-            rc[4 * q4] = c4.x; rc[4 * q4 + 1] = c4.y; rc[4 * q4 + 2] = c4.z; rc[4 * q4 + 3] = c4.w;
-            rs[4 * q4] = s4.x; rs[4 * q4 + 1] = s4.y; rs[4 * q4 + 2] = s4.z; rs[4 * q4 + 3] = s4.w;
-          }
-        }
-      }
       bool got = wait_bounded(&acc_full[a], (t >> 1) & 1, abort_flag, p.err, kErrTimeoutProjection, to);
       if (got && !params_ready) {
         got = wait_bounded(pbar, 0, abort_flag, p.err, kErrTimeoutProjection, to);
@@ -275,16 +261,22 @@ __global__ void __launch_bounds__(kProjThreads, 1)
         const int h = h0 + hh;
         const uint32_t col0 = (uint32_t)(hh * D);
         const float* bias = sbias + nt * C::NT + hh * D;
-        // pass 1: sum of squares of (acc + bias) over the head (tcgen05.ld is warp-wide: every lane)
+        // pass 1: sum of squares of (acc + bias) over the head (tcgen05.ld is warp-wide: every lane),
+        // in wide loads: each load's wait is a round trip of the order of a thousand cycles while the
+        // MMAs of the next tile write tensor memory
         float rn = 1.f;
         if (wn) {
+          constexpr int W1 = D % 64 == 0 ? 64 : 48;
           float ss = 0.f;
 #pragma unroll 1
-          for (int c = 0; c < D; c += 16) {
-            uint32_t v[16];
-            tmem_ld16(tbase + col0 + (uint32_t)c, v);
+          for (int c = 0; c < D; c += W1) {
+            uint32_t v[W1];
+            if constexpr (W1 == 64)
+              tmem_ld64(tbase + col0 + (uint32_t)c, v);
+            else
+              tmem_ld48(tbase + col0 + (uint32_t)c, v);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
+            for (int i = 0; i < W1; ++i) {
               const float x = __uint_as_float(v[i]) + bias[c + i];
               ss = fmaf(x, x, ss);
             }
@@ -301,9 +293,20 @@ __global__ void __launch_bounds__(kProjThreads, 1)
 #pragma unroll
         for (int c = 0; c < D / 2; c += 16) {
           if (c < pair0 || c >= pair1) continue;
+          // the RoPE pairs' cos / sin first: their global loads are then in flight during the TMEM wait
+          float cc[16], sn[16];
+          if (rope) {
+            const float4* cp = reinterpret_cast<const float4*>(p.cs + (int64_t)rrow * (D / 2) + c);
+            const float4* sp = reinterpret_cast<const float4*>(p.cs + p.sin_off + (int64_t)rrow * (D / 2) + c);
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              const float4 c4 = __ldg(cp + q4), s4 = __ldg(sp + q4);
+              cc[4 * q4] = c4.x; cc[4 * q4 + 1] = c4.y; cc[4 * q4 + 2] = c4.z; cc[4 * q4 + 3] = c4.w;
+              sn[4 * q4] = s4.x; sn[4 * q4 + 1] = s4.y; sn[4 * q4 + 2] = s4.z; sn[4 * q4 + 3] = s4.w;
+            }
+          }
           uint32_t v1[16], v2[16];
-          tmem_ld16(tbase + col0 + (uint32_t)c, v1);
-          tmem_ld16(tbase + col0 + (uint32_t)(c + D / 2), v2);
+          tmem_ld16_pair(tbase + col0 + (uint32_t)c, tbase + col0 + (uint32_t)(c + D / 2), v1, v2);
           float x1[16], x2[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -318,23 +321,6 @@ __global__ void __launch_bounds__(kProjThreads, 1)
             }
           }
           if (rope) {
-            float cc[16], sn[16];
-            if constexpr (CS_REGS) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                cc[i] = rc[c + i];
-                sn[i] = rs[c + i];
-              }
-            } else {
-              const float4* cp = reinterpret_cast<const float4*>(p.cs + (int64_t)rrow * (D / 2) + c);
-              const float4* sp = reinterpret_cast<const float4*>(p.cs + p.sin_off + (int64_t)rrow * (D / 2) + c);
-#pragma unroll
-              for (int q4 = 0; q4 < 4; ++q4) {
-                const float4 c4 = __ldg(cp + q4), s4 = __ldg(sp + q4);
-                cc[4 * q4] = c4.x; cc[4 * q4 + 1] = c4.y; cc[4 * q4 + 2] = c4.z; cc[4 * q4 + 3] = c4.w;
-                sn[4 * q4] = s4.x; sn[4 * q4 + 1] = s4.y; sn[4 * q4 + 2] = s4.z; sn[4 * q4 + 3] = s4.w;
-              }
-            }
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const float xa = x1[i], xc = x2[i];

@@ -184,8 +184,9 @@ def test_projection_and_linear_validation():
     assert proj() == _lib.NSA_ERR_UNSUPPORTED                                               # bf16 inputs only
     d.in_dtype = _lib.NSA_BF16
     d.causal = 1
-    assert proj() == _lib.NSA_ERR_UNSUPPORTED                                               # sequence layouts: no mask
-    d.causal = 0
+    s.q_count = 2000
+    assert proj() == _lib.NSA_ERR_UNSUPPORTED                                               # mask over a partial shard
+    d.causal, s.q_count = 0, 3952
 
     ld = _lib.LinearDesc()
     ld.M, ld.N, ld.K, ld.lda = 3952, 1536, 1536, 1536

@@ -202,3 +202,29 @@ def test_sequence_sharded_projection(world, local):
     want = O.joint_attention_batched(oracle_qkv(x, w, b, xt, wkv, bkv), L, Lt, L + lv, q_w, k_w, cos, sin, bias=bias,
                                      acc=np.float64)
     assert_close_bf16(got, want, D, what=f"sequence-sharded projection x{world}")
+
+
+@pytest.mark.parametrize("theta,window,L", [(1e6, 0, 300), (1e4, 100, 300), (1e4, 512, 1024)])
+def test_gemma_projected_layer(theta, window, L):
+    """A Gemma3 layer's attention from its normalised input rows (K = 640): the te.qkv linear with the
+    q/k RMSNorm and the 1D RoPE in the GEMM epilogue (one head of 256 per tile), then causal GQA 4/1
+    attention with an optional sliding window over the prepared tiles, against the oracle's
+    linear + gemma_attention (tools/reference.py:186-194)."""
+    from nanosaur2_web_b200.blocks import gemma_layer_attention_projected
+    from nanosaur2_web_b200.ops import ropeTable
+    B, K, GD = 2, 640, 256
+    rng = np.random.default_rng(L + window)
+    x = bf16_round(rng.standard_normal((B, L, K), dtype=np.float32))
+    w = bf16_round(rng.standard_normal((6 * GD, K), dtype=np.float32) / np.sqrt(K))
+    q_w = (1.0 + 0.2 * rng.standard_normal(GD)).astype(np.float32)
+    k_w = (1.0 + 0.2 * rng.standard_normal(GD)).astype(np.float32)
+    out = gemma_layer_attention_projected(t(x, torch.bfloat16), w_qkv=t(w, torch.bfloat16), q_norm=t(q_w),
+                                          k_norm=t(k_w), cs=ropeTable(L, GD, theta, DEV), window=window,
+                                          out_dtype=torch.float32)
+    check_device()
+    got = out.cpu().numpy()
+    for bb in range(B):
+        qkv = O.linear(x[bb], w, acc=np.float64)
+        want = O.gemma_attention(qkv[:, :4 * GD], qkv[:, 4 * GD:5 * GD], qkv[:, 5 * GD:], q_w, k_w, theta, window,
+                                 acc=np.float64)
+        assert_close_bf16(got[bb], want, GD, what=f"gemma projected theta={theta} window={window} b={bb}")
