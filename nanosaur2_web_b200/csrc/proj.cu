@@ -42,6 +42,19 @@ struct ProjCfg {
   static_assert(NT % 16 == 0 && NT <= 256 && STAGE % 1024 == 0, "projection tile");
 };
 
+// 16 consecutive floats of a shared-memory vector (bias, norm weight) in four 16-byte reads; every
+// offset used is a multiple of 16 floats.
+__device__ __forceinline__ void lds16(const float* src, float (&o)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 v = reinterpret_cast<const float4*>(src)[q];
+    o[4 * q] = v.x;
+    o[4 * q + 1] = v.y;
+    o[4 * q + 2] = v.z;
+    o[4 * q + 3] = v.w;
+  }
+}
+
 __device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, const float (&v)[16]) {
   uint4 o[2];
   uint32_t* u = reinterpret_cast<uint32_t*>(o);
@@ -276,9 +289,14 @@ __global__ void __launch_bounds__(kProjThreads, 1)
             else
               tmem_ld48(tbase + col0 + (uint32_t)c, v);
 #pragma unroll
-            for (int i = 0; i < W1; ++i) {
-              const float x = __uint_as_float(v[i]) + bias[c + i];
-              ss = fmaf(x, x, ss);
+            for (int i0 = 0; i0 < W1; i0 += 16) {
+              float bb[16];
+              lds16(bias + c + i0, bb);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float x = __uint_as_float(v[i0 + i]) + bb[i];
+                ss = fmaf(x, x, ss);
+              }
             }
           }
           rn = rsqrtf(ss / (float)D + p.eps);
@@ -307,17 +325,21 @@ __global__ void __launch_bounds__(kProjThreads, 1)
           }
           uint32_t v1[16], v2[16];
           tmem_ld16_pair(tbase + col0 + (uint32_t)c, tbase + col0 + (uint32_t)(c + D / 2), v1, v2);
-          float x1[16], x2[16];
+          float x1[16], x2[16], b1[16], b2[16];
+          lds16(bias + c, b1);
+          lds16(bias + D / 2 + c, b2);
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            x1[i] = __uint_as_float(v1[i]) + bias[c + i];
-            x2[i] = __uint_as_float(v2[i]) + bias[D / 2 + c + i];
+            x1[i] = __uint_as_float(v1[i]) + b1[i];
+            x2[i] = __uint_as_float(v2[i]) + b2[i];
           }
           if (wn) {
+            lds16(wn + c, b1);
+            lds16(wn + D / 2 + c, b2);
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              x1[i] *= rn * wn[c + i];
-              x2[i] *= rn * wn[D / 2 + c + i];
+              x1[i] *= rn * b1[i];
+              x2[i] *= rn * b2[i];
             }
           }
           if (rope) {
