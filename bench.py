@@ -218,6 +218,17 @@ def measured_peak():
     return FALLBACK_PEAK_TFLOPS, "fallback (1.59 PFLOP/s burst, earlier measurement on this pool)"
 
 
+def measured_hbm():
+    """HBM copy bandwidth in GB/s: MEASURED_PEAKS.json hbm_gbs, else the pool's earlier 6.65 TB/s."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        try:
+            return float(json.load(open(p))["hbm_gbs"])
+        except Exception:
+            pass
+    return 6650.0
+
+
 def ncu_traffic_per_launch():
     """Per-launch DRAM traffic of the attention kernel on this workload from the committed ncu summary
     (profiles/attention_cfg2.md, line 'dram_bytes_per_launch = N'), or None."""
@@ -804,6 +815,97 @@ def run_config7(args, rank, world, local_rank):
           flush=True)
 
 
+def run_config8(args, rank, world, local_rank):
+    """Config 8 (Gemma's side of the "next" steps, widened to the whole attention half of the layer):
+    config 4's 18 Gemma3-270M layers (batch 16 x 1024 tokens, 15 local with a 512-key window, 3 global)
+    on the fp32 residual stream x [B, L, 640] (app/models/gemma3.js:62-77; tools/reference.py:187-196):
+    input RMSNorm to bf16, te.qkv with the q/k norms and RoPE in the GEMM epilogue, attention, te.o,
+    and the post-attention RMSNorm added into x (blocks.gemma_attention_sublayer, five launches per
+    layer).  Batch-sharded over the ranks (strong scaling).  The line also reports the unfused form:
+    torch elementwise norms, cuBLAS linears and the fused prologue + attention."""
+    import torch
+
+    from nanosaur2_web_b200.blocks import (GEMMA_HEAD_DIM, GEMMA_HEADS, gemma_attention_sublayer,
+                                           gemma_layer_attention, gemma_rope_theta, gemma_sublayer_buffers)
+    from nanosaur2_web_b200.ops import ropeTable
+    from nanosaur2_web_b200.sharding import split_range, sum_over_ranks
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, L, LAYERS, WINDOW, Hd, EPS = 16, 1024, 18, 512, 640, 1e-6
+    QKV, A = 6 * GEMMA_HEAD_DIM, GEMMA_HEADS * GEMMA_HEAD_DIM
+    b0, b1 = split_range(B, world, rank)
+    nb = b1 - b0
+    g = torch.Generator(device=dev).manual_seed(8000 + rank)
+    x = torch.randn((nb, L, Hd), device=dev, generator=g) * 8.0            # 42 MB residual stream per 16
+    layers = []
+    for _ in range(3):   # three weight sets rotate (the 18 layers' weights are 18 x 3.3 MB in the model)
+        layers.append({
+            "in_norm": 1.0 + 0.2 * torch.randn(Hd, device=dev, generator=g),
+            "post_norm": 1.0 + 0.2 * torch.randn(Hd, device=dev, generator=g),
+            "q_norm": 1.0 + 0.2 * torch.randn(GEMMA_HEAD_DIM, device=dev, generator=g),
+            "k_norm": 1.0 + 0.2 * torch.randn(GEMMA_HEAD_DIM, device=dev, generator=g),
+            "w_qkv": (torch.randn((QKV, Hd), device=dev, generator=g) / math.sqrt(Hd)).to(torch.bfloat16),
+            "w_o": (torch.randn((Hd, A), device=dev, generator=g) / math.sqrt(A)).to(torch.bfloat16)})
+    tables = {th: ropeTable(L, GEMMA_HEAD_DIM, th, dev) for th in (1e4, 1e6)}
+    bufs = gemma_sublayer_buffers(nb, L, Hd, dev)
+    qkv = torch.empty((nb, L, QKV), dtype=torch.bfloat16, device=dev)
+    a = torch.empty((nb, L, A), dtype=torch.bfloat16, device=dev)
+
+    def step(i):
+        for layer in range(LAYERS):
+            th = gemma_rope_theta(layer)
+            gemma_attention_sublayer(x, **layers[(i * LAYERS + layer) % 3], cs=tables[th],
+                                     window=0 if th == 1e6 else WINDOW, eps=EPS, buffers=bufs)
+
+    def rms(t, w):
+        return t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + EPS) * w
+
+    def step_unfused(i):
+        for layer in range(LAYERS):
+            th = gemma_rope_theta(layer)
+            wl = layers[(i * LAYERS + layer) % 3]
+            torch.matmul(rms(x, wl["in_norm"]).to(torch.bfloat16), wl["w_qkv"].T, out=qkv)   # cuBLAS
+            gemma_layer_attention(qkv, q_norm=wl["q_norm"], k_norm=wl["k_norm"], cs=tables[th],
+                                  window=0 if th == 1e6 else WINDOW, out=a)
+            x.add_(rms(torch.matmul(a, wl["w_o"].T).float(), wl["post_norm"]))
+
+    per_elem_attn = sum(4.0 * GEMMA_HEADS * gemma_pairs(L, 0 if gemma_rope_theta(i) == 1e6 else WINDOW) *
+                        GEMMA_HEAD_DIM for i in range(LAYERS))
+    per_elem_lin = LAYERS * 2.0 * L * Hd * (QKV + A)
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(local_rank) as clocks:
+        ms = _timed(step, args.steps, args.warmup, world, stream)
+    ms_unfused = _timed(step_unfused, args.steps, args.warmup, world, stream)
+    flops = sum_over_ranks((per_elem_attn + per_elem_lin) * nb * args.steps)
+    nsteps = min(args.steps, 3)
+    kst = _kernel_stats(step, nsteps)
+    if rank != 0:
+        return
+    roof = _roofline(kst, "attn_persist_kernel")
+    peak, _src = measured_peak()
+    for key, name, kernel in (("projection", "projection", "proj_kernel<256>"),
+                              ("output_projection", "linear", "linear_kernel")):
+        _, kms, kfl, _ = kst[name]
+        roof[key] = {"kernel": kernel, "achieved": kfl / (kms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
+                     "frac": kfl / (kms * 1e-3) / 1e12 / peak, "ms_per_step": kms / nsteps}
+    rl, rms_ms, _, rbytes = kst["rmsnorm"]
+    hbm = measured_hbm()
+    roof["rmsnorm"] = {"kernel": "rmsnorm_kernel", "bound": "hbm", "achieved": rbytes / (rms_ms * 1e-3) / 1e9,
+                       "peak": hbm, "unit": "GB/s", "frac": rbytes / (rms_ms * 1e-3) / 1e9 / hbm,
+                       "launches_per_step": rl / nsteps, "ms_per_step": rms_ms / nsteps}
+    cfg = {"workload": "config 8: Gemma3-270M text encoder, the attention half of config 4's 18 layers (B=16 x "
+                       "1024, GQA 4/1, head dim 256, causal, 15 local window 512 + 3 global) on the fp32 residual "
+                       "stream (hidden 640): input RMSNorm, te.qkv linear with q/k RMSNorm + 1D RoPE in the GEMM "
+                       "epilogue, attention, te.o linear, post-attention RMSNorm accumulated into the stream",
+           "global_batch": B, "seq_len": L, "layers": LAYERS, "hidden": Hd, "parallelism": f"batch-sharded x{world}",
+           "l2": "each layer reads and rewrites the 42 MB stream and three weight sets rotate; the per-layer "
+                 "intermediates (h 21 MB, q'/k'/v' 42 MB, a 34 MB, o 42 MB) exceed the 126 MB L2 together",
+           "flops_note": "18 * (2*L*640*(1536 + 1024) linears + 4*Hq*valid pairs*256 attention) per element"}
+    print(json.dumps(_line(args, world, flops / (ms * 1e-3) / 1e12, ms, cfg, roof, clocks.summary(),
+                           5 * LAYERS * args.steps, "strong", unfused_ms_per_step=ms_unfused / args.steps)),
+          flush=True)
+
+
 def run_profile(args, local_rank):
     """Small driver for ncu captures: the same fused call as the benchmark on ``--batch`` elements of
     config 2, ``--warmup`` + ``--steps`` launches of each kernel, nothing else on the GPU."""
@@ -845,10 +947,11 @@ def main():
     ap.add_argument("--seq-mode", choices=["auto", "nccl", "p2p", "ce"], default="auto",
                     help="config 5: k'|v' exchange by NCCL all-gather, peer stores from the prologue, or "
                          "copy-engine pushes")
-    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5, 6, 7], default=2,
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5, 6, 7, 8], default=2,
                     help="BASELINE config to run (2 = the headline line; 3, 4, 5 print their own line; 6 = the "
                          "config-2 block step from the block input, QKV projection fused with the prologue; 7 = "
-                         "config 4's Gemma layers from the layer input)")
+                         "config 4's Gemma layers from the layer input; 8 = the attention half of config 4's "
+                         "Gemma layers on the residual stream)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -871,8 +974,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5, 6: run_config6, 7: run_config7}[args.config](
-            args, rank, world, local_rank)
+        {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5, 6: run_config6, 7: run_config7,
+         8: run_config8}[args.config](args, rank, world, local_rank)
     finally:
         if world > 1:
             dist.destroy_process_group()

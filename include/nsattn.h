@@ -272,6 +272,24 @@ nsa_status nsa_linear(const nsa_linear_desc* desc, const void* A, const void* W,
                       const float* gate, float* C, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * nsa_rmsnorm: ops.rmsnorm(gpu, x, weight, cols, eps, out) (app/gpu/ops.js:111-116, kernels.js:62-80)
+ *   Y[r*ldy + c] = X[r*ldx + c] * rsqrt(mean_c(X[r][c]^2) + eps) * weight[c]
+ * over `rows` rows of `cols` fp32 values.  out_dtype NSA_BF16 writes the next GEMM's bf16 operand
+ * (the Gemma layer's input norm before te.qkv, app/models/gemma3.js:62-63).  accumulate = 1 (fp32 Y
+ * only) fuses the ops.accumulate that follows (ops.js:188-192; gemma3.js:74-77, the post-attention
+ * norm added into the residual stream): Y[...] += X * r * weight.  X and Y must not overlap.
+ * ------------------------------------------------------------------------------------------------ */
+typedef struct nsa_rmsnorm_desc {
+  int32_t rows, cols;
+  int64_t ldx;         /* X row pitch in elements (0: cols) */
+  int64_t ldy;         /* Y row pitch in elements (0: cols) */
+  int32_t out_dtype;   /* NSA_F32 or NSA_BF16 */
+  int32_t accumulate;  /* 1: Y += norm(X) (NSA_F32 only) */
+  float eps;           /* >= 0; the reference's default is 1e-6 */
+} nsa_rmsnorm_desc;
+nsa_status nsa_rmsnorm(const nsa_rmsnorm_desc* desc, const float* X, const float* weight, void* Y, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
  * RoPE tables in the reference layout: cos block [L][D/2] then sin block [L][D/2] (sinOff = L*D/2).
  *   nsa_rope2d_table: app/models/common.js:28-43 (tools/reference.py:220-227): L = h*w tokens,
  *     the first D/4 pairs rotate by the centred column, the next D/4 by the centred row, theta 1e4.

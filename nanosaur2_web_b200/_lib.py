@@ -67,6 +67,12 @@ class LinearDesc(ctypes.Structure):
                 ("alpha", _f32), ("resid", _i32), ("act", _i32)]
 
 
+class RmsnormDesc(ctypes.Structure):
+    """nsa_rmsnorm_desc (include/nsattn.h)."""
+    _fields_ = [("rows", _i32), ("cols", _i32), ("ldx", _i64), ("ldy", _i64), ("out_dtype", _i32),
+                ("accumulate", _i32), ("eps", _f32)]
+
+
 class KernelStat(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 32), ("launches", _i64), ("total_ms", ctypes.c_double),
                 ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
@@ -98,6 +104,7 @@ SIGNATURES = {
     "nsa_seq_shard_projection": (_i32, [ctypes.POINTER(FusedDesc), ctypes.POINTER(SeqShard), ctypes.POINTER(ProjDesc),
                                         _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "nsa_linear": (_i32, [ctypes.POINTER(LinearDesc), _vp, _vp, _vp, _vp, _vp, _vp]),
+    "nsa_rmsnorm": (_i32, [ctypes.POINTER(RmsnormDesc), _vp, _vp, _vp, _vp]),
     "nsa_rope2d_table": (_i32, [_i32, _i32, _i32, _vp, _vp]),
     "nsa_rope1d_table": (_i32, [_i32, _i32, _f32, _vp, _vp]),
     "nsa_check_device": (_i32, [_vp]),

@@ -16,6 +16,10 @@
 * ``gemma_layer_attention_projected(...)``: the Gemma layer's attention from its normalised input
   rows: the ``te.qkv`` linear with the q/k norms and RoPE in the GEMM epilogue, then the causal
   attention over the prepared tiles.
+* ``gemma_attention_sublayer(...)``: the attention half of a Gemma layer on its fp32 residual stream
+  (app/models/gemma3.js:62-77; tools/reference.py:187-196): input RMSNorm to a bf16 operand, the
+  projected attention above, the ``te.o`` linear, and the post-attention RMSNorm added into the
+  stream, five launches.
 * ``gemma_layer_attention(...)``: one Gemma3 layer's attention, headNorm(q), headNorm(k) with the
   local/global RoPE table + causal GQA 4/1 attention (app/models/gemma3.js:63-70;
   tools/reference.py:186-194), with an optional sliding window.
@@ -31,7 +35,7 @@ import torch
 
 from . import _lib
 from ._lib import FusedDesc, NsaError, ProjDesc, SeqShard, check, lib
-from .ops import RopeTable, dtype_code, stream_handle
+from .ops import RopeTable, dtype_code, linear, rmsnorm, stream_handle
 
 DIT_HEADS, DIT_HEAD_DIM = 16, 96
 GEMMA_HEADS, GEMMA_KV_HEADS, GEMMA_HEAD_DIM = 4, 1, 256
@@ -266,6 +270,41 @@ def gemma_layer_attention_projected(x: torch.Tensor, *, w_qkv: torch.Tensor, q_n
         check(L_.nsa_seq_shard_attention(ctypes.byref(d), ctypes.byref(s), q_prime.data_ptr(), kv_packed.data_ptr(),
                                          None, None, out.data_ptr(), stream))
     return out
+
+
+def gemma_sublayer_buffers(B: int, L: int, hidden: int, device) -> dict:
+    """Intermediates of ``gemma_attention_sublayer``: the normalised input h (bf16 [B, L, hidden]),
+    the projection's q_prime / kv_packed, the attention output a (bf16 [B, L, 1024]) and the te.o
+    output o (fp32 [B*L, hidden])."""
+    return {"h": torch.empty((B, L, hidden), dtype=torch.bfloat16, device=device),
+            "proj": gemma_projection_buffers(B, L, device),
+            "a": torch.empty((B, L, GEMMA_HEADS * GEMMA_HEAD_DIM), dtype=torch.bfloat16, device=device),
+            "o": torch.empty((B * L, hidden), dtype=torch.float32, device=device)}
+
+
+def gemma_attention_sublayer(x: torch.Tensor, *, in_norm: torch.Tensor, w_qkv: torch.Tensor, q_norm: torch.Tensor,
+                             k_norm: torch.Tensor, w_o: torch.Tensor, post_norm: torch.Tensor, cs: RopeTable,
+                             window: int = 0, eps: float = 1e-6, buffers: Optional[dict] = None) -> torch.Tensor:
+    """The attention half of one Gemma3 layer, in place on the residual stream x (fp32 [B, L, hidden])
+    (app/models/gemma3.js:62-77; tools/reference.py:187-196):
+        h = rmsnorm(x, in_norm)                       nsa_rmsnorm, bf16 output
+        a = attention(headNorm(h W_qkv^T))            nsa_seq_shard_projection + nsa_seq_shard_attention
+        x += rmsnorm(a W_o^T, post_norm)              nsa_linear (te.o) + nsa_rmsnorm accumulate
+    w_qkv [1536, hidden] and w_o [hidden, 1024] bf16; norm weights fp32, lifted by +1 (gemma3.js:22).
+    ``buffers`` = gemma_sublayer_buffers(B, L, hidden, device), to reuse.  Returns x."""
+    if x.dim() != 3 or x.dtype != torch.float32 or not x.is_contiguous():
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "x must be a contiguous float32 [B, L, hidden] tensor")
+    B, L, hidden = x.shape
+    if w_o.shape != (hidden, GEMMA_HEADS * GEMMA_HEAD_DIM):
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "w_o must be [hidden, 1024]")
+    buf = buffers if buffers is not None else gemma_sublayer_buffers(B, L, hidden, x.device)
+    h, a, o = buf["h"], buf["a"], buf["o"]
+    rmsnorm(x, in_norm, hidden, eps, h)
+    gemma_layer_attention_projected(h, w_qkv=w_qkv, q_norm=q_norm, k_norm=k_norm, cs=cs, window=window, eps=eps,
+                                    out=a, buffers=buf["proj"])
+    linear(a.view(B * L, -1), w_o, out=o)
+    rmsnorm(o, post_norm, hidden, eps, x.view(B * L, hidden), accumulate=True)
+    return x
 
 
 def text_refine_attention(qkv: torch.Tensor, *, q_norm: torch.Tensor, k_norm: torch.Tensor,

@@ -1052,6 +1052,42 @@ nsa_status nsa_linear(const nsa_linear_desc* d, const void* A, const void* W, co
   return NSA_OK;
 }
 
+nsa_status nsa_rmsnorm(const nsa_rmsnorm_desc* d, const float* X, const float* weight, void* Y, void* stream) {
+  if (!d) return fail(NSA_ERR_INVALID_ARGUMENT, "desc is NULL");
+  if (d->rows < 0 || d->cols < 1) return fail(NSA_ERR_INVALID_ARGUMENT, "need rows >= 0 and cols >= 1");
+  const int64_t ldx = d->ldx ? d->ldx : d->cols, ldy = d->ldy ? d->ldy : d->cols;
+  if (ldx < d->cols || ldy < d->cols) return fail(NSA_ERR_INVALID_ARGUMENT, "ldx and ldy must be >= cols");
+  if (d->out_dtype != NSA_F32 && d->out_dtype != NSA_BF16) return fail(NSA_ERR_INVALID_ARGUMENT, "bad out_dtype");
+  if (d->accumulate && d->out_dtype != NSA_F32) return fail(NSA_ERR_INVALID_ARGUMENT, "accumulate needs an fp32 Y");
+  if (!(d->eps >= 0.f)) return fail(NSA_ERR_INVALID_ARGUMENT, "eps must be >= 0");
+  if (d->rows == 0) return NSA_OK;   // nothing to normalise (empty tensors may carry NULL pointers)
+  if (!X || !weight || !Y) return fail(NSA_ERR_INVALID_ARGUMENT, "X, weight and Y must be device pointers");
+  const int esz = d->out_dtype == NSA_F32 ? 4 : 2;
+  // X and Y must not overlap (a row's values are read before and while its outputs are written)
+  const uintptr_t x0 = reinterpret_cast<uintptr_t>(X), y0 = reinterpret_cast<uintptr_t>(Y);
+  const uintptr_t x1 = x0 + (uintptr_t)(((int64_t)(d->rows - 1) * ldx + d->cols) * 4);
+  const uintptr_t y1 = y0 + (uintptr_t)(((int64_t)(d->rows - 1) * ldy + d->cols) * esz);
+  if (x0 < y1 && y0 < x1) return fail(NSA_ERR_INVALID_ARGUMENT, "X and Y must not overlap");
+  nsa::RmsParams p{};
+  p.rows = d->rows;
+  p.cols = d->cols;
+  p.ldx = ldx;
+  p.ldy = ldy;
+  p.x = X;
+  p.w = weight;
+  p.y = Y;
+  p.out_bf16 = d->out_dtype == NSA_BF16;
+  p.accumulate = d->accumulate ? 1 : 0;
+  p.eps = d->eps;
+  p.vec = d->cols % 4 == 0 && ldx % 4 == 0 && ldy % 4 == 0 && (x0 & 15) == 0 &&
+          (reinterpret_cast<uintptr_t>(weight) & 15) == 0 && (y0 & (uintptr_t)(4 * esz - 1)) == 0;
+  const double bytes = (double)d->rows * d->cols * (4.0 + esz * (d->accumulate ? 2.0 : 1.0));
+  const cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  cudaError_t e = profiled("rmsnorm", 0.0, bytes, strm, [&] { return nsa::launch_rmsnorm(p, strm); });
+  if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+  return NSA_OK;
+}
+
 nsa_status nsa_seq_shard_attention(const nsa_fused_desc* d, const nsa_seq_shard* s, const void* q_prime,
                                    const void* kv_packed, const int32_t* kv_len, const float* bias, void* out,
                                    void* stream) {

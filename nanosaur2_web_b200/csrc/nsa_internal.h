@@ -187,6 +187,20 @@ struct LinearParams {
 };
 cudaError_t launch_linear(const LinearParams& p, const CUtensorMap& tmA, const CUtensorMap& tmW, cudaStream_t stream);
 
+// Row RMSNorm (rmsnorm.cu): Y[r][c] (=|+=) X[r][c] * rsqrt(mean(X[r]^2) + eps) * w[c].
+struct RmsParams {
+  int rows, cols;
+  int64_t ldx, ldy;
+  const float* x;
+  const float* w;
+  void* y;          // fp32, or bf16 when out_bf16
+  int out_bf16;
+  int accumulate;   // fp32 Y only
+  int vec;          // cols, ldx, ldy multiples of 4; x, w, y 16-byte aligned
+  float eps;
+};
+cudaError_t launch_rmsnorm(const RmsParams& p, cudaStream_t stream);
+
 // Returns cudaErrorInvalidValue for unsupported head dims.
 cudaError_t launch_attention(const AttnParams& p, int D, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                              const CUtensorMap& tmV, const CUtensorMap& tmVd, cudaStream_t stream);

@@ -1,0 +1,122 @@
+// Row RMSNorm for sm_100a: ops.rmsnorm (app/gpu/ops.js:111-116, kernels.js:62-80)
+//   Y[r][c] = X[r][c] * rsqrt(mean_c(X[r][c]^2) + eps) * w[c]
+// and the Gemma layer's rmsnorm followed by ops.accumulate (app/models/gemma3.js:74-77, :86-88;
+// ops.js:188-192) as one pass: Y[r][c] += X[r][c] * rsqrt(...) * w[c].  The product keeps the
+// reference's order, (x * r) * w, so the only difference is the order of the sum of squares.
+//
+// One warp per row, eight rows per 256-thread block.  Rows of up to 1024 fp32 values stay in
+// registers (eight 16-byte loads per lane); longer rows are read a second time (from L1).  The
+// kernel is HBM-bound: X is read once, Y written once (and read once when accumulating); bf16 output
+// feeds the next GEMM's A operand directly (the QKV projection of the Gemma layer).
+#include <cuda_bf16.h>
+
+#include "nsa_internal.h"
+
+namespace nsa {
+
+namespace {
+
+constexpr int kRmsWarps = 8;
+constexpr int kRmsCache = 8;   // float4 per lane held in registers
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float sq4(float4 v) { return v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
+
+template <bool BF16, bool ACC>
+__device__ __forceinline__ void emit4(const RmsParams& p, int64_t row, int i, float4 v, float r) {
+  const float4 w = reinterpret_cast<const float4*>(p.w)[i];
+  const float4 y = make_float4(v.x * r * w.x, v.y * r * w.y, v.z * r * w.z, v.w * r * w.w);
+  if constexpr (BF16) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(y.x, y.y), hi = __floats2bfloat162_rn(y.z, y.w);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&lo);
+    u.y = *reinterpret_cast<uint32_t*>(&hi);
+    reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.y) + row * p.ldy)[i] = u;
+  } else {
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.y) + row * p.ldy) + i;
+    if constexpr (ACC) {
+      const float4 o = *dst;
+      *dst = make_float4(o.x + y.x, o.y + y.y, o.z + y.z, o.w + y.w);
+    } else {
+      *dst = y;
+    }
+  }
+}
+
+template <bool BF16, bool ACC>
+__device__ __forceinline__ void emit1(const RmsParams& p, int64_t row, int c, float v, float r) {
+  const float y = v * r * p.w[c];
+  if constexpr (BF16) {
+    static_cast<__nv_bfloat16*>(p.y)[row * p.ldy + c] = __float2bfloat16_rn(y);
+  } else {
+    float* dst = static_cast<float*>(p.y) + row * p.ldy + c;
+    if constexpr (ACC)
+      *dst += y;
+    else
+      *dst = y;
+  }
+}
+
+// VEC: cols, ldx and ldy multiples of 4 and X, w, Y 16-byte aligned (8-byte for bf16 Y rows).
+template <bool VEC, bool BF16, bool ACC>
+__global__ void __launch_bounds__(kRmsWarps * 32) rmsnorm_kernel(const RmsParams p) {
+  const int lane = threadIdx.x % 32;
+  const int64_t row = (int64_t)blockIdx.x * kRmsWarps + threadIdx.x / 32;
+  if (row >= p.rows) return;
+  const float* xr = p.x + row * p.ldx;
+  float ss = 0.f;
+  if constexpr (VEC) {
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
+    const int nv = p.cols / 4;
+    float4 v[kRmsCache];
+#pragma unroll
+    for (int j = 0; j < kRmsCache; ++j) {
+      const int i = lane + 32 * j;
+      v[j] = i < nv ? __ldg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      ss += sq4(v[j]);
+    }
+    for (int i = lane + 32 * kRmsCache; i < nv; i += 32) ss += sq4(__ldg(x4 + i));
+    const float r = rsqrtf(warp_sum(ss) / (float)p.cols + p.eps);
+#pragma unroll
+    for (int j = 0; j < kRmsCache; ++j) {
+      const int i = lane + 32 * j;
+      if (i < nv) emit4<BF16, ACC>(p, row, i, v[j], r);
+    }
+    for (int i = lane + 32 * kRmsCache; i < nv; i += 32) emit4<BF16, ACC>(p, row, i, __ldg(x4 + i), r);
+  } else {
+    for (int c = lane; c < p.cols; c += 32) {
+      const float t = xr[c];
+      ss += t * t;
+    }
+    const float r = rsqrtf(warp_sum(ss) / (float)p.cols + p.eps);
+    for (int c = lane; c < p.cols; c += 32) emit1<BF16, ACC>(p, row, c, xr[c], r);
+  }
+}
+
+template <bool VEC>
+cudaError_t launch_v(const RmsParams& p, cudaStream_t stream) {
+  const long long blocks = ((long long)p.rows + kRmsWarps - 1) / kRmsWarps;
+  if (blocks > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
+  const dim3 grid((unsigned)blocks), block(kRmsWarps * 32);
+  if (p.out_bf16)
+    rmsnorm_kernel<VEC, true, false><<<grid, block, 0, stream>>>(p);
+  else if (p.accumulate)
+    rmsnorm_kernel<VEC, false, true><<<grid, block, 0, stream>>>(p);
+  else
+    rmsnorm_kernel<VEC, false, false><<<grid, block, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_rmsnorm(const RmsParams& p, cudaStream_t stream) {
+  if (p.rows <= 0) return cudaSuccess;
+  return p.vec ? launch_v<true>(p, stream) : launch_v<false>(p, stream);
+}
+
+}  // namespace nsa

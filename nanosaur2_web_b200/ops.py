@@ -26,8 +26,8 @@ import torch
 from . import _lib
 from ._lib import NSA_BF16, NSA_F32, AttentionDesc, NsaError, check, lib
 
-__all__ = ["attention", "headNorm", "rope2dTable", "ropeTable", "RopeTable", "NsaError", "dtype_code",
-           "stream_handle", "check_device"]
+__all__ = ["attention", "headNorm", "linear", "rmsnorm", "rope2dTable", "ropeTable", "RopeTable", "NsaError",
+           "dtype_code", "stream_handle", "check_device"]
 
 
 def dtype_code(t: torch.Tensor) -> int:
@@ -128,6 +128,44 @@ def linear(x: torch.Tensor, W: torch.Tensor, *, bias: Optional[torch.Tensor] = N
     with torch.cuda.device(x.device):
         check(lib().nsa_linear(ctypes.byref(d), x.data_ptr(), W.data_ptr(), _ptr(bias), _ptr(gate), out.data_ptr(),
                                stream_handle(x.device)))
+    return out
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, cols: Optional[int] = None, eps: float = 1e-6,
+            out: Optional[torch.Tensor] = None, *, accumulate: bool = False,
+            out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """y = x * rsqrt(mean(x^2) + eps) * weight over rows of ``cols`` values (app/gpu/ops.js:111-116,
+    kernels.js:62-80).  x fp32 [..., cols] with unit inner stride; out fp32 or bf16 (the next GEMM's
+    operand), allocated like x when not given.  ``accumulate`` adds into ``out`` instead, the
+    ops.accumulate that follows the Gemma layer's post-attention norm (app/models/gemma3.js:74-77)."""
+    _require_cuda(x, weight, out)
+    cols = cols or x.shape[-1]
+    if x.dtype != torch.float32 or weight.dtype != torch.float32 or x.stride(-1) != 1 or x.shape[-1] != cols:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "x and weight must be float32, x [..., cols] with unit inner stride")
+    if weight.numel() < cols or not weight.is_contiguous():
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "weight must be a contiguous [cols] tensor")
+    if out is None:
+        if accumulate:
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "accumulate needs out")
+        out = torch.empty(x.shape, dtype=out_dtype or torch.float32, device=x.device)
+    if out.shape != x.shape or out.stride(-1) != 1:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "out must match x's shape with unit inner stride")
+
+    def rows(t):   # [rows, cols] view with a row pitch: 2-D tensors as they are, others contiguous
+        if t.dim() == 2:
+            return t
+        if not t.is_contiguous():
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "x and out of more than two dims must be contiguous")
+        return t.view(-1, cols)
+
+    x2, o2 = rows(x), rows(out)
+    d = _lib.RmsnormDesc()
+    d.rows, d.cols = x2.shape[0], cols
+    d.ldx, d.ldy = x2.stride(0), o2.stride(0)
+    d.out_dtype, d.accumulate, d.eps = dtype_code(out), int(bool(accumulate)), eps
+    with torch.cuda.device(x.device):
+        check(lib().nsa_rmsnorm(ctypes.byref(d), x2.data_ptr(), weight.data_ptr(), o2.data_ptr(),
+                                stream_handle(x.device)))
     return out
 
 

@@ -223,6 +223,19 @@ def gemma_attention(q_raw, k_raw, v, q_w, k_w, theta, window=0, eps=1e-6, acc=np
     return attention(q, k, v, H, D, group=H // KH, causal=True, window=window, acc=acc)
 
 
+def gemma_attention_sublayer(x, in_w, w_q, w_k, w_v, q_w, k_w, w_o, post_w, theta, window=0, eps=1e-6,
+                             acc=np.float32):
+    """The attention half of one Gemma3 layer on the residual stream x [L, hidden]
+    (tools/reference.py:187-196; app/models/gemma3.js:62-77): h = rms_norm(x, in_w), q/k/v = h W^T,
+    a = gemma_attention(q, k, v), then x + rms_norm(a W_o^T, post_w).  Norm weights are the lifted
+    (w - 1) + 1 values.  Returns the updated residual stream."""
+    x = np.asarray(x, acc)
+    h = rms_norm(x, in_w, eps, acc)
+    a = gemma_attention(linear(h, w_q, acc=acc), linear(h, w_k, acc=acc), linear(h, w_v, acc=acc), q_w, k_w,
+                        theta, window, eps, acc)
+    return x + rms_norm(linear(a, w_o, acc=acc), post_w, eps, acc)
+
+
 # ----------------------------------------------------------------------------- batched helpers
 
 def joint_attention_batched(qkv, L, Lt, kv_len, q_w, k_w, cos, sin, bias=None, H=DIT_HEADS,

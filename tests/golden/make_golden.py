@@ -17,6 +17,9 @@ drives its real code paths with small seeded stand-in weights (no model files ex
 * ``rope_2d`` / ``gemma_rope`` tables and ``rms_norm`` / ``rope_split_half`` on seeded inputs.
 * ``lin`` (``:208-210``), the q|k|v projection's linear, on small seeded operands with and without a
   bias (``--only linear`` writes just this fixture).
+* the attention half of ``gemma_encode``'s layers 0 and 5 (``:187-196``: input norm, q/k/v linears,
+  head norms, RoPE, causal SDPA, o linear, post-attention norm, residual add) on a 64-wide residual
+  stream with bf16-exact linear weights (``--only gemma_sublayer``).
 
 The qkv projection outputs of the DiT are rounded to bf16 inside the reference run (a hook on its
 ``lin``), so the bf16 CUDA path sees exactly the inputs the fp32 reference saw.  The Gemma inputs
@@ -108,8 +111,8 @@ def dit_has(name):
     return True
 
 
-def gemma_shapes(role):
-    Hd, I, V = 640, 64, 300
+def gemma_shapes(role, Hd=640):
+    I, V = 64, 300
     if role == "model.embed_tokens.weight":
         return ((V, Hd), "emb")
     if role == "model.norm.weight":
@@ -193,6 +196,49 @@ def capture_gemma(R, seed, L):
     return records
 
 
+class Bf16LinearWeights(StandInWeights):
+    """Stand-in weights whose matrices are bf16-exact, so a bf16 GEMM sees the reference's values."""
+
+    def __call__(self, name):
+        t = super().__call__(name)
+        return bf16_round(t) if t.dim() == 2 and not name.endswith("embed_tokens.weight") else t
+
+
+def write_gemma_sublayer(R, out, L=40, hidden=64):
+    """The attention half of gemma_encode's layers 0 (local) and 5 (global) (tools/reference.py:187-196)
+    on a 64-wide residual stream (the attention shapes are the model's: 4 + 1 heads of 256): the layer
+    input x, the updated x after ``x + rms_norm(a @ W_o^T, post)``, and the weights, with the linear
+    weights bf16-exact.  The reference's 2-D rms_norm calls give, per layer, the input norm (its x is
+    the layer input), the post-attention norm and the pre-MLP norm (its x is the updated stream)."""
+    W = Bf16LinearWeights(lambda role: gemma_shapes(role, hidden), 4321, lambda n: True)
+    calls = []
+    orig_rms = R.rms_norm
+
+    def rms_hook(x, wt, eps=1e-6):
+        if x.dim() == 2:
+            calls.append((x.detach().clone(), wt.detach().clone()))
+        return orig_rms(x, wt, eps)
+
+    R.rms_norm = rms_hook
+    try:
+        ids = [2] + [int(i) for i in torch.randint(3, 300, (L - 1,), generator=torch.Generator().manual_seed(4321))]
+        R.gemma_encode(W, ids)
+    finally:
+        R.rms_norm = orig_rms
+    assert len(calls) == 4 * 17 + 1, len(calls)
+    p = "model.layers.0."
+    rec = {}
+    for layer in (0, 5):
+        (x_in, w_in), (_, w_post), (x_mid, _) = calls[4 * layer:4 * layer + 3]
+        rec[f"x_in{layer}"], rec[f"x_mid{layer}"] = np32(x_in), np32(x_mid)
+    np.savez_compressed(
+        os.path.join(out, "gemma_sublayer.npz"), **rec, layers=np.array([0, 5]),
+        in_w=np32(w_in), post_w=np32(w_post),
+        q_w=np32(W(p + "self_attn.q_norm.weight") + 1.0), k_w=np32(W(p + "self_attn.k_norm.weight") + 1.0),
+        w_q=np32(W(p + "self_attn.q_proj.weight")), w_k=np32(W(p + "self_attn.k_proj.weight")),
+        w_v=np32(W(p + "self_attn.v_proj.weight")), w_o=np32(W(p + "self_attn.o_proj.weight")))
+
+
 def np32(t):
     return t.detach().float().cpu().numpy().astype(np.float32)
 
@@ -225,15 +271,18 @@ def main():
     ap.add_argument("--reference", default=os.environ.get("NANOSAUR2_REFERENCE"),
                     help="checkout of the reference repository (or NANOSAUR2_REFERENCE)")
     ap.add_argument("--out", default=HERE)
-    ap.add_argument("--only", choices=["linear"], help="write one fixture only")
+    ap.add_argument("--only", choices=["linear", "gemma_sublayer"], help="write one fixture only")
     args = ap.parse_args()
     if not args.reference:
         ap.error("pass --reference <checkout of the reference> or set NANOSAUR2_REFERENCE")
     sys.path.insert(0, os.path.join(args.reference, "tools"))
     import reference as R  # noqa: E402  (the unmodified reference module)
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    write_linear(R, args.out)
-    if args.only == "linear":
+    if args.only in (None, "linear"):
+        write_linear(R, args.out)
+    if args.only in (None, "gemma_sublayer"):
+        write_gemma_sublayer(R, args.out)
+    if args.only:
         return
 
     # ---- DiT: 4x5 latent (20 image tokens), 10 text slots with emphasis weights and dropped tokens

@@ -46,7 +46,8 @@ def test_struct_layouts_match_c(tmp_path):
                    'offsetof(nsa_seq_shard, qkv_text_row0));printf("%zu %zu %zu %zu\\n", sizeof(nsa_proj_desc),'
                    'offsetof(nsa_proj_desc, x_rows), offsetof(nsa_proj_desc, text_rows), offsetof(nsa_proj_desc, b_kv));'
                    'printf("%zu %zu %zu\\n", sizeof(nsa_linear_desc), offsetof(nsa_linear_desc, lda), '
-                   'offsetof(nsa_linear_desc, act));return 0;}\n')
+                   'offsetof(nsa_linear_desc, act));printf("%zu %zu %zu\\n", sizeof(nsa_rmsnorm_desc), '
+                   'offsetof(nsa_rmsnorm_desc, ldy), offsetof(nsa_rmsnorm_desc, eps));return 0;}\n')
     exe = tmp_path / "sizes"
     subprocess.run(["gcc", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)], check=True)
     got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
@@ -54,7 +55,8 @@ def test_struct_layouts_match_c(tmp_path):
             _lib.FusedDesc.b_begin.offset, ctypes.sizeof(_lib.KernelStat), _lib.KernelStat.bytes.offset,
             ctypes.sizeof(_lib.SeqShard), _lib.SeqShard.qkv_text_row0.offset, ctypes.sizeof(_lib.ProjDesc),
             _lib.ProjDesc.x_rows.offset, _lib.ProjDesc.text_rows.offset, _lib.ProjDesc.b_kv.offset,
-            ctypes.sizeof(_lib.LinearDesc), _lib.LinearDesc.lda.offset, _lib.LinearDesc.act.offset]
+            ctypes.sizeof(_lib.LinearDesc), _lib.LinearDesc.lda.offset, _lib.LinearDesc.act.offset,
+            ctypes.sizeof(_lib.RmsnormDesc), _lib.RmsnormDesc.ldy.offset, _lib.RmsnormDesc.eps.offset]
     assert got == want
 
 
@@ -206,3 +208,31 @@ def test_projection_and_linear_validation():
     assert lin() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # act 0 or 1
     ld.act = 0
     assert lin(bias=fake + 4) == _lib.NSA_ERR_INVALID_ARGUMENT                              # unaligned bias
+
+
+def test_rmsnorm_validation():
+    """nsa_rmsnorm rejects bad arguments before touching the device (no GPU needed)."""
+    L = _lib.lib()
+    fake = 1 << 32
+    d = _lib.RmsnormDesc()
+    d.rows, d.cols, d.eps = 1024, 640, 1e-6
+
+    def rms(x=fake, w=fake + (1 << 28), y=fake + (1 << 30)):
+        return L.nsa_rmsnorm(ctypes.byref(d), x, w, y, None)
+    assert L.nsa_rmsnorm(None, fake, fake, fake, None) == _lib.NSA_ERR_INVALID_ARGUMENT
+    assert rms(w=None) == _lib.NSA_ERR_INVALID_ARGUMENT                                     # missing weight
+    d.cols = 0
+    assert rms() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # cols >= 1
+    d.cols, d.ldx = 640, 600
+    assert rms() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # ldx < cols
+    d.ldx, d.out_dtype = 0, 7
+    assert rms() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # bad dtype
+    d.out_dtype, d.accumulate = _lib.NSA_BF16, 1
+    assert rms() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # accumulate needs fp32
+    d.out_dtype, d.accumulate, d.eps = _lib.NSA_F32, 0, -1.0
+    assert rms() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # eps >= 0
+    d.eps = 1e-6
+    assert rms(y=fake + 4 * 640) == _lib.NSA_ERR_INVALID_ARGUMENT                           # Y overlaps X
+    assert b"overlap" in L.nsa_last_error()
+    d.rows = 0
+    assert rms(x=None, w=None, y=None) == _lib.NSA_OK                                       # empty: nothing to do

@@ -1,0 +1,135 @@
+"""nsa_rmsnorm and the Gemma layer's attention half built on it, against the CPU oracle.
+
+* ops.rmsnorm (app/gpu/ops.js:111-116, kernels.js:62-80): fp32 and bf16 outputs, the fused
+  accumulate (gemma3.js:74-77), the vector and the scalar paths, rows longer than the register cache.
+* blocks.gemma_attention_sublayer (app/models/gemma3.js:62-77; tools/reference.py:187-196) against
+  the reference's own layers 0 and 5 (tests/golden/gemma_sublayer.npz, a 64-wide residual stream)
+  and against the oracle at the model's width (640) on a batch of two 1024-token sequences.
+
+Tolerances.  rmsnorm: fp32 in, fp32 math; only the order of the sum of squares differs, so 1e-5
+relative.  The sublayer computes its GEMM operands in bf16 (h, q', k', v, P, a: about 2^-9 relative
+each); the post-attention RMSNorm rescales o to unit RMS, so those roundings show as absolute error
+on the O(1) update.  Emulating the bf16 roundings on the CPU gives 0.021 max-abs on an update of
+|x| <= 3.8; the test allows 6e-2 max-abs and asks for a cosine >= 0.9999 between the updates."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib_loaded():
+    torch.cuda.set_device(DEV)
+    from nanosaur2_web_b200 import _lib
+    _lib.lib()
+    yield
+    torch.cuda.synchronize()
+
+
+def t(x, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(device=DEV, dtype=dtype)
+
+
+def check_device():
+    from nanosaur2_web_b200.ops import check_device as chk
+    chk(DEV)
+
+
+@pytest.mark.parametrize("rows,cols,ldx,ldy", [(1000, 640, 640, 640), (37, 100, 100, 104), (19, 101, 103, 101),
+                                               (9, 2000, 2000, 2000), (1, 4, 4, 4)])
+def test_rmsnorm_f32_bf16_accumulate(rows, cols, ldx, ldy):
+    from nanosaur2_web_b200.ops import rmsnorm
+    rng = np.random.default_rng(rows * 7 + cols)
+    xs = (3.0 * rng.standard_normal((rows, ldx))).astype(np.float32)
+    w = (1.0 + 0.25 * rng.standard_normal(cols)).astype(np.float32)
+    x = t(xs)[:, :cols]
+    want = O.rms_norm(xs[:, :cols], w, 1e-6, acc=np.float64)
+    # fp32 output into a wider buffer whose other columns stay untouched
+    y = torch.full((rows, ldy), 5.0, device=DEV)
+    rmsnorm(x, t(w), cols, 1e-6, y[:, :cols])
+    check_device()
+    got = y.cpu().numpy()
+    np.testing.assert_allclose(got[:, :cols], want, rtol=1e-5, atol=1e-6)
+    assert (got[:, cols:] == 5.0).all()
+    # bf16 output (the next GEMM's operand)
+    yb = torch.empty((rows, ldy), dtype=torch.bfloat16, device=DEV)[:, :cols]
+    rmsnorm(x, t(w), cols, 1e-6, yb)
+    check_device()
+    np.testing.assert_allclose(yb.float().cpu().numpy(), want, rtol=2 ** -8, atol=1e-6)
+    # accumulate: Y += norm(X)
+    base = rng.standard_normal((rows, ldy)).astype(np.float32)
+    ya = t(base)
+    rmsnorm(x, t(w), cols, 1e-6, ya[:, :cols], accumulate=True)
+    check_device()
+    got = ya.cpu().numpy()
+    np.testing.assert_allclose(got[:, :cols], base[:, :cols] + want, rtol=1e-5, atol=1e-5)
+    np.testing.assert_array_equal(got[:, cols:], base[:, cols:])
+
+
+def test_rmsnorm_zero_rows_is_a_no_op():
+    from nanosaur2_web_b200.ops import rmsnorm
+    x = torch.empty((0, 640), device=DEV)
+    y = rmsnorm(x, torch.ones(640, device=DEV))
+    check_device()
+    assert y.shape == (0, 640)
+
+
+def _sublayer_inputs(g):
+    w_qkv = np.concatenate([g["w_q"], g["w_k"], g["w_v"]])
+    return dict(in_norm=t(g["in_w"]), w_qkv=t(w_qkv, torch.bfloat16), q_norm=t(g["q_w"]), k_norm=t(g["k_w"]),
+                w_o=t(g["w_o"], torch.bfloat16), post_norm=t(g["post_w"]))
+
+
+def _check_update(got, x, want):
+    d, dw = got - x, want - x
+    assert np.abs(got - want).max() <= 6e-2, np.abs(got - want).max()
+    cos = float(np.sum(d * dw) / (np.linalg.norm(d) * np.linalg.norm(dw)))
+    assert cos >= 0.9999, cos
+
+
+@pytest.mark.parametrize("layer", [0, 5])
+def test_gemma_sublayer_matches_reference_layers(golden, layer):
+    """The reference's gemma_encode layers 0 (local, theta 1e4) and 5 (global, 1e6), 40 tokens."""
+    from nanosaur2_web_b200.blocks import GEMMA_HEAD_DIM, gemma_attention_sublayer
+    from nanosaur2_web_b200.ops import ropeTable
+    g = golden("gemma_sublayer")
+    x_in, want = g[f"x_in{layer}"], g[f"x_mid{layer}"]
+    L = x_in.shape[0]
+    x = t(x_in[None])
+    gemma_attention_sublayer(x, **_sublayer_inputs(g), cs=ropeTable(L, GEMMA_HEAD_DIM, O.gemma_rope_theta(layer), DEV))
+    check_device()
+    _check_update(x[0].cpu().numpy(), x_in, want)
+
+
+def test_gemma_sublayer_model_width_batch():
+    """hidden 640, B = 2 x 1024 tokens, a local layer with the 512-key window, against the oracle."""
+    from nanosaur2_web_b200.blocks import GEMMA_HEAD_DIM, gemma_attention_sublayer, gemma_sublayer_buffers
+    from nanosaur2_web_b200.ops import ropeTable
+    from tests._helpers import bf16_round
+    B, L, Hd, window = 2, 1024, 640, 512
+    rng = np.random.default_rng(11)
+    g = {"in_w": (1.0 + 0.25 * rng.standard_normal(Hd)).astype(np.float32),
+         "post_w": (1.0 + 0.25 * rng.standard_normal(Hd)).astype(np.float32),
+         "q_w": (1.0 + 0.25 * rng.standard_normal(256)).astype(np.float32),
+         "k_w": (1.0 + 0.25 * rng.standard_normal(256)).astype(np.float32),
+         "w_q": bf16_round(rng.standard_normal((1024, Hd), dtype=np.float32) / np.sqrt(Hd)),
+         "w_k": bf16_round(rng.standard_normal((256, Hd), dtype=np.float32) / np.sqrt(Hd)),
+         "w_v": bf16_round(rng.standard_normal((256, Hd), dtype=np.float32) / np.sqrt(Hd)),
+         "w_o": bf16_round(rng.standard_normal((Hd, 1024), dtype=np.float32) / 32.0)}
+    x_in = (8.0 * rng.standard_normal((B, L, Hd))).astype(np.float32)
+    x = t(x_in)
+    bufs = gemma_sublayer_buffers(B, L, Hd, DEV)
+    gemma_attention_sublayer(x, **_sublayer_inputs(g), cs=ropeTable(L, GEMMA_HEAD_DIM, 1e4, DEV), window=window,
+                             buffers=bufs)
+    check_device()
+    got = x.cpu().numpy()
+    for b in range(B):
+        want = O.gemma_attention_sublayer(x_in[b], g["in_w"], g["w_q"], g["w_k"], g["w_v"], g["q_w"], g["k_w"],
+                                          g["w_o"], g["post_w"], 1e4, window=window)
+        _check_update(got[b], x_in[b], want)

@@ -87,6 +87,19 @@ def test_gemma_layer(golden, layer):
     np.testing.assert_allclose(out, g["out"], rtol=1e-4, atol=2e-5)
 
 
+@pytest.mark.parametrize("layer", [0, 5])
+def test_gemma_attention_sublayer(golden, layer):
+    """Input norm -> q/k/v linears -> head norms + RoPE -> causal attention -> o linear ->
+    post-attention norm -> residual add, against gemma_encode's own layers (64-wide stream)."""
+    g = golden("gemma_sublayer")
+    x, want = g[f"x_in{layer}"], g[f"x_mid{layer}"]
+    got = O.gemma_attention_sublayer(x, g["in_w"], g["w_q"], g["w_k"], g["w_v"], g["q_w"], g["k_w"], g["w_o"],
+                                     g["post_w"], O.gemma_rope_theta(layer))
+    assert got.shape == x.shape == (40, 64)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+    assert np.abs(want - x).max() > 0.1   # the sublayer changed the stream
+
+
 def test_batched_joint_matches_unbatched(golden):
     g = golden("dit_joint_block")
     L, Lt = g["q_raw"].shape[0], g["ky_raw"].shape[0]
