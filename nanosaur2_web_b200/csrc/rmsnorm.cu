@@ -4,8 +4,9 @@
 // ops.js:188-192) as one pass: Y[r][c] += X[r][c] * rsqrt(...) * w[c].  The product keeps the
 // reference's order, (x * r) * w, so the only difference is the order of the sum of squares.
 //
-// One warp per row, eight rows per 256-thread block.  Rows of up to 1024 fp32 values stay in
-// registers (eight 16-byte loads per lane); longer rows are read a second time (from L1).  The
+// One warp per row, eight rows per 256-thread block.  Rows of up to 640 fp32 values stay in
+// registers (five 16-byte loads per lane, with the weights and, accumulating, Y requested in the same
+// round trip); longer rows read the rest a second time (from L1).  The
 // kernel is HBM-bound: X is read once, Y written once (and read once when accumulating); bf16 output
 // feeds the next GEMM's A operand directly (the QKV projection of the Gemma layer).
 #include <cuda_bf16.h>
@@ -17,7 +18,7 @@ namespace nsa {
 namespace {
 
 constexpr int kRmsWarps = 8;
-constexpr int kRmsCache = 8;   // float4 per lane held in registers
+constexpr int kRmsCache = 5;   // float4 per lane held in registers: a 640-wide row (Gemma's hidden size)
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -27,9 +28,9 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 __device__ __forceinline__ float sq4(float4 v) { return v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
 
+// y = (x * r) * w for four values, then stored (bf16 / fp32) or added to `acc` (the prefetched Y).
 template <bool BF16, bool ACC>
-__device__ __forceinline__ void emit4(const RmsParams& p, int64_t row, int i, float4 v, float r) {
-  const float4 w = reinterpret_cast<const float4*>(p.w)[i];
+__device__ __forceinline__ void emit4(const RmsParams& p, int64_t row, int i, float4 v, float r, float4 w, float4 acc) {
   const float4 y = make_float4(v.x * r * w.x, v.y * r * w.y, v.z * r * w.z, v.w * r * w.w);
   if constexpr (BF16) {
     __nv_bfloat162 lo = __floats2bfloat162_rn(y.x, y.y), hi = __floats2bfloat162_rn(y.z, y.w);
@@ -39,12 +40,10 @@ __device__ __forceinline__ void emit4(const RmsParams& p, int64_t row, int i, fl
     reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.y) + row * p.ldy)[i] = u;
   } else {
     float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.y) + row * p.ldy) + i;
-    if constexpr (ACC) {
-      const float4 o = *dst;
-      *dst = make_float4(o.x + y.x, o.y + y.y, o.z + y.z, o.w + y.w);
-    } else {
+    if constexpr (ACC)
+      *dst = make_float4(acc.x + y.x, acc.y + y.y, acc.z + y.z, acc.w + y.w);
+    else
       *dst = y;
-    }
   }
 }
 
@@ -71,23 +70,41 @@ __global__ void __launch_bounds__(kRmsWarps * 32) rmsnorm_kernel(const RmsParams
   const float* xr = p.x + row * p.ldx;
   float ss = 0.f;
   if constexpr (VEC) {
+    // X, the weights and (accumulating) Y of the cached part are all requested before the reduction,
+    // so a row costs one memory round trip instead of two
     const float4* x4 = reinterpret_cast<const float4*>(xr);
+    const float4* w4 = reinterpret_cast<const float4*>(p.w);
+    float4* y4 = ACC ? reinterpret_cast<float4*>(static_cast<float*>(p.y) + row * p.ldy) : nullptr;
     const int nv = p.cols / 4;
-    float4 v[kRmsCache];
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 v[kRmsCache], wv[kRmsCache], yv[ACC ? kRmsCache : 1];
 #pragma unroll
     for (int j = 0; j < kRmsCache; ++j) {
       const int i = lane + 32 * j;
-      v[j] = i < nv ? __ldg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-      ss += sq4(v[j]);
+      const bool in = i < nv;
+      v[j] = in ? __ldg(x4 + i) : z;
+      wv[j] = in ? __ldg(w4 + i) : z;
+      if constexpr (ACC) yv[j] = in ? y4[i] : z;
     }
+#pragma unroll
+    for (int j = 0; j < kRmsCache; ++j) ss += sq4(v[j]);
     for (int i = lane + 32 * kRmsCache; i < nv; i += 32) ss += sq4(__ldg(x4 + i));
     const float r = rsqrtf(warp_sum(ss) / (float)p.cols + p.eps);
 #pragma unroll
     for (int j = 0; j < kRmsCache; ++j) {
       const int i = lane + 32 * j;
-      if (i < nv) emit4<BF16, ACC>(p, row, i, v[j], r);
+      if (i >= nv) continue;
+      if constexpr (ACC)
+        emit4<BF16, ACC>(p, row, i, v[j], r, wv[j], yv[j]);
+      else
+        emit4<BF16, ACC>(p, row, i, v[j], r, wv[j], z);
     }
-    for (int i = lane + 32 * kRmsCache; i < nv; i += 32) emit4<BF16, ACC>(p, row, i, __ldg(x4 + i), r);
+    for (int i = lane + 32 * kRmsCache; i < nv; i += 32) {
+      if constexpr (ACC)
+        emit4<BF16, ACC>(p, row, i, __ldg(x4 + i), r, __ldg(w4 + i), y4[i]);
+      else
+        emit4<BF16, ACC>(p, row, i, __ldg(x4 + i), r, __ldg(w4 + i), z);
+    }
   } else {
     for (int c = lane; c < p.cols; c += 32) {
       const float t = xr[c];
