@@ -82,3 +82,21 @@ def test_gather_views_are_in_place_chunks():
         # ncclAllGather's in-place form: sendbuff = recvbuff + rank * sendcount
         assert inp.data_ptr() == out.data_ptr() + rank * inp.numel() * inp.element_size()
         assert out.data_ptr() == kv.data_ptr() + kv_rows * ld * kv.element_size()
+
+
+def test_rmsnorm_and_sublayer_host_checks():
+    """Argument errors of ops.rmsnorm and blocks.gemma_attention_sublayer raise NsaError before any
+    device work, as the reference's operators throw synchronously."""
+    import torch
+
+    from nanosaur2_web_b200.ops import NsaError, rmsnorm
+    x = torch.zeros(2, 8, 64)
+    with pytest.raises(NsaError):
+        rmsnorm(x, torch.ones(64))                                    # host tensors
+    kw = dict(in_norm=None, w_qkv=None, q_norm=None, k_norm=None, post_norm=None, cs=None)
+    with pytest.raises(NsaError):
+        blocks.gemma_attention_sublayer(x.double(), w_o=torch.zeros(64, 1024), **kw)   # fp32 stream only
+    with pytest.raises(NsaError):
+        blocks.gemma_attention_sublayer(x[:, :, :32], w_o=torch.zeros(32, 1024), **kw)  # not contiguous
+    with pytest.raises(NsaError):
+        blocks.gemma_attention_sublayer(x, w_o=torch.zeros(64, 512), **kw)            # w_o [hidden, 1024]
