@@ -989,7 +989,26 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* d, const nsa_seq_shard
     pp.n_sets = 2;
     flops += 2.0 * pl.Bs * (pl.Lk - sp.L) * (double)(2 * d->Hkv) * D * K;
   }
-  cudaError_t e = profiled("projection", flops, 0.0, strm, [&] { return nsa::launch_projection(pp, D, tx, tw, strm); });
+  // head dim 256: the RoPE table as a [2 * rows][128] fp32 map (cos block, then sin block), boxes of
+  // [32 rows][16 values] with the 64-byte swizzle, for the epilogue's per-warp staging
+  CUtensorMap tcs;
+  const CUtensorMap* tcs_ptr = nullptr;
+  if (D == 256 && cs && d->sinOff > 0 && d->sinOff % (D / 2) == 0) {
+    EncodeTiledFn fn = encode_fn();
+    const cuuint64_t cd[2] = {(cuuint64_t)(D / 2), (cuuint64_t)(2 * (d->sinOff / (D / 2)))};
+    const cuuint64_t cst[1] = {(cuuint64_t)(D / 2) * 4};
+    const cuuint32_t cb[2] = {16, 32};
+    const cuuint32_t ce[2] = {1, 1};
+    if (fn && fn(&tcs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(cs), cd, cst, cb, ce,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+      tcs_ptr = &tcs;
+      pp.cs_tma = 1;
+      pp.cs_rows = (int)(d->sinOff / (D / 2));
+    }
+  }
+  cudaError_t e = profiled("projection", flops, 0.0, strm,
+                           [&] { return nsa::launch_projection(pp, D, tx, tw, tcs_ptr, strm); });
   if (e == cudaErrorNotSupported)
     return fail(NSA_ERR_UNSUPPORTED, "the projection's bias vectors do not fit in shared memory");
   if (e != cudaSuccess) return cuda_fail(e, "projection launch");

@@ -153,6 +153,8 @@ struct ProjParams {
   const float* k_w;        // [D] k RMSNorm weight
   const float* cs;         // RoPE table (image rows): cos [rows][D/2], sin at sin_off; null = none
   int64_t sin_off;
+  int cs_tma;              // head dim 256: the table is also mapped as tmCS ([2 cs_rows][128] fp32,
+  int cs_rows;             //   box [32 rows][16], 64-byte swizzle) and staged per epilogue warp by TMA
   float eps;
   const int* kv_len;       // [B_total] valid keys, or null (Lk)
   __nv_bfloat16* q_prime;
@@ -166,7 +168,7 @@ struct ProjParams {
 // vectors leave no room for a 2-stage ring.  tmX[s]: 3-D map [B][rows][K] over set s's input, box
 // [1][128][64], 128-byte swizzle; tmW[s]: 2-D map [N][K], box [heads-per-tile * D][64].
 cudaError_t launch_projection(ProjParams p, int D, const CUtensorMap* tmX, const CUtensorMap* tmW,
-                              cudaStream_t stream);
+                              const CUtensorMap* tmCS, cudaStream_t stream);
 int projection_heads_per_tile(int D);   // 0: unsupported head dim
 
 // Linear layer with the reference's GEMM epilogue (linear.cu): C = epilogue(alpha * A W^T) over M x N

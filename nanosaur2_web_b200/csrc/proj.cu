@@ -19,7 +19,8 @@
 //               columns, then bias + norm weight + RoPE, bf16 stores.  Bias and norm weights sit in
 //               shared memory.  Tensor-memory reads are few and wide (a wait costs about a thousand
 //               cycles while the next tile's MMAs run), and each chunk's cos / sin loads are issued
-//               before its tensor-memory wait.
+//               before its tensor-memory wait; at head dim 256 they come through shared memory, one
+//               TMA box of the warp's 32 table rows per chunk.
 #include "nsa_internal.h"
 #include "ptx.cuh"
 
@@ -39,8 +40,13 @@ struct ProjCfg {
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr uint32_t ACC_COLS = 256;            // TMEM columns per accumulator
   static constexpr uint32_t IDESC = idesc_bf16_f32(128, NT, 0, 0);
+  // One head per tile: the RoPE rows come through shared memory (see the epilogue)
+  static constexpr bool kTableTma = D == 256;
   static_assert(NT % 16 == 0 && NT <= 256 && STAGE % 1024 == 0, "projection tile");
 };
+
+constexpr int kTableWarpBytes = 4096;             // cos [32][16] fp32 + sin [32][16] fp32
+constexpr int kTableBytes = 8 * kTableWarpBytes;  // eight epilogue warps (a multiple of 1024)
 
 // 16 consecutive floats of a shared-memory vector (bias, norm weight) in four 16-byte reads; every
 // offset used is a multiple of 16 floats.
@@ -67,13 +73,18 @@ __device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, const float (&
 template <int D>
 __global__ void __launch_bounds__(kProjThreads, 1)
     proj_kernel(const __grid_constant__ CUtensorMap tmX0, const __grid_constant__ CUtensorMap tmW0,
-                const __grid_constant__ CUtensorMap tmX1, const __grid_constant__ CUtensorMap tmW1, const ProjParams p) {
+                const __grid_constant__ CUtensorMap tmX1, const __grid_constant__ CUtensorMap tmW1,
+                const __grid_constant__ CUtensorMap tmCS, const ProjParams p) {
   using C = ProjCfg<D>;
   const int S = p.stages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int nb0 = p.set[0].n_tiles * C::NT, nb1 = p.n_sets > 1 ? p.set[1].n_tiles * C::NT : 0;
-  float* sbias0 = reinterpret_cast<float*>(smem + S * C::STAGE);   // [nb0] (zeros without a bias)
+  // head dim 256: per epilogue warp, the cos and sin rows of its 32 output rows for one 16-pair chunk
+  // ([32][16] fp32 each, 64-byte swizzle), staged by TMA
+  const bool cs_tma = C::kTableTma && p.cs_tma;
+  uint8_t* stable = smem + S * C::STAGE;                            // [8 warps][cos 2 KB | sin 2 KB]
+  float* sbias0 = reinterpret_cast<float*>(stable + (cs_tma ? kTableBytes : 0));   // [nb0] (zeros without a bias)
   float* sbias1 = sbias0 + nb0;                                    // [nb1]
   float* sqw = sbias1 + nb1;                                       // [D] q norm weight
   float* skw = sqw + D;                                            // [D] k norm weight
@@ -83,7 +94,8 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   uint64_t* acc_empty = acc_full + 2;   // [2] accumulator read out (256 epilogue arrivals)
   uint64_t* drain = acc_empty + 2;      // MMAs of an aborted CTA finished
   uint64_t* pbar = drain + 1;           // bias vectors and norm weights landed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pbar + 1);
+  uint64_t* tbar = pbar + 1;            // [8] one epilogue warp's table chunk landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tbar + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint64_t to = p.timeout_ns;
@@ -99,6 +111,7 @@ __global__ void __launch_bounds__(kProjThreads, 1)
     }
     mbar_init(drain, 1);
     mbar_init(pbar, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&tbar[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -236,6 +249,20 @@ __global__ void __launch_bounds__(kProjThreads, 1)
     const int hh0 = C::HPT >= 2 ? group : 0;
     bool params_ready = false;
     int t = 0;
+    // Head dim 256: a thread's RoPE row is 128 cos + 128 sin values, and 32 lanes of a warp hold 32
+    // rows, so per-thread loads would touch 32 lines per instruction.  Instead lane 0 brings the warp's
+    // 32 table rows of one 16-pair chunk into shared memory with two TMA box loads (64-byte swizzle)
+    // and every lane reads its row from there without bank conflicts.  One chunk is in flight at a
+    // time: the next is issued as soon as the current one has been read.
+    uint8_t* tbuf = stable + ew * kTableWarpBytes;
+    uint32_t t_issued = 0, t_done = 0;   // table loads of this warp (warp-uniform counts)
+    bool aborted = false;
+    auto issue_table = [&](int c, int tr0) {   // lane 0 only
+      fence_proxy_async_smem();   // the lanes' reads of the previous chunk come before the overwrite
+      mbar_arrive_expect_tx(&tbar[ew], kTableWarpBytes);
+      tma_load_2d(tbuf, &tmCS, &tbar[ew], c, tr0);
+      tma_load_2d(tbuf + kTableWarpBytes / 2, &tmCS, &tbar[ew], c, p.cs_rows + tr0);
+    };
     for (int u = blockIdx.x; u < tiles; u += G) {
       int si, bl, m0, nt, part, h0;
       if (!decode(u, si, bl, m0, nt, part, h0)) continue;
@@ -260,6 +287,16 @@ __global__ void __launch_bounds__(kProjThreads, 1)
       const float* wn = part == 0 ? sqw : (part == 1 ? skw : nullptr);
       const bool rope = q.image && part < 2 && p.cs != nullptr && valid;
       const int rrow = q.rope_row0 + r;
+      // TMA table path: decided per warp (rows without data are rotated too, then zeroed); the first
+      // chunk's rows are in flight during the accumulator wait.  Table rows past the cos block read
+      // sin rows or the zero fill, only for rows that hold no data.
+      const int tr0 = q.rope_row0 + m0 + quarter * 32;
+      const bool rope_w = cs_tma && q.image && part < 2 && p.cs != nullptr && m0 + quarter * 32 < q.valid_q;
+      if (rope_w) {
+        if (lane == 0) issue_table(pair0, tr0);
+        ++t_issued;
+      }
+      const bool rot = cs_tma ? rope_w : rope;
       bool got = wait_bounded(&acc_full[a], (t >> 1) & 1, abort_flag, p.err, kErrTimeoutProjection, to);
       if (got && !params_ready) {
         got = wait_bounded(pbar, 0, abort_flag, p.err, kErrTimeoutProjection, to);
@@ -313,7 +350,28 @@ __global__ void __launch_bounds__(kProjThreads, 1)
           if (c < pair0 || c >= pair1) continue;
           // the RoPE pairs' cos / sin first: their global loads are then in flight during the TMEM wait
           float cc[16], sn[16];
-          if (rope) {
+          if (rope_w) {
+            const bool ok = wait_bounded(&tbar[ew], t_done & 1, abort_flag, p.err, kErrTimeoutProjection, to);
+            if (!__all_sync(0xffffffffu, ok)) {
+              aborted = true;
+              break;
+            }
+            ++t_done;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              // the 64-byte swizzle XORs the 16-byte chunk index with bits 1-2 of the row
+              const int phys = k ^ ((lane >> 1) & 3);
+              const float4 c4 = *reinterpret_cast<const float4*>(tbuf + lane * 64 + phys * 16);
+              const float4 s4 = *reinterpret_cast<const float4*>(tbuf + kTableWarpBytes / 2 + lane * 64 + phys * 16);
+              cc[4 * k] = c4.x; cc[4 * k + 1] = c4.y; cc[4 * k + 2] = c4.z; cc[4 * k + 3] = c4.w;
+              sn[4 * k] = s4.x; sn[4 * k + 1] = s4.y; sn[4 * k + 2] = s4.z; sn[4 * k + 3] = s4.w;
+            }
+            __syncwarp();
+            if (c + 16 < pair1) {
+              if (lane == 0) issue_table(c + 16, tr0);
+              ++t_issued;
+            }
+          } else if (rope && !cs_tma) {
             const float4* cp = reinterpret_cast<const float4*>(p.cs + (int64_t)rrow * (D / 2) + c);
             const float4* sp = reinterpret_cast<const float4*>(p.cs + p.sin_off + (int64_t)rrow * (D / 2) + c);
 #pragma unroll
@@ -342,7 +400,7 @@ __global__ void __launch_bounds__(kProjThreads, 1)
               x2[i] *= rn * b2[i];
             }
           }
-          if (rope) {
+          if (rot) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const float xa = x1[i], xc = x2[i];
@@ -359,12 +417,16 @@ __global__ void __launch_bounds__(kProjThreads, 1)
             store_bf16x16(dst + D / 2 + c, x2);
           }
         }
+        if (aborted) break;
       }
+      if (aborted) break;
       // the accumulator has been read: the issuer may start the tile after next in it
       tc_fence_before();
       mbar_arrive(&acc_empty[a]);
       ++t;
     }
+    // a table load still in flight (the CTA gave up) lands before the CTA's shared memory goes away
+    if (t_issued > t_done && lane == 0) wait_drain(&tbar[ew], t_done & 1, to);
   }
   tc_fence_before();
   __syncthreads();
@@ -375,7 +437,8 @@ __global__ void __launch_bounds__(kProjThreads, 1)
 }
 
 template <int D>
-cudaError_t launch_proj_d(ProjParams p, const CUtensorMap* tmX, const CUtensorMap* tmW, cudaStream_t stream) {
+cudaError_t launch_proj_d(ProjParams p, const CUtensorMap* tmX, const CUtensorMap* tmW, const CUtensorMap* tmCS,
+                          cudaStream_t stream) {
   using C = ProjCfg<D>;
   static int sms = 0;
   if (!sms) {
@@ -394,7 +457,11 @@ cudaError_t launch_proj_d(ProjParams p, const CUtensorMap* tmX, const CUtensorMa
   if (tiles > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   // ring depth: as many stages (up to 5) as fit beside the bias vectors, the norm weights, the
   // barriers and the alignment slack
-  const size_t fixed = 1024 + bias_bytes + 2 * D * 4 + 256;
+  if (!C::kTableTma || !tmCS) p.cs_tma = 0;
+  // the table buffers take shared memory only while a ring of two or more stages still fits
+  if (p.cs_tma && (232448 - (long long)(1024 + kTableBytes + bias_bytes + 2 * D * 4 + 256)) / C::STAGE < 2)
+    p.cs_tma = 0;
+  const size_t fixed = 1024 + (p.cs_tma ? kTableBytes : 0) + bias_bytes + 2 * D * 4 + 256;
   const long long room = 232448 - (long long)fixed;
   int stages = room > 0 ? (int)(room / C::STAGE) : 0;
   if (stages > 5) stages = 5;
@@ -405,7 +472,7 @@ cudaError_t launch_proj_d(ProjParams p, const CUtensorMap* tmX, const CUtensorMa
   if (e != cudaSuccess) return e;
   const int grid = tiles < sms ? (int)tiles : sms;
   proj_kernel<D><<<grid, kProjThreads, smem, stream>>>(tmX[0], tmW[0], tmX[p.n_sets > 1 ? 1 : 0],
-                                                       tmW[p.n_sets > 1 ? 1 : 0], p);
+                                                       tmW[p.n_sets > 1 ? 1 : 0], p.cs_tma ? *tmCS : tmX[0], p);
   return cudaGetLastError();
 }
 
@@ -422,12 +489,12 @@ int projection_heads_per_tile(int D) {
 }
 
 cudaError_t launch_projection(ProjParams p, int D, const CUtensorMap* tmX, const CUtensorMap* tmW,
-                              cudaStream_t stream) {
+                              const CUtensorMap* tmCS, cudaStream_t stream) {
   switch (D) {
-    case 64: return launch_proj_d<64>(p, tmX, tmW, stream);
-    case 96: return launch_proj_d<96>(p, tmX, tmW, stream);
-    case 128: return launch_proj_d<128>(p, tmX, tmW, stream);
-    case 256: return launch_proj_d<256>(p, tmX, tmW, stream);
+    case 64: return launch_proj_d<64>(p, tmX, tmW, tmCS, stream);
+    case 96: return launch_proj_d<96>(p, tmX, tmW, tmCS, stream);
+    case 128: return launch_proj_d<128>(p, tmX, tmW, tmCS, stream);
+    case 256: return launch_proj_d<256>(p, tmX, tmW, tmCS, stream);
     default: return cudaErrorInvalidValue;
   }
 }
