@@ -96,7 +96,8 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 }
 
 // 2D tiled bulk load global -> shared, completing `bytes` on `bar`.  `x` (innermost coordinate)
-// is always a multiple of 32 elements here, so every copy starts on a 16-byte boundary.
+// times the element size is always a multiple of 16 bytes here (32 or 64 bf16 columns, 16 fp32 RoPE
+// table columns), so every copy starts on a 16-byte boundary.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
