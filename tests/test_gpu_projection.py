@@ -228,3 +228,28 @@ def test_gemma_projected_layer(theta, window, L):
         want = O.gemma_attention(qkv[:, :4 * GD], qkv[:, 4 * GD:5 * GD], qkv[:, 5 * GD:], q_w, k_w, theta, window,
                                  acc=np.float64)
         assert_close_bf16(got[bb], want, GD, what=f"gemma projected theta={theta} window={window} b={bb}")
+
+
+def test_gemma_projected_unaligned_sin_block():
+    """Head dim 256 with a RoPE table whose sin block does not start on a row boundary (sinOff =
+    L*128 + 4): the epilogue cannot map the table as rows and reads each row's cos / sin directly.
+    Same results as the oracle (and as the staged path of the test above)."""
+    from nanosaur2_web_b200.blocks import gemma_layer_attention_projected
+    from nanosaur2_web_b200.ops import RopeTable
+    B, L, K, GD, theta = 1, 200, 640, 256, 1e4
+    rng = np.random.default_rng(77)
+    x = bf16_round(rng.standard_normal((B, L, K), dtype=np.float32))
+    w = bf16_round(rng.standard_normal((6 * GD, K), dtype=np.float32) / np.sqrt(K))
+    q_w = (1.0 + 0.2 * rng.standard_normal(GD)).astype(np.float32)
+    k_w = (1.0 + 0.2 * rng.standard_normal(GD)).astype(np.float32)
+    cos, sin = O.rope_1d(L, theta, GD)
+    buf = np.zeros(L * GD + 4, np.float32)
+    buf[:L * GD // 2] = cos.reshape(-1)
+    buf[L * GD // 2 + 4:] = sin.reshape(-1)
+    cs = RopeTable(t(buf), L * GD // 2 + 4, L, GD)
+    out = gemma_layer_attention_projected(t(x, torch.bfloat16), w_qkv=t(w, torch.bfloat16), q_norm=t(q_w),
+                                          k_norm=t(k_w), cs=cs, out_dtype=torch.float32)
+    check_device()
+    qkv = O.linear(x[0], w, acc=np.float64)
+    want = O.gemma_attention(qkv[:, :4 * GD], qkv[:, 4 * GD:5 * GD], qkv[:, 5 * GD:], q_w, k_w, theta, acc=np.float64)
+    assert_close_bf16(out[0].cpu().numpy(), want, GD, what="gemma projected, sin block off the row grid")
