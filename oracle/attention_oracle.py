@@ -223,6 +223,33 @@ def gemma_attention(q_raw, k_raw, v, q_w, k_w, theta, window=0, eps=1e-6, acc=np
     return attention(q, k, v, H, D, group=H // KH, causal=True, window=window, acc=acc)
 
 
+def group_norm(x, groups, w, b, eps=1e-6, acc=np.float32):
+    """GroupNorm over x [C, ...]: mean and biased variance per group of C/groups channels, then
+    (x - mean) / sqrt(var + eps) * w[c] + b[c] (F.group_norm as tools/reference.py:339 calls it;
+    app/models/vae.js:78 ops.groupNorm without SiLU)."""
+    x = np.asarray(x, acc)
+    C = x.shape[0]
+    g = x.reshape(groups, -1)
+    mean = g.mean(axis=1, keepdims=True)
+    var = ((g - mean) ** 2).mean(axis=1, keepdims=True)
+    n = ((g - mean) / np.sqrt(var + acc(eps))).reshape(x.shape)
+    shape = (C,) + (1,) * (x.ndim - 1)
+    return n * np.asarray(w, acc).reshape(shape) + np.asarray(b, acc).reshape(shape)
+
+
+def vae_attention(x, gn_w, gn_b, w_q, b_q, w_k, b_k, w_v, b_v, w_o, b_o, groups=32, eps=1e-6, acc=np.float32):
+    """The VAE decoder's single-head attention block over all pixels (tools/reference.py:352-357;
+    app/models/vae.js:77-88): x [C, h, w]; n = group_norm(x); q/k/v = 1x1 convolutions of n (linears
+    over the channels, weights [C, C]); softmax(q k^T / sqrt(C)) v over the h*w pixels with head dim
+    C; then x + proj_out(a).  Returns [C, h, w]."""
+    x = np.asarray(x, acc)
+    C = x.shape[0]
+    n = group_norm(x, groups, gn_w, gn_b, eps, acc).reshape(C, -1).T          # [hw, C]
+    q, k, v = (linear(n, w, bb, acc) for w, bb in ((w_q, b_q), (w_k, b_k), (w_v, b_v)))
+    a = attention(q, k, v, 1, C, acc=acc)                                    # [hw, C]
+    return x + linear(a, w_o, b_o, acc).T.reshape(x.shape)
+
+
 def gemma_attention_sublayer(x, in_w, w_q, w_k, w_v, q_w, k_w, w_o, post_w, theta, window=0, eps=1e-6,
                              acc=np.float32):
     """The attention half of one Gemma3 layer on the residual stream x [L, hidden]

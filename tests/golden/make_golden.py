@@ -20,6 +20,9 @@ drives its real code paths with small seeded stand-in weights (no model files ex
 * the attention half of ``gemma_encode``'s layers 0 and 5 (``:187-196``: input norm, q/k/v linears,
   head norms, RoPE, causal SDPA, o linear, post-attention norm, residual add) on a 64-wide residual
   stream with bf16-exact linear weights (``--only gemma_sublayer``).
+* ``VAE.attn`` (``:352-357``), the VAE decoder's single-head attention block (group norm, q/k/v 1x1
+  convolutions, SDPA with head dim C, proj_out, residual) on a 64 x 6 x 5 activation
+  (``--only vae_attention``).
 
 The qkv projection outputs of the DiT are rounded to bf16 inside the reference run (a hook on its
 ``lin``), so the bf16 CUDA path sees exactly the inputs the fp32 reference saw.  The Gemma inputs
@@ -239,6 +242,36 @@ def write_gemma_sublayer(R, out, L=40, hidden=64):
         w_v=np32(W(p + "self_attn.v_proj.weight")), w_o=np32(W(p + "self_attn.o_proj.weight")))
 
 
+def write_vae_attention(R, out, C=64, h=6, w=5):
+    """VAE.attn (tools/reference.py:352-357) on a [1, C, h, w] activation with seeded stand-in weights:
+    group norm (32 groups), q/k/v 1x1 convolutions, single-head SDPA over the h*w pixels with head dim
+    C, proj_out and the residual."""
+
+    class Params:
+        def __init__(self, d):
+            self.d = d
+
+        def __call__(self, name):
+            return self.d[name]
+
+        def has(self, name):
+            return name in self.d
+
+    gen = torch.Generator().manual_seed(55)
+    p = "decoder.mid.attn_1"
+    d = {p + ".norm.weight": 1.0 + 0.25 * torch.randn(C, generator=gen), p + ".norm.bias": 0.1 * torch.randn(C, generator=gen)}
+    for part in (".q", ".k", ".v", ".proj_out"):
+        d[p + part + ".weight"] = torch.randn(C, C, 1, 1, generator=gen) / C ** 0.5
+        d[p + part + ".bias"] = 0.1 * torch.randn(C, generator=gen)
+    x = 2.0 * torch.randn(1, C, h, w, generator=gen)
+    y = R.VAE(Params(d)).attn(x, p)
+    np.savez_compressed(
+        os.path.join(out, "vae_attention.npz"), x=np32(x[0]), y=np32(y[0]),
+        gn_w=np32(d[p + ".norm.weight"]), gn_b=np32(d[p + ".norm.bias"]),
+        **{f"w_{k}": np32(d[f"{p}.{n}.weight"].reshape(C, C)) for k, n in (("q", "q"), ("k", "k"), ("v", "v"), ("o", "proj_out"))},
+        **{f"b_{k}": np32(d[f"{p}.{n}.bias"]) for k, n in (("q", "q"), ("k", "k"), ("v", "v"), ("o", "proj_out"))})
+
+
 def np32(t):
     return t.detach().float().cpu().numpy().astype(np.float32)
 
@@ -271,7 +304,7 @@ def main():
     ap.add_argument("--reference", default=os.environ.get("NANOSAUR2_REFERENCE"),
                     help="checkout of the reference repository (or NANOSAUR2_REFERENCE)")
     ap.add_argument("--out", default=HERE)
-    ap.add_argument("--only", choices=["linear", "gemma_sublayer"], help="write one fixture only")
+    ap.add_argument("--only", choices=["linear", "gemma_sublayer", "vae_attention"], help="write one fixture only")
     args = ap.parse_args()
     if not args.reference:
         ap.error("pass --reference <checkout of the reference> or set NANOSAUR2_REFERENCE")
@@ -282,6 +315,8 @@ def main():
         write_linear(R, args.out)
     if args.only in (None, "gemma_sublayer"):
         write_gemma_sublayer(R, args.out)
+    if args.only in (None, "vae_attention"):
+        write_vae_attention(R, args.out)
     if args.only:
         return
 

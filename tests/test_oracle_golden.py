@@ -116,3 +116,15 @@ def test_batched_joint_matches_unbatched(golden):
     out2 = O.joint_attention_batched(qkv, L, Lt, [L + valid], g["q_w"], g["k_w"], g["cos"], g["sin"],
                                      bias=g["txt_bias"][None])
     np.testing.assert_allclose(out2[0], g["out"], rtol=1e-4, atol=1e-5)
+
+
+def test_vae_attention(golden):
+    """The VAE decoder's attention block (tools/reference.py:352-357; app/models/vae.js:77-88): group
+    norm, q/k/v 1x1 convolutions, single-head attention with head dim C over the pixels, proj_out,
+    residual, against the reference's own VAE.attn (C = 64, 6 x 5 pixels)."""
+    g = golden("vae_attention")
+    got = O.vae_attention(g["x"], g["gn_w"], g["gn_b"], g["w_q"], g["b_q"], g["w_k"], g["b_k"], g["w_v"], g["b_v"],
+                          g["w_o"], g["b_o"])
+    assert got.shape == g["x"].shape == (64, 6, 5)
+    np.testing.assert_allclose(got, g["y"], rtol=1e-4, atol=1e-4)
+    assert np.abs(g["y"] - g["x"]).max() > 0.05   # the block changed the activation
