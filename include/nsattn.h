@@ -290,6 +290,21 @@ typedef struct nsa_rmsnorm_desc {
 nsa_status nsa_rmsnorm(const nsa_rmsnorm_desc* desc, const float* X, const float* weight, void* Y, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * nsa_glu: ops.glu(gpu, x, act) (app/gpu/ops.js:141-148, kernels.js:346-360) over the [gate | up]
+ * halves of a gate_up linear's output:  Y[r*ldy + j] = act(X[r*ldx + j]) * X[r*ldx + I + j], j < I.
+ * act 0 = SiLU (SwiGLU), 1 = GELU with the tanh approximation (Gemma's MLP, app/models/gemma3.js:81).
+ * X fp32; Y fp32 or bf16 (the down projection's operand).  X and Y must not overlap.
+ * ------------------------------------------------------------------------------------------------ */
+typedef struct nsa_glu_desc {
+  int32_t rows, I;
+  int64_t ldx;         /* X row pitch in elements (0: 2*I) */
+  int64_t ldy;         /* Y row pitch in elements (0: I) */
+  int32_t act;         /* 0 SiLU, 1 GELU (tanh) */
+  int32_t out_dtype;   /* NSA_F32 or NSA_BF16 */
+} nsa_glu_desc;
+nsa_status nsa_glu(const nsa_glu_desc* desc, const float* X, void* Y, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
  * RoPE tables in the reference layout: cos block [L][D/2] then sin block [L][D/2] (sinOff = L*D/2).
  *   nsa_rope2d_table: app/models/common.js:28-43 (tools/reference.py:220-227): L = h*w tokens,
  *     the first D/4 pairs rotate by the centred column, the next D/4 by the centred row, theta 1e4.

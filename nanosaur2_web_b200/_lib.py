@@ -73,6 +73,11 @@ class RmsnormDesc(ctypes.Structure):
                 ("accumulate", _i32), ("eps", _f32)]
 
 
+class GluDesc(ctypes.Structure):
+    """nsa_glu_desc (include/nsattn.h)."""
+    _fields_ = [("rows", _i32), ("I", _i32), ("ldx", _i64), ("ldy", _i64), ("act", _i32), ("out_dtype", _i32)]
+
+
 class KernelStat(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 32), ("launches", _i64), ("total_ms", ctypes.c_double),
                 ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
@@ -105,6 +110,7 @@ SIGNATURES = {
                                         _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "nsa_linear": (_i32, [ctypes.POINTER(LinearDesc), _vp, _vp, _vp, _vp, _vp, _vp]),
     "nsa_rmsnorm": (_i32, [ctypes.POINTER(RmsnormDesc), _vp, _vp, _vp, _vp]),
+    "nsa_glu": (_i32, [ctypes.POINTER(GluDesc), _vp, _vp, _vp]),
     "nsa_rope2d_table": (_i32, [_i32, _i32, _i32, _vp, _vp]),
     "nsa_rope1d_table": (_i32, [_i32, _i32, _f32, _vp, _vp]),
     "nsa_check_device": (_i32, [_vp]),

@@ -20,6 +20,9 @@
   (app/models/gemma3.js:62-77; tools/reference.py:187-196): input RMSNorm to a bf16 operand, the
   projected attention above, the ``te.o`` linear, and the post-attention RMSNorm added into the
   stream, five launches.
+* ``gemma_mlp_sublayer(...)`` / ``gemma_layer(...)``: the MLP half (app/models/gemma3.js:78-89: pre-MLP
+  RMSNorm, gate_up linear, GELU-tanh GLU, down linear, post-MLP RMSNorm accumulated) and the whole
+  layer, attention half then MLP half.
 * ``gemma_layer_attention(...)``: one Gemma3 layer's attention, headNorm(q), headNorm(k) with the
   local/global RoPE table + causal GQA 4/1 attention (app/models/gemma3.js:63-70;
   tools/reference.py:186-194), with an optional sliding window.
@@ -35,7 +38,7 @@ import torch
 
 from . import _lib
 from ._lib import FusedDesc, NsaError, ProjDesc, SeqShard, check, lib
-from .ops import RopeTable, dtype_code, linear, rmsnorm, stream_handle
+from .ops import RopeTable, dtype_code, glu, linear, rmsnorm, stream_handle
 
 DIT_HEADS, DIT_HEAD_DIM = 16, 96
 GEMMA_HEADS, GEMMA_KV_HEADS, GEMMA_HEAD_DIM = 4, 1, 256
@@ -305,6 +308,53 @@ def gemma_attention_sublayer(x: torch.Tensor, *, in_norm: torch.Tensor, w_qkv: t
     linear(a.view(B * L, -1), w_o, out=o)
     rmsnorm(o, post_norm, hidden, eps, x.view(B * L, hidden), accumulate=True)
     return x
+
+
+def gemma_mlp_buffers(B: int, L: int, hidden: int, inter: int, device) -> dict:
+    """Intermediates of ``gemma_mlp_sublayer``: h2 (bf16 [B*L, hidden]), gu (fp32 [B*L, 2*inter]),
+    g (bf16 [B*L, inter]) and d (fp32 [B*L, hidden])."""
+    M = B * L
+    return {"h": torch.empty((M, hidden), dtype=torch.bfloat16, device=device),
+            "gu": torch.empty((M, 2 * inter), dtype=torch.float32, device=device),
+            "g": torch.empty((M, inter), dtype=torch.bfloat16, device=device),
+            "d": torch.empty((M, hidden), dtype=torch.float32, device=device)}
+
+
+def gemma_mlp_sublayer(x: torch.Tensor, *, pre_norm: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
+                       post_norm: torch.Tensor, eps: float = 1e-6, buffers: Optional[dict] = None) -> torch.Tensor:
+    """The MLP half of one Gemma3 layer, in place on the residual stream x (fp32 [B, L, hidden])
+    (app/models/gemma3.js:78-89; tools/reference.py:197-199):
+        h2 = rmsnorm(x, pre_norm)                     nsa_rmsnorm, bf16 output
+        g  = gelu_tanh(h2 W_gate^T) * (h2 W_up^T)     nsa_linear (gate_up) + nsa_glu, bf16 output
+        x += rmsnorm(g W_down^T, post_norm)           nsa_linear (down) + nsa_rmsnorm accumulate
+    w_gate_up [2*inter, hidden] (gate rows, then up rows: the reference's concatLinears, gemma3.js:33)
+    and w_down [hidden, inter] bf16; norm weights fp32, lifted by +1.  Returns x."""
+    if x.dim() != 3 or x.dtype != torch.float32 or not x.is_contiguous():
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "x must be a contiguous float32 [B, L, hidden] tensor")
+    B, L, hidden = x.shape
+    if w_gate_up.dim() != 2 or w_gate_up.shape[1] != hidden or w_gate_up.shape[0] % 2:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "w_gate_up must be [2*inter, hidden]")
+    inter = w_gate_up.shape[0] // 2
+    if w_down.shape != (hidden, inter):
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "w_down must be [hidden, inter]")
+    buf = buffers if buffers is not None else gemma_mlp_buffers(B, L, hidden, inter, x.device)
+    xs = x.view(B * L, hidden)
+    rmsnorm(xs, pre_norm, hidden, eps, buf["h"])
+    linear(buf["h"], w_gate_up, out=buf["gu"])
+    glu(buf["gu"], "gelu_tanh", out=buf["g"])
+    linear(buf["g"], w_down, out=buf["d"])
+    rmsnorm(buf["d"], post_norm, hidden, eps, xs, accumulate=True)
+    return x
+
+
+def gemma_layer(x: torch.Tensor, *, attn: dict, mlp: dict, cs: RopeTable, window: int = 0, eps: float = 1e-6,
+                buffers: Optional[Tuple[dict, dict]] = None) -> torch.Tensor:
+    """One whole Gemma3 layer in place on x (app/models/gemma3.js:62-89): ``gemma_attention_sublayer(x,
+    **attn)`` then ``gemma_mlp_sublayer(x, **mlp)``.  ``buffers`` = (gemma_sublayer_buffers(...),
+    gemma_mlp_buffers(...)), to reuse."""
+    ab, mb = buffers if buffers is not None else (None, None)
+    gemma_attention_sublayer(x, **attn, cs=cs, window=window, eps=eps, buffers=ab)
+    return gemma_mlp_sublayer(x, **mlp, eps=eps, buffers=mb)
 
 
 def text_refine_attention(qkv: torch.Tensor, *, q_norm: torch.Tensor, k_norm: torch.Tensor,

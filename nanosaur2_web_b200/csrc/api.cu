@@ -1107,6 +1107,37 @@ nsa_status nsa_rmsnorm(const nsa_rmsnorm_desc* d, const float* X, const float* w
   return NSA_OK;
 }
 
+nsa_status nsa_glu(const nsa_glu_desc* d, const float* X, void* Y, void* stream) {
+  if (!d) return fail(NSA_ERR_INVALID_ARGUMENT, "desc is NULL");
+  if (d->rows < 0 || d->I < 1) return fail(NSA_ERR_INVALID_ARGUMENT, "need rows >= 0 and I >= 1");
+  const int64_t ldx = d->ldx ? d->ldx : 2 * (int64_t)d->I, ldy = d->ldy ? d->ldy : d->I;
+  if (ldx < 2 * (int64_t)d->I || ldy < d->I) return fail(NSA_ERR_INVALID_ARGUMENT, "need ldx >= 2*I and ldy >= I");
+  if (d->act != 0 && d->act != 1) return fail(NSA_ERR_INVALID_ARGUMENT, "act is 0 (silu) or 1 (gelu_tanh)");
+  if (d->out_dtype != NSA_F32 && d->out_dtype != NSA_BF16) return fail(NSA_ERR_INVALID_ARGUMENT, "bad out_dtype");
+  if (d->rows == 0) return NSA_OK;
+  if (!X || !Y) return fail(NSA_ERR_INVALID_ARGUMENT, "X and Y must be device pointers");
+  const int esz = d->out_dtype == NSA_F32 ? 4 : 2;
+  const uintptr_t x0 = reinterpret_cast<uintptr_t>(X), y0 = reinterpret_cast<uintptr_t>(Y);
+  const uintptr_t x1 = x0 + (uintptr_t)(((int64_t)(d->rows - 1) * ldx + 2 * (int64_t)d->I) * 4);
+  const uintptr_t y1 = y0 + (uintptr_t)(((int64_t)(d->rows - 1) * ldy + d->I) * esz);
+  if (x0 < y1 && y0 < x1) return fail(NSA_ERR_INVALID_ARGUMENT, "X and Y must not overlap");
+  nsa::GluParams p{};
+  p.rows = d->rows;
+  p.I = d->I;
+  p.ldx = ldx;
+  p.ldy = ldy;
+  p.x = X;
+  p.y = Y;
+  p.out_bf16 = d->out_dtype == NSA_BF16;
+  p.act = d->act;
+  p.vec = d->I % 4 == 0 && ldx % 4 == 0 && ldy % 4 == 0 && (x0 & 15) == 0 && (y0 & (uintptr_t)(4 * esz - 1)) == 0;
+  const double bytes = (double)d->rows * d->I * (8.0 + esz);
+  const cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  cudaError_t e = profiled("glu", 0.0, bytes, strm, [&] { return nsa::launch_glu(p, strm); });
+  if (e != cudaSuccess) return cuda_fail(e, "glu launch");
+  return NSA_OK;
+}
+
 nsa_status nsa_seq_shard_attention(const nsa_fused_desc* d, const nsa_seq_shard* s, const void* q_prime,
                                    const void* kv_packed, const int32_t* kv_len, const float* bias, void* out,
                                    void* stream) {

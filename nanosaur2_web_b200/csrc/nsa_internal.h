@@ -203,6 +203,18 @@ struct RmsParams {
 };
 cudaError_t launch_rmsnorm(const RmsParams& p, cudaStream_t stream);
 
+// Gated linear unit (glu.cu): Y[r][j] = act(X[r][j]) * X[r][I + j].
+struct GluParams {
+  int rows, I;
+  int64_t ldx, ldy;
+  const float* x;
+  void* y;          // fp32, or bf16 when out_bf16
+  int out_bf16;
+  int act;          // 0 SiLU, 1 GELU (tanh approximation)
+  int vec;          // I, ldx, ldy multiples of 4; x 16-byte, y 16 (fp32) / 8 (bf16) byte aligned
+};
+cudaError_t launch_glu(const GluParams& p, cudaStream_t stream);
+
 // Returns cudaErrorInvalidValue for unsupported head dims.
 cudaError_t launch_attention(const AttnParams& p, int D, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                              const CUtensorMap& tmV, const CUtensorMap& tmVd, cudaStream_t stream);

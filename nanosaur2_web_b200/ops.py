@@ -26,7 +26,7 @@ import torch
 from . import _lib
 from ._lib import NSA_BF16, NSA_F32, AttentionDesc, NsaError, check, lib
 
-__all__ = ["attention", "headNorm", "linear", "rmsnorm", "rope2dTable", "ropeTable", "RopeTable", "NsaError",
+__all__ = ["attention", "headNorm", "linear", "rmsnorm", "glu", "rope2dTable", "ropeTable", "RopeTable", "NsaError",
            "dtype_code", "stream_handle", "check_device"]
 
 
@@ -166,6 +166,29 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, cols: Optional[int] = None, e
     with torch.cuda.device(x.device):
         check(lib().nsa_rmsnorm(ctypes.byref(d), x2.data_ptr(), weight.data_ptr(), o2.data_ptr(),
                                 stream_handle(x.device)))
+    return out
+
+
+def glu(x: torch.Tensor, act: str = "gelu_tanh", out: Optional[torch.Tensor] = None,
+        out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """ops.glu (app/gpu/ops.js:141-148): x fp32 [rows, 2I] = [gate | up] -> act(gate) * up, [rows, I];
+    act "silu" or "gelu_tanh" (Gemma's MLP).  out fp32 or bf16 (the down projection's operand),
+    allocated when not given."""
+    _require_cuda(x, out)
+    if x.dim() != 2 or x.dtype != torch.float32 or x.stride(1) != 1 or x.shape[1] % 2:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "x must be float32 [rows, 2I] with unit inner stride")
+    rows, I = x.shape[0], x.shape[1] // 2
+    if act not in ("silu", "gelu_tanh"):
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "act is 'silu' or 'gelu_tanh'")
+    if out is None:
+        out = torch.empty((rows, I), dtype=out_dtype or torch.float32, device=x.device)
+    if out.dim() != 2 or out.shape != (rows, I) or out.stride(1) != 1:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "out must be [rows, I] with unit inner stride")
+    d = _lib.GluDesc()
+    d.rows, d.I, d.ldx, d.ldy = rows, I, x.stride(0), out.stride(0)
+    d.act, d.out_dtype = (0 if act == "silu" else 1), dtype_code(out)
+    with torch.cuda.device(x.device):
+        check(lib().nsa_glu(ctypes.byref(d), x.data_ptr(), out.data_ptr(), stream_handle(x.device)))
     return out
 
 

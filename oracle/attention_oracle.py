@@ -250,6 +250,30 @@ def vae_attention(x, gn_w, gn_b, w_q, b_q, w_k, b_k, w_v, b_v, w_o, b_o, groups=
     return x + linear(a, w_o, b_o, acc).T.reshape(x.shape)
 
 
+def glu(x, act="gelu_tanh", acc=np.float32):
+    """ops.glu (app/gpu/ops.js:141-148, kernels.js:346-360): x [rows, 2I] = [gate | up] ->
+    act(gate) * up.  gelu_tanh is PyTorch's approximate="tanh" GELU (tools/reference.py:198),
+    0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))); silu is x / (1 + exp(-x))."""
+    x = np.asarray(x, acc)
+    I = x.shape[-1] // 2
+    g, u = x[..., :I], x[..., I:]
+    if act == "silu":
+        a = g / (acc(1) + np.exp(-g))
+    else:
+        a = acc(0.5) * g * (acc(1) + np.tanh(acc(math.sqrt(2.0 / math.pi)) * (g + acc(0.044715) * g * g * g)))
+    return a * u
+
+
+def gemma_mlp_sublayer(x, pre_w, w_gate, w_up, w_down, post_w, eps=1e-6, acc=np.float32):
+    """The MLP half of one Gemma3 layer on the residual stream x [L, hidden]
+    (tools/reference.py:197-199; app/models/gemma3.js:78-89): h = rms_norm(x, pre_w),
+    g = gelu_tanh(h W_gate^T) * (h W_up^T), then x + rms_norm(g W_down^T, post_w)."""
+    x = np.asarray(x, acc)
+    h = rms_norm(x, pre_w, eps, acc)
+    g = glu(np.concatenate([linear(h, w_gate, acc=acc), linear(h, w_up, acc=acc)], axis=-1), "gelu_tanh", acc)
+    return x + rms_norm(linear(g, w_down, acc=acc), post_w, eps, acc)
+
+
 def gemma_attention_sublayer(x, in_w, w_q, w_k, w_v, q_w, k_w, w_o, post_w, theta, window=0, eps=1e-6,
                              acc=np.float32):
     """The attention half of one Gemma3 layer on the residual stream x [L, hidden]

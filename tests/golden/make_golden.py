@@ -17,9 +17,9 @@ drives its real code paths with small seeded stand-in weights (no model files ex
 * ``rope_2d`` / ``gemma_rope`` tables and ``rms_norm`` / ``rope_split_half`` on seeded inputs.
 * ``lin`` (``:208-210``), the q|k|v projection's linear, on small seeded operands with and without a
   bias (``--only linear`` writes just this fixture).
-* the attention half of ``gemma_encode``'s layers 0 and 5 (``:187-196``: input norm, q/k/v linears,
-  head norms, RoPE, causal SDPA, o linear, post-attention norm, residual add) on a 64-wide residual
-  stream with bf16-exact linear weights (``--only gemma_sublayer``).
+* ``gemma_encode``'s layers 0 and 5 (``:187-199``: input norm, q/k/v linears, head norms, RoPE,
+  causal SDPA, o linear, post-attention norm, residual add; then the GELU-tanh MLP with its norms) on
+  a 64-wide residual stream with bf16-exact linear weights (``--only gemma_sublayer``).
 * ``VAE.attn`` (``:352-357``), the VAE decoder's single-head attention block (group norm, q/k/v 1x1
   convolutions, SDPA with head dim C, proj_out, residual) on a 64 x 6 x 5 activation
   (``--only vae_attention``).
@@ -208,11 +208,13 @@ class Bf16LinearWeights(StandInWeights):
 
 
 def write_gemma_sublayer(R, out, L=40, hidden=64):
-    """The attention half of gemma_encode's layers 0 (local) and 5 (global) (tools/reference.py:187-196)
-    on a 64-wide residual stream (the attention shapes are the model's: 4 + 1 heads of 256): the layer
-    input x, the updated x after ``x + rms_norm(a @ W_o^T, post)``, and the weights, with the linear
-    weights bf16-exact.  The reference's 2-D rms_norm calls give, per layer, the input norm (its x is
-    the layer input), the post-attention norm and the pre-MLP norm (its x is the updated stream)."""
+    """gemma_encode's layers 0 (local) and 5 (global) (tools/reference.py:187-199) on a 64-wide residual
+    stream (the attention shapes are the model's: 4 + 1 heads of 256; MLP width 64): the layer input
+    x, x after the attention half ``x + rms_norm(a @ W_o^T, post)``, the layer output after the MLP
+    half, and the weights, with the linear weights bf16-exact.  The reference's 2-D rms_norm calls
+    give, per layer, the input norm (its x is the layer input), the post-attention norm, the pre-MLP
+    norm (its x is the stream after attention), the post-MLP norm, and then the next layer's input
+    norm (its x is the layer output)."""
     W = Bf16LinearWeights(lambda role: gemma_shapes(role, hidden), 4321, lambda n: True)
     calls = []
     orig_rms = R.rms_norm
@@ -232,11 +234,14 @@ def write_gemma_sublayer(R, out, L=40, hidden=64):
     p = "model.layers.0."
     rec = {}
     for layer in (0, 5):
-        (x_in, w_in), (_, w_post), (x_mid, _) = calls[4 * layer:4 * layer + 3]
-        rec[f"x_in{layer}"], rec[f"x_mid{layer}"] = np32(x_in), np32(x_mid)
+        (x_in, w_in), (_, w_post), (x_mid, pre_ff_w), (_, post_ff_w) = calls[4 * layer:4 * layer + 4]
+        x_out = calls[4 * layer + 4][0]   # the next layer's input norm sees the layer's output
+        rec[f"x_in{layer}"], rec[f"x_mid{layer}"], rec[f"x_out{layer}"] = np32(x_in), np32(x_mid), np32(x_out)
     np.savez_compressed(
         os.path.join(out, "gemma_sublayer.npz"), **rec, layers=np.array([0, 5]),
-        in_w=np32(w_in), post_w=np32(w_post),
+        in_w=np32(w_in), post_w=np32(w_post), pre_ff_w=np32(pre_ff_w), post_ff_w=np32(post_ff_w),
+        w_gate=np32(W(p + "mlp.gate_proj.weight")), w_up=np32(W(p + "mlp.up_proj.weight")),
+        w_down=np32(W(p + "mlp.down_proj.weight")),
         q_w=np32(W(p + "self_attn.q_norm.weight") + 1.0), k_w=np32(W(p + "self_attn.k_norm.weight") + 1.0),
         w_q=np32(W(p + "self_attn.q_proj.weight")), w_k=np32(W(p + "self_attn.k_proj.weight")),
         w_v=np32(W(p + "self_attn.v_proj.weight")), w_o=np32(W(p + "self_attn.o_proj.weight")))

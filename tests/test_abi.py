@@ -47,7 +47,8 @@ def test_struct_layouts_match_c(tmp_path):
                    'offsetof(nsa_proj_desc, x_rows), offsetof(nsa_proj_desc, text_rows), offsetof(nsa_proj_desc, b_kv));'
                    'printf("%zu %zu %zu\\n", sizeof(nsa_linear_desc), offsetof(nsa_linear_desc, lda), '
                    'offsetof(nsa_linear_desc, act));printf("%zu %zu %zu\\n", sizeof(nsa_rmsnorm_desc), '
-                   'offsetof(nsa_rmsnorm_desc, ldy), offsetof(nsa_rmsnorm_desc, eps));return 0;}\n')
+                   'offsetof(nsa_rmsnorm_desc, ldy), offsetof(nsa_rmsnorm_desc, eps));printf("%zu %zu %zu\\n", '
+                   'sizeof(nsa_glu_desc), offsetof(nsa_glu_desc, ldy), offsetof(nsa_glu_desc, out_dtype));return 0;}\n')
     exe = tmp_path / "sizes"
     subprocess.run(["gcc", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)], check=True)
     got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
@@ -56,7 +57,8 @@ def test_struct_layouts_match_c(tmp_path):
             ctypes.sizeof(_lib.SeqShard), _lib.SeqShard.qkv_text_row0.offset, ctypes.sizeof(_lib.ProjDesc),
             _lib.ProjDesc.x_rows.offset, _lib.ProjDesc.text_rows.offset, _lib.ProjDesc.b_kv.offset,
             ctypes.sizeof(_lib.LinearDesc), _lib.LinearDesc.lda.offset, _lib.LinearDesc.act.offset,
-            ctypes.sizeof(_lib.RmsnormDesc), _lib.RmsnormDesc.ldy.offset, _lib.RmsnormDesc.eps.offset]
+            ctypes.sizeof(_lib.RmsnormDesc), _lib.RmsnormDesc.ldy.offset, _lib.RmsnormDesc.eps.offset,
+            ctypes.sizeof(_lib.GluDesc), _lib.GluDesc.ldy.offset, _lib.GluDesc.out_dtype.offset]
     assert got == want
 
 
@@ -236,3 +238,25 @@ def test_rmsnorm_validation():
     assert b"overlap" in L.nsa_last_error()
     d.rows = 0
     assert rms(x=None, w=None, y=None) == _lib.NSA_OK                                       # empty: nothing to do
+
+
+def test_glu_validation():
+    """nsa_glu rejects bad arguments before touching the device (no GPU needed)."""
+    L = _lib.lib()
+    fake = 1 << 32
+    d = _lib.GluDesc()
+    d.rows, d.I, d.act = 1024, 2048, 1
+
+    def glu(x=fake, y=fake + (1 << 30)):
+        return L.nsa_glu(ctypes.byref(d), x, y, None)
+    assert L.nsa_glu(None, fake, fake, None) == _lib.NSA_ERR_INVALID_ARGUMENT
+    d.ldx = 2048
+    assert glu() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # ldx < 2*I
+    d.ldx, d.act = 0, 2
+    assert glu() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # act 0 or 1
+    d.act, d.out_dtype = 1, 5
+    assert glu() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # bad dtype
+    d.out_dtype = _lib.NSA_F32
+    assert glu(y=fake + 4096) == _lib.NSA_ERR_INVALID_ARGUMENT                              # Y overlaps X
+    d.rows = 0
+    assert glu(x=None, y=None) == _lib.NSA_OK                                               # empty: nothing to do

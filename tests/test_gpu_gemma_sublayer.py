@@ -6,11 +6,17 @@
   the reference's own layers 0 and 5 (tests/golden/gemma_sublayer.npz, a 64-wide residual stream)
   and against the oracle at the model's width (640) on a batch of two 1024-token sequences.
 
+* ops.glu (app/gpu/ops.js:141-148): SiLU and GELU-tanh, fp32 and bf16 outputs, vector and scalar
+  paths; blocks.gemma_mlp_sublayer and blocks.gemma_layer (app/models/gemma3.js:62-89) against the
+  reference's layers 0 and 5 (attention half, then MLP half) and the oracle at the model's width.
+
 Tolerances.  rmsnorm: fp32 in, fp32 math; only the order of the sum of squares differs, so 1e-5
-relative.  The sublayer computes its GEMM operands in bf16 (h, q', k', v, P, a: about 2^-9 relative
+relative.  glu: fp32 math with CUDA's tanhf / expf, 1e-5 relative (bf16 output: 2^-8).  The sublayer computes its GEMM operands in bf16 (h, q', k', v, P, a: about 2^-9 relative
 each); the post-attention RMSNorm rescales o to unit RMS, so those roundings show as absolute error
 on the O(1) update.  Emulating the bf16 roundings on the CPU gives 0.021 max-abs on an update of
-|x| <= 3.8; the test allows 6e-2 max-abs and asks for a cosine >= 0.9999 between the updates."""
+|x| <= 3.8; the test allows 6e-2 max-abs and asks for a cosine >= 0.9999 between the updates.  The
+MLP half rounds h2 and g to bf16: emulated 0.020 max-abs on an update of |x| <= 7.9; the same bounds,
+and 1e-1 for a whole layer (both halves)."""
 
 import numpy as np
 import pytest
@@ -86,9 +92,9 @@ def _sublayer_inputs(g):
                 w_o=t(g["w_o"], torch.bfloat16), post_norm=t(g["post_w"]))
 
 
-def _check_update(got, x, want):
+def _check_update(got, x, want, tol=6e-2):
     d, dw = got - x, want - x
-    assert np.abs(got - want).max() <= 6e-2, np.abs(got - want).max()
+    assert np.abs(got - want).max() <= tol, np.abs(got - want).max()
     cos = float(np.sum(d * dw) / (np.linalg.norm(d) * np.linalg.norm(dw)))
     assert cos >= 0.9999, cos
 
@@ -133,3 +139,67 @@ def test_gemma_sublayer_model_width_batch():
         want = O.gemma_attention_sublayer(x_in[b], g["in_w"], g["w_q"], g["w_k"], g["w_v"], g["q_w"], g["k_w"],
                                           g["w_o"], g["post_w"], 1e4, window=window)
         _check_update(got[b], x_in[b], want)
+
+
+@pytest.mark.parametrize("rows,I,ldx,ldy", [(1000, 2048, 4096, 2048), (17, 101, 210, 103), (3, 4, 8, 4)])
+@pytest.mark.parametrize("act", ["silu", "gelu_tanh"])
+def test_glu(rows, I, ldx, ldy, act):
+    from nanosaur2_web_b200.ops import glu
+    rng = np.random.default_rng(rows + I)
+    xs = (3.0 * rng.standard_normal((rows, ldx))).astype(np.float32)
+    x = t(xs)[:, :2 * I]
+    want = O.glu(xs[:, :2 * I], act, acc=np.float64)
+    y = torch.full((rows, ldy), 9.0, device=DEV)
+    glu(x, act, out=y[:, :I])
+    check_device()
+    got = y.cpu().numpy()
+    np.testing.assert_allclose(got[:, :I], want, rtol=1e-5, atol=1e-5)
+    assert (got[:, I:] == 9.0).all()
+    yb = glu(x, act, out_dtype=torch.bfloat16)
+    check_device()
+    np.testing.assert_allclose(yb.float().cpu().numpy(), want, rtol=2 ** -8, atol=1e-5)
+
+
+def _mlp_inputs(g):
+    return dict(pre_norm=t(g["pre_ff_w"]), w_gate_up=t(np.concatenate([g["w_gate"], g["w_up"]]), torch.bfloat16),
+                w_down=t(g["w_down"], torch.bfloat16), post_norm=t(g["post_ff_w"]))
+
+
+@pytest.mark.parametrize("layer", [0, 5])
+def test_gemma_layer_matches_reference_layers(golden, layer):
+    """The reference's gemma_encode layers 0 and 5, 40 tokens: the MLP half from the stream after
+    attention, and the whole layer (attention half, then MLP half) from the layer input."""
+    from nanosaur2_web_b200.blocks import GEMMA_HEAD_DIM, gemma_layer, gemma_mlp_sublayer
+    from nanosaur2_web_b200.ops import ropeTable
+    g = golden("gemma_sublayer")
+    x_mid, x_out, x_in = g[f"x_mid{layer}"], g[f"x_out{layer}"], g[f"x_in{layer}"]
+    x = t(x_mid[None])
+    gemma_mlp_sublayer(x, **_mlp_inputs(g))
+    check_device()
+    _check_update(x[0].cpu().numpy(), x_mid, x_out)
+    x = t(x_in[None])
+    gemma_layer(x, attn=_sublayer_inputs(g), mlp=_mlp_inputs(g),
+                cs=ropeTable(x_in.shape[0], GEMMA_HEAD_DIM, O.gemma_rope_theta(layer), DEV))
+    check_device()
+    _check_update(x[0].cpu().numpy(), x_in, x_out, tol=1e-1)
+
+
+def test_gemma_mlp_model_width():
+    """hidden 640, MLP width 2048 (Gemma3-270M), B = 2 x 256 tokens, against the oracle."""
+    from nanosaur2_web_b200.blocks import gemma_mlp_buffers, gemma_mlp_sublayer
+    from tests._helpers import bf16_round
+    B, L, Hd, I = 2, 256, 640, 2048
+    rng = np.random.default_rng(12)
+    pre = (1.0 + 0.25 * rng.standard_normal(Hd)).astype(np.float32)
+    post = (1.0 + 0.25 * rng.standard_normal(Hd)).astype(np.float32)
+    wg = bf16_round(rng.standard_normal((I, Hd), dtype=np.float32) / np.sqrt(Hd))
+    wu = bf16_round(rng.standard_normal((I, Hd), dtype=np.float32) / np.sqrt(Hd))
+    wd = bf16_round(rng.standard_normal((Hd, I), dtype=np.float32) / np.sqrt(I))
+    x_in = (8.0 * rng.standard_normal((B, L, Hd))).astype(np.float32)
+    x = t(x_in)
+    gemma_mlp_sublayer(x, pre_norm=t(pre), w_gate_up=t(np.concatenate([wg, wu]), torch.bfloat16),
+                       w_down=t(wd, torch.bfloat16), post_norm=t(post), buffers=gemma_mlp_buffers(B, L, Hd, I, DEV))
+    check_device()
+    got = x.cpu().numpy()
+    for b in range(B):
+        _check_update(got[b], x_in[b], O.gemma_mlp_sublayer(x_in[b], pre, wg, wu, wd, post, acc=np.float64))

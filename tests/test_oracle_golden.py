@@ -128,3 +128,20 @@ def test_vae_attention(golden):
     assert got.shape == g["x"].shape == (64, 6, 5)
     np.testing.assert_allclose(got, g["y"], rtol=1e-4, atol=1e-4)
     assert np.abs(g["y"] - g["x"]).max() > 0.05   # the block changed the activation
+
+
+@pytest.mark.parametrize("layer", [0, 5])
+def test_gemma_mlp_sublayer(golden, layer):
+    """Pre-MLP norm -> gate / up linears -> GELU-tanh GLU -> down linear -> post-MLP norm -> residual
+    add, against gemma_encode's own layers: the stream after attention to the layer's output."""
+    g = golden("gemma_sublayer")
+    x, want = g[f"x_mid{layer}"], g[f"x_out{layer}"]
+    got = O.gemma_mlp_sublayer(x, g["pre_ff_w"], g["w_gate"], g["w_up"], g["w_down"], g["post_ff_w"])
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+    assert np.abs(want - x).max() > 0.1
+    # the whole layer: attention half, then MLP half
+    xin = g[f"x_in{layer}"]
+    mid = O.gemma_attention_sublayer(xin, g["in_w"], g["w_q"], g["w_k"], g["w_v"], g["q_w"], g["k_w"], g["w_o"],
+                                     g["post_w"], O.gemma_rope_theta(layer))
+    np.testing.assert_allclose(O.gemma_mlp_sublayer(mid, g["pre_ff_w"], g["w_gate"], g["w_up"], g["w_down"],
+                                                    g["post_ff_w"]), want, rtol=2e-4, atol=2e-4)
