@@ -821,41 +821,52 @@ def run_config8(args, rank, world, local_rank):
     on the fp32 residual stream x [B, L, 640] (app/models/gemma3.js:62-77; tools/reference.py:187-196):
     input RMSNorm to bf16, te.qkv with the q/k norms and RoPE in the GEMM epilogue, attention, te.o,
     and the post-attention RMSNorm added into x (blocks.gemma_attention_sublayer, five launches per
-    layer).  Batch-sharded over the ranks (strong scaling).  The line also reports the unfused form:
-    torch elementwise norms, cuBLAS linears and the fused prologue + attention."""
+    layer).  Config 9 runs the whole layers (app/models/gemma3.js:62-89; tools/reference.py:187-199):
+    the attention half, then the MLP half (pre-MLP RMSNorm, gate_up linear to 2 x 2048, GELU-tanh GLU,
+    down linear, post-MLP RMSNorm accumulated; blocks.gemma_layer, ten launches per layer).
+    Batch-sharded over the ranks (strong scaling).  The line also reports the unfused form: torch
+    elementwise norms and GLU, cuBLAS linears and the fused prologue + attention."""
     import torch
+    import torch.nn.functional as F
 
-    from nanosaur2_web_b200.blocks import (GEMMA_HEAD_DIM, GEMMA_HEADS, gemma_attention_sublayer,
-                                           gemma_layer_attention, gemma_rope_theta, gemma_sublayer_buffers)
+    from nanosaur2_web_b200.blocks import (GEMMA_HEAD_DIM, GEMMA_HEADS, gemma_attention_sublayer, gemma_layer,
+                                           gemma_layer_attention, gemma_mlp_buffers, gemma_rope_theta,
+                                           gemma_sublayer_buffers)
     from nanosaur2_web_b200.ops import ropeTable
     from nanosaur2_web_b200.sharding import split_range, sum_over_ranks
+    whole = args.config == 9
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    B, L, LAYERS, WINDOW, Hd, EPS = 16, 1024, 18, 512, 640, 1e-6
+    B, L, LAYERS, WINDOW, Hd, I, EPS = 16, 1024, 18, 512, 640, 2048, 1e-6
     QKV, A = 6 * GEMMA_HEAD_DIM, GEMMA_HEADS * GEMMA_HEAD_DIM
     b0, b1 = split_range(B, world, rank)
     nb = b1 - b0
     g = torch.Generator(device=dev).manual_seed(8000 + rank)
     x = torch.randn((nb, L, Hd), device=dev, generator=g) * 8.0            # 42 MB residual stream per 16
     layers = []
-    for _ in range(3):   # three weight sets rotate (the 18 layers' weights are 18 x 3.3 MB in the model)
-        layers.append({
-            "in_norm": 1.0 + 0.2 * torch.randn(Hd, device=dev, generator=g),
-            "post_norm": 1.0 + 0.2 * torch.randn(Hd, device=dev, generator=g),
-            "q_norm": 1.0 + 0.2 * torch.randn(GEMMA_HEAD_DIM, device=dev, generator=g),
-            "k_norm": 1.0 + 0.2 * torch.randn(GEMMA_HEAD_DIM, device=dev, generator=g),
-            "w_qkv": (torch.randn((QKV, Hd), device=dev, generator=g) / math.sqrt(Hd)).to(torch.bfloat16),
-            "w_o": (torch.randn((Hd, A), device=dev, generator=g) / math.sqrt(A)).to(torch.bfloat16)})
+    for _ in range(3):   # three weight sets rotate (the model's 18 layers hold 18 x 11 MB)
+        norm = lambda n: 1.0 + 0.2 * torch.randn(n, device=dev, generator=g)  # noqa: E731
+        lin = lambda o, i: (torch.randn((o, i), device=dev, generator=g) / math.sqrt(i)).to(torch.bfloat16)  # noqa: E731
+        layers.append({"attn": {"in_norm": norm(Hd), "post_norm": norm(Hd), "q_norm": norm(GEMMA_HEAD_DIM),
+                                "k_norm": norm(GEMMA_HEAD_DIM), "w_qkv": lin(QKV, Hd), "w_o": lin(Hd, A)},
+                       "mlp": {"pre_norm": norm(Hd), "post_norm": norm(Hd), "w_gate_up": lin(2 * I, Hd),
+                               "w_down": lin(Hd, I)}})
     tables = {th: ropeTable(L, GEMMA_HEAD_DIM, th, dev) for th in (1e4, 1e6)}
     bufs = gemma_sublayer_buffers(nb, L, Hd, dev)
+    mbufs = gemma_mlp_buffers(nb, L, Hd, I, dev) if whole else None
     qkv = torch.empty((nb, L, QKV), dtype=torch.bfloat16, device=dev)
     a = torch.empty((nb, L, A), dtype=torch.bfloat16, device=dev)
 
     def step(i):
         for layer in range(LAYERS):
             th = gemma_rope_theta(layer)
-            gemma_attention_sublayer(x, **layers[(i * LAYERS + layer) % 3], cs=tables[th],
-                                     window=0 if th == 1e6 else WINDOW, eps=EPS, buffers=bufs)
+            wl = layers[(i * LAYERS + layer) % 3]
+            win = 0 if th == 1e6 else WINDOW
+            if whole:
+                gemma_layer(x, attn=wl["attn"], mlp=wl["mlp"], cs=tables[th], window=win, eps=EPS,
+                            buffers=(bufs, mbufs))
+            else:
+                gemma_attention_sublayer(x, **wl["attn"], cs=tables[th], window=win, eps=EPS, buffers=bufs)
 
     def rms(t, w):
         return t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + EPS) * w
@@ -863,15 +874,19 @@ def run_config8(args, rank, world, local_rank):
     def step_unfused(i):
         for layer in range(LAYERS):
             th = gemma_rope_theta(layer)
-            wl = layers[(i * LAYERS + layer) % 3]
-            torch.matmul(rms(x, wl["in_norm"]).to(torch.bfloat16), wl["w_qkv"].T, out=qkv)   # cuBLAS
-            gemma_layer_attention(qkv, q_norm=wl["q_norm"], k_norm=wl["k_norm"], cs=tables[th],
+            wa, wm = layers[(i * LAYERS + layer) % 3]["attn"], layers[(i * LAYERS + layer) % 3]["mlp"]
+            torch.matmul(rms(x, wa["in_norm"]).to(torch.bfloat16), wa["w_qkv"].T, out=qkv)   # cuBLAS
+            gemma_layer_attention(qkv, q_norm=wa["q_norm"], k_norm=wa["k_norm"], cs=tables[th],
                                   window=0 if th == 1e6 else WINDOW, out=a)
-            x.add_(rms(torch.matmul(a, wl["w_o"].T).float(), wl["post_norm"]))
+            x.add_(rms(torch.matmul(a, wa["w_o"].T).float(), wa["post_norm"]))
+            if whole:
+                gu = torch.matmul(rms(x, wm["pre_norm"]).to(torch.bfloat16), wm["w_gate_up"].T).float()
+                gg = (F.gelu(gu[..., :I], approximate="tanh") * gu[..., I:]).to(torch.bfloat16)
+                x.add_(rms(torch.matmul(gg, wm["w_down"].T).float(), wm["post_norm"]))
 
     per_elem_attn = sum(4.0 * GEMMA_HEADS * gemma_pairs(L, 0 if gemma_rope_theta(i) == 1e6 else WINDOW) *
                         GEMMA_HEAD_DIM for i in range(LAYERS))
-    per_elem_lin = LAYERS * 2.0 * L * Hd * (QKV + A)
+    per_elem_lin = LAYERS * 2.0 * L * Hd * (QKV + A + (3 * I if whole else 0))
     stream = torch.cuda.current_stream(dev)
     with ClockSampler(local_rank) as clocks:
         ms = _timed(step, args.steps, args.warmup, world, stream)
@@ -884,25 +899,36 @@ def run_config8(args, rank, world, local_rank):
     roof = _roofline(kst, "attn_persist_kernel")
     peak, _src = measured_peak()
     for key, name, kernel in (("projection", "projection", "proj_kernel<256>"),
-                              ("output_projection", "linear", "linear_kernel")):
+                              ("linears", "linear", "linear_kernel")):
         _, kms, kfl, _ = kst[name]
         roof[key] = {"kernel": kernel, "achieved": kfl / (kms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
                      "frac": kfl / (kms * 1e-3) / 1e12 / peak, "ms_per_step": kms / nsteps}
-    rl, rms_ms, _, rbytes = kst["rmsnorm"]
     hbm = measured_hbm()
-    roof["rmsnorm"] = {"kernel": "rmsnorm_kernel", "bound": "hbm", "achieved": rbytes / (rms_ms * 1e-3) / 1e9,
-                       "peak": hbm, "unit": "GB/s", "frac": rbytes / (rms_ms * 1e-3) / 1e9 / hbm,
-                       "launches_per_step": rl / nsteps, "ms_per_step": rms_ms / nsteps}
-    cfg = {"workload": "config 8: Gemma3-270M text encoder, the attention half of config 4's 18 layers (B=16 x "
-                       "1024, GQA 4/1, head dim 256, causal, 15 local window 512 + 3 global) on the fp32 residual "
-                       "stream (hidden 640): input RMSNorm, te.qkv linear with q/k RMSNorm + 1D RoPE in the GEMM "
-                       "epilogue, attention, te.o linear, post-attention RMSNorm accumulated into the stream",
-           "global_batch": B, "seq_len": L, "layers": LAYERS, "hidden": Hd, "parallelism": f"batch-sharded x{world}",
+    for name in ("rmsnorm", "glu") if whole else ("rmsnorm",):
+        nl, nms, _, nbytes = kst[name]
+        roof[name] = {"kernel": name + "_kernel", "bound": "hbm", "achieved": nbytes / (nms * 1e-3) / 1e9,
+                      "peak": hbm, "unit": "GB/s", "frac": nbytes / (nms * 1e-3) / 1e9 / hbm,
+                      "launches_per_step": nl / nsteps, "ms_per_step": nms / nsteps}
+    if whole:
+        work = ("config 9: Gemma3-270M text encoder, config 4's 18 whole layers (B=16 x 1024, GQA 4/1, head dim "
+                "256, causal, 15 local window 512 + 3 global, MLP 2048 GELU-tanh) on the fp32 residual stream "
+                "(hidden 640): the attention half of config 8, then pre-MLP RMSNorm, gate_up linear, GLU, down "
+                "linear, post-MLP RMSNorm accumulated into the stream")
+        note = "18 * (2*L*640*(1536 + 1024 + 3*2048) linears + 4*Hq*valid pairs*256 attention) per element"
+    else:
+        work = ("config 8: Gemma3-270M text encoder, the attention half of config 4's 18 layers (B=16 x 1024, GQA "
+                "4/1, head dim 256, causal, 15 local window 512 + 3 global) on the fp32 residual stream (hidden "
+                "640): input RMSNorm, te.qkv linear with q/k RMSNorm + 1D RoPE in the GEMM epilogue, attention, "
+                "te.o linear, post-attention RMSNorm accumulated into the stream")
+        note = "18 * (2*L*640*(1536 + 1024) linears + 4*Hq*valid pairs*256 attention) per element"
+    cfg = {"workload": work, "global_batch": B, "seq_len": L, "layers": LAYERS, "hidden": Hd,
+           "parallelism": f"batch-sharded x{world}",
            "l2": "each layer reads and rewrites the 42 MB stream and three weight sets rotate; the per-layer "
-                 "intermediates (h 21 MB, q'/k'/v' 42 MB, a 34 MB, o 42 MB) exceed the 126 MB L2 together",
-           "flops_note": "18 * (2*L*640*(1536 + 1024) linears + 4*Hq*valid pairs*256 attention) per element"}
+                 "intermediates (h 21 MB, q'/k'/v' 42 MB, a 34 MB, o 42 MB; MLP gu 268 MB) exceed the 126 MB L2",
+           "flops_note": note}
     print(json.dumps(_line(args, world, flops / (ms * 1e-3) / 1e12, ms, cfg, roof, clocks.summary(),
-                           5 * LAYERS * args.steps, "strong", unfused_ms_per_step=ms_unfused / args.steps)),
+                           (10 if whole else 5) * LAYERS * args.steps, "strong",
+                           unfused_ms_per_step=ms_unfused / args.steps)),
           flush=True)
 
 
@@ -947,11 +973,11 @@ def main():
     ap.add_argument("--seq-mode", choices=["auto", "nccl", "p2p", "ce"], default="auto",
                     help="config 5: k'|v' exchange by NCCL all-gather, peer stores from the prologue, or "
                          "copy-engine pushes")
-    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5, 6, 7, 8], default=2,
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5, 6, 7, 8, 9], default=2,
                     help="BASELINE config to run (2 = the headline line; 3, 4, 5 print their own line; 6 = the "
                          "config-2 block step from the block input, QKV projection fused with the prologue; 7 = "
                          "config 4's Gemma layers from the layer input; 8 = the attention half of config 4's "
-                         "Gemma layers on the residual stream)")
+                         "Gemma layers on the residual stream; 9 = the whole Gemma layers)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -975,7 +1001,7 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     try:
         {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5, 6: run_config6, 7: run_config7,
-         8: run_config8}[args.config](args, rank, world, local_rank)
+         8: run_config8, 9: run_config8}[args.config](args, rank, world, local_rank)
     finally:
         if world > 1:
             dist.destroy_process_group()
