@@ -260,3 +260,45 @@ def test_glu_validation():
     assert glu(y=fake + 4096) == _lib.NSA_ERR_INVALID_ARGUMENT                              # Y overlaps X
     d.rows = 0
     assert glu(x=None, y=None) == _lib.NSA_OK                                               # empty: nothing to do
+
+
+def test_native_c_caller(tmp_path):
+    """A plain C program compiled against include/nsattn.h and linked with libnsattn.so (the way a
+    cgo / N-API / JNI host binds it) gets the version string and the same synchronous argument errors
+    the Python mirror sees, with messages, and never needs a GPU for them."""
+    src = tmp_path / "caller.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include <string.h>
+#include "nsattn.h"
+static int expect(const char* what, nsa_status got, nsa_status want) {
+  if (got != want) { printf("FAIL %s: %d (%s)\n", what, (int)got, nsa_last_error()); return 1; }
+  printf("ok %s: %s\n", what, nsa_last_error());
+  return 0;
+}
+int main(void) {
+  void* p = (void*)0x100000;
+  int bad = 0;
+  if (strstr(nsa_version(), "sm_100a") == NULL) bad++;
+  nsa_attention_desc a; memset(&a, 0, sizeof a);
+  a.Lq = a.Lk = 64; a.H = 2; a.D = 80; a.ldq = a.ldk = a.ldv = 160; a.group = 1; a.B = 1; a.ldo = 160;
+  bad += expect("attention head dim 80", nsa_attention(&a, p, p, p, NULL, NULL, p, p, 1 << 20, NULL), NSA_ERR_UNSUPPORTED);
+  nsa_linear_desc l; memset(&l, 0, sizeof l); l.M = 128; l.N = 256; l.K = 100; l.lda = 100;
+  bad += expect("linear K % 8", nsa_linear(&l, p, p, NULL, NULL, (float*)p, NULL), NSA_ERR_INVALID_ARGUMENT);
+  nsa_rmsnorm_desc r; memset(&r, 0, sizeof r); r.rows = 8; r.cols = 640; r.out_dtype = NSA_BF16; r.accumulate = 1;
+  bad += expect("rmsnorm accumulate into bf16", nsa_rmsnorm(&r, (const float*)p, (const float*)p, (char*)p + (1 << 24), NULL),
+                NSA_ERR_INVALID_ARGUMENT);
+  nsa_glu_desc g; memset(&g, 0, sizeof g); g.rows = 8; g.I = 16; g.act = 7;
+  bad += expect("glu act", nsa_glu(&g, (const float*)p, (char*)p + (1 << 24), NULL), NSA_ERR_INVALID_ARGUMENT);
+  bad += expect("rope1d odd D", nsa_rope1d_table(16, 7, 1e4f, (float*)p, NULL), NSA_ERR_INVALID_ARGUMENT);
+  bad += expect("status string", strcmp(nsa_status_string(NSA_ERR_DEVICE), "") != 0 ? NSA_OK : NSA_ERR_CUDA, NSA_OK);
+  return bad;
+}
+''')
+    exe = tmp_path / "caller"
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    subprocess.run(["gcc", "-I", os.path.dirname(HEADER), str(src), "-L", libdir, "-lnsattn", f"-Wl,-rpath,{libdir}",
+                    "-o", str(exe)], check=True)
+    res = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert res.stdout.count("ok ") == 6
