@@ -50,6 +50,16 @@ def gemma_pairs(L, window):
     return sum(min(i + 1, window) for i in range(L))
 
 
+def gemma_encoder_flops(L, layers=18, window=512, hidden=640, inter=2048, whole=False):
+    """Algorithmic FLOPs per sequence of config 4's Gemma layers from the residual stream: the te.qkv
+    (1536 outputs) and te.o (1024 inputs) linears, attention at 4 * Hq * valid pairs * 256 (local
+    layers windowed, every sixth layer global), and with ``whole`` the MLP's gate_up (2 x inter) and
+    down linears."""
+    attn = sum(4.0 * 4 * gemma_pairs(L, 0 if (i + 1) % 6 == 0 else window) * 256 for i in range(layers))
+    lin = layers * 2.0 * L * hidden * (1536 + 1024 + (3 * inter if whole else 0))
+    return attn + lin
+
+
 def make_inputs(seed, B, bf16=True):
     from tests._helpers import joint_inputs
     return joint_inputs(seed, B, IMG_H, IMG_W, LT, (32, 256), C=C, bf16=bf16)
@@ -884,14 +894,12 @@ def run_config8(args, rank, world, local_rank):
                 gg = (F.gelu(gu[..., :I], approximate="tanh") * gu[..., I:]).to(torch.bfloat16)
                 x.add_(rms(torch.matmul(gg, wm["w_down"].T).float(), wm["post_norm"]))
 
-    per_elem_attn = sum(4.0 * GEMMA_HEADS * gemma_pairs(L, 0 if gemma_rope_theta(i) == 1e6 else WINDOW) *
-                        GEMMA_HEAD_DIM for i in range(LAYERS))
-    per_elem_lin = LAYERS * 2.0 * L * Hd * (QKV + A + (3 * I if whole else 0))
+    per_elem = gemma_encoder_flops(L, LAYERS, WINDOW, Hd, I, whole)
     stream = torch.cuda.current_stream(dev)
     with ClockSampler(local_rank) as clocks:
         ms = _timed(step, args.steps, args.warmup, world, stream)
     ms_unfused = _timed(step_unfused, args.steps, args.warmup, world, stream)
-    flops = sum_over_ranks((per_elem_attn + per_elem_lin) * nb * args.steps)
+    flops = sum_over_ranks(per_elem * nb * args.steps)
     nsteps = min(args.steps, 3)
     kst = _kernel_stats(step, nsteps)
     if rank != 0:

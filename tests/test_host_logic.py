@@ -51,6 +51,22 @@ def test_bench_flop_counts():
     assert g == 524800 and l == 393472
 
 
+def test_gemma_encoder_flops_brute_force():
+    """Configs 8 and 9: the FLOP count against an explicit count of the masked (query, key) pairs and of
+    every linear's multiply-adds, on a short sequence."""
+    import bench
+    L, window, layers = 40, 16, 7
+    pairs = []
+    for i in range(layers):
+        glob = (i + 1) % 6 == 0
+        pairs.append(sum(1 for q in range(L) for k in range(L) if k <= q and (glob or q - window < k)))
+    attn = sum(4 * 4 * p * 256 for p in pairs)
+    lin_attn = layers * 2 * L * 640 * (1536 + 1024)
+    lin_mlp = layers * 2 * L * (640 * 2 * 2048 + 2048 * 640)
+    assert bench.gemma_encoder_flops(L, layers, window) == attn + lin_attn
+    assert bench.gemma_encoder_flops(L, layers, window, whole=True) == attn + lin_attn + lin_mlp
+
+
 @pytest.mark.parametrize("L,world", [(16384, 2), (16384, 4), (16384, 8), (3952, 4), (512, 1)])
 def test_seq_shard_rows_tile_the_image_rows(L, world):
     from nanosaur2_web_b200.seqshard import seq_shard_rows
