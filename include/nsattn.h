@@ -256,6 +256,8 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* desc, const nsa_seq_sh
  * The DiT block's output projection is the gated form (app/models/nanosaur2.js:210). A is bf16
  * [M][lda], W bf16 in the Linear layout [N][K], C fp32 (the reference's residual stream), bias and
  * gate fp32.  K, lda multiples of 8; N, ldc, cOff and gOff multiples of 4; pointers 16-byte aligned.
+ * N <= 4096: the bias and gate vectors are staged whole in shared memory beside the operand ring
+ * (wider outputs return NSA_ERR_UNSUPPORTED; split them into column ranges with cOff).
  * (The reference's int8 ConvRot weights and LoRA deltas are not part of this entry.)
  * ------------------------------------------------------------------------------------------------ */
 typedef struct nsa_linear_desc {
