@@ -21,7 +21,6 @@ import argparse
 import json
 import math
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -123,80 +122,81 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- CPU baseline
 
+SAMPLE_ROWS = 512   # query rows per CPU sample (all 16 heads, all keys, prologue of every key)
+
+
 class CpuSample:
-    """The CPU restatement of the reference (oracle/attention_oracle.py, fp32 numpy) on config 2's
-    inputs (batch element 0), timed on bounded samples: some heads x the first ``rows`` query rows
-    against all keys, prologue (q/k RMSNorm + 2D RoPE) included."""
+    """The reference's CPU path for one DiT attention step, restated in PyTorch with the same torch
+    calls (oracle/torch_reference.py: rms_norm, split-half RoPE, F.scaled_dot_product_attention with
+    the additive key bias, tools/reference.py:96-104,230-237,272-286), fp32 on every host thread, on
+    config 2's inputs.  One sample is batch element 0: all 16 heads x the first SAMPLE_ROWS query rows
+    against all keys, with the RMSNorm + RoPE of every key row included, so both CPU legs amortise the
+    key prologue the same way."""
 
     def __init__(self):
+        import torch
+
         from oracle import attention_oracle as O
-        self.O = O
-        qkv, self.q_w, self.k_w, lv, bias = make_inputs(1234, 1)
-        self.x = qkv[0]
+        from oracle import torch_reference as TR
+        self.TR, self.torch = TR, torch
+        torch.set_num_threads(os.cpu_count() or 1)
+        qkv, q_w, k_w, lv, bias = make_inputs(1234, 1)
         self.L = IMG_H * IMG_W
         self.n = self.L + int(lv[0])
-        self.bias = np.concatenate([np.zeros(self.L, np.float32), bias[0][: self.n - self.L]])
-        self.cos, self.sin = O.rope_2d(IMG_H, IMG_W)
+        cos, sin = O.rope_2d(IMG_H, IMG_W)
+        T = torch.from_numpy
+        self.x, self.q_w, self.k_w = T(qkv[0]), T(q_w), T(k_w)
+        self.cos, self.sin, self.bias = T(cos), T(sin), T(bias[0])
 
-    def run(self, heads, rows=None):
+    def run(self, rows=SAMPLE_ROWS):
         """One pass over the sample; returns (flops, seconds)."""
-        O, x, L, n = self.O, self.x, self.L, self.n
-        nrows = L if rows is None else rows
         t0 = time.perf_counter()
-        for h in heads:
-            q = O.head_norm(x[:nrows, h * D:(h + 1) * D], self.q_w, 1, D, self.cos[:nrows], self.sin[:nrows])
-            k = np.concatenate([O.head_norm(x[:L, C + h * D:C + (h + 1) * D], self.k_w, 1, D, self.cos, self.sin),
-                                O.head_norm(x[L:n, C + h * D:C + (h + 1) * D], self.k_w, 1, D)])
-            v = x[:n, 2 * C + h * D:2 * C + (h + 1) * D]
-            O.attention(q, k, v, 1, D, bias=self.bias)
-        return 4.0 * len(heads) * nrows * n * D, time.perf_counter() - t0
+        self.TR.joint_attention_step(self.x, self.L, self.n, self.q_w, self.k_w, self.cos, self.sin, self.bias,
+                                     q_rows=rows)
+        return 4.0 * H * rows * self.n * D, time.perf_counter() - t0
 
-    def describe(self, heads, rows=None):
-        nrows = self.L if rows is None else rows
-        return (f"batch element 0 of config 2, {len(heads)} of 16 heads, {nrows} of {self.L} query rows x {self.n} "
-                f"keys, fp32 numpy (prologue + attention)")
+    def describe(self, rows=SAMPLE_ROWS):
+        return (f"batch element 0 of config 2: all 16 heads x {rows} of {self.L} query rows x {self.n} keys, "
+                f"q/k RMSNorm + RoPE of every key row included; PyTorch fp32 CPU "
+                f"(F.scaled_dot_product_attention), {self.torch.get_num_threads()} threads")
 
 
 def cpu_baseline(min_seconds=10.0):
-    """TFLOP/s of the CPU restatement on all 16 heads of one config-2 batch element, repeated until
-    ``min_seconds`` of CPU work; returns (TFLOP/s, seconds, description)."""
+    """TFLOP/s of the reference's PyTorch CPU path on the bounded config-2 sample, repeated (after one
+    untimed pass) until ``min_seconds`` of CPU work; returns (TFLOP/s, seconds, description)."""
     s = CpuSample()
-    heads = tuple(range(H))
+    s.run()
     flops, el, reps = 0.0, 0.0, 0
     while reps == 0 or el < min_seconds:
-        f, t = s.run(heads)
+        f, t = s.run()
         flops, el, reps = flops + f, el + t, reps + 1
-    return flops / el / 1e12, el, s.describe(heads) + f", {reps} repetition(s) in {el:.1f} s"
+    return flops / el / 1e12, el, s.describe() + f", {reps} sample(s) in {el:.1f} s"
 
 
 def cpu_threads():
     try:
-        import threadpoolctl
-        info = threadpoolctl.threadpool_info()
-        n = [i.get("num_threads") for i in info if i.get("user_api") == "blas"]
-        if n:
-            return int(n[0])
+        import torch
+        return int(torch.get_num_threads())
     except Exception:
-        pass
-    return os.cpu_count() or 1
+        return os.cpu_count() or 1
 
 
 # ----------------------------------------------------------------------------- reference arm
 
 def run_reference(args, rank):
-    """The reference arm: the CPU restatement of the reference's attention (fp32, all host BLAS
-    threads) on config 2; each step is one head x 512 query rows against all keys of batch element 0."""
+    """The reference arm: the reference's PyTorch fp32 CPU path (CpuSample) on config 2, every host
+    thread; each step is one bounded sample (all 16 heads x SAMPLE_ROWS query rows, all keys)."""
     if rank != 0:
         return
     s = CpuSample()
     flops = secs = 0.0
     for i in range(args.warmup + args.steps):
-        f, t = s.run((i % H,), rows=512)
+        f, t = s.run()
         if i >= args.warmup:
             flops, secs = flops + f, secs + t
     value = flops / secs / 1e12
     cores = cpu_threads()
-    sample = "per step: " + s.describe((0,), rows=512)
+    sample = "per step: " + s.describe()
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * secs / args.steps,
@@ -237,17 +237,6 @@ def measured_hbm():
         except Exception:
             pass
     return 6650.0
-
-
-def ncu_traffic_per_launch():
-    """Per-launch DRAM traffic of the attention kernel on this workload from the committed ncu summary
-    (profiles/attention_cfg2.md, line 'dram_bytes_per_launch = N'), or None."""
-    p = os.path.join(ROOT, "profiles", "attention_cfg2.md")
-    if os.path.exists(p):
-        m = re.search(r"dram_bytes_per_launch\s*=\s*([0-9.eE+]+)", open(p).read())
-        if m:
-            return float(m.group(1))
-    return None
 
 
 def run_ours(args, rank, world, local_rank):
@@ -327,7 +316,6 @@ def run_ours(args, rank, world, local_rank):
     att_ms = att.total_ms / max(att.launches, 1)
     att_tflops = (total_flops / args.steps) / (att_ms * 1e-3) / 1e12
     peak, peak_src = measured_peak()
-    traffic = ncu_traffic_per_launch()
 
     # ---- end to end through the public call with pinned host buffers.  Every step copies its
     # inputs host -> device and its output back; the copies of neighbouring steps overlap the
@@ -400,7 +388,9 @@ def run_ours(args, rank, world, local_rank):
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config_dict(world),
         "roofline": {"bound": "tensor", "achieved": att_tflops, "peak": peak, "unit": "TFLOP/s",
-                     "frac": att_tflops / peak, "traffic": traffic, "peak_source": peak_src,
+                     "frac": att_tflops / peak, "traffic": None,
+                     "traffic_note": "DRAM bytes need an ncu capture; none runs inside the bench",
+                     "peak_source": peak_src,
                      "kernel": "attn_fwd_kernel<96>", "kernel_ms": att_ms,
                      "prologue_ms": (pro.total_ms / max(pro.launches, 1)) if pro else None,
                      "prologue_gbs": (pro.bytes / max(pro.launches, 1)) / (pro.total_ms / max(pro.launches, 1) * 1e-3) / 1e9

@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define NSA_ABI_VERSION 1
+#define NSA_ABI_VERSION 2
 
 typedef enum nsa_status {
   NSA_OK = 0,
@@ -40,6 +40,14 @@ typedef enum nsa_status {
 } nsa_status;
 
 typedef enum nsa_dtype { NSA_F32 = 0, NSA_BF16 = 1 } nsa_dtype;
+
+/* Tensor-core precision of the attention products (the descriptors' `compute` field).
+ *   NSA_COMPUTE_BF16: q/k/v (fp32 or bf16) are rounded to bf16, fp32 accumulation (the default).
+ *   NSA_COMPUTE_TF32: fp32 inputs stay fp32 through the prologue and are multiplied at tf32 precision
+ *     (10-bit mantissa against bf16's 7), fp32 accumulation: the closer match to the reference's fp32
+ *     math (kernels.js:132-305, tools/reference.py:230-237) at half the bf16 tensor rate.  Head dim
+ *     96 with fp32 inputs only (the DiT's fp32 path); other shapes return NSA_ERR_UNSUPPORTED. */
+typedef enum nsa_compute { NSA_COMPUTE_BF16 = 0, NSA_COMPUTE_TF32 = 1 } nsa_compute;
 
 /* Library version string, e.g. "nsattn 0.1.0 sm_100a". */
 const char* nsa_version(void);
@@ -75,6 +83,7 @@ typedef struct nsa_attention_desc {
   int32_t out_dtype;  /* nsa_dtype of out */
   float scale;        /* 0 = 1/sqrt(D) (ops.js:206,214) */
   int32_t b_begin, b_count, h_begin, h_count;
+  int32_t compute;    /* nsa_compute (0: bf16 tensor cores) */
 } nsa_attention_desc;
 
 size_t nsa_attention_workspace_size(const nsa_attention_desc* desc);
@@ -122,6 +131,7 @@ typedef struct nsa_fused_desc {
   int64_t ldo, o_bstride, oOff;
   float scale;        /* 0 = 1/sqrt(D) */
   int32_t b_begin, b_count, h_begin, h_count;
+  int32_t compute;    /* nsa_compute (0: bf16 tensor cores) */
 } nsa_fused_desc;
 
 size_t nsa_fused_attention_workspace_size(const nsa_fused_desc* desc);
@@ -136,15 +146,19 @@ nsa_status nsa_fused_attention(const nsa_fused_desc* desc, const void* qkv, cons
  * allocate device memory (a host runtime whose allocator is closed to plugins, or a process that
  * must not call cudaMalloc while it shares the GPU): instead of a caller workspace it uses a scratch
  * array of NSA_NOALLOC_SCRATCH_BYTES built into the library, which every GPU that loads it holds
- * until exit.  The caller passes only inputs and outputs; nothing on this path allocates.
+ * until exit.  The caller passes only inputs and outputs; nothing on this path calls an allocator.
  *  - Shapes whose nsa_fused_attention_workspace_size() exceeds NSA_NOALLOC_SCRATCH_BYTES are
  *    rejected with NSA_ERR_WORKSPACE and a message (e.g. one config-2 DiT batch element or a
  *    16 x 1024-token Gemma layer fit; the batch-2 DiT call does not).
- *  - The first call on each device looks up the scratch address on that device
- *    (cudaGetSymbolAddress); make that first call before any stream capture.
- *  - All calls share the scratch and it keeps the previous call's contents (nothing in it has to
- *    start at zero).  Calls that overlap on the GPU (other streams or threads on the same device)
- *    race on it: order them, e.g. on one stream.
+ *  - Every call looks up the scratch address on the current device (cudaGetSymbolAddress).  The
+ *    first call on a device also loads the module that holds the array there, which is when the
+ *    driver reserves its 64 MiB (an implicit device allocation that can synchronise the device);
+ *    with CUDA_MODULE_LOADING=EAGER that happens when the library is loaded instead.  Make the first
+ *    call at start-up, before any stream capture.
+ *  - All calls share the scratch and it keeps the previous call's contents.  What must start at
+ *    zero (the counters of the tail split) is cleared by each call's own prologue.  Calls that
+ *    overlap on the GPU (other streams or threads on the same device) race on it: order them, e.g.
+ *    on one stream.
  * ------------------------------------------------------------------------------------------------ */
 #define NSA_NOALLOC_SCRATCH_BYTES (64u << 20)
 nsa_status nsa_fused_attention_noalloc(const nsa_fused_desc* desc, const void* qkv, const float* q_norm_w,

@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(HERE, "libnsattn.so")
 
 NSA_OK, NSA_ERR_INVALID_ARGUMENT, NSA_ERR_UNSUPPORTED, NSA_ERR_WORKSPACE, NSA_ERR_CUDA, NSA_ERR_DEVICE = range(6)
 NSA_F32, NSA_BF16 = 0, 1
+NSA_COMPUTE_BF16, NSA_COMPUTE_TF32 = 0, 1
 NSA_IPC_HANDLE_BYTES = 72
 
 _i32, _i64, _f32, _vp, _sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
@@ -30,6 +31,7 @@ class AttentionDesc(ctypes.Structure):
         ("ldo", _i64), ("oOff", _i64),
         ("in_dtype", _i32), ("out_dtype", _i32), ("scale", _f32),
         ("b_begin", _i32), ("b_count", _i32), ("h_begin", _i32), ("h_count", _i32),
+        ("compute", _i32),
     ]
 
 
@@ -46,6 +48,7 @@ class FusedDesc(ctypes.Structure):
         ("ldo", _i64), ("o_bstride", _i64), ("oOff", _i64),
         ("scale", _f32),
         ("b_begin", _i32), ("b_count", _i32), ("h_begin", _i32), ("h_count", _i32),
+        ("compute", _i32),
     ]
 
 

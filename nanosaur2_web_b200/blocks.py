@@ -23,6 +23,9 @@
 * ``gemma_mlp_sublayer(...)`` / ``gemma_layer(...)``: the MLP half (app/models/gemma3.js:78-89: pre-MLP
   RMSNorm, gate_up linear, GELU-tanh GLU, down linear, post-MLP RMSNorm accumulated) and the whole
   layer, attention half then MLP half.
+* ``vae_attention(...)``: the VAE decoder's single-head attention over all latent pixels, head dim C
+  = 512 (app/models/vae.js:77-88; tools/reference.py:352-357): ``ops.attention`` with H = 1, D = C on
+  the packed qkv rows of the group-normed input.
 * ``gemma_layer_attention(...)``: one Gemma3 layer's attention, headNorm(q), headNorm(k) with the
   local/global RoPE table + causal GQA 4/1 attention (app/models/gemma3.js:63-70;
   tools/reference.py:186-194), with an optional sliding window.
@@ -64,7 +67,8 @@ def prepare_text_bias(weights: Sequence[float]) -> Tuple[list, Optional[list]]:
 def _fused(qkv: torch.Tensor, *, Lq: int, Lk: int, Hq: int, Hkv: int, D: int, qOff: int, kOff: int, vOff: int,
            q_norm: torch.Tensor, k_norm: torch.Tensor, cs: Optional[RopeTable], kv_len: Optional[torch.Tensor],
            bias: Optional[torch.Tensor], biasStart: int, causal: bool, window: int, eps: float,
-           out: Optional[torch.Tensor], out_dtype: Optional[torch.dtype], shard, workspace: Optional[torch.Tensor]):
+           out: Optional[torch.Tensor], out_dtype: Optional[torch.dtype], shard, workspace: Optional[torch.Tensor],
+           compute: int = _lib.NSA_COMPUTE_BF16):
     for t in (qkv, q_norm, k_norm, kv_len, bias, out):
         if t is not None and not t.is_cuda:
             raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "tensors must live on a CUDA device")
@@ -95,6 +99,7 @@ def _fused(qkv: torch.Tensor, *, Lq: int, Lk: int, Hq: int, Hkv: int, D: int, qO
     d.bias_bstride = bias.stride(0) if (bias is not None and bias.dim() == 2) else 0
     d.ldo, d.o_bstride, d.oOff = out.stride(1), out.stride(0), 0
     d.scale = 0.0
+    d.compute = compute
     if shard is not None:
         d.b_begin, d.b_count, d.h_begin, d.h_count = shard
     L = lib()
@@ -119,6 +124,7 @@ def fused_workspace_bytes(**kw) -> int:
     d.Hq, d.Hkv, d.D = kw["Hq"], kw["Hkv"], kw["D"]
     d.in_dtype, d.out_dtype = kw.get("in_dtype", _lib.NSA_BF16), kw.get("out_dtype", _lib.NSA_BF16)
     d.causal, d.window = int(kw.get("causal", 0)), kw.get("window", 0)
+    d.compute = kw.get("compute", _lib.NSA_COMPUTE_BF16)
     shard = kw.get("shard")
     if shard is not None:
         d.b_begin, d.b_count, d.h_begin, d.h_count = shard
@@ -129,15 +135,17 @@ def dit_block_attention(qkv: torch.Tensor, *, L: int, q_norm: torch.Tensor, k_no
                         cs: Optional[RopeTable], text_rows: int = 0, kv_len: Optional[torch.Tensor] = None,
                         bias: Optional[torch.Tensor] = None, eps: float = 1e-6, out: Optional[torch.Tensor] = None,
                         out_dtype: Optional[torch.dtype] = None, shard=None,
-                        workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+                        workspace: Optional[torch.Tensor] = None, tf32: bool = False) -> torch.Tensor:
     """qkv: [B, L + text_rows, 3*1536] with rows [0, L) image q|k|v and rows [L, L+text_rows) text k|v
     (app/models/nanosaur2.js:194-202).  kv_len[b] = L + valid text rows; bias: [B, text_rows] log prompt
     weights of the text keys (biasStart = L).  With text_rows = 0 this is an odd, image-only block.
-    Returns [B, L, 1536]."""
+    ``tf32`` (fp32 qkv only): keep the prepared q/k/v in fp32 and multiply at tf32 precision, the
+    closer match to the reference's fp32 math (NSA_COMPUTE_TF32).  Returns [B, L, 1536]."""
     C = DIT_HEADS * DIT_HEAD_DIM
     return _fused(qkv, Lq=L, Lk=L + text_rows, Hq=DIT_HEADS, Hkv=DIT_HEADS, D=DIT_HEAD_DIM, qOff=0, kOff=C,
                   vOff=2 * C, q_norm=q_norm, k_norm=k_norm, cs=cs, kv_len=kv_len, bias=bias, biasStart=L,
-                  causal=False, window=0, eps=eps, out=out, out_dtype=out_dtype, shard=shard, workspace=workspace)
+                  causal=False, window=0, eps=eps, out=out, out_dtype=out_dtype, shard=shard, workspace=workspace,
+                  compute=_lib.NSA_COMPUTE_TF32 if tf32 else _lib.NSA_COMPUTE_BF16)
 
 
 def projection_buffers(B: int, L: int, text_rows: int, device) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -385,3 +393,17 @@ def gemma_layer_attention(qkv: torch.Tensor, *, q_norm: torch.Tensor, k_norm: to
     return _fused(qkv, Lq=Lt, Lk=Lt, Hq=H, Hkv=KH, D=D, qOff=0, kOff=H * D, vOff=(H + KH) * D, q_norm=q_norm,
                   k_norm=k_norm, cs=cs, kv_len=kv_len, bias=None, biasStart=0, causal=True, window=window, eps=eps,
                   out=out, out_dtype=out_dtype, shard=shard, workspace=workspace)
+
+
+def vae_attention(qkv: torch.Tensor, *, C: int = 512, out: Optional[torch.Tensor] = None,
+                  out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """The VAE decoder's attention call (app/models/vae.js:82): one head of dim C over all hw pixels of
+    the packed q|k|v rows [hw, 3C] (or [B, hw, 3C]) that the qkv linear of the group-normed input
+    writes; scale 1/sqrt(C); returns [hw, C].  Head dim 512 runs on the kernel that splits each query
+    tile's output columns over two CTAs."""
+    from .ops import attention
+    hw = qkv.shape[-2]
+    if qkv.shape[-1] != 3 * C:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "qkv rows must hold q | k | v of C channels each")
+    return attention(q=qkv, k=qkv, v=qkv, Lq=hw, Lk=hw, H=1, D=C, ldq=3 * C, ldk=3 * C, ldv=3 * C, qOff=0, kOff=C,
+                     vOff=2 * C, out=out, out_dtype=out_dtype)

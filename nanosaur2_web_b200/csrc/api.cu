@@ -46,16 +46,27 @@ unsigned long long wait_timeout_ns() {
 
 // ------------------------------------------------------------------------------------ profiler
 
+// Valid (query, key) pairs of an attention launch whose per-batch key counts (kv_len) live on the
+// device: the profiler copies them into pinned host memory on the launch's stream, before the start
+// event, and counts the pairs when the records are read (after the stop event has completed).
+struct PairCount {
+  int Bs = 0, Lq = 0, Lk = 0, causal = 0, window = 0, D = 0, Hqs = 0;
+  int32_t* kv_host = nullptr;   // [Bs] pinned, or null: every element has Lk keys
+};
+
 struct ProfRecord {
   std::string name;
   double flops, bytes;
   cudaEvent_t start, stop;
+  PairCount pairs;   // Bs > 0: flops are counted from the copied kv_len at read time
 };
 
 std::mutex g_prof_mu;
 bool g_prof_on = false;
 std::vector<ProfRecord> g_prof_records;
 std::vector<cudaEvent_t> g_event_pool;
+std::vector<int32_t*> g_pinned_pool;   // pinned kv_len copies, kBatchSlots ints each
+constexpr int kBatchSlots = 4096;
 
 cudaEvent_t take_event() {
   if (!g_event_pool.empty()) {
@@ -68,8 +79,31 @@ cudaEvent_t take_event() {
   return e;
 }
 
+// Valid (query, key) pairs of one batch element with n valid keys: query i sees keys
+// [max(0, i - window + 1), min(n, i + 1)) when causal, [.., n) otherwise (the kernels' masks).
+double valid_pairs(int Lq, int n, int causal, int window) {
+  if (!causal && window <= 0) return (double)Lq * n;
+  double pairs = 0;
+  for (int i = 0; i < Lq; ++i) {
+    const int hi = causal ? std::min(n, i + 1) : n;
+    const int lo = window > 0 ? std::max(0, i - window + 1) : 0;
+    if (hi > lo) pairs += hi - lo;
+  }
+  return pairs;
+}
+
+double pair_flops(const PairCount& c) {
+  double f = 0;
+  for (int b = 0; b < c.Bs; ++b) {
+    const int n = c.kv_host ? std::min(std::max(c.kv_host[b], 0), c.Lk) : c.Lk;
+    f += 4.0 * c.Hqs * valid_pairs(c.Lq, n, c.causal, c.window) * c.D;
+  }
+  return f;
+}
+
 template <class Launch>
-cudaError_t profiled(const char* name, double flops, double bytes, cudaStream_t stream, Launch&& launch) {
+cudaError_t profiled(const char* name, double flops, double bytes, cudaStream_t stream, Launch&& launch,
+                     PairCount pairs = PairCount{}, const int32_t* kv_len_dev = nullptr) {
   bool on;
   {
     std::lock_guard<std::mutex> lk(g_prof_mu);
@@ -81,12 +115,29 @@ cudaError_t profiled(const char* name, double flops, double bytes, cudaStream_t 
     std::lock_guard<std::mutex> lk(g_prof_mu);
     a = take_event();
     b = take_event();
+    if (pairs.Bs > 0 && kv_len_dev) {
+      if (pairs.Bs > kBatchSlots) {
+        pairs.Bs = 0;   // too many elements to copy: keep the host-side count
+      } else {
+        if (g_pinned_pool.empty()) {
+          int32_t* h = nullptr;
+          if (cudaMallocHost(&h, kBatchSlots * sizeof(int32_t)) == cudaSuccess) g_pinned_pool.push_back(h);
+        }
+        if (!g_pinned_pool.empty()) {
+          pairs.kv_host = g_pinned_pool.back();
+          g_pinned_pool.pop_back();
+          cudaMemcpyAsync(pairs.kv_host, kv_len_dev, pairs.Bs * sizeof(int32_t), cudaMemcpyDeviceToHost, stream);
+        } else {
+          pairs.Bs = 0;
+        }
+      }
+    }
   }
   cudaEventRecord(a, stream);
   const cudaError_t e = launch();
   cudaEventRecord(b, stream);
   std::lock_guard<std::mutex> lk(g_prof_mu);
-  g_prof_records.push_back({name, flops, bytes, a, b});
+  g_prof_records.push_back({name, flops, bytes, a, b, pairs});
   return e;
 }
 
@@ -124,16 +175,19 @@ bool encode_rows(CUtensorMap* map, const void* base, int64_t width, int64_t ld, 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Map over a head-major bf16 tile buffer [rows][D]; boxes of [box_rows rows][blk elements].
-bool encode_tiles(CUtensorMap* map, void* base, int D, int64_t rows, int blk, int box_rows) {
+// Map over a head-major tile buffer [rows][D] of bf16 (esize 2) or fp32 (esize 4) elements; boxes of
+// [box_rows rows][blk elements], swizzled by the box row's width (128 or 64 bytes) as the tcgen05
+// descriptors expect.
+bool encode_tiles(CUtensorMap* map, void* base, int D, int64_t rows, int blk, int box_rows, int esize = 2) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * esize};
   const cuuint32_t box[2] = {(cuuint32_t)blk, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  const CUtensorMapSwizzle sw = blk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+  const CUtensorMapSwizzle sw = blk * esize == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUtensorMapDataType dt = esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  return fn(map, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -146,6 +200,10 @@ struct Plan {
   int B, Lq, Lk, Hq, group, D;       // full problem
   int b0, Bs, hq0, Hqs, hkv0, Hkvs;  // shard
   int NQ, BN, blk, Lq_pad, Lk_pad;
+  int v_rows;         // V tiles' TMA box rows
+  bool v_direct_ok;   // the head dim's kernel can read V from the input rows
+  bool tf32;          // fp32 tiles and tf32 MMAs (NSA_COMPUTE_TF32)
+  int esize;          // bytes per tile element (2 bf16, 4 fp32)
   bool qtmem;
   int split_cap;   // work units whose key range may be split over two CTAs (0: never)
   size_t q_bytes, k_bytes, v_bytes, split_bytes, total;
@@ -155,7 +213,7 @@ struct Plan {
 size_t split_scratch_bytes(int units, int NQ, int D) {
   if (units <= 0) return 0;
   const size_t rows = (size_t)units * 2 * NQ * nsa::kTileM;
-  return align_up(rows * D * 4, 256) + align_up(rows * 2 * 4, 256) + align_up((size_t)units * 4, 256);
+  return align_up(rows * D * 4, 256) + align_up(rows * 2 * 4, 256) + align_up((size_t)units * 2 * 4, 256);
 }
 
 struct SplitScratch {
@@ -196,6 +254,7 @@ int split_units_for(const Plan& pl, int causal, int window) {
 struct CommonArgs {
   int B, Lq, Lk, H, group, D, causal, window, in_dtype, out_dtype;
   int b_begin, b_count, h_begin, h_count;
+  int compute;   // nsa_compute
 };
 
 nsa_status make_plan(const CommonArgs& a, Plan* pl) {
@@ -203,10 +262,17 @@ nsa_status make_plan(const CommonArgs& a, Plan* pl) {
     return fail(NSA_ERR_INVALID_ARGUMENT, "B, Lq, Lk, H and D must be >= 1");
   if (a.group < 1 || a.H % a.group != 0)
     return fail(NSA_ERR_INVALID_ARGUMENT, "group must divide the number of query heads");
-  const nsa::AttnGeometry geo = nsa::attention_geometry(a.D);
+  if (a.compute != NSA_COMPUTE_BF16 && a.compute != NSA_COMPUTE_TF32)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "compute must be NSA_COMPUTE_BF16 or NSA_COMPUTE_TF32");
+  const bool tf32 = a.compute == NSA_COMPUTE_TF32;
+  if (tf32 && (a.D != 96 || a.in_dtype != NSA_F32))
+    return fail(NSA_ERR_UNSUPPORTED, "tf32 compute covers head dim 96 with fp32 inputs");
+  // the tf32 kernel: one 128-row query tile per unit, 128-key tiles, fp32 boxes of 32 elements
+  const nsa::AttnGeometry geo = tf32 ? nsa::AttnGeometry{1, 128, 32, false, 128, false} : nsa::attention_geometry(a.D);
   const int NQ = geo.NQ;
   if (NQ == 0)
-    return fail(NSA_ERR_UNSUPPORTED, "attention: unsupported head dim " + std::to_string(a.D) + " (64, 96, 128, 256)");
+    return fail(NSA_ERR_UNSUPPORTED,
+                "attention: unsupported head dim " + std::to_string(a.D) + " (64, 96, 128, 256, 512)");
   if (a.in_dtype != NSA_F32 && a.in_dtype != NSA_BF16) return fail(NSA_ERR_INVALID_ARGUMENT, "bad input dtype");
   if (a.out_dtype != NSA_F32 && a.out_dtype != NSA_BF16) return fail(NSA_ERR_INVALID_ARGUMENT, "bad output dtype");
   if (a.window < 0) return fail(NSA_ERR_INVALID_ARGUMENT, "window must be >= 0");
@@ -225,14 +291,18 @@ nsa_status make_plan(const CommonArgs& a, Plan* pl) {
   p.BN = geo.BN;
   p.blk = geo.blk;
   p.qtmem = geo.qtmem;
+  p.v_rows = geo.v_rows;
+  p.v_direct_ok = geo.v_direct_ok;
+  p.tf32 = tf32;
+  p.esize = tf32 ? 4 : 2;
   p.Lq_pad = (int)round_up(a.Lq, (int64_t)NQ * nsa::kTileM);
   p.Lk_pad = (int)round_up(a.Lk, geo.BN);
   const int64_t q_rows = (int64_t)p.Bs * p.Hqs * p.Lq_pad;
   const int64_t kv_rows = (int64_t)p.Bs * p.Hkvs * p.Lk_pad;
   if (q_rows >= (int64_t)1 << 31 || kv_rows >= (int64_t)1 << 31 || (int64_t)p.Bs * p.Hqs * (p.Lq_pad / (NQ * 128)) >= (int64_t)1 << 31)
     return fail(NSA_ERR_UNSUPPORTED, "problem too large for one launch");
-  p.q_bytes = align_up((size_t)q_rows * a.D * 2, 1024);
-  p.k_bytes = align_up((size_t)kv_rows * a.D * 2, 1024);
+  p.q_bytes = align_up((size_t)q_rows * a.D * p.esize, 1024);
+  p.k_bytes = align_up((size_t)kv_rows * a.D * p.esize, 1024);
   p.v_bytes = p.k_bytes;
   const long long units = (long long)p.Bs * p.Hqs * (p.Lq_pad / (NQ * nsa::kTileM));
   p.split_cap = (NQ == 2 && !a.causal && !a.window) ? (int)std::min<long long>(units, nsa::kSplitUnitsMax) : 0;
@@ -296,11 +366,23 @@ void set_split(nsa::AttnParams* ap, const Plan& pl, const CommonArgs& a, const S
   ap->split_count = s.count;
 }
 
-// Algorithmic flops of one attention launch: 4 * B * H * valid pairs * D (app/gpu/ops.js:207).
+// Algorithmic flops of one attention launch: 4 * B * H * valid pairs * D (app/gpu/ops.js:207), the
+// causal and window masks counted here; per-batch key counts on the device (kv_len) are counted by
+// the profiler from a copy (attn_pairs).
 double attn_flops(const Plan& pl, const CommonArgs& a) {
-  double pairs = (double)pl.Lq * pl.Lk;
-  if (a.causal) pairs = (double)pl.Lq * (pl.Lq + 1) / 2.0;
-  return 4.0 * pl.Bs * pl.Hqs * pairs * pl.D;
+  return 4.0 * pl.Bs * pl.Hqs * valid_pairs(pl.Lq, pl.Lk, a.causal, a.window) * pl.D;
+}
+
+PairCount attn_pairs(const Plan& pl, const CommonArgs& a) {
+  PairCount c;
+  c.Bs = pl.Bs;
+  c.Lq = pl.Lq;
+  c.Lk = pl.Lk;
+  c.causal = a.causal;
+  c.window = a.window;
+  c.D = pl.D;
+  c.Hqs = pl.Hqs;
+  return c;
 }
 
 // Prologue + attention launches shared by nsa_attention and nsa_fused_attention.
@@ -319,6 +401,7 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
   if (!err) return fail(NSA_ERR_CUDA, "cannot resolve the device error word on this device");
 
   pp.src_f32 = a.in_dtype == NSA_F32;
+  pp.out_f32 = pl.tf32 ? 1 : 0;
   pp.B = pl.Bs;
   pp.b_begin = pl.b0;
   pp.Lq = pl.Lq;
@@ -337,14 +420,14 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
   for (int i = 0; i < 3; ++i) pp.row0[i] = pp.src_row0[i] = 0;
   const SplitScratch split = split_scratch(base + pl.q_bytes + pl.k_bytes + pl.v_bytes, pl.split_cap, pl.NQ, pl.D);
   pp.zero_ptr = pl.split_cap > 0 ? split.count : nullptr;   // the attention's split counters start at zero
-  pp.zero_count = pl.split_cap;
+  pp.zero_count = 2 * pl.split_cap;   // two counters (query tiles) per split unit
   auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
   pp.skip_q = 0;
   // V needs no normalisation: for bf16 rows that a tiled map can cover (16-byte aligned rows and
   // head offsets, whole rows per batch element) the attention kernel reads V tiles of valid keys
   // straight from the input, and the prologue writes only the last partial tile and the padding.
   static const unsigned v_direct_enabled = env_flag("NSA_V_DIRECT", 1);   // NSA_V_DIRECT=0 turns it off
-  const bool v_direct = v_direct_enabled && a.in_dtype == NSA_BF16 && al16(pp.v.ptr) &&
+  const bool v_direct = v_direct_enabled && pl.v_direct_ok && a.in_dtype == NSA_BF16 && al16(pp.v.ptr) &&
                         pp.v.ld % 8 == 0 && pp.v.off % 8 == 0 &&
                         (pl.B == 1 || (pp.v.bstride > 0 && pp.v.bstride % pp.v.ld == 0)) &&
                         pp.v.off + (int64_t)(pl.hkv0 + pl.Hkvs) * pl.D <= pp.v.ld;
@@ -358,9 +441,9 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
   if (e != cudaSuccess) return cuda_fail(e, "prologue launch");
 
   CUtensorMap tq, tk, tv;
-  const bool maps_ok = encode_tiles(&tq, Qs, pl.D, (int64_t)pl.Bs * pl.Hqs * pl.Lq_pad, pl.blk, nsa::kTileM);
-  if (!maps_ok || !encode_tiles(&tk, Ks, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk, pl.BN) ||
-      !encode_tiles(&tv, Vs, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk, pl.BN))
+  const bool maps_ok = encode_tiles(&tq, Qs, pl.D, (int64_t)pl.Bs * pl.Hqs * pl.Lq_pad, pl.blk, nsa::kTileM, pl.esize);
+  if (!maps_ok || !encode_tiles(&tk, Ks, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk, pl.BN, pl.esize) ||
+      !encode_tiles(&tv, Vs, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk, pl.v_rows, pl.esize))
     return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed (driver entry point unavailable?)");
   CUtensorMap tvd = tv;
   if (v_direct) {
@@ -390,8 +473,12 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
   ap.q_b0 = pl.b0;
   ap.q_h0 = pl.hq0;
   const double flops = attn_flops(pl, a);
-  e = profiled("attention", flops, 0.0, stream,
-               [&] { return nsa::launch_attention(ap, pl.D, tq, tk, tv, tvd, stream); });
+  e = profiled(pl.tf32 ? "attention_tf32" : "attention", flops, 0.0, stream,
+               [&] {
+                 return pl.tf32 ? nsa::launch_attention_tf32(ap, tq, tk, tv, stream)
+                                : nsa::launch_attention(ap, pl.D, tq, tk, tv, tvd, stream);
+               },
+               attn_pairs(pl, a), kv_len ? kv_len + pl.b0 : nullptr);
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");
   return NSA_OK;
 }
@@ -412,13 +499,13 @@ __global__ void selftest_wait_kernel(int* err, unsigned long long timeout_ns) {
 
 CommonArgs common_from(const nsa_attention_desc* d) {
   return CommonArgs{d->B, d->Lq, d->Lk, d->H, d->group, d->D, d->causal, d->window, d->in_dtype, d->out_dtype,
-                    d->b_begin, d->b_count, d->h_begin, d->h_count};
+                    d->b_begin, d->b_count, d->h_begin, d->h_count, d->compute};
 }
 
 CommonArgs common_from(const nsa_fused_desc* d) {
   const int group = d->Hkv > 0 ? d->Hq / d->Hkv : 0;
   return CommonArgs{d->B, d->Lq, d->Lk, d->Hq, group, d->D, d->causal, d->window, d->in_dtype, d->out_dtype,
-                    d->b_begin, d->b_count, d->h_begin, d->h_count};
+                    d->b_begin, d->b_count, d->h_begin, d->h_count, d->compute};
 }
 
 // ------------------------------------------------------------------------------------ sequence shards
@@ -449,6 +536,10 @@ nsa_status make_seq_plan(const nsa_fused_desc* d, const nsa_seq_shard* s, SeqPla
     return fail(NSA_ERR_INVALID_ARGUMENT, "shard rows [q_begin, q_begin + q_count) must lie in [0, Lq)");
   if (s->qkv_image_row0 < 0 || s->qkv_text_row0 < 0)
     return fail(NSA_ERR_INVALID_ARGUMENT, "qkv_image_row0 and qkv_text_row0 must be >= 0");
+  if (d->D == 512)
+    return fail(NSA_ERR_UNSUPPORTED, "head dim 512 runs through nsa_attention / nsa_fused_attention, not sequence shards");
+  if (d->compute != NSA_COMPUTE_BF16)
+    return fail(NSA_ERR_UNSUPPORTED, "sequence shards compute in bf16 (compute = NSA_COMPUTE_BF16)");
   SeqPlan p{};
   p.a = common_from(d);
   p.a.Lq = s->q_count;
@@ -497,18 +588,39 @@ namespace nsa {
 
 void record_error(const std::string& msg) { g_last_error = msg; }
 
+// Resolved at every call rather than cached: after a cudaDeviceReset (or anything else that reloads
+// the module) a cached address would be stale, and the lookup is cheap.
 int* device_error_word() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_device_error_word) != cudaSuccess) return nullptr;
+  return static_cast<int*>(p);
+}
+
+int device_sm_count() {
   static std::mutex mu;
-  static int* cache[128] = {};
+  static int cache[128] = {};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 148;
   std::lock_guard<std::mutex> lk(mu);
-  if (!cache[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_device_error_word) != cudaSuccess) return nullptr;
-    cache[dev] = static_cast<int*>(p);
+  if (cache[dev] <= 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+    cache[dev] = n;
   }
   return cache[dev];
+}
+
+cudaError_t once_per_device(DeviceOnce& state, cudaError_t (*setup)()) {
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(mu);
+  if (state.done[dev]) return cudaSuccess;
+  e = setup();
+  if (e == cudaSuccess) state.done[dev] = true;
+  return e;
 }
 
 }  // namespace nsa
@@ -667,6 +779,7 @@ void nsa_profiler_reset(void) {
     cudaEventSynchronize(r.stop);
     g_event_pool.push_back(r.start);
     g_event_pool.push_back(r.stop);
+    if (r.pairs.kv_host) g_pinned_pool.push_back(r.pairs.kv_host);
   }
   g_prof_records.clear();
 }
@@ -688,7 +801,7 @@ int32_t nsa_profiler_read(nsa_kernel_stat* out, int32_t max_entries) {
     }
     st->launches += 1;
     st->total_ms += ms;
-    st->flops += r.flops;
+    st->flops += r.pairs.kv_host ? pair_flops(r.pairs) : r.flops;
     st->bytes += r.bytes;
   }
   const int32_t n = (int32_t)stats.size();
@@ -834,7 +947,7 @@ nsa_status nsa_seq_shard_prologue_peers(const nsa_fused_desc* d, const nsa_seq_s
   const SplitScratch split =
       split_scratch(static_cast<uint8_t*>(q_prime) + sp.q_tiles_bytes, pl.split_cap, pl.NQ, pl.D);
   pp.zero_ptr = pl.split_cap > 0 ? split.count : nullptr;   // the attention's split counters start at zero
-  pp.zero_count = pl.split_cap;
+  pp.zero_count = 2 * pl.split_cap;   // two counters (query tiles) per split unit
   const double in_elem = d->in_dtype == NSA_F32 ? 4.0 : 2.0;
   const cudaStream_t strm = static_cast<cudaStream_t>(stream);
   double bytes = (double)pl.Bs * sp.q_count * (pl.Hqs + 2.0 * pl.Hkvs) * pl.D * (in_elem + 2.0);
@@ -948,7 +1061,7 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* d, const nsa_seq_shard
   pp.q_prime = Q;
   pp.kv_packed = KV;
   pp.zero_ptr = pl.split_cap > 0 ? split.count : nullptr;   // the attention's split counters start at zero
-  pp.zero_count = pl.split_cap;
+  pp.zero_count = 2 * pl.split_cap;   // two counters (query tiles) per split unit
   pp.err = err;
   pp.timeout_ns = wait_timeout_ns();
 
@@ -1175,7 +1288,8 @@ nsa_status nsa_seq_shard_attention(const nsa_fused_desc* d, const nsa_seq_shard*
                           pl.D));
   const cudaStream_t strm = static_cast<cudaStream_t>(stream);
   cudaError_t e = profiled("attention", attn_flops(pl, sp.a), 0.0, strm,
-                           [&] { return nsa::launch_attention(ap, pl.D, tq, tkv, tkv, tkv, strm); });
+                           [&] { return nsa::launch_attention(ap, pl.D, tq, tkv, tkv, tkv, strm); },
+                           attn_pairs(pl, sp.a), kv_len ? kv_len + pl.b0 : nullptr);
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");
   return NSA_OK;
 }

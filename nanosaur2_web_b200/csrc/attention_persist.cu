@@ -30,49 +30,73 @@ constexpr float kLog2eP = 1.4426950408889634f;
 constexpr float kRescaleP = 8.0f;   // log2 units: P may reach 2^8 before O is rescaled
 constexpr int kKeyBiasP = 1024;     // keys covered by the shared-memory key bias/mask table
 
+// Tile geometry of the persistent one-query-tile kernel: bf16 operands at head dim 256 (Gemma), or
+// fp32 operands multiplied as tf32 at head dim 96 (the DiT's fp32 path, tighter than bf16).
+template <bool TF32>
 struct CfgP {
-  static constexpr int D = 256, BN = 128, NS = 1;
-  static constexpr int BLK = 64, NB = D / BLK, ROWB = BLK * 2;
-  static constexpr uint32_t SWZ = 2u;                  // 128-byte swizzle
-  static constexpr int QBLK_BYTES = kTileM * ROWB;     // [128 rows][64]
+  static constexpr int D = TF32 ? 96 : 256, BN = 128, NS = 1;
+  static constexpr int ESZ = TF32 ? 4 : 2;                   // operand bytes per element
+  static constexpr int ROWB = 128;                           // bytes per row of a swizzle block
+  static constexpr int BLK = ROWB / ESZ, NB = D / BLK;       // elements per block row, blocks per row
+  static constexpr int KMMA = TF32 ? 8 : 16;                 // K of one MMA (32 bytes of a row)
+  static constexpr uint32_t SWZ = 2u;                        // 128-byte swizzle
+  static constexpr int QBLK_BYTES = kTileM * ROWB;           // [128 rows][BLK]
   static constexpr int KBLK_BYTES = BN * ROWB;
-  static constexpr int Q_TILE_BYTES = kTileM * D * 2;
-  static constexpr int KV_TILE_BYTES = BN * D * 2;
-  static constexpr int KSTEPS_QK = D / 16, KSTEPS_PV = BN / 16, PV_HALF0 = 4;
+  static constexpr int Q_TILE_BYTES = kTileM * D * ESZ;
+  static constexpr int KV_TILE_BYTES = BN * D * ESZ;
+  static constexpr int KSTEPS_QK = D / KMMA, KSTEPS_PV = BN / KMMA, PV_HALF0 = 64 / KMMA;
+  static constexpr int P_HALF_COLS = TF32 ? 64 : 32;        // TMEM columns of 64 keys of P
   static constexpr int THREADS = 256;
   static constexpr int NBARS = 4 * NS + 2 + 4 + 2 + 4 + 1;
   static constexpr int SMEM_BYTES = Q_TILE_BYTES + 2 * NS * KV_TILE_BYTES + kKeyBiasP * 4 + NBARS * 8 + 16 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, BN, 0, 0);
-  static constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, D, 0, 1);
+  static constexpr uint32_t IDESC_QK = TF32 ? idesc_tf32_f32(128, BN, 0, 0) : idesc_bf16_f32(128, BN, 0, 0);
+  static constexpr uint32_t IDESC_PV = TF32 ? idesc_tf32_f32(128, D, 0, 1) : idesc_bf16_f32(128, D, 0, 1);
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(SMEM_BYTES > 117 * 1024, "one CTA per SM (each allocates all 512 TMEM columns)");
+  static_assert(256 + D <= 512, "tensor memory: S0, S1 and O");
   static __device__ __forceinline__ uint32_t s_col(int buf) { return (uint32_t)(buf * BN); }
   static __device__ __forceinline__ uint32_t o_col() { return 256u; }
   static __device__ __forceinline__ uint32_t kmajor_off(int kk, int blk_bytes) {
-    constexpr int per_blk = BLK / 16;
+    constexpr int per_blk = BLK / KMMA;
     return (uint32_t)((kk / per_blk) * blk_bytes + (kk % per_blk) * 32);
   }
 };
 
+template <bool TF32>
+__device__ __forceinline__ void p_mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  if constexpr (TF32) mma_ss_tf32(d, a, b, idesc, acc);
+  else mma_ss(d, a, b, idesc, acc);
+}
+template <bool TF32>
+__device__ __forceinline__ void p_mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  if constexpr (TF32) mma_ts_tf32(d, a, b, idesc, acc);
+  else mma_ts(d, a, b, idesc, acc);
+}
+
+template <bool TF32>
 __device__ __forceinline__ void p_issue_qk(uint32_t d_tmem, uint32_t sq, uint32_t sk) {
-  using C = CfgP;
+  using C = CfgP<TF32>;
 #pragma unroll
   for (int kk = 0; kk < C::KSTEPS_QK; ++kk) {
     const uint64_t a = smem_desc(sq + C::kmajor_off(kk, C::QBLK_BYTES), 16, 8 * C::ROWB, C::SWZ);
     const uint64_t b = smem_desc(sk + C::kmajor_off(kk, C::KBLK_BYTES), 16, 8 * C::ROWB, C::SWZ);
-    mma_ss(d_tmem, a, b, C::IDESC_QK, kk > 0 ? 1u : 0u);
+    p_mma_ss<TF32>(d_tmem, a, b, C::IDESC_QK, kk > 0 ? 1u : 0u);
   }
 }
 
+template <bool TF32>
 __device__ __forceinline__ void p_issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint32_t sv, bool accumulate,
                                                 int half) {
-  using C = CfgP;
+  using C = CfgP<TF32>;
   const int k_begin = half == 0 ? 0 : C::PV_HALF0;
   const int k_end = half == 0 ? C::PV_HALF0 : C::KSTEPS_PV;
 #pragma unroll
   for (int kk = k_begin; kk < k_end; ++kk) {
-    const uint64_t b = smem_desc(sv + (uint32_t)(kk * 16 * C::ROWB), C::KBLK_BYTES, 8 * C::ROWB, C::SWZ);
-    mma_ts(d_tmem, p_tmem + (uint32_t)(kk * 8), b, C::IDESC_PV, (accumulate || kk > 0) ? 1u : 0u);
+    // V is MN-major: KMMA keys per k-step, head-dim blocks of BLK elements KBLK_BYTES apart; P takes
+    // 8 TMEM columns per k-step (16 bf16 keys two to a column, or 8 fp32 keys)
+    const uint64_t b = smem_desc(sv + (uint32_t)(kk * C::KMMA * C::ROWB), C::KBLK_BYTES, 8 * C::ROWB, C::SWZ);
+    p_mma_ts<TF32>(d_tmem, p_tmem + (uint32_t)(kk * 8), b, C::IDESC_PV, (accumulate || kk > 0) ? 1u : 0u);
   }
 }
 
@@ -82,7 +106,7 @@ struct Unit {
 };
 
 __device__ __forceinline__ Unit decode_unit(const AttnParams& p, int u) {
-  constexpr int BN = CfgP::BN;
+  constexpr int BN = CfgP<false>::BN;
   Unit w;
   const int bh = p.B * p.Hq;
   const int qb_raw = u / bh, rest = u % bh;
@@ -103,11 +127,12 @@ __device__ __forceinline__ Unit decode_unit(const AttnParams& p, int u) {
   return w;
 }
 
-__global__ void __launch_bounds__(CfgP::THREADS, 1)
+template <bool TF32>
+__global__ void __launch_bounds__(CfgP<TF32>::THREADS, 1)
     attn_persist_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmVd,
                         const AttnParams p) {
-  using C = CfgP;
+  using C = CfgP<TF32>;
   constexpr int D = C::D, BN = C::BN, NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -241,7 +266,7 @@ __global__ void __launch_bounds__(CfgP::THREADS, 1)
         const int s = gk % NS;
         if (!wait_bounded(&k_full[s], (gk / NS) & 1, abort_flag, p.err, kErrTimeoutMma, to)) return false;
         tc_fence_after();
-        p_issue_qk(tmem + C::s_col(t_idx & 1), sq, sk + (uint32_t)(s * C::KV_TILE_BYTES));
+        p_issue_qk<TF32>(tmem + C::s_col(t_idx & 1), sq, sk + (uint32_t)(s * C::KV_TILE_BYTES));
         tc_commit(&s_full[t_idx & 1]);
         tc_commit(&k_empty[s]);
         if (last) tc_commit(q_empty);   // the unit's last S: Q may be replaced
@@ -263,7 +288,7 @@ __global__ void __launch_bounds__(CfgP::THREADS, 1)
             ok = wait_bounded(&p_full[(t & 1) * 2 + h], (t >> 1) & 1, abort_flag, p.err, kErrTimeoutMma, to);
             if (!ok) break;
             tc_fence_after();
-            p_issue_pv_half(tmem + C::o_col(), tmem + C::s_col(t & 1), sv + (uint32_t)(s * C::KV_TILE_BYTES), j > 0, h);
+            p_issue_pv_half<TF32>(tmem + C::o_col(), tmem + C::s_col(t & 1), sv + (uint32_t)(s * C::KV_TILE_BYTES), j > 0, h);
           }
           if (!ok) break;
           tc_commit(&o_full[0]);
@@ -409,17 +434,32 @@ __global__ void __launch_bounds__(CfgP::THREADS, 1)
         uint64_t ls[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          // keys 64*half .. 64*half+63 -> P columns 32*half .. 32*half+31
-          uint32_t pk[32];
+          if constexpr (TF32) {
+            // keys 64*half .. 64*half+63 -> P columns 64*half .. 64*half+63, fp32 (read as tf32)
+            uint32_t pf[64];
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            float y0, y1;
-            f2_unpack(f2_fma(f2_pack(x[64 * half + 2 * c], x[64 * half + 2 * c + 1]), sc2, nm2), y0, y1);
-            const float a0 = ex2(y0), a1 = ex2(y1);
-            ls[c & 3] = f2_add(ls[c & 3], f2_pack(a0, a1));
-            pk[c] = pack_bf16x2(a0, a1);
+            for (int c = 0; c < 32; ++c) {
+              float y0, y1;
+              f2_unpack(f2_fma(f2_pack(x[64 * half + 2 * c], x[64 * half + 2 * c + 1]), sc2, nm2), y0, y1);
+              const float a0 = ex2(y0), a1 = ex2(y1);
+              ls[c & 3] = f2_add(ls[c & 3], f2_pack(a0, a1));
+              pf[2 * c] = __float_as_uint(a0);
+              pf[2 * c + 1] = __float_as_uint(a1);
+            }
+            tmem_st64(s_addr + (uint32_t)(64 * half), pf);
+          } else {
+            // keys 64*half .. 64*half+63 -> P columns 32*half .. 32*half+31, bf16 pairs
+            uint32_t pk[32];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              float y0, y1;
+              f2_unpack(f2_fma(f2_pack(x[64 * half + 2 * c], x[64 * half + 2 * c + 1]), sc2, nm2), y0, y1);
+              const float a0 = ex2(y0), a1 = ex2(y1);
+              ls[c & 3] = f2_add(ls[c & 3], f2_pack(a0, a1));
+              pk[c] = pack_bf16x2(a0, a1);
+            }
+            tmem_st32(s_addr + (uint32_t)(32 * half), pk);
           }
-          tmem_st32(s_addr + (uint32_t)(32 * half), pk);
           tc_fence_before();
           mbar_arrive(&p_full[sbuf * 2 + half]);
         }
@@ -486,31 +526,37 @@ __global__ void __launch_bounds__(CfgP::THREADS, 1)
   }
 }
 
+template <bool TF32>
+cudaError_t launch_persist_t(const AttnParams& p, const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                             const CUtensorMap& tmV, const CUtensorMap& tmVd, cudaStream_t stream) {
+  using C = CfgP<TF32>;
+  static DeviceOnce once;
+  cudaError_t e = once_per_device(once, [] {
+    return cudaFuncSetAttribute(attn_persist_kernel<TF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                CfgP<TF32>::SMEM_BYTES);
+  });
+  if (e != cudaSuccess) return e;
+  const int sms = device_sm_count();
+  if (p.split_units > 0) return cudaErrorInvalidValue;   // the tail split is for two-tile kernels
+  if (TF32 && p.v_direct) return cudaErrorInvalidValue;  // fp32 V tiles come from the prologue
+  const long long units = (long long)p.B * p.Hq * p.q_blocks;
+  if (units <= 0) return cudaSuccess;
+  if (units > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
+  const int grid = (int)(units < sms ? units : sms);
+  attn_persist_kernel<TF32><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tmQ, tmK, tmV, tmVd, p);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_attention_persist(const AttnParams& p, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                                      const CUtensorMap& tmV, const CUtensorMap& tmVd, cudaStream_t stream) {
-  using C = CfgP;
-  static bool configured[128] = {};
-  static int sms[128] = {};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
-    e = cudaFuncSetAttribute(attn_persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
-  }
-  if (p.split_units > 0) return cudaErrorInvalidValue;   // the tail split is for two-tile kernels
-  const long long units = (long long)p.B * p.Hq * p.q_blocks;
-  if (units <= 0) return cudaSuccess;
-  if (units > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
-  const int grid = (int)(units < sms[dev] ? units : sms[dev]);
-  attn_persist_kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tmQ, tmK, tmV, tmVd, p);
-  return cudaGetLastError();
+  return launch_persist_t<false>(p, tmQ, tmK, tmV, tmVd, stream);
+}
+
+cudaError_t launch_attention_tf32(const AttnParams& p, const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                                  const CUtensorMap& tmV, cudaStream_t stream) {
+  return launch_persist_t<true>(p, tmQ, tmK, tmV, tmV, stream);
 }
 
 }  // namespace nsa

@@ -68,13 +68,7 @@ void launch_a(const GluParams& p, dim3 grid, cudaStream_t stream) {
 
 cudaError_t launch_glu(const GluParams& p, cudaStream_t stream) {
   if (p.rows <= 0) return cudaSuccess;
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
+  const int sms = device_sm_count();
   const int64_t n = (int64_t)p.rows * (p.vec ? p.I / 4 : p.I);
   const int64_t want = (n + kGluThreads - 1) / kGluThreads;
   const dim3 grid((unsigned)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8));   // grid-stride beyond 8 waves

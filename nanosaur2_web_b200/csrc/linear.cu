@@ -222,19 +222,18 @@ __global__ void __launch_bounds__(kLinThreads, 1)
 }  // namespace
 
 cudaError_t launch_linear(const LinearParams& p, const CUtensorMap& tmA, const CUtensorMap& tmW, cudaStream_t stream) {
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
+  const int sms = device_sm_count();
   const long long tiles = (long long)p.m_tiles * p.n_tiles;
   if (tiles <= 0) return cudaSuccess;
   if (tiles > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   const size_t smem = 1024 + (size_t)kLinStages * kLinStage + 2 * (size_t)p.n_tiles * kLinNT * 4 + 256;
   if (smem > 232448) return cudaErrorNotSupported;
-  cudaError_t e = cudaFuncSetAttribute(linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // the limit is raised once per device to the whole 227 KB, so launches of different sizes from
+  // several host threads never race on the attribute
+  static DeviceOnce once;
+  cudaError_t e = once_per_device(once, [] {
+    return cudaFuncSetAttribute(linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+  });
   if (e != cudaSuccess) return e;
   const int grid = tiles < sms ? (int)tiles : sms;
   linear_kernel<<<grid, kLinThreads, smem, stream>>>(tmA, tmW, p);

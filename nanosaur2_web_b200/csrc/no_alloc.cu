@@ -10,12 +10,15 @@
 // path calls cudaMalloc, cudaFree or any allocating routine.
 //
 // The array is kNoAllocScratchBytes (64 MiB) of device memory.  Every GPU that loads this part of
-// the library holds it until the process exits.  All calls on a device share it, and it keeps what
+// the library holds it until the process exits.  It is reserved when the module is loaded on a
+// device: with CUDA's default lazy loading that is this entry point's first call on that device (a
+// device allocation the driver makes, which can synchronise the device), with
+// CUDA_MODULE_LOADING=EAGER it is when the library is loaded.  A caller that must avoid that
+// allocation on its hot path makes one call at start-up, before any stream capture.  All calls on a device share it, and it keeps what
 // the previous call left: the prologue rewrites every byte the attention kernel later reads (zero
 // rows included), so nothing has to be cleared between calls.  Two calls whose work overlaps on the
 // GPU (different streams, or different host threads on the same device) race on the array; callers
 // must order them, e.g. by issuing them on one stream.
-#include <mutex>
 #include <string>
 
 #include "nsa_internal.h"
@@ -30,27 +33,20 @@ constexpr size_t kNoAllocScratchBytes = NSA_NOALLOC_SCRATCH_BYTES;
 // with cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Device address of the array on each device, resolved once per device with that device current.
+// Device address of the array on the current device, looked up with that device current.  It is
+// resolved at every call instead of cached: after a cudaDeviceReset, or anything else that unloads
+// and reloads the module, a cached address would point at freed memory, and the lookup is cheap.
+// The first lookup on a device loads this file's module there (CUDA loads modules lazily by
+// default), which is when the array is reserved.
 void* scratch_address(nsa_status* st) {
-  static std::mutex mu;
-  static void* addr[128] = {};
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) {
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr) {
     *st = NSA_ERR_CUDA;
     return nullptr;
   }
-  std::lock_guard<std::mutex> lk(mu);
-  if (!addr[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      *st = NSA_ERR_CUDA;
-      return nullptr;
-    }
-    addr[dev] = p;
-  }
   *st = NSA_OK;
-  return addr[dev];
+  return p;
 }
 
 }  // namespace

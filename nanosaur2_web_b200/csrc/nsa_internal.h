@@ -66,6 +66,9 @@ struct PrologueParams {
   // peer_off[i] bytes (another GPU's buffer mapped into this process; sequence shards).
   int n_peers;
   int64_t peer_off[kMaxPeers];
+  // 1: the tiles are fp32 (the tf32 path; TileOut::ptr then points at floats and its strides count
+  // floats); 0: bf16
+  int out_f32;
 };
 
 struct AttnParams {
@@ -99,7 +102,7 @@ struct AttnParams {
   int split_first, split_units;
   float* part_o;         // [split_units][2][2 * 128][D]
   float* part_ml;        // [split_units][2][2 * 128][2]
-  int* split_count;      // [split_units], zero at launch (the prologue clears it)
+  int* split_count;      // [split_units][2] (one per query tile), zero at launch (the prologue clears it)
   // V straight from the input (tmVd) for key tiles that hold only valid keys: box (x, y) with
   // x = vd_x0 + h*vd_xh + c*blk (h = local kv head), y = b*vd_yb + key (b = global batch index);
   // other tiles come from the prologue's V tiles (tmV).
@@ -116,11 +119,27 @@ struct AttnGeometry {
   int BN;       // keys per K/V tile (TMA box rows)
   int blk;      // swizzle block width in elements (TMA box columns)
   bool qtmem;   // Q copied into tensor memory by the softmax threads (S = Q K^T reads it from there)
+  int v_rows;   // rows of the V tiles' TMA box (BN, or the 32-key chunks of head dim 512)
+  bool v_direct_ok;   // the kernel can read V straight from the input rows
 };
 AttnGeometry attention_geometry(int D);   // NQ = 0: unsupported head dim
+// head dim 512 (attention_d512.cu): two CTAs per 128-row query tile, one per half of the output
+// columns; no V-from-input path and no tail split
+cudaError_t launch_attention_d512(const AttnParams& p, const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                                  const CUtensorMap& tmV, cudaStream_t stream);
+int attention_d512_v_box_rows();
 // persistent head-dim-256 kernel (attention_persist.cu): one CTA per SM looping over work units
 cudaError_t launch_attention_persist(const AttnParams& p, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                                      const CUtensorMap& tmV, const CUtensorMap& tmVd, cudaStream_t stream);
+// the same persistent kernel at head dim 96 on fp32 Q' / K' / V' tiles with tf32 MMAs (the fp32 path
+// whose tolerance is tighter than bf16); maps are fp32 boxes of [rows][32] with the 128-byte swizzle
+cudaError_t launch_attention_tf32(const AttnParams& p, const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                                  const CUtensorMap& tmV, cudaStream_t stream);
+
+// persistent two-query-tile kernel for head dims 64 and 96 (attention_persist2.cu): one CTA per SM
+// looping over work items (units, and the halves of the split tail's units)
+cudaError_t launch_attention_persist2(const AttnParams& p, int D, const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                                      const CUtensorMap& tmV, const CUtensorMap& tmVd, cudaStream_t stream);
 
 cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream);
 
@@ -225,6 +244,15 @@ cudaError_t launch_rope2d_table(int h, int w, int D, float* out, cudaStream_t st
 cudaError_t launch_rope1d_table(int L, int D, float theta, float* out, cudaStream_t stream);
 
 int* device_error_word();   // address of the library's device error word on the current device
+// SM count of the current device (cached per device; safe to call from several host threads).
+int device_sm_count();
+// First-launch set-up of a kernel on the current device (shared-memory attribute, register check):
+// `setup` runs at most once per device and per `state`, under a lock, so host threads that launch
+// concurrently never race on it; a failed set-up is retried at the next launch.
+struct DeviceOnce {
+  bool done[128] = {};
+};
+cudaError_t once_per_device(DeviceOnce& state, cudaError_t (*setup)());
 void record_error(const std::string& msg);   // sets the calling thread's nsa_last_error() message
 
 }  // namespace nsa

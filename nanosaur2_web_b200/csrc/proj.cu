@@ -440,13 +440,7 @@ template <int D>
 cudaError_t launch_proj_d(ProjParams p, const CUtensorMap* tmX, const CUtensorMap* tmW, const CUtensorMap* tmCS,
                           cudaStream_t stream) {
   using C = ProjCfg<D>;
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
+  const int sms = device_sm_count();
   long long tiles = 0;
   size_t bias_bytes = 0;
   for (int s = 0; s < p.n_sets; ++s) {
@@ -468,7 +462,12 @@ cudaError_t launch_proj_d(ProjParams p, const CUtensorMap* tmX, const CUtensorMa
   if (stages < 2) return cudaErrorNotSupported;
   p.stages = stages;
   const size_t smem = fixed + (size_t)stages * C::STAGE;
-  cudaError_t e = cudaFuncSetAttribute(proj_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // the limit is raised once per device to the whole 227 KB, so launches of different sizes from
+  // several host threads never race on the attribute
+  static DeviceOnce once;
+  cudaError_t e = once_per_device(once, [] {
+    return cudaFuncSetAttribute(proj_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+  });
   if (e != cudaSuccess) return e;
   const int grid = tiles < sms ? (int)tiles : sms;
   proj_kernel<D><<<grid, kProjThreads, smem, stream>>>(tmX[0], tmW[0], tmX[p.n_sets > 1 ? 1 : 0],

@@ -82,6 +82,9 @@ __global__ void __launch_bounds__(kPrologueThreads) prologue_kernel(const Prolog
         ss = warp_sum(ss);
         r = rsqrtf(ss / (float)D + p.eps);
       }
+      float* yf = p.out_f32 ? reinterpret_cast<float*>(dst.ptr) + (int64_t)bl * dst.bs + (int64_t)(h0 + hh) * dst.hs +
+                                  (int64_t)r_out * dst.rs
+                            : nullptr;
       for (int i = lane; i < half; i += 32) {
         float y1 = x[i], y2 = x[i + half];
         if (w) {
@@ -96,11 +99,26 @@ __global__ void __launch_bounds__(kPrologueThreads) prologue_kernel(const Prolog
           y1 = t1;
           y2 = t2;
         }
-        y[i] = __float2bfloat16(y1);
-        y[i + half] = __float2bfloat16(y2);
+        if (yf) {   // fp32 tiles (the tf32 path): written straight from the lanes, coalesced
+          yf[i] = y1;
+          yf[i + half] = y2;
+        } else {
+          y[i] = __float2bfloat16(y1);
+          y[i + half] = __float2bfloat16(y2);
+        }
       }
     }
     __syncthreads();
+    if (p.out_f32) {
+      if (!valid) {   // zero rows (padding, masked keys) as fp32
+        for (int e = threadIdx.x; e < hn * D; e += blockDim.x) {
+          const int hh = e / D, d = e % D;
+          reinterpret_cast<float*>(dst.ptr)[(int64_t)bl * dst.bs + (int64_t)(h0 + hh) * dst.hs + (int64_t)r_out * dst.rs + d] = 0.f;
+        }
+      }
+      __syncthreads();
+      continue;
+    }
     // 16-byte stores: head hh of the produced row occupies D contiguous bf16 at its destination.
     const int chunks_per_head = D / 8;
     for (int c = threadIdx.x; c < hn * chunks_per_head; c += blockDim.x) {
@@ -538,7 +556,7 @@ cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream) {
   const int elem = p.src_f32 ? 4 : 2;
   // Rows that also go to other GPUs take the row-per-block kernel: its consecutive threads write
   // each row's head segments contiguously, which NVLink stores need to run at speed.
-  if (p.n_peers == 0 && (p.D == 64 || p.D == 96 || p.D == 128 || p.D == 256) && vec_ok(p, elem))
+  if (p.n_peers == 0 && !p.out_f32 && (p.D == 64 || p.D == 96 || p.D == 128 || p.D == 256) && vec_ok(p, elem))
     return p.src_f32 ? launch_vec_t<float>(p, stream) : launch_vec_t<__nv_bfloat16>(p, stream);
   dim3 grid(rows, p.B, p.skip_q ? 2 : 3);
   prologue_kernel<<<grid, kPrologueThreads, 0, stream>>>(p);

@@ -81,6 +81,25 @@ __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, vol
   }
 }
 
+// The same bounded wait for roles that are far ahead of their consumers (a table builder working
+// an item in advance): between polls the thread sleeps `sleep_ns`, so its spinning does not take
+// issue slots from the warps that share its SM sub-partition.
+__device__ __forceinline__ bool wait_bounded_lazy(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                  int* err_word, int code, uint64_t timeout_ns, uint32_t sleep_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    __nanosleep(sleep_ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      *abort_flag = 1;
+      if (err_word) atomicCAS(err_word, 0, code);
+      return false;
+    }
+  }
+}
+
 // Wait used while tearing down after an abort: ignores the abort flag, only the time limit.
 __device__ __forceinline__ void wait_drain(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer_ns();
@@ -171,6 +190,26 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       : "memory");
 }
 
+// The same two forms with kind::tf32: fp32 operands multiplied at tf32 precision, fp32 accumulate.
+__device__ __forceinline__ void mma_ss_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_tf32(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor (sm_100 format): start address, leading / stride byte offsets
 // (16-byte units), version 1 at bits 46-47, swizzle mode at bits 61-63
 // (0 none, 2 = 128-byte, 4 = 64-byte, 6 = 32-byte swizzle).
@@ -195,6 +234,15 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn, in
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+
+// Instruction descriptor for kind::tf32 (A and B format code 2) with an fp32 accumulator.
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N, int a_mn, int b_mn) {
+  return (1u << 4)      // D format: f32
+         | (2u << 7)    // A format: tf32
+         | (2u << 10)   // B format: tf32
+         | (static_cast<uint32_t>(a_mn) << 15) | (static_cast<uint32_t>(b_mn) << 16) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
 
 // Per-warpgroup register reallocation; every warp of the warpgroup executes it.
 template <int N>

@@ -200,12 +200,14 @@ def attention(*, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, Lq: int, Lk:
               ldq: int, ldk: int, ldv: int, qOff: int = 0, kOff: int = 0, vOff: int = 0, group: int = 1,
               causal: bool = False, bias: Optional[torch.Tensor] = None, biasStart: int = 0,
               out: Optional[torch.Tensor] = None, window: int = 0, kv_len: Optional[torch.Tensor] = None,
-              out_dtype: Optional[torch.dtype] = None, scale: float = 0.0, shard=None) -> torch.Tensor:
+              out_dtype: Optional[torch.dtype] = None, scale: float = 0.0, shard=None,
+              tf32: bool = False) -> torch.Tensor:
     """Multi-head attention (app/gpu/ops.js:194-242).
 
     q: [Lq, ldq] (or [B, Lq, ldq]) with head h at column qOff + h*D; k, v: [Lk, ldk] / [Lk, ldv] with kv
     head h // group at kOff / vOff + (h // group) * D; bias: [biasLen] (or [B, biasLen]) additive
     score bias for keys biasStart..; out: [Lq, H*D] (or [B, Lq, H*D]), allocated when not given.
+    ``tf32`` (fp32 q/k/v at head dim 96): multiply at tf32 precision instead of rounding to bf16.
     """
     _require_cuda(q, k, v, bias, out, kv_len)
     B = q.shape[0] if q.dim() == 3 else 1
@@ -234,6 +236,7 @@ def attention(*, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, Lq: int, Lk:
     d.oOff = 0
     d.in_dtype, d.out_dtype = dtype_code(q), dtype_code(out)
     d.scale = scale
+    d.compute = _lib.NSA_COMPUTE_TF32 if tf32 else _lib.NSA_COMPUTE_BF16
     if shard is not None:
         d.b_begin, d.b_count, d.h_begin, d.h_count = shard
     L = lib()

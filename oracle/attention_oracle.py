@@ -290,24 +290,27 @@ def gemma_attention_sublayer(x, in_w, w_q, w_k, w_v, q_w, k_w, w_o, post_w, thet
 # ----------------------------------------------------------------------------- batched helpers
 
 def joint_attention_batched(qkv, L, Lt, kv_len, q_w, k_w, cos, sin, bias=None, H=DIT_HEADS,
-                            D=DIT_HEAD_DIM, eps=1e-6, acc=np.float32, heads=None):
+                            D=DIT_HEAD_DIM, eps=1e-6, acc=np.float32, heads=None, rows=None):
     """Batched form of ``dit_joint_attention`` on the packed buffer the CUDA path takes:
     qkv [B, L + Lt, 3*H*D] with rows [0, L) image q|k|v and rows [L, L+Lt) text k|v (q unused);
     kv_len[b] = L + valid text rows; bias [B, Lt] on the text keys.  ``heads`` restricts the
-    computation to a subset of heads (the output keeps zeros elsewhere).  Returns [B, L, H*D]."""
+    computation to a subset of heads (the output keeps zeros elsewhere).  ``rows`` (an index array
+    into [0, L)) restricts it to those query rows, every key still taking part: the result is then
+    [B, len(rows), H*D], row i being query rows[i].  Returns [B, L, H*D] otherwise."""
     qkv = np.asarray(qkv)
     B = qkv.shape[0]
     C = H * D
-    out = np.zeros((B, L, C), dtype=acc)
+    qi = np.arange(L) if rows is None else np.asarray(rows, np.int64)
+    out = np.zeros((B, qi.size, C), dtype=acc)
     hs = list(range(H)) if heads is None else list(heads)
     for b in range(B):
         n = int(kv_len[b])
-        rows = qkv[b].astype(acc)
-        q = rows[:L, 0:C]
-        k_img = rows[:L, C:2 * C]
-        v_all = rows[:n, 2 * C:3 * C]
-        k_txt = rows[L:n, C:2 * C]
-        qn = head_norm(q, q_w, H, D, cos, sin, eps, acc)
+        x = qkv[b]
+        q = x[qi, 0:C].astype(acc)
+        k_img = x[:L, C:2 * C].astype(acc)
+        v_all = x[:n, 2 * C:3 * C].astype(acc)
+        k_txt = x[L:n, C:2 * C].astype(acc)
+        qn = head_norm(q, q_w, H, D, cos[qi], sin[qi], eps, acc)
         kn = head_norm(k_img, k_w, H, D, cos, sin, eps, acc)
         if n > L:
             kn = np.concatenate([kn, head_norm(k_txt, k_w, H, D, None, None, eps, acc)])

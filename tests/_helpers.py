@@ -12,9 +12,12 @@ BF16_MIN_COS = 0.9999
 
 def bf16_round(x: np.ndarray) -> np.ndarray:
     """Round float32 values to the nearest bfloat16 (ties to even), returned as float32."""
-    a = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    rounded = ((a + 0x7FFF + ((a >> 16) & 1)) >> 16) << 16
-    return rounded.astype(np.uint32).view(np.float32).reshape(np.shape(x))
+    # uint32 arithmetic cannot overflow for finite values or infinities (the largest pattern,
+    # 0xFF800000, plus 0x8000 stays below 2^32)
+    a = np.array(x, dtype=np.float32, copy=True).view(np.uint32)
+    a += np.uint32(0x7FFF) + ((a >> np.uint32(16)) & np.uint32(1))
+    a &= np.uint32(0xFFFF0000)
+    return a.view(np.float32).reshape(np.shape(x))
 
 
 def per_head_cosine(a: np.ndarray, b: np.ndarray, D: int) -> np.ndarray:

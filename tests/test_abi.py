@@ -100,7 +100,7 @@ def _split_scratch(units, D, nq=2):
     u = min(units, 74)
     up = lambda x: (x + 255) // 256 * 256
     rows = u * 2 * nq * 128
-    return up(rows * D * 4) + up(rows * 2 * 4) + up(u * 4)
+    return up(rows * D * 4) + up(rows * 2 * 4) + up(u * 2 * 4)   # two hand-off counters (query tiles) per unit
 
 
 def test_workspace_sizes():
@@ -302,3 +302,35 @@ int main(void) {
     res = subprocess.run([str(exe)], capture_output=True, text=True)
     assert res.returncode == 0, res.stdout + res.stderr
     assert res.stdout.count("ok ") == 6
+
+
+def _node_api_include():
+    """Directory holding node_api.h (NODE_API_INCLUDE, the usual install prefixes, node-gyp's cache)."""
+    cands = [os.environ.get("NODE_API_INCLUDE", ""), "/usr/include/node", "/usr/local/include/node"]
+    gyp = os.path.expanduser("~/.cache/node-gyp")
+    if os.path.isdir(gyp):
+        cands += [os.path.join(gyp, v, "include", "node") for v in sorted(os.listdir(gyp))]
+    for c in cands:
+        if c and os.path.exists(os.path.join(c, "node_api.h")):
+            return c
+    return None
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None or _node_api_include() is None,
+                    reason="node_api.h is not installed here (no Node.js toolchain): the addon cannot be compiled")
+def test_napi_addon_compiles(tmp_path):
+    """The N-API addon (nanosaur2_web_b200/napi/nsattn_addon.c) compiles against node_api.h and the
+    library header, as node-gyp would build it."""
+    src = os.path.join(ROOT, "nanosaur2_web_b200", "napi", "nsattn_addon.c")
+    res = subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-fPIC", "-c", "-I", os.path.join(ROOT, "include"),
+                          "-I", _node_api_include(), "-DNODE_GYP_MODULE_NAME=nsattn_addon", src, "-o",
+                          str(tmp_path / "addon.o")], capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+
+
+def test_napi_addon_calls_only_declared_entry_points():
+    """Every nsa_* function the addon calls is declared in include/nsattn.h (and so exported)."""
+    src = open(os.path.join(ROOT, "nanosaur2_web_b200", "napi", "nsattn_addon.c")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    called = set(re.findall(r"\b(nsa_[a-z0-9_]+)\s*\(", src))
+    assert called and called <= set(declared_functions())

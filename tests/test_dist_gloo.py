@@ -123,3 +123,72 @@ def test_two_rank_sequence_shard_gather_assembles_all_keys():
         assert p.exitcode == 0
     for rank, err in results:
         assert err == 0.0, (rank, err)
+
+
+def _gate_worker(rank, world, port, leave_after, q):
+    """Ranks step through a StepGate; rank world-1 leaves between steps after ``leave_after`` steps
+    (no collective in flight).  The others must see PeerTimeout at the next step's gate, naming it,
+    before any collective of that step, and then abort the process group."""
+    import torch
+    import torch.distributed as dist
+
+    from nanosaur2_web_b200 import health
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    health.init_process_group_bounded("gloo", rank, world, timeout_s=20)
+    gate = health.StepGate(health.default_store(), rank, world, timeout_s=1.5)
+    steps_done, result = 0, None
+    try:
+        for step in range(4):
+            if rank == world - 1 and step == leave_after:
+                result = ("left", step)
+                break
+            gate.enter(step)
+            t = torch.tensor([float(rank)])
+            dist.all_reduce(t)   # the step's collective: only reached when every rank is present
+            assert t.item() == sum(range(world))
+            steps_done += 1
+        else:
+            result = ("done", steps_done)
+    except health.PeerTimeout as e:
+        result = ("timeout", e.step, e.missing, steps_done)
+    if result[0] == "left":
+        q.put((rank, result))
+        q.close()
+        q.join_thread()   # the result must reach the parent before the hard exit
+        os._exit(0)   # leave without a goodbye, as a crashed rank would
+    health.abort_process_group()
+    q.put((rank, result))
+
+
+@pytest.mark.timeout(120)
+def test_step_gate_detects_a_rank_that_left():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world = 3
+    procs = [ctx.Process(target=_gate_worker, args=(r, world, port, 2, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=100) for _ in procs)
+    for p in procs:
+        p.join(timeout=30)
+        assert p.exitcode == 0
+    assert results[2] == ("left", 2)
+    for r in (0, 1):
+        assert results[r] == ("timeout", 2, [2], 2), results[r]
+
+
+@pytest.mark.timeout(120)
+def test_step_gate_passes_when_every_rank_arrives():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gate_worker, args=(r, 2, port, 99, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=100) for _ in procs)
+    for p in procs:
+        p.join(timeout=30)
+        assert p.exitcode == 0
+    assert results == {0: ("done", 4), 1: ("done", 4)}

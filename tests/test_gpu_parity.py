@@ -352,3 +352,65 @@ def test_reference_call_shape_fp32():
     want = O.attention(qkv[:L, :1536], qkv[:, 1536:3072], qkv[:, 3072:], 16, 96,
                        bias=np.concatenate([np.zeros(L, np.float32), bias]), acc=np.float64)
     assert_close_bf16(out.cpu().numpy(), want, 96, what="reference call shape")
+
+
+# ----------------------------------------------------------------------------- tf32 path
+
+TF32_MAX_ABS, TF32_MIN_COS = 2.5e-3, 0.999999   # tighter than the bf16 bound (2e-2, 0.9999)
+
+
+def test_config1_tf32_fp32_inputs():
+    """BASELINE config 1 (48x48 + 128 text slots, fp32) through the tf32 path (NSA_COMPUTE_TF32): fp32
+    prepared q/k/v, tf32 tensor-core products, against the fp64 oracle at a tolerance tighter than the
+    bf16 path's: max-abs <= 2.5e-3 and per-head cosine >= 0.999999."""
+    from nanosaur2_web_b200.blocks import dit_block_attention
+    from nanosaur2_web_b200.ops import rope2dTable
+    h = w = 48
+    qkv, q_w, k_w, lv, bias = joint_inputs(11, 1, h, w, 128, (20, 128), bf16=False)
+    L = h * w
+    cs = rope2dTable(h, w, 96, DEV)
+    out = dit_block_attention(t(qkv), L=L, text_rows=128, q_norm=t(q_w), k_norm=t(k_w), cs=cs,
+                              kv_len=t((L + lv).astype(np.int32), torch.int32), bias=t(bias), out_dtype=torch.float32,
+                              tf32=True)
+    check_device()
+    heads = list(range(16))
+    want = _oracle_joint(qkv, L, 128, q_w, k_w, lv, bias, h, w, heads)
+    got = out.cpu().numpy()
+    assert_close_bf16(got, want, 96, max_abs=TF32_MAX_ABS, min_cos=TF32_MIN_COS, what="config 1 tf32")
+    # and it is really the tighter path: the bf16 path's error on the same inputs is several times larger
+    out16 = dit_block_attention(t(qkv), L=L, text_rows=128, q_norm=t(q_w), k_norm=t(k_w), cs=cs,
+                                kv_len=t((L + lv).astype(np.int32), torch.int32), bias=t(bias),
+                                out_dtype=torch.float32)
+    check_device()
+    err32 = float(np.max(np.abs(got - want)))
+    err16 = float(np.max(np.abs(out16.cpu().numpy() - want)))
+    assert err32 * 3 < err16, (err32, err16)
+
+
+@pytest.mark.parametrize("L,Lk,causal", [(300, 317, False), (100, 100, True), (129, 1000, False)])
+def test_generic_attention_tf32(L, Lk, causal):
+    """ops.attention with tf32=True on fp32 rows: ragged tiles, a causal mask, more keys than queries."""
+    from nanosaur2_web_b200.ops import attention
+    rng = np.random.default_rng(L + Lk)
+    H, D = 3, 96
+    q = rng.standard_normal((L, H * D), dtype=np.float32)
+    kv = rng.standard_normal((Lk, 2 * H * D), dtype=np.float32)
+    out = attention(q=t(q), k=t(kv), v=t(kv), Lq=L, Lk=Lk, H=H, D=D, ldq=H * D, ldk=2 * H * D, ldv=2 * H * D,
+                    kOff=0, vOff=H * D, causal=causal, tf32=True)
+    check_device()
+    want = O.attention(q, kv[:, : H * D], kv[:, H * D:], H, D, causal=causal, acc=np.float64)
+    assert_close_bf16(out.cpu().numpy(), want, D, max_abs=TF32_MAX_ABS, min_cos=TF32_MIN_COS,
+                      what=f"tf32 L={L} Lk={Lk} causal={causal}")
+
+
+def test_tf32_rejects_other_shapes():
+    from nanosaur2_web_b200 import _lib
+    from nanosaur2_web_b200.ops import attention
+    q = torch.zeros(8, 64, device=DEV)
+    with pytest.raises(_lib.NsaError) as ei:
+        attention(q=q, k=q, v=q, Lq=8, Lk=8, H=1, D=64, ldq=64, ldk=64, ldv=64, tf32=True)
+    assert ei.value.status == _lib.NSA_ERR_UNSUPPORTED
+    q = torch.zeros(8, 96, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(_lib.NsaError) as ei:
+        attention(q=q, k=q, v=q, Lq=8, Lk=8, H=1, D=96, ldq=96, ldk=96, ldv=96, tf32=True)
+    assert ei.value.status == _lib.NSA_ERR_UNSUPPORTED

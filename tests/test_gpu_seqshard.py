@@ -101,15 +101,24 @@ def test_seq_shard_matches_fused_and_oracle(hw, Lt, lv, world, local_qkv):
     assert_close_bf16(got_np[..., cols], want[..., cols], 96, what=f"seq shard {hw} x{world}")
 
 
-def test_seq_shard_config5_size_matches_fused():
-    """Config 5's shapes (128x128 = 16384 image rows + 256 text slots) split over 8 emulated ranks:
-    identical to the single fused call; one batch element keeps the test short."""
+def test_seq_shard_config5_size_matches_fused_and_oracle():
+    """Config 5's shapes (128x128 = 16384 image rows + 256 text slots, batch 2) split over 8 emulated
+    ranks: identical to the single fused call, and both within the bf16 tolerance of the fp64 oracle
+    for all 16 heads on three 128-row query blocks (the first, one in the middle, the last), each
+    against all 16384 + Lv keys (up to 149 key tiles of 112 per query block)."""
     from nanosaur2_web_b200.ops import check_device
     h = w = 128
-    x = _inputs(555, 1, h, w, 256, (32, 256))
-    got = _seq_sharded(x, h, w, 256, 8, True, out_dtype=torch.bfloat16)
-    full = _fused(x, h, w, 256, out_dtype=torch.bfloat16)
+    L, Lt = h * w, 256
+    x = _inputs(555, 2, h, w, Lt, (32, 256))
+    got = _seq_sharded(x, h, w, Lt, 8, True, out_dtype=torch.bfloat16)
+    full = _fused(x, h, w, Lt, out_dtype=torch.bfloat16)
     check_device()
     assert torch.isfinite(got).all()
     assert torch.equal(got, full)
-
+    qkv, q_w, k_w, lvs, bias = x["np"]
+    rows = np.concatenate([np.arange(0, 128), np.arange(8192, 8320), np.arange(L - 128, L)])
+    cos, sin = O.rope_2d(h, w)
+    want = O.joint_attention_batched(qkv, L, Lt, L + lvs, q_w, k_w, cos, sin, bias=bias, acc=np.float64, rows=rows)
+    got_np = got.float().cpu().numpy()
+    for b in range(2):
+        assert_close_bf16(got_np[b, rows], want[b], 96, what=f"config 5, b={b}, 16 heads")

@@ -145,3 +145,23 @@ def test_gemma_mlp_sublayer(golden, layer):
                                      g["post_w"], O.gemma_rope_theta(layer))
     np.testing.assert_allclose(O.gemma_mlp_sublayer(mid, g["pre_ff_w"], g["w_gate"], g["w_up"], g["w_down"],
                                                     g["post_ff_w"]), want, rtol=2e-4, atol=2e-4)
+
+
+def test_torch_restatement_matches_reference_block(golden):
+    """The PyTorch CPU restatement that bench.py times as the CPU baseline (oracle/torch_reference.py)
+    reproduces the reference's own joint block output, and a row-limited sample gives the same rows."""
+    import torch
+
+    from oracle import torch_reference as TR
+    g = golden("dit_joint_block")
+    L, Lt = g["q_raw"].shape[0], g["ky_raw"].shape[0]
+    qkv = np.zeros((L + Lt, 4608), np.float32)
+    qkv[:L, :1536], qkv[:L, 1536:3072], qkv[:L, 3072:] = g["q_raw"], g["k_raw"], g["v"]
+    qkv[L:, 1536:3072], qkv[L:, 3072:] = g["ky_raw"], g["vy"]
+    T = torch.from_numpy
+    out = TR.joint_attention_step(T(qkv), L, L + Lt, T(g["q_w"]), T(g["k_w"]), T(g["cos"]), T(g["sin"]),
+                                  T(g["txt_bias"].astype(np.float32)))
+    np.testing.assert_allclose(out.numpy(), g["out"], rtol=1e-4, atol=1e-5)
+    part = TR.joint_attention_step(T(qkv), L, L + Lt, T(g["q_w"]), T(g["k_w"]), T(g["cos"]), T(g["sin"]),
+                                   T(g["txt_bias"].astype(np.float32)), q_rows=7)
+    np.testing.assert_allclose(part.numpy(), out.numpy()[:7], rtol=1e-5, atol=1e-6)

@@ -4,8 +4,9 @@ Some hosts of this library cannot give it a workspace: their allocator is closed
 must not call cudaMalloc while sharing the GPU with latency-critical work.  For them the fused
 attention step runs on a scratch array built into the library.  This test calls that entry point
 through the C ABI, twice in a row on different shapes (so the second call runs on the scratch the
-first one left behind), and checks each output against the regular workspace entry point within the
-bf16 tolerance the other parity tests use.  It also checks that a shape above the scratch limit is
+first one left behind), and checks each output against the regular workspace entry point: within the
+bf16 tolerance the other parity tests use and, since both run the same kernels on the same inputs,
+bit for bit (the tail split merges its halves in a fixed order, so this holds for split launches too).  It also checks that a shape above the scratch limit is
 refused with NSA_ERR_WORKSPACE and a message, without launching anything.
 
 The file name makes pytest collect it last; it needs nothing from the other tests.
@@ -74,6 +75,9 @@ def test_noalloc_matches_workspace_entry_point_twice():
     ref, na = _both(d, _t(qkv, torch.bfloat16), _t(q_w), _t(k_w), cs.buf, _t((L + lv).astype(np.int32), torch.int32),
                     _t(bias))
     assert_close_bf16(na, ref, 96, what="no-alloc call 1 (DiT joint)")
+    # the same kernels on the same inputs: the outputs must be identical, bit for bit (a stale row
+    # of the previous call's scratch would show up here)
+    np.testing.assert_array_equal(na, ref)
     # call 2, right after: a causal Gemma layer with a window, on the scratch call 1 left behind
     B, Lg = 2, 384
     qkv2, q_w2, k_w2 = gemma_inputs(2025, B, Lg)
@@ -81,6 +85,7 @@ def test_noalloc_matches_workspace_entry_point_twice():
     d2 = _desc(B, Lg, Lg, 4, 1, 256, 1536, (0, 1024, 1280), causal=1, window=200, sin_off=cs2.sinOff)
     ref2, na2 = _both(d2, _t(qkv2, torch.bfloat16), _t(q_w2), _t(k_w2), cs2.buf, None, None)
     assert_close_bf16(na2, ref2, 256, what="no-alloc call 2 (Gemma)")
+    np.testing.assert_array_equal(na2, ref2)
 
 
 def test_noalloc_rejects_shapes_above_the_scratch_limit():
