@@ -456,9 +456,14 @@ def _kernel_stats(step, steps):
     return out
 
 
-def _roofline(kstats, kernel):
-    launches, ms, flops, _ = kstats["attention"]
+def _roofline(kstats, kernel, name="attention", peak_scale=1.0, peak_note=None):
+    """Roofline of the library profiler's kernel ``name``: its algorithmic TFLOP/s against the measured
+    dense bf16 peak times ``peak_scale`` (0.5 for tf32, whose dense rate is half of bf16's)."""
+    launches, ms, flops, _ = kstats[name]
     peak, src = measured_peak()
+    peak *= peak_scale
+    if peak_note:
+        src = f"{src}; {peak_note}"
     achieved = flops / (ms * 1e-3) / 1e12
     pro = kstats.get("prologue")
     return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
@@ -466,10 +471,10 @@ def _roofline(kstats, kernel):
             "prologue_gbs": (pro[3] / (pro[1] * 1e-3) / 1e9) if pro and pro[1] > 0 else None}
 
 
-def _line(args, world, value, ms, config, roofline, clocks, launches, scaling, **extra):
+def _line(args, world, value, ms, config, roofline, clocks, launches, scaling, dtype="bf16", **extra):
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": scaling,
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config, "roofline": roofline,
+            "vs_baseline": None, "dtype": dtype, "data": "synthetic", "config": config, "roofline": roofline,
             "clocks": clocks, "gpu_launches": launches}
     line.update(extra)
     return line
@@ -580,6 +585,98 @@ def run_config4(args, rank, world, local_rank):
            "flops_note": "valid (unmasked) pairs only: 4*Hq*pairs*256 per element-layer"}
     print(json.dumps(_line(args, world, flops / (ms * 1e-3) / 1e12, ms, cfg, _roofline(kst, "attn_fwd_kernel<256>"),
                            clocks.summary(), 2 * LAYERS * args.steps, "strong")), flush=True)
+
+
+def run_config1(args, rank, world, local_rank):
+    """Config 1: the reference's own CPU-runnable case (48x48 = 2304 image tokens + 128 text slots,
+    valid length ~U[20, 128], batch 1, 16 heads x 96), fp32 inputs as tools/reference.py computes it, on
+    the tf32 path (NSA_COMPUTE_TF32: fp32 prepared q/k/v, tf32 tensor-core products).  A step is one
+    fused call; the bf16 path on the same inputs is timed beside it."""
+    import torch
+
+    from nanosaur2_web_b200.blocks import dit_block_attention
+    from nanosaur2_web_b200.ops import rope2dTable
+    from nanosaur2_web_b200.sharding import sum_over_ranks
+    from tests._helpers import joint_inputs
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    HW, LT1 = 48, 128
+    L = HW * HW
+    sets = [joint_inputs(1100 + 17 * rank + i, 1, HW, HW, LT1, (20, 128), bf16=False) for i in range(3)]
+    x = [torch.from_numpy(s[0]).to(dev) for s in sets]   # three 45 MB fp32 inputs rotate (> L2)
+    kv_len = [torch.from_numpy((L + s[3]).astype(np.int32)).to(dev) for s in sets]
+    bias = [torch.from_numpy(s[4]).to(dev) for s in sets]
+    qn, kn = torch.from_numpy(sets[0][1]).to(dev), torch.from_numpy(sets[0][2]).to(dev)
+    cs = rope2dTable(HW, HW, D, dev)
+    out = torch.empty((1, L, C), dtype=torch.float32, device=dev)
+    flops_of = [4.0 * H * L * (L + int(s[3][0])) * D for s in sets]
+
+    def step_with(tf32):
+        def step(i):
+            j = i % 3
+            dit_block_attention(x[j], L=L, text_rows=LT1, q_norm=qn, k_norm=kn, cs=cs, kv_len=kv_len[j],
+                                bias=bias[j], out=out, tf32=tf32)
+        return step
+
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(local_rank) as clocks:
+        ms = _timed(step_with(True), args.steps, args.warmup, world, stream)
+    ms16 = _timed(step_with(False), args.steps, args.warmup, world, stream)
+    flops = sum(flops_of[i % 3] for i in range(args.steps))
+    flops_all = sum_over_ranks(flops)
+    kst = _kernel_stats(step_with(True), min(args.steps, 20))
+    kst16 = _kernel_stats(step_with(False), min(args.steps, 20))
+    if rank != 0:
+        return
+    cfg = {"workload": "config 1: DiT joint attention, 48x48=2304 image + 128 text slots (valid ~U[20,128]), batch 1, "
+                       "16 heads x 96, fp32 inputs, fused q/k RMSNorm + 2D RoPE, log-weight key bias, tf32 products",
+           "global_batch": world, "seq_len": L + LT1, "parallelism": f"replicas x{world}",
+           "l2": "three 45 MB fp32 inputs rotate (135 MB > 126 MB L2)"}
+    att16 = kst16["attention"]
+    extra = {"bf16_path": {"ms_per_step": ms16 / args.steps, "value": flops_all / (ms16 * 1e-3) / 1e12,
+                           "attention_tflops": att16[2] / (att16[1] * 1e-3) / 1e12}}
+    print(json.dumps(_line(args, world, flops_all / (ms * 1e-3) / 1e12, ms, cfg,
+                           _roofline(kst, "attn_persist_kernel<tf32> (head dim 96)", name="attention_tf32",
+                                     peak_scale=0.5, peak_note="tf32 dense peak taken as half the bf16 figure"),
+                           clocks.summary(), 2 * args.steps, "weak", dtype="tf32", **extra)), flush=True)
+
+
+def run_config10(args, rank, world, local_rank):
+    """The VAE decoder's single-head attention at head dim 512 (app/models/vae.js:77-88;
+    tools/reference.py:352-357) at the 832x1216 latent resolution: 104 x 152 = 15808 pixels attending to
+    each other, q/k/v from the fp32 qkv linear, one call per decode.  A step is one call; each rank runs
+    its own (replicas)."""
+    import torch
+
+    from nanosaur2_web_b200.blocks import vae_attention
+    from nanosaur2_web_b200.sharding import sum_over_ranks
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    HV, WV, CV = 104, 152, 512
+    hw = HV * WV
+    rng = np.random.default_rng(1000 + rank)
+    x = [torch.from_numpy(rng.standard_normal((hw, 3 * CV), dtype=np.float32)).to(dev) for _ in range(2)]
+    out = torch.empty((hw, CV), dtype=torch.float32, device=dev)
+
+    def step(i):
+        vae_attention(x[i % 2], C=CV, out=out)
+
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(local_rank) as clocks:
+        ms = _timed(step, args.steps, args.warmup, world, stream)
+    flops = sum_over_ranks(4.0 * hw * hw * CV * args.steps)
+    kst = _kernel_stats(step, min(args.steps, 5))
+    if rank != 0:
+        return
+    cfg = {"workload": "VAE decoder attention: one head of dim 512 over 104x152=15808 latent pixels (832x1216 image), "
+                       "fp32 q|k|v rows, bf16 tensor cores",
+           "global_batch": world, "seq_len": hw, "parallelism": f"replicas x{world}",
+           "l2": "two 97 MB input sets alternate (> 126 MB L2)",
+           "flops_note": "algorithmic 4*hw*hw*512; the kernel computes S twice (two CTAs per query tile), "
+                         "1.5x these flops on the tensor cores"}
+    print(json.dumps(_line(args, world, flops / (ms * 1e-3) / 1e12, ms, cfg,
+                           _roofline(kst, "attn_d512_kernel"), clocks.summary(), 2 * args.steps, "weak")),
+          flush=True)
 
 
 def run_config5(args, rank, world, local_rank):
@@ -971,11 +1068,12 @@ def main():
     ap.add_argument("--seq-mode", choices=["auto", "nccl", "p2p", "ce"], default="auto",
                     help="config 5: k'|v' exchange by NCCL all-gather, peer stores from the prologue, or "
                          "copy-engine pushes")
-    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5, 6, 7, 8, 9], default=2,
+    ap.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5, 6, 7, 8, 9, 10], default=2,
                     help="BASELINE config to run (2 = the headline line; 3, 4, 5 print their own line; 6 = the "
                          "config-2 block step from the block input, QKV projection fused with the prologue; 7 = "
                          "config 4's Gemma layers from the layer input; 8 = the attention half of config 4's "
-                         "Gemma layers on the residual stream; 9 = the whole Gemma layers)")
+                         "Gemma layers on the residual stream; 9 = the whole Gemma layers; 1 = config 1 on the tf32 "
+                         "path; 10 = the VAE decoder's head-dim-512 attention)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -997,9 +1095,19 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
+    gate = None
+    if world > 1:
+        # every rank must be present before the first collective and before the teardown; a rank that is
+        # gone shows up here as PeerTimeout on the host instead of as a collective that never ends
+        from nanosaur2_web_b200.health import StepGate, default_store
+        gate = StepGate(default_store(), rank, world, timeout_s=60.0, prefix=f"bench_c{args.config}")
+        gate.enter(0)
     try:
-        {2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5, 6: run_config6, 7: run_config7,
+        {1: run_config1, 2: run_ours, 3: run_config3, 4: run_config4, 5: run_config5, 6: run_config6, 7: run_config7,
+         10: run_config10,
          8: run_config8, 9: run_config8}[args.config](args, rank, world, local_rank)
+        if gate is not None:
+            gate.enter(1)
     finally:
         if world > 1:
             dist.destroy_process_group()

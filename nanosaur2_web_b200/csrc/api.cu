@@ -178,14 +178,18 @@ bool encode_rows(CUtensorMap* map, const void* base, int64_t width, int64_t ld, 
 // Map over a head-major tile buffer [rows][D] of bf16 (esize 2) or fp32 (esize 4) elements; boxes of
 // [box_rows rows][blk elements], swizzled by the box row's width (128 or 64 bytes) as the tcgen05
 // descriptors expect.
-bool encode_tiles(CUtensorMap* map, void* base, int D, int64_t rows, int blk, int box_rows, int esize = 2) {
+// atom32: the 128-byte swizzle with 32-byte atoms (MN-major tf32 operands of tcgen05.mma).
+bool encode_tiles(CUtensorMap* map, void* base, int D, int64_t rows, int blk, int box_rows, int esize = 2,
+                  bool atom32 = false) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)D * esize};
   const cuuint32_t box[2] = {(cuuint32_t)blk, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  const CUtensorMapSwizzle sw = blk * esize == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUtensorMapSwizzle sw = atom32                 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                : blk * esize == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                                     : CU_TENSOR_MAP_SWIZZLE_64B;
   const CUtensorMapDataType dt = esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   return fn(map, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -443,7 +447,7 @@ nsa_status run(const Plan& pl, nsa::PrologueParams pp, const CommonArgs& a, cons
   CUtensorMap tq, tk, tv;
   const bool maps_ok = encode_tiles(&tq, Qs, pl.D, (int64_t)pl.Bs * pl.Hqs * pl.Lq_pad, pl.blk, nsa::kTileM, pl.esize);
   if (!maps_ok || !encode_tiles(&tk, Ks, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk, pl.BN, pl.esize) ||
-      !encode_tiles(&tv, Vs, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk, pl.v_rows, pl.esize))
+      !encode_tiles(&tv, Vs, pl.D, (int64_t)pl.Bs * pl.Hkvs * pl.Lk_pad, pl.blk, pl.v_rows, pl.esize, pl.tf32))
     return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed (driver entry point unavailable?)");
   CUtensorMap tvd = tv;
   if (v_direct) {

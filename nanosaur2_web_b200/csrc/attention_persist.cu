@@ -94,8 +94,11 @@ __device__ __forceinline__ void p_issue_pv_half(uint32_t d_tmem, uint32_t p_tmem
 #pragma unroll
   for (int kk = k_begin; kk < k_end; ++kk) {
     // V is MN-major: KMMA keys per k-step, head-dim blocks of BLK elements KBLK_BYTES apart; P takes
-    // 8 TMEM columns per k-step (16 bf16 keys two to a column, or 8 fp32 keys)
-    const uint64_t b = smem_desc(sv + (uint32_t)(kk * C::KMMA * C::ROWB), C::KBLK_BYTES, 8 * C::ROWB, C::SWZ);
+    // 8 TMEM columns per k-step (16 bf16 keys two to a column, or 8 fp32 keys).  An MN-major tf32
+    // operand must use the 128-byte swizzle with 32-byte atoms (layout code 1, 4-row groups 512 bytes
+    // apart), which the V map's CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B writes.
+    const uint64_t b = smem_desc(sv + (uint32_t)(kk * C::KMMA * C::ROWB), C::KBLK_BYTES, TF32 ? 4 * C::ROWB : 8 * C::ROWB,
+                                 TF32 ? 1u : C::SWZ);
     p_mma_ts<TF32>(d_tmem, p_tmem + (uint32_t)(kk * 8), b, C::IDESC_PV, (accumulate || kk > 0) ? 1u : 0u);
   }
 }
@@ -443,8 +446,8 @@ __global__ void __launch_bounds__(CfgP<TF32>::THREADS, 1)
               f2_unpack(f2_fma(f2_pack(x[64 * half + 2 * c], x[64 * half + 2 * c + 1]), sc2, nm2), y0, y1);
               const float a0 = ex2(y0), a1 = ex2(y1);
               ls[c & 3] = f2_add(ls[c & 3], f2_pack(a0, a1));
-              pf[2 * c] = __float_as_uint(a0);
-              pf[2 * c + 1] = __float_as_uint(a1);
+              pf[2 * c] = __float_as_uint(round_tf32(a0));
+              pf[2 * c + 1] = __float_as_uint(round_tf32(a1));
             }
             tmem_st64(s_addr + (uint32_t)(64 * half), pf);
           } else {

@@ -132,7 +132,8 @@ int attention_d512_v_box_rows();
 cudaError_t launch_attention_persist(const AttnParams& p, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                                      const CUtensorMap& tmV, const CUtensorMap& tmVd, cudaStream_t stream);
 // the same persistent kernel at head dim 96 on fp32 Q' / K' / V' tiles with tf32 MMAs (the fp32 path
-// whose tolerance is tighter than bf16); maps are fp32 boxes of [rows][32] with the 128-byte swizzle
+// whose tolerance is tighter than bf16); maps are fp32 boxes of [rows][32] with the 128-byte swizzle,
+// the V map with 32-byte swizzle atoms (an MN-major tf32 operand needs that layout)
 cudaError_t launch_attention_tf32(const AttnParams& p, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                                   const CUtensorMap& tmV, cudaStream_t stream);
 

@@ -5,6 +5,7 @@
 //   * the in-place per-head norm (+RoPE) that mirrors ops.headNorm (app/gpu/ops.js:131-138);
 //   * the RoPE table builders of app/models/common.js:15-43.
 #include "nsa_internal.h"
+#include "ptx.cuh"
 
 namespace nsa {
 
@@ -99,9 +100,9 @@ __global__ void __launch_bounds__(kPrologueThreads) prologue_kernel(const Prolog
           y1 = t1;
           y2 = t2;
         }
-        if (yf) {   // fp32 tiles (the tf32 path): written straight from the lanes, coalesced
-          yf[i] = y1;
-          yf[i + half] = y2;
+        if (yf) {   // fp32 tiles (the tf32 path), rounded to tf32: written straight from the lanes, coalesced
+          yf[i] = round_tf32(y1);
+          yf[i + half] = round_tf32(y2);
         } else {
           y[i] = __float2bfloat16(y1);
           y[i + half] = __float2bfloat16(y2);
@@ -170,6 +171,9 @@ __global__ void __launch_bounds__(256, NSA_PROLOGUE_MIN_BLOCKS) prologue_vec_ker
   const int valid_rows = part == 0 ? p.Lq : (p.kv_len ? min(p.kv_len[b], p.Lk) : p.Lk);
   const bool valid = in_range && row < valid_rows;
   const bool rope = part < 2 && p.cs != nullptr && row < p.rope_rows;
+  // V rows of key tiles the attention kernel reads straight from the input: nothing to read or
+  // write (V has no norm, so no lane of such a row takes part in a shuffle below)
+  if (part == 2 && p.v_tile > 0 && row < valid_rows / p.v_tile * p.v_tile) return;
 
   float x1[S], x2[S];
 #pragma unroll
@@ -215,7 +219,6 @@ __global__ void __launch_bounds__(256, NSA_PROLOGUE_MIN_BLOCKS) prologue_vec_ker
     r = rsqrtf(ss / (float)D + p.eps);
   }
   if (!in_range) return;
-  if (part == 2 && p.v_tile > 0 && row < valid_rows / p.v_tile * p.v_tile) return;   // read from the input
   if (valid) {
     if (w) {
       const float4* w1 = reinterpret_cast<const float4*>(w + sub * S);
@@ -544,6 +547,7 @@ cudaError_t launch_vec_t(const PrologueParams& p, cudaStream_t stream) {
     case 256:
       if constexpr (sizeof(T) == 2) return launch_stream<256, NSA_PROLOGUE_P256>(p, stream);
       return launch_vec<256, NSA_PROLOGUE_P256, T>(p, stream);
+    case 512: return launch_vec<512, 16, T>(p, stream);   // the VAE's head dim: 16 lanes per head
     default: return cudaErrorNotSupported;
   }
 }
@@ -556,7 +560,8 @@ cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream) {
   const int elem = p.src_f32 ? 4 : 2;
   // Rows that also go to other GPUs take the row-per-block kernel: its consecutive threads write
   // each row's head segments contiguously, which NVLink stores need to run at speed.
-  if (p.n_peers == 0 && !p.out_f32 && (p.D == 64 || p.D == 96 || p.D == 128 || p.D == 256) && vec_ok(p, elem))
+  if (p.n_peers == 0 && !p.out_f32 && (p.D == 64 || p.D == 96 || p.D == 128 || p.D == 256 || p.D == 512) &&
+      vec_ok(p, elem))
     return p.src_f32 ? launch_vec_t<float>(p, stream) : launch_vec_t<__nv_bfloat16>(p, stream);
   dim3 grid(rows, p.B, p.skip_q ? 2 : 3);
   prologue_kernel<<<grid, kPrologueThreads, 0, stream>>>(p);

@@ -310,6 +310,15 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
+// fp32 -> tf32 with round-to-nearest (ties away), kept in a 32-bit register (low 13 bits zero).  The
+// tensor core drops those bits of an fp32 operand when it reads it as tf32; rounding first halves
+// that error.
+__device__ __forceinline__ float round_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

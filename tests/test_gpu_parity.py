@@ -377,14 +377,14 @@ def test_config1_tf32_fp32_inputs():
     want = _oracle_joint(qkv, L, 128, q_w, k_w, lv, bias, h, w, heads)
     got = out.cpu().numpy()
     assert_close_bf16(got, want, 96, max_abs=TF32_MAX_ABS, min_cos=TF32_MIN_COS, what="config 1 tf32")
-    # and it is really the tighter path: the bf16 path's error on the same inputs is several times larger
+    # and it is really the tighter path: the bf16 path's error on the same inputs is at least twice as large
     out16 = dit_block_attention(t(qkv), L=L, text_rows=128, q_norm=t(q_w), k_norm=t(k_w), cs=cs,
                                 kv_len=t((L + lv).astype(np.int32), torch.int32), bias=t(bias),
                                 out_dtype=torch.float32)
     check_device()
     err32 = float(np.max(np.abs(got - want)))
     err16 = float(np.max(np.abs(out16.cpu().numpy() - want)))
-    assert err32 * 3 < err16, (err32, err16)
+    assert err32 * 2 < err16, (err32, err16)
 
 
 @pytest.mark.parametrize("L,Lk,causal", [(300, 317, False), (100, 100, True), (129, 1000, False)])
