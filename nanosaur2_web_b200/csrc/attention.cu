@@ -660,13 +660,9 @@ cudaError_t launch_d(const AttnParams& p, const CUtensorMap& tmQ, const CUtensor
 }  // namespace
 
 // Head dim 256 runs the persistent kernel of attention_persist.cu unless built with
-// NSA_PERSIST_256=0.  Head dims 64 and 96 run the per-unit kernel above; NSA_PERSIST_2TILE=1 selects
-// the persistent kernel of attention_persist2.cu instead (measured slower per key step so far).
+// NSA_PERSIST_256=0.
 #ifndef NSA_PERSIST_256
 #define NSA_PERSIST_256 1
-#endif
-#ifndef NSA_PERSIST_2TILE
-#define NSA_PERSIST_2TILE 0
 #endif
 
 AttnGeometry attention_geometry(int D) {
@@ -683,10 +679,8 @@ AttnGeometry attention_geometry(int D) {
 cudaError_t launch_attention(const AttnParams& p, int D, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                              const CUtensorMap& tmV, const CUtensorMap& tmVd, cudaStream_t stream) {
   switch (D) {
-    case 64: return NSA_PERSIST_2TILE ? launch_attention_persist2(p, 64, tmQ, tmK, tmV, tmVd, stream)
-                                      : launch_d<64>(p, tmQ, tmK, tmV, tmVd, stream);
-    case 96: return NSA_PERSIST_2TILE ? launch_attention_persist2(p, 96, tmQ, tmK, tmV, tmVd, stream)
-                                      : launch_d<96>(p, tmQ, tmK, tmV, tmVd, stream);
+    case 64: return launch_d<64>(p, tmQ, tmK, tmV, tmVd, stream);
+    case 96: return launch_d<96>(p, tmQ, tmK, tmV, tmVd, stream);
     case 128: return launch_d<128>(p, tmQ, tmK, tmV, tmVd, stream);
     case 256: return NSA_PERSIST_256 ? launch_attention_persist(p, tmQ, tmK, tmV, tmVd, stream)
                                      : launch_d<256>(p, tmQ, tmK, tmV, tmVd, stream);

@@ -1,5 +1,5 @@
-// Tile geometry and MMA-issue helpers shared by the two-query-tile attention kernels (the
-// one-CTA-per-unit kernel of attention.cu and the persistent kernel of attention_persist2.cu).
+// Tile geometry and MMA-issue helpers of the per-unit attention kernels (attention.cu): the
+// two-query-tile kernels at head dims 64, 96 and 128 and the one-tile kernel at head dim 256.
 #pragma once
 
 #include "nsa_internal.h"

@@ -137,11 +137,6 @@ cudaError_t launch_attention_persist(const AttnParams& p, const CUtensorMap& tmQ
 cudaError_t launch_attention_tf32(const AttnParams& p, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                                   const CUtensorMap& tmV, cudaStream_t stream);
 
-// persistent two-query-tile kernel for head dims 64 and 96 (attention_persist2.cu): one CTA per SM
-// looping over work items (units, and the halves of the split tail's units)
-cudaError_t launch_attention_persist2(const AttnParams& p, int D, const CUtensorMap& tmQ, const CUtensorMap& tmK,
-                                      const CUtensorMap& tmV, const CUtensorMap& tmVd, cudaStream_t stream);
-
 cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream);
 
 // QKV projection GEMM with the prologue in its epilogue (proj.cu): rows of X [.][K] times W^T

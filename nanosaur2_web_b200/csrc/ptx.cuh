@@ -81,25 +81,6 @@ __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, vol
   }
 }
 
-// The same bounded wait for roles that are far ahead of their consumers (a table builder working
-// an item in advance): between polls the thread sleeps `sleep_ns`, so its spinning does not take
-// issue slots from the warps that share its SM sub-partition.
-__device__ __forceinline__ bool wait_bounded_lazy(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                                  int* err_word, int code, uint64_t timeout_ns, uint32_t sleep_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (;;) {
-    __nanosleep(sleep_ns);
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > timeout_ns) {
-      *abort_flag = 1;
-      if (err_word) atomicCAS(err_word, 0, code);
-      return false;
-    }
-  }
-}
-
 // Wait used while tearing down after an abort: ignores the abort flag, only the time limit.
 __device__ __forceinline__ void wait_drain(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer_ns();
