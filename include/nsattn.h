@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define NSA_ABI_VERSION 2
+#define NSA_ABI_VERSION 3
 
 typedef enum nsa_status {
   NSA_OK = 0,
@@ -265,15 +265,26 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* desc, const nsa_seq_sh
 /* ------------------------------------------------------------------------------------------------
  * nsa_linear: ops.linear(gpu, x, W, {bias, resid, gate, gOff, act, ldc, cOff}) (app/gpu/ops.js:50-66)
  * with the epilogue of the reference's tiled GEMM (app/gpu/gemm.js:155-165):
- *   r = alpha * sum_k A[m][k] W[n][k] (+ bias[n]) (silu when act = 1), then
- *   C[m*ldc + cOff + n] = r, or with resid: C[...] += r, or with resid and a gate: C[...] += gate[gOff + n] * r.
+ *   r = alpha * sum_k A[m][k] W[n][k] (* w_scale[n]) (+ bias[n]) (+ LoRA delta[m][n]) (silu when act = 1),
+ *   then C[m*ldc + cOff + n] = r, or with resid: C[...] += r, or with resid and a gate:
+ *   C[...] += gate[gOff + n] * r.
  * The DiT block's output projection is the gated form (app/models/nanosaur2.js:210). A is bf16
- * [M][lda], W bf16 in the Linear layout [N][K], C fp32 (the reference's residual stream), bias and
- * gate fp32.  K, lda multiples of 8; N, ldc, cOff and gOff multiples of 4; pointers 16-byte aligned.
+ * [M][lda], W in the Linear layout [N][K], C fp32 (the reference's residual stream) or, with
+ * out_dtype NSA_BF16, bf16 (store form only: the next GEMM's operand), bias and gate fp32.
+ * K, lda multiples of 8; N, ldc, cOff and gOff multiples of 4; pointers 16-byte aligned.
  * N <= 4096: the bias and gate vectors are staged whole in shared memory beside the operand ring
  * (wider outputs return NSA_ERR_UNSUPPORTED; split them into column ranges with cOff).
- * (The reference's int8 ConvRot weights and LoRA deltas are not part of this entry.)
+ * Weight formats (the reference's GEMM B formats "bf16" and "i8", gemm.js:9-10):
+ *   NSA_W_BF16  W bf16 [N][K].
+ *   NSA_W_I8    W int8 [N][K] of the ConvRot-quantised model (tools/quant.py:48-57) with the per-row
+ *               fp32 scale w_scale[N] (gemm.js:159); K a multiple of 16.  A must be the rotated input
+ *               (nsa_rotate, ops.rotate: ops.js:34-45, 54), as the reference passes `xr`.
+ * LoRA side paths (ops.js:55-57, 70-86; app/lora.js:143-150): lora_rank R > 0 adds
+ *   delta = sum_i scale_i * B_i (A_i x) over the entries packed by nsa_lora_pack into lora_a [R][K] and
+ *   lora_b [N][R] (bf16).  The call first writes T = A @ lora_a^T into the caller's scratch lora_t
+ *   (bf16 [M][R]), then accumulates T @ lora_b^T in the same tensor-memory accumulator as A @ W^T.
  * ------------------------------------------------------------------------------------------------ */
+typedef enum nsa_weight_format { NSA_W_BF16 = 0, NSA_W_I8 = 1 } nsa_weight_format;
 typedef struct nsa_linear_desc {
   int32_t M, N, K;
   int64_t lda;      /* A row pitch in elements */
@@ -283,9 +294,47 @@ typedef struct nsa_linear_desc {
   float alpha;      /* 0 means 1 */
   int32_t resid;    /* 1: accumulate into C (opts.resid) */
   int32_t act;      /* 0: none, 1: silu (opts.act) */
+  int32_t out_dtype;        /* NSA_F32 (C is float*) or NSA_BF16 (C is bf16, no resid) */
+  int32_t w_format;         /* NSA_W_BF16 or NSA_W_I8 */
+  const float* w_scale;     /* NSA_W_I8: [N] per-row scales */
+  int32_t lora_rank;        /* R, a multiple of 64 (nsa_lora_rank); 0: no LoRA */
+  const void* lora_a;       /* bf16 [R][K] */
+  const void* lora_b;       /* bf16 [N][R] */
+  void* lora_t;             /* bf16 [M][R] scratch written by the call */
 } nsa_linear_desc;
 nsa_status nsa_linear(const nsa_linear_desc* desc, const void* A, const void* W, const float* bias,
-                      const float* gate, float* C, void* stream);
+                      const float* gate, void* C, void* stream);
+
+/* nsa_rotate: ops.rotate(gpu, x) (app/gpu/ops.js:38-45, the hadamard kernel of kernels.js:379-407):
+ * every group of 256 consecutive columns of a row is multiplied by the normalised regular Hadamard
+ * matrix H256 = (H4 (x) H4 (x) H4 (x) H4) / 16 (tools/quant.py:21-30).  X and Y fp32 or bf16 (a bf16 Y
+ * is nsa_linear's A for int8 weights); cols a multiple of 256; row pitches multiples of 8 elements;
+ * pointers 16-byte aligned; X and Y must not overlap. */
+typedef struct nsa_rotate_desc {
+  int32_t rows, cols;
+  int64_t ldx;         /* X row pitch in elements (0: cols) */
+  int64_t ldy;         /* Y row pitch in elements (0: cols) */
+  int32_t in_dtype;    /* NSA_F32 or NSA_BF16 */
+  int32_t out_dtype;   /* NSA_F32 or NSA_BF16 */
+} nsa_rotate_desc;
+nsa_status nsa_rotate(const nsa_rotate_desc* desc, const void* X, void* Y, void* stream);
+
+/* LoRA entries of one linear (app/lora.js:143-150): A [r][K] and B [n][r] fp32 device matrices (for
+ * int8 weights A's rows already rotated, as the reference's loader does, app/lora.js:126), the output
+ * columns [off, off + n) of the linear (the slice of a stacked q|k|v weight) and the scale
+ * strength * alpha / r.  nsa_lora_rank returns R = the ranks' sum rounded up to 64 (0 for none);
+ * nsa_lora_pack writes lora_a [R][K] and lora_b [N][R] for nsa_linear: lora_b's rows are divided by
+ * alpha * w_scale[n] (w_scale NULL for bf16 weights), which the linear's epilogue multiplies back.  A
+ * strength change (or another alpha) is a re-pack; the entries array is host memory. */
+typedef struct nsa_lora_entry {
+  const float* A;
+  const float* B;
+  int32_t r, off, n;
+  float scale;
+} nsa_lora_entry;
+int32_t nsa_lora_rank(const nsa_lora_entry* entries, int32_t count);
+nsa_status nsa_lora_pack(const nsa_lora_entry* entries, int32_t count, int32_t N, int32_t K, const float* w_scale,
+                         float alpha, void* lora_a, void* lora_b, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * nsa_rmsnorm: ops.rmsnorm(gpu, x, weight, cols, eps, out) (app/gpu/ops.js:111-116, kernels.js:62-80)

@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(HERE, "libnsattn.so")
 NSA_OK, NSA_ERR_INVALID_ARGUMENT, NSA_ERR_UNSUPPORTED, NSA_ERR_WORKSPACE, NSA_ERR_CUDA, NSA_ERR_DEVICE = range(6)
 NSA_F32, NSA_BF16 = 0, 1
 NSA_COMPUTE_BF16, NSA_COMPUTE_TF32 = 0, 1
+NSA_W_BF16, NSA_W_I8 = 0, 1
 NSA_IPC_HANDLE_BYTES = 72
 
 _i32, _i64, _f32, _vp, _sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
@@ -67,7 +68,18 @@ class ProjDesc(ctypes.Structure):
 class LinearDesc(ctypes.Structure):
     """nsa_linear_desc (include/nsattn.h)."""
     _fields_ = [("M", _i32), ("N", _i32), ("K", _i32), ("lda", _i64), ("ldc", _i64), ("cOff", _i64), ("gOff", _i64),
-                ("alpha", _f32), ("resid", _i32), ("act", _i32)]
+                ("alpha", _f32), ("resid", _i32), ("act", _i32), ("out_dtype", _i32), ("w_format", _i32),
+                ("w_scale", _vp), ("lora_rank", _i32), ("lora_a", _vp), ("lora_b", _vp), ("lora_t", _vp)]
+
+
+class RotateDesc(ctypes.Structure):
+    """nsa_rotate_desc (include/nsattn.h)."""
+    _fields_ = [("rows", _i32), ("cols", _i32), ("ldx", _i64), ("ldy", _i64), ("in_dtype", _i32), ("out_dtype", _i32)]
+
+
+class LoraEntry(ctypes.Structure):
+    """nsa_lora_entry (include/nsattn.h)."""
+    _fields_ = [("A", _vp), ("B", _vp), ("r", _i32), ("off", _i32), ("n", _i32), ("scale", _f32)]
 
 
 class RmsnormDesc(ctypes.Structure):
@@ -112,6 +124,9 @@ SIGNATURES = {
     "nsa_seq_shard_projection": (_i32, [ctypes.POINTER(FusedDesc), ctypes.POINTER(SeqShard), ctypes.POINTER(ProjDesc),
                                         _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "nsa_linear": (_i32, [ctypes.POINTER(LinearDesc), _vp, _vp, _vp, _vp, _vp, _vp]),
+    "nsa_rotate": (_i32, [ctypes.POINTER(RotateDesc), _vp, _vp, _vp]),
+    "nsa_lora_rank": (_i32, [ctypes.POINTER(LoraEntry), _i32]),
+    "nsa_lora_pack": (_i32, [ctypes.POINTER(LoraEntry), _i32, _i32, _i32, _vp, _f32, _vp, _vp, _vp]),
     "nsa_rmsnorm": (_i32, [ctypes.POINTER(RmsnormDesc), _vp, _vp, _vp, _vp]),
     "nsa_glu": (_i32, [ctypes.POINTER(GluDesc), _vp, _vp, _vp]),
     "nsa_rope2d_table": (_i32, [_i32, _i32, _i32, _vp, _vp]),

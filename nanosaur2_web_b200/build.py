@@ -19,7 +19,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(HERE, "libnsattn.so")
-SOURCES = ["api.cu", "attention.cu", "attention_persist.cu", "attention_d512.cu", "prologue.cu", "no_alloc.cu", "proj.cu", "linear.cu", "rmsnorm.cu", "glu.cu"]
+SOURCES = ["api.cu", "attention.cu", "attention_persist.cu", "attention_d512.cu", "prologue.cu", "no_alloc.cu", "proj.cu", "linear.cu", "rmsnorm.cu", "glu.cu", "rotate.cu", "lora.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -1140,7 +1140,7 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* d, const nsa_seq_shard
 }
 
 nsa_status nsa_linear(const nsa_linear_desc* d, const void* A, const void* W, const float* bias, const float* gate,
-                      float* C, void* stream) {
+                      void* C, void* stream) {
   if (!d) return fail(NSA_ERR_INVALID_ARGUMENT, "desc is NULL");
   if (!A || !W || !C) return fail(NSA_ERR_INVALID_ARGUMENT, "A, W and C must be device pointers");
   if (d->M < 1 || d->N < 1 || d->K < 1) return fail(NSA_ERR_INVALID_ARGUMENT, "M, N and K must be >= 1");
@@ -1149,42 +1149,161 @@ nsa_status nsa_linear(const nsa_linear_desc* d, const void* A, const void* W, co
     return fail(NSA_ERR_INVALID_ARGUMENT, "K and lda must be multiples of 8 with lda >= K");
   if (d->N % 4 || ldc % 4 || d->cOff % 4 || d->gOff % 4 || d->cOff < 0 || d->gOff < 0 || ldc < d->cOff + d->N)
     return fail(NSA_ERR_INVALID_ARGUMENT, "N, ldc, cOff and gOff must be multiples of 4, with ldc >= cOff + N");
+  if (d->out_dtype != NSA_F32 && d->out_dtype != NSA_BF16) return fail(NSA_ERR_INVALID_ARGUMENT, "bad out_dtype");
+  if (d->w_format != NSA_W_BF16 && d->w_format != NSA_W_I8)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "w_format is NSA_W_BF16 or NSA_W_I8");
+  const bool i8 = d->w_format == NSA_W_I8;
   auto a16 = [](const void* ptr) { return ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
-  if (!a16(A) || !a16(W) || !a16(C) || !a16(bias) || !a16(gate))
+  if (!a16(A) || !a16(W) || !a16(C) || !a16(bias) || !a16(gate) || !a16(d->w_scale) || !a16(d->lora_a) ||
+      !a16(d->lora_b) || !a16(d->lora_t))
     return fail(NSA_ERR_INVALID_ARGUMENT, "pointers must be 16-byte aligned");
   if (gate && !d->resid) return fail(NSA_ERR_INVALID_ARGUMENT, "a gate needs resid (C += gate * r)");
+  if (d->out_dtype == NSA_BF16 && d->resid)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "the bf16 output is the store form (no resid)");
   if (d->act != 0 && d->act != 1) return fail(NSA_ERR_INVALID_ARGUMENT, "act is 0 (none) or 1 (silu)");
+  if (i8 && !d->w_scale) return fail(NSA_ERR_INVALID_ARGUMENT, "int8 weights need w_scale[N]");
+  if (i8 && d->K % 16) return fail(NSA_ERR_INVALID_ARGUMENT, "int8 weights need K a multiple of 16");
+  const int R = d->lora_rank;
+  if (R < 0 || R % 64) return fail(NSA_ERR_INVALID_ARGUMENT, "lora_rank must be a multiple of 64 (0: no LoRA)");
+  if (R && (!d->lora_a || !d->lora_b || !d->lora_t))
+    return fail(NSA_ERR_INVALID_ARGUMENT, "a LoRA needs lora_a, lora_b and the lora_t scratch");
+  if (d->out_dtype == NSA_BF16 && (ldc % 8 || d->cOff % 8))
+    return fail(NSA_ERR_INVALID_ARGUMENT, "a bf16 C needs ldc and cOff multiples of 8 (16-byte rows)");
   int* err = nsa::device_error_word();
   if (!err) return fail(NSA_ERR_CUDA, "cannot resolve the device error word on this device");
-  CUtensorMap ta, tw;
-  const cuuint64_t ad[2] = {(cuuint64_t)d->K, (cuuint64_t)d->M};
-  const cuuint64_t as[1] = {(cuuint64_t)d->lda * 2};
-  const cuuint32_t ab[2] = {64, 128};
-  const cuuint64_t wd[2] = {(cuuint64_t)d->K, (cuuint64_t)d->N};
-  const cuuint64_t ws[1] = {(cuuint64_t)d->K * 2};
-  const cuuint32_t wb[2] = {64, 256};
-  if (!encode_sw128(&ta, A, 2, ad, as, ab) || !encode_sw128(&tw, W, 2, wd, ws, wb))
-    return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the linear operands");
-  nsa::LinearParams p{};
-  p.M = d->M;
-  p.N = d->N;
-  p.k_steps = (d->K + 63) / 64;
-  p.m_tiles = (d->M + 127) / 128;
-  p.n_tiles = (d->N + 255) / 256;
-  p.alpha = d->alpha != 0.f ? d->alpha : 1.f;
+  const cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  const float alpha = d->alpha != 0.f ? d->alpha : 1.f;
+  // A [M][K] bf16 and W [N][K] (bf16 swizzled for the MMA, or int8 plain rows for the converters)
+  auto map2d = [](CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esz, int64_t width, int64_t rows,
+                  int64_t ld, uint32_t box_rows, CUtensorMapSwizzle sw, uint32_t box_cols = 64) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)(ld * esz)};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  };
+  const auto BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+  auto base_params = [&](int M, int N, int K) {
+    nsa::LinearParams p{};
+    p.M = M;
+    p.N = N;
+    p.k_steps = (K + 63) / 64;
+    p.m_tiles = (M + 127) / 128;
+    p.n_tiles = (N + 255) / 256;
+    p.alpha = 1.f;
+    p.err = err;
+    p.timeout_ns = wait_timeout_ns();
+    return p;
+  };
+  CUtensorMap ta, tw, tt, tl, tc;
+  if (R) {
+    // T = A @ lora_a^T, bf16 [M][R]: the LoRA's first factor, one small GEMM before the main one
+    CUtensorMap la;
+    if (!map2d(&ta, A, BF, 2, d->K, d->M, d->lda, 128, SW) || !map2d(&la, d->lora_a, BF, 2, d->K, R, d->K, 256, SW) ||
+        !map2d(&tc, d->lora_t, BF, 2, R, d->M, R, 32, SW, 64))
+      return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the LoRA operands");
+    nsa::LinearParams pt = base_params(d->M, R, d->K);
+    pt.C16 = static_cast<__nv_bfloat16*>(d->lora_t);
+    pt.ldc = R;
+    cudaError_t e = profiled("linear_lora_t", 2.0 * d->M * (double)R * d->K, 0.0, strm,
+                             [&] { return nsa::launch_linear(pt, ta, la, ta, la, tc, strm); });
+    if (e != cudaSuccess) return cuda_fail(e, "LoRA factor launch");
+  }
+  bool ok = map2d(&ta, A, BF, 2, d->K, d->M, d->lda, 128, SW) &&
+            (i8 ? map2d(&tw, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, d->K, d->N, d->K, 256, CU_TENSOR_MAP_SWIZZLE_NONE)
+                : map2d(&tw, W, BF, 2, d->K, d->N, d->K, 256, SW));
+  if (ok && R) ok = map2d(&tt, d->lora_t, BF, 2, R, d->M, R, 128, SW) && map2d(&tl, d->lora_b, BF, 2, R, d->N, R, 256, SW);
+  const bool c16 = d->out_dtype == NSA_BF16;
+  if (ok)
+    ok = c16 ? map2d(&tc, static_cast<__nv_bfloat16*>(C) + d->cOff, BF, 2, d->N, d->M, ldc, 32, SW, 64)
+             : map2d(&tc, static_cast<float*>(C) + d->cOff, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d->N, d->M, ldc, 32, SW, 32);
+  if (!ok) return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the linear operands");
+  nsa::LinearParams p = base_params(d->M, d->N, d->K);
+  p.lora_steps = R / 64;
+  p.alpha = alpha;
   p.bias = bias;
   p.gate = gate ? gate + d->gOff : nullptr;
   p.resid = d->resid ? 1 : 0;
   p.act = d->act;
-  p.C = C + d->cOff;
+  p.w_i8 = i8 ? 1 : 0;
+  p.w_scale = d->w_scale;
+  if (d->out_dtype == NSA_BF16)
+    p.C16 = static_cast<__nv_bfloat16*>(C) + d->cOff;
+  else
+    p.C = static_cast<float*>(C) + d->cOff;
   p.ldc = ldc;
-  p.err = err;
-  p.timeout_ns = wait_timeout_ns();
-  const cudaStream_t strm = static_cast<cudaStream_t>(stream);
-  const double flops = 2.0 * d->M * (double)d->N * d->K;
-  cudaError_t e = profiled("linear", flops, 0.0, strm, [&] { return nsa::launch_linear(p, ta, tw, strm); });
-  if (e == cudaErrorNotSupported) return fail(NSA_ERR_UNSUPPORTED, "N too large for the staged bias / gate");
+  const double flops = 2.0 * d->M * (double)d->N * (d->K + R);
+  cudaError_t e = profiled(i8 ? "linear_i8" : "linear", flops, 0.0, strm,
+                           [&] { return nsa::launch_linear(p, ta, tw, R ? tt : ta, R ? tl : tw, tc, strm); });
   if (e != cudaSuccess) return cuda_fail(e, "linear launch");
+  return NSA_OK;
+}
+
+nsa_status nsa_rotate(const nsa_rotate_desc* d, const void* X, void* Y, void* stream) {
+  if (!d) return fail(NSA_ERR_INVALID_ARGUMENT, "desc is NULL");
+  if (d->rows < 0 || d->cols < 256 || d->cols % 256)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "need rows >= 0 and cols a positive multiple of 256");
+  const int64_t ldx = d->ldx ? d->ldx : d->cols, ldy = d->ldy ? d->ldy : d->cols;
+  if (ldx < d->cols || ldy < d->cols || ldx % 8 || ldy % 8)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "ldx and ldy must be multiples of 8 and >= cols");
+  if ((d->in_dtype != NSA_F32 && d->in_dtype != NSA_BF16) || (d->out_dtype != NSA_F32 && d->out_dtype != NSA_BF16))
+    return fail(NSA_ERR_INVALID_ARGUMENT, "bad in_dtype / out_dtype");
+  if (d->rows == 0) return NSA_OK;
+  if (!X || !Y || !aligned16(X) || !aligned16(Y))
+    return fail(NSA_ERR_INVALID_ARGUMENT, "X and Y must be 16-byte aligned device pointers");
+  const int ei = d->in_dtype == NSA_F32 ? 4 : 2, eo = d->out_dtype == NSA_F32 ? 4 : 2;
+  const uintptr_t x0 = reinterpret_cast<uintptr_t>(X), y0 = reinterpret_cast<uintptr_t>(Y);
+  const uintptr_t x1 = x0 + (uintptr_t)(((int64_t)(d->rows - 1) * ldx + d->cols) * ei);
+  const uintptr_t y1 = y0 + (uintptr_t)(((int64_t)(d->rows - 1) * ldy + d->cols) * eo);
+  if (x0 < y1 && y0 < x1) return fail(NSA_ERR_INVALID_ARGUMENT, "X and Y must not overlap");
+  nsa::RotateParams p{};
+  p.rows = d->rows;
+  p.cols = d->cols;
+  p.ldx = ldx;
+  p.ldy = ldy;
+  p.x = X;
+  p.y = Y;
+  p.in_bf16 = d->in_dtype == NSA_BF16;
+  p.out_bf16 = d->out_dtype == NSA_BF16;
+  const cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  cudaError_t e = profiled("rotate", 0.0, (double)d->rows * d->cols * (ei + eo), strm,
+                           [&] { return nsa::launch_rotate(p, strm); });
+  if (e != cudaSuccess) return cuda_fail(e, "rotate launch");
+  return NSA_OK;
+}
+
+int32_t nsa_lora_rank(const nsa_lora_entry* entries, int32_t count) {
+  if (!entries || count <= 0) return 0;
+  int64_t r = 0;
+  for (int i = 0; i < count; ++i) r += entries[i].r > 0 ? entries[i].r : 0;
+  r = (r + 63) / 64 * 64;
+  return r > 0x7FFFFFFF ? -1 : (int32_t)r;
+}
+
+nsa_status nsa_lora_pack(const nsa_lora_entry* entries, int32_t count, int32_t N, int32_t K, const float* w_scale,
+                         float alpha, void* lora_a, void* lora_b, void* stream) {
+  if (count < 0 || (count > 0 && !entries)) return fail(NSA_ERR_INVALID_ARGUMENT, "entries is NULL");
+  if (N < 1 || K < 1) return fail(NSA_ERR_INVALID_ARGUMENT, "N and K must be >= 1");
+  if (!(alpha != 0.f)) alpha = 1.f;
+  std::vector<nsa::LoraPackEntry> pe;
+  for (int i = 0; i < count; ++i) {
+    const nsa_lora_entry& e = entries[i];
+    if (e.r < 1 || e.n < 1 || e.off < 0 || (int64_t)e.off + e.n > N || !e.A || !e.B)
+      return fail(NSA_ERR_INVALID_ARGUMENT, "LoRA entry " + std::to_string(i) +
+                                                ": need r >= 1, 0 <= off, off + n <= N and device A, B");
+    pe.push_back({e.A, e.B, e.r, e.off, e.n, e.scale});
+  }
+  const int32_t R = nsa_lora_rank(entries, count);
+  if (R <= 0) return count == 0 ? NSA_OK : fail(NSA_ERR_INVALID_ARGUMENT, "LoRA ranks overflow");
+  if (!lora_a || !lora_b) return fail(NSA_ERR_INVALID_ARGUMENT, "lora_a and lora_b must be device pointers");
+  const cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  cudaError_t e = nsa::launch_lora_pack(pe.data(), count, N, K, R, w_scale, alpha,
+                                        static_cast<__nv_bfloat16*>(lora_a), static_cast<__nv_bfloat16*>(lora_b), strm);
+  if (e != cudaSuccess) return cuda_fail(e, "LoRA pack");
   return NSA_OK;
 }
 

@@ -1,19 +1,32 @@
 // Linear layer for sm_100a with the reference's GEMM epilogue: ops.linear (app/gpu/ops.js:50-66)
 // over the tiled GEMM of app/gpu/gemm.js, whose epilogue (gemm.js:155-165) is
-//   r = alpha * acc (+ bias[n]) (silu), then C = r, C += r, or C += gate[gOff + n] * r (in place).
+//   r = alpha * acc (* rowScale[n] for int8 weights) (+ bias[n]) (+ LoRA delta) (silu), then
+//   C = r, C += r, or C += gate[gOff + n] * r (in place).
 // The DiT block's output projection is the gated form: x += gate * (a @ W_proj^T + b)
-// (app/models/nanosaur2.js:210; tools/reference.py:285).  A and W are bf16 (W in the Linear layout
-// [N][K]); C is fp32, the reference's residual stream.
+// (app/models/nanosaur2.js:210; tools/reference.py:285).  A is bf16, W bf16 or int8 (the ConvRot
+// weights, whose input A the caller has rotated: ops.js:34-38, 54), both in the Linear layout
+// [N][K]; C is fp32 (the reference's residual stream) or bf16 for the store form.
 //
 // CTA (one per SM, persistent over 128 x 256 output tiles), the QKV projection's structure:
-//   warp 0      TMA producer: A [128 rows][64] and W [256 rows][64] slices, 4-stage ring
+//   warp 0      TMA producer: A [128 rows][64] and W [256 rows][64] slices through a ring
 //   warp 1      TMEM allocator + MMA issuer: 128 x 256 x 16 tcgen05.mma into one of two accumulators
 //   warps 2-9   epilogue, two groups of four warps, each group half of the tile's columns; a thread
-//               owns one output row: alpha, bias, silu, then the store (16-byte stores) or the
-//               residual / gated residual (16-byte fp32 vector reductions into C).  Bias and gate are
-//               bulk-copied into shared memory.
+//               owns one output row of 32 (fp32) or 64 (bf16) columns at a time: alpha, row scale,
+//               bias, silu, gate, then the row goes into the warp's 128-byte-swizzled staging rows and
+//               one lane hands the [32 rows][128 bytes] box to the TMA: a tiled store, or for the
+//               residual forms an fp32 add-reduce into C performed in L2 (the reference's in-place
+//               C += gate * r).  Rows and columns past M / N are clipped by the tensor map.
+//   warps 10-13 (int8 weights only) converters: each int8 W slice lands beside the stage's bf16 slot
+//               and is rewritten there as the bf16 operand (wconv.cuh) before the MMA reads it.
+//
+// LoRA side paths (ops.js:55-57, 70-86: delta = sum_i scale_i B_i (A_i x), added before the
+// activation) run as extra K steps of the same accumulation: after the K/64 slices of A and W come
+// the slices of T = x A_cat^T [M][R] (one small GEMM before this one) against B_cat [N][R], whose rows
+// hold scale_i B_i / (alpha * rowScale[n]) (nsa_lora_pack), so that the epilogue's alpha * rowScale
+// multiplies the delta back to scale_i B_i (A_i x).
 #include "nsa_internal.h"
 #include "ptx.cuh"
+#include "wconv.cuh"
 
 namespace nsa {
 
@@ -21,57 +34,61 @@ namespace {
 
 constexpr int kLinBK = 64;
 constexpr int kLinNT = 256;
-constexpr int kLinThreads = 320;
 constexpr int kLinA = 128 * kLinBK * 2;
 constexpr int kLinB = kLinNT * kLinBK * 2;
-constexpr int kLinStage = kLinA + kLinB;   // 48 KB
-constexpr int kLinStages = 4;
+constexpr int kLinB8 = kLinNT * kLinBK;   // int8 W slice
 constexpr uint32_t kLinIdesc = idesc_bf16_f32(128, kLinNT, 0, 0);
+
+template <bool I8>
+struct LinCfg {
+  static constexpr int THREADS = I8 ? 448 : 320;
+  static constexpr int STAGE = kLinA + kLinB + (I8 ? kLinB8 : 0);   // 48 KB, 64 KB with the int8 slot
+  static constexpr int STAGES = I8 ? 3 : 4;
+  static_assert(STAGE % 1024 == 0, "stage alignment");
+};
+constexpr int kLinStaging = 8 * 4096;   // one [32 rows][128 bytes] staging box per epilogue warp
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + expf(-x)); }
 
-__global__ void __launch_bounds__(kLinThreads, 1)
+template <bool I8>
+__global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
     linear_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                  const LinearParams p) {
-  constexpr int S = kLinStages;
+                  const __grid_constant__ CUtensorMap tmT, const __grid_constant__ CUtensorMap tmL,
+                  const __grid_constant__ CUtensorMap tmC, const LinearParams p) {
+  constexpr int S = LinCfg<I8>::STAGES;
+  constexpr int STAGE = LinCfg<I8>::STAGE;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int nvec = p.n_tiles * kLinNT;                               // bias / gate entries staged
-  float* sbias = reinterpret_cast<float*>(smem + S * kLinStage);     // [nvec], zeros past N or without a bias
-  float* sgate = sbias + nvec;                                       // [nvec], ones without a gate
-  uint64_t* full = reinterpret_cast<uint64_t*>(sgate + nvec);
+  uint8_t* staging = smem + S * STAGE;                               // [8 warps][32 rows][128 bytes]
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + kLinStaging);
   uint64_t* empty = full + S;
-  uint64_t* acc_full = empty + S;
+  uint64_t* conv = empty + S;           // int8: the stage's bf16 W slot is written (4 converter warps)
+  uint64_t* acc_full = conv + S;
   uint64_t* acc_empty = acc_full + 2;   // 256 epilogue arrivals
   uint64_t* drain = acc_empty + 2;
-  uint64_t* pbar = drain + 1;           // bias / gate landed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pbar + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint64_t to = p.timeout_ns;
+  const int steps = p.k_steps + p.lora_steps;   // K slices per tile
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 4);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 256);
     }
     mbar_init(drain, 1);
-    mbar_init(pbar, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
-  }
-  // entries the bulk copies do not cover: past N, or no bias / gate at all
-  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
-    if (!p.bias || i >= p.N) sbias[i] = 0.f;
-    if (!p.gate || i >= p.N) sgate[i] = 1.f;
   }
   tc_fence_before();
   __syncthreads();
@@ -85,27 +102,33 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmW);
-      const uint32_t vb = (uint32_t)p.N * 4;
-      mbar_arrive_expect_tx(pbar, (p.bias ? vb : 0u) + (p.gate ? vb : 0u));
-      if (p.bias) bulk_load(sbias, p.bias, vb, pbar);
-      if (p.gate) bulk_load(sgate, p.gate, vb, pbar);
+      tma_prefetch_desc(&tmC);
+      if (p.lora_steps) {
+        tma_prefetch_desc(&tmT);
+        tma_prefetch_desc(&tmL);
+      }
       int step = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < tiles; u += G) {
         const int nt = u % p.n_tiles, m0 = (u / p.n_tiles) * 128;
-        for (int ks = 0; ks < p.k_steps; ++ks, ++step) {
+        for (int ks = 0; ks < steps; ++ks, ++step) {
           const int s = step % S;
           if (step >= S && !wait_bounded(&empty[s], ((step / S) - 1) & 1, abort_flag, p.err, kErrTimeoutProjection, to)) {
             ok = false;
             break;
           }
-          uint8_t* st = smem + s * kLinStage;
-          mbar_arrive_expect_tx(&full[s], kLinStage);
-          tma_load_2d(st, &tmA, &full[s], ks * kLinBK, m0);
-          tma_load_2d(st + kLinA, &tmW, &full[s], ks * kLinBK, nt * kLinNT);
+          uint8_t* st = smem + s * STAGE;
+          if (ks < p.k_steps) {
+            mbar_arrive_expect_tx(&full[s], kLinA + (I8 ? kLinB8 : kLinB));
+            tma_load_2d(st, &tmA, &full[s], ks * kLinBK, m0);
+            tma_load_2d(st + kLinA + (I8 ? kLinB : 0), &tmW, &full[s], ks * kLinBK, nt * kLinNT);
+          } else {   // LoRA slices: T rows against B_cat rows, straight into the bf16 slots
+            mbar_arrive_expect_tx(&full[s], kLinA + kLinB);
+            tma_load_2d(st, &tmT, &full[s], (ks - p.k_steps) * kLinBK, m0);
+            tma_load_2d(st + kLinA, &tmL, &full[s], (ks - p.k_steps) * kLinBK, nt * kLinNT);
+          }
         }
       }
-      wait_drain(pbar, 0, to);
       for (int i = step > S ? step - S : 0; i < step; ++i) wait_drain(&full[i % S], (i / S) & 1, to);
     }
   } else if (warp == 1) {
@@ -121,14 +144,14 @@ __global__ void __launch_bounds__(kLinThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem + (uint32_t)a * 256u;
-        for (int ks = 0; ks < p.k_steps; ++ks, ++step) {
+        for (int ks = 0; ks < steps; ++ks, ++step) {
           const int s = step % S;
-          if (!wait_bounded(&full[s], (step / S) & 1, abort_flag, p.err, kErrTimeoutProjection, to)) {
+          if (!wait_bounded(I8 ? &conv[s] : &full[s], (step / S) & 1, abort_flag, p.err, kErrTimeoutProjection, to)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * kLinStage), sb = sa + kLinA;
+          const uint32_t sa = smem_u32(smem + s * STAGE), sb = sa + kLinA;
 #pragma unroll
           for (int kk = 0; kk < kLinBK / 16; ++kk)
             mma_ss(d_tmem, smem_desc(sa + kk * 32, 16, 1024, 2), smem_desc(sb + kk * 32, 16, 1024, 2), kLinIdesc,
@@ -144,71 +167,100 @@ __global__ void __launch_bounds__(kLinThreads, 1)
         wait_drain(drain, 0, to);
       }
     }
-  } else {
+  } else if (warp < 10) {
     // ---------------------------------------------------------------- epilogue (warps 2-9)
     const int group = (warp - 2) / 4;
     const int quarter = warp % 4;
-    const int row_local = quarter * 32 + lane;
-    bool params_ready = false;
+    uint8_t* stg = staging + (warp - 2) * 4096;
+    const bool f32_out = p.C16 == nullptr;
     int t = 0;
     for (int u = blockIdx.x; u < tiles; u += G) {
       const int nt = u % p.n_tiles, m0 = (u / p.n_tiles) * 128;
       const int a = t & 1;
-      bool got = wait_bounded(&acc_full[a], (t >> 1) & 1, abort_flag, p.err, kErrTimeoutProjection, to);
-      if (got && !params_ready) {
-        got = wait_bounded(pbar, 0, abort_flag, p.err, kErrTimeoutProjection, to);
-        params_ready = true;
-      }
+      const bool got = wait_bounded(&acc_full[a], (t >> 1) & 1, abort_flag, p.err, kErrTimeoutProjection, to);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)a * 256u;
-      const int r = m0 + row_local;
-      float* crow = p.C + (int64_t)r * p.ldc;
+      const int row0 = m0 + quarter * 32;   // this warp's 32 rows (TMEM lanes)
 #pragma unroll 1
       for (int c64 = group * 128; c64 < group * 128 + 128; c64 += 64) {
-        // 64 columns under one wait (warp-wide: every lane, whatever its row)
-        uint32_t v64[64];
-        tmem_ld64(tbase + (uint32_t)c64, v64);
+        const int n64 = nt * kLinNT + c64;
+        if (n64 >= p.N) break;   // warp-uniform: nothing of this chunk is inside C
+        uint32_t v[64];
+        tmem_ld64(tbase + (uint32_t)c64, v);
 #pragma unroll
-        for (int sub = 0; sub < 4; ++sub) {
-          const int c = c64 + sub * 16;
-          const int n = nt * kLinNT + c;
-          if (r >= p.M || n >= p.N) continue;
-          float y[16];
+        for (int h = 0; h < 2; ++h) {   // fp32: two boxes of 32 columns; bf16: one box of 64
+          if (!f32_out && h == 1) break;
+          const int n0 = n64 + h * 32;
+          if (n0 >= p.N || row0 >= p.M) continue;
+          // the previous box of this warp must have left the staging rows
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+          uint8_t* row = stg + lane * 128;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float x = p.alpha * __uint_as_float(v64[sub * 16 + i]) + sbias[n + i];
-            if (p.act == 1) x = silu(x);
-            y[i] = x;
+          for (int c = 0; c < 8; ++c) {   // 16-byte chunk c of the row, at position c ^ (row & 7)
+            float y[8];
+#pragma unroll
+            for (int g4 = 0; g4 < 2; ++g4) {   // columns in fours: bias, row scale, gate (zero / one past N)
+              if (f32_out && g4 == 1) break;
+              const int j0 = f32_out ? 4 * c : 8 * c + 4 * g4;   // first column of the four within the box
+              const int n = n0 + j0;
+              const bool in = n < p.N;
+              const float4 bb = in && p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + n)) : make_float4(0.f, 0.f, 0.f, 0.f);
+              float4 mm = make_float4(p.alpha, p.alpha, p.alpha, p.alpha);
+              if (I8 && in) {
+                const float4 rs = __ldg(reinterpret_cast<const float4*>(p.w_scale + n));
+                mm = make_float4(mm.x * rs.x, mm.y * rs.y, mm.z * rs.z, mm.w * rs.w);
+              }
+              const float4 gg = in && p.gate ? __ldg(reinterpret_cast<const float4*>(p.gate + n)) : make_float4(1.f, 1.f, 1.f, 1.f);
+              const float bv[4] = {bb.x, bb.y, bb.z, bb.w}, mv[4] = {mm.x, mm.y, mm.z, mm.w}, gv[4] = {gg.x, gg.y, gg.z, gg.w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                // both candidate indices are compile-time constants (no local-memory copy of v)
+                const uint32_t acc = f32_out ? v[h * 32 + 4 * c + i] : v[(8 * c + 4 * g4 + i) & 63];
+                float x = mv[i] * __uint_as_float(acc) + bv[i];
+                if (p.act == 1) x = silu(x);
+                y[4 * g4 + i] = p.resid ? gv[i] * x : x;
+              }
+            }
+            const uint4 w = f32_out ? make_uint4(__float_as_uint(y[0]), __float_as_uint(y[1]), __float_as_uint(y[2]),
+                                                 __float_as_uint(y[3]))
+                                    : make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
+                                                 pack_bf16x2(y[6], y[7]));
+            *reinterpret_cast<uint4*>(row + ((c ^ (lane & 7)) << 4)) = w;
           }
-          // The residual forms add into C with vector reductions (each element has one owner, so this
-          // is the in-place C += g * r of the reference without a load round trip per chunk).
-          if (n + 16 <= p.N) {
-            float4* dst = reinterpret_cast<float4*>(crow + n);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              if (p.resid)
-                atomicAdd(dst + q, make_float4(sgate[n + 4 * q] * y[4 * q], sgate[n + 4 * q + 1] * y[4 * q + 1],
-                                               sgate[n + 4 * q + 2] * y[4 * q + 2],
-                                               sgate[n + 4 * q + 3] * y[4 * q + 3]));
-              else
-                dst[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              if (n + i >= p.N) break;
-              if (p.resid)
-                atomicAdd(crow + n + i, sgate[n + i] * y[i]);
-              else
-                crow[n + i] = y[i];
-            }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (p.resid)
+              tma_reduce_add_2d(&tmC, stg, n0, row0);
+            else
+              tma_store_2d(&tmC, stg, n0, row0);
+            bulk_commit_group();
           }
         }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[a]);
       ++t;
+    }
+    if (lane == 0) bulk_wait_all();
+  } else if (I8) {
+    // ---------------------------------------------------------------- int8 converters (warps 10-13)
+    const int ct = threadIdx.x - 320;
+    int step = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < tiles; u += G) {
+      for (int ks = 0; ks < steps; ++ks, ++step) {
+        const int s = step % S;
+        ok = __all_sync(0xffffffffu,
+                        wait_bounded(&full[s], (step / S) & 1, abort_flag, p.err, kErrTimeoutProjection, to));
+        if (!ok) break;
+        uint8_t* st = smem + s * STAGE;
+        if (ks < p.k_steps) convert_i8_slice<kLinNT, 128>(st + kLinA + kLinB, st + kLinA, ct);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
+      }
     }
   }
   tc_fence_before();
@@ -219,25 +271,34 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   }
 }
 
-}  // namespace
-
-cudaError_t launch_linear(const LinearParams& p, const CUtensorMap& tmA, const CUtensorMap& tmW, cudaStream_t stream) {
+template <bool I8>
+cudaError_t launch_linear_t(const LinearParams& p, const CUtensorMap& tmA, const CUtensorMap& tmW,
+                            const CUtensorMap& tmT, const CUtensorMap& tmL, const CUtensorMap& tmC,
+                            cudaStream_t stream) {
   const int sms = device_sm_count();
   const long long tiles = (long long)p.m_tiles * p.n_tiles;
   if (tiles <= 0) return cudaSuccess;
   if (tiles > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
-  const size_t smem = 1024 + (size_t)kLinStages * kLinStage + 2 * (size_t)p.n_tiles * kLinNT * 4 + 256;
-  if (smem > 232448) return cudaErrorNotSupported;
+  const size_t smem = 1024 + (size_t)LinCfg<I8>::STAGES * LinCfg<I8>::STAGE + kLinStaging + 256;
+  static_assert(1024 + 4 * (kLinA + kLinB) + kLinStaging + 256 <= 232448, "shared memory");
   // the limit is raised once per device to the whole 227 KB, so launches of different sizes from
   // several host threads never race on the attribute
   static DeviceOnce once;
   cudaError_t e = once_per_device(once, [] {
-    return cudaFuncSetAttribute(linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    return cudaFuncSetAttribute(linear_kernel<I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
   });
   if (e != cudaSuccess) return e;
   const int grid = tiles < sms ? (int)tiles : sms;
-  linear_kernel<<<grid, kLinThreads, smem, stream>>>(tmA, tmW, p);
+  linear_kernel<I8><<<grid, LinCfg<I8>::THREADS, smem, stream>>>(tmA, tmW, tmT, tmL, tmC, p);
   return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_linear(const LinearParams& p, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmT,
+                          const CUtensorMap& tmL, const CUtensorMap& tmC, cudaStream_t stream) {
+  return p.w_i8 ? launch_linear_t<true>(p, tmA, tmW, tmT, tmL, tmC, stream)
+                : launch_linear_t<false>(p, tmA, tmW, tmT, tmL, tmC, stream);
 }
 
 }  // namespace nsa

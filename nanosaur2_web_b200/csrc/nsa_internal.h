@@ -187,22 +187,54 @@ cudaError_t launch_projection(ProjParams p, int D, const CUtensorMap* tmX, const
 int projection_heads_per_tile(int D);   // 0: unsupported head dim
 
 // Linear layer with the reference's GEMM epilogue (linear.cu): C = epilogue(alpha * A W^T) over M x N
-// with A [M][K] bf16 (tmA: 2-D map, box [128][64]), W [N][K] bf16 (tmW: box [256][64]), 128-byte
-// swizzle; r = alpha*acc (+ bias[n]) (silu if act == 1), then C[m][n] = r or, with resid,
-// C[m][n] += gate[n] * r (gate null: 1).  C is fp32 with row pitch ldc (already offset by cOff).
+// with A [M][K] bf16 (tmA: 2-D map, box [128][64], 128-byte swizzle) and W [N][K] bf16 (tmW: box
+// [256][64], 128-byte swizzle) or int8 (w_i8: box [256][64] without swizzle, converted in shared memory;
+// w_scale[n] multiplies row n's dot product); r = alpha*acc (*w_scale[n]) (+ bias[n]) (silu if act == 1),
+// then C[m][n] = r or, with resid, C[m][n] += gate[n] * r (gate null: 1); with C16 set, the bf16 store
+// form C16[m][n] = r instead (bias, gate and w_scale 16-byte aligned).  lora_steps more K slices follow the K/64 of A and W: T (tmT, [M][R] bf16,
+// box [128][64]) against B_cat (tmL, [N][R] bf16, box [256][64]).  C / C16 have row pitch ldc (already
+// offset by cOff).
 struct LinearParams {
   int M, N, k_steps, m_tiles, n_tiles;
+  int lora_steps;
   float alpha;
   const float* bias;   // [N] or null (16-byte aligned, N a multiple of 4)
   const float* gate;   // [N] (offset by gOff) or null
   int resid;
   int act;             // 0 none, 1 silu
+  int w_i8;            // W is int8 with per-row scales w_scale[N]
+  const float* w_scale;
   float* C;
+  __nv_bfloat16* C16;  // bf16 output instead of C (store form only)
   int64_t ldc;
   int* err;
   unsigned long long timeout_ns;
 };
-cudaError_t launch_linear(const LinearParams& p, const CUtensorMap& tmA, const CUtensorMap& tmW, cudaStream_t stream);
+// tmC: 2-D map over C ([M][N] at C + cOff, row pitch ldc; fp32 box [32 rows][32], bf16 box [32 rows][64],
+// 128-byte swizzle): the epilogue's tiled stores and fp32 add-reductions.
+cudaError_t launch_linear(const LinearParams& p, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmT,
+                          const CUtensorMap& tmL, const CUtensorMap& tmC, cudaStream_t stream);
+
+// ConvRot input rotation (rotate.cu): Y[r][g*256 + i] = sum_j H256[i][j] X[r][g*256 + j] / 16 for every
+// group g of 256 columns (cols a multiple of 256; X rows 16-byte aligned).
+struct RotateParams {
+  int rows, cols;
+  int64_t ldx, ldy;
+  const void* x;    // fp32, or bf16 when in_bf16
+  void* y;          // fp32, or bf16 when out_bf16
+  int in_bf16, out_bf16;
+};
+cudaError_t launch_rotate(const RotateParams& p, cudaStream_t stream);
+
+// LoRA packing (lora.cu): A_cat [R][K] and B_cat [N][R] bf16 from fp32 entries (device pointers).
+struct LoraPackEntry {
+  const float* A;   // [r][K]
+  const float* B;   // [n][r]
+  int r, off, n;
+  float scale;
+};
+cudaError_t launch_lora_pack(const LoraPackEntry* e, int count, int N, int K, int R, const float* w_scale, float alpha,
+                             __nv_bfloat16* a_cat, __nv_bfloat16* b_cat, cudaStream_t stream);
 
 // Row RMSNorm (rmsnorm.cu): Y[r][c] (=|+=) X[r][c] * rsqrt(mean(X[r]^2) + eps) * w[c].
 struct RmsParams {

@@ -26,7 +26,7 @@ import torch
 from . import _lib
 from ._lib import NSA_BF16, NSA_F32, AttentionDesc, NsaError, check, lib
 
-__all__ = ["attention", "headNorm", "linear", "rmsnorm", "glu", "rope2dTable", "ropeTable", "RopeTable", "NsaError",
+__all__ = ["attention", "headNorm", "linear", "lora_pack", "LoraPack", "rotate", "rmsnorm", "glu", "rope2dTable", "ropeTable", "RopeTable", "NsaError",
            "dtype_code", "stream_handle", "check_device"]
 
 
@@ -101,30 +101,122 @@ def headNorm(X: torch.Tensor, weight: torch.Tensor, *, L: int, H: int, D: int, l
                                   float(eps), stream_handle(X.device)))
 
 
+@dataclass
+class LoraPack:
+    """The LoRA side paths of one linear packed for ``linear`` (nsa_lora_pack): ``a`` bf16 [R, K],
+    ``b`` bf16 [R] columns per output row [N, R], ``R`` the padded rank, and the ``alpha`` / weight
+    scales ``b`` was divided by."""
+    a: torch.Tensor
+    b: torch.Tensor
+    R: int
+    N: int
+    K: int
+    alpha: float
+    w_scale: Optional[torch.Tensor]
+
+
+def lora_pack(entries, N: int, K: int, *, w_scale: Optional[torch.Tensor] = None, alpha: float = 1.0,
+              rotate_a: bool = False) -> Optional[LoraPack]:
+    """Pack LoRA entries ``[{"A": [r, K] fp32, "B": [n, r] fp32, "scale": s, "off": o, "n": n}]`` of one
+    linear (app/lora.js:143-150: scale = strength * alpha / r, [off, off + n) the output columns).  For
+    int8 ConvRot weights pass their ``w_scale``, and ``rotate_a=True`` when A's rows are not rotated yet
+    (the reference's loader rotates them, app/lora.js:126).  Returns None for no entries."""
+    entries = list(entries)
+    if not entries:
+        return None
+    dev = entries[0]["A"].device
+    _require_cuda(w_scale, *[e["A"] for e in entries], *[e["B"] for e in entries])
+    keep = []
+    arr = (_lib.LoraEntry * len(entries))()
+    for i, e in enumerate(entries):
+        A, B = e["A"], e["B"]
+        if A.dtype != torch.float32 or B.dtype != torch.float32 or A.dim() != 2 or B.dim() != 2:
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "LoRA A and B must be 2-D float32 tensors")
+        r = A.shape[0]
+        if A.shape[1] != K or B.shape[1] != r:
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, f"LoRA entry {i}: A must be [r, {K}] and B [n, r]")
+        A = A.contiguous()
+        if rotate_a:
+            A = rotate(A)
+        B = B.contiguous()
+        keep += [A, B]
+        arr[i].A, arr[i].B, arr[i].r = A.data_ptr(), B.data_ptr(), r
+        arr[i].off, arr[i].n, arr[i].scale = int(e.get("off", 0)), int(e.get("n", B.shape[0])), float(e["scale"])
+        if B.shape[0] != arr[i].n:
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, f"LoRA entry {i}: B has {B.shape[0]} rows, n = {arr[i].n}")
+    R = lib().nsa_lora_rank(arr, len(entries))
+    a = torch.empty((R, K), dtype=torch.bfloat16, device=dev)
+    b = torch.empty((N, R), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        check(lib().nsa_lora_pack(arr, len(entries), N, K, _ptr(w_scale), float(alpha), a.data_ptr(), b.data_ptr(),
+                                  stream_handle(dev)))
+    return LoraPack(a, b, R, N, K, float(alpha), w_scale)
+
+
+def rotate(x: torch.Tensor, out: Optional[torch.Tensor] = None, *,
+           out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """ConvRot input rotation (app/gpu/ops.js:38-45): every group of 256 columns times the normalised
+    regular Hadamard matrix H256.  x fp32 or bf16 [rows, cols] (cols a multiple of 256, unit inner
+    stride); out fp32 or bf16 (``out_dtype``, default x's dtype)."""
+    _require_cuda(x, out)
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "x must be [rows, cols] with unit inner stride")
+    if out is None:
+        out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    if out.dim() != 2 or out.stride(1) != 1 or tuple(out.shape) != tuple(x.shape):
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "out must match x's shape with unit inner stride")
+    d = _lib.RotateDesc()
+    d.rows, d.cols = x.shape
+    d.ldx, d.ldy = x.stride(0), out.stride(0)
+    d.in_dtype, d.out_dtype = dtype_code(x), dtype_code(out)
+    with torch.cuda.device(x.device):
+        check(lib().nsa_rotate(ctypes.byref(d), x.data_ptr(), out.data_ptr(), stream_handle(x.device)))
+    return out
+
+
 def linear(x: torch.Tensor, W: torch.Tensor, *, bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
            resid: bool = False, gate: Optional[torch.Tensor] = None, gOff: int = 0, act: Optional[str] = None,
-           cOff: int = 0, alpha: float = 1.0) -> torch.Tensor:
-    """y = x @ W^T (+ bias) (silu), then out = y, out += y (resid) or out += gate[gOff + n] * y (resid + gate)
-    (app/gpu/ops.js:50-66 with the epilogue of app/gpu/gemm.js:155-165).  x [M, K] bf16 (row pitch
-    x.stride(0)), W [N, K] bf16 contiguous, out [M, ldc] fp32 written at columns cOff..cOff+N-1,
-    allocated [M, N] when not given."""
-    _require_cuda(x, W, bias, out, gate)
-    if x.dim() != 2 or x.dtype != torch.bfloat16 or x.stride(1) != 1 or W.dtype != torch.bfloat16:
-        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "x must be [M, K] and W [N, K], both bf16 with unit inner stride")
+           cOff: int = 0, alpha: float = 1.0, w_scale: Optional[torch.Tensor] = None,
+           lora: Optional[LoraPack] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """y = x @ W^T (* w_scale) (+ bias) (+ LoRA delta) (silu), then out = y, out += y (resid) or
+    out += gate[gOff + n] * y (resid + gate) (app/gpu/ops.js:50-66 with the epilogue of
+    app/gpu/gemm.js:155-165).  x [M, K] bf16 (row pitch x.stride(0)); W [N, K] contiguous, bf16, or
+    int8 with per-row float32 ``w_scale`` [N] (the ConvRot weights: x must then be the rotated input,
+    ``rotate``); ``lora`` from ``lora_pack``.  out [M, ldc] float32 (or bfloat16 for the store form)
+    written at columns cOff..cOff+N-1, allocated [M, N] (dtype ``out_dtype``) when not given."""
+    _require_cuda(x, W, bias, out, gate, w_scale)
+    if x.dim() != 2 or x.dtype != torch.bfloat16 or x.stride(1) != 1 or W.dtype not in (torch.bfloat16, torch.int8):
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT,
+                       "x must be [M, K] bf16 and W [N, K] bf16 or int8, with unit inner stride")
     if not W.is_contiguous():
         raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "W must be contiguous [N, K]")
+    i8 = W.dtype == torch.int8
+    if i8 and (w_scale is None or w_scale.dtype != torch.float32 or w_scale.numel() != W.shape[0]
+               or not w_scale.is_contiguous()):
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "int8 weights need a contiguous float32 w_scale of N entries")
     M, K = x.shape
     N = W.shape[0]
     if out is None:
         if resid:
             raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "resid needs out")
-        out = torch.empty((M, N), dtype=torch.float32, device=x.device)
-    if out.dtype != torch.float32 or out.dim() != 2 or out.stride(1) != 1:
-        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "out must be a float32 [M, ldc] tensor with unit inner stride")
+        out = torch.empty((M, N), dtype=out_dtype or torch.float32, device=x.device)
+    if out.dtype not in (torch.float32, torch.bfloat16) or out.dim() != 2 or out.stride(1) != 1:
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "out must be a float32 or bfloat16 [M, ldc] tensor with unit inner stride")
     d = _lib.LinearDesc()
     d.M, d.N, d.K = M, N, K
     d.lda, d.ldc, d.cOff, d.gOff = x.stride(0), out.stride(0), cOff, gOff
     d.alpha, d.resid, d.act = alpha, int(bool(resid)), {None: 0, "none": 0, "silu": 1}[act]
+    d.out_dtype = dtype_code(out)
+    d.w_format = _lib.NSA_W_I8 if i8 else _lib.NSA_W_BF16
+    d.w_scale = _ptr(w_scale) if i8 else None
+    t = None
+    if lora is not None:
+        if lora.N != N or lora.K != K:
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, f"the LoRA pack is for [{lora.N}, {lora.K}], W is [{N}, {K}]")
+        if lora.alpha != float(alpha) or (lora.w_scale is None) == i8:
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "the LoRA pack was made for another alpha or weight format")
+        t = torch.empty((M, lora.R), dtype=torch.bfloat16, device=x.device)
+        d.lora_rank, d.lora_a, d.lora_b, d.lora_t = lora.R, lora.a.data_ptr(), lora.b.data_ptr(), t.data_ptr()
     with torch.cuda.device(x.device):
         check(lib().nsa_linear(ctypes.byref(d), x.data_ptr(), W.data_ptr(), _ptr(bias), _ptr(gate), out.data_ptr(),
                                stream_handle(x.device)))

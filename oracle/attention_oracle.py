@@ -51,6 +51,63 @@ def linear_epilogue(y, out=None, gate=None, resid=False, act=None, acc=np.float3
     return np.asarray(out, acc) + g * y
 
 
+# ----------------------------------------------------------------------------- int8 ConvRot and LoRA
+
+CONVROT_GROUP = 256   # tools/quant.py:18
+
+
+def hadamard(n=CONVROT_GROUP, acc=np.float32):
+    """The normalised regular Hadamard matrix of tools/quant.py:21-30: Kronecker powers of
+    H4 = [[1,1,1,-1],[1,1,-1,1],[1,-1,1,1],[-1,1,1,1]], divided by sqrt(n) (n a power of 4)."""
+    h4 = np.array([[1, 1, 1, -1], [1, 1, -1, 1], [1, -1, 1, 1], [-1, 1, 1, 1]], dtype=acc)
+    h = h4
+    while h.shape[0] < n:
+        h = np.kron(h, h4)
+    if h.shape[0] != n:
+        raise ValueError(f"size must be a power of 4, got {n}")
+    return h / acc(math.sqrt(n))
+
+
+def rotate(x, group=CONVROT_GROUP, acc=np.float32):
+    """ConvRot rotation of the last axis in groups of 256 (ops.rotate, app/gpu/ops.js:38-45, and the
+    hadamard kernel, app/gpu/kernels.js:379-407; tools/quant.py:33-37 for weights): y = x @ H^T per
+    group, H symmetric."""
+    x = np.asarray(x, acc)
+    k = x.shape[-1]
+    h = hadamard(group, acc)
+    return (x.reshape(*x.shape[:-1], k // group, group) @ h.T).reshape(x.shape)
+
+
+def quantize_int8_convrot(w):
+    """tools/quant.py:48-57: per-output-row int8 of the rotated weight; returns (q int8 [N][K],
+    scale float32 [N]).  Rounding is to nearest even, as torch.round."""
+    rot = rotate(np.asarray(w, np.float32), acc=np.float32)
+    scale = np.maximum(np.abs(rot).max(axis=1, keepdims=True) / np.float32(127.0), np.float32(1e-30))
+    q = np.clip(np.round(rot / scale), -128, 127).astype(np.int8)
+    return q, scale.reshape(-1).astype(np.float32)
+
+
+def linear_int8(xr, q, scale, b=None, acc=np.float32):
+    """The reference's GEMM with an "i8" B (app/gpu/gemm.js:10, 119-130, epilogue 159-160): the int8
+    weights are read as exact integers, the row's dot product times scale[n], then the bias.  xr is the
+    rotated input (app/gpu/ops.js:54)."""
+    y = (np.asarray(xr, acc) @ np.asarray(q, acc).T) * np.asarray(scale, acc)
+    return y + np.asarray(b, acc) if b is not None else y
+
+
+def lora_delta(x, entries, N, acc=np.float32):
+    """delta = sum_i scale_i * B_i (A_i x) over output columns [off_i, off_i + n_i)
+    (app/gpu/ops.js:70-86; entries as app/lora.js:143-150 builds them: dicts with A [r][K], B [n][r],
+    scale, off, n).  For int8 layers A's rows are rotated and x is the rotated input."""
+    x = np.asarray(x, acc)
+    d = np.zeros((x.shape[0], N), acc)
+    for e in entries:
+        off = int(e.get("off", 0))
+        B = np.asarray(e["B"], acc)
+        d[:, off:off + B.shape[0]] += acc(e["scale"]) * ((x @ np.asarray(e["A"], acc).T) @ B.T)
+    return d
+
+
 # ----------------------------------------------------------------------------- prologue pieces
 
 def rms_norm(x, w, eps=1e-6, acc=np.float32):

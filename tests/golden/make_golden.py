@@ -20,6 +20,12 @@ drives its real code paths with small seeded stand-in weights (no model files ex
 * ``gemma_encode``'s layers 0 and 5 (``:187-199``: input norm, q/k/v linears, head norms, RoPE,
   causal SDPA, o linear, post-attention norm, residual add; then the GELU-tanh MLP with its norms) on
   a 64-wide residual stream with bf16-exact linear weights (``--only gemma_sublayer``).
+* an int8 ConvRot linear with two LoRAs (``--only convrot``): a seeded weight quantised by the
+  reference's ``quant.quantize_int8_convrot`` (``tools/quant.py:48-57``), written with a bias to a
+  temporary safetensors file beside two LoRA files (PEFT names with an alpha, kohya names without),
+  loaded through the reference's ``Weights`` (``tools/reference.py:48-67``: dequantise on access, LoRA
+  deltas merged, ``lora_deltas`` at ``:70-94``) and applied with its ``lin``; plus ``quant.hadamard``
+  and ``quant.rotate`` on seeded inputs (H16 and a rotation by H256).
 * ``VAE.attn`` (``:352-357``), the VAE decoder's single-head attention block (group norm, q/k/v 1x1
   convolutions, SDPA with head dim C, proj_out, residual) on a 64 x 6 x 5 activation
   (``--only vae_attention``).
@@ -304,12 +310,47 @@ def write_linear(R, out):
                         y_nobias=np32(y_nobias))
 
 
+def write_convrot(R, out, N=32, K=512, M=9):
+    """int8 ConvRot weights and LoRAs through the reference's own loader and lin."""
+    import tempfile
+
+    import quant  # the reference's tools/quant.py (on sys.path beside reference.py)
+    from safetensors.torch import save_file
+
+    gen = torch.Generator().manual_seed(505)
+    w = torch.randn(N, K, generator=gen) / 16
+    b = torch.randn(N, generator=gen)
+    x = torch.randn(M, K, generator=gen)
+    a1 = torch.randn(8, K, generator=gen) / 16
+    b1 = torch.randn(N, 8, generator=gen) / 8
+    a2 = torch.randn(4, K, generator=gen) / 16
+    b2 = torch.randn(N, 4, generator=gen) / 8
+    alpha1, s1, s2 = 4.0, 0.8, -0.5
+    qt = quant.quantize_int8_convrot(w)
+    with tempfile.TemporaryDirectory() as d:
+        base, l1, l2 = (os.path.join(d, f) for f in ("base.safetensors", "l1.safetensors", "l2.safetensors"))
+        save_file({"blk.lin.weight": qt["weight"], "blk.lin.weight_scale": qt["weight_scale"],
+                   "blk.lin.comfy_quant": qt["comfy_quant"], "blk.lin.bias": b}, base)
+        save_file({"diffusion_model.blk.lin.lora_A.weight": a1, "diffusion_model.blk.lin.lora_B.weight": b1,
+                   "diffusion_model.blk.lin.alpha": torch.tensor(alpha1)}, l1)
+        save_file({"lora_unet_blk_lin.lora_down.weight": a2, "lora_unet_blk_lin.lora_up.weight": b2}, l2)
+        y_base = R.lin(R.Weights(base), "blk.lin", x)
+        y_lora = R.lin(R.Weights(base, loras=[(l1, s1), (l2, s2)]), "blk.lin", x)
+    hx = torch.randn(3, 512, generator=gen)
+    np.savez_compressed(
+        os.path.join(out, "convrot.npz"), x=np32(x), w=np32(w), b=np32(b), q=qt["weight"].numpy(),
+        scale=np32(qt["weight_scale"].reshape(-1)), a1=np32(a1), b1=np32(b1), a2=np32(a2), b2=np32(b2),
+        alpha1=alpha1, s1=s1, s2=s2, y_base=np32(y_base), y_lora=np32(y_lora), h16=np32(quant.hadamard(16, "cpu")),
+        hx=np32(hx), hx_rot=np32(quant.rotate(hx)))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("NANOSAUR2_REFERENCE"),
                     help="checkout of the reference repository (or NANOSAUR2_REFERENCE)")
     ap.add_argument("--out", default=HERE)
-    ap.add_argument("--only", choices=["linear", "gemma_sublayer", "vae_attention"], help="write one fixture only")
+    ap.add_argument("--only", choices=["linear", "gemma_sublayer", "vae_attention", "convrot"],
+                    help="write one fixture only")
     args = ap.parse_args()
     if not args.reference:
         ap.error("pass --reference <checkout of the reference> or set NANOSAUR2_REFERENCE")
@@ -322,6 +363,8 @@ def main():
         write_gemma_sublayer(R, args.out)
     if args.only in (None, "vae_attention"):
         write_vae_attention(R, args.out)
+    if args.only in (None, "convrot"):
+        write_convrot(R, args.out)
     if args.only:
         return
 

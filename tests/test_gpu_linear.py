@@ -81,3 +81,145 @@ def test_linear_plain_residual_without_bias():
     check_device()
     want = O.linear_epilogue(O.linear(a, w, acc=np.float64), x, resid=True, acc=np.float64)
     np.testing.assert_allclose(out.cpu().numpy(), want, rtol=1e-3, atol=2e-3)
+
+
+# ----------------------------------------------------------------------------- ConvRot int8 and LoRA
+# The int8 weights are exact integers in the bf16 operand the tensor core reads, so the int8 product is
+# compared with the oracle on the same (rotated, bf16-rounded) input at the fp32-accumulation bound.
+# The LoRA side path is evaluated as bf16 T = x A_cat^T and bf16 B_cat = scale B / (alpha w_scale); the
+# oracle emulates those two roundings, and the bound adds one bf16 step of the delta.
+
+def test_rotate_matches_oracle():
+    """ops.rotate (app/gpu/ops.js:38-45) over 300 rows x 1536 columns (6 groups of 256), fp32 and bf16
+    in and out, with row pitches wider than the rows."""
+    from nanosaur2_web_b200.ops import rotate
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal((300, 1544), dtype=np.float32)
+    want = O.rotate(x[:, :1536], acc=np.float64)
+    xt = t(x)[:, :1536]
+    y32 = rotate(xt)
+    out = torch.full((300, 1560), 5.0, device=DEV, dtype=torch.bfloat16)
+    rotate(xt, out=out[:, :1536])
+    check_device()
+    np.testing.assert_allclose(y32.cpu().numpy(), want, rtol=1e-5, atol=1e-5)
+    got = out.float().cpu().numpy()
+    np.testing.assert_allclose(got[:, :1536], want, rtol=2 ** -8, atol=1e-6)
+    assert (got[:, 1536:] == 5.0).all()
+    xb = bf16_round(x[:, :1536])
+    y16 = rotate(t(xb, torch.bfloat16), out_dtype=torch.bfloat16)
+    check_device()
+    np.testing.assert_allclose(y16.float().cpu().numpy(), O.rotate(xb, acc=np.float64), rtol=2 ** -8, atol=1e-6)
+
+
+def test_int8_convrot_linear_golden(golden):
+    """The reference's own int8 layer (tools/quant.py quantiser, tools/reference.py loader and lin,
+    tests/golden/convrot.npz): x rotated on the GPU, int8 GEMM with row scales and bias."""
+    from nanosaur2_web_b200.ops import linear, rotate
+    g = golden("convrot")
+    xr = rotate(t(g["x"]), out_dtype=torch.bfloat16)
+    y = linear(xr, t(g["q"], torch.int8), bias=t(g["b"]), w_scale=t(g["scale"]))
+    check_device()
+    xr_np = xr.float().cpu().numpy()
+    np.testing.assert_allclose(xr_np, O.rotate(g["x"], acc=np.float64), rtol=2 ** -8, atol=1e-6)
+    want = O.linear_int8(xr_np, g["q"], g["scale"], g["b"], acc=np.float64)
+    np.testing.assert_allclose(y.cpu().numpy(), want, rtol=1e-4, atol=1e-4)
+    # end to end against the reference's fp32 result: the bf16 rounding of the rotated input
+    np.testing.assert_allclose(y.cpu().numpy(), g["y_base"], rtol=1e-2, atol=2e-2)
+
+
+def _lora_oracle(xr, q_or_w, scale, b, entries, N, alpha=1.0):
+    """The oracle's linear with the bf16 roundings of the packed side path emulated.  Returns the
+    result and a bound on what one bf16 step of each T element (whose rounding the GPU takes after its
+    own fp32 summation order) can move it: sum_j |T[m][j]| 2^-8 |B_eff[n][j]|."""
+    a_cat = np.concatenate([bf16_round(e["A"]) for e in entries])
+    T = bf16_round((np.asarray(xr, np.float64) @ a_cat.astype(np.float64).T).astype(np.float32)).astype(np.float64)
+    y = (O.linear_int8(xr, q_or_w, scale, acc=np.float64) if scale is not None
+         else O.linear(xr, q_or_w, acc=np.float64)) * alpha
+    bound = np.zeros_like(y)
+    r0 = 0
+    for e in entries:
+        r = e["A"].shape[0]
+        off = int(e.get("off", 0))
+        den = alpha * (scale[off:off + e["B"].shape[0], None].astype(np.float64) if scale is not None else 1.0)
+        bq = bf16_round((e["scale"] * e["B"].astype(np.float64) / den).astype(np.float32)).astype(np.float64) * den
+        y[:, off:off + bq.shape[0]] += T[:, r0:r0 + r] @ bq.T
+        bound[:, off:off + bq.shape[0]] += (np.abs(T[:, r0:r0 + r]) * 2 ** -8) @ np.abs(bq).T
+        r0 += r
+    return (y + b if b is not None else y), bound
+
+
+def assert_close_with_bound(got, want, bound, rtol=1e-3, atol=2e-3):
+    err = np.abs(np.asarray(got, np.float64) - want)
+    lim = rtol * np.abs(want) + atol + bound
+    bad = err > lim
+    assert not bad.any(), f"{bad.sum()} elements off; worst excess {(err - lim).max():.3g}"
+
+
+def test_int8_convrot_linear_loras_golden(golden):
+    """Two LoRAs (PEFT with alpha, kohya without) on the int8 layer; A rows rotated on the GPU as the
+    reference's loader does (app/lora.js:126); against the reference's merged weight."""
+    from nanosaur2_web_b200.ops import linear, lora_pack, rotate
+    g = golden("convrot")
+    N, K = g["q"].shape
+    r1 = g["a1"].shape[0]
+    ents = [dict(A=t(g["a1"]), B=t(g["b1"]), scale=float(g["s1"]) * float(g["alpha1"]) / r1),
+            dict(A=t(g["a2"]), B=t(g["b2"]), scale=float(g["s2"]))]
+    scale = t(g["scale"])
+    pack = lora_pack(ents, N, K, w_scale=scale, rotate_a=True)
+    assert pack.R == 64
+    xr = rotate(t(g["x"]), out_dtype=torch.bfloat16)
+    y = linear(xr, t(g["q"], torch.int8), bias=t(g["b"]), w_scale=scale, lora=pack)
+    check_device()
+    xr_np = xr.float().cpu().numpy()
+    rot = [dict(e, A=O.rotate(g[a], acc=np.float64).astype(np.float32), B=g[b])
+           for e, a, b in ((ents[0], "a1", "b1"), (ents[1], "a2", "b2"))]
+    want, bound = _lora_oracle(xr_np, g["q"], g["scale"], g["b"], rot, N)
+    assert_close_with_bound(y.cpu().numpy(), want, bound, rtol=1e-3, atol=1e-3)
+    np.testing.assert_allclose(y.cpu().numpy(), g["y_lora"], rtol=1e-2, atol=3e-2)
+
+
+def test_int8_linear_dit_shape_gated_residual_with_lora_slices():
+    """The DiT output projection's shape (M 1000, N = K = 1536) with int8 weights, the gated residual,
+    and two LoRA entries on column slices (the stacked-weight form, app/lora.js:149 off / n)."""
+    from nanosaur2_web_b200.ops import linear, lora_pack
+    rng = np.random.default_rng(33)
+    M, N, K = 1000, 1536, 1536
+    xr = bf16_round(rng.standard_normal((M, K), dtype=np.float32))
+    q = rng.integers(-128, 128, size=(N, K), dtype=np.int8)
+    scale = (rng.uniform(0.5, 2.0, N) / (127 * np.sqrt(K))).astype(np.float32)
+    b = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    x0 = rng.standard_normal((M, N), dtype=np.float32)
+    mod = rng.standard_normal(3 * N).astype(np.float32)
+    ents = [dict(A=rng.standard_normal((16, K), dtype=np.float32) / 40, B=rng.standard_normal((512, 16), dtype=np.float32) / 4,
+                 scale=0.7, off=0, n=512),
+            dict(A=rng.standard_normal((24, K), dtype=np.float32) / 40, B=rng.standard_normal((1024, 24), dtype=np.float32) / 4,
+                 scale=-0.3, off=512, n=1024)]
+    pack = lora_pack([dict(e, A=t(e["A"]), B=t(e["B"])) for e in ents], N, K, w_scale=t(scale))
+    out = t(x0)
+    linear(t(xr, torch.bfloat16), t(q, torch.int8), bias=t(b), w_scale=t(scale), lora=pack, out=out, resid=True,
+           gate=t(mod), gOff=N)
+    check_device()
+    y, bound = _lora_oracle(xr, q, scale, b, ents, N)
+    want = O.linear_epilogue(y, x0, mod[N:2 * N], resid=True, acc=np.float64)
+    assert_close_with_bound(out.cpu().numpy(), want, bound * np.abs(mod[N:2 * N]))
+
+
+def test_bf16_linear_lora_alpha_silu_and_bf16_output():
+    """bf16 weights with a LoRA, alpha 0.5 (folded out of B_cat and back in the epilogue), silu, and the
+    bf16 store form; ragged M / N / K."""
+    from nanosaur2_web_b200.ops import linear, lora_pack
+    rng, a, w, b = operands(34, 300, 200, 200)
+    ents = [dict(A=rng.standard_normal((8, 200), dtype=np.float32) / 8, B=rng.standard_normal((200, 8), dtype=np.float32) / 4,
+                 scale=1.5)]
+    pack = lora_pack([dict(e, A=t(e["A"]), B=t(e["B"])) for e in ents], 200, 200, alpha=0.5)
+    y32 = linear(t(a, torch.bfloat16), t(w, torch.bfloat16), bias=t(b), act="silu", alpha=0.5, lora=pack)
+    y16 = linear(t(a, torch.bfloat16), t(w, torch.bfloat16), bias=t(b), act="silu", alpha=0.5, lora=pack,
+                 out_dtype=torch.bfloat16)
+    check_device()
+    y, bound = _lora_oracle(a, w, None, b, ents, 200, alpha=0.5)
+    want = O.linear_epilogue(y, act="silu", acc=np.float64)
+    assert_close_with_bound(y32.cpu().numpy(), want, bound * 1.1)   # silu' <= 1.1
+    # the bf16 store form is the fp32 result rounded once (same tiles, same summation order)
+    np.testing.assert_array_equal(y16.float().cpu().numpy(), bf16_round(y32.cpu().numpy()))
+    with pytest.raises(Exception, match="another alpha"):
+        linear(t(a, torch.bfloat16), t(w, torch.bfloat16), lora=pack)

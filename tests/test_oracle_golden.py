@@ -36,6 +36,48 @@ def test_linear(golden):
     np.testing.assert_allclose(O.linear(t["x"], t["w"]), t["y_nobias"], **TOL)
 
 
+def convrot_lora_entries(t, rotated=True):
+    """The two LoRAs of the convrot fixture as app/lora.js:120-150 builds them: A rows rotated for the
+    int8 layer, scale = strength * alpha / r (the kohya file has no alpha: scale = strength)."""
+    r1 = t["a1"].shape[0]
+    rot = (lambda a: O.rotate(a, acc=np.float64)) if rotated else (lambda a: a)
+    return [dict(A=rot(t["a1"]), B=t["b1"], scale=float(t["s1"]) * float(t["alpha1"]) / r1),
+            dict(A=rot(t["a2"]), B=t["b2"], scale=float(t["s2"]))]
+
+
+def test_convrot_hadamard_and_rotation(golden):
+    t = golden("convrot")
+    np.testing.assert_array_equal(O.hadamard(16), t["h16"])
+    np.testing.assert_allclose(O.rotate(t["hx"]), t["hx_rot"], rtol=1e-5, atol=2e-6)
+    # H256 is symmetric and orthogonal: rotating twice is the identity (tools/quant.py:67)
+    np.testing.assert_allclose(O.rotate(O.rotate(t["hx"], acc=np.float64), acc=np.float64), t["hx"], atol=1e-12)
+
+
+def test_convrot_quantizer(golden):
+    """tools/quant.py:48-57 restated: the same int8 weights except where fp32 summation order moves a
+    value across a rounding tie, and there by one step."""
+    t = golden("convrot")
+    q, scale = O.quantize_int8_convrot(t["w"])
+    np.testing.assert_allclose(scale, t["scale"], rtol=1e-6)
+    diff = q.astype(np.int32) - t["q"].astype(np.int32)
+    assert np.abs(diff).max() <= 1
+    pre = O.rotate(t["w"], acc=np.float64) / t["scale"][:, None].astype(np.float64)
+    ties = np.abs(np.abs(pre - np.floor(pre)) - 0.5) < 1e-4
+    assert not (diff != 0)[~ties].any()
+
+
+def test_convrot_int8_linear_with_loras(golden):
+    """The JS side path (rotated input, int8 GEMM with row scales, bias, LoRA delta from rotated A rows:
+    app/gpu/ops.js:50-86, gemm.js:159-160) equals the reference's merged, dequantised weight through
+    its own loader and lin (tools/reference.py:48-94, 208-210)."""
+    t = golden("convrot")
+    xr = O.rotate(t["x"], acc=np.float64)
+    y = O.linear_int8(xr, t["q"], t["scale"], t["b"], acc=np.float64)
+    np.testing.assert_allclose(y, t["y_base"], rtol=1e-5, atol=2e-5)
+    y = y + O.lora_delta(xr, convrot_lora_entries(t), t["q"].shape[0], acc=np.float64)
+    np.testing.assert_allclose(y, t["y_lora"], rtol=1e-5, atol=2e-5)
+
+
 def test_gemma_theta_schedule():
     assert [O.gemma_rope_theta(i) for i in range(12)] == [1e4] * 5 + [1e6] + [1e4] * 5 + [1e6]
 
