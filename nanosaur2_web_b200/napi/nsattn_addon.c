@@ -11,7 +11,12 @@
  *   fusedAttention(opts)   the DiT block's / Gemma layer's headNorm + attention sequence
  *                          (nanosaur2.js:196-208, gemma3.js:63-70)        -> nsa_fused_attention
  *   fusedWorkspaceBytes(opts)                                            -> nsa_fused_attention_workspace_size
- *   linear(opts)           ops.linear(gpu, x, W, {bias,resid,gate,gOff,act,ldc,cOff}) (ops.js:50-66)
+ *   linear(opts)           ops.linear(gpu, x, W, {bias,resid,gate,gOff,act,ldc,cOff}) (ops.js:50-66),
+ *                          with int8 ConvRot weights (wI8, wScale) and packed LoRAs (loraRank, loraA,
+ *                          loraB, loraT)
+ *   rotate(opts)           ops.rotate(gpu, x) (ops.js:38-45)                -> nsa_rotate
+ *   loraPack(opts)         the LoRA side paths of one weight (app/lora.js:143-150), entries
+ *                          [{A, B, r, off, n, scale}]; returns the packed rank R -> nsa_lora_pack
  *   rmsnorm(opts)          ops.rmsnorm(gpu, x, weight, cols, eps, out) (ops.js:111-116)
  *   glu(opts)              ops.glu(gpu, x, act) (ops.js:141-148)
  *   rope2dTable(opts) / ropeTable(opts)   common.js:28-43 / 18-24 into a device buffer
@@ -243,6 +248,13 @@ static napi_value Linear(napi_env env, napi_callback_info info) {
   d.alpha = fnum(env, o, "alpha", 1.f);
   d.resid = (int32_t)num(env, o, "resid", 0);
   d.act = (int32_t)num(env, o, "act", 0);
+  d.out_dtype = dtype(env, o, "outBf16");
+  d.w_format = num(env, o, "wI8", 0) ? NSA_W_I8 : NSA_W_BF16;
+  d.w_scale = (const float*)ptr(env, o, "wScale");
+  d.lora_rank = (int32_t)num(env, o, "loraRank", 0);
+  d.lora_a = ptr(env, o, "loraA");
+  d.lora_b = ptr(env, o, "loraB");
+  d.lora_t = ptr(env, o, "loraT");
   return done(env, nsa_linear(&d, ptr(env, o, "x"), ptr(env, o, "W"), ptr(env, o, "bias"), ptr(env, o, "gate"),
                               ptr(env, o, "out"), ptr(env, o, "stream")));
 }
@@ -274,6 +286,57 @@ static napi_value Glu(napi_env env, napi_callback_info info) {
   d.act = (int32_t)num(env, o, "act", 0);
   d.out_dtype = dtype(env, o, "outBf16");
   return done(env, nsa_glu(&d, ptr(env, o, "x"), ptr(env, o, "out"), ptr(env, o, "stream")));
+}
+
+static napi_value Rotate(napi_env env, napi_callback_info info) {
+  napi_value o = opts_arg(env, info);
+  if (!o) return NULL;
+  nsa_rotate_desc d;
+  memset(&d, 0, sizeof d);
+  d.rows = (int32_t)num(env, o, "rows", 0);
+  d.cols = (int32_t)num(env, o, "cols", 0);
+  d.ldx = num(env, o, "ldx", 0);
+  d.ldy = num(env, o, "ldy", 0);
+  d.in_dtype = dtype(env, o, "inBf16");
+  d.out_dtype = dtype(env, o, "outBf16");
+  return done(env, nsa_rotate(&d, ptr(env, o, "x"), ptr(env, o, "out"), ptr(env, o, "stream")));
+}
+
+#define NSA_ADDON_MAX_LORAS 64
+
+static napi_value LoraPack(napi_env env, napi_callback_info info) {
+  napi_value o = opts_arg(env, info);
+  if (!o) return NULL;
+  nsa_lora_entry e[NSA_ADDON_MAX_LORAS];
+  uint32_t count = 0;
+  if (has(env, o, "entries")) {
+    napi_value arr;
+    napi_get_named_property(env, o, "entries", &arr);
+    napi_get_array_length(env, arr, &count);
+  }
+  if (count > NSA_ADDON_MAX_LORAS) {
+    napi_throw_error(env, "NSA_ERR_INVALID_ARGUMENT", "too many LoRA entries for one weight");
+    return NULL;
+  }
+  napi_value arr;
+  if (count) napi_get_named_property(env, o, "entries", &arr);
+  for (uint32_t i = 0; i < count; ++i) {
+    napi_value it;
+    napi_get_element(env, arr, i, &it);
+    e[i].A = (const float*)ptr(env, it, "A");
+    e[i].B = (const float*)ptr(env, it, "B");
+    e[i].r = (int32_t)num(env, it, "r", 0);
+    e[i].off = (int32_t)num(env, it, "off", 0);
+    e[i].n = (int32_t)num(env, it, "n", 0);
+    e[i].scale = fnum(env, it, "scale", 1.f);
+  }
+  nsa_status st = nsa_lora_pack(e, (int32_t)count, (int32_t)num(env, o, "N", 0), (int32_t)num(env, o, "K", 0),
+                                (const float*)ptr(env, o, "wScale"), fnum(env, o, "alpha", 1.f), ptr(env, o, "loraA"),
+                                ptr(env, o, "loraB"), ptr(env, o, "stream"));
+  if (st != NSA_OK) return done(env, st);   /* throws */
+  napi_value r;
+  napi_create_int32(env, nsa_lora_rank(e, (int32_t)count), &r);
+  return r;
 }
 
 /* ----------------------------------------------------------------------------- tables, errors */
@@ -313,6 +376,8 @@ static napi_value Init(napi_env env, napi_value exports) {
   export_fn(env, exports, "linear", Linear);
   export_fn(env, exports, "rmsnorm", Rmsnorm);
   export_fn(env, exports, "glu", Glu);
+  export_fn(env, exports, "rotate", Rotate);
+  export_fn(env, exports, "loraPack", LoraPack);
   export_fn(env, exports, "rope2dTable", Rope2dTable);
   export_fn(env, exports, "ropeTable", RopeTable);
   export_fn(env, exports, "checkDevice", CheckDevice);
