@@ -4,6 +4,9 @@
 //     tools/reference.py:96-104,240-241) on the way, and zero-filling padded / masked rows;
 //   * the in-place per-head norm (+RoPE) that mirrors ops.headNorm (app/gpu/ops.js:131-138);
 //   * the RoPE table builders of app/models/common.js:15-43.
+#include <algorithm>
+#include <numeric>
+
 #include "nsa_internal.h"
 #include "ptx.cuh"
 
@@ -275,14 +278,143 @@ __global__ void __launch_bounds__(256, NSA_PROLOGUE_MIN_BLOCKS) prologue_vec_ker
   if (part > 0 && p.n_peers > 0) __threadfence_system();   // peer stores visible before any later signal
 }
 
+// Lane-per-chunk prologue (bf16 input, head dims 64 / 96 / 128).  Eight lanes per head; lane s < D/16
+// owns elements [8s, 8s + 8) of both halves of the head, so the RoPE pair (i, i + D/2) stays in one
+// lane with one 16-byte load and one 16-byte store per half, and the head's RMSNorm sum is a
+// three-step shuffle over its eight lanes (lanes past D/16 contribute zeros).  A thread holds only
+// 16 values per row (the norm weights come from shared memory), so the SM runs 32 warps, and the blocks stride over (row, head, lane) items with the next item's two loads issued
+// before the current one is normalised, rotated and stored: the kernel is HBM-latency-bound, and this
+// keeps about twice as many reads in flight per SM as one (row, head) item per thread.  Any head
+// count works (a head's eight lanes are an aligned group of a warp), so every shard of a call takes
+// the same kernel and the same summation order.
+#ifndef NSA_LANE_MIN_BLOCKS
+#define NSA_LANE_MIN_BLOCKS 4
+#endif
+template <int D>
+__global__ void __launch_bounds__(256, NSA_LANE_MIN_BLOCKS) prologue_lane_kernel(const PrologueParams p) {
+  using T = __nv_bfloat16;
+  constexpr int HALF = D / 2;
+  constexpr int P = D / 16;   // lanes of a head that own data
+  static_assert(P >= 1 && P <= 8 && D % 16 == 0, "head dim");
+  if (blockIdx.x == 0 && blockIdx.y == 0)
+    for (int i = threadIdx.x; i < p.zero_count; i += blockDim.x) p.zero_ptr[i] = 0;
+  const int part = blockIdx.y / p.B + (p.skip_q ? 1 : 0);
+  const int bl = blockIdx.y % p.B;
+  const int b = p.b_begin + bl;
+  const int H = part == 0 ? p.Hq : p.Hkv;
+  const int pad = p.rows[part];
+  const RowView& view = part == 0 ? p.q : (part == 1 ? p.k : p.v);
+  const int h_begin = part == 0 ? p.hq_begin : p.hkv_begin;
+  const float* w = part == 0 ? p.q_w : (part == 1 ? p.k_w : nullptr);
+  const int valid_rows = part == 0 ? p.Lq : (p.kv_len ? min(p.kv_len[b], p.Lk) : p.Lk);
+  // first produced row: V rows of whole tiles of valid keys come from the input instead
+  const int r_begin = (part == 2 && p.v_tile > 0) ? max(0, valid_rows / p.v_tile * p.v_tile - p.row0[2]) : 0;
+  // (row, head, lane) items, item = (row * H + head) * 8 + lane; the launcher keeps the count below
+  // 2^31 and makes the stride a multiple of 8 * H, so a thread's lane and head never change and its
+  // row advances by a constant
+  const int nrows = max(pad - r_begin, 0);
+  const int count = nrows * H * 8;
+  const int stride = gridDim.x * blockDim.x;
+  const int di = stride / (8 * H);
+  const int it0 = blockIdx.x * blockDim.x + threadIdx.x;
+  const int sub = it0 % 8;
+  const int hh = (it0 / 8) % H;
+  const int i0 = it0 / (8 * H);
+  const bool lane_on = sub < P;
+  // the part's norm weights, read per row from shared memory (registers are kept for the loads)
+  __shared__ __align__(16) float sw[D];
+  if (w)
+    for (int e = threadIdx.x; e < D; e += blockDim.x) sw[e] = w[e];
+  __syncthreads();
+  const int ok_rows = min(nrows, valid_rows - p.row0[part] - r_begin);   // rows with data
+  // addresses are rebuilt from the kernel parameters at each use (constant-bank operands), which
+  // keeps the live registers at what 32 warps per SM allow
+  auto load = [&](int i, uint4& a, uint4& c) {   // produced row r_begin + i (zeros past the data)
+    const bool ok = lane_on && i < ok_rows;
+    const T* src = reinterpret_cast<const T*>(view.ptr) + (int64_t)b * view.bstride + view.off +
+                   (int64_t)(h_begin + hh) * D + sub * 8 + (int64_t)(p.src_row0[part] + r_begin + i) * view.ld;
+    a = ok ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0u, 0u, 0u, 0u);
+    c = ok ? __ldg(reinterpret_cast<const uint4*>(src + HALF)) : make_uint4(0u, 0u, 0u, 0u);
+  };
+  const TileOut& to = p.out[part];
+  int i = i0;
+  uint4 a, c;
+  load(i, a, c);
+  // the bound is uniform over the block (its first item), so every lane reaches the shuffles
+  for (int first = blockIdx.x * blockDim.x; first < count; first += stride, i += di) {
+    uint4 na, nc;
+    load(i + di, na, nc);
+    const int r_out = r_begin + i;
+    const int row = p.row0[part] + r_out;   // key / query index and RoPE row
+    const bool in_range = lane_on && i < nrows;
+    const bool valid = in_range && row < valid_rows;
+    float x1[8], x2[8];
+    {
+      const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wc[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        x1[2 * e] = __uint_as_float(wa[e] << 16);
+        x1[2 * e + 1] = __uint_as_float(wa[e] & 0xffff0000u);
+        x2[2 * e] = __uint_as_float(wc[e] << 16);
+        x2[2 * e + 1] = __uint_as_float(wc[e] & 0xffff0000u);
+      }
+    }
+    if (w) {   // uniform over the block: every lane reaches the shuffles
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += x1[e] * x1[e] + x2[e] * x2[e];
+      ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      const float r = rsqrtf(ss / (float)D + p.eps);
+      const float4* w1 = reinterpret_cast<const float4*>(sw + (lane_on ? sub * 8 : 0));
+      const float4* w2 = reinterpret_cast<const float4*>(sw + HALF + (lane_on ? sub * 8 : 0));
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const float4 a4 = w1[q], c4 = w2[q];
+        const float wa[4] = {a4.x, a4.y, a4.z, a4.w}, wc[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          x1[4 * q + e] *= r * wa[e];
+          x2[4 * q + e] *= r * wc[e];
+        }
+      }
+    }
+    if (valid && part < 2 && p.cs != nullptr && row < p.rope_rows) {
+      const float4* cp = reinterpret_cast<const float4*>(p.cs + (int64_t)row * HALF + sub * 8);
+      const float4* sp = reinterpret_cast<const float4*>(p.cs + p.sin_off + (int64_t)row * HALF + sub * 8);
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const float4 c4 = __ldg(cp + q), s4 = __ldg(sp + q);
+        const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float xa = x1[4 * q + e], xc = x2[4 * q + e];
+          x1[4 * q + e] = xa * cc[e] - xc * sn[e];
+          x2[4 * q + e] = xc * cc[e] + xa * sn[e];
+        }
+      }
+    }
+    if (in_range) {
+      __nv_bfloat16* dst = to.ptr + (int64_t)bl * to.bs + (int64_t)hh * to.hs + (int64_t)r_out * to.rs + sub * 8;
+      *reinterpret_cast<uint4*>(dst) = make_uint4(pack_bf16x2(x1[0], x1[1]), pack_bf16x2(x1[2], x1[3]),
+                                                  pack_bf16x2(x1[4], x1[5]), pack_bf16x2(x1[6], x1[7]));
+      *reinterpret_cast<uint4*>(dst + HALF) = make_uint4(pack_bf16x2(x2[0], x2[1]), pack_bf16x2(x2[2], x2[3]),
+                                                         pack_bf16x2(x2[4], x2[5]), pack_bf16x2(x2[6], x2[7]));
+    }
+    a = na;
+    c = nc;
+  }
+}
+
 // Streaming form of the vector prologue (bf16 input, head dim 256): the thread mapping and the
 // arithmetic are the vector kernel's, but the blocks of one (part, batch element) stride over its
 // (row, head) items, NSA_PROLOGUE_ITEMS per thread, and each thread issues the loads of its next
 // item before it normalises, rotates and stores the current one, so its HBM reads stay in flight
 // while it computes.  V rows of key tiles the attention kernel reads straight from the input are
-// not visited.  At head dim 256 (P = 8, two items of 64 bytes in flight per thread at 127
-// registers, 16 warps per SM) it beats the one-item-per-thread kernel; at head dim 96 its 168
-// registers leave too few warps per SM and the vector kernel stays ahead.
+// not visited.  At head dim 256 (P = 8, two items of 64 bytes in flight per thread, 16 warps per SM)
+// it beats the one-item-per-thread kernel.  The values stay packed two to a register until they are
+// used, which is what lets the next item's loads sit beside the current item's arithmetic.
 #ifndef NSA_PROLOGUE_ITEMS
 #define NSA_PROLOGUE_ITEMS 8   // (row, head) items per thread and part
 #endif
@@ -342,74 +474,68 @@ __global__ void __launch_bounds__(kStreamThreads, 4) prologue_stream_kernel(cons
     const int row = p.row0[part] + r_out;   // key / query index and RoPE row
     const bool valid = in_range && row < valid_rows;
     const bool rope = part < 2 && p.cs != nullptr && row < p.rope_rows;
-    float x1[S], x2[S];
-#pragma unroll
-    for (int v = 0; v < NV; ++v) {
-      const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a[v]);
-      const __nv_bfloat162* pc = reinterpret_cast<const __nv_bfloat162*>(&c[v]);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 fa = __bfloat1622float2(pa[e]);
-        const float2 fc = __bfloat1622float2(pc[e]);
-        x1[v * 8 + 2 * e] = fa.x;
-        x1[v * 8 + 2 * e + 1] = fa.y;
-        x2[v * 8 + 2 * e] = fc.x;
-        x2[v * 8 + 2 * e + 1] = fc.y;
-      }
-    }
-    // w is uniform over the block (one part per blockIdx.y), so every lane reaches the shuffle.
+    // The values stay packed (two bf16 per register) and are widened where they are used, so that
+    // the next item's loads and this item's arithmetic fit beside each other in registers.
     float r = 1.f;
-    if (w) {
-      float ss = 0.f;
+    if (w) {   // w is uniform over the block (one part per blockIdx.y): every lane reaches the shuffle
+      uint64_t acc = f2_pack(0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < S; ++i) ss += x1[i] * x1[i] + x2[i] * x2[i];
+      for (int v = 0; v < NV; ++v) {
+        const uint32_t wa[4] = {a[v].x, a[v].y, a[v].z, a[v].w}, wc[4] = {c[v].x, c[v].y, c[v].z, c[v].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint64_t xa = f2_pack(__uint_as_float(wa[e] << 16), __uint_as_float(wa[e] & 0xffff0000u));
+          const uint64_t xc = f2_pack(__uint_as_float(wc[e] << 16), __uint_as_float(wc[e] & 0xffff0000u));
+          acc = f2_fma(xa, xa, acc);
+          acc = f2_fma(xc, xc, acc);
+        }
+      }
+      float s0, s1;
+      f2_unpack(acc, s0, s1);
+      float ss = s0 + s1;
 #pragma unroll
       for (int o = 1; o < P; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       r = rsqrtf(ss / (float)D + p.eps);
     }
     if (in_range) {
-      if (valid) {
-        if (w) {
-          const float4* w1 = reinterpret_cast<const float4*>(w + sub * S);
-          const float4* w2 = reinterpret_cast<const float4*>(w + HALF + sub * S);
+      __nv_bfloat16* dst = to.ptr + (int64_t)bl * to.bs + (int64_t)hh * to.hs + (int64_t)r_out * to.rs + sub * S;
+      const bool do_w = valid && w != nullptr, do_rope = valid && rope;
 #pragma unroll
-          for (int v = 0; v < S / 4; ++v) {
-            const float4 wa = __ldg(w1 + v), wc = __ldg(w2 + v);
-            x1[4 * v] *= r * wa.x; x1[4 * v + 1] *= r * wa.y; x1[4 * v + 2] *= r * wa.z; x1[4 * v + 3] *= r * wa.w;
-            x2[4 * v] *= r * wc.x; x2[4 * v + 1] *= r * wc.y; x2[4 * v + 2] *= r * wc.z; x2[4 * v + 3] *= r * wc.w;
+      for (int v = 0; v < NV; ++v) {
+        const uint32_t wa[4] = {a[v].x, a[v].y, a[v].z, a[v].w}, wc[4] = {c[v].x, c[v].y, c[v].z, c[v].w};
+        uint32_t o1[4], o2[4];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {   // four elements of each half at a time
+          float x1[4] = {__uint_as_float(wa[2 * q] << 16), __uint_as_float(wa[2 * q] & 0xffff0000u),
+                         __uint_as_float(wa[2 * q + 1] << 16), __uint_as_float(wa[2 * q + 1] & 0xffff0000u)};
+          float x2[4] = {__uint_as_float(wc[2 * q] << 16), __uint_as_float(wc[2 * q] & 0xffff0000u),
+                         __uint_as_float(wc[2 * q + 1] << 16), __uint_as_float(wc[2 * q + 1] & 0xffff0000u)};
+          const int j = sub * S + v * 8 + q * 4;   // element of the first half
+          if (do_w) {
+            const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + j));
+            const float4 w2 = __ldg(reinterpret_cast<const float4*>(w + HALF + j));
+            x1[0] *= r * w1.x; x1[1] *= r * w1.y; x1[2] *= r * w1.z; x1[3] *= r * w1.w;
+            x2[0] *= r * w2.x; x2[1] *= r * w2.y; x2[2] *= r * w2.z; x2[3] *= r * w2.w;
           }
-        }
-        if (rope) {
-          const float4* cp = reinterpret_cast<const float4*>(p.cs + (int64_t)row * HALF + sub * S);
-          const float4* sp = reinterpret_cast<const float4*>(p.cs + p.sin_off + (int64_t)row * HALF + sub * S);
-#pragma unroll
-          for (int v = 0; v < S / 4; ++v) {
-            const float4 c4 = __ldg(cp + v), s4 = __ldg(sp + v);
+          if (do_rope) {
+            const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cs + (int64_t)row * HALF + j));
+            const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.cs + p.sin_off + (int64_t)row * HALF + j));
             const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float xa = x1[4 * v + e], xc = x2[4 * v + e];
-              x1[4 * v + e] = xa * cc[e] - xc * sn[e];
-              x2[4 * v + e] = xc * cc[e] + xa * sn[e];
+              const float xa = x1[e], xc = x2[e];
+              x1[e] = xa * cc[e] - xc * sn[e];
+              x2[e] = xc * cc[e] + xa * sn[e];
             }
           }
+          o1[2 * q] = pack_bf16x2(x1[0], x1[1]);
+          o1[2 * q + 1] = pack_bf16x2(x1[2], x1[3]);
+          o2[2 * q] = pack_bf16x2(x2[0], x2[1]);
+          o2[2 * q + 1] = pack_bf16x2(x2[2], x2[3]);
         }
-      }
-      __nv_bfloat16* dst = to.ptr + (int64_t)bl * to.bs + (int64_t)hh * to.hs + (int64_t)r_out * to.rs + sub * S;
-#pragma unroll
-      for (int v = 0; v < S / 8; ++v) {
-        uint4 o1, o2;
-        uint32_t* u1 = reinterpret_cast<uint32_t*>(&o1);
-        uint32_t* u2 = reinterpret_cast<uint32_t*>(&o2);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          __nv_bfloat162 t1 = __floats2bfloat162_rn(x1[v * 8 + 2 * e], x1[v * 8 + 2 * e + 1]);
-          __nv_bfloat162 t2 = __floats2bfloat162_rn(x2[v * 8 + 2 * e], x2[v * 8 + 2 * e + 1]);
-          u1[e] = *reinterpret_cast<uint32_t*>(&t1);
-          u2[e] = *reinterpret_cast<uint32_t*>(&t2);
-        }
-        reinterpret_cast<uint4*>(dst)[v] = o1;
-        reinterpret_cast<uint4*>(dst + HALF)[v] = o2;
+        const uint4 u1 = make_uint4(o1[0], o1[1], o1[2], o1[3]), u2 = make_uint4(o2[0], o2[1], o2[2], o2[3]);
+        reinterpret_cast<uint4*>(dst)[v] = u1;
+        reinterpret_cast<uint4*>(dst + HALF)[v] = u2;
       }
     }
 #pragma unroll
@@ -519,6 +645,29 @@ cudaError_t launch_stream(const PrologueParams& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// Lane kernel grid: the blocks of each (part, batch element) stride over its items.
+template <int D>
+cudaError_t launch_lane(const PrologueParams& p, cudaStream_t stream) {
+  const int rows = (!p.skip_q && p.rows[0] > p.rows[1]) ? p.rows[0] : (p.rows[1] > p.rows[2] ? p.rows[1] : p.rows[2]);
+  const int H = (!p.skip_q && p.Hq > p.Hkv) ? p.Hq : p.Hkv;
+  const int groups = (p.skip_q ? 2 : 3) * p.B;
+  if (3LL * p.B > 65535 || p.Hq < 1 || p.Hkv < 1 || (long long)rows * H * 8 >= (1LL << 31)) return cudaErrorInvalidValue;
+  // the stride (blocks * 256 items) must be a multiple of 8 * H for the query and the key heads
+  auto need_blocks = [](int h) { return h / std::gcd(h, 32); };
+  const long long m = std::lcm(need_blocks(p.skip_q ? p.Hkv : p.Hq), need_blocks(p.Hkv));
+#ifndef NSA_LANE_BLOCKS_PER_SM
+#define NSA_LANE_BLOCKS_PER_SM 6
+#endif
+  // six blocks per SM with four resident (measured at config 2: 31.3 us, against 35.4 with one
+  // resident wave and 38.0 with eight per SM)
+  const long long want = std::max(1LL, (long long)device_sm_count() * NSA_LANE_BLOCKS_PER_SM / groups);
+  const long long need = ((long long)rows * H * 8 + 255) / 256;
+  const long long bx = (std::max(1LL, std::min(want, need)) + m - 1) / m * m;
+  if (bx > 0x7FFFFFFFLL / 256) return cudaErrorInvalidValue;
+  prologue_lane_kernel<D><<<dim3((unsigned)bx, groups), 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
 template <int D, int P, typename T>
 cudaError_t launch_vec(const PrologueParams& p, cudaStream_t stream) {
   const int rows = (!p.skip_q && p.rows[0] > p.rows[1]) ? p.rows[0] : (p.rows[1] > p.rows[2] ? p.rows[1] : p.rows[2]);
@@ -541,9 +690,15 @@ cudaError_t launch_vec(const PrologueParams& p, cudaStream_t stream) {
 template <typename T>
 cudaError_t launch_vec_t(const PrologueParams& p, cudaStream_t stream) {
   switch (p.D) {
-    case 64: return launch_vec<64, 2, T>(p, stream);
-    case 96: return launch_vec<96, NSA_PROLOGUE_P96, T>(p, stream);
-    case 128: return launch_vec<128, 2, T>(p, stream);
+    case 64:
+      if constexpr (sizeof(T) == 2) return launch_lane<64>(p, stream);
+      return launch_vec<64, 2, T>(p, stream);
+    case 96:
+      if constexpr (sizeof(T) == 2) return launch_lane<96>(p, stream);
+      return launch_vec<96, NSA_PROLOGUE_P96, T>(p, stream);
+    case 128:
+      if constexpr (sizeof(T) == 2) return launch_lane<128>(p, stream);
+      return launch_vec<128, 2, T>(p, stream);
     case 256:
       if constexpr (sizeof(T) == 2) return launch_stream<256, NSA_PROLOGUE_P256>(p, stream);
       return launch_vec<256, NSA_PROLOGUE_P256, T>(p, stream);
