@@ -256,6 +256,23 @@ typedef struct nsa_proj_desc {
   int32_t text_rows;          /* rows of one element of x_text */
   const void* w_kv;           /* [2*Hkv*D][K] */
   const float* b_kv;          /* [2*Hkv*D] or NULL */
+  /* int8 ConvRot weights (tools/quant.py:48-57): w_qkv / w_kv hold the int8 values as exact bf16
+   * (nsa_expand_i8, once at load) and these the per-row scales, multiplied before the bias (the
+   * reference's "i8" GEMM epilogue, app/gpu/gemm.js:159); x / x_text must be the rotated inputs
+   * (nsa_rotate).  NULL: plain bf16 weights.  Head dims 64, 96 and 128. */
+  const float* w_qkv_scale;
+  const float* w_kv_scale;
+  /* LoRA side paths (app/gpu/ops.js:55-57, 70-86) of each weight, packed by nsa_lora_pack with the
+   * same scales and alpha 1: rank R a multiple of 64 (0: none).  The call first writes T = x A^T into
+   * lora_t (bf16: [b_count][x_rows][R_qkv], then [b_count][text_rows][R_kv]) and then accumulates
+   * T B^T with the weight's product. */
+  int32_t lora_rank_qkv;
+  const void* lora_a_qkv;     /* bf16 [R_qkv][K] */
+  const void* lora_b_qkv;     /* bf16 [(Hq + 2*Hkv)*D][R_qkv] */
+  int32_t lora_rank_kv;
+  const void* lora_a_kv;      /* bf16 [R_kv][K] */
+  const void* lora_b_kv;      /* bf16 [2*Hkv*D][R_kv] */
+  void* lora_t;
 } nsa_proj_desc;
 nsa_status nsa_seq_shard_projection(const nsa_fused_desc* desc, const nsa_seq_shard* shard,
                                     const nsa_proj_desc* proj, const float* q_norm_w, const float* k_norm_w,
@@ -333,6 +350,9 @@ typedef struct nsa_lora_entry {
   float scale;
 } nsa_lora_entry;
 int32_t nsa_lora_rank(const nsa_lora_entry* entries, int32_t count);
+/* int8 weights -> their exact bf16 values (every integer in [-128, 127] is a bf16), for the
+ * projection's ConvRot form: count elements, out 16-byte aligned. */
+nsa_status nsa_expand_i8(const int8_t* W, int64_t count, void* out_bf16, void* stream);
 nsa_status nsa_lora_pack(const nsa_lora_entry* entries, int32_t count, int32_t N, int32_t K, const float* w_scale,
                          float alpha, void* lora_a, void* lora_b, void* stream);
 

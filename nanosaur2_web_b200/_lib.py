@@ -62,7 +62,9 @@ class ProjDesc(ctypes.Structure):
     """nsa_proj_desc (include/nsattn.h)."""
     _fields_ = [("K", _i32), ("x", _vp), ("ldx", _i64), ("x_bstride", _i64), ("x_rows", _i32), ("w_qkv", _vp),
                 ("b_qkv", _vp), ("x_text", _vp), ("ld_text", _i64), ("text_bstride", _i64), ("text_rows", _i32),
-                ("w_kv", _vp), ("b_kv", _vp)]
+                ("w_kv", _vp), ("b_kv", _vp), ("w_qkv_scale", _vp), ("w_kv_scale", _vp), ("lora_rank_qkv", _i32),
+                ("lora_a_qkv", _vp), ("lora_b_qkv", _vp), ("lora_rank_kv", _i32), ("lora_a_kv", _vp),
+                ("lora_b_kv", _vp), ("lora_t", _vp)]
 
 
 class LinearDesc(ctypes.Structure):
@@ -126,6 +128,7 @@ SIGNATURES = {
     "nsa_linear": (_i32, [ctypes.POINTER(LinearDesc), _vp, _vp, _vp, _vp, _vp, _vp]),
     "nsa_rotate": (_i32, [ctypes.POINTER(RotateDesc), _vp, _vp, _vp]),
     "nsa_lora_rank": (_i32, [ctypes.POINTER(LoraEntry), _i32]),
+    "nsa_expand_i8": (_i32, [_vp, _i64, _vp, _vp]),
     "nsa_lora_pack": (_i32, [ctypes.POINTER(LoraEntry), _i32, _i32, _i32, _vp, _f32, _vp, _vp, _vp]),
     "nsa_rmsnorm": (_i32, [ctypes.POINTER(RmsnormDesc), _vp, _vp, _vp, _vp]),
     "nsa_glu": (_i32, [ctypes.POINTER(GluDesc), _vp, _vp, _vp]),

@@ -170,13 +170,18 @@ def dit_block_attention_projected(x: torch.Tensor, *, w_qkv: torch.Tensor, b_qkv
                                   b_kv: Optional[torch.Tensor] = None, kv_len: Optional[torch.Tensor] = None,
                                   bias: Optional[torch.Tensor] = None, eps: float = 1e-6,
                                   out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
-                                  buffers: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
+                                  buffers: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                                  w_qkv_scale: Optional[torch.Tensor] = None, w_kv_scale: Optional[torch.Tensor] = None,
+                                  lora_qkv=None, lora_kv=None) -> torch.Tensor:
     """One DiT block's attention step from its input rows (app/models/nanosaur2.js:196-208):
     x [B, L, K] bf16 (the modulated block input), w_qkv [3*1536, K] bf16 and b_qkv [3*1536] fp32
     (``attn.qkv_x``), x_text [B, text_rows, K] with w_kv [2*1536, K] / b_kv (``attn.kv_y``) for the
     text keys.  kv_len[b] = L + valid text rows; bias [B, text_rows] log prompt weights.
-    ``buffers`` = projection_buffers(...) to reuse across calls.  Returns [B, L, 1536]."""
-    tensors = (x, w_qkv, b_qkv, q_norm, k_norm, x_text, w_kv, b_kv, kv_len, bias, out)
+    ``buffers`` = projection_buffers(...) to reuse across calls.  Returns [B, L, 1536].
+    int8 ConvRot weights: pass ``ops.expand_i8(W)`` as the weight, its row scales as ``w_*_scale``, and
+    rotated inputs (``ops.rotate``).  LoRA side paths: ``ops.lora_pack`` results for either weight
+    (packed with the same scales)."""
+    tensors = (x, w_qkv, b_qkv, q_norm, k_norm, x_text, w_kv, b_kv, kv_len, bias, out, w_qkv_scale, w_kv_scale)
     if any(t is not None and not t.is_cuda for t in tensors):
         raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "tensors must live on a CUDA device")
     if x.dim() != 3 or x.stride(-1) != 1 or x.dtype != torch.bfloat16:
@@ -209,6 +214,21 @@ def dit_block_attention_projected(x: torch.Tensor, *, w_qkv: torch.Tensor, b_qkv
     if x_text is not None:
         p.x_text, p.ld_text, p.text_bstride, p.text_rows = x_text.data_ptr(), x_text.stride(1), x_text.stride(0), text_rows
         p.w_kv, p.b_kv = w_kv.data_ptr(), None if b_kv is None else b_kv.data_ptr()
+    for sc in (w_qkv_scale, w_kv_scale):
+        if sc is not None and (sc.dtype != torch.float32 or not sc.is_contiguous()):
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "weight scales must be contiguous float32")
+    p.w_qkv_scale = None if w_qkv_scale is None else w_qkv_scale.data_ptr()
+    p.w_kv_scale = None if w_kv_scale is None else w_kv_scale.data_ptr()
+    lora_t = None
+    if lora_qkv is not None or (lora_kv is not None and x_text is not None):
+        rq = lora_qkv.R if lora_qkv is not None else 0
+        rk = lora_kv.R if (lora_kv is not None and x_text is not None) else 0
+        lora_t = torch.empty(B * L * rq + B * text_rows * rk, dtype=torch.bfloat16, device=x.device)
+        if rq:
+            p.lora_rank_qkv, p.lora_a_qkv, p.lora_b_qkv = rq, lora_qkv.a.data_ptr(), lora_qkv.b.data_ptr()
+        if rk:
+            p.lora_rank_kv, p.lora_a_kv, p.lora_b_kv = rk, lora_kv.a.data_ptr(), lora_kv.b.data_ptr()
+        p.lora_t = lora_t.data_ptr()
     d.b_begin, d.b_count = 0, B
     L_ = lib()
     with torch.cuda.device(x.device):

@@ -988,6 +988,44 @@ bool encode_sw128(CUtensorMap* map, const void* base, int rank, const cuuint64_t
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D tiled map over a row-major matrix [rows][width] (row pitch `ld` elements of `esz` bytes), boxes
+// of [box_rows][box_cols].
+bool encode_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esz, int64_t width, int64_t rows,
+               int64_t ld, uint32_t box_rows, CUtensorMapSwizzle sw, uint32_t box_cols = 64) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(ld * esz)};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The LoRA factor T = A @ lora_a^T (bf16 [rows][R], row pitch R) with the linear kernel's store form:
+// the first of the two GEMMs the reference runs per side path (app/gpu/ops.js:80).
+cudaError_t run_lora_factor(const void* A, int64_t lda, int rows, int K, const void* lora_a, int R, void* T, int* err,
+                            cudaStream_t strm) {
+  CUtensorMap ta, la, tc;
+  if (!encode_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, rows, lda, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&la, lora_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, R, K, 256, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&tc, T, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, rows, R, 32, CU_TENSOR_MAP_SWIZZLE_128B, 64))
+    return cudaErrorInvalidValue;
+  nsa::LinearParams pt{};
+  pt.M = rows;
+  pt.N = R;
+  pt.k_steps = (K + 63) / 64;
+  pt.m_tiles = (rows + 127) / 128;
+  pt.n_tiles = (R + 255) / 256;
+  pt.alpha = 1.f;
+  pt.C16 = static_cast<__nv_bfloat16*>(T);
+  pt.ldc = R;
+  pt.err = err;
+  pt.timeout_ns = wait_timeout_ns();
+  return profiled("linear_lora_t", 2.0 * rows * (double)R * K, 0.0, strm,
+                  [&] { return nsa::launch_linear(pt, ta, la, ta, la, tc, strm); });
+}
+
 // X map [elements][rows][K] (box [1][128][64]) and W map [N][K] (box [N tile][64]) of one GEMM.
 bool proj_maps(CUtensorMap* tx, CUtensorMap* tw, const void* x, int64_t ld, int64_t bstride, int rows, int b_count,
                const void* w, int K, int N, int n_tile) {
@@ -1038,6 +1076,18 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* d, const nsa_seq_shard
                 "text keys (Lk > Lq) need x_text and w_kv (16-byte aligned, ld_text >= K, multiples of 8)");
   if (text && (int64_t)sp.text_row0 + (pl.Lk - sp.L) > proj->text_rows)
     return fail(NSA_ERR_INVALID_ARGUMENT, "the text rows exceed text_rows");
+  if ((proj->w_qkv_scale || proj->w_kv_scale) && D == 256)
+    return fail(NSA_ERR_UNSUPPORTED, "ConvRot weight scales at head dims 64, 96 and 128 (the Gemma encoder's "
+                                     "640-wide linears are never int8)");
+  if (!a16(proj->w_qkv_scale) || !a16(proj->w_kv_scale))
+    return fail(NSA_ERR_INVALID_ARGUMENT, "weight scales must be 16-byte aligned");
+  const int Rq = proj->lora_rank_qkv, Rk = text ? proj->lora_rank_kv : 0;
+  if (Rq < 0 || Rq % 64 || Rk < 0 || Rk % 64)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "LoRA ranks must be multiples of 64 (0: none)");
+  if ((Rq && (!proj->lora_a_qkv || !proj->lora_b_qkv)) || (Rk && (!proj->lora_a_kv || !proj->lora_b_kv)) ||
+      ((Rq || Rk) && !proj->lora_t) || !a16(proj->lora_a_qkv) || !a16(proj->lora_b_qkv) || !a16(proj->lora_a_kv) ||
+      !a16(proj->lora_b_kv) || !a16(proj->lora_t))
+    return fail(NSA_ERR_INVALID_ARGUMENT, "a LoRA needs 16-byte aligned lora_a, lora_b and the lora_t scratch");
   int* err = nsa::device_error_word();
   if (!err) return fail(NSA_ERR_CUDA, "cannot resolve the device error word on this device");
   const cudaStream_t strm = static_cast<cudaStream_t>(stream);
@@ -1069,6 +1119,39 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* d, const nsa_seq_shard
   pp.err = err;
   pp.timeout_ns = wait_timeout_ns();
 
+  // LoRA factors T = x A^T per set and batch element, into lora_t ([b_count][x_rows][R_qkv], then
+  // [b_count][text_rows][R_kv]), and the maps the kernel's extra K slices read
+  CUtensorMap tt[2], tl[2];
+  auto* T0 = static_cast<__nv_bfloat16*>(proj->lora_t);
+  auto* T1 = T0 ? T0 + (int64_t)pl.Bs * proj->x_rows * Rq : nullptr;
+  auto lora_maps = [&](int si, const void* x, int64_t ld, int64_t bstride, int rows, const void* a, const void* bcat,
+                       int R, __nv_bfloat16* T, int N) -> nsa_status {
+    for (int bl = 0; bl < pl.Bs; ++bl) {
+      cudaError_t e = run_lora_factor(static_cast<const __nv_bfloat16*>(x) + (int64_t)(pl.b0 + bl) * bstride, ld, rows,
+                                      K, a, R, T + (int64_t)bl * rows * R, err, strm);
+      if (e != cudaSuccess) return cuda_fail(e, "LoRA factor launch");
+    }
+    const cuuint64_t td[3] = {(cuuint64_t)R, (cuuint64_t)rows, (cuuint64_t)pl.Bs};
+    const cuuint64_t ts[2] = {(cuuint64_t)R * 2, (cuuint64_t)rows * R * 2};
+    const cuuint32_t tb[3] = {64, 128, 1};
+    const cuuint64_t ld2[2] = {(cuuint64_t)R, (cuuint64_t)N};
+    const cuuint64_t ls[1] = {(cuuint64_t)R * 2};
+    const cuuint32_t lb[2] = {64, (cuuint32_t)(hpt * D)};
+    if (!encode_sw128(&tt[si], T, 3, td, ts, tb) || !encode_sw128(&tl[si], bcat, 2, ld2, ls, lb))
+      return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the LoRA operands");
+    return NSA_OK;
+  };
+  if (Rq) {
+    nsa_status ls = lora_maps(0, proj->x, proj->ldx, proj->x_bstride, proj->x_rows, proj->lora_a_qkv,
+                              proj->lora_b_qkv, Rq, T0, (d->Hq + 2 * d->Hkv) * D);
+    if (ls != NSA_OK) return ls;
+  }
+  if (Rk) {
+    nsa_status ls = lora_maps(1, proj->x_text, proj->ld_text, proj->text_bstride, proj->text_rows, proj->lora_a_kv,
+                              proj->lora_b_kv, Rk, T1, 2 * d->Hkv * D);
+    if (ls != NSA_OK) return ls;
+  }
+
   // set 0, the image rows: q|k|v of the shard's own rows, q' rows past them zero
   CUtensorMap tx[2], tw[2];
   const auto* x0 = static_cast<const __nv_bfloat16*>(proj->x) + (int64_t)pl.b0 * proj->x_bstride;
@@ -1085,8 +1168,10 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* d, const nsa_seq_shard
   img.x_row0 = sp.img_row0;
   img.rope_row0 = sp.q_begin;
   img.bias = proj->b_qkv;
+  img.w_scale = proj->w_qkv_scale;
+  img.lora_steps = Rq / 64;
   pp.n_sets = 1;
-  double flops = 2.0 * pl.Bs * sp.q_count * (double)(d->Hq + 2 * d->Hkv) * D * K;
+  double flops = 2.0 * pl.Bs * sp.q_count * (double)(d->Hq + 2 * d->Hkv) * D * (K + Rq);
   // set 1, the text rows (every rank computes them) and the zero padding up to kv_rows
   if (text) {
     const auto* t0 = static_cast<const __nv_bfloat16*>(proj->x_text) + (int64_t)pl.b0 * proj->text_bstride;
@@ -1103,8 +1188,10 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* d, const nsa_seq_shard
     txt.x_row0 = sp.text_row0;
     txt.rope_row0 = 0;
     txt.bias = proj->b_kv;
+    txt.w_scale = proj->w_kv_scale;
+    txt.lora_steps = Rk / 64;
     pp.n_sets = 2;
-    flops += 2.0 * pl.Bs * (pl.Lk - sp.L) * (double)(2 * d->Hkv) * D * K;
+    flops += 2.0 * pl.Bs * (pl.Lk - sp.L) * (double)(2 * d->Hkv) * D * (K + Rk);
   }
   // head dim 256: the RoPE table as a [2 * rows][128] fp32 map (cos block, then sin block), boxes of
   // [32 rows][16 values] with the 64-byte swizzle, for the epilogue's per-warp staging
@@ -1125,7 +1212,7 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* d, const nsa_seq_shard
     }
   }
   cudaError_t e = profiled("projection", flops, 0.0, strm,
-                           [&] { return nsa::launch_projection(pp, D, tx, tw, tcs_ptr, strm); });
+                           [&] { return nsa::launch_projection(pp, D, tx, tw, tcs_ptr, tt, tl, strm); });
   if (e == cudaErrorNotSupported)
     return fail(NSA_ERR_UNSUPPORTED, "the projection's bias vectors do not fit in shared memory");
   if (e != cudaSuccess) return cuda_fail(e, "projection launch");
@@ -1176,14 +1263,7 @@ nsa_status nsa_linear(const nsa_linear_desc* d, const void* A, const void* W, co
   // A [M][K] bf16 and W [N][K] (bf16 swizzled for the MMA, or int8 plain rows for the converters)
   auto map2d = [](CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esz, int64_t width, int64_t rows,
                   int64_t ld, uint32_t box_rows, CUtensorMapSwizzle sw, uint32_t box_cols = 64) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)(ld * esz)};
-    const cuuint32_t box[2] = {box_cols, box_rows};
-    const cuuint32_t estr[2] = {1, 1};
-    return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return encode_2d(m, base, dt, esz, width, rows, ld, box_rows, sw, box_cols);
   };
   const auto BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
@@ -1202,15 +1282,7 @@ nsa_status nsa_linear(const nsa_linear_desc* d, const void* A, const void* W, co
   CUtensorMap ta, tw, tt, tl, tc;
   if (R) {
     // T = A @ lora_a^T, bf16 [M][R]: the LoRA's first factor, one small GEMM before the main one
-    CUtensorMap la;
-    if (!map2d(&ta, A, BF, 2, d->K, d->M, d->lda, 128, SW) || !map2d(&la, d->lora_a, BF, 2, d->K, R, d->K, 256, SW) ||
-        !map2d(&tc, d->lora_t, BF, 2, R, d->M, R, 32, SW, 64))
-      return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the LoRA operands");
-    nsa::LinearParams pt = base_params(d->M, R, d->K);
-    pt.C16 = static_cast<__nv_bfloat16*>(d->lora_t);
-    pt.ldc = R;
-    cudaError_t e = profiled("linear_lora_t", 2.0 * d->M * (double)R * d->K, 0.0, strm,
-                             [&] { return nsa::launch_linear(pt, ta, la, ta, la, tc, strm); });
+    cudaError_t e = run_lora_factor(A, d->lda, d->M, d->K, d->lora_a, R, d->lora_t, err, strm);
     if (e != cudaSuccess) return cuda_fail(e, "LoRA factor launch");
   }
   bool ok = map2d(&ta, A, BF, 2, d->K, d->M, d->lda, 128, SW) &&
@@ -1273,6 +1345,15 @@ nsa_status nsa_rotate(const nsa_rotate_desc* d, const void* X, void* Y, void* st
   cudaError_t e = profiled("rotate", 0.0, (double)d->rows * d->cols * (ei + eo), strm,
                            [&] { return nsa::launch_rotate(p, strm); });
   if (e != cudaSuccess) return cuda_fail(e, "rotate launch");
+  return NSA_OK;
+}
+
+nsa_status nsa_expand_i8(const int8_t* W, int64_t count, void* out_bf16, void* stream) {
+  if (count < 0) return fail(NSA_ERR_INVALID_ARGUMENT, "count must be >= 0");
+  if (count == 0) return NSA_OK;
+  if (!W || !out_bf16 || !aligned16(out_bf16)) return fail(NSA_ERR_INVALID_ARGUMENT, "W and a 16-byte aligned out");
+  cudaError_t e = nsa::launch_expand_i8(W, count, static_cast<__nv_bfloat16*>(out_bf16), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "expand_i8 launch");
   return NSA_OK;
 }
 

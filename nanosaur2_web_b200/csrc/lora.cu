@@ -9,6 +9,7 @@
 //                 entry's output columns, zero elsewhere,
 // so that x A_cat^T is one small GEMM and the delta is R more K steps of the main GEMM, whose epilogue
 // multiplies by alpha * rowScale[n] (rowScale = 1 for bf16 weights).  A strength change re-packs B_cat.
+// Also here: the exact bf16 expansion of int8 weights that the projection's ConvRot form takes.
 #include "nsa_internal.h"
 
 namespace nsa {
@@ -30,6 +31,11 @@ __global__ void lora_pack_b_kernel(const float* __restrict__ B, int r, int off, 
   }
 }
 
+__global__ void expand_i8_kernel(const int8_t* __restrict__ w, long long count, __nv_bfloat16* __restrict__ out) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < count; i += (long long)gridDim.x * blockDim.x)
+    out[i] = __float2bfloat16_rn((float)w[i]);   // exact: |w| <= 128
+}
+
 int blocks_for(long long count) {
   const long long b = (count + 255) / 256;
   const long long cap = (long long)device_sm_count() * 8;
@@ -37,6 +43,12 @@ int blocks_for(long long count) {
 }
 
 }  // namespace
+
+cudaError_t launch_expand_i8(const int8_t* w, long long count, __nv_bfloat16* out, cudaStream_t stream) {
+  if (count <= 0) return cudaSuccess;
+  expand_i8_kernel<<<blocks_for(count), 256, 0, stream>>>(w, count, out);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_lora_pack(const LoraPackEntry* e, int count, int N, int K, int R, const float* w_scale, float alpha,
                              __nv_bfloat16* a_cat, __nv_bfloat16* b_cat, cudaStream_t stream) {

@@ -154,6 +154,8 @@ struct ProjSet {
   int x_row0;              // input row of GEMM row 0
   int rope_row0;           // RoPE table row of GEMM row 0 (image: q_begin)
   const float* bias;       // [n_tiles * heads-per-tile * D] or null
+  const float* w_scale;    // per-row weight scales (int8 ConvRot weights given as bf16) or null
+  int lora_steps;          // 64-wide LoRA K slices after the K/64 of x and W (tmT / tmL of the set)
 };
 struct ProjParams {
   int B, b_begin;          // batch elements of the call and the first one's global index
@@ -182,8 +184,11 @@ struct ProjParams {
 // D in {64, 96, 128, 256}; cudaErrorInvalidValue otherwise, cudaErrorNotSupported when the bias
 // vectors leave no room for a 2-stage ring.  tmX[s]: 3-D map [B][rows][K] over set s's input, box
 // [1][128][64], 128-byte swizzle; tmW[s]: 2-D map [N][K], box [heads-per-tile * D][64].
+// tmT[s] / tmL[s]: set s's LoRA operands (3-D map [B][x rows][R] over T, box [1][128][64]; 2-D map
+// [N][R] over B_cat, box [N tile][64]), read only when set[s].lora_steps > 0.
 cudaError_t launch_projection(ProjParams p, int D, const CUtensorMap* tmX, const CUtensorMap* tmW,
-                              const CUtensorMap* tmCS, cudaStream_t stream);
+                              const CUtensorMap* tmCS, const CUtensorMap* tmT, const CUtensorMap* tmL,
+                              cudaStream_t stream);
 int projection_heads_per_tile(int D);   // 0: unsupported head dim
 
 // Linear layer with the reference's GEMM epilogue (linear.cu): C = epilogue(alpha * A W^T) over M x N
@@ -233,6 +238,7 @@ struct LoraPackEntry {
   int r, off, n;
   float scale;
 };
+cudaError_t launch_expand_i8(const int8_t* w, long long count, __nv_bfloat16* out, cudaStream_t stream);
 cudaError_t launch_lora_pack(const LoraPackEntry* e, int count, int N, int K, int R, const float* w_scale, float alpha,
                              __nv_bfloat16* a_cat, __nv_bfloat16* b_cat, cudaStream_t stream);
 

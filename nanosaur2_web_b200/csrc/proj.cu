@@ -61,6 +61,19 @@ __device__ __forceinline__ void lds16(const float* src, float (&o)[16]) {
   }
 }
 
+// 16 consecutive floats of a global vector (the per-row weight scales of int8 ConvRot weights); all
+// lanes of a warp read the same addresses.
+__device__ __forceinline__ void ldg16(const float* src, float (&o)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(src) + q);
+    o[4 * q] = v.x;
+    o[4 * q + 1] = v.y;
+    o[4 * q + 2] = v.z;
+    o[4 * q + 3] = v.w;
+  }
+}
+
 __device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, const float (&v)[16]) {
   uint4 o[2];
   uint32_t* u = reinterpret_cast<uint32_t*>(o);
@@ -74,7 +87,9 @@ template <int D>
 __global__ void __launch_bounds__(kProjThreads, 1)
     proj_kernel(const __grid_constant__ CUtensorMap tmX0, const __grid_constant__ CUtensorMap tmW0,
                 const __grid_constant__ CUtensorMap tmX1, const __grid_constant__ CUtensorMap tmW1,
-                const __grid_constant__ CUtensorMap tmCS, const ProjParams p) {
+                const __grid_constant__ CUtensorMap tmCS, const __grid_constant__ CUtensorMap tmT0,
+                const __grid_constant__ CUtensorMap tmL0, const __grid_constant__ CUtensorMap tmT1,
+                const __grid_constant__ CUtensorMap tmL1, const ProjParams p) {
   using C = ProjCfg<D>;
   const int S = p.stages;
   extern __shared__ uint8_t smem_raw[];
@@ -180,7 +195,8 @@ __global__ void __launch_bounds__(kProjThreads, 1)
       for (int u = blockIdx.x; ok && u < tiles; u += G) {
         int si, bl, m0, nt, part, h0;
         if (!decode(u, si, bl, m0, nt, part, h0)) continue;
-        for (int ks = 0; ks < p.k_steps; ++ks, ++step) {
+        const int steps = p.k_steps + p.set[si].lora_steps;
+        for (int ks = 0; ks < steps; ++ks, ++step) {
           const int s = step % S;
           if (step >= S &&
               !wait_bounded(&empty[s], ((step / S) - 1) & 1, abort_flag, p.err, kErrTimeoutProjection, to)) {
@@ -189,8 +205,14 @@ __global__ void __launch_bounds__(kProjThreads, 1)
           }
           uint8_t* st = smem + s * C::STAGE;
           mbar_arrive_expect_tx(&full[s], C::STAGE);
-          tma_load_3d(st, si ? &tmX1 : &tmX0, &full[s], ks * kProjBK, p.set[si].x_row0 + m0, bl);
-          tma_load_2d(st + C::A_BYTES, si ? &tmW1 : &tmW0, &full[s], ks * kProjBK, nt * C::NT);
+          if (ks < p.k_steps) {
+            tma_load_3d(st, si ? &tmX1 : &tmX0, &full[s], ks * kProjBK, p.set[si].x_row0 + m0, bl);
+            tma_load_2d(st + C::A_BYTES, si ? &tmW1 : &tmW0, &full[s], ks * kProjBK, nt * C::NT);
+          } else {   // LoRA slices: T rows (same row index as x) against B_cat rows
+            const int kl = (ks - p.k_steps) * kProjBK;
+            tma_load_3d(st, si ? &tmT1 : &tmT0, &full[s], kl, p.set[si].x_row0 + m0, bl);
+            tma_load_2d(st + C::A_BYTES, si ? &tmL1 : &tmL0, &full[s], kl, nt * C::NT);
+          }
         }
       }
       // copies still landing complete before the CTA may exit
@@ -212,7 +234,8 @@ __global__ void __launch_bounds__(kProjThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem + (uint32_t)a * C::ACC_COLS;
-        for (int ks = 0; ks < p.k_steps; ++ks, ++step) {
+        const int steps = p.k_steps + p.set[si].lora_steps;
+        for (int ks = 0; ks < steps; ++ks, ++step) {
           const int s = step % S;
           if (!wait_bounded(&full[s], (step / S) & 1, abort_flag, p.err, kErrTimeoutProjection, to)) {
             ok = false;
@@ -311,6 +334,11 @@ __global__ void __launch_bounds__(kProjThreads, 1)
         const int h = h0 + hh;
         const uint32_t col0 = (uint32_t)(hh * D);
         const float* bias = sbias + nt * C::NT + hh * D;
+        // int8 ConvRot weights (given as their exact bf16 values): the row scales of this head's columns.
+        // Not at head dim 256: that is the Gemma encoder, whose 640-wide linears are never ConvRot
+        // weights (the quantiser needs K % 256 == 0, tools/quant.py:43-44), and its epilogue has no
+        // registers to spare.
+        const float* wsc = (D != 256 && q.w_scale) ? q.w_scale + nt * C::NT + hh * D : nullptr;
         // pass 1: sum of squares of (acc + bias) over the head (tcgen05.ld is warp-wide: every lane),
         // in wide loads: each load's wait is a round trip of the order of a thousand cycles while the
         // MMAs of the next tile write tensor memory
@@ -329,10 +357,20 @@ __global__ void __launch_bounds__(kProjThreads, 1)
             for (int i0 = 0; i0 < W1; i0 += 16) {
               float bb[16];
               lds16(bias + c + i0, bb);
+              if (wsc) {
+                float ws[16];
+                ldg16(wsc + c + i0, ws);
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const float x = __uint_as_float(v[i0 + i]) + bb[i];
-                ss = fmaf(x, x, ss);
+                for (int i = 0; i < 16; ++i) {
+                  const float x = fmaf(__uint_as_float(v[i0 + i]), ws[i], bb[i]);
+                  ss = fmaf(x, x, ss);
+                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const float x = __uint_as_float(v[i0 + i]) + bb[i];
+                  ss = fmaf(x, x, ss);
+                }
               }
             }
           }
@@ -386,10 +424,21 @@ __global__ void __launch_bounds__(kProjThreads, 1)
           float x1[16], x2[16], b1[16], b2[16];
           lds16(bias + c, b1);
           lds16(bias + D / 2 + c, b2);
+          if (wsc) {
+            float s1[16], s2[16];
+            ldg16(wsc + c, s1);
+            ldg16(wsc + D / 2 + c, s2);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            x1[i] = __uint_as_float(v1[i]) + b1[i];
-            x2[i] = __uint_as_float(v2[i]) + b2[i];
+            for (int i = 0; i < 16; ++i) {
+              x1[i] = fmaf(__uint_as_float(v1[i]), s1[i], b1[i]);
+              x2[i] = fmaf(__uint_as_float(v2[i]), s2[i], b2[i]);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              x1[i] = __uint_as_float(v1[i]) + b1[i];
+              x2[i] = __uint_as_float(v2[i]) + b2[i];
+            }
           }
           if (wn) {
             lds16(wn + c, b1);
@@ -438,7 +487,7 @@ __global__ void __launch_bounds__(kProjThreads, 1)
 
 template <int D>
 cudaError_t launch_proj_d(ProjParams p, const CUtensorMap* tmX, const CUtensorMap* tmW, const CUtensorMap* tmCS,
-                          cudaStream_t stream) {
+                          const CUtensorMap* tmT, const CUtensorMap* tmL, cudaStream_t stream) {
   using C = ProjCfg<D>;
   const int sms = device_sm_count();
   long long tiles = 0;
@@ -470,8 +519,12 @@ cudaError_t launch_proj_d(ProjParams p, const CUtensorMap* tmX, const CUtensorMa
   });
   if (e != cudaSuccess) return e;
   const int grid = tiles < sms ? (int)tiles : sms;
-  proj_kernel<D><<<grid, kProjThreads, smem, stream>>>(tmX[0], tmW[0], tmX[p.n_sets > 1 ? 1 : 0],
-                                                       tmW[p.n_sets > 1 ? 1 : 0], p.cs_tma ? *tmCS : tmX[0], p);
+  const int s1 = p.n_sets > 1 ? 1 : 0;
+  // sets without a LoRA pass their x / W maps in the T / B_cat slots (never loaded)
+  proj_kernel<D><<<grid, kProjThreads, smem, stream>>>(
+      tmX[0], tmW[0], tmX[s1], tmW[s1], p.cs_tma ? *tmCS : tmX[0], p.set[0].lora_steps ? tmT[0] : tmX[0],
+      p.set[0].lora_steps ? tmL[0] : tmW[0], p.set[s1].lora_steps ? tmT[s1] : tmX[s1],
+      p.set[s1].lora_steps ? tmL[s1] : tmW[s1], p);
   return cudaGetLastError();
 }
 
@@ -488,12 +541,13 @@ int projection_heads_per_tile(int D) {
 }
 
 cudaError_t launch_projection(ProjParams p, int D, const CUtensorMap* tmX, const CUtensorMap* tmW,
-                              const CUtensorMap* tmCS, cudaStream_t stream) {
+                              const CUtensorMap* tmCS, const CUtensorMap* tmT, const CUtensorMap* tmL,
+                              cudaStream_t stream) {
   switch (D) {
-    case 64: return launch_proj_d<64>(p, tmX, tmW, tmCS, stream);
-    case 96: return launch_proj_d<96>(p, tmX, tmW, tmCS, stream);
-    case 128: return launch_proj_d<128>(p, tmX, tmW, tmCS, stream);
-    case 256: return launch_proj_d<256>(p, tmX, tmW, tmCS, stream);
+    case 64: return launch_proj_d<64>(p, tmX, tmW, tmCS, tmT, tmL, stream);
+    case 96: return launch_proj_d<96>(p, tmX, tmW, tmCS, tmT, tmL, stream);
+    case 128: return launch_proj_d<128>(p, tmX, tmW, tmCS, tmT, tmL, stream);
+    case 256: return launch_proj_d<256>(p, tmX, tmW, tmCS, tmT, tmL, stream);
     default: return cudaErrorInvalidValue;
   }
 }

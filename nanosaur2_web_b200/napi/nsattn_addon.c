@@ -17,6 +17,8 @@
  *   rotate(opts)           ops.rotate(gpu, x) (ops.js:38-45)                -> nsa_rotate
  *   loraPack(opts)         the LoRA side paths of one weight (app/lora.js:143-150), entries
  *                          [{A, B, r, off, n, scale}]; returns the packed rank R -> nsa_lora_pack
+ *   expandI8(opts)         int8 weights -> exact bf16 values (the projection's ConvRot form)
+ *                                                                        -> nsa_expand_i8
  *   rmsnorm(opts)          ops.rmsnorm(gpu, x, weight, cols, eps, out) (ops.js:111-116)
  *   glu(opts)              ops.glu(gpu, x, act) (ops.js:141-148)
  *   rope2dTable(opts) / ropeTable(opts)   common.js:28-43 / 18-24 into a device buffer
@@ -302,6 +304,13 @@ static napi_value Rotate(napi_env env, napi_callback_info info) {
   return done(env, nsa_rotate(&d, ptr(env, o, "x"), ptr(env, o, "out"), ptr(env, o, "stream")));
 }
 
+static napi_value ExpandI8(napi_env env, napi_callback_info info) {
+  napi_value o = opts_arg(env, info);
+  if (!o) return NULL;
+  return done(env, nsa_expand_i8((const int8_t*)ptr(env, o, "W"), num(env, o, "count", 0), ptr(env, o, "out"),
+                                 ptr(env, o, "stream")));
+}
+
 #define NSA_ADDON_MAX_LORAS 64
 
 static napi_value LoraPack(napi_env env, napi_callback_info info) {
@@ -378,6 +387,7 @@ static napi_value Init(napi_env env, napi_value exports) {
   export_fn(env, exports, "glu", Glu);
   export_fn(env, exports, "rotate", Rotate);
   export_fn(env, exports, "loraPack", LoraPack);
+  export_fn(env, exports, "expandI8", ExpandI8);
   export_fn(env, exports, "rope2dTable", Rope2dTable);
   export_fn(env, exports, "ropeTable", RopeTable);
   export_fn(env, exports, "checkDevice", CheckDevice);

@@ -26,7 +26,7 @@ import torch
 from . import _lib
 from ._lib import NSA_BF16, NSA_F32, AttentionDesc, NsaError, check, lib
 
-__all__ = ["attention", "headNorm", "linear", "lora_pack", "LoraPack", "rotate", "rmsnorm", "glu", "rope2dTable", "ropeTable", "RopeTable", "NsaError",
+__all__ = ["attention", "headNorm", "linear", "lora_pack", "LoraPack", "rotate", "expand_i8", "rmsnorm", "glu", "rope2dTable", "ropeTable", "RopeTable", "NsaError",
            "dtype_code", "stream_handle", "check_device"]
 
 
@@ -151,6 +151,18 @@ def lora_pack(entries, N: int, K: int, *, w_scale: Optional[torch.Tensor] = None
         check(lib().nsa_lora_pack(arr, len(entries), N, K, _ptr(w_scale), float(alpha), a.data_ptr(), b.data_ptr(),
                                   stream_handle(dev)))
     return LoraPack(a, b, R, N, K, float(alpha), w_scale)
+
+
+def expand_i8(W: torch.Tensor) -> torch.Tensor:
+    """int8 weights -> their exact bf16 values (nsa_expand_i8), the form the QKV projection takes
+    ConvRot weights in (with their row scales passed separately)."""
+    _require_cuda(W)
+    if W.dtype != torch.int8 or not W.is_contiguous():
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "W must be a contiguous int8 tensor")
+    out = torch.empty(W.shape, dtype=torch.bfloat16, device=W.device)
+    with torch.cuda.device(W.device):
+        check(lib().nsa_expand_i8(W.data_ptr(), W.numel(), out.data_ptr(), stream_handle(W.device)))
+    return out
 
 
 def rotate(x: torch.Tensor, out: Optional[torch.Tensor] = None, *,

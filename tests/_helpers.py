@@ -6,6 +6,8 @@ from __future__ import annotations
 
 import numpy as np
 
+from oracle import attention_oracle as O
+
 BF16_MAX_ABS = 2e-2
 BF16_MIN_COS = 0.9999
 
@@ -68,3 +70,25 @@ def gemma_inputs(seed: int, B: int, L: int, bf16: bool = True):
     q_w = (1.0 + 0.2 * rng.standard_normal(256)).astype(np.float32)
     k_w = (1.0 + 0.2 * rng.standard_normal(256)).astype(np.float32)
     return qkv, q_w, k_w
+
+
+def lora_oracle(xr, q_or_w, scale, b, entries, N, alpha=1.0):
+    """The oracle's linear (oracle.linear / linear_int8) plus LoRA side paths, with the bf16 roundings
+    of the packed side path (nsa_lora_pack, the T factor) emulated.  Returns the
+    result and a bound on what one bf16 step of each T element (whose rounding the GPU takes after its
+    own fp32 summation order) can move it: sum_j |T[m][j]| 2^-8 |B_eff[n][j]|."""
+    a_cat = np.concatenate([bf16_round(e["A"]) for e in entries])
+    T = bf16_round((np.asarray(xr, np.float64) @ a_cat.astype(np.float64).T).astype(np.float32)).astype(np.float64)
+    y = (O.linear_int8(xr, q_or_w, scale, acc=np.float64) if scale is not None
+         else O.linear(xr, q_or_w, acc=np.float64)) * alpha
+    bound = np.zeros_like(y)
+    r0 = 0
+    for e in entries:
+        r = e["A"].shape[0]
+        off = int(e.get("off", 0))
+        den = alpha * (scale[off:off + e["B"].shape[0], None].astype(np.float64) if scale is not None else 1.0)
+        bq = bf16_round((e["scale"] * e["B"].astype(np.float64) / den).astype(np.float32)).astype(np.float64) * den
+        y[:, off:off + bq.shape[0]] += T[:, r0:r0 + r] @ bq.T
+        bound[:, off:off + bq.shape[0]] += (np.abs(T[:, r0:r0 + r]) * 2 ** -8) @ np.abs(bq).T
+        r0 += r
+    return (y + b if b is not None else y), bound

@@ -8,7 +8,7 @@ import pytest
 import torch
 
 from oracle import attention_oracle as O
-from tests._helpers import bf16_round
+from tests._helpers import bf16_round, lora_oracle as _lora_oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -125,27 +125,6 @@ def test_int8_convrot_linear_golden(golden):
     np.testing.assert_allclose(y.cpu().numpy(), want, rtol=1e-4, atol=1e-4)
     # end to end against the reference's fp32 result: the bf16 rounding of the rotated input
     np.testing.assert_allclose(y.cpu().numpy(), g["y_base"], rtol=1e-2, atol=2e-2)
-
-
-def _lora_oracle(xr, q_or_w, scale, b, entries, N, alpha=1.0):
-    """The oracle's linear with the bf16 roundings of the packed side path emulated.  Returns the
-    result and a bound on what one bf16 step of each T element (whose rounding the GPU takes after its
-    own fp32 summation order) can move it: sum_j |T[m][j]| 2^-8 |B_eff[n][j]|."""
-    a_cat = np.concatenate([bf16_round(e["A"]) for e in entries])
-    T = bf16_round((np.asarray(xr, np.float64) @ a_cat.astype(np.float64).T).astype(np.float32)).astype(np.float64)
-    y = (O.linear_int8(xr, q_or_w, scale, acc=np.float64) if scale is not None
-         else O.linear(xr, q_or_w, acc=np.float64)) * alpha
-    bound = np.zeros_like(y)
-    r0 = 0
-    for e in entries:
-        r = e["A"].shape[0]
-        off = int(e.get("off", 0))
-        den = alpha * (scale[off:off + e["B"].shape[0], None].astype(np.float64) if scale is not None else 1.0)
-        bq = bf16_round((e["scale"] * e["B"].astype(np.float64) / den).astype(np.float32)).astype(np.float64) * den
-        y[:, off:off + bq.shape[0]] += T[:, r0:r0 + r] @ bq.T
-        bound[:, off:off + bq.shape[0]] += (np.abs(T[:, r0:r0 + r]) * 2 ** -8) @ np.abs(bq).T
-        r0 += r
-    return (y + b if b is not None else y), bound
 
 
 def assert_close_with_bound(got, want, bound, rtol=1e-3, atol=2e-3):

@@ -253,3 +253,86 @@ def test_gemma_projected_unaligned_sin_block():
     qkv = O.linear(x[0], w, acc=np.float64)
     want = O.gemma_attention(qkv[:, :4 * GD], qkv[:, 4 * GD:5 * GD], qkv[:, 5 * GD:], q_w, k_w, theta, acc=np.float64)
     assert_close_bf16(out[0].cpu().numpy(), want, GD, what="gemma projected, sin block off the row grid")
+
+
+def test_projected_block_int8_convrot_with_loras():
+    """The projection with int8 ConvRot weights (given as their exact bf16 values, ops.expand_i8, with
+    the row scales in the epilogue: app/gpu/gemm.js:159) and LoRA side paths on both weights: on
+    w_qkv a full-width entry and one on the q slice only, on w_kv one full-width entry (app/lora.js:149
+    off / n).  The inputs stand for rotated rows (the rotation itself is tested with nsa_rotate).  The
+    oracle builds q|k|v with the int8 GEMM plus the side paths (the packed bf16 roundings emulated)
+    and runs the DiT block's head norms, RoPE and joint attention on them."""
+    from nanosaur2_web_b200.blocks import dit_block_attention_projected
+    from nanosaur2_web_b200.ops import expand_i8, lora_pack, rope2dTable
+    from tests._helpers import lora_oracle
+    rng = np.random.default_rng(123)
+    h, wd, Lt, B, K = 12, 20, 32, 2, 512
+    L = h * wd
+    x = bf16_round(rng.standard_normal((B, L, K), dtype=np.float32))
+    xt = bf16_round(rng.standard_normal((B, Lt, K), dtype=np.float32))
+    q8 = rng.integers(-128, 128, size=(3 * C, K), dtype=np.int8)
+    kv8 = rng.integers(-128, 128, size=(2 * C, K), dtype=np.int8)
+    sq = (rng.uniform(0.5, 2.0, 3 * C) / (127 * np.sqrt(K / 3))).astype(np.float32)
+    skv = (rng.uniform(0.5, 2.0, 2 * C) / (127 * np.sqrt(K / 3))).astype(np.float32)
+    b = (0.1 * rng.standard_normal(3 * C)).astype(np.float32)
+    bkv = (0.1 * rng.standard_normal(2 * C)).astype(np.float32)
+    q_w = (1.0 + 0.2 * rng.standard_normal(D)).astype(np.float32)
+    k_w = (1.0 + 0.2 * rng.standard_normal(D)).astype(np.float32)
+    lv = np.array([20, 32], np.int32)
+    bias = np.log(rng.choice(np.array([0.7, 1.0, 1.3], np.float32), size=(B, Lt))).astype(np.float32)
+    ent_q = [dict(A=rng.standard_normal((16, K), dtype=np.float32) / 30, B=rng.standard_normal((3 * C, 16), dtype=np.float32) / 4,
+                  scale=0.6, off=0, n=3 * C),
+             dict(A=rng.standard_normal((8, K), dtype=np.float32) / 30, B=rng.standard_normal((C, 8), dtype=np.float32) / 4,
+                  scale=-0.4, off=0, n=C)]
+    ent_kv = [dict(A=rng.standard_normal((32, K), dtype=np.float32) / 30, B=rng.standard_normal((2 * C, 32), dtype=np.float32) / 4,
+                   scale=0.5, off=0, n=2 * C)]
+    sq_t, skv_t = t(sq), t(skv)
+    pk_q = lora_pack([dict(e, A=t(e["A"]), B=t(e["B"])) for e in ent_q], 3 * C, K, w_scale=sq_t)
+    pk_kv = lora_pack([dict(e, A=t(e["A"]), B=t(e["B"])) for e in ent_kv], 2 * C, K, w_scale=skv_t)
+    out = dit_block_attention_projected(
+        t(x, torch.bfloat16), w_qkv=expand_i8(t(q8, torch.int8)), b_qkv=t(b), q_norm=t(q_w), k_norm=t(k_w),
+        cs=rope2dTable(h, wd, D, DEV), x_text=t(xt, torch.bfloat16), w_kv=expand_i8(t(kv8, torch.int8)), b_kv=t(bkv),
+        kv_len=t(L + lv, torch.int32), bias=t(bias), out_dtype=torch.float32, w_qkv_scale=sq_t, w_kv_scale=skv_t,
+        lora_qkv=pk_q, lora_kv=pk_kv)
+    check_device()
+    qkv = np.zeros((B, L + Lt, 3 * C), np.float64)
+    for bb in range(B):
+        qkv[bb, :L] = lora_oracle(x[bb], q8, sq, b, ent_q, 3 * C)[0]
+        qkv[bb, L:, C:] = lora_oracle(xt[bb], kv8, skv, bkv, ent_kv, 2 * C)[0]
+    cos, sin = O.rope_2d(h, wd)
+    want = O.joint_attention_batched(qkv, L, Lt, L + lv, q_w, k_w, cos, sin, bias=bias, acc=np.float64)
+    assert_close_bf16(out.cpu().numpy(), want, D, what="int8 ConvRot projection with LoRAs")
+    # the side paths matter at this size: without them the result is far outside the bound
+    qkv0 = np.zeros_like(qkv)
+    for bb in range(B):
+        qkv0[bb, :L] = O.linear_int8(x[bb], q8, sq, b, acc=np.float64)
+        qkv0[bb, L:, C:] = O.linear_int8(xt[bb], kv8, skv, bkv, acc=np.float64)
+    base = O.joint_attention_batched(qkv0, L, Lt, L + lv, q_w, k_w, cos, sin, bias=bias, acc=np.float64)
+    assert np.abs(base - want).max() > 10 * np.abs(out.cpu().numpy() - want).max()
+
+
+def test_projection_rejects_scales_at_head_dim_256():
+    from nanosaur2_web_b200 import _lib
+    from nanosaur2_web_b200.blocks import gemma_projection_buffers  # noqa: F401  (module import only)
+    d = _lib.FusedDesc()
+    d.B, d.Lq, d.Lk, d.Hq, d.Hkv, d.D = 1, 128, 128, 4, 1, 256
+    d.in_dtype = d.out_dtype = _lib.NSA_BF16
+    d.causal = 1
+    d.b_begin, d.b_count = 0, 1
+    s = _lib.SeqShard(0, 128, 0, 0)
+    p = _lib.ProjDesc()
+    x = torch.zeros((128, 640), dtype=torch.bfloat16, device=DEV)
+    w = torch.zeros((6 * 256, 640), dtype=torch.bfloat16, device=DEV)
+    sc = torch.ones(6 * 256, device=DEV)
+    p.K, p.x, p.ldx, p.x_bstride, p.x_rows, p.w_qkv = 640, x.data_ptr(), 640, 0, 128, w.data_ptr()
+    p.w_qkv_scale = sc.data_ptr()
+    qn = torch.ones(256, device=DEV)
+    buf = torch.zeros(1 << 22, dtype=torch.uint8, device=DEV)
+    st = _lib.lib().nsa_seq_shard_projection(ctypes_ref(d), ctypes_ref(s), ctypes_ref(p), qn.data_ptr(), qn.data_ptr(),
+                                             None, None, buf.data_ptr(), buf.data_ptr(), None)
+    assert st == _lib.NSA_ERR_UNSUPPORTED
+
+
+def ctypes_ref(x):
+    import ctypes
+    return ctypes.byref(x)
