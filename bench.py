@@ -583,7 +583,7 @@ def run_config4(args, rank, world, local_rank):
            "global_batch": B, "seq_len": L, "layers": LAYERS, "parallelism": f"batch-sharded x{world}",
            "l2": "three 50 MB layer inputs rotate (150 MB > 126 MB L2)",
            "flops_note": "valid (unmasked) pairs only: 4*Hq*pairs*256 per element-layer"}
-    print(json.dumps(_line(args, world, flops / (ms * 1e-3) / 1e12, ms, cfg, _roofline(kst, "attn_fwd_kernel<256>"),
+    print(json.dumps(_line(args, world, flops / (ms * 1e-3) / 1e12, ms, cfg, _roofline(kst, "attn_persist_kernel"),
                            clocks.summary(), 2 * LAYERS * args.steps, "strong")), flush=True)
 
 

@@ -639,7 +639,12 @@ cudaError_t launch_stream(const PrologueParams& p, cudaStream_t stream) {
   const int rows = (!p.skip_q && p.rows[0] > p.rows[1]) ? p.rows[0] : (p.rows[1] > p.rows[2] ? p.rows[1] : p.rows[2]);
   const int H = (!p.skip_q && p.Hq > p.Hkv) ? p.Hq : p.Hkv;
   const long long threads = ((long long)rows * H * P + NSA_PROLOGUE_ITEMS - 1) / NSA_PROLOGUE_ITEMS;
-  const long long blocks = (threads + kStreamThreads - 1) / kStreamThreads;
+  const long long groups = (p.skip_q ? 2 : 3) * (long long)p.B;
+  // NSA_PROLOGUE_ITEMS items per thread while that fills the SMs; a small call (one or two sequences
+  // per GPU) spreads its items over one resident wave instead of running eight in a row per thread
+  const long long wave = std::max(1LL, (long long)device_sm_count() * 4 / groups);
+  const long long one_each = ((long long)rows * H * P + kStreamThreads - 1) / kStreamThreads;
+  const long long blocks = std::max((threads + kStreamThreads - 1) / kStreamThreads, std::min(wave, one_each));
   if (blocks > 0x7FFFFFFFLL || 3LL * p.B > 65535) return cudaErrorInvalidValue;
   prologue_stream_kernel<D, P><<<dim3((unsigned)blocks, (p.skip_q ? 2 : 3) * p.B), kStreamThreads, 0, stream>>>(p);
   return cudaGetLastError();
