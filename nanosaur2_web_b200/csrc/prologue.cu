@@ -278,7 +278,8 @@ __global__ void __launch_bounds__(256, NSA_PROLOGUE_MIN_BLOCKS) prologue_vec_ker
   if (part > 0 && p.n_peers > 0) __threadfence_system();   // peer stores visible before any later signal
 }
 
-// Lane-per-chunk prologue (bf16 input, head dims 64 / 96 / 128).  Eight lanes per head; lane s < D/16
+// Lane-per-chunk prologue (bf16 or fp32 input; bf16 tiles, or fp32 tiles rounded to tf32 for the tf32
+// path; head dims 64 / 96 / 128).  Eight lanes per head; lane s < D/16
 // owns elements [8s, 8s + 8) of both halves of the head, so the RoPE pair (i, i + D/2) stays in one
 // lane with one 16-byte load and one 16-byte store per half, and the head's RMSNorm sum is a
 // three-step shuffle over its eight lanes (lanes past D/16 contribute zeros).  A thread holds only
@@ -290,9 +291,9 @@ __global__ void __launch_bounds__(256, NSA_PROLOGUE_MIN_BLOCKS) prologue_vec_ker
 #ifndef NSA_LANE_MIN_BLOCKS
 #define NSA_LANE_MIN_BLOCKS 4
 #endif
-template <int D>
+template <int D, typename T, bool OUT_F32>
 __global__ void __launch_bounds__(256, NSA_LANE_MIN_BLOCKS) prologue_lane_kernel(const PrologueParams p) {
-  using T = __nv_bfloat16;
+  constexpr int NV = sizeof(T) / 2;   // 16-byte input vectors per half (8 bf16 or 2 x 4 fp32)
   constexpr int HALF = D / 2;
   constexpr int P = D / 16;   // lanes of a head that own data
   static_assert(P >= 1 && P <= 8 && D % 16 == 0, "head dim");
@@ -329,34 +330,45 @@ __global__ void __launch_bounds__(256, NSA_LANE_MIN_BLOCKS) prologue_lane_kernel
   const int ok_rows = min(nrows, valid_rows - p.row0[part] - r_begin);   // rows with data
   // addresses are rebuilt from the kernel parameters at each use (constant-bank operands), which
   // keeps the live registers at what 32 warps per SM allow
-  auto load = [&](int i, uint4& a, uint4& c) {   // produced row r_begin + i (zeros past the data)
+  auto load = [&](int i, uint4 (&a)[NV], uint4 (&c)[NV]) {   // produced row r_begin + i (zeros past the data)
     const bool ok = lane_on && i < ok_rows;
     const T* src = reinterpret_cast<const T*>(view.ptr) + (int64_t)b * view.bstride + view.off +
                    (int64_t)(h_begin + hh) * D + sub * 8 + (int64_t)(p.src_row0[part] + r_begin + i) * view.ld;
-    a = ok ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0u, 0u, 0u, 0u);
-    c = ok ? __ldg(reinterpret_cast<const uint4*>(src + HALF)) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      a[v] = ok ? __ldg(reinterpret_cast<const uint4*>(src) + v) : make_uint4(0u, 0u, 0u, 0u);
+      c[v] = ok ? __ldg(reinterpret_cast<const uint4*>(src + HALF) + v) : make_uint4(0u, 0u, 0u, 0u);
+    }
   };
   const TileOut& to = p.out[part];
   int i = i0;
-  uint4 a, c;
+  uint4 a[NV], c[NV];
   load(i, a, c);
   // the bound is uniform over the block (its first item), so every lane reaches the shuffles
   for (int first = blockIdx.x * blockDim.x; first < count; first += stride, i += di) {
-    uint4 na, nc;
+    uint4 na[NV], nc[NV];
     load(i + di, na, nc);
     const int r_out = r_begin + i;
     const int row = p.row0[part] + r_out;   // key / query index and RoPE row
     const bool in_range = lane_on && i < nrows;
     const bool valid = in_range && row < valid_rows;
     float x1[8], x2[8];
-    {
-      const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wc[4] = {c.x, c.y, c.z, c.w};
+    if constexpr (NV == 1) {
+      const uint32_t wa[4] = {a[0].x, a[0].y, a[0].z, a[0].w}, wc[4] = {c[0].x, c[0].y, c[0].z, c[0].w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         x1[2 * e] = __uint_as_float(wa[e] << 16);
         x1[2 * e + 1] = __uint_as_float(wa[e] & 0xffff0000u);
         x2[2 * e] = __uint_as_float(wc[e] << 16);
         x2[2 * e + 1] = __uint_as_float(wc[e] & 0xffff0000u);
+      }
+    } else {
+#pragma unroll
+      for (int v = 0; v < 2; ++v) {
+        x1[4 * v] = __uint_as_float(a[v].x); x1[4 * v + 1] = __uint_as_float(a[v].y);
+        x1[4 * v + 2] = __uint_as_float(a[v].z); x1[4 * v + 3] = __uint_as_float(a[v].w);
+        x2[4 * v] = __uint_as_float(c[v].x); x2[4 * v + 1] = __uint_as_float(c[v].y);
+        x2[4 * v + 2] = __uint_as_float(c[v].z); x2[4 * v + 3] = __uint_as_float(c[v].w);
       }
     }
     if (w) {   // uniform over the block: every lane reaches the shuffles
@@ -396,14 +408,29 @@ __global__ void __launch_bounds__(256, NSA_LANE_MIN_BLOCKS) prologue_lane_kernel
       }
     }
     if (in_range) {
-      __nv_bfloat16* dst = to.ptr + (int64_t)bl * to.bs + (int64_t)hh * to.hs + (int64_t)r_out * to.rs + sub * 8;
-      *reinterpret_cast<uint4*>(dst) = make_uint4(pack_bf16x2(x1[0], x1[1]), pack_bf16x2(x1[2], x1[3]),
-                                                  pack_bf16x2(x1[4], x1[5]), pack_bf16x2(x1[6], x1[7]));
-      *reinterpret_cast<uint4*>(dst + HALF) = make_uint4(pack_bf16x2(x2[0], x2[1]), pack_bf16x2(x2[2], x2[3]),
-                                                         pack_bf16x2(x2[4], x2[5]), pack_bf16x2(x2[6], x2[7]));
+      const int64_t off = (int64_t)bl * to.bs + (int64_t)hh * to.hs + (int64_t)r_out * to.rs + sub * 8;
+      if constexpr (OUT_F32) {   // the tf32 path: fp32 tiles rounded to tf32 (TileOut strides count floats)
+        float* dst = reinterpret_cast<float*>(to.ptr) + off;
+#pragma unroll
+        for (int v = 0; v < 2; ++v) {
+          reinterpret_cast<float4*>(dst)[v] = make_float4(round_tf32(x1[4 * v]), round_tf32(x1[4 * v + 1]),
+                                                          round_tf32(x1[4 * v + 2]), round_tf32(x1[4 * v + 3]));
+          reinterpret_cast<float4*>(dst + HALF)[v] = make_float4(round_tf32(x2[4 * v]), round_tf32(x2[4 * v + 1]),
+                                                                 round_tf32(x2[4 * v + 2]), round_tf32(x2[4 * v + 3]));
+        }
+      } else {
+        __nv_bfloat16* dst = to.ptr + off;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pack_bf16x2(x1[0], x1[1]), pack_bf16x2(x1[2], x1[3]),
+                                                    pack_bf16x2(x1[4], x1[5]), pack_bf16x2(x1[6], x1[7]));
+        *reinterpret_cast<uint4*>(dst + HALF) = make_uint4(pack_bf16x2(x2[0], x2[1]), pack_bf16x2(x2[2], x2[3]),
+                                                           pack_bf16x2(x2[4], x2[5]), pack_bf16x2(x2[6], x2[7]));
+      }
     }
-    a = na;
-    c = nc;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      a[v] = na[v];
+      c[v] = nc[v];
+    }
   }
 }
 
@@ -621,14 +648,14 @@ bool aligned16(const void* ptr, int64_t elem_offset_multiple_bytes) {
 
 // Every vector access of the fast path is 16-byte aligned iff the bases, strides, offsets and the
 // per-thread chunk are (the chunk and head sizes are multiples of 16 bytes by construction).
-bool vec_ok(const PrologueParams& p, int elem) {
+bool vec_ok(const PrologueParams& p, int elem, int out_elem) {
   const RowView* vs[3] = {&p.q, &p.k, &p.v};
   for (const RowView* v : vs)
     if (!aligned16(v->ptr, v->ld * elem) || ((v->bstride * elem) & 15) || ((v->off * elem) & 15)) return false;
   if (p.cs && (!aligned16(p.cs, p.sin_off * 4))) return false;
   for (int i = p.skip_q ? 1 : 0; i < 3; ++i) {
     const TileOut& o = p.out[i];
-    if (!aligned16(o.ptr, o.bs * 2) || ((o.hs * 2) & 15) || ((o.rs * 2) & 15)) return false;
+    if (!aligned16(o.ptr, o.bs * out_elem) || ((o.hs * out_elem) & 15) || ((o.rs * out_elem) & 15)) return false;
   }
   if ((p.q_w && !aligned16(p.q_w, 0)) || (p.k_w && !aligned16(p.k_w, 0))) return false;
   return true;
@@ -651,7 +678,7 @@ cudaError_t launch_stream(const PrologueParams& p, cudaStream_t stream) {
 }
 
 // Lane kernel grid: the blocks of each (part, batch element) stride over its items.
-template <int D>
+template <int D, typename T>
 cudaError_t launch_lane(const PrologueParams& p, cudaStream_t stream) {
   const int rows = (!p.skip_q && p.rows[0] > p.rows[1]) ? p.rows[0] : (p.rows[1] > p.rows[2] ? p.rows[1] : p.rows[2]);
   const int H = (!p.skip_q && p.Hq > p.Hkv) ? p.Hq : p.Hkv;
@@ -669,7 +696,10 @@ cudaError_t launch_lane(const PrologueParams& p, cudaStream_t stream) {
   const long long need = ((long long)rows * H * 8 + 255) / 256;
   const long long bx = (std::max(1LL, std::min(want, need)) + m - 1) / m * m;
   if (bx > 0x7FFFFFFFLL / 256) return cudaErrorInvalidValue;
-  prologue_lane_kernel<D><<<dim3((unsigned)bx, groups), 256, 0, stream>>>(p);
+  if (p.out_f32)
+    prologue_lane_kernel<D, T, true><<<dim3((unsigned)bx, groups), 256, 0, stream>>>(p);
+  else
+    prologue_lane_kernel<D, T, false><<<dim3((unsigned)bx, groups), 256, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
@@ -695,15 +725,9 @@ cudaError_t launch_vec(const PrologueParams& p, cudaStream_t stream) {
 template <typename T>
 cudaError_t launch_vec_t(const PrologueParams& p, cudaStream_t stream) {
   switch (p.D) {
-    case 64:
-      if constexpr (sizeof(T) == 2) return launch_lane<64>(p, stream);
-      return launch_vec<64, 2, T>(p, stream);
-    case 96:
-      if constexpr (sizeof(T) == 2) return launch_lane<96>(p, stream);
-      return launch_vec<96, NSA_PROLOGUE_P96, T>(p, stream);
-    case 128:
-      if constexpr (sizeof(T) == 2) return launch_lane<128>(p, stream);
-      return launch_vec<128, 2, T>(p, stream);
+    case 64: return launch_lane<64, T>(p, stream);
+    case 96: return launch_lane<96, T>(p, stream);
+    case 128: return launch_lane<128, T>(p, stream);
     case 256:
       if constexpr (sizeof(T) == 2) return launch_stream<256, NSA_PROLOGUE_P256>(p, stream);
       return launch_vec<256, NSA_PROLOGUE_P256, T>(p, stream);
@@ -720,8 +744,10 @@ cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t stream) {
   const int elem = p.src_f32 ? 4 : 2;
   // Rows that also go to other GPUs take the row-per-block kernel: its consecutive threads write
   // each row's head segments contiguously, which NVLink stores need to run at speed.
-  if (p.n_peers == 0 && !p.out_f32 && (p.D == 64 || p.D == 96 || p.D == 128 || p.D == 256 || p.D == 512) &&
-      vec_ok(p, elem))
+  // fp32 (tf32-path) tiles come from the lane kernel only (head dims 64 / 96 / 128)
+  const bool lane_d = p.D == 64 || p.D == 96 || p.D == 128;
+  if (p.n_peers == 0 && (p.out_f32 ? lane_d : (lane_d || p.D == 256 || p.D == 512)) &&
+      vec_ok(p, elem, p.out_f32 ? 4 : 2))
     return p.src_f32 ? launch_vec_t<float>(p, stream) : launch_vec_t<__nv_bfloat16>(p, stream);
   dim3 grid(rows, p.B, p.skip_q ? 2 : 3);
   prologue_kernel<<<grid, kPrologueThreads, 0, stream>>>(p);
