@@ -341,13 +341,19 @@ __global__ void __launch_bounds__(256, NSA_LANE_MIN_BLOCKS) prologue_lane_kernel
     }
   };
   const TileOut& to = p.out[part];
+#ifndef NSA_LANE_DEPTH
+#define NSA_LANE_DEPTH 1
+#endif
+  constexpr int DEPTH = NSA_LANE_DEPTH;   // items whose loads are in flight beyond the current one
   int i = i0;
   uint4 a[NV], c[NV];
+  uint4 pa[DEPTH][NV], pc[DEPTH][NV];
   load(i, a, c);
+#pragma unroll
+  for (int k = 0; k < DEPTH - 1; ++k) load(i + (k + 1) * di, pa[k], pc[k]);
   // the bound is uniform over the block (its first item), so every lane reaches the shuffles
   for (int first = blockIdx.x * blockDim.x; first < count; first += stride, i += di) {
-    uint4 na[NV], nc[NV];
-    load(i + di, na, nc);
+    load(i + DEPTH * di, pa[DEPTH - 1], pc[DEPTH - 1]);
     const int r_out = r_begin + i;
     const int row = p.row0[part] + r_out;   // key / query index and RoPE row
     const bool in_range = lane_on && i < nrows;
@@ -428,9 +434,16 @@ __global__ void __launch_bounds__(256, NSA_LANE_MIN_BLOCKS) prologue_lane_kernel
     }
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
-      a[v] = na[v];
-      c[v] = nc[v];
+      a[v] = pa[0][v];
+      c[v] = pc[0][v];
     }
+#pragma unroll
+    for (int k = 0; k < DEPTH - 1; ++k)
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        pa[k][v] = pa[k + 1][v];
+        pc[k][v] = pc[k + 1][v];
+      }
   }
 }
 
