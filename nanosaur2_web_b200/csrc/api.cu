@@ -1193,11 +1193,11 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* d, const nsa_seq_shard
     pp.n_sets = 2;
     flops += 2.0 * pl.Bs * (pl.Lk - sp.L) * (double)(2 * d->Hkv) * D * (K + Rk);
   }
-  // head dim 256: the RoPE table as a [2 * rows][128] fp32 map (cos block, then sin block), boxes of
-  // [32 rows][16 values] with the 64-byte swizzle, for the epilogue's per-warp staging
+  // head dims 96 and 256: the RoPE table as a [2 * rows][D/2] fp32 map (cos block, then sin block),
+  // boxes of [32 rows][16 values] with the 64-byte swizzle, for the epilogue's per-warp staging
   CUtensorMap tcs;
   const CUtensorMap* tcs_ptr = nullptr;
-  if (D == 256 && cs && d->sinOff > 0 && d->sinOff % (D / 2) == 0) {
+  if ((D == 256 || D == 96) && cs && d->sinOff > 0 && d->sinOff % (D / 2) == 0) {
     EncodeTiledFn fn = encode_fn();
     const cuuint64_t cd[2] = {(cuuint64_t)(D / 2), (cuuint64_t)(2 * (d->sinOff / (D / 2)))};
     const cuuint64_t cst[1] = {(cuuint64_t)(D / 2) * 4};

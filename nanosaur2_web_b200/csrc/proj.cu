@@ -19,8 +19,8 @@
 //               columns, then bias + norm weight + RoPE, bf16 stores.  Bias and norm weights sit in
 //               shared memory.  Tensor-memory reads are few and wide (a wait costs about a thousand
 //               cycles while the next tile's MMAs run), and each chunk's cos / sin loads are issued
-//               before its tensor-memory wait; at head dim 256 they come through shared memory, one
-//               TMA box of the warp's 32 table rows per chunk.
+//               before its tensor-memory wait; at head dims 96 and 256 they come through shared
+//               memory, one TMA box of the warp's 32 table rows per chunk.
 #include "nsa_internal.h"
 #include "ptx.cuh"
 
@@ -40,8 +40,9 @@ struct ProjCfg {
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr uint32_t ACC_COLS = 256;            // TMEM columns per accumulator
   static constexpr uint32_t IDESC = idesc_bf16_f32(128, NT, 0, 0);
-  // One head per tile: the RoPE rows come through shared memory (see the epilogue)
-  static constexpr bool kTableTma = D == 256;
+  // One head per epilogue group (head dims 96 and 256): the RoPE rows come through shared memory,
+  // one TMA box of the warp's 32 table rows per 16-pair chunk (see the epilogue)
+  static constexpr bool kTableTma = D == 256 || D == 96;
   static_assert(NT % 16 == 0 && NT <= 256 && STAGE % 1024 == 0, "projection tile");
 };
 
@@ -272,8 +273,8 @@ __global__ void __launch_bounds__(kProjThreads, 1)
     const int hh0 = C::HPT >= 2 ? group : 0;
     bool params_ready = false;
     int t = 0;
-    // Head dim 256: a thread's RoPE row is 128 cos + 128 sin values, and 32 lanes of a warp hold 32
-    // rows, so per-thread loads would touch 32 lines per instruction.  Instead lane 0 brings the warp's
+    // Head dims 96 and 256: a thread's RoPE row is D/2 cos + D/2 sin values, and 32 lanes of a warp
+    // hold 32 rows, so per-thread loads would touch 32 lines per instruction.  Instead lane 0 brings the warp's
     // 32 table rows of one 16-pair chunk into shared memory with two TMA box loads (64-byte swizzle)
     // and every lane reads its row from there without bank conflicts.  One chunk is in flight at a
     // time: the next is issued as soon as the current one has been read.
