@@ -104,7 +104,11 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   float* sbias1 = sbias0 + nb0;                                    // [nb1]
   float* sqw = sbias1 + nb1;                                       // [D] q norm weight
   float* skw = sqw + D;                                            // [D] k norm weight
-  uint64_t* full = reinterpret_cast<uint64_t*>(skw + D);           // 16-byte aligned (all sizes x 16 B)
+  // one head per tile (head dim 256): the two epilogue warps of a TMEM lane quarter each sum the
+  // squares of their own half of the row and swap the partial sums here ([tile parity][warp][lane])
+  float* xss = skw + D;
+  volatile int* xflag = reinterpret_cast<volatile int*>(xss + 2 * 256);   // [warp][lane]: last tile + 1
+  uint64_t* full = reinterpret_cast<uint64_t*>(xss + 3 * 256);      // 16-byte aligned (all sizes x 16 B)
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;       // [2] accumulator ready for the epilogue
   uint64_t* acc_empty = acc_full + 2;   // [2] accumulator read out (256 epilogue arrivals)
@@ -138,6 +142,7 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   if (blockIdx.x == 0)
     for (int i = threadIdx.x; i < p.zero_count; i += blockDim.x) p.zero_ptr[i] = 0;
   // a missing bias reads as zeros
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) xflag[i] = 0;
   if (!p.set[0].bias)
     for (int i = threadIdx.x; i < nb0; i += blockDim.x) sbias0[i] = 0.f;
   if (nb1 && !p.set[1].bias)
@@ -346,9 +351,12 @@ __global__ void __launch_bounds__(kProjThreads, 1)
         float rn = 1.f;
         if (wn) {
           constexpr int W1 = D % 64 == 0 ? 64 : 48;
+          // one head per tile: this group's columns only (its pairs' two halves), the partner warp's
+          // partial sum comes through shared memory; otherwise the whole head
+          constexpr bool kSplitSum = C::HPT == 1 && D / 4 == W1;
           float ss = 0.f;
 #pragma unroll 1
-          for (int c = 0; c < D; c += W1) {
+          for (int c = kSplitSum ? pair0 : 0; c < D; c += kSplitSum ? D / 2 : W1) {
             uint32_t v[W1];
             if constexpr (W1 == 64)
               tmem_ld64(tbase + col0 + (uint32_t)c, v);
@@ -374,6 +382,33 @@ __global__ void __launch_bounds__(kProjThreads, 1)
                 }
               }
             }
+          }
+          if constexpr (kSplitSum) {
+            // publish, wait (bounded) for the partner warp's partial of the same tile, add in group order
+            const int slot = (t & 1) * 256;
+            xss[slot + ew * 32 + lane] = ss;
+            __threadfence_block();
+            xflag[ew * 32 + lane] = t + 1;
+            const int pw = ew ^ 4;
+            bool seen = xflag[pw * 32 + lane] >= t + 1;
+            if (!seen) {
+              const uint64_t t0 = globaltimer_ns();
+              while (!(seen = xflag[pw * 32 + lane] >= t + 1)) {
+                if (*abort_flag) break;
+                if (globaltimer_ns() - t0 > to) {
+                  *abort_flag = 1;
+                  atomicCAS(p.err, 0, kErrTimeoutProjection);
+                  break;
+                }
+              }
+            }
+            if (!__all_sync(0xffffffffu, seen)) {
+              aborted = true;
+              break;
+            }
+            __threadfence_block();
+            const float mine = ss, other = xss[slot + pw * 32 + lane];
+            ss = group == 0 ? mine + other : other + mine;
           }
           rn = rsqrtf(ss / (float)D + p.eps);
         }
@@ -503,9 +538,9 @@ cudaError_t launch_proj_d(ProjParams p, const CUtensorMap* tmX, const CUtensorMa
   // barriers and the alignment slack
   if (!C::kTableTma || !tmCS) p.cs_tma = 0;
   // the table buffers take shared memory only while a ring of two or more stages still fits
-  if (p.cs_tma && (232448 - (long long)(1024 + kTableBytes + bias_bytes + 2 * D * 4 + 256)) / C::STAGE < 2)
+  if (p.cs_tma && (232448 - (long long)(1024 + kTableBytes + bias_bytes + 2 * D * 4 + 3 * 256 * 4 + 256)) / C::STAGE < 2)
     p.cs_tma = 0;
-  const size_t fixed = 1024 + (p.cs_tma ? kTableBytes : 0) + bias_bytes + 2 * D * 4 + 256;
+  const size_t fixed = 1024 + (p.cs_tma ? kTableBytes : 0) + bias_bytes + 2 * D * 4 + 3 * 256 * 4 + 256;
   const long long room = 232448 - (long long)fixed;
   int stages = room > 0 ? (int)(room / C::STAGE) : 0;
   if (stages > 5) stages = 5;
