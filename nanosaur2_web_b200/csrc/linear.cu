@@ -38,6 +38,9 @@ constexpr int kLinA = 128 * kLinBK * 2;
 constexpr int kLinB = kLinNT * kLinBK * 2;
 constexpr int kLinB8 = kLinNT * kLinBK;   // int8 W slice
 constexpr uint32_t kLinIdesc = idesc_bf16_f32(128, kLinNT, 0, 0);
+// a last column tile with at most 128 columns inside N (te.o and the MLP's down projection at N = 640)
+// multiplies only its first 128 W rows: half the MMA time of that tile
+constexpr uint32_t kLinIdescHalf = idesc_bf16_f32(128, kLinNT / 2, 0, 0);
 
 template <bool I8>
 struct LinCfg {
@@ -144,6 +147,7 @@ __global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem + (uint32_t)a * 256u;
+        const uint32_t idesc = p.N - (u % p.n_tiles) * kLinNT <= kLinNT / 2 ? kLinIdescHalf : kLinIdesc;
         for (int ks = 0; ks < steps; ++ks, ++step) {
           const int s = step % S;
           if (!wait_bounded(I8 ? &conv[s] : &full[s], (step / S) & 1, abort_flag, p.err, kErrTimeoutProjection, to)) {
@@ -154,7 +158,7 @@ __global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
           const uint32_t sa = smem_u32(smem + s * STAGE), sb = sa + kLinA;
 #pragma unroll
           for (int kk = 0; kk < kLinBK / 16; ++kk)
-            mma_ss(d_tmem, smem_desc(sa + kk * 32, 16, 1024, 2), smem_desc(sb + kk * 32, 16, 1024, 2), kLinIdesc,
+            mma_ss(d_tmem, smem_desc(sa + kk * 32, 16, 1024, 2), smem_desc(sb + kk * 32, 16, 1024, 2), idesc,
                    (ks > 0 || kk > 0) ? 1u : 0u);
           tc_commit(&empty[s]);
         }

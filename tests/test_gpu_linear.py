@@ -202,3 +202,23 @@ def test_bf16_linear_lora_alpha_silu_and_bf16_output():
     np.testing.assert_array_equal(y16.float().cpu().numpy(), bf16_round(y32.cpu().numpy()))
     with pytest.raises(Exception, match="another alpha"):
         linear(t(a, torch.bfloat16), t(w, torch.bfloat16), lora=pack)
+
+
+@pytest.mark.parametrize("N", [640, 352, 96])
+def test_linear_half_width_last_tile(N):
+    """Column counts whose last 256-wide tile holds at most 128 columns (te.o and the MLP down
+    projection at N = 640): that tile multiplies only its first 128 weight rows; a plain store and a
+    gated residual both match the oracle."""
+    from nanosaur2_web_b200.ops import linear
+    M, K = 300, 1024
+    rng, a, w, b = operands(40 + N, M, N, K)
+    y = linear(t(a, torch.bfloat16), t(w, torch.bfloat16), bias=t(b))
+    x0 = rng.standard_normal((M, N), dtype=np.float32)
+    g = rng.standard_normal(N).astype(np.float32)
+    out = t(x0)
+    linear(t(a, torch.bfloat16), t(w, torch.bfloat16), bias=t(b), out=out, resid=True, gate=t(g))
+    check_device()
+    want = O.linear(a, w, b, acc=np.float64)
+    np.testing.assert_allclose(y.cpu().numpy(), want, rtol=1e-3, atol=2e-3)
+    np.testing.assert_allclose(out.cpu().numpy(), O.linear_epilogue(want, x0, g, resid=True, acc=np.float64),
+                               rtol=1e-3, atol=2e-3)
