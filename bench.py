@@ -944,8 +944,9 @@ def run_config8(args, rank, world, local_rank):
     input RMSNorm to bf16, te.qkv with the q/k norms and RoPE in the GEMM epilogue, attention, te.o,
     and the post-attention RMSNorm added into x (blocks.gemma_attention_sublayer, five launches per
     layer).  Config 9 runs the whole layers (app/models/gemma3.js:62-89; tools/reference.py:187-199):
-    the attention half, then the MLP half (pre-MLP RMSNorm, gate_up linear to 2 x 2048, GELU-tanh GLU,
-    down linear, post-MLP RMSNorm accumulated; blocks.gemma_layer, ten launches per layer).
+    the attention half, then the MLP half (pre-MLP RMSNorm, gate_up linear to 2 x 2048 with the GELU-tanh
+    GLU in its epilogue, down linear, post-MLP RMSNorm accumulated; blocks.gemma_layer, nine launches
+    per layer).
     Batch-sharded over the ranks (strong scaling).  The line also reports the unfused form: torch
     elementwise norms and GLU, cuBLAS linears and the fused prologue + attention."""
     import torch
@@ -954,7 +955,7 @@ def run_config8(args, rank, world, local_rank):
     from nanosaur2_web_b200.blocks import (GEMMA_HEAD_DIM, GEMMA_HEADS, gemma_attention_sublayer, gemma_layer,
                                            gemma_layer_attention, gemma_mlp_buffers, gemma_rope_theta,
                                            gemma_sublayer_buffers)
-    from nanosaur2_web_b200.ops import ropeTable
+    from nanosaur2_web_b200.ops import glu_interleave, ropeTable
     from nanosaur2_web_b200.sharding import split_range, sum_over_ranks
     whole = args.config == 9
     dev = torch.device("cuda", local_rank)
@@ -973,9 +974,13 @@ def run_config8(args, rank, world, local_rank):
                                 "k_norm": norm(GEMMA_HEAD_DIM), "w_qkv": lin(QKV, Hd), "w_o": lin(Hd, A)},
                        "mlp": {"pre_norm": norm(Hd), "post_norm": norm(Hd), "w_gate_up": lin(2 * I, Hd),
                                "w_down": lin(Hd, I)}})
+        # the fused step reads the gate_up weight in the GLU epilogue's row order, prepared once as a
+        # load-time conversion; the unfused form keeps the [gate; up] rows
+        layers[-1]["mlp_fused"] = dict(layers[-1]["mlp"], w_gate_up=glu_interleave(layers[-1]["mlp"]["w_gate_up"]),
+                                       gate_up_interleaved=True)
     tables = {th: ropeTable(L, GEMMA_HEAD_DIM, th, dev) for th in (1e4, 1e6)}
     bufs = gemma_sublayer_buffers(nb, L, Hd, dev)
-    mbufs = gemma_mlp_buffers(nb, L, Hd, I, dev) if whole else None
+    mbufs = gemma_mlp_buffers(nb, L, Hd, I, dev, gate_up_interleaved=True) if whole else None
     qkv = torch.empty((nb, L, QKV), dtype=torch.bfloat16, device=dev)
     a = torch.empty((nb, L, A), dtype=torch.bfloat16, device=dev)
 
@@ -985,7 +990,7 @@ def run_config8(args, rank, world, local_rank):
             wl = layers[(i * LAYERS + layer) % 3]
             win = 0 if th == 1e6 else WINDOW
             if whole:
-                gemma_layer(x, attn=wl["attn"], mlp=wl["mlp"], cs=tables[th], window=win, eps=EPS,
+                gemma_layer(x, attn=wl["attn"], mlp=wl["mlp_fused"], cs=tables[th], window=win, eps=EPS,
                             buffers=(bufs, mbufs))
             else:
                 gemma_attention_sublayer(x, **wl["attn"], cs=tables[th], window=win, eps=EPS, buffers=bufs)
@@ -1024,7 +1029,7 @@ def run_config8(args, rank, world, local_rank):
         roof[key] = {"kernel": kernel, "achieved": kfl / (kms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
                      "frac": kfl / (kms * 1e-3) / 1e12 / peak, "ms_per_step": kms / nsteps}
     hbm = measured_hbm()
-    for name in ("rmsnorm", "glu") if whole else ("rmsnorm",):
+    for name in ("rmsnorm",):
         nl, nms, _, nbytes = kst[name]
         roof[name] = {"kernel": name + "_kernel", "bound": "hbm", "achieved": nbytes / (nms * 1e-3) / 1e9,
                       "peak": hbm, "unit": "GB/s", "frac": nbytes / (nms * 1e-3) / 1e9 / hbm,
@@ -1032,8 +1037,8 @@ def run_config8(args, rank, world, local_rank):
     if whole:
         work = ("config 9: Gemma3-270M text encoder, config 4's 18 whole layers (B=16 x 1024, GQA 4/1, head dim "
                 "256, causal, 15 local window 512 + 3 global, MLP 2048 GELU-tanh) on the fp32 residual stream "
-                "(hidden 640): the attention half of config 8, then pre-MLP RMSNorm, gate_up linear, GLU, down "
-                "linear, post-MLP RMSNorm accumulated into the stream")
+                "(hidden 640): the attention half of config 8, then pre-MLP RMSNorm, gate_up linear with the "
+                "GLU in its epilogue, down linear, post-MLP RMSNorm accumulated into the stream")
         note = "18 * (2*L*640*(1536 + 1024 + 3*2048) linears + 4*Hq*valid pairs*256 attention) per element"
     else:
         work = ("config 8: Gemma3-270M text encoder, the attention half of config 4's 18 layers (B=16 x 1024, GQA "
@@ -1044,10 +1049,10 @@ def run_config8(args, rank, world, local_rank):
     cfg = {"workload": work, "global_batch": B, "seq_len": L, "layers": LAYERS, "hidden": Hd,
            "parallelism": f"batch-sharded x{world}",
            "l2": "each layer reads and rewrites the 42 MB stream and three weight sets rotate; the per-layer "
-                 "intermediates (h 21 MB, q'/k'/v' 42 MB, a 34 MB, o 42 MB; MLP gu 268 MB) exceed the 126 MB L2",
+                 "intermediates (h 21 MB, q'/k'/v' 42 MB, a 34 MB, o 42 MB; MLP g 67 MB) exceed the 126 MB L2",
            "flops_note": note}
     print(json.dumps(_line(args, world, flops / (ms * 1e-3) / 1e12, ms, cfg, roof, clocks.summary(),
-                           (10 if whole else 5) * LAYERS * args.steps, "strong",
+                           (9 if whole else 5) * LAYERS * args.steps, "strong",
                            unfused_ms_per_step=ms_unfused / args.steps)),
           flush=True)
 

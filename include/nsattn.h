@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define NSA_ABI_VERSION 3
+#define NSA_ABI_VERSION 4
 
 typedef enum nsa_status {
   NSA_OK = 0,
@@ -289,10 +289,10 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* desc, const nsa_seq_sh
  * [M][lda], W in the Linear layout [N][K], C fp32 (the reference's residual stream) or, with
  * out_dtype NSA_BF16, bf16 (store form only: the next GEMM's operand), bias and gate fp32.
  * K, lda multiples of 8; N, ldc, cOff and gOff multiples of 4; pointers 16-byte aligned.
- * N <= 4096: the bias and gate vectors are staged whole in shared memory beside the operand ring
- * (wider outputs return NSA_ERR_UNSUPPORTED; split them into column ranges with cOff).
  * Weight formats (the reference's GEMM B formats "bf16" and "i8", gemm.js:9-10):
- *   NSA_W_BF16  W bf16 [N][K].
+ *   NSA_W_BF16  W bf16 [N][K]; a non-NULL w_scale[N] multiplies row n's dot product as for NSA_W_I8
+ *               (an int8 ConvRot weight expanded once by nsa_expand_i8: the same values, so the same
+ *               results as NSA_W_I8, at the bf16 MMA rate for twice the weight bytes).
  *   NSA_W_I8    W int8 [N][K] of the ConvRot-quantised model (tools/quant.py:48-57) with the per-row
  *               fp32 scale w_scale[N] (gemm.js:159); K a multiple of 16.  A must be the rotated input
  *               (nsa_rotate, ops.rotate: ops.js:34-45, 54), as the reference passes `xr`.
@@ -300,6 +300,11 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* desc, const nsa_seq_sh
  *   delta = sum_i scale_i * B_i (A_i x) over the entries packed by nsa_lora_pack into lora_a [R][K] and
  *   lora_b [N][R] (bf16).  The call first writes T = A @ lora_a^T into the caller's scratch lora_t
  *   (bf16 [M][R]), then accumulates T @ lora_b^T in the same tensor-memory accumulator as A @ W^T.
+ * Fused GLU (glu = 1 SiLU, 2 GELU-tanh): the gate_up linear followed by ops.glu (app/models/gemma3.js:
+ *   80-81; ops.js:141-148) in one call.  W (and bias, w_scale) must be in the tiled order that
+ *   nsa_glu_interleave writes from the [gate; up] layout; then
+ *   C[m*ldc + cOff + j] = act(r_gate[m][j]) * r_up[m][j] for j < N / 2, with r as above before the act.
+ *   N a multiple of 256; no resid, gate, act or LoRA (NSA_ERR_INVALID_ARGUMENT otherwise).
  * ------------------------------------------------------------------------------------------------ */
 typedef enum nsa_weight_format { NSA_W_BF16 = 0, NSA_W_I8 = 1 } nsa_weight_format;
 typedef struct nsa_linear_desc {
@@ -313,11 +318,12 @@ typedef struct nsa_linear_desc {
   int32_t act;      /* 0: none, 1: silu (opts.act) */
   int32_t out_dtype;        /* NSA_F32 (C is float*) or NSA_BF16 (C is bf16, no resid) */
   int32_t w_format;         /* NSA_W_BF16 or NSA_W_I8 */
-  const float* w_scale;     /* NSA_W_I8: [N] per-row scales */
+  const float* w_scale;     /* [N] per-row scales: required for NSA_W_I8, optional for NSA_W_BF16 */
   int32_t lora_rank;        /* R, a multiple of 64 (nsa_lora_rank); 0: no LoRA */
   const void* lora_a;       /* bf16 [R][K] */
   const void* lora_b;       /* bf16 [N][R] */
   void* lora_t;             /* bf16 [M][R] scratch written by the call */
+  int32_t glu;              /* 0: none; 1 SiLU / 2 GELU-tanh GLU of the interleaved gate|up output (C: N / 2 columns) */
 } nsa_linear_desc;
 nsa_status nsa_linear(const nsa_linear_desc* desc, const void* A, const void* W, const float* bias,
                       const float* gate, void* C, void* stream);
@@ -388,6 +394,12 @@ typedef struct nsa_glu_desc {
   int32_t out_dtype;   /* NSA_F32 or NSA_BF16 */
 } nsa_glu_desc;
 nsa_status nsa_glu(const nsa_glu_desc* desc, const float* X, void* Y, void* stream);
+/* nsa_glu_interleave: the row order nsa_linear's fused GLU reads.  src holds 2I rows of row_bytes
+ * bytes, the gate rows [0, I) above the up rows [I, 2I) (a gate_up weight, bias or w_scale); dst row
+ * 256 t + j is gate row 128 t + j for j < 128 and up row I + 128 t + (j - 128) otherwise.  I a
+ * multiple of 128; row_bytes a multiple of 4; src and dst 4-byte aligned and not overlapping.  A
+ * one-time weight preparation, like the reference's load-time conversions. */
+nsa_status nsa_glu_interleave(const void* src, void* dst, int32_t I, int64_t row_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * RoPE tables in the reference layout: cos block [L][D/2] then sin block [L][D/2] (sinOff = L*D/2).

@@ -71,7 +71,7 @@ class LinearDesc(ctypes.Structure):
     """nsa_linear_desc (include/nsattn.h)."""
     _fields_ = [("M", _i32), ("N", _i32), ("K", _i32), ("lda", _i64), ("ldc", _i64), ("cOff", _i64), ("gOff", _i64),
                 ("alpha", _f32), ("resid", _i32), ("act", _i32), ("out_dtype", _i32), ("w_format", _i32),
-                ("w_scale", _vp), ("lora_rank", _i32), ("lora_a", _vp), ("lora_b", _vp), ("lora_t", _vp)]
+                ("w_scale", _vp), ("lora_rank", _i32), ("lora_a", _vp), ("lora_b", _vp), ("lora_t", _vp), ("glu", _i32)]
 
 
 class RotateDesc(ctypes.Structure):
@@ -132,6 +132,7 @@ SIGNATURES = {
     "nsa_lora_pack": (_i32, [ctypes.POINTER(LoraEntry), _i32, _i32, _i32, _vp, _f32, _vp, _vp, _vp]),
     "nsa_rmsnorm": (_i32, [ctypes.POINTER(RmsnormDesc), _vp, _vp, _vp, _vp]),
     "nsa_glu": (_i32, [ctypes.POINTER(GluDesc), _vp, _vp, _vp]),
+    "nsa_glu_interleave": (_i32, [_vp, _vp, _i32, _i64, _vp]),
     "nsa_rope2d_table": (_i32, [_i32, _i32, _i32, _vp, _vp]),
     "nsa_rope1d_table": (_i32, [_i32, _i32, _f32, _vp, _vp]),
     "nsa_check_device": (_i32, [_vp]),

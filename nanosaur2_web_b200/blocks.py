@@ -338,25 +338,31 @@ def gemma_attention_sublayer(x: torch.Tensor, *, in_norm: torch.Tensor, w_qkv: t
     return x
 
 
-def gemma_mlp_buffers(B: int, L: int, hidden: int, inter: int, device) -> dict:
-    """Intermediates of ``gemma_mlp_sublayer``: h2 (bf16 [B*L, hidden]), gu (fp32 [B*L, 2*inter]),
-    g (bf16 [B*L, inter]) and d (fp32 [B*L, hidden])."""
+def gemma_mlp_buffers(B: int, L: int, hidden: int, inter: int, device, gate_up_interleaved: bool = False) -> dict:
+    """Intermediates of ``gemma_mlp_sublayer``: h2 (bf16 [B*L, hidden]), gu (fp32 [B*L, 2*inter]; not
+    needed when the GLU runs in the gate_up linear's epilogue), g (bf16 [B*L, inter]) and d (fp32
+    [B*L, hidden])."""
     M = B * L
-    return {"h": torch.empty((M, hidden), dtype=torch.bfloat16, device=device),
-            "gu": torch.empty((M, 2 * inter), dtype=torch.float32, device=device),
-            "g": torch.empty((M, inter), dtype=torch.bfloat16, device=device),
-            "d": torch.empty((M, hidden), dtype=torch.float32, device=device)}
+    buf = {"h": torch.empty((M, hidden), dtype=torch.bfloat16, device=device),
+           "g": torch.empty((M, inter), dtype=torch.bfloat16, device=device),
+           "d": torch.empty((M, hidden), dtype=torch.float32, device=device)}
+    if not gate_up_interleaved:
+        buf["gu"] = torch.empty((M, 2 * inter), dtype=torch.float32, device=device)
+    return buf
 
 
 def gemma_mlp_sublayer(x: torch.Tensor, *, pre_norm: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
-                       post_norm: torch.Tensor, eps: float = 1e-6, buffers: Optional[dict] = None) -> torch.Tensor:
+                       post_norm: torch.Tensor, eps: float = 1e-6, buffers: Optional[dict] = None,
+                       gate_up_interleaved: bool = False) -> torch.Tensor:
     """The MLP half of one Gemma3 layer, in place on the residual stream x (fp32 [B, L, hidden])
     (app/models/gemma3.js:78-89; tools/reference.py:197-199):
         h2 = rmsnorm(x, pre_norm)                     nsa_rmsnorm, bf16 output
         g  = gelu_tanh(h2 W_gate^T) * (h2 W_up^T)     nsa_linear (gate_up) + nsa_glu, bf16 output
         x += rmsnorm(g W_down^T, post_norm)           nsa_linear (down) + nsa_rmsnorm accumulate
     w_gate_up [2*inter, hidden] (gate rows, then up rows: the reference's concatLinears, gemma3.js:33)
-    and w_down [hidden, inter] bf16; norm weights fp32, lifted by +1.  Returns x."""
+    and w_down [hidden, inter] bf16; norm weights fp32, lifted by +1.  With ``gate_up_interleaved``
+    w_gate_up is in ``glu_interleave`` order (inter a multiple of 128) and the GLU runs in the gate_up
+    linear's epilogue: g is written straight from the accumulator, without the fp32 gu.  Returns x."""
     if x.dim() != 3 or x.dtype != torch.float32 or not x.is_contiguous():
         raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "x must be a contiguous float32 [B, L, hidden] tensor")
     B, L, hidden = x.shape
@@ -365,11 +371,14 @@ def gemma_mlp_sublayer(x: torch.Tensor, *, pre_norm: torch.Tensor, w_gate_up: to
     inter = w_gate_up.shape[0] // 2
     if w_down.shape != (hidden, inter):
         raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "w_down must be [hidden, inter]")
-    buf = buffers if buffers is not None else gemma_mlp_buffers(B, L, hidden, inter, x.device)
+    buf = buffers if buffers is not None else gemma_mlp_buffers(B, L, hidden, inter, x.device, gate_up_interleaved)
     xs = x.view(B * L, hidden)
     rmsnorm(xs, pre_norm, hidden, eps, buf["h"])
-    linear(buf["h"], w_gate_up, out=buf["gu"])
-    glu(buf["gu"], "gelu_tanh", out=buf["g"])
+    if gate_up_interleaved:
+        linear(buf["h"], w_gate_up, out=buf["g"], glu="gelu_tanh")
+    else:
+        linear(buf["h"], w_gate_up, out=buf["gu"])
+        glu(buf["gu"], "gelu_tanh", out=buf["g"])
     linear(buf["g"], w_down, out=buf["d"])
     rmsnorm(buf["d"], post_norm, hidden, eps, xs, accumulate=True)
     return x

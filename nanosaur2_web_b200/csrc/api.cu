@@ -1231,10 +1231,14 @@ nsa_status nsa_linear(const nsa_linear_desc* d, const void* A, const void* W, co
   if (!d) return fail(NSA_ERR_INVALID_ARGUMENT, "desc is NULL");
   if (!A || !W || !C) return fail(NSA_ERR_INVALID_ARGUMENT, "A, W and C must be device pointers");
   if (d->M < 1 || d->N < 1 || d->K < 1) return fail(NSA_ERR_INVALID_ARGUMENT, "M, N and K must be >= 1");
-  const int64_t ldc = d->ldc ? d->ldc : d->N;
+  if (d->glu < 0 || d->glu > 2) return fail(NSA_ERR_INVALID_ARGUMENT, "glu is 0 (none), 1 (silu) or 2 (gelu_tanh)");
+  const int64_t n_out = d->glu ? d->N / 2 : d->N;   // the fused GLU writes half the columns
+  const int64_t ldc = d->ldc ? d->ldc : n_out;
   if (d->K % 8 || d->lda < d->K || d->lda % 8)
     return fail(NSA_ERR_INVALID_ARGUMENT, "K and lda must be multiples of 8 with lda >= K");
-  if (d->N % 4 || ldc % 4 || d->cOff % 4 || d->gOff % 4 || d->cOff < 0 || d->gOff < 0 || ldc < d->cOff + d->N)
+  if (d->glu && (d->N % 256 || d->resid || gate || d->act || d->lora_rank))
+    return fail(NSA_ERR_INVALID_ARGUMENT, "the fused GLU needs N a multiple of 256 and no resid, gate, act or LoRA");
+  if (d->N % 4 || ldc % 4 || d->cOff % 4 || d->gOff % 4 || d->cOff < 0 || d->gOff < 0 || ldc < d->cOff + n_out)
     return fail(NSA_ERR_INVALID_ARGUMENT, "N, ldc, cOff and gOff must be multiples of 4, with ldc >= cOff + N");
   if (d->out_dtype != NSA_F32 && d->out_dtype != NSA_BF16) return fail(NSA_ERR_INVALID_ARGUMENT, "bad out_dtype");
   if (d->w_format != NSA_W_BF16 && d->w_format != NSA_W_I8)
@@ -1291,8 +1295,8 @@ nsa_status nsa_linear(const nsa_linear_desc* d, const void* A, const void* W, co
   if (ok && R) ok = map2d(&tt, d->lora_t, BF, 2, R, d->M, R, 128, SW) && map2d(&tl, d->lora_b, BF, 2, R, d->N, R, 256, SW);
   const bool c16 = d->out_dtype == NSA_BF16;
   if (ok)
-    ok = c16 ? map2d(&tc, static_cast<__nv_bfloat16*>(C) + d->cOff, BF, 2, d->N, d->M, ldc, 32, SW, 64)
-             : map2d(&tc, static_cast<float*>(C) + d->cOff, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d->N, d->M, ldc, 32, SW, 32);
+    ok = c16 ? map2d(&tc, static_cast<__nv_bfloat16*>(C) + d->cOff, BF, 2, n_out, d->M, ldc, 32, SW, 64)
+             : map2d(&tc, static_cast<float*>(C) + d->cOff, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, n_out, d->M, ldc, 32, SW, 32);
   if (!ok) return fail(NSA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the linear operands");
   nsa::LinearParams p = base_params(d->M, d->N, d->K);
   p.lora_steps = R / 64;
@@ -1303,6 +1307,7 @@ nsa_status nsa_linear(const nsa_linear_desc* d, const void* A, const void* W, co
   p.act = d->act;
   p.w_i8 = i8 ? 1 : 0;
   p.w_scale = d->w_scale;
+  p.glu = d->glu;
   if (d->out_dtype == NSA_BF16)
     p.C16 = static_cast<__nv_bfloat16*>(C) + d->cOff;
   else
@@ -1421,6 +1426,21 @@ nsa_status nsa_rmsnorm(const nsa_rmsnorm_desc* d, const float* X, const float* w
   const cudaStream_t strm = static_cast<cudaStream_t>(stream);
   cudaError_t e = profiled("rmsnorm", 0.0, bytes, strm, [&] { return nsa::launch_rmsnorm(p, strm); });
   if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+  return NSA_OK;
+}
+
+nsa_status nsa_glu_interleave(const void* src, void* dst, int32_t I, int64_t row_bytes, void* stream) {
+  if (!src || !dst) return fail(NSA_ERR_INVALID_ARGUMENT, "src and dst must be device pointers");
+  if (I < 128 || I % 128) return fail(NSA_ERR_INVALID_ARGUMENT, "I must be a positive multiple of 128");
+  if (row_bytes < 4 || row_bytes % 4) return fail(NSA_ERR_INVALID_ARGUMENT, "row_bytes must be a positive multiple of 4");
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 3)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "src and dst must be 4-byte aligned");
+  const uintptr_t bytes = (uintptr_t)(2 * (int64_t)I * row_bytes);
+  const uintptr_t s0 = reinterpret_cast<uintptr_t>(src), d0 = reinterpret_cast<uintptr_t>(dst);
+  if (s0 < d0 + bytes && d0 < s0 + bytes) return fail(NSA_ERR_INVALID_ARGUMENT, "src and dst must not overlap");
+  const cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  cudaError_t e = nsa::launch_glu_interleave(src, dst, I, row_bytes, strm);
+  if (e != cudaSuccess) return cuda_fail(e, "glu interleave launch");
   return NSA_OK;
 }
 

@@ -6,6 +6,7 @@
 // or bf16 (the down projection's A operand).  HBM-bound: 8 bytes read per output.
 #include <cuda_bf16.h>
 
+#include "act.cuh"
 #include "nsa_internal.h"
 
 namespace nsa {
@@ -13,15 +14,6 @@ namespace nsa {
 namespace {
 
 constexpr int kGluThreads = 256;
-
-template <int ACT>
-__device__ __forceinline__ float glu_act(float x) {
-  if constexpr (ACT == 0) {
-    return x / (1.f + expf(-x));
-  } else {
-    return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
-  }
-}
 
 // VEC: I, ldx, ldy multiples of 4; X 16-byte aligned, Y 16-byte (fp32) / 8-byte (bf16) aligned.
 template <int ACT, bool BF16, bool VEC>
@@ -64,7 +56,42 @@ void launch_a(const GluParams& p, dim3 grid, cudaStream_t stream) {
     glu_kernel<ACT, false, VEC><<<grid, kGluThreads, 0, stream>>>(p);
 }
 
+// Row permutation of a gate_up weight (or its bias / row scales) for nsa_linear's fused GLU:
+// destination row 256 t + j takes gate row 128 t + j for j < 128 and up row I + 128 t + (j - 128)
+// otherwise, so that each 256-row tile of the linear holds 128 gate rows and their up rows.
+// One 16-byte piece (or one 4-byte word when the rows are not 16-byte multiples) per thread.
+template <typename T>
+__global__ void __launch_bounds__(kGluThreads) glu_interleave_kernel(const uint8_t* __restrict__ src,
+                                                                    uint8_t* __restrict__ dst, int I,
+                                                                    int64_t row_bytes) {
+  const int64_t per_row = row_bytes / (int64_t)sizeof(T);
+  const int64_t n = 2 * (int64_t)I * per_row;
+  for (int64_t i = (int64_t)blockIdx.x * kGluThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kGluThreads) {
+    const int64_t r = i / per_row, c = i - r * per_row;
+    const int64_t t = r / 256, j = r % 256;
+    const int64_t s = j < 128 ? 128 * t + j : I + 128 * t + (j - 128);
+    reinterpret_cast<T*>(dst + r * row_bytes)[c] = reinterpret_cast<const T*>(src + s * row_bytes)[c];
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_glu_interleave(const void* src, void* dst, int I, int64_t row_bytes, cudaStream_t stream) {
+  if (I <= 0) return cudaSuccess;
+  const bool vec = row_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
+  const int64_t n = 2 * (int64_t)I * (row_bytes / (vec ? 16 : 4));
+  const int64_t want = (n + kGluThreads - 1) / kGluThreads;
+  const int64_t cap = (int64_t)device_sm_count() * 8;
+  const dim3 grid((unsigned)(want < cap ? want : cap));
+  const uint8_t* s = static_cast<const uint8_t*>(src);
+  uint8_t* d = static_cast<uint8_t*>(dst);
+  if (vec)
+    glu_interleave_kernel<uint4><<<grid, kGluThreads, 0, stream>>>(s, d, I, row_bytes);
+  else
+    glu_interleave_kernel<uint32_t><<<grid, kGluThreads, 0, stream>>>(s, d, I, row_bytes);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_glu(const GluParams& p, cudaStream_t stream) {
   if (p.rows <= 0) return cudaSuccess;

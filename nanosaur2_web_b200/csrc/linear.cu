@@ -25,6 +25,7 @@
 // hold scale_i B_i / (alpha * rowScale[n]) (nsa_lora_pack), so that the epilogue's alpha * rowScale
 // multiplies the delta back to scale_i B_i (A_i x).
 #include "nsa_internal.h"
+#include "act.cuh"
 #include "ptx.cuh"
 #include "wconv.cuh"
 
@@ -186,6 +187,70 @@ __global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)a * 256u;
       const int row0 = m0 + quarter * 32;   // this warp's 32 rows (TMEM lanes)
+      if (p.glu) {
+        // Fused GLU (ops.glu after the gate_up linear, gemma3.js:80-81): with the weight rows
+        // interleaved per tile (nsa_glu_interleave), accumulator column c < 128 is the gate and 128 + c
+        // the up projection of output feature 128 * nt + c.  Group g writes features 64g .. 64g + 63:
+        // y = act(gate) * up in fp32, then one 64-column bf16 box, or two 32-column fp32 boxes.
+        const int f0 = nt * 128 + group * 64;   // first output column of this warp's box(es)
+        const int n_out = p.N / 2;
+        if (f0 < n_out && row0 < p.M) {
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            const int cg = group * 64 + h * 32;   // gate column in the tile; up at 128 + cg
+            uint32_t gv[32], uv[32];
+            tmem_ld32(tbase + (uint32_t)cg, gv);
+            tmem_ld32(tbase + 128u + (uint32_t)cg, uv);
+            if (f32_out || h == 0) {   // the staging rows are free once the previous box has been read
+              if (lane == 0) bulk_wait_read_all();
+              __syncwarp();
+            }
+            uint8_t* row = stg + lane * 128;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {   // four features at a time
+              const int ng = nt * kLinNT + cg + 4 * q;   // interleaved weight rows of the gate / up values
+              const float4 bg = p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + ng)) : make_float4(0.f, 0.f, 0.f, 0.f);
+              const float4 bu = p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + ng + 128)) : make_float4(0.f, 0.f, 0.f, 0.f);
+              float4 mg = make_float4(p.alpha, p.alpha, p.alpha, p.alpha), mu = mg;
+              if (I8 || p.w_scale) {
+                const float4 rg = __ldg(reinterpret_cast<const float4*>(p.w_scale + ng));
+                const float4 ru = __ldg(reinterpret_cast<const float4*>(p.w_scale + ng + 128));
+                mg = make_float4(mg.x * rg.x, mg.y * rg.y, mg.z * rg.z, mg.w * rg.w);
+                mu = make_float4(mu.x * ru.x, mu.y * ru.y, mu.z * ru.z, mu.w * ru.w);
+              }
+              const float bgv[4] = {bg.x, bg.y, bg.z, bg.w}, buv[4] = {bu.x, bu.y, bu.z, bu.w};
+              const float mgv[4] = {mg.x, mg.y, mg.z, mg.w}, muv[4] = {mu.x, mu.y, mu.z, mu.w};
+              float y[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float g = mgv[i] * __uint_as_float(gv[4 * q + i]) + bgv[i];
+                const float up = muv[i] * __uint_as_float(uv[4 * q + i]) + buv[i];
+                y[i] = (p.glu == 1 ? glu_act<0>(g) : glu_act<1>(g)) * up;
+              }
+              if (f32_out) {
+                *reinterpret_cast<uint4*>(row + ((q ^ (lane & 7)) << 4)) =
+                    make_uint4(__float_as_uint(y[0]), __float_as_uint(y[1]), __float_as_uint(y[2]), __float_as_uint(y[3]));
+              } else {   // bf16: features 4q .. 4q+3 of this half are half a 16-byte chunk
+                const int c = h * 4 + q / 2;
+                uint2* dst = reinterpret_cast<uint2*>(row + ((c ^ (lane & 7)) << 4) + (q & 1) * 8);
+                *dst = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+              }
+            }
+            if (f32_out || h == 1) {
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmC, stg, f32_out ? f0 + h * 32 : f0, row0);
+                bulk_commit_group();
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[a]);
+        ++t;
+        continue;
+      }
 #pragma unroll 1
       for (int c64 = group * 128; c64 < group * 128 + 128; c64 += 64) {
         const int n64 = nt * kLinNT + c64;
@@ -212,7 +277,7 @@ __global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
               const bool in = n < p.N;
               const float4 bb = in && p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + n)) : make_float4(0.f, 0.f, 0.f, 0.f);
               float4 mm = make_float4(p.alpha, p.alpha, p.alpha, p.alpha);
-              if (I8 && in) {
+              if ((I8 || p.w_scale) && in) {
                 const float4 rs = __ldg(reinterpret_cast<const float4*>(p.w_scale + n));
                 mm = make_float4(mm.x * rs.x, mm.y * rs.y, mm.z * rs.z, mm.w * rs.w);
               }

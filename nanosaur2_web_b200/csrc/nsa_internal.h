@@ -208,7 +208,9 @@ struct LinearParams {
   int resid;
   int act;             // 0 none, 1 silu
   int w_i8;            // W is int8 with per-row scales w_scale[N]
-  const float* w_scale;
+  int glu;             // 1 SiLU / 2 GELU-tanh GLU of the [128 gate | 128 up] column halves of each tile
+                       // (weight rows interleaved per tile): C has N / 2 columns
+  const float* w_scale;   // per-row scales [N]: required with w_i8, optional for bf16 W (an expanded int8 W)
   float* C;
   __nv_bfloat16* C16;  // bf16 output instead of C (store form only)
   int64_t ldc;
@@ -267,6 +269,8 @@ struct GluParams {
   int vec;          // I, ldx, ldy multiples of 4; x 16-byte, y 16 (fp32) / 8 (bf16) byte aligned
 };
 cudaError_t launch_glu(const GluParams& p, cudaStream_t stream);
+// Gate/up row interleave per 128-row tile for the linear's fused GLU (glu.cu); row_bytes a multiple of 4.
+cudaError_t launch_glu_interleave(const void* src, void* dst, int I, int64_t row_bytes, cudaStream_t stream);
 
 // Returns cudaErrorInvalidValue for unsupported head dims.
 cudaError_t launch_attention(const AttnParams& p, int D, const CUtensorMap& tmQ, const CUtensorMap& tmK,

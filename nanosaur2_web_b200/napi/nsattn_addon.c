@@ -13,7 +13,7 @@
  *   fusedWorkspaceBytes(opts)                                            -> nsa_fused_attention_workspace_size
  *   linear(opts)           ops.linear(gpu, x, W, {bias,resid,gate,gOff,act,ldc,cOff}) (ops.js:50-66),
  *                          with int8 ConvRot weights (wI8, wScale) and packed LoRAs (loraRank, loraA,
- *                          loraB, loraT)
+ *                          loraB, loraT) and the fused GLU of a gate_up linear (glu: 1 silu, 2 gelu_tanh)
  *   rotate(opts)           ops.rotate(gpu, x) (ops.js:38-45)                -> nsa_rotate
  *   loraPack(opts)         the LoRA side paths of one weight (app/lora.js:143-150), entries
  *                          [{A, B, r, off, n, scale}]; returns the packed rank R -> nsa_lora_pack
@@ -21,6 +21,8 @@
  *                                                                        -> nsa_expand_i8
  *   rmsnorm(opts)          ops.rmsnorm(gpu, x, weight, cols, eps, out) (ops.js:111-116)
  *   glu(opts)              ops.glu(gpu, x, act) (ops.js:141-148)
+ *   gluInterleave(opts)    a gate_up weight / bias / scale in the fused GLU's row order
+ *                          {src, dst, I, rowBytes}                        -> nsa_glu_interleave
  *   rope2dTable(opts) / ropeTable(opts)   common.js:28-43 / 18-24 into a device buffer
  *   checkDevice(opts)      the async error surfacing at read/sync (device.js:224-231)
  *
@@ -257,6 +259,7 @@ static napi_value Linear(napi_env env, napi_callback_info info) {
   d.lora_a = ptr(env, o, "loraA");
   d.lora_b = ptr(env, o, "loraB");
   d.lora_t = ptr(env, o, "loraT");
+  d.glu = (int32_t)num(env, o, "glu", 0);
   return done(env, nsa_linear(&d, ptr(env, o, "x"), ptr(env, o, "W"), ptr(env, o, "bias"), ptr(env, o, "gate"),
                               ptr(env, o, "out"), ptr(env, o, "stream")));
 }
@@ -288,6 +291,13 @@ static napi_value Glu(napi_env env, napi_callback_info info) {
   d.act = (int32_t)num(env, o, "act", 0);
   d.out_dtype = dtype(env, o, "outBf16");
   return done(env, nsa_glu(&d, ptr(env, o, "x"), ptr(env, o, "out"), ptr(env, o, "stream")));
+}
+
+static napi_value GluInterleave(napi_env env, napi_callback_info info) {
+  napi_value o = opts_arg(env, info);
+  if (!o) return NULL;
+  return done(env, nsa_glu_interleave(ptr(env, o, "src"), ptr(env, o, "dst"), (int32_t)num(env, o, "I", 0),
+                                      num(env, o, "rowBytes", 0), ptr(env, o, "stream")));
 }
 
 static napi_value Rotate(napi_env env, napi_callback_info info) {
@@ -385,6 +395,7 @@ static napi_value Init(napi_env env, napi_value exports) {
   export_fn(env, exports, "linear", Linear);
   export_fn(env, exports, "rmsnorm", Rmsnorm);
   export_fn(env, exports, "glu", Glu);
+  export_fn(env, exports, "gluInterleave", GluInterleave);
   export_fn(env, exports, "rotate", Rotate);
   export_fn(env, exports, "loraPack", LoraPack);
   export_fn(env, exports, "expandI8", ExpandI8);

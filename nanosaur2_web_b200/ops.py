@@ -26,7 +26,7 @@ import torch
 from . import _lib
 from ._lib import NSA_BF16, NSA_F32, AttentionDesc, NsaError, check, lib
 
-__all__ = ["attention", "headNorm", "linear", "lora_pack", "LoraPack", "rotate", "expand_i8", "rmsnorm", "glu", "rope2dTable", "ropeTable", "RopeTable", "NsaError",
+__all__ = ["attention", "headNorm", "linear", "lora_pack", "LoraPack", "rotate", "expand_i8", "rmsnorm", "glu", "glu_interleave", "rope2dTable", "ropeTable", "RopeTable", "NsaError",
            "dtype_code", "stream_handle", "check_device"]
 
 
@@ -189,13 +189,17 @@ def rotate(x: torch.Tensor, out: Optional[torch.Tensor] = None, *,
 def linear(x: torch.Tensor, W: torch.Tensor, *, bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
            resid: bool = False, gate: Optional[torch.Tensor] = None, gOff: int = 0, act: Optional[str] = None,
            cOff: int = 0, alpha: float = 1.0, w_scale: Optional[torch.Tensor] = None,
-           lora: Optional[LoraPack] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+           lora: Optional[LoraPack] = None, out_dtype: Optional[torch.dtype] = None,
+           glu: Optional[str] = None) -> torch.Tensor:
     """y = x @ W^T (* w_scale) (+ bias) (+ LoRA delta) (silu), then out = y, out += y (resid) or
     out += gate[gOff + n] * y (resid + gate) (app/gpu/ops.js:50-66 with the epilogue of
     app/gpu/gemm.js:155-165).  x [M, K] bf16 (row pitch x.stride(0)); W [N, K] contiguous, bf16, or
     int8 with per-row float32 ``w_scale`` [N] (the ConvRot weights: x must then be the rotated input,
-    ``rotate``); ``lora`` from ``lora_pack``.  out [M, ldc] float32 (or bfloat16 for the store form)
-    written at columns cOff..cOff+N-1, allocated [M, N] (dtype ``out_dtype``) when not given."""
+    ``rotate``; ``expand_i8(W)`` with the same ``w_scale`` gives the same result at the bf16 rate);
+    ``lora`` from ``lora_pack``.  out [M, ldc] float32 (or bfloat16 for the store form)
+    written at columns cOff..cOff+N-1, allocated [M, N] (dtype ``out_dtype``) when not given.
+    ``glu`` "silu" / "gelu_tanh" fuses ops.glu (ops.js:141-148) into the gate_up linear: W, bias and
+    w_scale in ``glu_interleave`` order, out [M, N / 2] = act(gate) * up."""
     _require_cuda(x, W, bias, out, gate, w_scale)
     if x.dim() != 2 or x.dtype != torch.bfloat16 or x.stride(1) != 1 or W.dtype not in (torch.bfloat16, torch.int8):
         raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT,
@@ -203,15 +207,19 @@ def linear(x: torch.Tensor, W: torch.Tensor, *, bias: Optional[torch.Tensor] = N
     if not W.is_contiguous():
         raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "W must be contiguous [N, K]")
     i8 = W.dtype == torch.int8
-    if i8 and (w_scale is None or w_scale.dtype != torch.float32 or w_scale.numel() != W.shape[0]
-               or not w_scale.is_contiguous()):
+    if i8 and w_scale is None:
         raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "int8 weights need a contiguous float32 w_scale of N entries")
+    if w_scale is not None and (w_scale.dtype != torch.float32 or w_scale.numel() != W.shape[0]
+                                or not w_scale.is_contiguous()):
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "w_scale must be a contiguous float32 tensor of N entries")
     M, K = x.shape
     N = W.shape[0]
+    if glu not in (None, "silu", "gelu_tanh"):
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "glu is None, 'silu' or 'gelu_tanh'")
     if out is None:
         if resid:
             raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "resid needs out")
-        out = torch.empty((M, N), dtype=out_dtype or torch.float32, device=x.device)
+        out = torch.empty((M, N // 2 if glu else N), dtype=out_dtype or torch.float32, device=x.device)
     if out.dtype not in (torch.float32, torch.bfloat16) or out.dim() != 2 or out.stride(1) != 1:
         raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "out must be a float32 or bfloat16 [M, ldc] tensor with unit inner stride")
     d = _lib.LinearDesc()
@@ -220,12 +228,13 @@ def linear(x: torch.Tensor, W: torch.Tensor, *, bias: Optional[torch.Tensor] = N
     d.alpha, d.resid, d.act = alpha, int(bool(resid)), {None: 0, "none": 0, "silu": 1}[act]
     d.out_dtype = dtype_code(out)
     d.w_format = _lib.NSA_W_I8 if i8 else _lib.NSA_W_BF16
-    d.w_scale = _ptr(w_scale) if i8 else None
+    d.w_scale = _ptr(w_scale)
+    d.glu = {None: 0, "silu": 1, "gelu_tanh": 2}[glu]
     t = None
     if lora is not None:
         if lora.N != N or lora.K != K:
             raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, f"the LoRA pack is for [{lora.N}, {lora.K}], W is [{N}, {K}]")
-        if lora.alpha != float(alpha) or (lora.w_scale is None) == i8:
+        if lora.alpha != float(alpha) or (lora.w_scale is None) != (w_scale is None):
             raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "the LoRA pack was made for another alpha or weight format")
         t = torch.empty((M, lora.R), dtype=torch.bfloat16, device=x.device)
         d.lora_rank, d.lora_a, d.lora_b, d.lora_t = lora.R, lora.a.data_ptr(), lora.b.data_ptr(), t.data_ptr()
@@ -270,6 +279,21 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, cols: Optional[int] = None, e
     with torch.cuda.device(x.device):
         check(lib().nsa_rmsnorm(ctypes.byref(d), x2.data_ptr(), weight.data_ptr(), o2.data_ptr(),
                                 stream_handle(x.device)))
+    return out
+
+
+def glu_interleave(t: torch.Tensor) -> torch.Tensor:
+    """The row order ``linear(..., glu=)`` reads, from a gate_up tensor whose 2I rows are [gate; up]
+    (the weight [2I, K], its bias or its w_scale [2I]): row 256 j + i is gate row 128 j + i for
+    i < 128 and up row I + 128 j + i - 128 otherwise.  I a multiple of 128; a new tensor, made once
+    at load time (nsa_glu_interleave)."""
+    _require_cuda(t)
+    if t.dim() not in (1, 2) or t.shape[0] % 256 or not t.is_contiguous():
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "t must be a contiguous [2I] or [2I, K] tensor, I a multiple of 128")
+    out = torch.empty_like(t)
+    row_bytes = t.element_size() * (t.shape[1] if t.dim() == 2 else 1)
+    with torch.cuda.device(t.device):
+        check(lib().nsa_glu_interleave(t.data_ptr(), out.data_ptr(), t.shape[0] // 2, row_bytes, stream_handle(t.device)))
     return out
 
 

@@ -184,9 +184,12 @@ def test_gemma_layer_matches_reference_layers(golden, layer):
     _check_update(x[0].cpu().numpy(), x_in, x_out, tol=1e-1)
 
 
-def test_gemma_mlp_model_width():
-    """hidden 640, MLP width 2048 (Gemma3-270M), B = 2 x 256 tokens, against the oracle."""
+@pytest.mark.parametrize("fused", [False, True])
+def test_gemma_mlp_model_width(fused):
+    """hidden 640, MLP width 2048 (Gemma3-270M), B = 2 x 256 tokens, against the oracle; ``fused``
+    runs the GLU in the gate_up linear's epilogue (interleaved weight), which gives the same bits."""
     from nanosaur2_web_b200.blocks import gemma_mlp_buffers, gemma_mlp_sublayer
+    from nanosaur2_web_b200.ops import glu_interleave
     from tests._helpers import bf16_round
     B, L, Hd, I = 2, 256, 640, 2048
     rng = np.random.default_rng(12)
@@ -197,9 +200,16 @@ def test_gemma_mlp_model_width():
     wd = bf16_round(rng.standard_normal((Hd, I), dtype=np.float32) / np.sqrt(I))
     x_in = (8.0 * rng.standard_normal((B, L, Hd))).astype(np.float32)
     x = t(x_in)
-    gemma_mlp_sublayer(x, pre_norm=t(pre), w_gate_up=t(np.concatenate([wg, wu]), torch.bfloat16),
-                       w_down=t(wd, torch.bfloat16), post_norm=t(post), buffers=gemma_mlp_buffers(B, L, Hd, I, DEV))
+    wgu = t(np.concatenate([wg, wu]), torch.bfloat16)
+    gemma_mlp_sublayer(x, pre_norm=t(pre), w_gate_up=glu_interleave(wgu) if fused else wgu,
+                       w_down=t(wd, torch.bfloat16), post_norm=t(post), buffers=gemma_mlp_buffers(B, L, Hd, I, DEV, fused),
+                       gate_up_interleaved=fused)
     check_device()
     got = x.cpu().numpy()
+    if fused:
+        x2 = t(x_in)
+        gemma_mlp_sublayer(x2, pre_norm=t(pre), w_gate_up=wgu, w_down=t(wd, torch.bfloat16), post_norm=t(post))
+        check_device()
+        np.testing.assert_array_equal(got, x2.cpu().numpy())
     for b in range(B):
         _check_update(got[b], x_in[b], O.gemma_mlp_sublayer(x_in[b], pre, wg, wu, wd, post, acc=np.float64))

@@ -222,3 +222,99 @@ def test_linear_half_width_last_tile(N):
     np.testing.assert_allclose(y.cpu().numpy(), want, rtol=1e-3, atol=2e-3)
     np.testing.assert_allclose(out.cpu().numpy(), O.linear_epilogue(want, x0, g, resid=True, acc=np.float64),
                                rtol=1e-3, atol=2e-3)
+
+
+def _interleave_rows(x, I):
+    """The fused GLU's row order (nsa_glu_interleave): row 256 j + i = gate row 128 j + i (i < 128),
+    else up row I + 128 j + i - 128."""
+    idx = np.concatenate([np.concatenate([np.arange(128 * j, 128 * j + 128), I + np.arange(128 * j, 128 * j + 128)])
+                          for j in range(I // 128)])
+    return x[idx]
+
+
+@pytest.mark.parametrize("act,out_dtype", [("gelu_tanh", torch.bfloat16), ("silu", torch.float32),
+                                           ("gelu_tanh", torch.float32)])
+def test_fused_glu_linear_matches_linear_then_glu(act, out_dtype):
+    """The gate_up linear with ops.glu in its epilogue (app/models/gemma3.js:80-81): ragged M = 300,
+    K = 200 (a partial K slice), I = 384 (three tiles); interleaved weight and bias.  Same MMAs and the
+    same activation code as nsa_linear + nsa_glu, so the two paths agree to the last bit; both match
+    the float64 oracle."""
+    from nanosaur2_web_b200.ops import glu, glu_interleave, linear
+    M, I, K = 300, 384, 200
+    rng, a, w, b = operands(50, M, 2 * I, K)
+    wi, bi = glu_interleave(t(w, torch.bfloat16)), glu_interleave(t(b))
+    np.testing.assert_array_equal(wi.float().cpu().numpy(), _interleave_rows(w, I))
+    np.testing.assert_array_equal(bi.cpu().numpy(), _interleave_rows(b, I))
+    fused = linear(t(a, torch.bfloat16), wi, bias=bi, glu=act, out_dtype=out_dtype)
+    gu = linear(t(a, torch.bfloat16), t(w, torch.bfloat16), bias=t(b))
+    plain = glu(gu, act, out_dtype=out_dtype)
+    check_device()
+    assert fused.shape == (M, I) and fused.dtype == out_dtype
+    np.testing.assert_array_equal(fused.float().cpu().numpy(), plain.float().cpu().numpy())
+    want = O.glu(O.linear(a, w, b, acc=np.float64), act, acc=np.float64)
+    tol = 2 ** -8 if out_dtype == torch.bfloat16 else 1e-3
+    np.testing.assert_allclose(fused.float().cpu().numpy(), want, rtol=tol, atol=2e-3)
+
+
+def test_fused_glu_int8_column_window():
+    """int8 ConvRot gate_up weights with interleaved row scales, alpha 0.5, written into columns
+    [64, 64 + I) of a wider bf16 output that keeps its other columns; against linear + glu."""
+    from nanosaur2_web_b200.ops import glu, glu_interleave, linear
+    M, I, K = 260, 256, 512
+    rng = np.random.default_rng(51)
+    xr = bf16_round(rng.standard_normal((M, K), dtype=np.float32))
+    q = rng.integers(-127, 128, size=(2 * I, K), dtype=np.int8)
+    scale = (0.02 * (1 + rng.random(2 * I))).astype(np.float32)
+    b = (0.1 * rng.standard_normal(2 * I)).astype(np.float32)
+    out = torch.full((M, I + 128), 7.0, dtype=torch.bfloat16, device=DEV)
+    linear(t(xr, torch.bfloat16), glu_interleave(t(q, torch.int8)), bias=glu_interleave(t(b)),
+           w_scale=glu_interleave(t(scale)), alpha=0.5, glu="silu", out=out, cOff=64)
+    gu = linear(t(xr, torch.bfloat16), t(q, torch.int8), bias=t(b), w_scale=t(scale), alpha=0.5)
+    plain = glu(gu, "silu", out_dtype=torch.bfloat16)
+    check_device()
+    got = out.float().cpu().numpy()
+    np.testing.assert_array_equal(got[:, 64:64 + I], plain.float().cpu().numpy())
+    assert (got[:, :64] == 7.0).all() and (got[:, 64 + I:] == 7.0).all()
+
+
+def test_fused_glu_rejects_unsupported_forms():
+    """N off the 256-row tiles, resid, act and LoRA do not combine with the fused GLU."""
+    from nanosaur2_web_b200.ops import NsaError, linear
+    _, a, w, b = operands(52, 64, 384, 64)
+    with pytest.raises(NsaError, match="fused GLU"):
+        linear(t(a, torch.bfloat16), t(w, torch.bfloat16), glu="silu")
+    _, a, w, b = operands(53, 64, 512, 64)
+    out = torch.zeros((64, 256), device=DEV)
+    with pytest.raises(NsaError, match="fused GLU"):
+        linear(t(a, torch.bfloat16), t(w, torch.bfloat16), glu="silu", out=out, resid=True)
+    with pytest.raises(NsaError, match="fused GLU"):
+        linear(t(a, torch.bfloat16), t(w, torch.bfloat16), glu="silu", act="silu")
+
+
+def test_expanded_int8_weight_matches_int8_path():
+    """An int8 ConvRot weight expanded once to bf16 (nsa_expand_i8) with the same row scales gives the
+    int8 path's bits at the bf16 MMA rate: plain store (N = 640, a half-width last tile), and a gated
+    residual with a LoRA packed for the scaled weight."""
+    from nanosaur2_web_b200.ops import expand_i8, linear, lora_pack
+    M, N, K = 300, 640, 512
+    rng = np.random.default_rng(54)
+    xr = t(bf16_round(rng.standard_normal((M, K), dtype=np.float32)), torch.bfloat16)
+    q = t(rng.integers(-127, 128, size=(N, K), dtype=np.int8), torch.int8)
+    scale = t((0.02 * (1 + rng.random(N))).astype(np.float32))
+    b = t((0.1 * rng.standard_normal(N)).astype(np.float32))
+    wx = expand_i8(q)
+    np.testing.assert_array_equal(wx.float().cpu().numpy(), q.float().cpu().numpy())
+    np.testing.assert_array_equal(linear(xr, wx, bias=b, w_scale=scale).cpu().numpy(),
+                                  linear(xr, q, bias=b, w_scale=scale).cpu().numpy())
+    ents = [dict(A=t(rng.standard_normal((16, K), dtype=np.float32) / 16),
+                 B=t(rng.standard_normal((N, 16), dtype=np.float32) / 4), scale=0.7)]
+    pack = lora_pack(ents, N, K, w_scale=scale)
+    x0 = rng.standard_normal((M, N), dtype=np.float32)
+    g = t(rng.standard_normal(N).astype(np.float32))
+    o8, ox = t(x0), t(x0)
+    linear(xr, q, bias=b, w_scale=scale, lora=pack, out=o8, resid=True, gate=g)
+    linear(xr, wx, bias=b, w_scale=scale, lora=pack, out=ox, resid=True, gate=g)
+    check_device()
+    np.testing.assert_array_equal(ox.cpu().numpy(), o8.cpu().numpy())
+    with pytest.raises(Exception, match="another alpha or weight format"):
+        linear(xr, wx, lora=pack)
