@@ -45,7 +45,6 @@ struct CfgP {
   static constexpr int Q_TILE_BYTES = kTileM * D * ESZ;
   static constexpr int KV_TILE_BYTES = BN * D * ESZ;
   static constexpr int KSTEPS_QK = D / KMMA, KSTEPS_PV = BN / KMMA, PV_HALF0 = 64 / KMMA;
-  static constexpr int P_HALF_COLS = TF32 ? 64 : 32;        // TMEM columns of 64 keys of P
   static constexpr int THREADS = 256;
   static constexpr int NBARS = 4 * NS + 2 + 4 + 2 + 4 + 1;
   static constexpr int SMEM_BYTES = Q_TILE_BYTES + 2 * NS * KV_TILE_BYTES + kKeyBiasP * 4 + NBARS * 8 + 16 + 1024;
