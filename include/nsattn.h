@@ -307,6 +307,14 @@ nsa_status nsa_seq_shard_projection(const nsa_fused_desc* desc, const nsa_seq_sh
  *   N a multiple of 256; no resid, gate, act or LoRA (NSA_ERR_INVALID_ARGUMENT otherwise).
  * ------------------------------------------------------------------------------------------------ */
 typedef enum nsa_weight_format { NSA_W_BF16 = 0, NSA_W_I8 = 1 } nsa_weight_format;
+/* Tile schedule (the result is the same bits either way):
+ *   NSA_LINEAR_SINGLE  one CTA per 128 x 256 tile, 64-wide K steps;
+ *   NSA_LINEAR_PAIR    two CTAs (a cluster on two SMs) per 256 x 256 tile, each loading its 128 rows of A
+ *                      and half the tile's W rows, 128-wide K steps; bf16 weights and M > 128 only;
+ *   NSA_LINEAR_AUTO    pairs for bf16 weights when K + lora_rank >= 2048 and M x N >= 2^26 (on B200 pairs
+ *                      measured 10% ahead at 16384 x 4096 x 4096 and level or behind on the DiT and Gemma
+ *                      linears), unless NSA_LINEAR_PAIR=0. */
+typedef enum nsa_linear_schedule { NSA_LINEAR_AUTO = 0, NSA_LINEAR_SINGLE = 1, NSA_LINEAR_PAIR = 2 } nsa_linear_schedule;
 typedef struct nsa_linear_desc {
   int32_t M, N, K;
   int64_t lda;      /* A row pitch in elements */
@@ -324,6 +332,7 @@ typedef struct nsa_linear_desc {
   const void* lora_b;       /* bf16 [N][R] */
   void* lora_t;             /* bf16 [M][R] scratch written by the call */
   int32_t glu;              /* 0: none; 1 SiLU / 2 GELU-tanh GLU of the interleaved gate|up output (C: N / 2 columns) */
+  int32_t schedule;         /* NSA_LINEAR_AUTO (0), NSA_LINEAR_SINGLE or NSA_LINEAR_PAIR (bf16 W only) */
 } nsa_linear_desc;
 nsa_status nsa_linear(const nsa_linear_desc* desc, const void* A, const void* W, const float* bias,
                       const float* gate, void* C, void* stream);

@@ -71,7 +71,8 @@ class LinearDesc(ctypes.Structure):
     """nsa_linear_desc (include/nsattn.h)."""
     _fields_ = [("M", _i32), ("N", _i32), ("K", _i32), ("lda", _i64), ("ldc", _i64), ("cOff", _i64), ("gOff", _i64),
                 ("alpha", _f32), ("resid", _i32), ("act", _i32), ("out_dtype", _i32), ("w_format", _i32),
-                ("w_scale", _vp), ("lora_rank", _i32), ("lora_a", _vp), ("lora_b", _vp), ("lora_t", _vp), ("glu", _i32)]
+                ("w_scale", _vp), ("lora_rank", _i32), ("lora_a", _vp), ("lora_b", _vp), ("lora_t", _vp), ("glu", _i32),
+                ("schedule", _i32)]
 
 
 class RotateDesc(ctypes.Structure):

@@ -1002,6 +1002,12 @@ bool encode_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esz
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// CTA pairs for the bf16 linear: on unless NSA_LINEAR_PAIR=0 (read once).
+bool linear_pairs_enabled() {
+  static const unsigned on = env_flag("NSA_LINEAR_PAIR", 1);
+  return on != 0;
+}
+
 // The LoRA factor T = A @ lora_a^T (bf16 [rows][R], row pitch R) with the linear kernel's store form:
 // the first of the two GEMMs the reference runs per side path (app/gpu/ops.js:80).
 cudaError_t run_lora_factor(const void* A, int64_t lda, int rows, int K, const void* lora_a, int R, void* T, int* err,
@@ -1289,10 +1295,21 @@ nsa_status nsa_linear(const nsa_linear_desc* d, const void* A, const void* W, co
     cudaError_t e = run_lora_factor(A, d->lda, d->M, d->K, d->lora_a, R, d->lora_t, err, strm);
     if (e != cudaSuccess) return cuda_fail(e, "LoRA factor launch");
   }
+  // CTA pairs (256 x 256 tiles, each CTA loading 128 of a tile's W rows, 128-wide K steps) lead only on
+  // large GEMMs (16384 x 4096 x 4096: 1491 vs 1344 TFLOP/s); on the DiT and Gemma linears (K 640-2048,
+  // 2-14 tiles per SM) single CTAs with their deeper 64-wide ring are level or ahead
+  if (d->schedule < NSA_LINEAR_AUTO || d->schedule > NSA_LINEAR_PAIR)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "schedule is NSA_LINEAR_AUTO, NSA_LINEAR_SINGLE or NSA_LINEAR_PAIR");
+  if (d->schedule == NSA_LINEAR_PAIR && (i8 || d->M <= 128))
+    return fail(NSA_ERR_INVALID_ARGUMENT, "CTA pairs need bf16 weights and M > 128");
+  const bool pair = d->schedule == NSA_LINEAR_PAIR ||
+                    (d->schedule == NSA_LINEAR_AUTO && !i8 && d->K + R >= 2048 &&
+                     (int64_t)d->M * d->N >= (int64_t(1) << 26) && linear_pairs_enabled());
+  const uint32_t wbox = pair ? 128 : 256;
   bool ok = map2d(&ta, A, BF, 2, d->K, d->M, d->lda, 128, SW) &&
             (i8 ? map2d(&tw, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, d->K, d->N, d->K, 256, CU_TENSOR_MAP_SWIZZLE_NONE)
-                : map2d(&tw, W, BF, 2, d->K, d->N, d->K, 256, SW));
-  if (ok && R) ok = map2d(&tt, d->lora_t, BF, 2, R, d->M, R, 128, SW) && map2d(&tl, d->lora_b, BF, 2, R, d->N, R, 256, SW);
+                : map2d(&tw, W, BF, 2, d->K, d->N, d->K, wbox, SW));
+  if (ok && R) ok = map2d(&tt, d->lora_t, BF, 2, R, d->M, R, 128, SW) && map2d(&tl, d->lora_b, BF, 2, R, d->N, R, wbox, SW);
   const bool c16 = d->out_dtype == NSA_BF16;
   if (ok)
     ok = c16 ? map2d(&tc, static_cast<__nv_bfloat16*>(C) + d->cOff, BF, 2, n_out, d->M, ldc, 32, SW, 64)
@@ -1308,6 +1325,7 @@ nsa_status nsa_linear(const nsa_linear_desc* d, const void* A, const void* W, co
   p.w_i8 = i8 ? 1 : 0;
   p.w_scale = d->w_scale;
   p.glu = d->glu;
+  p.pair = pair ? 1 : 0;
   if (d->out_dtype == NSA_BF16)
     p.C16 = static_cast<__nv_bfloat16*>(C) + d->cOff;
   else

@@ -10,6 +10,11 @@
 // CTA (one per SM, persistent over 128 x 256 output tiles), the QKV projection's structure:
 //   warp 0      TMA producer: A [128 rows][64] and W [256 rows][64] slices through a ring
 //   warp 1      TMEM allocator + MMA issuer: 128 x 256 x 16 tcgen05.mma into one of two accumulators
+// With bf16 weights two CTAs on two SMs (a cluster) share each 256 x 256 tile instead: each loads its
+// own 128 rows of A and 128 of the tile's 256 W rows, and the even CTA issues M = 256 cta_group::2 MMAs
+// that read both CTAs' shared memory and write each CTA's 128 accumulator rows into its own tensor
+// memory.  Per SM and K slice the ring then carries 32 KB instead of 48 for the same MMA work, which
+// the operand traffic through shared memory (TMA writes plus MMA reads) had bounded at 128 x 256.
 //   warps 2-9   epilogue, two groups of four warps, each group half of the tile's columns; a thread
 //               owns one output row of 32 (fp32) or 64 (bf16) columns at a time: alpha, row scale,
 //               bias, silu, gate, then the row goes into the warp's 128-byte-swizzled staging rows and
@@ -39,28 +44,44 @@ constexpr int kLinA = 128 * kLinBK * 2;
 constexpr int kLinB = kLinNT * kLinBK * 2;
 constexpr int kLinB8 = kLinNT * kLinBK;   // int8 W slice
 constexpr uint32_t kLinIdesc = idesc_bf16_f32(128, kLinNT, 0, 0);
+constexpr uint32_t kLinIdescPair = idesc_bf16_f32(256, kLinNT, 0, 0);
+constexpr uint32_t kLinIdescPairHalf = idesc_bf16_f32(256, kLinNT / 2, 0, 0);
 // a last column tile with at most 128 columns inside N (te.o and the MLP's down projection at N = 640)
 // multiplies only its first 128 W rows: half the MMA time of that tile
 constexpr uint32_t kLinIdescHalf = idesc_bf16_f32(128, kLinNT / 2, 0, 0);
 
-template <bool I8>
+// A stage holds ATOMS K slices of 64 (one 128-byte swizzle row each) of A and of this CTA's W rows,
+// atom j of A at j * A_ATOM and of W at A_BYTES + j * B_ATOM.  CTA pairs take 128-wide K steps: eight
+// MMAs per barrier wait and commit of the issuing thread, whose per-step overhead (wait, commit,
+// bookkeeping) otherwise leaves the tensor pipe idle between steps; single CTAs keep 64-wide steps,
+// which leave room for a four-stage ring.
+template <bool I8, bool PAIR>
 struct LinCfg {
+  static_assert(!(I8 && PAIR), "int8 weights run on single CTAs");
   static constexpr int THREADS = I8 ? 448 : 320;
-  static constexpr int STAGE = kLinA + kLinB + (I8 ? kLinB8 : 0);   // 48 KB, 64 KB with the int8 slot
-  static constexpr int STAGES = I8 ? 3 : 4;
+  static constexpr int ATOMS = PAIR ? 2 : 1;
+  static constexpr int BK = 64 * ATOMS;
+  static constexpr int BROWS = PAIR ? kLinNT / 2 : kLinNT;   // W rows per CTA
+  static constexpr int A_ATOM = 128 * 128, B_ATOM = BROWS * 128;
+  static constexpr int A_BYTES = ATOMS * A_ATOM, B_BYTES = ATOMS * B_ATOM;
+  // 48 KB single, 64 KB per CTA of a pair, 64 KB for int8 (the bf16 W slot plus the int8 landing slot)
+  static constexpr int STAGE = A_BYTES + B_BYTES + (I8 ? kLinB8 : 0);
+  static constexpr int STAGES = I8 ? 3 : (PAIR ? 3 : 4);
   static_assert(STAGE % 1024 == 0, "stage alignment");
+  static_assert(!I8 || (A_BYTES == kLinA && B_BYTES == kLinB), "int8 stage layout");
 };
 constexpr int kLinStaging = 8 * 4096;   // one [32 rows][128 bytes] staging box per epilogue warp
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + expf(-x)); }
 
-template <bool I8>
-__global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
+template <bool I8, bool PAIR>
+__global__ void __launch_bounds__(LinCfg<I8, PAIR>::THREADS, 1)
     linear_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                   const __grid_constant__ CUtensorMap tmT, const __grid_constant__ CUtensorMap tmL,
                   const __grid_constant__ CUtensorMap tmC, const LinearParams p) {
-  constexpr int S = LinCfg<I8>::STAGES;
-  constexpr int STAGE = LinCfg<I8>::STAGE;
+  using Cfg = LinCfg<I8, PAIR>;
+  constexpr int S = Cfg::STAGES;
+  constexpr int STAGE = Cfg::STAGE;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + S * STAGE;                               // [8 warps][32 rows][128 bytes]
@@ -68,13 +89,15 @@ __global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
   uint64_t* empty = full + S;
   uint64_t* conv = empty + S;           // int8: the stage's bf16 W slot is written (4 converter warps)
   uint64_t* acc_full = conv + S;
-  uint64_t* acc_empty = acc_full + 2;   // 256 epilogue arrivals
+  uint64_t* acc_empty = acc_full + 2;   // 256 epilogue arrivals (a pair: one per epilogue warp of both CTAs)
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint64_t to = p.timeout_ns;
-  const int steps = p.k_steps + p.lora_steps;   // K slices per tile
+  // K steps per tile: the main ones over A and W, then the LoRA ones over T and B_cat
+  const int ksteps = (p.k_steps + Cfg::ATOMS - 1) / Cfg::ATOMS;
+  const int steps = ksteps + (p.lora_steps + Cfg::ATOMS - 1) / Cfg::ATOMS;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -84,22 +107,37 @@ __global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 256);
+      mbar_init(&acc_empty[i], PAIR ? 16 : 256);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();   // both CTAs' barriers exist before either signals the other's
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int tiles = p.m_tiles * p.n_tiles;
-  const int G = gridDim.x;
+  // work units: 128-row tiles, or 256-row tiles of a CTA pair (this CTA: rows rank * 128 .. + 127)
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  constexpr int MU = PAIR ? 256 : 128;
+  const int tiles = (PAIR ? (p.m_tiles + 1) / 2 : p.m_tiles) * p.n_tiles;
+  const int G = PAIR ? (int)gridDim.x / 2 : (int)gridDim.x;
+  const int u0 = PAIR ? (int)blockIdx.x / 2 : (int)blockIdx.x;
+  // a pair's last column tile with at most 128 columns inside N: N = 128 MMAs whose B rows come 64
+  // from each CTA (W rows n0 .. n0+63 and n0+64 .. n0+127)
+  auto half_tile = [&](int nt) { return p.N - nt * kLinNT <= kLinNT / 2; };
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -113,8 +151,8 @@ __global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
       }
       int step = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < tiles; u += G) {
-        const int nt = u % p.n_tiles, m0 = (u / p.n_tiles) * 128;
+      for (int u = u0; ok && u < tiles; u += G) {
+        const int nt = u % p.n_tiles, m0 = (u / p.n_tiles) * MU + (int)rank * 128;
         for (int ks = 0; ks < steps; ++ks, ++step) {
           const int s = step % S;
           if (step >= S && !wait_bounded(&empty[s], ((step / S) - 1) & 1, abort_flag, p.err, kErrTimeoutProjection, to)) {
@@ -122,25 +160,61 @@ __global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
             break;
           }
           uint8_t* st = smem + s * STAGE;
-          if (ks < p.k_steps) {
+          if constexpr (!I8) {
+            // atoms of A (or T) and of this CTA's W (or B_cat) rows; a pair's boxes all complete on the
+            // rank-0 CTA's barrier, which expects both CTAs' bytes
+            const bool main = ks < ksteps;
+            const CUtensorMap* ma = main ? &tmA : &tmT;
+            const CUtensorMap* mw = main ? &tmW : &tmL;
+            const int kx = (main ? ks : ks - ksteps) * Cfg::BK;
+            const int brow = nt * kLinNT + (PAIR ? (int)rank * (half_tile(nt) ? kLinNT / 4 : kLinNT / 2) : 0);
+            if constexpr (PAIR) {
+              const uint32_t fbar = mapa_shared(&full[s], 0);
+              if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * STAGE);
+#pragma unroll
+              for (int j = 0; j < Cfg::ATOMS; ++j) {
+                tma_load_2d_pair(st + j * Cfg::A_ATOM, ma, fbar, kx + 64 * j, m0);
+                tma_load_2d_pair(st + Cfg::A_BYTES + j * Cfg::B_ATOM, mw, fbar, kx + 64 * j, brow);
+              }
+            } else {
+              mbar_arrive_expect_tx(&full[s], STAGE);
+#pragma unroll
+              for (int j = 0; j < Cfg::ATOMS; ++j) {
+                tma_load_2d(st + j * Cfg::A_ATOM, ma, &full[s], kx + 64 * j, m0);
+                tma_load_2d(st + Cfg::A_BYTES + j * Cfg::B_ATOM, mw, &full[s], kx + 64 * j, brow);
+              }
+            }
+          } else if (ks < ksteps) {
             mbar_arrive_expect_tx(&full[s], kLinA + (I8 ? kLinB8 : kLinB));
             tma_load_2d(st, &tmA, &full[s], ks * kLinBK, m0);
             tma_load_2d(st + kLinA + (I8 ? kLinB : 0), &tmW, &full[s], ks * kLinBK, nt * kLinNT);
-          } else {   // LoRA slices: T rows against B_cat rows, straight into the bf16 slots
+          } else {   // int8 weights' LoRA slices: T rows against B_cat rows, straight into the bf16 slots
             mbar_arrive_expect_tx(&full[s], kLinA + kLinB);
-            tma_load_2d(st, &tmT, &full[s], (ks - p.k_steps) * kLinBK, m0);
-            tma_load_2d(st + kLinA, &tmL, &full[s], (ks - p.k_steps) * kLinBK, nt * kLinNT);
+            tma_load_2d(st, &tmT, &full[s], (ks - ksteps) * kLinBK, m0);
+            tma_load_2d(st + kLinA, &tmL, &full[s], (ks - ksteps) * kLinBK, nt * kLinNT);
           }
         }
       }
-      for (int i = step > S ? step - S : 0; i < step; ++i) wait_drain(&full[i % S], (i / S) & 1, to);
+      // boxes still in flight (a CTA that gave up) land before shared memory goes away; a pair's
+      // complete on the rank-0 CTA's barriers, which track both CTAs' boxes
+      if (rank == 0)
+        for (int i = step > S ? step - S : 0; i < step; ++i) wait_drain(&full[i % S], (i / S) & 1, to);
     }
   } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // ---------------------------------------------------------------- MMA issuer (rank 0 of a pair)
+    if (lane == 0 && rank == 0) {
       int step = 0, t = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < tiles; u += G) {
+      // a pair's commits arrive on the barrier of the same offset in each CTA
+      auto commit = [&](uint64_t* bar) {
+        if constexpr (PAIR) {
+          tc_commit_pair(mapa_shared(bar, 0));
+          tc_commit_pair(mapa_shared(bar, 1));
+        } else {
+          tc_commit(bar);
+        }
+      };
+      for (int u = u0; ok && u < tiles; u += G) {
         const int a = t & 1;
         if (t >= 2 && !wait_bounded(&acc_empty[a], ((t >> 1) - 1) & 1, abort_flag, p.err, kErrTimeoutProjection, to)) {
           ok = false;
@@ -148,27 +222,45 @@ __global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem + (uint32_t)a * 256u;
-        const uint32_t idesc = p.N - (u % p.n_tiles) * kLinNT <= kLinNT / 2 ? kLinIdescHalf : kLinIdesc;
+        const bool half = half_tile(u % p.n_tiles);
+        const uint32_t idesc = PAIR ? (half ? kLinIdescPairHalf : kLinIdescPair) : (half ? kLinIdescHalf : kLinIdesc);
+        // the stage's barrier was peeked at (non-blocking) before the previous step's MMAs; only a
+        // stage that was not ready then costs a blocking wait here
+        bool ready = false;
         for (int ks = 0; ks < steps; ++ks, ++step) {
           const int s = step % S;
-          if (!wait_bounded(I8 ? &conv[s] : &full[s], (step / S) & 1, abort_flag, p.err, kErrTimeoutProjection, to)) {
+          uint64_t* fb = I8 ? &conv[s] : &full[s];
+          if (!ready && !wait_bounded(fb, (step / S) & 1, abort_flag, p.err, kErrTimeoutProjection, to)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * STAGE), sb = sa + kLinA;
+          if (ks + 1 < steps) {
+            const int s1 = (step + 1) % S;
+            ready = mbar_test_wait(I8 ? &conv[s1] : &full[s1], ((step + 1) / S) & 1);
+          }
+          const uint32_t sa = smem_u32(smem + s * STAGE);
+          const uint64_t da0 = smem_desc(sa, 16, 1024, 2), db0 = smem_desc(sa + Cfg::A_BYTES, 16, 1024, 2);
 #pragma unroll
-          for (int kk = 0; kk < kLinBK / 16; ++kk)
-            mma_ss(d_tmem, smem_desc(sa + kk * 32, 16, 1024, 2), smem_desc(sb + kk * 32, 16, 1024, 2), idesc,
-                   (ks > 0 || kk > 0) ? 1u : 0u);
-          tc_commit(&empty[s]);
+          for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
+            // descriptor start addresses in 16-byte units: atom kk / 4, 32 bytes per K step of 16 inside it
+            const uint64_t da = da0 + (uint64_t)(((kk >> 2) * Cfg::A_ATOM + (kk & 3) * 32) >> 4);
+            const uint64_t db = db0 + (uint64_t)(((kk >> 2) * Cfg::B_ATOM + (kk & 3) * 32) >> 4);
+            if constexpr (PAIR)
+              mma_ss_pair(d_tmem, da, db, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+            else
+              mma_ss(d_tmem, da, db, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+          }
+          commit(&empty[s]);
         }
         if (!ok) break;
-        tc_commit(&acc_full[a]);
+        commit(&acc_full[a]);
         ++t;
       }
       if (!ok) {
-        tc_commit(drain);
+        if constexpr (PAIR)
+          tc_commit_pair(mapa_shared(drain, 0));
+        else
+          tc_commit(drain);
         wait_drain(drain, 0, to);
       }
     }
@@ -179,8 +271,19 @@ __global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
     uint8_t* stg = staging + (warp - 2) * 4096;
     const bool f32_out = p.C16 == nullptr;
     int t = 0;
-    for (int u = blockIdx.x; u < tiles; u += G) {
-      const int nt = u % p.n_tiles, m0 = (u / p.n_tiles) * 128;
+    // the accumulator has been read: this warp's share of the release (a pair: one arrival per warp on
+    // the rank-0 CTA's barrier, after every lane's loads)
+    auto release_acc = [&](int a) {
+      tc_fence_before();
+      if constexpr (PAIR) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[a], 0));
+      } else {
+        mbar_arrive(&acc_empty[a]);
+      }
+    };
+    for (int u = u0; u < tiles; u += G) {
+      const int nt = u % p.n_tiles, m0 = (u / p.n_tiles) * MU + (int)rank * 128;
       const int a = t & 1;
       const bool got = wait_bounded(&acc_full[a], (t >> 1) & 1, abort_flag, p.err, kErrTimeoutProjection, to);
       if (!__all_sync(0xffffffffu, got)) break;
@@ -246,8 +349,7 @@ __global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
             }
           }
         }
-        tc_fence_before();
-        mbar_arrive(&acc_empty[a]);
+        release_acc(a);
         ++t;
         continue;
       }
@@ -309,8 +411,7 @@ __global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&acc_empty[a]);
+      release_acc(a);
       ++t;
     }
     if (lane == 0) bulk_wait_all();
@@ -319,55 +420,110 @@ __global__ void __launch_bounds__(LinCfg<I8>::THREADS, 1)
     const int ct = threadIdx.x - 320;
     int step = 0;
     bool ok = true;
-    for (int u = blockIdx.x; ok && u < tiles; u += G) {
+    for (int u = u0; ok && u < tiles; u += G) {
       for (int ks = 0; ks < steps; ++ks, ++step) {
         const int s = step % S;
         ok = __all_sync(0xffffffffu,
                         wait_bounded(&full[s], (step / S) & 1, abort_flag, p.err, kErrTimeoutProjection, to));
         if (!ok) break;
         uint8_t* st = smem + s * STAGE;
-        if (ks < p.k_steps) convert_i8_slice<kLinNT, 128>(st + kLinA + kLinB, st + kLinA, ct);
+        if (ks < ksteps) convert_i8_slice<kLinNT, 128>(st + kLinA + kLinB, st + kLinA, ct);
         __syncwarp();
         if (lane == 0) mbar_arrive(&conv[s]);
       }
     }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();   // neither CTA leaves while the other may still touch its shared or tensor memory
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem, 512);
+    else
+      tmem_dealloc(tmem, 512);
   }
 }
 
-template <bool I8>
+template <bool I8, bool PAIR>
+constexpr size_t linear_smem() {
+  return 1024 + (size_t)LinCfg<I8, PAIR>::STAGES * LinCfg<I8, PAIR>::STAGE + kLinStaging + 256;
+}
+static_assert(linear_smem<false, false>() <= 232448 && linear_smem<true, false>() <= 232448 &&
+                  linear_smem<false, true>() <= 232448,
+              "shared memory");
+
+template <bool I8, bool PAIR>
 cudaError_t launch_linear_t(const LinearParams& p, const CUtensorMap& tmA, const CUtensorMap& tmW,
                             const CUtensorMap& tmT, const CUtensorMap& tmL, const CUtensorMap& tmC,
                             cudaStream_t stream) {
   const int sms = device_sm_count();
-  const long long tiles = (long long)p.m_tiles * p.n_tiles;
+  const long long tiles = (long long)(PAIR ? (p.m_tiles + 1) / 2 : p.m_tiles) * p.n_tiles;
   if (tiles <= 0) return cudaSuccess;
   if (tiles > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
-  const size_t smem = 1024 + (size_t)LinCfg<I8>::STAGES * LinCfg<I8>::STAGE + kLinStaging + 256;
-  static_assert(1024 + 4 * (kLinA + kLinB) + kLinStaging + 256 <= 232448, "shared memory");
+  constexpr size_t smem = linear_smem<I8, PAIR>();
   // the limit is raised once per device to the whole 227 KB, so launches of different sizes from
-  // several host threads never race on the attribute
+  // several host threads never race on the attribute; a pair kernel also records how many of its
+  // two-CTA clusters fit on the device at once (the persistent grid must not exceed it)
   static DeviceOnce once;
+  static int max_clusters[128];
   cudaError_t e = once_per_device(once, [] {
-    return cudaFuncSetAttribute(linear_kernel<I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    cudaError_t r = cudaFuncSetAttribute(linear_kernel<I8, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    if (r != cudaSuccess || !PAIR) return r;
+    int dev = 0;
+    if ((r = cudaGetDevice(&dev)) != cudaSuccess) return r;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (unsigned)device_sm_count());
+    cfg.blockDim = dim3(LinCfg<I8, PAIR>::THREADS);
+    cfg.dynamicSmemBytes = linear_smem<I8, PAIR>();
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    r = cudaOccupancyMaxActiveClusters(&n, linear_kernel<I8, PAIR>, &cfg);
+    if (r == cudaSuccess && n < 1) r = cudaErrorNotSupported;
+    if (r == cudaSuccess) max_clusters[dev & 127] = n;
+    return r;
   });
   if (e != cudaSuccess) return e;
-  const int grid = tiles < sms ? (int)tiles : sms;
-  linear_kernel<I8><<<grid, LinCfg<I8>::THREADS, smem, stream>>>(tmA, tmW, tmT, tmL, tmC, p);
-  return cudaGetLastError();
+  if constexpr (PAIR) {
+    int dev = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    const int mc = max_clusters[dev & 127];
+    const int clusters = tiles < mc ? (int)tiles : mc;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (unsigned)clusters);
+    cfg.blockDim = dim3(LinCfg<I8, PAIR>::THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, linear_kernel<I8, PAIR>, tmA, tmW, tmT, tmL, tmC, p);
+  } else {
+    const int grid = tiles < sms ? (int)tiles : sms;
+    linear_kernel<I8, PAIR><<<grid, LinCfg<I8, PAIR>::THREADS, smem, stream>>>(tmA, tmW, tmT, tmL, tmC, p);
+    return cudaGetLastError();
+  }
 }
 
 }  // namespace
 
 cudaError_t launch_linear(const LinearParams& p, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmT,
                           const CUtensorMap& tmL, const CUtensorMap& tmC, cudaStream_t stream) {
-  return p.w_i8 ? launch_linear_t<true>(p, tmA, tmW, tmT, tmL, tmC, stream)
-                : launch_linear_t<false>(p, tmA, tmW, tmT, tmL, tmC, stream);
+  if (p.w_i8) return launch_linear_t<true, false>(p, tmA, tmW, tmT, tmL, tmC, stream);
+  return p.pair ? launch_linear_t<false, true>(p, tmA, tmW, tmT, tmL, tmC, stream)
+                : launch_linear_t<false, false>(p, tmA, tmW, tmT, tmL, tmC, stream);
 }
 
 }  // namespace nsa

@@ -208,6 +208,7 @@ struct LinearParams {
   int resid;
   int act;             // 0 none, 1 silu
   int w_i8;            // W is int8 with per-row scales w_scale[N]
+  int pair;            // bf16 W only: CTA pairs on 256 x 256 tiles (tmW / tmL boxes of 128 rows instead of 256)
   int glu;             // 1 SiLU / 2 GELU-tanh GLU of the [128 gate | 128 up] column halves of each tile
                        // (weight rows interleaved per tile): C has N / 2 columns
   const float* w_scale;   // per-row scales [N]: required with w_i8, optional for bf16 W (an expanded int8 W)

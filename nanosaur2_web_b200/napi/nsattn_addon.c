@@ -13,7 +13,8 @@
  *   fusedWorkspaceBytes(opts)                                            -> nsa_fused_attention_workspace_size
  *   linear(opts)           ops.linear(gpu, x, W, {bias,resid,gate,gOff,act,ldc,cOff}) (ops.js:50-66),
  *                          with int8 ConvRot weights (wI8, wScale) and packed LoRAs (loraRank, loraA,
- *                          loraB, loraT) and the fused GLU of a gate_up linear (glu: 1 silu, 2 gelu_tanh)
+ *                          loraB, loraT), the fused GLU of a gate_up linear (glu: 1 silu, 2 gelu_tanh) and
+ *                          the tile schedule (schedule: 0 auto, 1 single CTAs, 2 CTA pairs)
  *   rotate(opts)           ops.rotate(gpu, x) (ops.js:38-45)                -> nsa_rotate
  *   loraPack(opts)         the LoRA side paths of one weight (app/lora.js:143-150), entries
  *                          [{A, B, r, off, n, scale}]; returns the packed rank R -> nsa_lora_pack
@@ -260,6 +261,7 @@ static napi_value Linear(napi_env env, napi_callback_info info) {
   d.lora_b = ptr(env, o, "loraB");
   d.lora_t = ptr(env, o, "loraT");
   d.glu = (int32_t)num(env, o, "glu", 0);
+  d.schedule = (int32_t)num(env, o, "schedule", NSA_LINEAR_AUTO);
   return done(env, nsa_linear(&d, ptr(env, o, "x"), ptr(env, o, "W"), ptr(env, o, "bias"), ptr(env, o, "gate"),
                               ptr(env, o, "out"), ptr(env, o, "stream")));
 }

@@ -190,7 +190,7 @@ def linear(x: torch.Tensor, W: torch.Tensor, *, bias: Optional[torch.Tensor] = N
            resid: bool = False, gate: Optional[torch.Tensor] = None, gOff: int = 0, act: Optional[str] = None,
            cOff: int = 0, alpha: float = 1.0, w_scale: Optional[torch.Tensor] = None,
            lora: Optional[LoraPack] = None, out_dtype: Optional[torch.dtype] = None,
-           glu: Optional[str] = None) -> torch.Tensor:
+           glu: Optional[str] = None, schedule: str = "auto") -> torch.Tensor:
     """y = x @ W^T (* w_scale) (+ bias) (+ LoRA delta) (silu), then out = y, out += y (resid) or
     out += gate[gOff + n] * y (resid + gate) (app/gpu/ops.js:50-66 with the epilogue of
     app/gpu/gemm.js:155-165).  x [M, K] bf16 (row pitch x.stride(0)); W [N, K] contiguous, bf16, or
@@ -199,7 +199,9 @@ def linear(x: torch.Tensor, W: torch.Tensor, *, bias: Optional[torch.Tensor] = N
     ``lora`` from ``lora_pack``.  out [M, ldc] float32 (or bfloat16 for the store form)
     written at columns cOff..cOff+N-1, allocated [M, N] (dtype ``out_dtype``) when not given.
     ``glu`` "silu" / "gelu_tanh" fuses ops.glu (ops.js:141-148) into the gate_up linear: W, bias and
-    w_scale in ``glu_interleave`` order, out [M, N / 2] = act(gate) * up."""
+    w_scale in ``glu_interleave`` order, out [M, N / 2] = act(gate) * up.  ``schedule`` "auto",
+    "single" (one CTA per 128 x 256 tile) or "pair" (two CTAs per 256 x 256 tile; bf16 W, M > 128):
+    the same result either way."""
     _require_cuda(x, W, bias, out, gate, w_scale)
     if x.dim() != 2 or x.dtype != torch.bfloat16 or x.stride(1) != 1 or W.dtype not in (torch.bfloat16, torch.int8):
         raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT,
@@ -230,6 +232,9 @@ def linear(x: torch.Tensor, W: torch.Tensor, *, bias: Optional[torch.Tensor] = N
     d.w_format = _lib.NSA_W_I8 if i8 else _lib.NSA_W_BF16
     d.w_scale = _ptr(w_scale)
     d.glu = {None: 0, "silu": 1, "gelu_tanh": 2}[glu]
+    if schedule not in ("auto", "single", "pair"):
+        raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "schedule is 'auto', 'single' or 'pair'")
+    d.schedule = {"auto": 0, "single": 1, "pair": 2}[schedule]
     t = None
     if lora is not None:
         if lora.N != N or lora.K != K:

@@ -318,3 +318,68 @@ def test_expanded_int8_weight_matches_int8_path():
     np.testing.assert_array_equal(ox.cpu().numpy(), o8.cpu().numpy())
     with pytest.raises(Exception, match="another alpha or weight format"):
         linear(xr, wx, lora=pack)
+
+
+@pytest.mark.parametrize("case", ["gated_ragged", "lora_silu_bf16", "glu", "half_tile_f32", "expanded_i8_lora"])
+def test_cta_pair_schedule_matches_single(case):
+    """The CTA-pair schedule (two CTAs per 256 x 256 tile, 128-wide K steps) and the single-CTA one
+    (128 x 256 tiles, 64-wide K steps) add the same products in the same order: equal bits, for ragged
+    M / K, LoRA slices, the fused GLU, a half-width last column tile and row-scaled (expanded int8)
+    weights; also against the oracle."""
+    from nanosaur2_web_b200.ops import expand_i8, glu_interleave, linear, lora_pack
+    rng = np.random.default_rng(60)
+    if case == "gated_ragged":
+        M, N, K = 600, 512, 1544
+    elif case == "lora_silu_bf16":
+        M, N, K = 300, 768, 1536
+    elif case == "glu":
+        M, N, K = 392, 768, 640
+    elif case == "half_tile_f32":
+        M, N, K = 1000, 640, 2048
+    else:
+        M, N, K = 260, 384, 1024
+    a = bf16_round(rng.standard_normal((M, K), dtype=np.float32))
+    w = bf16_round(rng.standard_normal((N, K), dtype=np.float32) / np.sqrt(K))
+    b = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    A, W, Bv = t(a, torch.bfloat16), t(w, torch.bfloat16), t(b)
+
+    def run(schedule):
+        if case == "gated_ragged":
+            x0, g = rng.standard_normal((M, N), dtype=np.float32), rng.standard_normal(N).astype(np.float32)
+            out = t(x0)
+            linear(A, W, bias=Bv, out=out, resid=True, gate=t(g), schedule=schedule)
+            return out, O.linear_epilogue(O.linear(a, w, b, acc=np.float64), x0, g, resid=True, acc=np.float64)
+        if case == "lora_silu_bf16":
+            ents = [dict(A=t(np.full((8, K), 0.01, np.float32)), B=t(np.full((N, 8), 0.02, np.float32)), scale=0.5)]
+            pack = lora_pack(ents, N, K)
+            return linear(A, W, bias=Bv, act="silu", lora=pack, out_dtype=torch.bfloat16, schedule=schedule), None
+        if case == "glu":
+            return linear(A, glu_interleave(W), bias=glu_interleave(Bv), glu="gelu_tanh", schedule=schedule), \
+                O.glu(O.linear(a, w, b, acc=np.float64), "gelu_tanh", acc=np.float64)
+        if case == "half_tile_f32":
+            return linear(A, W, bias=Bv, schedule=schedule), O.linear(a, w, b, acc=np.float64)
+        q = t(rng.integers(-127, 128, size=(N, K), dtype=np.int8), torch.int8)
+        sc = t((0.02 * (1 + rng.random(N))).astype(np.float32))
+        ents = [dict(A=t(rng.standard_normal((16, K), dtype=np.float32) / 16),
+                     B=t(rng.standard_normal((N, 16), dtype=np.float32) / 4), scale=0.7)]
+        return linear(A, expand_i8(q), bias=Bv, w_scale=sc, lora=lora_pack(ents, N, K, w_scale=sc),
+                      schedule=schedule), None
+
+    state = rng.bit_generator.state
+    y1, want = run("single")
+    rng.bit_generator.state = state
+    y2, _ = run("pair")
+    check_device()
+    np.testing.assert_array_equal(y2.float().cpu().numpy(), y1.float().cpu().numpy())
+    if want is not None:
+        np.testing.assert_allclose(y2.float().cpu().numpy(), want, rtol=1e-3, atol=2e-3)
+
+
+def test_cta_pair_schedule_rejects_int8_and_one_row_tile():
+    from nanosaur2_web_b200.ops import NsaError, linear
+    _, a, w, b = operands(61, 64, 256, 64)
+    with pytest.raises(NsaError, match="CTA pairs"):
+        linear(t(a, torch.bfloat16), t(w, torch.bfloat16), schedule="pair")
+    with pytest.raises(NsaError, match="CTA pairs"):
+        linear(t(a, torch.bfloat16), t(np.zeros((256, 64), np.int8), torch.int8), w_scale=t(np.ones(256, np.float32)),
+               schedule="pair")
