@@ -150,7 +150,7 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
 }
 
 // CTA-pair form: the box lands in this CTA's shared memory and completes its bytes on the mbarrier
-// at `bar_cluster` (the rank-0 CTA's, where the MMA issuer waits).  No multicast.
+// at `bar_cluster` (the rank-0 CTA's, where the MMA issuer waits).  Each CTA writes only its own shared memory.
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
                                                  int y) {
   asm volatile(
