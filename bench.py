@@ -945,8 +945,9 @@ def run_config8(args, rank, world, local_rank):
     and the post-attention RMSNorm added into x (blocks.gemma_attention_sublayer, five launches per
     layer).  Config 9 runs the whole layers (app/models/gemma3.js:62-89; tools/reference.py:187-199):
     the attention half, then the MLP half (pre-MLP RMSNorm, gate_up linear to 2 x 2048 with the GELU-tanh
-    GLU in its epilogue, down linear, post-MLP RMSNorm accumulated; blocks.gemma_layer, nine launches
-    per layer).
+    GLU in its epilogue, down linear, post-MLP RMSNorm accumulated; blocks.gemma_layer).  Each
+    accumulate into the stream also writes the norm that follows it (pre-MLP, next layer's input),
+    so a layer takes seven launches (config 8: four) after the first.
     Batch-sharded over the ranks (strong scaling).  The line also reports the unfused form: torch
     elementwise norms and GLU, cuBLAS linears and the fused prologue + attention."""
     import torch
@@ -985,15 +986,19 @@ def run_config8(args, rank, world, local_rank):
     a = torch.empty((nb, L, A), dtype=torch.bfloat16, device=dev)
 
     def step(i):
+        # each accumulate into x also writes the next norm's output (the pre-MLP norm, the next layer's
+        # input norm), so only the first layer of a step normalises x on its own
         for layer in range(LAYERS):
             th = gemma_rope_theta(layer)
             wl = layers[(i * LAYERS + layer) % 3]
+            nxt = layers[(i * LAYERS + layer + 1) % 3]["attn"]["in_norm"] if layer + 1 < LAYERS else None
             win = 0 if th == 1e6 else WINDOW
             if whole:
                 gemma_layer(x, attn=wl["attn"], mlp=wl["mlp_fused"], cs=tables[th], window=win, eps=EPS,
-                            buffers=(bufs, mbufs))
+                            buffers=(bufs, mbufs), h_ready=layer > 0, next_norm=nxt)
             else:
-                gemma_attention_sublayer(x, **wl["attn"], cs=tables[th], window=win, eps=EPS, buffers=bufs)
+                gemma_attention_sublayer(x, **wl["attn"], cs=tables[th], window=win, eps=EPS, buffers=bufs,
+                                         h_ready=layer > 0, next_norm=nxt, next_out=bufs["h"])
 
     def rms(t, w):
         return t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + EPS) * w
@@ -1052,7 +1057,7 @@ def run_config8(args, rank, world, local_rank):
                  "intermediates (h 21 MB, q'/k'/v' 42 MB, a 34 MB, o 42 MB; MLP g 67 MB) exceed the 126 MB L2",
            "flops_note": note}
     print(json.dumps(_line(args, world, flops / (ms * 1e-3) / 1e12, ms, cfg, roof, clocks.summary(),
-                           (9 if whole else 5) * LAYERS * args.steps, "strong",
+                           ((9 * LAYERS - 2 * LAYERS + 1) if whole else (5 * LAYERS - LAYERS + 1)) * args.steps, "strong",
                            unfused_ms_per_step=ms_unfused / args.steps)),
           flush=True)
 

@@ -386,6 +386,14 @@ typedef struct nsa_rmsnorm_desc {
   int32_t out_dtype;   /* NSA_F32 or NSA_BF16 */
   int32_t accumulate;  /* 1: Y += norm(X) (NSA_F32 only) */
   float eps;           /* >= 0; the reference's default is 1e-6 */
+  /* With accumulate = 1, optionally the next norm of the same rows in the same pass: the Gemma layer's
+   * pre-MLP norm after the post-attention accumulate, and the next layer's input norm after the
+   * post-MLP one (gemma3.js:77-79, 88 then 62): Z = rmsnorm(Y after the add) * next_weight, with the
+   * same eps.  Y's new values stay in registers, so Z costs its own write only. */
+  const float* next_weight;   /* [cols] or NULL (no Z) */
+  void* Z;                    /* [rows][ldz] */
+  int64_t ldz;                /* Z row pitch in elements (0: cols) */
+  int32_t z_dtype;            /* NSA_F32 or NSA_BF16 */
 } nsa_rmsnorm_desc;
 nsa_status nsa_rmsnorm(const nsa_rmsnorm_desc* desc, const float* X, const float* weight, void* Y, void* stream);
 

@@ -88,7 +88,8 @@ class LoraEntry(ctypes.Structure):
 class RmsnormDesc(ctypes.Structure):
     """nsa_rmsnorm_desc (include/nsattn.h)."""
     _fields_ = [("rows", _i32), ("cols", _i32), ("ldx", _i64), ("ldy", _i64), ("out_dtype", _i32),
-                ("accumulate", _i32), ("eps", _f32)]
+                ("accumulate", _i32), ("eps", _f32), ("next_weight", _vp), ("Z", _vp), ("ldz", _i64),
+                ("z_dtype", _i32)]
 
 
 class GluDesc(ctypes.Structure):

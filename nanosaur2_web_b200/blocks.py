@@ -315,14 +315,19 @@ def gemma_sublayer_buffers(B: int, L: int, hidden: int, device) -> dict:
 
 def gemma_attention_sublayer(x: torch.Tensor, *, in_norm: torch.Tensor, w_qkv: torch.Tensor, q_norm: torch.Tensor,
                              k_norm: torch.Tensor, w_o: torch.Tensor, post_norm: torch.Tensor, cs: RopeTable,
-                             window: int = 0, eps: float = 1e-6, buffers: Optional[dict] = None) -> torch.Tensor:
+                             window: int = 0, eps: float = 1e-6, buffers: Optional[dict] = None,
+                             h_ready: bool = False, next_norm: Optional[torch.Tensor] = None,
+                             next_out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """The attention half of one Gemma3 layer, in place on the residual stream x (fp32 [B, L, hidden])
     (app/models/gemma3.js:62-77; tools/reference.py:187-196):
         h = rmsnorm(x, in_norm)                       nsa_rmsnorm, bf16 output
         a = attention(headNorm(h W_qkv^T))            nsa_seq_shard_projection + nsa_seq_shard_attention
         x += rmsnorm(a W_o^T, post_norm)              nsa_linear (te.o) + nsa_rmsnorm accumulate
     w_qkv [1536, hidden] and w_o [hidden, 1024] bf16; norm weights fp32, lifted by +1 (gemma3.js:22).
-    ``buffers`` = gemma_sublayer_buffers(B, L, hidden, device), to reuse.  Returns x."""
+    ``buffers`` = gemma_sublayer_buffers(B, L, hidden, device), to reuse.  Chaining (the norms the
+    layer runs back to back, in one pass each): ``h_ready`` means buffers["h"] already holds
+    rmsnorm(x, in_norm) (written by the previous accumulate); ``next_norm`` makes the final accumulate
+    also write next_out = rmsnorm(x after the add, next_norm) (bf16).  Returns x."""
     if x.dim() != 3 or x.dtype != torch.float32 or not x.is_contiguous():
         raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "x must be a contiguous float32 [B, L, hidden] tensor")
     B, L, hidden = x.shape
@@ -330,11 +335,13 @@ def gemma_attention_sublayer(x: torch.Tensor, *, in_norm: torch.Tensor, w_qkv: t
         raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "w_o must be [hidden, 1024]")
     buf = buffers if buffers is not None else gemma_sublayer_buffers(B, L, hidden, x.device)
     h, a, o = buf["h"], buf["a"], buf["o"]
-    rmsnorm(x, in_norm, hidden, eps, h)
+    if not h_ready:
+        rmsnorm(x, in_norm, hidden, eps, h)
     gemma_layer_attention_projected(h, w_qkv=w_qkv, q_norm=q_norm, k_norm=k_norm, cs=cs, window=window, eps=eps,
                                     out=a, buffers=buf["proj"])
     linear(a.view(B * L, -1), w_o, out=o)
-    rmsnorm(o, post_norm, hidden, eps, x.view(B * L, hidden), accumulate=True)
+    rmsnorm(o, post_norm, hidden, eps, x.view(B * L, hidden), accumulate=True, next_weight=next_norm,
+            next_out=None if next_norm is None else next_out.view(B * L, hidden))
     return x
 
 
@@ -353,7 +360,8 @@ def gemma_mlp_buffers(B: int, L: int, hidden: int, inter: int, device, gate_up_i
 
 def gemma_mlp_sublayer(x: torch.Tensor, *, pre_norm: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
                        post_norm: torch.Tensor, eps: float = 1e-6, buffers: Optional[dict] = None,
-                       gate_up_interleaved: bool = False) -> torch.Tensor:
+                       gate_up_interleaved: bool = False, h_ready: bool = False,
+                       next_norm: Optional[torch.Tensor] = None, next_out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """The MLP half of one Gemma3 layer, in place on the residual stream x (fp32 [B, L, hidden])
     (app/models/gemma3.js:78-89; tools/reference.py:197-199):
         h2 = rmsnorm(x, pre_norm)                     nsa_rmsnorm, bf16 output
@@ -362,7 +370,10 @@ def gemma_mlp_sublayer(x: torch.Tensor, *, pre_norm: torch.Tensor, w_gate_up: to
     w_gate_up [2*inter, hidden] (gate rows, then up rows: the reference's concatLinears, gemma3.js:33)
     and w_down [hidden, inter] bf16; norm weights fp32, lifted by +1.  With ``gate_up_interleaved``
     w_gate_up is in ``glu_interleave`` order (inter a multiple of 128) and the GLU runs in the gate_up
-    linear's epilogue: g is written straight from the accumulator, without the fp32 gu.  Returns x."""
+    linear's epilogue: g is written straight from the accumulator, without the fp32 gu.  ``h_ready`` /
+    ``next_norm`` / ``next_out`` chain the norms as in ``gemma_attention_sublayer`` (buffers["h"] holds
+    rmsnorm(x, pre_norm) already; the final accumulate also writes the next layer's normalised input).
+    Returns x."""
     if x.dim() != 3 or x.dtype != torch.float32 or not x.is_contiguous():
         raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "x must be a contiguous float32 [B, L, hidden] tensor")
     B, L, hidden = x.shape
@@ -373,25 +384,38 @@ def gemma_mlp_sublayer(x: torch.Tensor, *, pre_norm: torch.Tensor, w_gate_up: to
         raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "w_down must be [hidden, inter]")
     buf = buffers if buffers is not None else gemma_mlp_buffers(B, L, hidden, inter, x.device, gate_up_interleaved)
     xs = x.view(B * L, hidden)
-    rmsnorm(xs, pre_norm, hidden, eps, buf["h"])
+    if not h_ready:
+        rmsnorm(xs, pre_norm, hidden, eps, buf["h"])
     if gate_up_interleaved:
         linear(buf["h"], w_gate_up, out=buf["g"], glu="gelu_tanh")
     else:
         linear(buf["h"], w_gate_up, out=buf["gu"])
         glu(buf["gu"], "gelu_tanh", out=buf["g"])
     linear(buf["g"], w_down, out=buf["d"])
-    rmsnorm(buf["d"], post_norm, hidden, eps, xs, accumulate=True)
+    rmsnorm(buf["d"], post_norm, hidden, eps, xs, accumulate=True, next_weight=next_norm,
+            next_out=None if next_norm is None else next_out.view(B * L, hidden))
     return x
 
 
 def gemma_layer(x: torch.Tensor, *, attn: dict, mlp: dict, cs: RopeTable, window: int = 0, eps: float = 1e-6,
-                buffers: Optional[Tuple[dict, dict]] = None) -> torch.Tensor:
+                buffers: Optional[Tuple[dict, dict]] = None, h_ready: bool = False,
+                next_norm: Optional[torch.Tensor] = None) -> torch.Tensor:
     """One whole Gemma3 layer in place on x (app/models/gemma3.js:62-89): ``gemma_attention_sublayer(x,
-    **attn)`` then ``gemma_mlp_sublayer(x, **mlp)``.  ``buffers`` = (gemma_sublayer_buffers(...),
-    gemma_mlp_buffers(...)), to reuse."""
-    ab, mb = buffers if buffers is not None else (None, None)
-    gemma_attention_sublayer(x, **attn, cs=cs, window=window, eps=eps, buffers=ab)
-    return gemma_mlp_sublayer(x, **mlp, eps=eps, buffers=mb)
+    **attn)`` then ``gemma_mlp_sublayer(x, **mlp)``, with the post-attention accumulate also writing
+    the MLP's normalised input (one pass for gemma3.js:74-79).  ``buffers`` = (gemma_sublayer_buffers(...),
+    gemma_mlp_buffers(...)), to reuse.  Across layers: ``next_norm`` (the next layer's in_norm) makes
+    the post-MLP accumulate write the next layer's normalised input into buffers[0]["h"], and the next
+    call passes ``h_ready=True``."""
+    B, L, hidden = x.shape
+    if buffers is None:
+        inter = mlp["w_down"].shape[1]
+        buffers = (gemma_sublayer_buffers(B, L, hidden, x.device),
+                   gemma_mlp_buffers(B, L, hidden, inter, x.device, mlp.get("gate_up_interleaved", False)))
+    ab, mb = buffers
+    gemma_attention_sublayer(x, **attn, cs=cs, window=window, eps=eps, buffers=ab, h_ready=h_ready,
+                             next_norm=mlp["pre_norm"], next_out=mb["h"])
+    return gemma_mlp_sublayer(x, **mlp, eps=eps, buffers=mb, h_ready=True, next_norm=next_norm,
+                              next_out=ab["h"] if next_norm is not None else None)
 
 
 def text_refine_attention(qkv: torch.Tensor, *, q_norm: torch.Tensor, k_norm: torch.Tensor,

@@ -1440,7 +1440,27 @@ nsa_status nsa_rmsnorm(const nsa_rmsnorm_desc* d, const float* X, const float* w
   p.eps = d->eps;
   p.vec = d->cols % 4 == 0 && ldx % 4 == 0 && ldy % 4 == 0 && (x0 & 15) == 0 &&
           (reinterpret_cast<uintptr_t>(weight) & 15) == 0 && (y0 & (uintptr_t)(4 * esz - 1)) == 0;
-  const double bytes = (double)d->rows * d->cols * (4.0 + esz * (d->accumulate ? 2.0 : 1.0));
+  double bytes = (double)d->rows * d->cols * (4.0 + esz * (d->accumulate ? 2.0 : 1.0));
+  if (d->next_weight) {
+    // the chained next norm: Z = rmsnorm(Y after the add) * next_weight
+    if (!d->accumulate) return fail(NSA_ERR_INVALID_ARGUMENT, "next_weight needs accumulate = 1");
+    if (!d->Z) return fail(NSA_ERR_INVALID_ARGUMENT, "next_weight needs Z");
+    if (d->z_dtype != NSA_F32 && d->z_dtype != NSA_BF16) return fail(NSA_ERR_INVALID_ARGUMENT, "bad z_dtype");
+    const int64_t ldz = d->ldz ? d->ldz : d->cols;
+    const int zsz = d->z_dtype == NSA_F32 ? 4 : 2;
+    const uintptr_t z0 = reinterpret_cast<uintptr_t>(d->Z);
+    if (ldz < d->cols || ldz % 4 || !p.vec || (z0 & (uintptr_t)(4 * zsz - 1)) ||
+        (reinterpret_cast<uintptr_t>(d->next_weight) & 15))
+      return fail(NSA_ERR_INVALID_ARGUMENT,
+                  "the chained norm needs cols, ldx, ldy, ldz multiples of 4 and 16-byte aligned X, Y, weights and Z rows");
+    const uintptr_t z1 = z0 + (uintptr_t)(((int64_t)(d->rows - 1) * ldz + d->cols) * zsz);
+    if ((z0 < y1 && y0 < z1) || (z0 < x1 && x0 < z1)) return fail(NSA_ERR_INVALID_ARGUMENT, "Z must not overlap X or Y");
+    p.w2 = d->next_weight;
+    p.z = d->Z;
+    p.ldz = ldz;
+    p.z_bf16 = d->z_dtype == NSA_BF16 ? 1 : 0;
+    bytes += (double)d->rows * d->cols * zsz;
+  }
   const cudaStream_t strm = static_cast<cudaStream_t>(stream);
   cudaError_t e = profiled("rmsnorm", 0.0, bytes, strm, [&] { return nsa::launch_rmsnorm(p, strm); });
   if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");

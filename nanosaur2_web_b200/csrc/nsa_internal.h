@@ -256,6 +256,10 @@ struct RmsParams {
   int accumulate;   // fp32 Y only
   int vec;          // cols, ldx, ldy multiples of 4; x, w, y 16-byte aligned
   float eps;
+  const float* w2;  // accumulate only: Z = rmsnorm(Y after the add) * w2 (vec path), or null
+  void* z;          // fp32, or bf16 when z_bf16
+  int64_t ldz;
+  int z_bf16;
 };
 cudaError_t launch_rmsnorm(const RmsParams& p, cudaStream_t stream);
 

@@ -8,7 +8,10 @@
 // registers (five 16-byte loads per lane, with the weights and, accumulating, Y requested in the same
 // round trip); longer rows read the rest a second time (from L1).  The
 // kernel is HBM-bound: X is read once, Y written once (and read once when accumulating); bf16 output
-// feeds the next GEMM's A operand directly (the QKV projection of the Gemma layer).
+// feeds the next GEMM's A operand directly (the QKV projection of the Gemma layer).  The chained form
+// (accumulate with a next weight) continues with the next norm of the updated rows, which the Gemma
+// layer runs right after each accumulate (the pre-MLP norm, the next layer's input norm): the new Y
+// values are still in registers, so Z = rmsnorm(Y) * w2 adds only its own write.
 #include <cuda_bf16.h>
 
 #include "nsa_internal.h"
@@ -26,7 +29,14 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-__device__ __forceinline__ float sq4(float4 v) { return v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
+// ss + x^2 + y^2 + z^2 + w^2 in a fixed order of fused multiply-adds (intrinsics: the compiler neither
+// contracts nor reorders them), so that every pass over the same values gives the same sum.
+__device__ __forceinline__ float sq4_acc(float ss, float4 v) {
+  ss = __fmaf_rn(v.x, v.x, ss);
+  ss = __fmaf_rn(v.y, v.y, ss);
+  ss = __fmaf_rn(v.z, v.z, ss);
+  return __fmaf_rn(v.w, v.w, ss);
+}
 
 // y = (x * r) * w for four values, then stored (bf16 / fp32) or added to `acc` (the prefetched Y).
 template <bool BF16, bool ACC>
@@ -61,9 +71,30 @@ __device__ __forceinline__ void emit1(const RmsParams& p, int64_t row, int c, fl
   }
 }
 
+// z row = y * r2 * w2 for four values (the same product order as emit4), bf16 or fp32.
+__device__ __forceinline__ void emit_z4(const RmsParams& p, int64_t row, int i, float4 y, float r2, float4 w) {
+  const float4 z = make_float4(y.x * r2 * w.x, y.y * r2 * w.y, y.z * r2 * w.z, y.w * r2 * w.w);
+  if (p.z_bf16) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(z.x, z.y), hi = __floats2bfloat162_rn(z.z, z.w);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&lo);
+    u.y = *reinterpret_cast<uint32_t*>(&hi);
+    reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.z) + row * p.ldz)[i] = u;
+  } else {
+    reinterpret_cast<float4*>(static_cast<float*>(p.z) + row * p.ldz)[i] = z;
+  }
+}
+
+__device__ __forceinline__ float4 add4(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+__device__ __forceinline__ float4 norm4(float4 v, float r, float4 w) {
+  return make_float4(v.x * r * w.x, v.y * r * w.y, v.z * r * w.z, v.w * r * w.w);
+}
+
 // VEC: cols, ldx and ldy multiples of 4 and X, w, Y 16-byte aligned (8-byte for bf16 Y rows).
-template <bool VEC, bool BF16, bool ACC>
+// CHAIN (VEC, ACC, fp32 Y): then Z = rmsnorm(new Y) * w2, Z's rows 8-byte (bf16) / 16-byte aligned.
+template <bool VEC, bool BF16, bool ACC, bool CHAIN>
 __global__ void __launch_bounds__(kRmsWarps * 32) rmsnorm_kernel(const RmsParams p) {
+  static_assert(!CHAIN || (VEC && ACC && !BF16), "the chained form follows the vector accumulate");
   const int lane = threadIdx.x % 32;
   const int64_t row = (int64_t)blockIdx.x * kRmsWarps + threadIdx.x / 32;
   if (row >= p.rows) return;
@@ -87,23 +118,50 @@ __global__ void __launch_bounds__(kRmsWarps * 32) rmsnorm_kernel(const RmsParams
       if constexpr (ACC) yv[j] = in ? y4[i] : z;
     }
 #pragma unroll
-    for (int j = 0; j < kRmsCache; ++j) ss += sq4(v[j]);
-    for (int i = lane + 32 * kRmsCache; i < nv; i += 32) ss += sq4(__ldg(x4 + i));
+    for (int j = 0; j < kRmsCache; ++j) ss = sq4_acc(ss, v[j]);
+    for (int i = lane + 32 * kRmsCache; i < nv; i += 32) ss = sq4_acc(ss, __ldg(x4 + i));
     const float r = rsqrtf(warp_sum(ss) / (float)p.cols + p.eps);
+    if constexpr (CHAIN) {
+      // Y += norm(X), then the next norm over the new Y in the same order of sums as a separate pass
+      float ss2 = 0.f;
 #pragma unroll
-    for (int j = 0; j < kRmsCache; ++j) {
-      const int i = lane + 32 * j;
-      if (i >= nv) continue;
-      if constexpr (ACC)
-        emit4<BF16, ACC>(p, row, i, v[j], r, wv[j], yv[j]);
-      else
-        emit4<BF16, ACC>(p, row, i, v[j], r, wv[j], z);
-    }
-    for (int i = lane + 32 * kRmsCache; i < nv; i += 32) {
-      if constexpr (ACC)
-        emit4<BF16, ACC>(p, row, i, __ldg(x4 + i), r, __ldg(w4 + i), y4[i]);
-      else
-        emit4<BF16, ACC>(p, row, i, __ldg(x4 + i), r, __ldg(w4 + i), z);
+      for (int j = 0; j < kRmsCache; ++j) {
+        const int i = lane + 32 * j;
+        if (i >= nv) continue;
+        yv[j] = add4(yv[j], norm4(v[j], r, wv[j]));
+        y4[i] = yv[j];
+      }
+#pragma unroll
+      for (int j = 0; j < kRmsCache; ++j) ss2 = sq4_acc(ss2, lane + 32 * j < nv ? yv[j] : z);
+      for (int i = lane + 32 * kRmsCache; i < nv; i += 32) {
+        const float4 yn = add4(y4[i], norm4(__ldg(x4 + i), r, __ldg(w4 + i)));
+        y4[i] = yn;
+        ss2 = sq4_acc(ss2, yn);
+      }
+      const float r2 = rsqrtf(warp_sum(ss2) / (float)p.cols + p.eps);
+      const float4* w24 = reinterpret_cast<const float4*>(p.w2);
+#pragma unroll
+      for (int j = 0; j < kRmsCache; ++j) {
+        const int i = lane + 32 * j;
+        if (i < nv) emit_z4(p, row, i, yv[j], r2, __ldg(w24 + i));
+      }
+      for (int i = lane + 32 * kRmsCache; i < nv; i += 32) emit_z4(p, row, i, y4[i], r2, __ldg(w24 + i));
+    } else {
+#pragma unroll
+      for (int j = 0; j < kRmsCache; ++j) {
+        const int i = lane + 32 * j;
+        if (i >= nv) continue;
+        if constexpr (ACC)
+          emit4<BF16, ACC>(p, row, i, v[j], r, wv[j], yv[j]);
+        else
+          emit4<BF16, ACC>(p, row, i, v[j], r, wv[j], z);
+      }
+      for (int i = lane + 32 * kRmsCache; i < nv; i += 32) {
+        if constexpr (ACC)
+          emit4<BF16, ACC>(p, row, i, __ldg(x4 + i), r, __ldg(w4 + i), y4[i]);
+        else
+          emit4<BF16, ACC>(p, row, i, __ldg(x4 + i), r, __ldg(w4 + i), z);
+      }
     }
   } else {
     for (int c = lane; c < p.cols; c += 32) {
@@ -121,11 +179,13 @@ cudaError_t launch_v(const RmsParams& p, cudaStream_t stream) {
   if (blocks > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   const dim3 grid((unsigned)blocks), block(kRmsWarps * 32);
   if (p.out_bf16)
-    rmsnorm_kernel<VEC, true, false><<<grid, block, 0, stream>>>(p);
+    rmsnorm_kernel<VEC, true, false, false><<<grid, block, 0, stream>>>(p);
+  else if (p.accumulate && VEC && p.w2)
+    rmsnorm_kernel<VEC, false, true, VEC><<<grid, block, 0, stream>>>(p);
   else if (p.accumulate)
-    rmsnorm_kernel<VEC, false, true><<<grid, block, 0, stream>>>(p);
+    rmsnorm_kernel<VEC, false, true, false><<<grid, block, 0, stream>>>(p);
   else
-    rmsnorm_kernel<VEC, false, false><<<grid, block, 0, stream>>>(p);
+    rmsnorm_kernel<VEC, false, false, false><<<grid, block, 0, stream>>>(p);
   return cudaGetLastError();
 }
 

@@ -20,7 +20,8 @@
  *                          [{A, B, r, off, n, scale}]; returns the packed rank R -> nsa_lora_pack
  *   expandI8(opts)         int8 weights -> exact bf16 values (the projection's ConvRot form)
  *                                                                        -> nsa_expand_i8
- *   rmsnorm(opts)          ops.rmsnorm(gpu, x, weight, cols, eps, out) (ops.js:111-116)
+ *   rmsnorm(opts)          ops.rmsnorm(gpu, x, weight, cols, eps, out) (ops.js:111-116), with the chained
+ *                          next norm of an accumulate (nextWeight, nextOut, ldz, nextOutBf16)
  *   glu(opts)              ops.glu(gpu, x, act) (ops.js:141-148)
  *   gluInterleave(opts)    a gate_up weight / bias / scale in the fused GLU's row order
  *                          {src, dst, I, rowBytes}                        -> nsa_glu_interleave
@@ -278,6 +279,10 @@ static napi_value Rmsnorm(napi_env env, napi_callback_info info) {
   d.out_dtype = dtype(env, o, "outBf16");
   d.accumulate = (int32_t)num(env, o, "accumulate", 0);
   d.eps = fnum(env, o, "eps", 1e-6f);
+  d.next_weight = (const float*)ptr(env, o, "nextWeight");
+  d.Z = ptr(env, o, "nextOut");
+  d.ldz = num(env, o, "ldz", 0);
+  d.z_dtype = dtype(env, o, "nextOutBf16");
   return done(env, nsa_rmsnorm(&d, ptr(env, o, "x"), ptr(env, o, "weight"), ptr(env, o, "out"), ptr(env, o, "stream")));
 }
 

@@ -251,11 +251,14 @@ def linear(x: torch.Tensor, W: torch.Tensor, *, bias: Optional[torch.Tensor] = N
 
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, cols: Optional[int] = None, eps: float = 1e-6,
             out: Optional[torch.Tensor] = None, *, accumulate: bool = False,
-            out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+            out_dtype: Optional[torch.dtype] = None, next_weight: Optional[torch.Tensor] = None,
+            next_out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y = x * rsqrt(mean(x^2) + eps) * weight over rows of ``cols`` values (app/gpu/ops.js:111-116,
     kernels.js:62-80).  x fp32 [..., cols] with unit inner stride; out fp32 or bf16 (the next GEMM's
     operand), allocated like x when not given.  ``accumulate`` adds into ``out`` instead, the
-    ops.accumulate that follows the Gemma layer's post-attention norm (app/models/gemma3.js:74-77)."""
+    ops.accumulate that follows the Gemma layer's post-attention norm (app/models/gemma3.js:74-77);
+    with ``next_weight`` the same pass also writes ``next_out`` = rmsnorm(out after the add) *
+    next_weight (fp32 or bf16, out's shape), the norm the layer runs next (gemma3.js:78-79)."""
     _require_cuda(x, weight, out)
     cols = cols or x.shape[-1]
     if x.dtype != torch.float32 or weight.dtype != torch.float32 or x.stride(-1) != 1 or x.shape[-1] != cols:
@@ -281,6 +284,14 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, cols: Optional[int] = None, e
     d.rows, d.cols = x2.shape[0], cols
     d.ldx, d.ldy = x2.stride(0), o2.stride(0)
     d.out_dtype, d.accumulate, d.eps = dtype_code(out), int(bool(accumulate)), eps
+    if next_weight is not None:
+        _require_cuda(next_weight, next_out)
+        if next_out is None or next_out.shape != out.shape or next_out.stride(-1) != 1:
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "next_weight needs next_out of out's shape with unit inner stride")
+        if next_weight.dtype != torch.float32 or not next_weight.is_contiguous() or next_weight.numel() < cols:
+            raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "next_weight must be a contiguous float32 [cols] tensor")
+        z2 = rows(next_out)
+        d.next_weight, d.Z, d.ldz, d.z_dtype = next_weight.data_ptr(), z2.data_ptr(), z2.stride(0), dtype_code(next_out)
     with torch.cuda.device(x.device):
         check(lib().nsa_rmsnorm(ctypes.byref(d), x2.data_ptr(), weight.data_ptr(), o2.data_ptr(),
                                 stream_handle(x.device)))

@@ -18,6 +18,8 @@ on the O(1) update.  Emulating the bf16 roundings on the CPU gives 0.021 max-abs
 MLP half rounds h2 and g to bf16: emulated 0.020 max-abs on an update of |x| <= 7.9; the same bounds,
 and 1e-1 for a whole layer (both halves)."""
 
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -213,3 +215,73 @@ def test_gemma_mlp_model_width(fused):
         np.testing.assert_array_equal(got, x2.cpu().numpy())
     for b in range(B):
         _check_update(got[b], x_in[b], O.gemma_mlp_sublayer(x_in[b], pre, wg, wu, wd, post, acc=np.float64))
+
+
+@pytest.mark.parametrize("cols,z_dtype", [(640, torch.bfloat16), (640, torch.float32), (1000, torch.bfloat16)])
+def test_rmsnorm_chained_next_norm_matches_two_passes(cols, z_dtype):
+    """Y += rmsnorm(X) * w with the next norm Z = rmsnorm(new Y) * w2 in the same pass (gemma3.js:74-79)
+    gives the bits of the accumulate followed by a separate rmsnorm; 640 columns stay in registers,
+    1000 also re-read the rest of the row."""
+    from nanosaur2_web_b200.ops import NsaError, rmsnorm
+    rng = np.random.default_rng(70 + cols)
+    rows = 333
+    xs = rng.standard_normal((rows, cols), dtype=np.float32) * 3
+    ys = rng.standard_normal((rows, cols), dtype=np.float32) * 5
+    w = (1 + 0.2 * rng.standard_normal(cols)).astype(np.float32)
+    w2 = (1 + 0.2 * rng.standard_normal(cols)).astype(np.float32)
+    y1, y2 = t(ys), t(ys)
+    z1 = torch.empty((rows, cols), dtype=z_dtype, device=DEV)
+    rmsnorm(t(xs), t(w), cols, 1e-6, y1, accumulate=True)
+    rmsnorm(y1, t(w2), cols, 1e-6, z1)
+    z2 = torch.full((rows, cols), 7.0, dtype=z_dtype, device=DEV)
+    rmsnorm(t(xs), t(w), cols, 1e-6, y2, accumulate=True, next_weight=t(w2), next_out=z2)
+    check_device()
+    np.testing.assert_array_equal(y2.cpu().numpy(), y1.cpu().numpy())
+    np.testing.assert_array_equal(z2.float().cpu().numpy(), z1.float().cpu().numpy())
+    want_y = ys.astype(np.float64) + O.rms_norm(xs, w, acc=np.float64)
+    np.testing.assert_allclose(y2.cpu().numpy(), want_y, rtol=1e-5, atol=1e-4)
+    np.testing.assert_allclose(z2.float().cpu().numpy(), O.rms_norm(want_y, w2, acc=np.float64),
+                               rtol=2 ** -7 if z_dtype == torch.bfloat16 else 1e-4, atol=1e-3)
+    with pytest.raises(NsaError, match="next_weight needs accumulate"):
+        from nanosaur2_web_b200 import _lib
+        d = _lib.RmsnormDesc()
+        d.rows, d.cols, d.eps, d.out_dtype = rows, cols, 1e-6, _lib.NSA_F32
+        d.next_weight, d.Z, d.z_dtype = t(w2).data_ptr(), z2.data_ptr(), _lib.NSA_BF16
+        _lib.check(_lib.lib().nsa_rmsnorm(ctypes.byref(d), t(xs).data_ptr(), t(w).data_ptr(), y2.data_ptr(), None))
+
+
+def test_gemma_layers_chained_norms_match_separate():
+    """Two whole Gemma layers with the norms chained (post-attention accumulate -> pre-MLP norm,
+    post-MLP accumulate -> the next layer's input norm, four fewer passes over x) give the bits of
+    the same layers with every norm its own pass."""
+    from nanosaur2_web_b200.blocks import (GEMMA_HEAD_DIM, gemma_attention_sublayer, gemma_layer,
+                                           gemma_mlp_buffers, gemma_mlp_sublayer, gemma_sublayer_buffers)
+    from nanosaur2_web_b200.ops import glu_interleave, ropeTable
+    B, L, Hd, I = 2, 256, 640, 2048
+    rng = np.random.default_rng(71)
+
+    def norm(n):
+        return t((1.0 + 0.2 * rng.standard_normal(n)).astype(np.float32))
+
+    def lin(o, i):
+        return t(rng.standard_normal((o, i), dtype=np.float32) / np.sqrt(i), torch.bfloat16)
+
+    layers = []
+    for _ in range(2):
+        layers.append(({"in_norm": norm(Hd), "post_norm": norm(Hd), "q_norm": norm(GEMMA_HEAD_DIM),
+                        "k_norm": norm(GEMMA_HEAD_DIM), "w_qkv": lin(1536, Hd), "w_o": lin(Hd, 1024)},
+                       {"pre_norm": norm(Hd), "post_norm": norm(Hd), "w_gate_up": glu_interleave(lin(2 * I, Hd)),
+                        "w_down": lin(Hd, I), "gate_up_interleaved": True}))
+    cs = ropeTable(L, GEMMA_HEAD_DIM, 1e4, DEV)
+    x_in = (8.0 * rng.standard_normal((B, L, Hd))).astype(np.float32)
+    x1 = t(x_in)
+    for attn, mlp in layers:
+        gemma_attention_sublayer(x1, **attn, cs=cs, window=128)
+        gemma_mlp_sublayer(x1, **mlp)
+    x2 = t(x_in)
+    bufs = (gemma_sublayer_buffers(B, L, Hd, DEV), gemma_mlp_buffers(B, L, Hd, I, DEV, True))
+    for li, (attn, mlp) in enumerate(layers):
+        gemma_layer(x2, attn=attn, mlp=mlp, cs=cs, window=128, buffers=bufs, h_ready=li > 0,
+                    next_norm=layers[li + 1][0]["in_norm"] if li + 1 < len(layers) else None)
+    check_device()
+    np.testing.assert_array_equal(x2.cpu().numpy(), x1.cpu().numpy())
