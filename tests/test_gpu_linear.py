@@ -320,7 +320,8 @@ def test_expanded_int8_weight_matches_int8_path():
         linear(xr, wx, lora=pack)
 
 
-@pytest.mark.parametrize("case", ["gated_ragged", "lora_silu_bf16", "glu", "half_tile_f32", "expanded_i8_lora"])
+@pytest.mark.parametrize("case", ["gated_ragged", "gated_k2056", "lora_silu_bf16", "glu", "half_tile_f32",
+                                  "expanded_i8_lora"])
 def test_cta_pair_schedule_matches_single(case):
     """The CTA-pair schedule (two CTAs per 256 x 256 tile, 128-wide K steps) and the single-CTA one
     (128 x 256 tiles, 64-wide K steps) add the same products in the same order: equal bits, for ragged
@@ -330,6 +331,8 @@ def test_cta_pair_schedule_matches_single(case):
     rng = np.random.default_rng(60)
     if case == "gated_ragged":
         M, N, K = 600, 512, 1544
+    elif case == "gated_k2056":
+        M, N, K = 600, 512, 2056
     elif case == "lora_silu_bf16":
         M, N, K = 300, 768, 1536
     elif case == "glu":
@@ -344,7 +347,7 @@ def test_cta_pair_schedule_matches_single(case):
     A, W, Bv = t(a, torch.bfloat16), t(w, torch.bfloat16), t(b)
 
     def run(schedule):
-        if case == "gated_ragged":
+        if case in ("gated_ragged", "gated_k2056"):
             x0, g = rng.standard_normal((M, N), dtype=np.float32), rng.standard_normal(N).astype(np.float32)
             out = t(x0)
             linear(A, W, bias=Bv, out=out, resid=True, gate=t(g), schedule=schedule)
