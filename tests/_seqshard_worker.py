@@ -3,7 +3,7 @@
 Every rank builds the same seeded joint-attention inputs, keeps its own image rows plus the text rows
 (the local layout), and runs SeqShardedJointAttention, which gathers the k'|v' rows over NCCL.  Rank 0
 stitches the ranks' output rows together and compares them with the single-GPU fused call (to the
-size of P's bf16 rounding) and with the CPU oracle on a few heads; it writes the verdict as JSON to
+size of P's bf16 rounding) and with the CPU oracle on a few heads; it writes the outcome as JSON to
 argv[1].
 """
 

@@ -31,7 +31,7 @@ def _free_port():
 def test_seq_shard_two_gpus(tmp_path, mode):
     """The k'|v' exchange by NCCL all-gather, by the prologue's NVLink stores into the peer's buffer
     (CUDA IPC mapping), and by copy-engine pushes into it."""
-    out = tmp_path / "verdict.json"
+    out = tmp_path / "outcome.json"
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes", "1",
            "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(ROOT, "tests", "_seqshard_worker.py"), str(out), mode]
