@@ -16,6 +16,7 @@ NSA_OK, NSA_ERR_INVALID_ARGUMENT, NSA_ERR_UNSUPPORTED, NSA_ERR_WORKSPACE, NSA_ER
 NSA_F32, NSA_BF16 = 0, 1
 NSA_COMPUTE_BF16, NSA_COMPUTE_TF32 = 0, 1
 NSA_W_BF16, NSA_W_I8 = 0, 1
+NSA_LINEAR_AUTO, NSA_LINEAR_SINGLE, NSA_LINEAR_PAIR = 0, 1, 2
 NSA_IPC_HANDLE_BYTES = 72
 
 _i32, _i64, _f32, _vp, _sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t

@@ -1266,6 +1266,10 @@ nsa_status nsa_linear(const nsa_linear_desc* d, const void* A, const void* W, co
     return fail(NSA_ERR_INVALID_ARGUMENT, "a LoRA needs lora_a, lora_b and the lora_t scratch");
   if (d->out_dtype == NSA_BF16 && (ldc % 8 || d->cOff % 8))
     return fail(NSA_ERR_INVALID_ARGUMENT, "a bf16 C needs ldc and cOff multiples of 8 (16-byte rows)");
+  if (d->schedule < NSA_LINEAR_AUTO || d->schedule > NSA_LINEAR_PAIR)
+    return fail(NSA_ERR_INVALID_ARGUMENT, "schedule is NSA_LINEAR_AUTO, NSA_LINEAR_SINGLE or NSA_LINEAR_PAIR");
+  if (d->schedule == NSA_LINEAR_PAIR && (i8 || d->M <= 128))
+    return fail(NSA_ERR_INVALID_ARGUMENT, "CTA pairs need bf16 weights and M > 128");
   int* err = nsa::device_error_word();
   if (!err) return fail(NSA_ERR_CUDA, "cannot resolve the device error word on this device");
   const cudaStream_t strm = static_cast<cudaStream_t>(stream);
@@ -1298,10 +1302,6 @@ nsa_status nsa_linear(const nsa_linear_desc* d, const void* A, const void* W, co
   // CTA pairs (256 x 256 tiles, each CTA loading 128 of a tile's W rows, 128-wide K steps) lead only on
   // large GEMMs (16384 x 4096 x 4096: 1491 vs 1344 TFLOP/s); on the DiT and Gemma linears (K 640-2048,
   // 2-14 tiles per SM) single CTAs with their deeper 64-wide ring are level or ahead
-  if (d->schedule < NSA_LINEAR_AUTO || d->schedule > NSA_LINEAR_PAIR)
-    return fail(NSA_ERR_INVALID_ARGUMENT, "schedule is NSA_LINEAR_AUTO, NSA_LINEAR_SINGLE or NSA_LINEAR_PAIR");
-  if (d->schedule == NSA_LINEAR_PAIR && (i8 || d->M <= 128))
-    return fail(NSA_ERR_INVALID_ARGUMENT, "CTA pairs need bf16 weights and M > 128");
   const bool pair = d->schedule == NSA_LINEAR_PAIR ||
                     (d->schedule == NSA_LINEAR_AUTO && !i8 && d->K + R >= 2048 &&
                      (int64_t)d->M * d->N >= (int64_t(1) << 26) && linear_pairs_enabled());

@@ -234,7 +234,7 @@ def linear(x: torch.Tensor, W: torch.Tensor, *, bias: Optional[torch.Tensor] = N
     d.glu = {None: 0, "silu": 1, "gelu_tanh": 2}[glu]
     if schedule not in ("auto", "single", "pair"):
         raise NsaError(_lib.NSA_ERR_INVALID_ARGUMENT, "schedule is 'auto', 'single' or 'pair'")
-    d.schedule = {"auto": 0, "single": 1, "pair": 2}[schedule]
+    d.schedule = {"auto": _lib.NSA_LINEAR_AUTO, "single": _lib.NSA_LINEAR_SINGLE, "pair": _lib.NSA_LINEAR_PAIR}[schedule]
     t = None
     if lora is not None:
         if lora.N != N or lora.K != K:

@@ -210,6 +210,23 @@ def test_projection_and_linear_validation():
     assert lin() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # act 0 or 1
     ld.act = 0
     assert lin(bias=fake + 4) == _lib.NSA_ERR_INVALID_ARGUMENT                              # unaligned bias
+    ld.resid = 0
+    ld.glu = 3
+    assert lin() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # glu 0, 1 or 2
+    ld.glu, ld.N, ld.ldc = 2, 1664, 832
+    assert lin() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # GLU: N not whole tiles
+    ld.N, ld.resid = 1536, 1
+    assert lin() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # GLU has no resid form
+    assert b"fused GLU" in L.nsa_last_error()
+    ld.glu, ld.resid, ld.ldc = 0, 0, 0
+    ld.schedule = 5
+    assert lin() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # unknown schedule
+    ld.schedule, ld.M = _lib.NSA_LINEAR_PAIR, 128
+    assert lin() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # pairs need M > 128
+    assert b"CTA pairs" in L.nsa_last_error()
+    ld.M, ld.w_format, ld.w_scale = 3952, _lib.NSA_W_I8, fake
+    assert lin() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # pairs: bf16 weights only
+    ld.schedule, ld.w_format, ld.w_scale = 0, _lib.NSA_W_BF16, None
 
 
 def test_rmsnorm_validation():
@@ -236,6 +253,16 @@ def test_rmsnorm_validation():
     d.eps = 1e-6
     assert rms(y=fake + 4 * 640) == _lib.NSA_ERR_INVALID_ARGUMENT                           # Y overlaps X
     assert b"overlap" in L.nsa_last_error()
+    d.next_weight = fake + (1 << 29)
+    assert rms() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # next norm needs accumulate
+    d.accumulate = 1
+    assert rms() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # ... and a Z
+    d.Z, d.z_dtype = fake + 64, _lib.NSA_BF16
+    assert rms() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # Z overlaps X
+    assert b"overlap" in L.nsa_last_error()
+    d.Z, d.z_dtype = fake + (1 << 31), 9
+    assert rms() == _lib.NSA_ERR_INVALID_ARGUMENT                                           # bad z_dtype
+    d.next_weight, d.Z, d.accumulate = None, None, 0
     d.rows = 0
     assert rms(x=None, w=None, y=None) == _lib.NSA_OK                                       # empty: nothing to do
 
